@@ -1,0 +1,294 @@
+"""Benchmark of certified ExactAttention on B200: certified QK pairs/s (and tokens/s).
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5] [--splits S]
+               [--impl ours|reference]
+
+One step = one certified attention pass over the config's whole workload (c2 by default: the
+Qwen3-0.6B causal prefill, 16 q / 8 kv heads, 4096 tokens, d=128: 134,250,496 pairs).
+Under torchrun every rank runs its own copy of the workload (weak scaling: each GPU owns a batch
+element; the path has no data-path collective for these configs).
+
+  value      pairs/s over all ranks, inputs resident in HBM; CUDA events around each step on the
+             launch stream, L2 flushed (a 256 MiB write) between steps; max over ranks
+  e2e        the same metric through the host-pointer C ABI (ea_attention_cuda_ranges) from
+             pinned host buffers: H2D of q, k, v and the masks, and D2H of the output and flags,
+             inside the timed region
+  roofline   the tier-1 kernel against the int8 tensor-core roofline (SURVEY's 7,936 int8 ops per
+             pair) and its measured launch time
+  cpu_baseline  the reference's C++ certified kernel (oracle/_ref, all host threads) on a bounded
+             sample of the same workload, on this host
+`--impl reference` times only that CPU implementation, on the same config and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+INT8_OPS_PER_PAIR = 7936        # QK 4x4 slices + P.V 5x3 slices at d = 128
+BF16_EQUIV_FLOPS_PER_PAIR = 512  # 4 d
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"])
+    ap.add_argument("--splits", type=int, default=0, help="KV splits (0: config default)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.t.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 8 for i in range(4) if r[4 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def default_splits(name: str) -> int:
+    return {"c2": 1, "c3": 4, "c4": 1, "c5": 16}[name]
+
+
+def cpu_reference_step(name: str, budget_s: float = 12.0):
+    """The reference's C++ kernel (all host threads) on whole (sequence, kv head) segments of the
+    config until `budget_s` of CPU time; returns (pairs, seconds, segments, threads)."""
+    from exactattention_b200 import workloads
+    from oracle import ref
+
+    cfg = workloads.config(name)
+    threads = os.cpu_count() or 1
+    pairs, secs, segs = 0, 0.0, 0
+    for b, kvh, Q, K, V, rp, ki, canon in workloads.segments(cfg):
+        t0 = time.perf_counter()
+        ref.attention_ref(Q, K, V, cfg.alpha, rp, ki, threads=threads, splits=1, tile=64)
+        secs += time.perf_counter() - t0
+        pairs += int(rp[-1])
+        segs += 1
+        if secs >= budget_s:
+            break
+    return pairs, secs, segs, threads
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from exactattention_b200 import workloads
+
+    cfg = workloads.config(args.config)
+    from oracle import ref
+
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libexactattn_cpu.so not built"}))
+        return
+    budget = 6.0
+    for _ in range(args.warmup):
+        cpu_reference_step(args.config, budget_s=1.0)
+    tot_p, tot_s, segs = 0, 0.0, 0
+    for _ in range(args.steps):
+        p, s, n, threads = cpu_reference_step(args.config, budget_s=budget)
+        tot_p += p
+        tot_s += s
+        segs = n
+    v = tot_p / tot_s
+    sample = f"{segs} (sequence, kv head) segments of {args.config} per step ({tot_p // args.steps} pairs)"
+    print(json.dumps({
+        "impl": "reference", "metric": "certified QK pairs/s", "value": v, "unit": "pairs/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * tot_s / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": args.config, "pairs": cfg.pairs},
+        "cpu_baseline": {"value": v, "unit": "pairs/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": v, "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+
+    from exactattention_b200 import build, cuda, workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    build.build()
+    name = args.config
+    splits = args.splits or default_splits(name)
+    case = workloads.device_case(name, dev)
+    cfg = case["cfg"]
+    pairs = cfg.pairs
+    q, k, v, kw = case["q"], case["k"], case["v"], case["kw"]
+    stats = torch.zeros(8, dtype=torch.int64, device=dev)
+    cuda.reserve_workspace(q.shape[0], splits, v.shape[-1])
+    out = torch.empty((q.shape[0], v.shape[-1]), dtype=torch.int16, device=dev)
+    flags = torch.empty(q.shape[0], dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        cuda.launch(q, k, v, cfg.alpha, splits=splits, out_tensor=out, flags=flags, stats=stats, **kw)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    stats.zero_()
+    clocks = Clocks(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    st = stats.cpu().numpy()
+    ok = bool(not flags.any().item())
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * pairs / (ms_max / 1000.0)
+
+    # ---- e2e through the host C ABI ----
+    e2e = None
+    if not args.no_e2e and name == "c2":
+        qh = q.cpu().pin_memory().numpy().view(np.uint16)
+        kh = k.cpu().pin_memory().numpy().view(np.uint16)
+        vh = v.cpu().pin_memory().numpy().view(np.uint16)
+        kb = kw["kv_base"].cpu().pin_memory().numpy()
+        kl = kw["kv_len"].cpu().pin_memory().numpy()
+        oh = torch.empty(out.shape, dtype=torch.int16).pin_memory().numpy().view(np.uint16)
+        fh = torch.empty(flags.shape, dtype=torch.uint8).pin_memory().numpy()
+        for _ in range(2):
+            cuda.attention_cuda_ranges(qh, kh, vh, cfg.alpha, kb, kl, kw["max_row_keys"], splits=splits,
+                                       out_buf=oh, flags_buf=fh)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            cuda.attention_cuda_ranges(qh, kh, vh, cfg.alpha, kb, kl, kw["max_row_keys"], splits=splits,
+                                       out_buf=oh, flags_buf=fh)
+        e_ms = (time.perf_counter() - t0) * 1000 / args.steps
+        te = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        same = bool(np.array_equal(oh, out.cpu().numpy().view(np.uint16)))
+        h2d = qh.nbytes + kh.nbytes + vh.nbytes + kb.nbytes + kl.nbytes
+        e2e = {"value": world * pairs / (float(te.item()) / 1000.0), "unit": "pairs/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(oh.nbytes + fh.nbytes),
+               "ms_per_step": float(te.item()), "matches_device_output": same,
+               "path": "ea_attention_cuda_ranges (host pointers, pinned)"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    pk = peaks()
+    int8_peak_tops = 2.0 * pk["bf16_tflops"]   # dense int8 = 2x dense bf16 on B200 (assumed from the nominal ratio)
+    achieved = pairs * INT8_OPS_PER_PAIR / (ms / 1000.0) / 1e12
+    prof = os.path.join(ROOT, "profiles", f"simt_split_kernel_{name}.json")
+    traffic = json.load(open(prof)).get("dram_bytes_per_launch") if os.path.exists(prof) else None
+    cpu = None
+    if not args.no_cpu and world == 1:
+        from oracle import ref
+
+        if ref.available():
+            p_, s_, n_, th = cpu_reference_step(name, budget_s=12.0)
+            cpu = {"value": p_ / s_, "unit": "pairs/s", "cores": th, "kind": "reference",
+                   "sample": f"{n_} (sequence, kv head) segments of {name}, {p_} pairs, {s_:.1f} s"}
+    line = {
+        "metric": "certified QK pairs/s", "value": value, "unit": "pairs/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": name, "pairs_per_gpu": pairs, "rows": cfg.rows, "splits": splits,
+                   "heads": "16q/8kv", "head_dim": 128, "l2": "flushed (256 MiB write) between steps",
+                   "tokens_per_s": world * cfg.rows / (ms_max / 1000.0)},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak_tops, "unit": "TOPS(int8)",
+                     "frac": achieved / int8_peak_tops, "traffic": traffic,
+                     "kernel": "simt_split_kernel (tier 1; CUDA cores)",
+                     "peak_source": f"2 x {pk['source']} bf16 {pk['bf16_tflops']} TFLOP/s"},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps * (2 + (1 if splits > 1 else 0)),
+        "clocks": clk,
+        "certified": {"flags_all_zero": ok, "score_exact": int(st[0]), "weight_wide": int(st[1]),
+                      "tier3_rows": int(st[2]), "domain_rows": int(st[3]), "unresolved_rows": int(st[4]),
+                      "host_fallbacks": int(st[6])},
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+"""Loads libexactattn_cuda.so (built in-tree by build.py) and declares its C ABI
+(include/exactattn_cuda.h). There is no CPU fallback: a missing library or a missing GPU raises."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libexactattn_cuda.so")
+_lib = None
+
+EA_MASK_CSR, EA_MASK_RANGE, EA_MASK_PAGED, EA_MASK_HYBRID = 0, 1, 2, 3
+EA_STATS_LEN = 8
+STAT_NAMES = ("score_exact", "weight_wide", "tier3_rows", "domain_rows", "unresolved_rows", "pairs",
+              "host_fallbacks", "reserved")
+
+# Every symbol include/exactattn_cuda.h declares.
+EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda", "ea_launch_cuda",
+           "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error")
+
+
+class LaunchArgs(ctypes.Structure):
+    """ea_launch_t (include/exactattn_cuda.h), field for field."""
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("rows", ctypes.c_int64), ("d", ctypes.c_int),
+        ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("nkeys", ctypes.c_int64), ("dv", ctypes.c_int),
+        ("alpha", ctypes.c_float),
+        ("mask_kind", ctypes.c_int),
+        ("row_ptr", ctypes.c_void_p), ("key_idx", ctypes.c_void_p),
+        ("kv_base", ctypes.c_void_p), ("kv_len", ctypes.c_void_p),
+        ("page_table", ctypes.c_void_p), ("seq_lens", ctypes.c_void_p),
+        ("page_size", ctypes.c_int), ("max_pages", ctypes.c_int), ("q_heads", ctypes.c_int),
+        ("kv_heads", ctypes.c_int),
+        ("max_row_keys", ctypes.c_int64),
+        ("fp32_out", ctypes.c_int), ("splits", ctypes.c_int),
+        ("out", ctypes.c_void_p), ("flags", ctypes.c_void_p), ("stats", ctypes.c_void_p),
+    ]
+
+
+def load(path: str | None = None):
+    """The library handle, with argument types declared. Raises if it is not built."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise RuntimeError(f"{p} is missing: build it with `python -m exactattention_b200.build`")
+    lib = ctypes.CDLL(p)
+    P = ctypes.c_void_p
+    lib.ea_attention_cuda.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int64, ctypes.c_int,
+                                      ctypes.c_float, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_uint64, ctypes.c_int, P, P, P]
+    lib.ea_attention_cuda.restype = ctypes.c_int
+    lib.ea_attention_cuda_ranges.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int64, ctypes.c_int,
+                                             ctypes.c_float, P, P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P, P,
+                                             P]
+    lib.ea_attention_cuda_ranges.restype = ctypes.c_int
+    lib.ea_round_ratio_cuda.argtypes = [ctypes.c_uint64] * 4 + [ctypes.c_int] * 3 + [ctypes.POINTER(ctypes.c_int)]
+    lib.ea_round_ratio_cuda.restype = ctypes.c_float
+    lib.ea_launch_cuda.argtypes = [ctypes.POINTER(LaunchArgs), P]
+    lib.ea_launch_cuda.restype = ctypes.c_int
+    lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
+    lib.ea_reserve_workspace.restype = ctypes.c_int
+    lib.ea_cuda_release.argtypes = []
+    lib.ea_cuda_release.restype = None
+    lib.ea_cuda_last_error.argtypes = []
+    lib.ea_cuda_last_error.restype = ctypes.c_char_p
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc == 0:
+        return
+    lib = load()
+    msg = lib.ea_cuda_last_error().decode(errors="replace")
+    if rc == -1:
+        raise ValueError(f"{what}: invalid dimensions (code -1)")
+    if rc == -2:
+        raise ValueError(f"{what}: acc_bits must be 64 or 128 (code -2)")
+    if rc == -3:
+        raise ValueError(f"{what}: alpha is not finite (code -3)")
+    if rc == -5:
+        raise ValueError(f"{what}: unsupported layout (code -5)")
+    raise RuntimeError(f"{what}: CUDA error (code {rc}): {msg}")

@@ -1,0 +1,379 @@
+// C ABI of libexactattn_cuda.so (declared in include/exactattn_cuda.h): argument checks,
+// the per-device workspace, and the launch sequence tier 1 -> combine -> tier 3.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/exactattn_cuda.h"
+#include "ea_core.cuh"
+#include "ea_wide.h"
+
+namespace ea {
+cudaError_t launch_simt(const Prob& P, cudaStream_t st);
+cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
+}  // namespace ea
+
+using namespace ea;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail_cuda(cudaError_t e, const char* where) {
+  g_err = std::string(where) + ": " + cudaGetErrorString(e);
+  return -4;
+}
+
+// Grow-only device buffers of one device.
+struct Workspace {
+  int device = -1;
+  int sms = 148;
+  unsigned long long* stats = nullptr;  // STAT_LEN
+  int* t3_count = nullptr;
+  int* t3_list = nullptr;
+  int64_t t3_cap = 0;
+  void* part = nullptr;
+  size_t part_bytes = 0;
+  // staging for the host-pointer entry point
+  void* stage = nullptr;
+  size_t stage_bytes = 0;
+  cudaStream_t stream = nullptr;
+};
+
+std::mutex g_mu;
+std::vector<Workspace> g_ws;
+
+Workspace* workspace() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  for (auto& w : g_ws)
+    if (w.device == dev) return &w;
+  Workspace w;
+  w.device = dev;
+  cudaDeviceGetAttribute(&w.sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaMalloc(&w.stats, STAT_LEN * sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&w.t3_count, sizeof(int)) != cudaSuccess) return nullptr;
+  cudaMemset(w.stats, 0, STAT_LEN * sizeof(unsigned long long));
+  g_ws.push_back(w);
+  return &g_ws.back();
+}
+
+size_t part_bytes(int64_t rows, int splits, int dv) {
+  if (splits <= 1) return 0;
+  int64_t n = rows * (int64_t)splits;
+  return (size_t)n * (4 + 8 + 8 + 1 + 16) + (size_t)n * dv * (4 + 8 + 8) + 256;
+}
+
+bool grow(void** p, size_t* cap, size_t need) {
+  if (need <= *cap) return true;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  size_t n = need + need / 4;
+  if (cudaMalloc(p, n) != cudaSuccess) return false;
+  *cap = n;
+  return true;
+}
+
+int reserve(Workspace* w, int64_t rows, int splits, int dv) {
+  if (rows > w->t3_cap) {
+    if (w->t3_list) cudaFree(w->t3_list);
+    w->t3_list = nullptr;
+    if (cudaMalloc(&w->t3_list, (size_t)rows * sizeof(int)) != cudaSuccess) return fail_cuda(cudaErrorMemoryAllocation, "t3_list");
+    w->t3_cap = rows;
+  }
+  if (!grow(&w->part, &w->part_bytes, part_bytes(rows, splits, dv)))
+    return fail_cuda(cudaErrorMemoryAllocation, "partials");
+  return 0;
+}
+
+int window_bits(int d) {
+  int dl = 0;
+  while ((1 << dl) < d) ++dl;
+  int W = (61 - dl) / 2;
+  return W > 28 ? 28 : W;
+}
+
+int ceil_log2(int64_t n) {
+  int k = 0;
+  while (((int64_t)1 << k) < n) ++k;
+  return k;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ea_cuda_last_error(void) { return g_err.c_str(); }
+
+int ea_reserve_workspace(int64_t rows, int splits, int dv) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  return reserve(w, rows, splits, dv);
+}
+
+void ea_cuda_release(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (auto& w : g_ws) {
+    cudaSetDevice(w.device);
+    if (w.stats) cudaFree(w.stats);
+    if (w.t3_count) cudaFree(w.t3_count);
+    if (w.t3_list) cudaFree(w.t3_list);
+    if (w.part) cudaFree(w.part);
+    if (w.stage) cudaFree(w.stage);
+    if (w.stream) cudaStreamDestroy(w.stream);
+  }
+  g_ws.clear();
+  cudaSetDevice(cur);
+}
+
+int ea_launch_cuda(const ea_launch_t* a, void* stream) {
+  if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->splits <= 0 || a->rows < 0) return -1;
+  uint32_t ab;
+  memcpy(&ab, &a->alpha, 4);
+  int32_t am, ae;
+  if (!decode_fp32(ab, am, ae)) return -3;
+  if (a->mask_kind == EA_MASK_PAGED && (a->page_size <= 0 || a->q_heads <= 0 || a->kv_heads <= 0 ||
+                                        a->q_heads % a->kv_heads != 0))
+    return -5;
+  if (a->rows == 0) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  int rc = reserve(w, a->rows, a->splits, a->dv);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.q = a->q;
+  P.k = a->k;
+  P.v = a->v;
+  P.rows = a->rows;
+  P.d = a->d;
+  P.dv = a->dv;
+  P.W = window_bits(a->d);
+  P.am = am;
+  P.ae = ae;
+  P.fp32 = a->fp32_out ? 1 : 0;
+  P.kind = a->mask_kind;
+  P.row_ptr = a->row_ptr;
+  P.key_idx = a->key_idx;
+  P.kv_base = a->kv_base;
+  P.kv_len = a->kv_len;
+  P.page_table = a->page_table;
+  P.seq_lens = a->seq_lens;
+  P.page_size = a->page_size;
+  P.max_pages = a->max_pages;
+  P.hq = a->q_heads;
+  P.hkv = a->kv_heads;
+  P.group = a->kv_heads > 0 ? a->q_heads / a->kv_heads : 1;
+  P.splits = a->splits;
+  int64_t mk = a->max_row_keys < 2 ? 2 : a->max_row_keys;
+  P.key_log2 = ceil_log2(mk);
+  P.FZ = 61 - P.key_log2;
+  P.out = a->out;
+  P.flags = a->flags;
+  P.stats = a->stats ? (unsigned long long*)a->stats : w->stats;
+  P.t3_count = w->t3_count;
+  P.t3_list = w->t3_list;
+  if (a->splits > 1) {
+    int64_t n = a->rows * (int64_t)a->splits;
+    char* p = (char*)w->part;
+    auto take = [&](size_t bytes) {
+      char* r = p;
+      p += (bytes + 255) & ~(size_t)255;
+      return (void*)r;
+    };
+    P.pZ = (int64_t*)take(n * 8);
+    P.pZe = (uint64_t*)take(n * 8);
+    P.pN = (int64_t*)take(n * a->dv * 8);
+    P.pNe = (uint64_t*)take(n * a->dv * 8);
+    P.pR = (int32_t*)take(n * 4);
+    P.pNR = (int32_t*)take(n * a->dv * 4);
+    P.pSt = (uint8_t*)take(n);
+  }
+  cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
+  if (e != cudaSuccess) return fail_cuda(e, "memset");
+  e = launch_simt(P, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-1 launch");
+  int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
+  e = launch_tier3(P, blocks, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  return 0;
+}
+
+// Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back.
+// Exactly one of (row_ptr, key_idx) or (kv_base, kv_len) is used; neither: every key.
+static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v, int64_t nkeys,
+                    int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx, const int64_t* kv_base_h,
+                    const int64_t* kv_len_h, int64_t maxn, int fp32_out, int splits, void* out, uint8_t* flags,
+                    int64_t* stats) {
+  int64_t total = row_ptr ? row_ptr[rows] : 0;
+  const size_t osz = fp32_out ? 4 : 2;
+  // staging layout: q | k | v | mask | out | flags | stats
+  size_t off = 0;
+  auto slot = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  size_t oq = slot((size_t)rows * d * 2), ok = slot((size_t)nkeys * d * 2), ov = slot((size_t)nkeys * dv * 2);
+  size_t orp = slot((size_t)(rows + 1) * 8), oki = slot((size_t)(row_ptr ? total : 0) * 8);
+  size_t okb = slot((size_t)(row_ptr ? 0 : rows) * 8), okl = slot((size_t)(row_ptr ? 0 : rows) * 8);
+  size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
+
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace();
+    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+    if (!grow(&w->stage, &w->stage_bytes, off)) return fail_cuda(cudaErrorMemoryAllocation, "staging");
+    if (!w->stream && cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess)
+      return fail_cuda(cudaGetLastError(), "stream");
+  }
+  char* base = (char*)w->stage;
+  cudaStream_t st = w->stream;
+  cudaError_t e;
+#define EA_CPY(dst, src, n)                                                    \
+  if ((n) > 0) {                                                              \
+    e = cudaMemcpyAsync(base + (dst), (src), (n), cudaMemcpyHostToDevice, st); \
+    if (e != cudaSuccess) return fail_cuda(e, "h2d");                         \
+  }
+  EA_CPY(oq, q, (size_t)rows * d * 2);
+  EA_CPY(ok, k, (size_t)nkeys * d * 2);
+  EA_CPY(ov, v, (size_t)nkeys * dv * 2);
+  std::vector<int64_t> kb, kl;
+  if (row_ptr) {
+    EA_CPY(orp, row_ptr, (size_t)(rows + 1) * 8);
+    EA_CPY(oki, key_idx, (size_t)total * 8);
+  } else if (kv_len_h) {
+    EA_CPY(okb, kv_base_h, (size_t)rows * 8);
+    EA_CPY(okl, kv_len_h, (size_t)rows * 8);
+  } else {
+    kb.assign(rows, 0);
+    kl.assign(rows, nkeys);
+    EA_CPY(okb, kb.data(), (size_t)rows * 8);
+    EA_CPY(okl, kl.data(), (size_t)rows * 8);
+  }
+#undef EA_CPY
+  e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st);
+  if (e != cudaSuccess) return fail_cuda(e, "memset");
+
+  ea_launch_t a;
+  memset(&a, 0, sizeof(a));
+  a.q = (const uint16_t*)(base + oq);
+  a.rows = rows;
+  a.d = d;
+  a.k = (const uint16_t*)(base + ok);
+  a.v = (const uint16_t*)(base + ov);
+  a.nkeys = nkeys;
+  a.dv = dv;
+  a.alpha = alpha;
+  a.mask_kind = row_ptr ? EA_MASK_CSR : EA_MASK_RANGE;
+  a.row_ptr = (const int64_t*)(base + orp);
+  a.key_idx = (const int64_t*)(base + oki);
+  a.kv_base = (const int64_t*)(base + okb);
+  a.kv_len = (const int64_t*)(base + okl);
+  a.max_row_keys = maxn;
+  a.fp32_out = fp32_out;
+  a.splits = splits;
+  a.out = base + oo;
+  a.flags = (uint8_t*)(base + of);
+  a.stats = (int64_t*)(base + os);
+  int rc = ea_launch_cuda(&a, st);
+  if (rc) return rc;
+  int64_t hs[EA_STATS_LEN];
+  if ((e = cudaMemcpyAsync(out, base + oo, (size_t)rows * dv * osz, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(flags, base + of, (size_t)rows, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(hs, base + os, sizeof(hs), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+    return fail_cuda(e, "d2h");
+  if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e, "sync");
+  if (stats) {
+    stats[0] += hs[STAT_SCORE_EXACT];
+    stats[1] += hs[STAT_WEIGHT_WIDE];
+    stats[2] += hs[STAT_TIER3_ROWS];
+  }
+  return 0;
+}
+
+int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
+                      int64_t nkeys, int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx,
+                      int fp32_out, int acc_bits, int tile, int splits, uint64_t order_seed, int nthreads,
+                      void* out, uint8_t* flags, int64_t* stats) {
+  (void)order_seed;
+  (void)nthreads;
+  if (d <= 0 || d > 1024 || dv <= 0 || tile <= 0 || splits <= 0) return -1;
+  if (acc_bits != 64 && acc_bits != 128) return -2;
+  uint32_t ab;
+  memcpy(&ab, &alpha, 4);
+  int32_t am, ae;
+  if (!decode_fp32(ab, am, ae)) return -3;
+  if (rows <= 0) return 0;
+  int64_t maxn = 1;
+  if (row_ptr) {
+    for (int64_t r = 0; r < rows; ++r) {
+      int64_t n = row_ptr[r + 1] - row_ptr[r];
+      if (n > maxn) maxn = n;
+    }
+  } else {
+    maxn = nkeys;
+  }
+  return run_host(q, rows, d, k, v, nkeys, dv, alpha, row_ptr, key_idx, nullptr, nullptr, maxn, fp32_out, splits,
+                  out, flags, stats);
+}
+
+int ea_attention_cuda_ranges(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
+                             int64_t nkeys, int dv, float alpha, const int64_t* kv_base, const int64_t* kv_len,
+                             int64_t max_row_keys, int fp32_out, int splits, void* out, uint8_t* flags,
+                             int64_t* stats) {
+  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || !kv_base || !kv_len) return -1;
+  uint32_t ab;
+  memcpy(&ab, &alpha, 4);
+  int32_t am, ae;
+  if (!decode_fp32(ab, am, ae)) return -3;
+  if (rows <= 0) return 0;
+  return run_host(q, rows, d, k, v, nkeys, dv, alpha, nullptr, nullptr, kv_base, kv_len,
+                  max_row_keys < 1 ? 1 : max_row_keys, fp32_out, splits, out, flags, stats);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// ea_round_ratio_cuda: the reference's rounding export, evaluated by the device helper
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void round_ratio_kernel(uint64_t ah, uint64_t al, uint64_t bh, uint64_t bl, int E, int neg, int fp32,
+                                   uint32_t* out) {
+  uint32_t a[5] = {(uint32_t)al, (uint32_t)(al >> 32), (uint32_t)ah, (uint32_t)(ah >> 32), 0u};
+  uint32_t b[5] = {(uint32_t)bl, (uint32_t)(bl >> 32), (uint32_t)bh, (uint32_t)(bh >> 32), 0u};
+  Rnd r = fp32 ? round_ratio_big<8>(a, b, 5, E, neg, FP32_P, FP32_QMIN, FP32_EMAX)
+               : round_ratio_big<8>(a, b, 5, E, neg, BF16_P, BF16_QMIN, BF16_EMAX);
+  out[0] = fp32 ? rnd_to_f32_bits(r) : (rnd_to_bf16_bits(r) << 16);
+  out[1] = (uint32_t)r.ovf;
+}
+}  // namespace
+
+extern "C" float ea_round_ratio_cuda(uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo, int E, int neg,
+                                     int fp32, int* overflow) {
+  uint32_t* d = nullptr;
+  uint32_t h[2] = {0, 0};
+  if (cudaMalloc(&d, 8) != cudaSuccess) {
+    *overflow = -1;
+    return 0.0f;
+  }
+  round_ratio_kernel<<<1, 1>>>(a_hi, a_lo, b_hi, b_lo, E, neg, fp32, d);
+  cudaMemcpy(h, d, 8, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  *overflow = (int)h[1];
+  float f;
+  memcpy(&f, &h[0], 4);
+  return f;
+}

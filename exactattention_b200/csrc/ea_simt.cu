@@ -1,0 +1,710 @@
+// CUDA-core kernels of certified split-KV ExactAttention (tier 1 for any mask, the split combine,
+// and the wide-integer tier 3). Tensor-core kernels for the structured masks live in ea_tc.cu.
+//
+// Tier 1, one warp per (row, KV split), keys in tiles of 32 (one key per lane):
+//   score   q and k rows in block fixed point (window W bits below each row's leading bit),
+//           acc = sum Qfix Kfix exactly in int64 plus a per-element truncation bound err;
+//           t = RN32(alpha s) certified at both ends of [acc - err, acc + err]; otherwise the
+//           exact score (576-bit bins) decides (certified.py:93-138 is the reference's model).
+//   weight  RN24(2^t) by the 64-bit integer exp2, 128-bit when that is too close to a midpoint.
+//   tile    reference exponent Rt = max(E + 24); Z and per-channel N (anchor Rt + VE_c, VE_c the
+//           tile's largest |v| exponent in channel c) floor-shifted into int64 windows with
+//           lost-bit counts (certified.py:166-210), merged into the running partial
+//           (certified.py:213-246).
+// Combine: partials of every split are re-expressed at the largest reference exponent and
+// summed: integer addition, so the merged state does not depend on split order.
+// Finalize: both ends of the N/Z interval rounded; equal ends are the spec's bits
+// (certified.py:249-286). Anything uncertified goes to tier 3 on the device.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ea_core.cuh"
+#include "ea_numerics.h"
+#include "ea_wide.h"
+
+namespace ea {
+
+__device__ const uint64_t g_ta64[256] = EA_EXP2_TA64_INIT;
+__device__ const uint64_t g_tb64[256] = EA_EXP2_TB64_INIT;
+__device__ const uint64_t g_ta128[512] = EA_EXP2_TA128_INIT;
+__device__ const uint64_t g_tb128[512] = EA_EXP2_TB128_INIT;
+
+// ---------------------------------------------------------------------------
+// shared-memory layout of the tier-1 kernel (host computes the same sizes)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int simt_words(int d) { return (d + 1) / 2; }
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t simt_warp_bytes(int d, int dv) {
+  size_t qb = align16((size_t)d * 2), qf = align16((size_t)d * 4), ql = align16((size_t)d);
+  size_t kt = (size_t)simt_words(d) * 33 * 4, vt = (size_t)32 * dv * 2;
+  size_t tile = align16(kt > vt ? kt : vt);
+  return qb + qf + ql + tile + 32 * 4 + 32 * 4 + 32 * 4;
+}
+__host__ __device__ inline size_t simt_smem_bytes(int d, int dv, int warps) {
+  return 4096 + (size_t)warps * simt_warp_bytes(d, dv);
+}
+
+// warp reductions
+__device__ __forceinline__ int64_t warp_sum64(int64_t x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+__device__ __forceinline__ int warp_max32(int x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x = max(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+// Block fixed point of one bf16 value at lsb: sign * trunc(|m| 2^(e - lsb)), and whether bits
+// were dropped. Callers guarantee e - lsb <= W - bitlen(|m|) (the value fits the window).
+__device__ __forceinline__ int32_t fix_elem(int32_t m, int32_t e, int lsb, int& lost) {
+  int32_t mag = m < 0 ? -m : m;
+  int sh = e - lsb;
+  int32_t f;
+  if (sh >= 0) {
+    f = mag << sh;
+    lost = 0;
+  } else {
+    int s = -sh;
+    f = s >= 31 ? 0 : (mag >> s);
+    lost = (s >= 31) ? (mag != 0) : ((f << s) != mag);
+  }
+  return m < 0 ? -f : f;
+}
+
+// merge (Rb, Zb, Zeb) into the running (R, Z, Ze); false on lost headroom
+__device__ __forceinline__ bool merge_acc(int32_t& R, int64_t& Z, uint64_t& Ze, int32_t Rb, int64_t Zb, uint64_t Zeb) {
+  if (Rb == R_EMPTY) return true;
+  if (R == R_EMPTY) {
+    R = Rb; Z = Zb; Ze = Zeb;
+    return true;
+  }
+  int32_t Rn = max(R, Rb);
+  rescale(Z, Ze, Rn - R);
+  rescale(Zb, Zeb, Rn - Rb);
+  R = Rn;
+  Z += Zb;
+  Ze += Zeb;
+  return fits63(Z, Ze);
+}
+
+// Certified rounding of every channel of a row and the row's flag / tier-3 hand-off.
+// NR/N/Ne hold channels lane + 32 i.
+template <int CPL>
+__device__ void finalize_row(const Prob& P, int64_t r, int status, int32_t R, int64_t Z, uint64_t Ze,
+                             const int32_t* NR, const int64_t* N, const uint64_t* Ne, int lane) {
+  if (status == ST_DOMAIN) {
+    for (int c = lane; c < P.dv; c += 32) write_out(P, r, c, rnd_zero());
+    if (lane == 0) {
+      P.flags[r] = 2;
+      stat_add(P, STAT_DOMAIN_ROWS, 1);
+    }
+    return;
+  }
+  bool ok = status == ST_OK;
+  Rnd res[CPL];
+  if (ok) {
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      res[i] = rnd_zero();
+      int c = lane + 32 * i;
+      if (c >= P.dv || R == R_EMPTY || NR[i] == R_EMPTY) continue;
+      int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+      ok &= certify_ratio(N[i], Ne[i], (int64_t)NR[i] - P.FZ, Z, Ze, (int64_t)R - P.FZ, p, qmin, 127, res[i]);
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) {
+    if (lane == 0) {
+      push_tier3(P, r);
+      stat_add(P, STAT_TIER3_ROWS, 1);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    int c = lane + 32 * i;
+    if (c < P.dv) write_out(P, r, c, res[i]);
+  }
+  if (lane == 0) P.flags[r] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// tier 1
+// ---------------------------------------------------------------------------
+template <int CPL>
+__global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  uint64_t* sTA = (uint64_t*)smem;
+  uint64_t* sTB = sTA + 256;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    sTA[i] = g_ta64[i];
+    sTB[i] = g_tb64[i];
+  }
+  __syncthreads();
+
+  const int d = P.d, dv = P.dv, nw = simt_words(d);
+  unsigned char* ws = smem + 4096 + (size_t)warp * simt_warp_bytes(d, dv);
+  uint16_t* qbits = (uint16_t*)ws;
+  int32_t* qfix = (int32_t*)(ws + align16((size_t)d * 2));
+  uint8_t* qlost = (uint8_t*)((unsigned char*)qfix + align16((size_t)d * 4));
+  unsigned char* tile = (unsigned char*)qlost + align16((size_t)d);
+  size_t kt = (size_t)nw * 33 * 4, vt = (size_t)32 * dv * 2;
+  uint32_t* ktile = (uint32_t*)tile;
+  uint16_t* vtile = (uint16_t*)tile;
+  uint32_t* sM = (uint32_t*)(tile + align16(kt > vt ? kt : vt));
+  int32_t* sE = (int32_t*)(sM + 32);
+
+  const int64_t r = (int64_t)blockIdx.x * nwarps + warp;
+  if (r >= P.rows) return;
+  const int S = P.splits, s = blockIdx.y;
+  const int64_t L = row_len(P, r);
+  const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
+
+  // ---- q row: decode, leading exponent, block fixed point ----
+  int status = ST_OK;
+  int qlead = INT32_MIN;
+  for (int i = lane; i < d; i += 32) {
+    uint16_t b = P.q[r * d + i];
+    qbits[i] = b;
+    int32_t m, e;
+    if (!decode_bf16(b, m, e)) status = ST_DOMAIN;
+    if (m) qlead = max(qlead, e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1);
+  }
+  qlead = warp_max32(qlead);
+  status = warp_max32(status);
+  const int qlsb = qlead == INT32_MIN ? 0 : qlead + 1 - P.W;
+  for (int i = lane; i < d; i += 32) {
+    int32_t m, e;
+    decode_bf16(qbits[i], m, e);
+    int lost = 0;
+    qfix[i] = (m && status == ST_OK) ? fix_elem(m, e, qlsb, lost) : 0;
+    qlost[i] = (uint8_t)lost;
+  }
+  __syncwarp();
+
+  int32_t R = R_EMPTY;
+  int64_t Z = 0;
+  uint64_t Ze = 0;
+  int32_t NR[CPL];
+  int64_t N[CPL];
+  uint64_t Ne[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    NR[i] = R_EMPTY;
+    N[i] = 0;
+    Ne[i] = 0;
+  }
+  const int FZ = P.FZ;
+  unsigned long long n_exact = 0, n_wide = 0;
+
+  for (int64_t t0 = j0; t0 < j1 && status == ST_OK; t0 += 32) {
+    const int nt = (int)min((int64_t)32, j1 - t0);
+    const bool valid = lane < nt;
+    const int64_t myrow = valid ? key_row(P, r, t0 + lane) : 0;
+    // ---- K tile, transposed into 32-bit words [w][key] (row pitch 33: conflict-free) ----
+    for (int jj = 0; jj < nt; ++jj) {
+      int64_t kr = __shfl_sync(0xffffffffu, myrow, jj);
+      const uint16_t* src = P.k + kr * d;
+      for (int w = lane; w < nw; w += 32) {
+        uint32_t lo = src[2 * w];
+        uint32_t hi = (2 * w + 1 < d) ? src[2 * w + 1] : 0u;
+        ktile[w * 33 + jj] = lo | (hi << 16);
+      }
+    }
+    __syncwarp();
+    // ---- score, logit, weight of key `lane` ----
+    int kst = ST_OK;
+    uint32_t M = 0;
+    int32_t E = 0;
+    if (valid) {
+      int klead = INT32_MIN;
+      for (int w = 0; w < nw; ++w) {
+        uint32_t x = ktile[w * 33 + lane];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int32_t m, e;
+          if (!decode_bf16((x >> (16 * h)) & 0xFFFFu, m, e)) kst = ST_DOMAIN;
+          if (m) klead = max(klead, e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1);
+        }
+      }
+      Rnd t = rnd_zero();
+      if (kst == ST_OK) {
+        const int klsb = klead == INT32_MIN ? 0 : klead + 1 - P.W;
+        int64_t acc = 0;
+        uint64_t err = 0;
+        if (klead != INT32_MIN && qlead != INT32_MIN) {
+          for (int w = 0; w < nw; ++w) {
+            uint32_t x = ktile[w * 33 + lane];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              int i = 2 * w + h;
+              if (i >= d) break;
+              int32_t m, e;
+              decode_bf16((x >> (16 * h)) & 0xFFFFu, m, e);
+              int lost = 0;
+              int32_t kf = m ? fix_elem(m, e, klsb, lost) : 0;
+              int32_t qf = qfix[i];
+              acc += (int64_t)qf * kf;
+              err += (uint64_t)qlost[i] * (uint64_t)((kf < 0 ? -kf : kf) + lost) +
+                     (uint64_t)lost * (uint64_t)(qf < 0 ? -qf : qf);
+            }
+          }
+        }
+        int ls = logit_from_interval(acc, err, qlsb + klsb, P.am, P.ae, t);
+        if (ls == LOGIT_UNCERTIFIED) {
+          ++n_exact;
+          ExactScore sc;
+          score_clear(sc);
+          for (int i = 0; i < d; ++i) {
+            int32_t qm, qe, km, ke;
+            decode_bf16(qbits[i], qm, qe);
+            decode_bf16((ktile[(i >> 1) * 33 + lane] >> (16 * (i & 1))) & 0xFFFFu, km, ke);
+            if (qm && km) score_add(sc, qm * km, qe + ke);
+          }
+          ls = logit_exact(sc, P.am, P.ae, t);
+        }
+        if (ls == LOGIT_OVERFLOW) kst = ST_DOMAIN;
+      }
+      if (kst == ST_OK) {
+        int64_t E64;
+        int wst = weight_from_logit(t, sTA, sTB, M, E64);
+        if (wst == W_RISKY) {
+          ++n_wide;
+          wst = weight_from_logit_wide(t, g_ta128, g_tb128, M, E64);
+        }
+        if (wst != W_OK) kst = ST_TIER3;  // |t| >= 2^30 or a still-risky weight
+        E = (int32_t)E64;
+      }
+    }
+    kst = warp_max32(kst);
+    if (kst != ST_OK) {
+      status = kst;
+      break;
+    }
+    // ---- tile partial: Z ----
+    int32_t Rt = warp_max32(valid ? E + 24 : INT32_MIN);
+    int64_t zt = 0;
+    int zl = 0;
+    if (valid) zt = floor_shift((int64_t)M, E + FZ - Rt, zl);
+    int64_t Zt = warp_sum64(zt);
+    uint64_t Zet = (uint64_t)warp_sum64(zl);
+    if (valid) {
+      sM[lane] = M;
+      sE[lane] = E;
+    }
+    __syncwarp();
+    // ---- V tile (row-major) over the K tile's space ----
+    for (int jj = 0; jj < nt; ++jj) {
+      int64_t vr = __shfl_sync(0xffffffffu, myrow, jj);
+      const uint16_t* src = P.v + vr * dv;
+      for (int c = lane; c < dv; c += 32) vtile[jj * dv + c] = src[c];
+    }
+    __syncwarp();
+    bool ok = merge_acc(R, Z, Ze, Rt, Zt, Zet);
+    int vst = ST_OK;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      int c = lane + 32 * i;
+      if (c >= dv) continue;
+      int VE = INT32_MIN;
+      for (int jj = 0; jj < nt; ++jj) {
+        int32_t m, e;
+        if (!decode_bf16(vtile[jj * dv + c], m, e)) vst = ST_DOMAIN;
+        if (m) VE = max(VE, e + bitlen64((uint64_t)(m < 0 ? -m : m)));
+      }
+      if (VE == INT32_MIN) continue;
+      int32_t NRt = Rt + VE;
+      int64_t acc = 0;
+      uint64_t err = 0;
+      for (int jj = 0; jj < nt; ++jj) {
+        int32_t m, e;
+        decode_bf16(vtile[jj * dv + c], m, e);
+        if (!m) continue;
+        int lost;
+        acc += floor_shift((int64_t)sM[jj] * m, sE[jj] + e - NRt + FZ, lost);
+        err += (uint64_t)lost;
+      }
+      ok &= merge_acc(NR[i], N[i], Ne[i], NRt, acc, err);
+    }
+    vst = warp_max32(vst);
+    if (vst != ST_OK) status = vst;
+    if (!__all_sync(0xffffffffu, ok) && status == ST_OK) status = ST_TIER3;
+    __syncwarp();
+  }
+  status = warp_max32(status);
+  n_exact = (unsigned long long)warp_sum64((int64_t)n_exact);
+  n_wide = (unsigned long long)warp_sum64((int64_t)n_wide);
+  if (lane == 0) {
+    stat_add(P, STAT_SCORE_EXACT, n_exact);
+    stat_add(P, STAT_WEIGHT_WIDE, n_wide);
+    stat_add(P, STAT_PAIRS, (unsigned long long)(j1 - j0));
+  }
+
+  if (S == 1) {
+    finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+    return;
+  }
+  const int64_t pi = (int64_t)s * P.rows + r;
+  if (lane == 0) {
+    P.pR[pi] = R;
+    P.pZ[pi] = Z;
+    P.pZe[pi] = Ze;
+    P.pSt[pi] = (uint8_t)status;
+  }
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    int c = lane + 32 * i;
+    if (c >= dv) continue;
+    P.pNR[pi * dv + c] = NR[i];
+    P.pN[pi * dv + c] = N[i];
+    P.pNe[pi * dv + c] = Ne[i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// split combine: max reference exponent, rescale, integer sum (order-independent)
+// ---------------------------------------------------------------------------
+template <int CPL>
+__global__ void __launch_bounds__(128) combine_kernel(Prob P) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= P.rows) return;
+  const int S = P.splits, dv = P.dv;
+  int status = ST_OK;
+  int32_t R = R_EMPTY;
+  for (int s = 0; s < S; ++s) {
+    int64_t pi = (int64_t)s * P.rows + r;
+    status = max(status, (int)P.pSt[pi]);
+    if (P.pR[pi] != R_EMPTY) R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
+  }
+  int64_t Z = 0;
+  uint64_t Ze = 0;
+  bool ok = true;
+  if (status == ST_OK && R != R_EMPTY) {
+    for (int s = 0; s < S; ++s) {
+      int64_t pi = (int64_t)s * P.rows + r;
+      if (P.pR[pi] == R_EMPTY) continue;
+      int64_t z = P.pZ[pi];
+      uint64_t ze = P.pZe[pi];
+      rescale(z, ze, R - P.pR[pi]);
+      Z += z;
+      Ze += ze;
+    }
+    ok &= fits63(Z, Ze);
+  }
+  int32_t NR[CPL];
+  int64_t N[CPL];
+  uint64_t Ne[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    NR[i] = R_EMPTY;
+    N[i] = 0;
+    Ne[i] = 0;
+    int c = lane + 32 * i;
+    if (c >= dv || status != ST_OK) continue;
+    for (int s = 0; s < S; ++s) {
+      int32_t x = P.pNR[((int64_t)s * P.rows + r) * dv + c];
+      if (x != R_EMPTY) NR[i] = NR[i] == R_EMPTY ? x : max(NR[i], x);
+    }
+    if (NR[i] == R_EMPTY) continue;
+    for (int s = 0; s < S; ++s) {
+      int64_t pc = ((int64_t)s * P.rows + r) * dv + c;
+      int32_t x = P.pNR[pc];
+      if (x == R_EMPTY) continue;
+      int64_t n = P.pN[pc];
+      uint64_t ne = P.pNe[pc];
+      rescale(n, ne, NR[i] - x);
+      N[i] += n;
+      Ne[i] += ne;
+    }
+    ok &= fits63(N[i], Ne[i]);
+  }
+  if (!__all_sync(0xffffffffu, ok) && status == ST_OK) status = ST_TIER3;
+  finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+}
+
+// ---------------------------------------------------------------------------
+// tier 3: one block per listed row, wide fixed point over every key of the row
+// ---------------------------------------------------------------------------
+// Weights: the same certified logit (exact score when the window does not decide) and the
+// 128-bit exp2. Exponents are int64, so |t| up to 2^62 is handled; beyond that, or past the
+// reference's exponent-spread limit (reference.py:30, 116-118), the row is a domain error.
+// Accumulators: Z and each channel's N in Wide<LW> windows, Z in units 2^(R - FW) and N in units
+// 2^(R + 128 - FW) (|v| < 2^128), R the running reference exponent. Terms within about
+// 32 LW - 64 - key_log2 - 160 bits of the largest are kept exactly.
+constexpr int T3_THREADS = 128;
+constexpr int LW = 48;                 // 1536-bit windows
+constexpr int64_t MAX_SPREAD = 1ll << 20;
+
+__device__ __forceinline__ int64_t block_max64(int64_t x, int64_t* red) {
+  for (int o = 16; o; o >>= 1) x = max(x, (int64_t)__shfl_xor_sync(0xffffffffu, x, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  int64_t m = red[0];
+  for (int i = 1; i < T3_THREADS / 32; ++i) m = max(m, red[i]);
+  __syncthreads();
+  return m;
+}
+
+__global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
+  __shared__ uint32_t sM[T3_THREADS];
+  __shared__ int64_t sE[T3_THREADS];
+  __shared__ int64_t sRow[T3_THREADS];
+  __shared__ int64_t red[T3_THREADS / 32];
+  __shared__ int sStatus;
+  const int tid = threadIdx.x;
+  const int d = P.d, dv = P.dv;
+  const int64_t FW = 32ll * LW - 64 - P.key_log2;
+  const int count = *P.t3_count;
+
+  for (int item = blockIdx.x; item < count; item += gridDim.x) {
+    const int64_t r = P.t3_list[item];
+    const int64_t L = row_len(P, r);
+    // q row
+    int qlead = INT32_MIN;
+    int qbad = 0;
+    for (int i = 0; i < d; ++i) {
+      int32_t m, e;
+      if (!decode_bf16(P.q[r * d + i], m, e)) qbad = 1;
+      if (m) qlead = max(qlead, e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1);
+    }
+    const int qlsb = qlead == INT32_MIN ? 0 : qlead + 1 - P.W;
+    if (tid == 0) sStatus = qbad ? ST_DOMAIN : ST_OK;
+    __syncthreads();
+
+    for (int c0 = 0; c0 < dv; c0 += T3_THREADS) {
+      const int c = c0 + tid;
+      Wide<LW> Zw, Nw;
+      Zw.clear();
+      Nw.clear();
+      uint64_t Zerr = 0, Nerr = 0;
+      int64_t R = INT64_MIN, Emin = INT64_MAX, Emax = INT64_MIN;
+      bool has_n = false;
+      // sStatus is written only between the top of an iteration and its first barrier, and read
+      // only after that barrier, so every thread sees the same value and leaves together.
+      for (int64_t t0 = 0; t0 < L; t0 += T3_THREADS) {
+        const int nt = (int)min((int64_t)T3_THREADS, L - t0);
+        int st = ST_OK;
+        int64_t E = 0;
+        uint32_t M = 0;
+        if (tid < nt) {
+          const int64_t kr = key_row(P, r, t0 + tid);
+          sRow[tid] = kr;
+          const uint16_t* kp = P.k + kr * d;
+          int klead = INT32_MIN;
+          for (int i = 0; i < d; ++i) {
+            int32_t m, e;
+            if (!decode_bf16(kp[i], m, e)) st = ST_DOMAIN;
+            if (m) klead = max(klead, e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1);
+          }
+          const uint16_t* vp = P.v + kr * dv;
+          for (int i = 0; i < dv; ++i) {
+            int32_t m, e;
+            if (!decode_bf16(vp[i], m, e)) st = ST_DOMAIN;
+          }
+          Rnd t = rnd_zero();
+          if (st == ST_OK) {
+            const int klsb = klead == INT32_MIN ? 0 : klead + 1 - P.W;
+            int64_t acc = 0;
+            uint64_t err = 0;
+            if (klead != INT32_MIN && qlead != INT32_MIN) {
+              for (int i = 0; i < d; ++i) {
+                int32_t qm, qe, km, ke;
+                decode_bf16(P.q[r * d + i], qm, qe);
+                decode_bf16(kp[i], km, ke);
+                int ql = 0, kl = 0;
+                int32_t qf = qm ? fix_elem(qm, qe, qlsb, ql) : 0;
+                int32_t kf = km ? fix_elem(km, ke, klsb, kl) : 0;
+                acc += (int64_t)qf * kf;
+                err += (uint64_t)ql * (uint64_t)((kf < 0 ? -kf : kf) + kl) + (uint64_t)kl * (uint64_t)(qf < 0 ? -qf : qf);
+              }
+            }
+            int ls = logit_from_interval(acc, err, qlsb + klsb, P.am, P.ae, t);
+            if (ls == LOGIT_UNCERTIFIED) {
+              ExactScore sc;
+              score_clear(sc);
+              for (int i = 0; i < d; ++i) {
+                int32_t qm, qe, km, ke;
+                decode_bf16(P.q[r * d + i], qm, qe);
+                decode_bf16(kp[i], km, ke);
+                if (qm && km) score_add(sc, qm * km, qe + ke);
+              }
+              ls = logit_exact(sc, P.am, P.ae, t);
+            }
+            if (ls == LOGIT_OVERFLOW) st = ST_DOMAIN;
+          }
+          if (st == ST_OK) {
+            int ws = weight_from_logit_wide(t, g_ta128, g_tb128, M, E);
+            if (ws == W_HUGE) {
+              // integer t with |t| >= 2^30: w = 2^t exactly
+              int lead = t.qe + bitlen64(t.q) - 1;
+              if (lead >= 62) {
+                st = ST_DOMAIN;
+              } else {
+                int64_t n = (int64_t)(t.q << t.qe);
+                M = 1u << 23;
+                E = (t.neg ? -n : n) - 23;
+              }
+            } else if (ws == W_RISKY) {
+              st = ST_TIER3;  // unresolved (a 2^-97 event)
+            }
+          }
+          sM[tid] = M;
+          sE[tid] = E;
+        }
+        // block-wide status
+        if (st != ST_OK) atomicMax(&sStatus, st);
+        __syncthreads();
+        const int stc = sStatus;
+        if (stc != ST_OK) break;
+        const int64_t tmax = block_max64(tid < nt ? sE[tid] + 24 : INT64_MIN, red);
+        const int64_t tmin = -block_max64(tid < nt ? -sE[tid] : INT64_MIN, red);
+        Emax = max(Emax, tmax - 24);
+        Emin = min(Emin, tmin);
+        if (Emax - Emin > MAX_SPREAD) {  // uniform: both are block reductions
+          if (tid == 0) sStatus = ST_DOMAIN;
+          break;
+        }
+        if (tmax > R) {
+          if (R != INT64_MIN) {
+            Zw.normalize();
+            Nw.normalize();
+            int64_t sft = tmax - R;
+            bool l1 = Zw.shr(sft), l2 = Nw.shr(sft);
+            Zerr = sft >= 64 ? (Zerr != 0) : ((Zerr >> sft) + ((Zerr & ((1ull << sft) - 1)) != 0));
+            Nerr = sft >= 64 ? (Nerr != 0) : ((Nerr >> sft) + ((Nerr & ((1ull << sft) - 1)) != 0));
+            Zerr += l1;
+            Nerr += l2;
+          }
+          R = tmax;
+        }
+        for (int jj = 0; jj < nt; ++jj) {
+          const int64_t Ej = sE[jj];
+          Zw.add((int64_t)sM[jj], Ej - (R - FW), Zerr);
+          if (c < dv) {
+            int32_t m, e;
+            decode_bf16(P.v[sRow[jj] * dv + c], m, e);
+            if (m) {
+              has_n = true;
+              Nw.add((int64_t)sM[jj] * m, Ej + e - (R + 128 - FW), Nerr);
+            }
+          }
+        }
+        __syncthreads();
+      }
+      __syncthreads();
+      const int st = sStatus;
+      __syncthreads();  // every thread has read sStatus before any finalisation writes it
+      if (st == ST_OK && c < dv) {
+        Rnd res = rnd_zero();
+        bool ok = true;
+        if (R != INT64_MIN && has_n) {
+          Zw.normalize();
+          Nw.normalize();
+          uint32_t za[LW + 1], zb[LW + 1], na[LW + 1];
+          Zw.magnitude(za);
+          for (int i = 0; i <= LW; ++i) zb[i] = za[i];
+          big_add_u64(zb, LW + 1, Zerr);
+          bool nneg = Nw.magnitude(na);
+          // N interval [N, N + Nerr]
+          uint32_t nlo[LW + 1], nhi[LW + 1];
+          const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+          Rnd rl, rh;
+          if (!nneg) {
+            for (int i = 0; i <= LW; ++i) nlo[i] = nhi[i] = na[i];
+            big_add_u64(nhi, LW + 1, Nerr);
+            rl = round_ratio_big<LW + 4>(nlo, zb, LW + 1, 128, 0, p, qmin, 127);
+            rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
+          } else {
+            // N = -|N|; the high end N + Nerr may cross zero
+            for (int i = 0; i <= LW; ++i) nlo[i] = na[i];
+            rl = round_ratio_big<LW + 4>(nlo, za, LW + 1, 128, 1, p, qmin, 127);
+            // |N| - Nerr, or Nerr - |N| if that is negative
+            uint32_t e[LW + 1];
+            for (int i = 0; i <= LW; ++i) e[i] = 0;
+            big_add_u64(e, LW + 1, Nerr);
+            if (big_cmp(na, e, LW + 1) >= 0) {
+              for (int i = 0; i <= LW; ++i) nhi[i] = na[i];
+              big_sub(nhi, e, LW + 1);
+              rh = round_ratio_big<LW + 4>(nhi, zb, LW + 1, 128, 1, p, qmin, 127);
+            } else {
+              for (int i = 0; i <= LW; ++i) nhi[i] = e[i];
+              big_sub(nhi, na, LW + 1);
+              rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
+            }
+          }
+          ok = rnd_eq(rl, rh);
+          res = rl;
+          if (res.q == 0) res.neg = 0;
+        }
+        if (ok) {
+          write_out(P, r, c, res);
+        } else {
+          atomicMax(&sStatus, ST_TIER3);
+        }
+      }
+      __syncthreads();
+      const int st2 = sStatus;
+      __syncthreads();  // read before the next channel block can write it
+      if (st2 != ST_OK) break;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const int st = sStatus;
+      if (st == ST_DOMAIN) {
+        P.flags[r] = 2;
+        stat_add(P, STAT_DOMAIN_ROWS, 1);
+      } else if (st == ST_TIER3) {
+        P.flags[r] = 1;
+        stat_add(P, STAT_UNRESOLVED, 1);
+      } else {
+        P.flags[r] = 0;
+      }
+    }
+    const int stf = sStatus;
+    if (stf == ST_DOMAIN)
+      for (int c = tid; c < dv; c += T3_THREADS) write_out(P, r, c, rnd_zero());
+    __syncthreads();  // the next row resets sStatus
+  }
+}
+
+// ---------------------------------------------------------------------------
+// launchers (called from ea_api.cu)
+// ---------------------------------------------------------------------------
+template <int CPL>
+static cudaError_t launch_simt_cpl(const Prob& P, int warps, cudaStream_t st) {
+  size_t smem = simt_smem_bytes(P.d, P.dv, warps);
+  cudaError_t e = cudaFuncSetAttribute(simt_split_kernel<CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((P.rows + warps - 1) / warps), (unsigned)P.splits);
+  simt_split_kernel<CPL><<<grid, warps * 32, smem, st>>>(P);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || P.splits == 1) return e;
+  combine_kernel<CPL><<<(unsigned)((P.rows + 3) / 4), 128, 0, st>>>(P);
+  return cudaGetLastError();
+}
+
+int simt_warps_for(int d, int dv) {
+  int w = 4;
+  while (w > 1 && simt_smem_bytes(d, dv, w) > 200 * 1024) --w;
+  return w;
+}
+
+cudaError_t launch_simt(const Prob& P, cudaStream_t st) {
+  int warps = simt_warps_for(P.d, P.dv);
+  if (P.dv <= 32) return launch_simt_cpl<1>(P, warps, st);
+  if (P.dv <= 64) return launch_simt_cpl<2>(P, warps, st);
+  if (P.dv <= 128) return launch_simt_cpl<4>(P, warps, st);
+  return launch_simt_cpl<8>(P, warps, st);
+}
+
+cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st) {
+  tier3_kernel<<<blocks, T3_THREADS, 0, st>>>(P);
+  return cudaGetLastError();
+}
+
+}  // namespace ea

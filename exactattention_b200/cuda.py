@@ -1,0 +1,200 @@
+"""CUDA entry points of certified ExactAttention on B200.
+
+attention_cuda  numpy in / numpy out through the host-pointer C ABI `ea_attention_cuda`: the
+                drop-in for the reference's `exactattn.cpu.attention_cpu` (src/exactattn/cpu.py:
+                70-109), same signature and return value. Flagged rows are never recomputed on
+                the host: every tier runs on the GPU.
+launch          torch device tensors in, device tensors out, asynchronous on the current stream,
+                through `ea_launch_cuda`: the counterpart of the reference's device-level
+                `triton_kernels.launch` (src/exactattn/triton_kernels.py:1324-1351), with CSR,
+                per-row key ranges or a paged KV cache as the mask.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from .formats import ExactAttentionDomainError
+
+
+@dataclass
+class CudaStats:
+    """Per-call counters (the reference's CpuStats, cpu.py:54-59, plus the device tiers)."""
+    score_fallbacks: int = 0      # scores the window could not certify, recomputed exactly
+    weight_fallbacks: int = 0     # weights recomputed by the 128-bit exp2
+    final_fallbacks: int = 0      # rows sent to the wide-integer tier
+    rows: int = 0
+    flagged_rows: int = 0         # rows with flag != 0 (domain errors)
+    host_fallbacks: int = 0       # always 0
+
+
+def attention_cuda(q, k, v, alpha, row_ptr=None, key_idx=None, out="bf16", acc_bits=64, tile=64,
+                   splits=1, order_seed=0, threads=None, stats: CudaStats | None = None,
+                   fallback=True):
+    """q: (rows, d) bf16 bits; k: (n, d); v: (n, dv). The mask is CSR (row_ptr, key_idx); None
+    means every row attends every key. Returns (out, flags) like attention_cpu; raises
+    ExactAttentionDomainError if any row saw a NaN/inf input or an infinite logit.
+    `fallback` is accepted for compatibility: nothing is recomputed on the host."""
+    lib = _lib.load()
+    q = np.ascontiguousarray(q, dtype=np.uint16)
+    k = np.ascontiguousarray(k, dtype=np.uint16)
+    v = np.ascontiguousarray(v, dtype=np.uint16)
+    rows, d = q.shape
+    n, dv = v.shape
+    if k.shape[0] != n or k.shape[1] != d:
+        raise ValueError("k must be (n, d) with v (n, dv)")
+    if row_ptr is not None:
+        row_ptr = np.ascontiguousarray(row_ptr, dtype=np.int64)
+        key_idx = np.ascontiguousarray(key_idx, dtype=np.int64)
+        if row_ptr.shape[0] != rows + 1:
+            raise ValueError("row_ptr must have rows + 1 entries")
+        if key_idx.size and (key_idx.min() < 0 or key_idx.max() >= n):
+            raise ValueError("key_idx out of range")
+    fp32 = out == "fp32"
+    if out not in ("bf16", "fp32"):
+        raise ValueError("out must be 'bf16' or 'fp32'")
+    res = np.zeros((rows, dv), dtype=np.float32 if fp32 else np.uint16)
+    flags = np.zeros(rows, dtype=np.uint8)
+    st = np.zeros(3, dtype=np.int64)
+    rc = lib.ea_attention_cuda(q.ctypes.data, rows, d, k.ctypes.data, v.ctypes.data, n, dv,
+                               ctypes.c_float(float(np.float32(alpha))),
+                               row_ptr.ctypes.data if row_ptr is not None else None,
+                               key_idx.ctypes.data if row_ptr is not None else None,
+                               int(fp32), acc_bits, tile, splits, order_seed, threads or os.cpu_count() or 1,
+                               res.ctypes.data, flags.ctypes.data, st.ctypes.data)
+    _lib.check(rc, "ea_attention_cuda")
+    if stats is not None:
+        stats.score_fallbacks += int(st[0])
+        stats.weight_fallbacks += int(st[1])
+        stats.final_fallbacks += int(st[2])
+        stats.rows += rows
+        stats.flagged_rows += int((flags != 0).sum())
+    if np.any(flags == 2):
+        raise ExactAttentionDomainError("non-finite input or logit overflow")
+    if np.any(flags == 1):
+        raise RuntimeError("rows left uncertified by every device tier (library bug)")
+    return res, flags
+
+
+def round_ratio(a: int, b: int, E: int, neg: bool, fp32: bool) -> tuple[float, bool]:
+    """The reference's `cpu.round_ratio` (cpu.py:112-117), evaluated by the device helper."""
+    lib = _lib.load()
+    ov = ctypes.c_int(0)
+    f = lib.ea_round_ratio_cuda(a >> 64, a & ((1 << 64) - 1), b >> 64, b & ((1 << 64) - 1), E, int(neg),
+                                int(fp32), ctypes.byref(ov))
+    return float(f), bool(ov.value)
+
+
+# ---------------------------------------------------------------------------
+# torch device API
+# ---------------------------------------------------------------------------
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
+           seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
+           out_tensor=None, flags=None, stats=None, stream=None):
+    """Device-level launch, no host sync. q (rows, d), k, v: torch tensors of bf16 bits (any
+    16-bit dtype) on one CUDA device. One mask: CSR (row_ptr, key_idx int64), RANGE
+    (kv_base, kv_len int64: row r attends k rows kv_base[r] + [0, kv_len[r])), or PAGED
+    (page_table (B, max_pages) int32, seq_lens (B,) int32, page_size, q_heads, kv_heads; k/v
+    laid out (pages, kv_heads, page_size, d); row r is sequence r // q_heads, head r % q_heads),
+    or HYBRID (kv_base/kv_len and row_ptr/key_idx together: the range, then the CSR list).
+    max_row_keys bounds every row's key count (required for RANGE/PAGED without a host sync).
+    Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
+    import torch
+
+    lib = _lib.load()
+    dev = q.device
+    if dev.type != "cuda":
+        raise RuntimeError("launch needs CUDA tensors (there is no CPU path)")
+    rows, d = q.shape[0], q.shape[-1]
+    dv = v.shape[-1]
+    if out_tensor is None:
+        out_tensor = torch.empty((rows, dv), dtype=torch.int32 if out == "fp32" else torch.int16, device=dev)
+    if flags is None:
+        flags = torch.empty(rows, dtype=torch.uint8, device=dev)
+    a = _lib.LaunchArgs()
+    a.q, a.rows, a.d = q.data_ptr(), rows, d
+    a.k, a.v, a.nkeys, a.dv = k.data_ptr(), v.data_ptr(), k.numel() // d, dv
+    a.alpha = float(np.float32(alpha))
+    if row_ptr is not None and kv_len is not None:
+        a.mask_kind = _lib.EA_MASK_HYBRID
+        a.row_ptr, a.key_idx = _ptr(row_ptr), _ptr(key_idx)
+        a.kv_base, a.kv_len = _ptr(kv_base), _ptr(kv_len)
+        if max_row_keys is None:
+            max_row_keys = int((kv_len + row_ptr[1:] - row_ptr[:-1]).max().item()) if rows else 1
+    elif row_ptr is not None:
+        a.mask_kind = _lib.EA_MASK_CSR
+        a.row_ptr, a.key_idx = _ptr(row_ptr), _ptr(key_idx)
+        if max_row_keys is None:
+            max_row_keys = int((row_ptr[1:] - row_ptr[:-1]).max().item()) if rows else 1
+    elif kv_len is not None:
+        a.mask_kind = _lib.EA_MASK_RANGE
+        a.kv_base, a.kv_len = _ptr(kv_base), _ptr(kv_len)
+        if max_row_keys is None:
+            max_row_keys = int(kv_len.max().item()) if rows else 1
+    elif page_table is not None:
+        a.mask_kind = _lib.EA_MASK_PAGED
+        a.page_table, a.seq_lens = _ptr(page_table), _ptr(seq_lens)
+        a.page_size, a.max_pages = int(page_size), int(page_table.shape[-1])
+        a.q_heads, a.kv_heads = int(q_heads), int(kv_heads)
+        if max_row_keys is None:
+            max_row_keys = int(seq_lens.max().item()) if seq_lens.numel() else 1
+    else:
+        raise ValueError("launch needs a mask: row_ptr/key_idx, kv_base/kv_len or page_table/seq_lens")
+    a.max_row_keys = int(max(1, max_row_keys))
+    a.fp32_out = int(out == "fp32")
+    a.splits = int(splits)
+    a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
+    a.stats = _ptr(stats)
+    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
+    return out_tensor, flags
+
+
+def reserve_workspace(rows: int, splits: int, dv: int) -> None:
+    _lib.check(_lib.load().ea_reserve_workspace(rows, splits, dv), "ea_reserve_workspace")
+
+
+def release() -> None:
+    _lib.load().ea_cuda_release()
+
+
+def attention_cuda_ranges(q, k, v, alpha, kv_base, kv_len, max_row_keys=None, out="bf16", splits=1,
+                          stats: CudaStats | None = None, out_buf=None, flags_buf=None):
+    """Host buffers through `ea_attention_cuda_ranges`: row r attends k rows
+    kv_base[r] + [0, kv_len[r]). Host arrays may be pinned (torch pin_memory) numpy views.
+    Returns (out, flags); raises like attention_cuda."""
+    lib = _lib.load()
+    rows, d = q.shape
+    n, dv = v.shape
+    fp32 = out == "fp32"
+    res = out_buf if out_buf is not None else np.zeros((rows, dv), dtype=np.float32 if fp32 else np.uint16)
+    flags = flags_buf if flags_buf is not None else np.zeros(rows, dtype=np.uint8)
+    st = np.zeros(3, dtype=np.int64)
+    mk = int(max_row_keys if max_row_keys is not None else (kv_len.max() if rows else 1))
+    rc = lib.ea_attention_cuda_ranges(q.ctypes.data, rows, d, k.ctypes.data, v.ctypes.data, n, dv,
+                                      ctypes.c_float(float(np.float32(alpha))), kv_base.ctypes.data,
+                                      kv_len.ctypes.data, mk, int(fp32), splits, res.ctypes.data, flags.ctypes.data,
+                                      st.ctypes.data)
+    _lib.check(rc, "ea_attention_cuda_ranges")
+    if stats is not None:
+        stats.score_fallbacks += int(st[0])
+        stats.weight_fallbacks += int(st[1])
+        stats.final_fallbacks += int(st[2])
+        stats.rows += rows
+        stats.flagged_rows += int((flags != 0).sum())
+    if np.any(flags == 2):
+        raise ExactAttentionDomainError("non-finite input or logit overflow")
+    if np.any(flags == 1):
+        raise RuntimeError("rows left uncertified by every device tier (library bug)")
+    return res, flags

@@ -1,0 +1,111 @@
+/* C ABI of the B200 (sm_100a) certified ExactAttention library, libexactattn_cuda.so.
+ *
+ * Every entry point returns bits identical to the spec's (docs/SPEC.md of the reference) or a
+ * per-row domain-error flag. Rows that the fast tier cannot certify are recomputed on the GPU
+ * (a wide-integer tier); nothing falls back to the CPU.
+ *
+ * Return codes: 0 OK; -1 bad dimensions; -2 acc_bits not 64/128; -3 non-finite alpha;
+ * -4 CUDA error; -5 unsupported layout.
+ * Per-row flags: 0 certified, 2 NaN/inf input or an fp32 logit overflow (the reference raises
+ * ExactAttentionDomainError), 1 never expected (no device tier certified the row).
+ */
+#ifndef EXACTATTN_CUDA_H
+#define EXACTATTN_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host-pointer entry point: the drop-in for the reference's
+ *   int ea_attention_cpu(const uint16_t* q, int64_t rows, int d, const uint16_t* k,
+ *       const uint16_t* v, int64_t nkeys, int dv, float alpha, const int64_t* row_ptr,
+ *       const int64_t* key_idx, int fp32_out, int acc_bits, int tile, int splits,
+ *       uint64_t order_seed, int nthreads, void* out, uint8_t* flags, int64_t* stats)
+ * (reference csrc/exact_attention_cpu.cpp:585-588, bound by src/exactattn/cpu.py:33-41).
+ * Same argument order and meaning. q (rows, d), k (nkeys, d), v (nkeys, dv) are bf16 bit
+ * patterns; row r attends key_idx[row_ptr[r] .. row_ptr[r+1]) (row_ptr == NULL: every key).
+ * acc_bits, tile, order_seed and nthreads are accepted for compatibility: the output does not
+ * depend on them. splits partitions each row's keys into KV splits merged exactly.
+ * out: rows x dv uint16 (bf16) or float (fp32_out). flags: rows bytes.
+ * stats[0..2] += (scores recomputed exactly, weights recomputed with the 128-bit exp2,
+ * rows sent to the wide tier). Synchronous. */
+int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
+                      int64_t nkeys, int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx,
+                      int fp32_out, int acc_bits, int tile, int splits, uint64_t order_seed, int nthreads,
+                      void* out, uint8_t* flags, int64_t* stats);
+
+/* Host-pointer entry point for contiguous key ranges (causal prefill, prefixes, decode):
+ * row r attends k rows kv_base[r] .. kv_base[r] + kv_len[r]. The compact form of the CSR mask
+ * above (no reference counterpart: the reference's C ABI takes CSR only); same outputs.
+ * max_row_keys >= every kv_len[r]. Synchronous; stats as ea_attention_cuda. */
+int ea_attention_cuda_ranges(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
+                             int64_t nkeys, int dv, float alpha, const int64_t* kv_base, const int64_t* kv_len,
+                             int64_t max_row_keys, int fp32_out, int splits, void* out, uint8_t* flags,
+                             int64_t* stats);
+
+/* RN-even of (a / b) * 2^E into fp32 (fp32 != 0) or bf16; a, b given as (hi, lo) 64-bit
+ * halves. Mirrors the reference's test export ea_round_ratio
+ * (csrc/exact_attention_cpu.cpp:630-638); evaluated on the GPU. */
+float ea_round_ratio_cuda(uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo, int E, int neg, int fp32,
+                          int* overflow);
+
+/* Mask layouts of the device-pointer entry point. */
+/* HYBRID: row r attends kv_base[r] + [0, kv_len[r]) followed by key_idx[row_ptr[r] .. row_ptr[r+1])
+ * (a shared prefix plus a per-row list: tree verification). */
+enum { EA_MASK_CSR = 0, EA_MASK_RANGE = 1, EA_MASK_PAGED = 2, EA_MASK_HYBRID = 3 };
+
+#define EA_STATS_LEN 8
+/* stats slots (int64, accumulated): 0 scores recomputed exactly, 1 weights by the 128-bit exp2,
+ * 2 rows sent to the wide tier, 3 domain-error rows, 4 unresolved rows (flag 1; never
+ * expected), 5 (row, key) pairs processed, 6 host fallbacks (always 0). */
+
+typedef struct ea_launch {
+  /* inputs, device pointers */
+  const uint16_t* q; /* (rows, d) */
+  int64_t rows;
+  int d;
+  const uint16_t* k; /* key rows of d values (CSR/RANGE: (nkeys, d); PAGED: (pages, kv_heads, page_size, d)) */
+  const uint16_t* v; /* value rows of dv values, same row indexing as k */
+  int64_t nkeys;
+  int dv;
+  float alpha;
+  /* mask */
+  int mask_kind;
+  const int64_t* row_ptr; /* CSR: rows + 1 */
+  const int64_t* key_idx; /* CSR */
+  const int64_t* kv_base; /* RANGE: row r attends k rows kv_base[r] .. kv_base[r] + kv_len[r] */
+  const int64_t* kv_len;
+  const int32_t* page_table; /* PAGED: (batch, max_pages) physical page ids */
+  const int32_t* seq_lens;   /* PAGED: (batch,) keys per sequence */
+  int page_size, max_pages, q_heads, kv_heads; /* PAGED: row r = seq (r / q_heads), head r % q_heads */
+  int64_t max_row_keys; /* >= every row's key count (sets the fixed-point headroom) */
+  int fp32_out;
+  int splits;
+  /* outputs, device pointers */
+  void* out;      /* (rows, dv) uint16 or float */
+  uint8_t* flags; /* (rows,) */
+  int64_t* stats; /* EA_STATS_LEN int64 counters, accumulated; may be NULL */
+} ea_launch_t;
+
+/* Device-pointer entry point: asynchronous on `stream` (a cudaStream_t, NULL = default).
+ * Uses a library-owned workspace on the current device (grown outside any stream capture by
+ * ea_reserve_workspace or on first use). The torch-tensor API builds on this. */
+int ea_launch_cuda(const ea_launch_t* args, void* stream);
+
+/* Sizes the workspace for up to `rows` rows, `splits` splits and dv channels on the current
+ * device; call before capturing a launch in a CUDA graph. */
+int ea_reserve_workspace(int64_t rows, int splits, int dv);
+
+/* Frees the workspace of every device. */
+void ea_cuda_release(void);
+
+/* Last CUDA error string of this library (thread-local). */
+const char* ea_cuda_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXACTATTN_CUDA_H */

@@ -1,0 +1,49 @@
+"""The C-ABI library builds for sm_100a, loads, and exports every symbol include/*.h declares.
+No compute calls: runs without a GPU."""
+
+import ctypes
+import os
+import re
+
+from exactattention_b200 import _lib
+
+ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+
+
+def declared_functions():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            names |= set(re.findall(r"^\s*(?:int|float|void|const char\*)\s+(ea_\w+)\s*\(", src, re.M))
+    return names
+
+
+def test_library_exports_every_declared_symbol(cuda_lib):
+    names = declared_functions()
+    assert {"ea_attention_cuda", "ea_launch_cuda", "ea_round_ratio_cuda", "ea_synth_fill"} <= names
+    for n in names:
+        assert hasattr(cuda_lib, n), n
+    assert set(_lib.EXPORTS) <= names
+
+
+def test_launch_struct_layout_matches_header(cuda_lib, tmp_path):
+    """The ctypes mirror of ea_launch_t has the C compiler's size and field offsets."""
+    import subprocess
+
+    fields = [f[0] for f in _lib.LaunchArgs._fields_]
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "exactattn_cuda.h"\nint main(void){'
+                   'printf("%zu", sizeof(ea_launch_t));'
+                   + "".join(f'printf(" %zu", offsetof(ea_launch_t, {f}));' for f in fields) + "return 0;}\n")
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), "-o", str(exe), str(src)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(_lib.LaunchArgs)
+    assert vals[1:] == [getattr(_lib.LaunchArgs, f).offset for f in fields]
+
+
+def test_build_targets_sm100a():
+    from exactattention_b200 import build
+
+    assert "arch=compute_100a,code=sm_100a" in build.FLAGS

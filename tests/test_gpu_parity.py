@@ -1,0 +1,335 @@
+"""Parity of the CUDA path with the oracle and the reference's golden vectors (B200 only).
+
+Every comparison is bit-exact: the spec defines one correct output per input.
+"""
+
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+from gen import KINDS, bf16
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def ea(cuda_lib):
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need CUDA"
+    import exactattention_b200 as ea
+
+    return ea
+
+
+# ---------------------------------------------------------------------------
+# golden vectors of the reference
+# ---------------------------------------------------------------------------
+
+def test_config1_golden(ea):
+    z = np.load(os.path.join(GOLDEN, "c1.npz"))
+    out = ea.attention(z["q"], z["k"], z["v"], z["alpha"])
+    assert sha(out) == "27b27a491d2064580a707b042c162d42e3a5f2ca4232043d3de870c840922843"
+    assert np.array_equal(out, z["out"])
+    out32 = ea.attention(z["q"], z["k"], z["v"], z["alpha"], out="fp32")
+    assert np.array_equal(out32.view(np.uint32), z["out32"].view(np.uint32))
+
+
+def test_small_cases_golden(ea):
+    z = np.load(os.path.join(GOLDEN, "small_cases.npz"))
+    for i in range(int(z["count"])):
+        key = f"case{i}"
+        fmt = str(z[key + "_fmt"])
+        out = ea.attention(z[key + "_q"], z[key + "_k"], z[key + "_v"], z[key + "_alpha"], mask=z[key + "_mask"],
+                           out=fmt)
+        exp = z[key + "_out"]
+        if fmt == "fp32":
+            assert np.array_equal(out.view(np.uint32), exp.view(np.uint32)), key
+        else:
+            assert np.array_equal(out, exp), key
+
+
+@pytest.mark.parametrize("splits", [1, 8])
+def test_fixture_heads_sha(ea, splits):
+    """The reference's portable fixture (scripts/fixture.py check): every causal row of two
+    real Qwen3-0.6B heads hashes to the recorded SHA-256."""
+    from exactattention_b200.cuda import CudaStats, attention_cuda
+
+    z = np.load(os.path.join(GOLDEN, "qwen3_heads.npz"))
+    exp = json.load(open(os.path.join(GOLDEN, "qwen3_heads.json")))
+    for key, info in exp["heads"].items():
+        q, k, v, a = z["q_" + key], z["k_" + key], z["v_" + key], np.float32(z["alpha_" + key])
+        L = q.shape[0]
+        kv = np.arange(1, L + 1)
+        rp = np.concatenate([[0], np.cumsum(kv)]).astype(np.int64)
+        ki = np.concatenate([np.arange(n) for n in kv]).astype(np.int64)
+        st = CudaStats()
+        out, flags = attention_cuda(q, k, v, a, rp, ki, splits=splits, stats=st)
+        assert sha(out) == info["sha256"], key
+        assert not flags.any() and st.host_fallbacks == 0
+
+
+# ---------------------------------------------------------------------------
+# random inputs vs the exact oracle
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("out", ["bf16", "fp32"])
+def test_random_rows_match_oracle(ea, kind, out):
+    from oracle import exact
+
+    from exactattention_b200.cuda import attention_cuda
+
+    rng = np.random.default_rng(hash((kind, out)) & 0xFFFF)
+    for trial in range(3):
+        d = int(rng.choice([16, 64, 128]))
+        dv = int(rng.choice([8, 32, 64, 128]))
+        n = int(rng.integers(1, 300))
+        vkind = ["normal", "wide", "dupes"][trial]
+        Q, K, V = bf16(rng, (3, d), kind), bf16(rng, (n, d), kind), bf16(rng, (n, dv), vkind)
+        alpha = exact.default_alpha(d)
+        splits = int(rng.integers(1, 9))
+        got, flags = attention_cuda(Q, K, V, alpha, out=out, splits=splits)
+        exp = exact.attention(Q, K, V, alpha, out=out)
+        assert not flags.any()
+        if out == "fp32":
+            assert np.array_equal(got.view(np.uint32), exp.view(np.uint32)), (kind, trial)
+        else:
+            assert np.array_equal(got, exp), (kind, trial)
+
+
+def test_schedule_invariance(ea):
+    """Any split count and any key order give the same bits (SPEC 5.3; the reference's
+    test_schedule_invariance_many_schedules)."""
+    from exactattention_b200.cuda import attention_cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(11)
+    d, dv, n, r = 128, 64, 700, 8
+    Q, K, V = bf16(rng, (r, d), "outlier"), bf16(rng, (n, d), "outlier"), bf16(rng, (n, dv))
+    alpha = exact.default_alpha(d)
+    base, flags = attention_cuda(Q, K, V, alpha)
+    assert not flags.any()
+    for splits in (2, 3, 7, 16, 64):
+        for perm_seed in (0, 1):
+            perm = np.random.default_rng(perm_seed).permutation(n)
+            rp = np.arange(r + 1, dtype=np.int64) * n
+            ki = np.tile(perm, r).astype(np.int64)
+            got, fl = attention_cuda(Q, K, V, alpha, rp, ki, splits=splits)
+            assert not fl.any() and np.array_equal(got, base), (splits, perm_seed)
+    for i in range(2):
+        assert np.array_equal(base[i], exact.attention_row(Q[i], K, V, alpha))
+
+
+def test_tree_mask_csr_equals_sequential(ea):
+    """Each tree node (prefix + ancestors) equals sequential decoding of its root-to-node path."""
+    from exactattention_b200.cuda import attention_cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(5)
+    d, dv, P, T = 64, 32, 300, 15
+    parent = [-1] + [int(rng.integers(0, i)) for i in range(1, T)]
+    Kp, Vp = bf16(rng, (P, d)), bf16(rng, (P, dv))
+    Kt, Vt, Qt = bf16(rng, (T, d)), bf16(rng, (T, dv)), bf16(rng, (T, d))
+    K, V = np.concatenate([Kp, Kt]), np.concatenate([Vp, Vt])
+    rows = []
+    for i in range(T):
+        path, x = [], i
+        while x != -1:
+            path.append(P + x)
+            x = parent[x]
+        rows.append(np.concatenate([np.arange(P), np.array(path)]))
+    rp = np.concatenate([[0], np.cumsum([len(x) for x in rows])]).astype(np.int64)
+    ki = np.concatenate(rows).astype(np.int64)
+    alpha = exact.default_alpha(d)
+    tree, flags = attention_cuda(Qt, K, V, alpha, rp, ki, splits=4)
+    assert not flags.any()
+    for i in range(T):
+        seq_idx = np.sort(rows[i])
+        seq, _ = attention_cuda(Qt[i:i + 1], K[seq_idx], V[seq_idx], alpha)
+        assert np.array_equal(tree[i], seq[0])
+        assert np.array_equal(tree[i], exact.attention_row(Qt[i], K[seq_idx], V[seq_idx], alpha))
+
+
+def test_nan_inf_rows_flagged(ea):
+    """Rows that see a NaN/inf (q, or an attended key/value) get flag 2; the others are exact."""
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(3)
+    d, dv, n = 32, 16, 40
+    Q, K, V = bf16(rng, (6, d)), bf16(rng, (n, d)), bf16(rng, (n, dv))
+    Q[1, 3] = 0x7FC0        # NaN in q row 1
+    K[10, 2] = 0x7F80       # +inf in key 10
+    V[20, 5] = 0xFF80       # -inf in value 20
+    mask = np.ones((6, n), bool)
+    mask[2:, 10] = False    # rows 2.. skip key 10
+    mask[3:, 20] = False    # rows 3.. skip key 20
+    rp, ki = exact.csr_from_mask(mask)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    out, flags = cuda.launch(t(Q), t(K), t(V), exact.default_alpha(d), row_ptr=t(rp), key_idx=t(ki))
+    flags = flags.cpu().numpy()
+    assert flags.tolist() == [2, 2, 2, 0, 0, 0]
+    out = out.cpu().numpy().view(np.uint16)
+    for r in (3, 4, 5):
+        sel = np.flatnonzero(mask[r])
+        assert np.array_equal(out[r], exact.attention_row(Q[r], K[sel], V[sel], exact.default_alpha(d)))
+    with pytest.raises(ea.ExactAttentionDomainError):
+        ea.attention(Q, K, V, exact.default_alpha(d), mask=mask)
+
+
+def test_empty_rows_and_single_key(ea):
+    from exactattention_b200.cuda import attention_cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(2)
+    d, dv = 16, 8
+    Q, K, V = bf16(rng, (3, d)), bf16(rng, (5, d)), bf16(rng, (5, dv))
+    rp = np.array([0, 0, 1, 1], np.int64)
+    ki = np.array([4], np.int64)
+    out, flags = attention_cuda(Q, K, V, exact.default_alpha(d), rp, ki)
+    assert not flags.any()
+    assert np.array_equal(out[0], np.zeros(dv, np.uint16)) and np.array_equal(out[2], np.zeros(dv, np.uint16))
+    assert np.array_equal(out[1], V[4])          # one key returns its value exactly
+
+
+def test_identical_keys_average_values(ea):
+    from exactattention_b200.cuda import attention_cuda
+    from exactattention_b200.formats import bf16_bits_to_float32
+    from oracle import exact
+
+    rng = np.random.default_rng(1)
+    q = bf16(rng, (1, 32))
+    k = np.repeat(bf16(rng, (1, 32)), 4, axis=0)
+    v = bf16(rng, (4, 32))
+    out, _ = attention_cuda(q, k, v, exact.default_alpha(32), out="fp32")
+    vf = bf16_bits_to_float32(v).astype(np.float64)
+    assert np.array_equal(out[0], np.float32(vf.mean(axis=0)))
+
+
+def test_round_ratio_export(ea):
+    """ea_round_ratio_cuda against the reference's round_rational known answers."""
+    from exactattention_b200.cuda import round_ratio
+
+    z = np.load(os.path.join(GOLDEN, "round_kat.npz"))
+    abEf, val, ovf = z["abEf"], z["val"], z["ovf"]
+    for i in range(0, len(val), 7):
+        a, b, E, is32 = (int(x) for x in abEf[i])
+        got, ov = round_ratio(a, b, E, False, bool(is32))
+        if ovf[i]:
+            assert ov
+        else:
+            assert not ov and got == val[i], (a, b, E, is32)
+
+
+# ---------------------------------------------------------------------------
+# device API mask layouts and the synthetic generator
+# ---------------------------------------------------------------------------
+
+def test_synth_device_matches_numpy(ea):
+    import torch
+
+    from exactattention_b200 import workloads as w
+
+    cfg = w.config("c2")
+    dk = w.synth_device(2, w.T_K, (1, 8, 4096, 128), cfg.k_scale).cpu().numpy().view(np.uint16)
+    for h in (0, 5):
+        assert np.array_equal(dk[0, h, 100:400], w.synth_rows(2, w.T_K, (1, 8, 4096, 128), 0, h, 100, 400, cfg.k_scale))
+    sh = w.synth_device(5, w.T_K, (4, 8, 1000, 128), None, 10, t0=5000, T_full=1 << 20).cpu().numpy().view(np.uint16)
+    assert np.array_equal(sh[3, 6], w.synth_rows(5, w.T_K, (4, 8, 1 << 20, 128), 3, 6, 5000, 6000, None, 10))
+    del torch
+
+
+def test_layouts_agree(ea):
+    """RANGE, PAGED and HYBRID descriptions of the same key sets give the CSR result."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(9)
+    dev = torch.device("cuda")
+    B, hq, hkv, d, ps = 3, 4, 2, 64, 16
+    ctx = rng.integers(1, 200, size=B)
+    npg = (ctx + ps - 1) // ps
+    perm = rng.permutation(int(npg.sum())).astype(np.int32)
+    maxp = int(npg.max())
+    pt = np.zeros((B, maxp), np.int32)
+    off = 0
+    for b in range(B):
+        pt[b, :npg[b]] = perm[off:off + npg[b]]
+        off += int(npg[b])
+    Kc = bf16(rng, (int(npg.sum()), hkv, ps, d), "outlier")
+    Vc = bf16(rng, (int(npg.sum()), hkv, ps, d))
+    Q = bf16(rng, (B * hq, d), "outlier")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(d)
+    o_p, f_p = cuda.launch(t(Q), t(Kc), t(Vc), alpha, page_table=t(pt), seq_lens=t(ctx.astype(np.int32)),
+                           page_size=ps, q_heads=hq, kv_heads=hkv, splits=3)
+    # the same keys as CSR rows of the flattened cache
+    rows = []
+    for r in range(B * hq):
+        b, h = divmod(r, hq)
+        j = np.arange(ctx[b])
+        rows.append(((pt[b, j // ps].astype(np.int64) * hkv + h // (hq // hkv)) * ps + j % ps))
+    rp = np.concatenate([[0], np.cumsum([len(x) for x in rows])]).astype(np.int64)
+    ki = np.concatenate(rows)
+    o_c, f_c = cuda.launch(t(Q), t(Kc), t(Vc), alpha, row_ptr=t(rp), key_idx=t(ki))
+    assert not f_p.any().item() and not f_c.any().item()
+    assert torch.equal(o_p, o_c)
+    # HYBRID: first 5 keys as a range over a copied contiguous cache, rest as CSR
+    Kf, Vf = Kc.reshape(-1, d), Vc.reshape(-1, d)
+    base = np.array([x[0] for x in rows], np.int64)
+    contig = [np.arange(len(x)) for x in rows]
+    Kl = np.concatenate([Kf[x] for x in rows])
+    Vl = np.concatenate([Vf[x] for x in rows])
+    starts = np.concatenate([[0], np.cumsum([len(x) for x in rows])[:-1]]).astype(np.int64)
+    n0 = np.minimum(5, [len(x) for x in rows]).astype(np.int64)
+    tails = [starts[i] + contig[i][n0[i]:] for i in range(len(rows))]
+    rp2 = np.concatenate([[0], np.cumsum([len(x) for x in tails])]).astype(np.int64)
+    ki2 = np.concatenate(tails).astype(np.int64)
+    o_h, f_h = cuda.launch(t(Q), t(Kl), t(Vl), alpha, kv_base=t(starts), kv_len=t(n0), row_ptr=t(rp2),
+                           key_idx=t(ki2), splits=2)
+    assert torch.equal(o_h, o_c)
+    del base
+
+
+# ---------------------------------------------------------------------------
+# full configurations vs the reference's SHA-256
+# ---------------------------------------------------------------------------
+
+def _configs():
+    p = os.path.join(GOLDEN, "configs.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+@pytest.mark.parametrize("name,splits", [("c2", 1), ("c3", 1), ("c3", 4), ("c3", 16), ("c4", 1), ("c5", 4)])
+def test_config_sha(ea, name, splits):
+    import torch
+
+    from exactattention_b200 import cuda, workloads as w
+
+    gold = _configs()
+    if name not in gold:
+        pytest.skip(f"no golden SHA for {name}")
+    case = w.device_case(name)
+    stats = torch.zeros(8, dtype=torch.int64, device="cuda")
+    out, flags = cuda.launch(case["q"], case["k"], case["v"], case["cfg"].alpha, splits=splits, stats=stats,
+                             **case["kw"])
+    torch.cuda.synchronize()
+    assert not flags.any().item()
+    assert sha(out.cpu().numpy().view(np.uint16)) == gold[name], name
+    st = stats.cpu().numpy()
+    assert st[6] == 0 and st[4] == 0
+    assert st[5] == case["cfg"].pairs
