@@ -13,7 +13,7 @@ _lib = None
 EA_MASK_CSR, EA_MASK_RANGE, EA_MASK_PAGED, EA_MASK_HYBRID = 0, 1, 2, 3
 EA_STATS_LEN = 8
 STAT_NAMES = ("score_exact", "weight_wide", "tier3_rows", "domain_rows", "unresolved_rows", "pairs",
-              "host_fallbacks", "reserved")
+              "host_fallbacks", "tc_pairs")
 
 # Every symbol include/exactattn_cuda.h declares.
 EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda", "ea_launch_cuda",
@@ -35,6 +35,7 @@ class LaunchArgs(ctypes.Structure):
         ("max_row_keys", ctypes.c_int64),
         ("fp32_out", ctypes.c_int), ("splits", ctypes.c_int),
         ("out", ctypes.c_void_p), ("flags", ctypes.c_void_p), ("stats", ctypes.c_void_p),
+        ("block_rows", ctypes.c_void_p), ("nblocks", ctypes.c_int64),
     ]
 
 

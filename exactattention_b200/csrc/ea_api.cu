@@ -4,6 +4,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -15,6 +16,7 @@
 namespace ea {
 cudaError_t launch_simt(const Prob& P, cudaStream_t st);
 cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
+cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st);
 }  // namespace ea
 
 using namespace ea;
@@ -202,7 +204,13 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   }
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
-  e = launch_simt(P, st);
+  const bool tc_ok = a->mask_kind == EA_MASK_RANGE && a->block_rows && a->nblocks > 0 && a->d == 128 &&
+                     a->dv == 128 && !a->fp32_out && a->splits == 1 && ((uintptr_t)a->q & 15) == 0 &&
+                     ((uintptr_t)a->k & 15) == 0;
+  if (tc_ok)
+    e = launch_tc_prefill(P, a->block_rows, a->nblocks, st);
+  else
+    e = launch_simt(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 launch");
   int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
   e = launch_tier3(P, blocks, st);
@@ -229,6 +237,32 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   size_t orp = slot((size_t)(rows + 1) * 8), oki = slot((size_t)(row_ptr ? total : 0) * 8);
   size_t okb = slot((size_t)(row_ptr ? 0 : rows) * 8), okl = slot((size_t)(row_ptr ? 0 : rows) * 8);
   size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
+  // row blocks for the tensor-core kernel (range masks): rows sharing kv_base, longest first
+  std::vector<int32_t> blocks;
+  if (kv_len_h && d == 128 && dv == 128 && !fp32_out && splits == 1 && rows < (1ll << 31)) {
+    std::vector<int32_t> order(rows);
+    for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {
+      if (kv_base_h[x] != kv_base_h[y]) return kv_base_h[x] < kv_base_h[y];
+      return kv_len_h[x] > kv_len_h[y];
+    });
+    std::vector<std::vector<int32_t>> bl;
+    for (int64_t i = 0; i < rows;) {
+      int64_t j = i;
+      while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
+      for (int64_t c = i; c < j; c += 128) {
+        std::vector<int32_t> b(128, -1);
+        for (int64_t u = c; u < j && u < c + 128; ++u) b[u - c] = order[u];
+        bl.push_back(b);
+      }
+      i = j;
+    }
+    std::stable_sort(bl.begin(), bl.end(), [&](const std::vector<int32_t>& x, const std::vector<int32_t>& y) {
+      return kv_len_h[x[0]] > kv_len_h[y[0]];
+    });
+    for (auto& b : bl) blocks.insert(blocks.end(), b.begin(), b.end());
+  }
+  size_t ob = slot(blocks.size() * 4);
 
   Workspace* w;
   {
@@ -263,6 +297,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
     EA_CPY(okb, kb.data(), (size_t)rows * 8);
     EA_CPY(okl, kl.data(), (size_t)rows * 8);
   }
+  EA_CPY(ob, blocks.data(), blocks.size() * 4);
 #undef EA_CPY
   e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
@@ -288,6 +323,8 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.out = base + oo;
   a.flags = (uint8_t*)(base + of);
   a.stats = (int64_t*)(base + os);
+  a.block_rows = blocks.empty() ? nullptr : (const int32_t*)(base + ob);
+  a.nblocks = (int64_t)(blocks.size() / 128);
   int rc = ea_launch_cuda(&a, st);
   if (rc) return rc;
   int64_t hs[EA_STATS_LEN];

@@ -26,6 +26,7 @@ enum Stat {
   STAT_UNRESOLVED = 4,    // rows no device tier certified (never expected; flagged 1)
   STAT_PAIRS = 5,         // (row, key) pairs processed by tier 1
   STAT_HOST_FALLBACKS = 6,// always 0: there is no host fallback
+  STAT_TC_PAIRS = 7,      // pairs whose scores and P.V ran on the tensor cores
   STAT_LEN = 8
 };
 

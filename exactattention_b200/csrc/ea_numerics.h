@@ -386,16 +386,17 @@ EA_HD Rnd round_ratio64(uint64_t a, uint64_t b, int sh, int neg, int p, int qmin
   return r;
 }
 
-// Both ends of N/Z for N in [N, N + Nerr] * 2^nunit and Z in [Z, Z + Zerr] * 2^zunit (Z > 0).
-// Returns true and the value when both ends round alike (certified.py:249-286).
-EA_HD bool certify_ratio(int64_t N, uint64_t Nerr, int64_t nunit, int64_t Z, uint64_t Zerr, int64_t zunit,
-                         int p, int qmin, int emax, Rnd& out) {
-  if (Z <= 0) return false;
+// Both ends of N/Z for N in [nlo, nhi] * 2^nunit and Z in [zlo, zhi] * 2^zunit (zlo > 0, all
+// magnitudes below 2^63). Returns true and the value when both ends round alike
+// (certified.py:249-286).
+EA_HD bool certify_ratio_lh(int64_t nlo_, int64_t nhi_, int64_t nunit, int64_t zlo_, int64_t zhi_, int64_t zunit,
+                            int p, int qmin, int emax, Rnd& out) {
+  if (zlo_ <= 0 || zhi_ < zlo_ || nhi_ < nlo_) return false;
   int64_t sh64 = nunit - zunit;
   if (sh64 > 100000 || sh64 < -100000) return false;
   int sh = (int)sh64;
-  uint64_t zlo = (uint64_t)Z, zhi = (uint64_t)Z + Zerr;
-  i128 nlo = (i128)N, nhi = (i128)N + (i128)Nerr;
+  uint64_t zlo = (uint64_t)zlo_, zhi = (uint64_t)zhi_;
+  i128 nlo = (i128)nlo_, nhi = (i128)nhi_;
   uint64_t ln, ld, hn, hd;
   int lneg, hneg;
   if (nlo >= 0) {
@@ -411,6 +412,13 @@ EA_HD bool certify_ratio(int64_t N, uint64_t Nerr, int64_t nunit, int64_t Z, uin
   out = rl;
   if (out.q == 0) out.neg = 0;
   return true;
+}
+
+// N in [N, N + Nerr] * 2^nunit and Z in [Z, Z + Zerr] * 2^zunit (Z > 0)
+EA_HD bool certify_ratio(int64_t N, uint64_t Nerr, int64_t nunit, int64_t Z, uint64_t Zerr, int64_t zunit,
+                         int p, int qmin, int emax, Rnd& out) {
+  if (Z <= 0 || Nerr >= (1ull << 62) || Zerr >= (1ull << 62)) return false;
+  return certify_ratio_lh(N, N + (int64_t)Nerr, nunit, Z, Z + (int64_t)Zerr, zunit, p, qmin, emax, out);
 }
 
 // ---------------------------------------------------------------------------

@@ -20,14 +20,10 @@
 
 #include "ea_core.cuh"
 #include "ea_numerics.h"
+#include "ea_tables.cuh"
 #include "ea_wide.h"
 
 namespace ea {
-
-__device__ const uint64_t g_ta64[256] = EA_EXP2_TA64_INIT;
-__device__ const uint64_t g_tb64[256] = EA_EXP2_TB64_INIT;
-__device__ const uint64_t g_ta128[512] = EA_EXP2_TA128_INIT;
-__device__ const uint64_t g_tb128[512] = EA_EXP2_TB128_INIT;
 
 // ---------------------------------------------------------------------------
 // shared-memory layout of the tier-1 kernel (host computes the same sizes)

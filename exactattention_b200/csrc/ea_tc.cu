@@ -1,0 +1,736 @@
+// Tensor-core (tcgen05 / TMEM) tier-1 kernel of certified ExactAttention for row blocks that share
+// a contiguous key range (causal / prefix prefill): d = dv = 128, 128 rows per CTA, 64-key tiles.
+//
+// Exactness (all integer):
+//   scores   q and k rows in block fixed point (W bits, two's complement) cut into 4 byte digits
+//            (low three unsigned, top signed); S = sum_(s,t) 2^(8(s+t)) Q_s . K_t with the 16 digit
+//            products grouped by s + t into 7 int32 TMEM accumulators (each |.| < 2^25), recombined
+//            in int64 (|S| < 2^61). The truncation bound err is summed over the lossy elements
+//            only; t = RN32(alpha S) is certified at both ends, else the exact score (576-bit bins,
+//            computed by one warp per pair) decides.
+//   weights  RN24(2^t) by the integer exp2; W = floor(w / 2^(Rt - 40)) (Rt: the row's tile bound
+//            max floor(t) + 2, so W < 2^40) cut into 5 unsigned byte digits.
+//   P.V      v in fixed point against the largest |v| exponent VE_c of each channel over the
+//            block's keys, |Vfix| < 2^23, 3 byte digits; sum_j W Vfix = sum_g 2^(8g) D_g with the
+//            15 digit products grouped into 7 int32 accumulators (|.| < 2^24), each shifted into the
+//            running int64 N (units 2^(R + VE_c - FN)); the floor of a right shift costs one unit.
+//   bounds   per row, in units of each channel's own N unit: truncated weights (< 1 W unit times
+//            |v| < 2^VE_c), truncated values (keys flagged lossy), shift floors and rescales.
+//            Z is kept exactly as in tier 1. The final N/Z interval is certified per channel;
+//            a row with any uncertified channel, a huge logit or a still-risky weight goes to tier 3.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ea_core.cuh"
+#include "ea_numerics.h"
+#include "ea_tables.cuh"
+#include "ea_tcgen05.cuh"
+
+namespace ea {
+
+namespace tck {
+
+constexpr int BM = 128, BN = 64, D = 128, DV = 128;
+constexpr int NQ = 4, NK = 4, NW = 5, NV = 3;
+constexpr int FW = 40, FV = 23;
+constexpr int THREADS = 256;
+constexpr uint32_t TMEM_COLS = 512;
+
+// shared memory map (bytes)
+constexpr uint32_t Q_PLANE = BM * D;         // 16384
+constexpr uint32_t K_PLANE = BN * D;         // 8192
+constexpr uint32_t V_PLANE = DV * BN;        // 8192
+constexpr uint32_t W_PLANE = BM * BN;        // 8192
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + NQ * Q_PLANE;
+constexpr uint32_t OFF_V = OFF_K + NK * K_PLANE;
+constexpr uint32_t OFF_W = OFF_V + NV * V_PLANE;
+constexpr uint32_t T_PITCH = BN + 1;
+constexpr uint32_t OFF_T = OFF_W + NW * W_PLANE;
+constexpr uint32_t OFF_SMALL = OFF_T + BM * T_PITCH * 4;
+
+struct Small {
+  int32_t rows[BM];
+  int32_t len[BM];
+  int32_t qlsb[BM];
+  uint32_t qlossy[BM][4];
+  int32_t rst[BM];        // row status
+  int32_t rok[BM];        // all channels certified
+  int32_t rt[2][BM];      // tile bound exchange
+  uint64_t zs[2][BM];     // tile Z exchange
+  uint32_t zl[2][BM];     // lossy weights exchange
+  uint64_t vw[2][BM];     // sum of W over keys with lossy values
+  int32_t klsb[BN];
+  uint32_t klossy[BN][4];
+  int32_t kbad[BN];
+  int32_t vlossy[BN];
+  int32_t ve[DV];
+  uint64_t ta[256];
+  uint64_t tb[256];
+  uint64_t bar;
+  uint32_t tmem;
+  int32_t maxlen;
+  int64_t base;
+};
+
+constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
+
+constexpr uint32_t T_UNCERT = 0x7FC00001u;  // pass-1 markers in the logit table (t is never NaN)
+constexpr uint32_t T_MASKED = 0x7FC00002u;
+
+__device__ __forceinline__ int32_t lead_of(int32_t m, int32_t e) {  // exponent of |m 2^e|'s leading bit
+  return e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1;
+}
+
+// floor(x * 2^s) of an int64 (s may be negative); callers keep left shifts in range
+__device__ __forceinline__ int64_t shift_floor(int64_t x, int s) {
+  if (s >= 0) return (int64_t)((uint64_t)x << s);
+  return s <= -63 ? (x < 0 ? -1 : 0) : (x >> (-s));
+}
+// ceil(u / 2^s) for s >= 0, u * 2^-s otherwise
+__device__ __forceinline__ uint64_t scale_ceil(uint64_t u, int s) {
+  if (s >= 0) return s >= 63 ? (u ? ~0ull >> 2 : 0) : (u << s);
+  int r = -s;
+  if (r >= 64) return u != 0;
+  return (u >> r) + ((u & ((1ull << r) - 1)) != 0);
+}
+
+__device__ __forceinline__ Rnd rnd_from_f32(uint32_t b) {
+  Rnd t = rnd_zero();
+  int32_t m, e;
+  decode_fp32(b, m, e);
+  t.q = (uint64_t)(m < 0 ? -m : m);
+  t.qe = e;
+  t.neg = m < 0;
+  if (t.q == 0) t.neg = 0;
+  return t;
+}
+
+// digit fixed point of one bf16 element against lsb, as a two's complement int32 (|x| < 2^27)
+__device__ __forceinline__ int32_t fixq(uint32_t bits, int lsb, int& lost, int& bad) {
+  int32_t m, e;
+  if (!decode_bf16(bits, m, e)) {
+    bad = 1;
+    lost = 0;
+    return 0;
+  }
+  if (!m) {
+    lost = 0;
+    return 0;
+  }
+  int32_t mag = m < 0 ? -m : m;
+  int sh = e - lsb;
+  int32_t f;
+  if (sh >= 0) {
+    f = mag << sh;
+    lost = 0;
+  } else {
+    int s = -sh;
+    f = s >= 31 ? 0 : (mag >> s);
+    lost = (s >= 31) ? 1 : ((f << s) != mag);
+  }
+  return m < 0 ? -f : f;
+}
+
+// int32 fixed-point value of digit planes at (row, byte k) of an R-row K-major tile
+__device__ __forceinline__ int32_t read_fix(const uint8_t* planes, uint32_t plane_bytes, uint32_t row, uint32_t k,
+                                            uint32_t R) {
+  uint32_t o = tc::kmajor_off(row, k, R);
+  uint32_t b0 = planes[o], b1 = planes[o + plane_bytes], b2 = planes[o + 2 * plane_bytes];
+  int32_t b3 = (int8_t)planes[o + 3 * plane_bytes];
+  return (int32_t)(b0 | (b1 << 8) | (b2 << 16)) + (b3 << 24);
+}
+
+// Truncation bound of one windowed score, in units 2^(qlsb + klsb): for the lossy elements only,
+// |q k - Q K| <= |dq| |k| + |Q| |dk| with |dq|, |dk| < 1 unit and |k| < |K| + 1 unit when k is lossy.
+__device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, const uint8_t* sK, int r, int kj) {
+  uint64_t err = 0;
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t ql = S.qlossy[r][w], kl = S.klossy[kj][w];
+    for (uint32_t m = ql; m; m &= m - 1) {
+      int i = 32 * w + __ffs(m) - 1;
+      int32_t kf = read_fix(sK, K_PLANE, kj, i, BN);
+      err += (uint64_t)(kf < 0 ? -kf : kf) + ((kl >> (i & 31)) & 1u);
+    }
+    for (uint32_t m = kl; m; m &= m - 1) {
+      int i = 32 * w + __ffs(m) - 1;
+      int32_t qf = read_fix(sQ, Q_PLANE, r, i, BM);
+      err += (uint64_t)(qf < 0 ? -qf : qf);
+    }
+  }
+  return err;
+}
+
+__device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_t& E) {
+  return weight_from_logit_wide(t, g_ta128, g_tb128, M, E);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const int32_t* __restrict__ block_rows) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sQ = smem + OFF_Q;
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
+  uint8_t* sW = smem + OFF_W;
+  uint32_t* sT = (uint32_t*)(smem + OFF_T);
+  Small& S = *(Small*)(smem + OFF_SMALL);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int blk = blockIdx.x;
+
+  // ---------------- set-up ----------------
+  if (tid < BM) {
+    int32_t row = block_rows[(int64_t)blk * BM + tid];
+    S.rows[tid] = row;
+    S.len[tid] = row >= 0 ? (int32_t)P.kv_len[row] : 0;
+    S.rst[tid] = ST_OK;
+    S.rok[tid] = 1;
+  }
+  for (int i = tid; i < 256; i += THREADS) {
+    S.ta[i] = g_ta64[i];
+    S.tb[i] = g_tb64[i];
+  }
+  if (tid == 0) {
+    tc::mbar_init(&S.bar, 1);
+    S.base = P.kv_base[block_rows[(int64_t)blk * BM]];
+  }
+  if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
+  __syncthreads();
+  if (tid == 0) {
+    int32_t m = 0;
+    for (int i = 0; i < BM; ++i) m = max(m, S.len[i]);
+    S.maxlen = m;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = S.tmem;
+  const int32_t maxlen = S.maxlen;
+  const int64_t base = S.base;
+
+  // q rows -> 4 digit planes; thread (row tid / 2, half tid % 2) converts 64 elements
+  {
+    const int i = tid >> 1, h = tid & 1;
+    const int32_t row = S.rows[i];
+    uint32_t bits[64];
+    int lead = INT32_MIN, bad = 0;
+    if (row >= 0) {
+      const uint4* src = (const uint4*)(P.q + (int64_t)row * D + 64 * h);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 x = src[c];
+        uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          bits[8 * c + 2 * u] = w4[u] & 0xFFFFu;
+          bits[8 * c + 2 * u + 1] = w4[u] >> 16;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        int32_t m, ex;
+        if (!decode_bf16(bits[e], m, ex)) bad = 1;
+        if (m) lead = max(lead, lead_of(m, ex));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 64; ++e) bits[e] = 0;
+    }
+    lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 1));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+    const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+    uint32_t lmask[2] = {0u, 0u};
+    uint32_t dig[NQ][16];
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+      int lost = 0, b2 = 0;
+      int32_t f = (bad || lead == INT32_MIN) ? 0 : fixq(bits[e], lsb, lost, b2);
+      if (lost) lmask[e >> 5] |= 1u << (e & 31);
+      uint32_t u = (uint32_t)f;
+#pragma unroll
+      for (int p = 0; p < NQ; ++p) {
+        uint32_t byte = (u >> (8 * p)) & 0xFFu;
+        if ((e & 3) == 0) dig[p][e >> 2] = byte;
+        else dig[p][e >> 2] |= byte << (8 * (e & 3));
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < NQ; ++p)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 v4 = make_uint4(dig[p][4 * c], dig[p][4 * c + 1], dig[p][4 * c + 2], dig[p][4 * c + 3]);
+        *(uint4*)(sQ + p * Q_PLANE + tc::kmajor_off(i, 64 * h + 16 * c, BM)) = v4;
+      }
+    S.qlossy[i][2 * h] = lmask[0];
+    S.qlossy[i][2 * h + 1] = lmask[1];
+    if (h == 0) {
+      S.qlsb[i] = lsb;
+      if (bad && row >= 0) S.rst[i] = ST_DOMAIN;
+    }
+  }
+  // channel exponents over the block's keys: VE_c = max (lead(v) + 1), or INT32_MIN if all zero
+  {
+    const int c = tid & 127, half = tid >> 7;
+    int ve = INT32_MIN;
+    for (int64_t j = half; j < maxlen; j += 2) {
+      int32_t m, e;
+      uint16_t b = P.v[(base + j) * DV + c];
+      decode_bf16(b, m, e);  // NaN/inf keys are caught per tile
+      if (m && ((b >> 7) & 0xFF) != 0xFF) ve = max(ve, lead_of(m, e) + 1);
+    }
+    int* red = (int*)sT;
+    red[tid] = ve;
+    __syncthreads();
+    if (half == 0) S.ve[c] = max(red[c], red[c + 128]);
+    __syncthreads();
+  }
+
+  // running state: thread (row r, channel half h): N for its 64 channels, per-row Z and bounds
+  const int r = 32 * (warp & 3) + lane, h = warp >> 2;
+  const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+  const int32_t myrow = S.rows[r];
+  const int32_t mylen = S.len[r];
+  const int FN = P.FZ, FZ = P.FZ;
+  int32_t R = R_EMPTY;
+  int64_t Z = 0;
+  uint64_t Zerr = 0, Nerr = 0;
+  int64_t N[64];
+#pragma unroll
+  for (int c = 0; c < 64; ++c) N[c] = 0;
+  uint32_t phase = 0;
+  bool ok_wait = true;
+  unsigned long long n_exact = 0, n_wide = 0;
+
+  for (int32_t j0 = 0; j0 < maxlen; j0 += BN) {
+    // ---------------- K tile -> digit planes (thread: key tid / 4, quarter tid % 4) ----------------
+    {
+      const int j = tid >> 2, qq = tid & 3;
+      const bool valid = j0 + j < maxlen;
+      uint32_t bits[32];
+      int lead = INT32_MIN, bad = 0;
+      if (valid) {
+        const uint4* src = (const uint4*)(P.k + (base + j0 + j) * D + 32 * qq);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 x = src[c];
+          uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            bits[8 * c + 2 * u] = w4[u] & 0xFFFFu;
+            bits[8 * c + 2 * u + 1] = w4[u] >> 16;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          int32_t m, ex;
+          if (!decode_bf16(bits[e], m, ex)) bad = 1;
+          if (m) lead = max(lead, lead_of(m, ex));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) bits[e] = 0;
+      }
+      lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 1));
+      lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 2));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+      bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+      const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+      uint32_t lmask = 0;
+      uint32_t dig[NK][8];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        int lost = 0, b2 = 0;
+        int32_t f = (bad || lead == INT32_MIN) ? 0 : fixq(bits[e], lsb, lost, b2);
+        if (lost) lmask |= 1u << e;
+        uint32_t u = (uint32_t)f;
+#pragma unroll
+        for (int p = 0; p < NK; ++p) {
+          uint32_t byte = (u >> (8 * p)) & 0xFFu;
+          if ((e & 3) == 0) dig[p][e >> 2] = byte;
+          else dig[p][e >> 2] |= byte << (8 * (e & 3));
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < NK; ++p)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint4 v4 = make_uint4(dig[p][4 * c], dig[p][4 * c + 1], dig[p][4 * c + 2], dig[p][4 * c + 3]);
+          *(uint4*)(sK + p * K_PLANE + tc::kmajor_off(j, 32 * qq + 16 * c, BN)) = v4;
+        }
+      S.klossy[j][qq] = lmask;
+      if (qq == 0) {
+        S.klsb[j] = lsb;
+        S.kbad[j] = bad;
+        S.vlossy[j] = 0;
+      }
+    }
+    __syncthreads();
+    // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 32 (tid / 128) ..) ----
+    {
+      const int c = tid & 127, kh = tid >> 7;
+      const int ve = S.ve[c];
+      const int lsb = ve == INT32_MIN ? 0 : ve - FV;
+      uint32_t dig[NV][8];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = 32 * kh + jj;
+        uint32_t b = (j0 + j < maxlen) ? (uint32_t)P.v[(base + j0 + j) * DV + c] : 0u;
+        int lost = 0, bad = 0;
+        int32_t f = ve == INT32_MIN ? 0 : fixq(b, lsb, lost, bad);
+        if (bad) {
+          atomicOr(&S.kbad[j], 1);
+          f = 0;
+        }
+        if (lost) {
+          atomicOr(&S.vlossy[j], 1);
+        }
+        uint32_t u = (uint32_t)f;
+#pragma unroll
+        for (int p = 0; p < NV; ++p) {
+          uint32_t byte = (u >> (8 * p)) & 0xFFu;
+          if ((jj & 3) == 0) dig[p][jj >> 2] = byte;
+          else dig[p][jj >> 2] |= byte << (8 * (jj & 3));
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < NV; ++p)
+#pragma unroll
+        for (int q4 = 0; q4 < 2; ++q4) {
+          uint4 v4 = make_uint4(dig[p][4 * q4], dig[p][4 * q4 + 1], dig[p][4 * q4 + 2], dig[p][4 * q4 + 3]);
+          *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(c, 32 * kh + 16 * q4, DV)) = v4;
+        }
+    }
+    tc::fence_async_smem();
+    __syncthreads();
+
+    // ---------------- score MMAs: 7 groups x 64 columns ----------------
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t aq = tc::smem_u32(sQ), bk = tc::smem_u32(sK);
+      for (int g = 0; g < NQ + NK - 1; ++g) {
+        bool first = true;
+        for (int s = 0; s < NQ; ++s) {
+          const int t = g - s;
+          if (t < 0 || t >= NK) continue;
+          const uint32_t idesc = tc::idesc_i8(128, BN, s == NQ - 1, t == NK - 1);
+          for (int ks = 0; ks < D / 32; ++ks) {
+            uint64_t ad = tc::smem_desc(aq + s * Q_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
+            uint64_t bd = tc::smem_desc(bk + t * K_PLANE + ks * 2 * (BN / 8) * 128, (BN / 8) * 128, 128);
+            tc::mma_i8(tmem + BN * g, ad, bd, idesc, !first);
+            first = false;
+          }
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar));
+    }
+    ok_wait &= tc::mbar_wait(&S.bar, phase);
+    phase ^= 1;
+    tc::fence_after_sync();
+
+    // ---------------- pass 1: certified logits of (r, keys 32h ..) ----------------
+    {
+      const int qlsb = S.qlsb[r];
+      const bool qlossy = (S.qlossy[r][0] | S.qlossy[r][1] | S.qlossy[r][2] | S.qlossy[r][3]) != 0;
+      int rstat = ST_OK;
+#pragma unroll 1
+      for (int c8 = 0; c8 < 4; ++c8) {
+        uint32_t dg[7][8];
+#pragma unroll
+        for (int g = 0; g < 7; ++g) tc::tmem_ld8(tlane + BN * g + 32 * h + 8 * c8, dg[g]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int kj = 32 * h + 8 * c8 + u;
+          const int32_t key = j0 + kj;
+          uint32_t out = T_MASKED;
+          if (myrow >= 0 && key < mylen) {
+            if (S.kbad[kj]) {
+              rstat = ST_DOMAIN;
+            } else {
+              int64_t acc = 0;
+#pragma unroll
+              for (int g = 0; g < 7; ++g) acc += (int64_t)(int32_t)dg[g][u] * ((int64_t)1 << (8 * g));
+              const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
+              const uint64_t err = (qlossy || klossy) ? score_err(S, sQ, sK, r, kj) : 0;
+              Rnd t = rnd_zero();
+              int ls = logit_from_interval(acc, err, qlsb + S.klsb[kj], P.am, P.ae, t);
+              if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
+              else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
+              else rstat = ST_DOMAIN;
+            }
+          }
+          sT[r * T_PITCH + kj] = out;
+        }
+      }
+      if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+
+    // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
+    for (int e0 = warp * 1024; e0 < (warp + 1) * 1024; e0 += 32) {
+      const int e = e0 + lane;
+      const int rr = e >> 6, kj = e & 63;
+      uint32_t hit = __ballot_sync(0xffffffffu, sT[rr * T_PITCH + kj] == T_UNCERT);
+      while (hit) {
+        const int src = __ffs(hit) - 1;
+        hit &= hit - 1;
+        const int pr = (e0 + src) >> 6, pk = (e0 + src) & 63;
+        const int64_t qrow = S.rows[pr], krow = base + j0 + pk;
+        ExactScore sc;
+        score_clear(sc);
+#pragma unroll
+        for (int m4 = 0; m4 < D / 32; ++m4) {
+          const int i = lane + 32 * m4;
+          int32_t qm, qe, km, ke;
+          decode_bf16(P.q[qrow * D + i], qm, qe);
+          decode_bf16(P.k[krow * D + i], km, ke);
+          if (qm && km) score_add(sc, qm * km, qe + ke);
+        }
+#pragma unroll
+        for (int b = 0; b < SCORE_BINS; ++b)
+#pragma unroll
+          for (int o = 16; o; o >>= 1) sc.bins[b] += __shfl_xor_sync(0xffffffffu, sc.bins[b], o);
+        if (lane == 0) {
+          Rnd t = rnd_zero();
+          int ls = logit_exact(sc, P.am, P.ae, t);
+          if (ls == LOGIT_OK) {
+            sT[pr * T_PITCH + pk] = rnd_to_f32_bits(t);
+          } else {
+            sT[pr * T_PITCH + pk] = T_MASKED;
+            atomicMax(&S.rst[pr], ST_DOMAIN);
+          }
+          ++n_exact;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---------------- pass 2: tile bound, weights, W digits ----------------
+    int32_t Rt;
+    {
+      int32_t rl = INT32_MIN;
+#pragma unroll 4
+      for (int u = 0; u < 32; ++u) {
+        const uint32_t tb = sT[r * T_PITCH + 32 * h + u];
+        if (tb == T_MASKED) continue;
+        Rnd t = rnd_from_f32(tb);
+        int64_t n;
+        uint64_t F;
+        if (split_logit(t, n, F) == W_HUGE) continue;  // handled below (row goes to tier 3)
+        rl = max(rl, (int32_t)n + 2);
+      }
+      S.rt[h][r] = rl;
+    }
+    __syncthreads();
+    Rt = max(S.rt[0][r], S.rt[1][r]);
+    {
+      uint64_t wsum = 0, vwsum = 0;
+      uint32_t nlw = 0;
+      int rstat = ST_OK;
+#pragma unroll 1
+      for (int wd = 0; wd < 8; ++wd) {
+        uint32_t word[NW];
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int kj = 32 * h + 4 * wd + u4;
+          const uint32_t tb = sT[r * T_PITCH + kj];
+          uint64_t W = 0;
+          if (tb != T_MASKED && Rt != INT32_MIN) {
+            Rnd t = rnd_from_f32(tb);
+            uint32_t M;
+            int64_t E;
+            int ws = weight_from_logit(t, S.ta, S.tb, M, E);
+            if (ws == W_RISKY) {
+              ++n_wide;
+              ws = wide_weight(t, M, E);
+            }
+            if (ws != W_OK) {
+              rstat = ST_TIER3;
+            } else {
+              const int sh = (int)(E + FW - Rt);
+              if (sh >= 0) {
+                W = (uint64_t)M << sh;
+              } else if (sh > -64) {
+                W = (uint64_t)M >> (-sh);
+                if ((W << (-sh)) != M) ++nlw;
+              } else {
+                ++nlw;
+              }
+              wsum += W;
+              if (S.vlossy[kj]) vwsum += W + 1;
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < NW; ++p) {
+            uint32_t byte = (uint32_t)(W >> (8 * p)) & 0xFFu;
+            word[p] = u4 == 0 ? byte : (word[p] | (byte << (8 * u4)));
+          }
+        }
+#pragma unroll
+        for (int p = 0; p < NW; ++p)
+          *(uint32_t*)(sW + p * W_PLANE + tc::kmajor_off(r, 32 * h + 4 * wd, BM)) = word[p];
+      }
+      S.zs[h][r] = wsum;
+      S.zl[h][r] = nlw;
+      S.vw[h][r] = vwsum;
+      if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
+    }
+    tc::fence_async_smem();
+    __syncthreads();
+
+    // ---------------- merge Z, rescale N, bounds ----------------
+    int sh_base = 0;  // (Rt - FW - FV) - (R - FN): shift of a W.Vfix unit into N units
+    if (Rt != INT32_MIN) {
+      const int32_t Rn = R == R_EMPTY ? Rt : max(R, Rt);
+      if (R != R_EMPTY && Rn > R) {
+        const int d = Rn - R;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) N[c] = shift_floor(N[c], -d);
+        Nerr = scale_ceil(Nerr, -d) + 1;
+        int lost;
+        Z = floor_shift(Z, -d, lost);
+        Zerr = scale_ceil(Zerr, -d) + (uint64_t)lost;
+      }
+      R = Rn;
+      const uint64_t zt = S.zs[0][r] + S.zs[1][r];
+      const uint64_t nlw = (uint64_t)S.zl[0][r] + S.zl[1][r];
+      const uint64_t vw = S.vw[0][r] + S.vw[1][r];
+      const int zsh = (Rt - FW) - (R - FZ);  // Z units
+      int lost = 0;
+      Z += floor_shift((int64_t)zt, zsh, lost);
+      Zerr += scale_ceil(nlw, zsh) + (uint64_t)lost;
+      sh_base = (Rt - FW - FV) - (R - FN);
+      // truncated weights: < 1 W unit times |v| < 2^VE -> 2^(Rt - FW - R + FN) N units each
+      Nerr += scale_ceil(nlw, sh_base + FV);
+      // truncated values (keys flagged lossy): < W + 1 W units times one V unit
+      Nerr += scale_ceil(vw, sh_base);
+      // floors of the 7 group shifts
+      for (int g = 0; g < 7; ++g)
+        if (8 * g + sh_base < 0) Nerr += 1;
+    }
+
+    // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6), drained into N ----------------
+#pragma unroll 1
+    for (int rd = 0; rd < 3; ++rd) {
+      const int g_lo = 3 * rd, g_hi = rd == 2 ? 7 : 3 * rd + 3;
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
+        for (int g = g_lo; g < g_hi; ++g) {
+          bool first = true;
+          for (int s = 0; s < NW; ++s) {
+            const int t = g - s;
+            if (t < 0 || t >= NV) continue;
+            const uint32_t idesc = tc::idesc_i8(128, DV, false, t == NV - 1);
+            for (int ks = 0; ks < BN / 32; ++ks) {
+              uint64_t ad = tc::smem_desc(aw + s * W_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
+              uint64_t bd = tc::smem_desc(bv + t * V_PLANE + ks * 2 * (DV / 8) * 128, (DV / 8) * 128, 128);
+              tc::mma_i8(tmem + DV * (g - g_lo), ad, bd, idesc, !first);
+              first = false;
+            }
+          }
+        }
+        tc::mma_commit(tc::smem_u32(&S.bar));
+      }
+      ok_wait &= tc::mbar_wait(&S.bar, phase);
+      phase ^= 1;
+      tc::fence_after_sync();
+      {  // warp-collective loads: every lane takes part (rows without visible keys add zeros)
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t dg[3][8];
+          const int ng = g_hi - g_lo;
+#pragma unroll
+          for (int gi = 0; gi < 3; ++gi)
+            if (gi < ng) tc::tmem_ld8(tlane + DV * gi + 64 * h + 8 * c8, dg[gi]);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int gi = 0; gi < 3; ++gi) {
+            if (gi >= ng) continue;
+            const int s = 8 * (g_lo + gi) + sh_base;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) N[8 * c8 + u] += shift_floor((int64_t)(int32_t)dg[gi][u], s);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncthreads();
+    }
+  }
+
+  // ---------------- finalise ----------------
+  {
+    const int st = S.rst[r];
+    uint32_t outw[32];
+    bool ok = ok_wait && st == ST_OK;
+    const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+    if (!P.fp32) {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        Rnd x = rnd_zero();
+        const int ve = S.ve[64 * h + c];
+        if (ok && R != R_EMPTY && ve != INT32_MIN) {
+          ok &= certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z,
+                                 Z + (int64_t)Zerr, (int64_t)R - FZ, p, qmin, 127, x);
+        }
+        uint32_t b = rnd_to_bf16_bits(x);
+        if (c & 1) outw[c >> 1] |= b << 16;
+        else outw[c >> 1] = b;
+      }
+    }
+    if (!ok) atomicAnd(&S.rok[r], 0);
+    __syncthreads();
+    if (myrow >= 0) {
+      const bool rowok = S.rok[r] != 0;
+      if (st == ST_DOMAIN) {
+        uint16_t* o = (uint16_t*)P.out;
+        if (!P.fp32)
+          for (int c = 0; c < 64; ++c) o[(int64_t)myrow * DV + 64 * h + c] = 0;
+        if (h == 0) {
+          P.flags[myrow] = 2;
+          stat_add(P, STAT_DOMAIN_ROWS, 1);
+        }
+      } else if (!rowok || P.fp32) {
+        if (h == 0) {
+          push_tier3(P, myrow);
+          stat_add(P, STAT_TIER3_ROWS, 1);
+        }
+      } else {
+        uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 64 * h);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) o[q4] = make_uint4(outw[4 * q4], outw[4 * q4 + 1], outw[4 * q4 + 2], outw[4 * q4 + 3]);
+        if (h == 0) P.flags[myrow] = 0;
+      }
+    }
+  }
+  n_exact = (unsigned long long)__reduce_add_sync(0xffffffffu, (unsigned)n_exact);
+  n_wide = (unsigned long long)__reduce_add_sync(0xffffffffu, (unsigned)n_wide);
+  if (lane == 0) {
+    stat_add(P, STAT_SCORE_EXACT, n_exact);
+    stat_add(P, STAT_WEIGHT_WIDE, n_wide);
+  }
+  if (tid == 0) {
+    unsigned long long pairs = 0;
+    for (int i = 0; i < BM; ++i) pairs += (unsigned long long)S.len[i];
+    stat_add(P, STAT_PAIRS, pairs);
+    stat_add(P, STAT_TC_PAIRS, pairs);
+    if (!ok_wait) stat_add(P, STAT_UNRESOLVED, 1000000);  // a bounded wait gave up: loud
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_free(tmem, TMEM_COLS);
+}
+
+}  // namespace tck
+
+cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(tck::tc_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)tck::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  tck::tc_prefill_kernel<<<(unsigned)nblocks, tck::THREADS, tck::SMEM_BYTES, st>>>(P, block_rows);
+  return cudaGetLastError();
+}
+
+size_t tc_prefill_smem_bytes() { return tck::SMEM_BYTES; }
+
+}  // namespace ea

@@ -1,0 +1,128 @@
+// Thin wrappers over the sm_100a tensor-core (tcgen05 / TMEM) and mbarrier PTX used by the
+// tensor-core kernels. Operand tiles live in shared memory in the canonical K-major layout
+// without swizzle: 8-row x 16-byte core matrices, each 128 contiguous bytes,
+//   byte (row m, k) of an R-row tile at ((k / 16) * (R / 8) + m / 8) * 128 + (m % 8) * 16 + k % 16,
+// so consecutive 8-row groups are 128 bytes apart (SBO) and consecutive 16-byte K chunks are
+// R * 16 bytes apart (LBO). Every wait is bounded: it gives up after a fixed number of polls or
+// two seconds of %globaltimer and reports failure, so a fault can never hang the device.
+#pragma once
+#include <stdint.h>
+
+namespace ea {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// byte offset of (row m, byte k) in a K-major tile of R rows (R multiple of 8)
+__host__ __device__ __forceinline__ uint32_t kmajor_off(uint32_t m, uint32_t k, uint32_t R) {
+  return ((k >> 4) * (R >> 3) + (m >> 3)) * 128u + (m & 7u) * 16u + (k & 15u);
+}
+
+// shared-memory matrix descriptor, K-major, no swizzle (version 1 for sm_100)
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version
+  return d;                // base offset 0, legacy LBO mode, layout type 0 (no swizzle)
+}
+
+// instruction descriptor of kind::i8 with s32 accumulation, both operands K-major
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_signed, bool b_signed) {
+  return (2u << 4)                           // D format: s32
+         | ((a_signed ? 1u : 0u) << 7)       // A: 0 u8, 1 s8
+         | ((b_signed ? 1u : 0u) << 10)      // B: 0 u8, 1 s8
+         | ((uint32_t)(N >> 3) << 17)        // N / 8
+         | ((uint32_t)(M >> 4) << 24);       // M / 16
+}
+
+// D[tmem] (+)= A[M x 32 bytes] * B[N x 32 bytes]^T, issued by one thread
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       bool accumulate) {
+  uint32_t acc = accumulate ? 1u : 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
+      :
+      : "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// arrive on an mbarrier once every tcgen05.mma issued so far by this thread has completed
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// generic-proxy shared-memory writes become visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// TMEM allocation by one full warp; the base address is written to shared memory
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 8 consecutive 32-bit columns of this thread's TMEM lane (warp w reads lanes 32 (w % 4) ..)
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+      : "r"(addr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// mbarrier with bounded waits
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with the given parity to complete. Returns false after 2 s (or 2^26
+// polls) without completion; callers then record an error and skip the dependent work.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 255u) == 255u && globaltimer() - t0 > 2000000000ull) return false;
+  }
+  return false;
+}
+
+}  // namespace tc
+}  // namespace ea

@@ -100,7 +100,7 @@ def _ptr(t):
 
 def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
            seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-           out_tensor=None, flags=None, stats=None, stream=None):
+           out_tensor=None, flags=None, stats=None, stream=None, blocks=None):
     """Device-level launch, no host sync. q (rows, d), k, v: torch tensors of bf16 bits (any
     16-bit dtype) on one CUDA device. One mask: CSR (row_ptr, key_idx int64), RANGE
     (kv_base, kv_len int64: row r attends k rows kv_base[r] + [0, kv_len[r])), or PAGED
@@ -108,6 +108,7 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     laid out (pages, kv_heads, page_size, d); row r is sequence r // q_heads, head r % q_heads),
     or HYBRID (kv_base/kv_len and row_ptr/key_idx together: the range, then the CSR list).
     max_row_keys bounds every row's key count (required for RANGE/PAGED without a host sync).
+    `blocks` (from row_blocks) lets RANGE masks with d = dv = 128 use the tensor-core kernel.
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
     import torch
 
@@ -155,6 +156,8 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     a.splits = int(splits)
     a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
     a.stats = _ptr(stats)
+    if blocks is not None:
+        a.block_rows, a.nblocks = blocks.data_ptr(), blocks.shape[0]
     s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
@@ -198,3 +201,26 @@ def attention_cuda_ranges(q, k, v, alpha, kv_base, kv_len, max_row_keys=None, ou
     if np.any(flags == 1):
         raise RuntimeError("rows left uncertified by every device tier (library bug)")
     return res, flags
+
+
+def row_blocks(kv_base: np.ndarray, kv_len: np.ndarray, bm: int = 128) -> np.ndarray:
+    """Groups RANGE-mask rows that share kv_base into blocks of `bm` (longest rows first, blocks
+    ordered longest first, -1 padding): the (nblocks, bm) int32 `blocks` argument of launch. The
+    grouping is a schedule only: any grouping gives the same bits."""
+    kv_base = np.asarray(kv_base, np.int64)
+    kv_len = np.asarray(kv_len, np.int64)
+    order = np.lexsort((-kv_len, kv_base))
+    b = kv_base[order]
+    cuts = np.flatnonzero(np.diff(b)) + 1
+    out = []
+    for grp in np.split(order, cuts):
+        for c in range(0, len(grp), bm):
+            blk = np.full(bm, -1, np.int32)
+            part = grp[c:c + bm]
+            blk[:len(part)] = part
+            out.append(blk)
+    if not out:
+        return np.zeros((0, bm), np.int32)
+    arr = np.stack(out)
+    first_len = kv_len[arr[:, 0]]
+    return arr[np.argsort(-first_len, kind="stable")]

@@ -59,7 +59,8 @@ enum { EA_MASK_CSR = 0, EA_MASK_RANGE = 1, EA_MASK_PAGED = 2, EA_MASK_HYBRID = 3
 #define EA_STATS_LEN 8
 /* stats slots (int64, accumulated): 0 scores recomputed exactly, 1 weights by the 128-bit exp2,
  * 2 rows sent to the wide tier, 3 domain-error rows, 4 unresolved rows (flag 1; never
- * expected), 5 (row, key) pairs processed, 6 host fallbacks (always 0). */
+ * expected), 5 (row, key) pairs processed, 6 host fallbacks (always 0), 7 pairs processed by the
+ * tensor-core kernel. */
 
 typedef struct ea_launch {
   /* inputs, device pointers */
@@ -87,6 +88,11 @@ typedef struct ea_launch {
   void* out;      /* (rows, dv) uint16 or float */
   uint8_t* flags; /* (rows,) */
   int64_t* stats; /* EA_STATS_LEN int64 counters, accumulated; may be NULL */
+  /* optional, RANGE masks: rows grouped into blocks of 128 that share kv_base (-1 pads a block),
+   * (nblocks, 128) int32. With it, d = dv = 128, bf16 output and splits == 1, the tensor-core
+   * kernel runs; any grouping gives the same bits. */
+  const int32_t* block_rows;
+  int64_t nblocks;
 } ea_launch_t;
 
 /* Device-pointer entry point: asynchronous on `stream` (a cudaStream_t, NULL = default).

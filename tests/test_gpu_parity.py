@@ -333,3 +333,74 @@ def test_config_sha(ea, name, splits):
     st = stats.cpu().numpy()
     assert st[6] == 0 and st[4] == 0
     assert st[5] == case["cfg"].pairs
+
+
+# ---------------------------------------------------------------------------
+# tensor-core (tcgen05) prefill kernel
+# ---------------------------------------------------------------------------
+
+def _causal_case(rng, S, kind, vkind, heads=2):
+    Q = bf16(rng, (heads * S, 128), kind)
+    K = bf16(rng, (S, 128), kind)
+    V = bf16(rng, (S, 128), vkind)
+    kv_base = np.zeros(heads * S, np.int64)
+    kv_len = np.tile(np.arange(1, S + 1, dtype=np.int64), heads)
+    return Q, K, V, kv_base, kv_len
+
+
+@pytest.mark.parametrize("kind,vkind", [("normal", "normal"), ("outlier", "wide"), ("wide", "normal"),
+                                        ("dupes", "dupes"), ("subnormal", "normal")])
+def test_tensor_core_prefill_matches_simt_and_oracle(ea, kind, vkind):
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(hash((kind, vkind)) & 0xFFFF)
+    S = 300
+    Q, K, V, kb, kl = _causal_case(rng, S, kind, vkind)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st_tc = torch.zeros(8, dtype=torch.int64, device=dev)
+    o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st_tc,
+                             blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
+    torch.cuda.synchronize()
+    st = st_tc.cpu().numpy()
+    assert st[7] == int(kl.sum()), "the tensor-core kernel did not run"
+    assert torch.equal(f_tc, f_s)
+    assert torch.equal(o_tc, o_s)
+    out = o_tc.cpu().numpy().view(np.uint16)
+    for r in (0, 1, 17, 150, S - 1, S, 2 * S - 1):
+        L = int(kl[r])
+        assert np.array_equal(out[r], exact.attention_row(Q[r], K[:L], V[:L], alpha)), r
+
+
+def test_tensor_core_ragged_blocks_and_nan(ea):
+    """Blocks with padding rows, rows of different ranges, and a NaN key that only some rows see."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(77)
+    n = 500
+    K, V = bf16(rng, (n, 128), "outlier"), bf16(rng, (n, 128))
+    Q = bf16(rng, (333, 128), "outlier")
+    kb = rng.choice([0, 100, 250], size=333).astype(np.int64)
+    kl = rng.integers(0, n - 250, size=333).astype(np.int64)
+    K[180, 5] = 0x7FC0
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st,
+                             blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
+    torch.cuda.synchronize()
+    assert st.cpu().numpy()[7] == int(kl.sum())
+    sees = (kb <= 180) & (180 < kb + kl)
+    assert np.array_equal(f_tc.cpu().numpy() == 2, sees)
+    assert torch.equal(f_tc, f_s)
+    ok = torch.from_numpy(~sees).to(dev)
+    assert torch.equal(o_tc[ok], o_s[ok])
