@@ -422,8 +422,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
       tc::mma_commit(tc::smem_u32(&S.bar));
     }
-    ok_wait &= tc::mbar_wait(&S.bar, phase);
-    phase ^= 1;
+    {
+      const bool okw = tc::mbar_wait(&S.bar, phase);
+      phase ^= 1;
+      // block-wide vote: a wait that gave up ends the tile loop for every thread together
+      if (!__syncthreads_and(okw)) {
+        ok_wait = false;
+        break;
+      }
+    }
     tc::fence_after_sync();
 
     // ---------------- pass 1: certified logits of (r, keys 32h ..) ----------------
@@ -632,8 +639,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         }
         tc::mma_commit(tc::smem_u32(&S.bar));
       }
-      ok_wait &= tc::mbar_wait(&S.bar, phase);
-      phase ^= 1;
+      {
+        const bool okw = tc::mbar_wait(&S.bar, phase);
+        phase ^= 1;
+        if (!__syncthreads_and(okw)) {
+          ok_wait = false;
+          break;
+        }
+      }
       tc::fence_after_sync();
       {  // warp-collective loads: every lane takes part (rows without visible keys add zeros)
 #pragma unroll
@@ -656,6 +669,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       tc::fence_before_sync();
       __syncthreads();
     }
+    if (!ok_wait) break;  // uniform: set by the block vote
   }
 
   // ---------------- finalise ----------------
