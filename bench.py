@@ -258,7 +258,8 @@ def main():
     pk = peaks()
     int8_peak_tops = 2.0 * pk["bf16_tflops"]   # dense int8 = 2x dense bf16 on B200 (assumed from the nominal ratio)
     achieved = pairs * INT8_OPS_PER_PAIR / (ms / 1000.0) / 1e12
-    prof = os.path.join(ROOT, "profiles", f"simt_split_kernel_{name}.json")
+    kern = "tc_prefill_kernel" if name == "c2" else "simt_split_kernel"
+    prof = os.path.join(ROOT, "profiles", f"{kern}_{name}.json")
     traffic = json.load(open(prof)).get("dram_bytes_per_launch") if os.path.exists(prof) else None
     cpu = None
     if not args.no_cpu and world == 1:
@@ -277,15 +278,16 @@ def main():
                    "tokens_per_s": world * cfg.rows / (ms_max / 1000.0)},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak_tops, "unit": "TOPS(int8)",
                      "frac": achieved / int8_peak_tops, "traffic": traffic,
-                     "kernel": "simt_split_kernel (tier 1; CUDA cores)",
+                     "kernel": kern + " (tier 1) with the tier-3 kernel in the same step",
                      "peak_source": f"2 x {pk['source']} bf16 {pk['bf16_tflops']} TFLOP/s"},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * (2 + (1 if splits > 1 else 0)),
+        "gpu_launches": args.steps * (2 + (1 if splits > 1 and name != "c2" else 0)),
         "clocks": clk,
         "certified": {"flags_all_zero": ok, "score_exact": int(st[0]), "weight_wide": int(st[1]),
                       "tier3_rows": int(st[2]), "domain_rows": int(st[3]), "unresolved_rows": int(st[4]),
-                      "host_fallbacks": int(st[6])},
+                      "host_fallbacks": int(st[6]), "tensor_core_pairs": int(st[7]),
+                      "per_step": True if args.steps == 1 else f"summed over {args.steps} steps"},
     }
     print(json.dumps(line))
 

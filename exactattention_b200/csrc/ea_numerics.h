@@ -171,6 +171,27 @@ EA_HD int logit_from_interval(int64_t acc, uint64_t err, int sexp, int32_t am, i
   return LOGIT_OK;
 }
 
+// t = RN32(alpha * acc * 2^sexp) for an exactly known score (err == 0), in 64-bit arithmetic:
+// with L = bitlen(|acc|), the top min(L, 40) bits A of |acc| times |am| < 2^24 fit in 64 bits;
+// the bits of |acc| below A only act as a sticky bit, because they change the product by less
+// than 2^24 units of A's last bit, while the rounding point lies at least 39 bits above it.
+EA_HD int logit_exact64(int64_t acc, int sexp, int32_t am, int32_t ae, Rnd& t) {
+  if (am == 0 || acc == 0) {
+    t = rnd_zero();
+    return LOGIT_OK;
+  }
+  const uint64_t a = uabs64(acc);
+  const int L = bitlen64(a);
+  const int drop = L > 40 ? L - 40 : 0;
+  const uint64_t top = a >> drop;
+  const bool sticky = drop ? (a & ((1ull << drop) - 1)) != 0 : false;
+  const uint64_t P = top * uabs64(am);  // < 2^64
+  t = round_u128((u128)P, ae + sexp + drop, (am < 0) != (acc < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  if (t.ovf) return LOGIT_OVERFLOW;
+  if (t.q == 0) t.neg = 0;
+  return LOGIT_OK;
+}
+
 // ---------------------------------------------------------------------------
 // weights w = RN24(2^t), unbounded exponent (SPEC step 3)
 // ---------------------------------------------------------------------------

@@ -8,11 +8,11 @@
 //            in int64 (|S| < 2^61). The truncation bound err is summed over the lossy elements
 //            only; t = RN32(alpha S) is certified at both ends, else the exact score (576-bit bins,
 //            computed by one warp per pair) decides.
-//   weights  RN24(2^t) by the integer exp2; W = floor(w / 2^(Rt - 40)) (Rt: the row's tile bound
-//            max floor(t) + 2, so W < 2^40) cut into 5 unsigned byte digits.
+//   weights  RN24(2^t) by the integer exp2; W = floor(w / 2^(Rt - 48)) (Rt: the row's tile bound
+//            max ceil(t) + 1 >= max floor(t) + 2 > log2 w, so W < 2^48) cut into 6 unsigned byte digits.
 //   P.V      v in fixed point against the largest |v| exponent VE_c of each channel over the
 //            block's keys, |Vfix| < 2^23, 3 byte digits; sum_j W Vfix = sum_g 2^(8g) D_g with the
-//            15 digit products grouped into 7 int32 accumulators (|.| < 2^24), each shifted into the
+//            18 digit products grouped into 8 int32 accumulators (|.| < 2^24), each shifted into the
 //            running int64 N (units 2^(R + VE_c - FN)); the floor of a right shift costs one unit.
 //   bounds   per row, in units of each channel's own N unit: truncated weights (< 1 W unit times
 //            |v| < 2^VE_c), truncated values (keys flagged lossy), shift floors and rescales.
@@ -31,8 +31,8 @@ namespace ea {
 namespace tck {
 
 constexpr int BM = 128, BN = 64, D = 128, DV = 128;
-constexpr int NQ = 4, NK = 4, NW = 5, NV = 3;
-constexpr int FW = 40, FV = 23;
+constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
+constexpr int FW = 48, FV = 23;
 constexpr int THREADS = 256;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -159,6 +159,10 @@ __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, co
     }
   }
   return err;
+}
+
+__device__ __noinline__ int logit_bounded(int64_t acc, uint64_t err, int sexp, int32_t am, int32_t ae, Rnd& t) {
+  return logit_from_interval(acc, err, sexp, am, ae, t);
 }
 
 __device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_t& E) {
@@ -457,9 +461,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
               for (int g = 0; g < 7; ++g) acc += (int64_t)(int32_t)dg[g][u] * ((int64_t)1 << (8 * g));
               const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
-              const uint64_t err = (qlossy || klossy) ? score_err(S, sQ, sK, r, kj) : 0;
               Rnd t = rnd_zero();
-              int ls = logit_from_interval(acc, err, qlsb + S.klsb[kj], P.am, P.ae, t);
+              int ls;
+              if (qlossy || klossy)
+                ls = logit_bounded(acc, score_err(S, sQ, sK, r, kj), qlsb + S.klsb[kj], P.am, P.ae, t);
+              else
+                ls = logit_exact64(acc, qlsb + S.klsb[kj], P.am, P.ae, t);
               if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
               else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
               else rstat = ST_DOMAIN;
@@ -515,16 +522,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     // ---------------- pass 2: tile bound, weights, W digits ----------------
     int32_t Rt;
     {
+      // w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1): ceil of the exact fp32 t is exact
       int32_t rl = INT32_MIN;
-#pragma unroll 4
+#pragma unroll 8
       for (int u = 0; u < 32; ++u) {
         const uint32_t tb = sT[r * T_PITCH + 32 * h + u];
-        if (tb == T_MASKED) continue;
-        Rnd t = rnd_from_f32(tb);
-        int64_t n;
-        uint64_t F;
-        if (split_logit(t, n, F) == W_HUGE) continue;  // handled below (row goes to tier 3)
-        rl = max(rl, (int32_t)n + 2);
+        const float tf = __uint_as_float(tb);
+        if (tb == T_MASKED || !(fabsf(tf) < 1073741824.0f)) continue;  // |t| >= 2^30: tier 3
+        rl = max(rl, __float2int_ru(tf) + 1);
       }
       S.rt[h][r] = rl;
     }
@@ -611,15 +616,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       Nerr += scale_ceil(nlw, sh_base + FV);
       // truncated values (keys flagged lossy): < W + 1 W units times one V unit
       Nerr += scale_ceil(vw, sh_base);
-      // floors of the 7 group shifts
-      for (int g = 0; g < 7; ++g)
+      // floors of the group shifts
+      for (int g = 0; g < NW + NV - 1; ++g)
         if (8 * g + sh_base < 0) Nerr += 1;
     }
 
     // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6), drained into N ----------------
 #pragma unroll 1
     for (int rd = 0; rd < 3; ++rd) {
-      const int g_lo = 3 * rd, g_hi = rd == 2 ? 7 : 3 * rd + 3;
+      const int g_lo = 3 * rd, g_hi = rd == 2 ? NW + NV - 1 : 3 * rd + 3;
       if (tid == 0) {
         tc::fence_after_sync();
         const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);

@@ -50,6 +50,15 @@ int probe_logit_interval(int64_t acc, uint64_t err, int sexp, uint32_t alpha_bit
   return s;
 }
 
+int probe_logit_exact64(int64_t acc, int sexp, uint32_t alpha_bits, uint32_t* t_bits) {
+  int32_t am, ae;
+  decode_fp32(alpha_bits, am, ae);
+  Rnd t = rnd_zero();
+  int s = logit_exact64(acc, sexp, am, ae, t);
+  *t_bits = rnd_to_f32_bits(t);
+  return s;
+}
+
 // exact logit of a q row and a k row of d bf16 values
 int probe_logit_exact(const uint16_t* q, const uint16_t* k, int d, uint32_t alpha_bits, uint32_t* t_bits) {
   int32_t am, ae;

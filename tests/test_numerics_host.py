@@ -23,6 +23,7 @@ def P(probe_lib):
     L.probe_round_ratio64.argtypes = [u64, u64, i32, i32, i32, ctypes.POINTER(i32)]
     L.probe_logit_interval.argtypes = [i64, u64, i32, u32, ctypes.POINTER(u32)]
     L.probe_logit_exact.argtypes = [ctypes.c_void_p, ctypes.c_void_p, i32, u32, ctypes.POINTER(u32)]
+    L.probe_logit_exact64.argtypes = [i64, i32, u32, ctypes.POINTER(u32)]
     L.probe_certify_ratio.argtypes = [i64, u64, i64, i64, u64, i64, i32, ctypes.POINTER(u32)]
     return L
 
@@ -111,6 +112,27 @@ def test_logit_interval_exact_point(P):
             assert st == 0 and tb.value == _bits(m, e)
         except exact.ExactAttentionDomainError:
             assert st == 2
+
+
+def test_logit_exact64_matches_oracle(P):
+    """The 64-bit fast path (top 40 bits of the score and a sticky bit) rounds like the exact
+    product, including the subnormal range, ties and overflow."""
+    rng = np.random.default_rng(12)
+    for alpha in (exact.default_alpha(128), np.float32(0.0883883), np.float32(-3.5e-39), np.float32(1.7e38)):
+        am, ae = exact.decode_fp32(alpha)
+        ab = exact.f32_to_bits(alpha)
+        for _ in range(4000):
+            acc = int(rng.integers(-2 ** 62, 2 ** 62)) >> int(rng.integers(0, 62))
+            if rng.random() < 0.2:   # low bits that only matter as sticky
+                acc = (acc >> 20 << 20) | int(rng.integers(0, 2))
+            sexp = int(rng.integers(-330, 120))
+            tb = u32()
+            st = P.probe_logit_exact64(acc, sexp, ab, tb)
+            try:
+                m, e = exact.round_dyadic(am * acc, ae + sexp, exact.FP32) if acc and am else (0, 0)
+                assert st == 0 and tb.value == _bits(m, e), (acc, sexp)
+            except exact.ExactAttentionDomainError:
+                assert st == 2
 
 
 def test_logit_interval_soundness(P):
