@@ -131,6 +131,40 @@ EA_HD Rnd round_u128(u128 A, int E, int neg, int p, int qmin, int emax, bool sti
   return r;
 }
 
+// round_u128 for A < 2^64, in 64-bit arithmetic only (the fast path of the kernels).
+EA_HD Rnd round_u64(uint64_t A, int E, int neg, int p, int qmin, int emax, bool sticky = false) {
+  Rnd r = rnd_zero();
+  r.neg = neg;
+  if (A == 0) return r;
+  const int bl = bitlen64(A);
+  const int K = bl - 1 + E;
+  int qe = K - (p - 1);
+  if (qe < qmin) qe = qmin;
+  const int sh = qe - E;
+  uint64_t q;
+  if (sh <= 0) {
+    q = A << (-sh);
+  } else if (sh > bl) {
+    q = 0;
+  } else if (sh == bl) {
+    const uint64_t half = 1ull << (sh - 1);
+    q = (A > half || (A == half && sticky)) ? 1 : 0;
+  } else {
+    q = A >> sh;
+    const uint64_t rem = A & ((1ull << sh) - 1), half = 1ull << (sh - 1);
+    if (rem > half || (rem == half && (sticky || (q & 1)))) ++q;
+  }
+  if (q == (1ull << p)) {
+    q >>= 1;
+    ++qe;
+  }
+  if (q == 0) return r;
+  r.q = q;
+  r.qe = qe;
+  if (qe + bitlen64(q) - 1 > emax) r.ovf = 1;
+  return r;
+}
+
 constexpr int FP32_P = 24, FP32_QMIN = -149, FP32_EMAX = 127;
 constexpr int BF16_P = 8, BF16_QMIN = -133, BF16_EMAX = 127;
 
@@ -186,7 +220,7 @@ EA_HD int logit_exact64(int64_t acc, int sexp, int32_t am, int32_t ae, Rnd& t) {
   const uint64_t top = a >> drop;
   const bool sticky = drop ? (a & ((1ull << drop) - 1)) != 0 : false;
   const uint64_t P = top * uabs64(am);  // < 2^64
-  t = round_u128((u128)P, ae + sexp + drop, (am < 0) != (acc < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  t = round_u64(P, ae + sexp + drop, (am < 0) != (acc < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
   if (t.ovf) return LOGIT_OVERFLOW;
   if (t.q == 0) t.neg = 0;
   return LOGIT_OK;
@@ -440,6 +474,24 @@ EA_HD bool certify_ratio(int64_t N, uint64_t Nerr, int64_t nunit, int64_t Z, uin
                          int p, int qmin, int emax, Rnd& out) {
   if (Z <= 0 || Nerr >= (1ull << 62) || Zerr >= (1ull << 62)) return false;
   return certify_ratio_lh(N, N + (int64_t)Nerr, nunit, Z, Z + (int64_t)Zerr, zunit, p, qmin, emax, out);
+}
+
+// t = RN32(alpha * S * 2^E) for an exact signed 128-bit S (|S| < 2^126).
+EA_HD int logit_i128(i128 S, int E, int32_t am, int32_t ae, Rnd& t) {
+  if (am == 0 || S == 0) {
+    t = rnd_zero();
+    return LOGIT_OK;
+  }
+  const int neg = (S < 0) != (am < 0);
+  const u128 a = S < 0 ? (u128)(-S) : (u128)S;
+  const int L = bitlen128(a);
+  const int drop = L > 40 ? L - 40 : 0;
+  const uint64_t top = (uint64_t)(a >> drop);
+  const bool sticky = drop ? (a & (((u128)1 << drop) - 1)) != 0 : false;
+  t = round_u64(top * uabs64(am), ae + E + drop, neg, FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  if (t.ovf) return LOGIT_OVERFLOW;
+  if (t.q == 0) t.neg = 0;
+  return LOGIT_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -1,22 +1,25 @@
 // Tensor-core (tcgen05 / TMEM) tier-1 kernel of certified ExactAttention for row blocks that share
-// a contiguous key range (causal / prefix prefill): d = dv = 128, 128 rows per CTA, 64-key tiles.
+// a contiguous key range (causal / prefix prefill): d = dv = 128, 128 rows per CTA, 64-key tiles,
+// 512 threads. Thread (row r = 32 (warp % 4) + lane, quarter u = warp / 4) owns TMEM lane r, keys
+// 16u .. 16u + 15 of every tile and channels 32u .. 32u + 31 of the row's running sums.
 //
 // Exactness (all integer):
 //   scores   q and k rows in block fixed point (W bits, two's complement) cut into 4 byte digits
 //            (low three unsigned, top signed); S = sum_(s,t) 2^(8(s+t)) Q_s . K_t with the 16 digit
 //            products grouped by s + t into 7 int32 TMEM accumulators (each |.| < 2^25), recombined
 //            in int64 (|S| < 2^61). The truncation bound err is summed over the lossy elements
-//            only; t = RN32(alpha S) is certified at both ends, else the exact score (576-bit bins,
-//            computed by one warp per pair) decides.
+//            only; t = RN32(alpha S) is certified at both ends, else the exact score (a 128-bit
+//            window over the pair's products, or 576-bit bins when they span more) decides, one
+//            warp per pair.
 //   weights  RN24(2^t) by the integer exp2; W = floor(w / 2^(Rt - 48)) (Rt: the row's tile bound
-//            max ceil(t) + 1 >= max floor(t) + 2 > log2 w, so W < 2^48) cut into 6 unsigned byte digits.
+//            max ceil(t) + 1 >= max floor(t) + 2 > log2 w, so W < 2^48) cut into 6 unsigned bytes.
 //   P.V      v in fixed point against the largest |v| exponent VE_c of each channel over the
 //            block's keys, |Vfix| < 2^23, 3 byte digits; sum_j W Vfix = sum_g 2^(8g) D_g with the
 //            18 digit products grouped into 8 int32 accumulators (|.| < 2^24), each shifted into the
 //            running int64 N (units 2^(R + VE_c - FN)); the floor of a right shift costs one unit.
 //   bounds   per row, in units of each channel's own N unit: truncated weights (< 1 W unit times
 //            |v| < 2^VE_c), truncated values (keys flagged lossy), shift floors and rescales.
-//            Z is kept exactly as in tier 1. The final N/Z interval is certified per channel;
+//            Z is exact up to counted truncations. The final N/Z interval is certified per channel;
 //            a row with any uncertified channel, a huge logit or a still-risky weight goes to tier 3.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -32,8 +35,10 @@ namespace tck {
 
 constexpr int BM = 128, BN = 64, D = 128, DV = 128;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
+constexpr int NGS = NQ + NK - 1;  // score groups
+constexpr int NGP = NW + NV - 1;  // P.V groups
 constexpr int FW = 48, FV = 23;
-constexpr int THREADS = 256;
+constexpr int THREADS = 512, NWARPS = THREADS / 32;
 constexpr uint32_t TMEM_COLS = 512;
 
 // shared memory map (bytes)
@@ -56,15 +61,16 @@ struct Small {
   uint32_t qlossy[BM][4];
   int32_t rst[BM];        // row status
   int32_t rok[BM];        // all channels certified
-  int32_t rt[2][BM];      // tile bound exchange
-  uint64_t zs[2][BM];     // tile Z exchange
-  uint32_t zl[2][BM];     // lossy weights exchange
-  uint64_t vw[2][BM];     // sum of W over keys with lossy values
+  int32_t rt[4][BM];      // tile bound exchange
+  uint32_t zl[4][BM];     // lossy weights exchange
+  uint64_t zs[4][BM];     // tile Z exchange
+  uint64_t vw[4][BM];     // sum of W + 1 over keys with lossy values
   int32_t klsb[BN];
   uint32_t klossy[BN][4];
   int32_t kbad[BN];
   int32_t vlossy[BN];
   int32_t ve[DV];
+  int32_t ve4[4][DV];
   uint64_t ta[256];
   uint64_t tb[256];
   uint64_t bar;
@@ -74,6 +80,7 @@ struct Small {
 };
 
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 constexpr uint32_t T_UNCERT = 0x7FC00001u;  // pass-1 markers in the logit table (t is never NaN)
 constexpr uint32_t T_MASKED = 0x7FC00002u;
@@ -87,7 +94,7 @@ __device__ __forceinline__ int64_t shift_floor(int64_t x, int s) {
   if (s >= 0) return (int64_t)((uint64_t)x << s);
   return s <= -63 ? (x < 0 ? -1 : 0) : (x >> (-s));
 }
-// ceil(u / 2^s) for s >= 0, u * 2^-s otherwise
+// ceil(u * 2^s): exact for s >= 0 (callers keep it in range), rounded up otherwise
 __device__ __forceinline__ uint64_t scale_ceil(uint64_t u, int s) {
   if (s >= 0) return s >= 63 ? (u ? ~0ull >> 2 : 0) : (u << s);
   int r = -s;
@@ -106,30 +113,49 @@ __device__ __forceinline__ Rnd rnd_from_f32(uint32_t b) {
   return t;
 }
 
-// digit fixed point of one bf16 element against lsb, as a two's complement int32 (|x| < 2^27)
+// block fixed point of one bf16 element against lsb, as a two's complement int32
 __device__ __forceinline__ int32_t fixq(uint32_t bits, int lsb, int& lost, int& bad) {
   int32_t m, e;
+  lost = 0;
   if (!decode_bf16(bits, m, e)) {
     bad = 1;
-    lost = 0;
     return 0;
   }
-  if (!m) {
-    lost = 0;
-    return 0;
-  }
+  if (!m) return 0;
   int32_t mag = m < 0 ? -m : m;
   int sh = e - lsb;
   int32_t f;
   if (sh >= 0) {
     f = mag << sh;
-    lost = 0;
   } else {
     int s = -sh;
     f = s >= 31 ? 0 : (mag >> s);
     lost = (s >= 31) ? 1 : ((f << s) != mag);
   }
   return m < 0 ? -f : f;
+}
+
+// byte p of each of four words, packed into one word (byte permutes)
+template <int p>
+__device__ __forceinline__ uint32_t pack4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+  constexpr uint32_t sel = (uint32_t)p | ((uint32_t)(p + 4) << 4);
+  return __byte_perm(__byte_perm(x0, x1, sel), __byte_perm(x2, x3, sel), 0x5410);
+}
+
+// 16 int32 values -> their byte planes 0 .. NP-1, each as one uint4 (16 bytes)
+template <int NP>
+__device__ __forceinline__ void planes16(const uint32_t* x, uint4* out) {
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    uint32_t w[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t a = x[4 * c], b = x[4 * c + 1], cc = x[4 * c + 2], d = x[4 * c + 3];
+      w[c] = p == 0 ? pack4<0>(a, b, cc, d) : p == 1 ? pack4<1>(a, b, cc, d) : p == 2 ? pack4<2>(a, b, cc, d)
+                                                                                       : pack4<3>(a, b, cc, d);
+    }
+    out[p] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
 }
 
 // int32 fixed-point value of digit planes at (row, byte k) of an R-row K-major tile
@@ -169,6 +195,67 @@ __device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_t& E) {
   return weight_from_logit_wide(t, g_ta128, g_tb128, M, E);
 }
 
+// Exact logit of q row `qrow` and k row `krow`, by the whole warp; every lane returns it.
+// Products q_i k_i = m 2^e (|m| < 2^16) summed exactly in a 128-bit window whose unit is 118
+// bits below the largest product bound; if some product falls below the window, 576-bit bins.
+__device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow, int64_t krow, Rnd& t) {
+  const int lane = threadIdx.x & 31;
+  int32_t pm[4], pe[4];
+  int emax = INT32_MIN;
+#pragma unroll
+  for (int m4 = 0; m4 < 4; ++m4) {
+    const int i = lane + 32 * m4;
+    int32_t qm, qe, km, ke;
+    decode_bf16(P.q[qrow * D + i], qm, qe);
+    decode_bf16(P.k[krow * D + i], km, ke);
+    pm[m4] = qm * km;
+    pe[m4] = qe + ke;
+    if (pm[m4]) emax = max(emax, pe[m4] + 16);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+  if (emax == INT32_MIN) {
+    t = rnd_zero();
+    return LOGIT_OK;
+  }
+  const int unit = emax - 118;
+  bool below = false;
+  i128 s = 0;
+#pragma unroll
+  for (int m4 = 0; m4 < 4; ++m4) {
+    if (!pm[m4]) continue;
+    const int sh = pe[m4] - unit;
+    if (sh < 0) below = true;
+    else s += (i128)pm[m4] << sh;
+  }
+  int ls;
+  if (!__any_sync(0xffffffffu, below)) {
+    uint64_t lo = (uint64_t)s;
+    int64_t hi = (int64_t)(s >> 64);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+      const int64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+      const uint64_t sum = lo + lo2;
+      hi = hi + hi2 + (sum < lo ? 1 : 0);
+      lo = sum;
+    }
+    ls = logit_i128((i128)(((u128)(uint64_t)hi << 64) | lo), unit, P.am, P.ae, t);
+  } else {
+    ExactScore sc;
+    score_clear(sc);
+#pragma unroll
+    for (int m4 = 0; m4 < 4; ++m4)
+      if (pm[m4]) score_add(sc, pm[m4], pe[m4]);
+#pragma unroll
+    for (int b = 0; b < SCORE_BINS; ++b)
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sc.bins[b] += __shfl_xor_sync(0xffffffffu, sc.bins[b], o);
+    ls = logit_exact(sc, P.am, P.ae, t);
+  }
+  return ls;
+}
+
 __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const int32_t* __restrict__ block_rows) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sQ = smem + OFF_Q;
@@ -189,9 +276,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     S.rst[tid] = ST_OK;
     S.rok[tid] = 1;
   }
-  for (int i = tid; i < 256; i += THREADS) {
-    S.ta[i] = g_ta64[i];
-    S.tb[i] = g_tb64[i];
+  if (tid < 256) {
+    S.ta[tid] = g_ta64[tid];
+    S.tb[tid] = g_tb64[tid];
   }
   if (tid == 0) {
     tc::mbar_init(&S.bar, 1);
@@ -211,18 +298,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   const int32_t maxlen = S.maxlen;
   const int64_t base = S.base;
 
-  // q rows -> 4 digit planes; thread (row tid / 2, half tid % 2) converts 64 elements
+  // q rows -> 4 digit planes; thread (row tid / 4, quarter tid % 4) converts 32 elements
   {
-    const int i = tid >> 1, h = tid & 1;
+    const int i = tid >> 2, qq = tid & 3;
     const int32_t row = S.rows[i];
-    uint32_t bits[64];
+    uint32_t bits[32];
     int lead = INT32_MIN, bad = 0;
     if (row >= 0) {
-      const uint4* src = (const uint4*)(P.q + (int64_t)row * D + 64 * h);
+      const uint4* src = (const uint4*)(P.q + (int64_t)row * D + 32 * qq);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint4 x = src[c];
-        uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+        const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           bits[8 * c + 2 * u] = w4[u] & 0xFFFFu;
@@ -230,66 +317,58 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         }
       }
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
+      for (int e = 0; e < 32; ++e) {
         int32_t m, ex;
         if (!decode_bf16(bits[e], m, ex)) bad = 1;
         if (m) lead = max(lead, lead_of(m, ex));
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 64; ++e) bits[e] = 0;
+      for (int e = 0; e < 32; ++e) bits[e] = 0;
     }
     lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 1));
+    lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 2));
     bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
+    bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
     const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
-    uint32_t lmask[2] = {0u, 0u};
-    uint32_t dig[NQ][16];
+    uint32_t lmask = 0;
+    uint32_t x[32];
 #pragma unroll
-    for (int e = 0; e < 64; ++e) {
+    for (int e = 0; e < 32; ++e) {
       int lost = 0, b2 = 0;
-      int32_t f = (bad || lead == INT32_MIN) ? 0 : fixq(bits[e], lsb, lost, b2);
-      if (lost) lmask[e >> 5] |= 1u << (e & 31);
-      uint32_t u = (uint32_t)f;
-#pragma unroll
-      for (int p = 0; p < NQ; ++p) {
-        uint32_t byte = (u >> (8 * p)) & 0xFFu;
-        if ((e & 3) == 0) dig[p][e >> 2] = byte;
-        else dig[p][e >> 2] |= byte << (8 * (e & 3));
-      }
+      x[e] = (bad || lead == INT32_MIN) ? 0u : (uint32_t)fixq(bits[e], lsb, lost, b2);
+      if (lost) lmask |= 1u << e;
     }
 #pragma unroll
-    for (int p = 0; p < NQ; ++p)
+    for (int c = 0; c < 2; ++c) {
+      uint4 pl[NQ];
+      planes16<NQ>(x + 16 * c, pl);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint4 v4 = make_uint4(dig[p][4 * c], dig[p][4 * c + 1], dig[p][4 * c + 2], dig[p][4 * c + 3]);
-        *(uint4*)(sQ + p * Q_PLANE + tc::kmajor_off(i, 64 * h + 16 * c, BM)) = v4;
-      }
-    S.qlossy[i][2 * h] = lmask[0];
-    S.qlossy[i][2 * h + 1] = lmask[1];
-    if (h == 0) {
+      for (int p = 0; p < NQ; ++p) *(uint4*)(sQ + p * Q_PLANE + tc::kmajor_off(i, 32 * qq + 16 * c, BM)) = pl[p];
+    }
+    S.qlossy[i][qq] = lmask;
+    if (qq == 0) {
       S.qlsb[i] = lsb;
       if (bad && row >= 0) S.rst[i] = ST_DOMAIN;
     }
   }
   // channel exponents over the block's keys: VE_c = max (lead(v) + 1), or INT32_MIN if all zero
   {
-    const int c = tid & 127, half = tid >> 7;
+    const int c = tid & 127, part = tid >> 7;
     int ve = INT32_MIN;
-    for (int64_t j = half; j < maxlen; j += 2) {
+    for (int64_t j = part; j < maxlen; j += 4) {
       int32_t m, e;
-      uint16_t b = P.v[(base + j) * DV + c];
+      const uint16_t b = P.v[(base + j) * DV + c];
       decode_bf16(b, m, e);  // NaN/inf keys are caught per tile
       if (m && ((b >> 7) & 0xFF) != 0xFF) ve = max(ve, lead_of(m, e) + 1);
     }
-    int* red = (int*)sT;
-    red[tid] = ve;
+    S.ve4[part][c] = ve;
     __syncthreads();
-    if (half == 0) S.ve[c] = max(red[c], red[c + 128]);
+    if (tid < DV) S.ve[tid] = max(max(S.ve4[0][tid], S.ve4[1][tid]), max(S.ve4[2][tid], S.ve4[3][tid]));
     __syncthreads();
   }
 
-  // running state: thread (row r, channel half h): N for its 64 channels, per-row Z and bounds
-  const int r = 32 * (warp & 3) + lane, h = warp >> 2;
+  const int r = 32 * (warp & 3) + lane, u4 = warp >> 2;
   const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
   const int32_t myrow = S.rows[r];
   const int32_t mylen = S.len[r];
@@ -297,26 +376,26 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   int32_t R = R_EMPTY;
   int64_t Z = 0;
   uint64_t Zerr = 0, Nerr = 0;
-  int64_t N[64];
+  int64_t N[32];
 #pragma unroll
-  for (int c = 0; c < 64; ++c) N[c] = 0;
+  for (int c = 0; c < 32; ++c) N[c] = 0;
   uint32_t phase = 0;
   bool ok_wait = true;
-  unsigned long long n_exact = 0, n_wide = 0;
+  unsigned n_exact = 0, n_wide = 0;
 
   for (int32_t j0 = 0; j0 < maxlen; j0 += BN) {
-    // ---------------- K tile -> digit planes (thread: key tid / 4, quarter tid % 4) ----------------
+    // ---------------- K tile -> digit planes (thread: key tid / 8, elements 16 (tid % 8) ..) --------
     {
-      const int j = tid >> 2, qq = tid & 3;
+      const int j = tid >> 3, e8 = tid & 7;
       const bool valid = j0 + j < maxlen;
-      uint32_t bits[32];
+      uint32_t bits[16];
       int lead = INT32_MIN, bad = 0;
       if (valid) {
-        const uint4* src = (const uint4*)(P.k + (base + j0 + j) * D + 32 * qq);
+        const uint4* src = (const uint4*)(P.k + (base + j0 + j) * D + 16 * e8);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint4 x = src[c];
-          uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+          const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             bits[8 * c + 2 * u] = w4[u] & 0xFFFFu;
@@ -324,84 +403,62 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           }
         }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < 16; ++e) {
           int32_t m, ex;
           if (!decode_bf16(bits[e], m, ex)) bad = 1;
           if (m) lead = max(lead, lead_of(m, ex));
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) bits[e] = 0;
+        for (int e = 0; e < 16; ++e) bits[e] = 0;
       }
-      lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 1));
-      lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, 2));
-      bad |= __shfl_xor_sync(0xffffffffu, bad, 1);
-      bad |= __shfl_xor_sync(0xffffffffu, bad, 2);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+      }
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
       uint32_t lmask = 0;
-      uint32_t dig[NK][8];
+      uint32_t x[16];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
+      for (int e = 0; e < 16; ++e) {
         int lost = 0, b2 = 0;
-        int32_t f = (bad || lead == INT32_MIN) ? 0 : fixq(bits[e], lsb, lost, b2);
+        x[e] = (bad || lead == INT32_MIN) ? 0u : (uint32_t)fixq(bits[e], lsb, lost, b2);
         if (lost) lmask |= 1u << e;
-        uint32_t u = (uint32_t)f;
-#pragma unroll
-        for (int p = 0; p < NK; ++p) {
-          uint32_t byte = (u >> (8 * p)) & 0xFFu;
-          if ((e & 3) == 0) dig[p][e >> 2] = byte;
-          else dig[p][e >> 2] |= byte << (8 * (e & 3));
-        }
       }
+      uint4 pl[NK];
+      planes16<NK>(x, pl);
 #pragma unroll
-      for (int p = 0; p < NK; ++p)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint4 v4 = make_uint4(dig[p][4 * c], dig[p][4 * c + 1], dig[p][4 * c + 2], dig[p][4 * c + 3]);
-          *(uint4*)(sK + p * K_PLANE + tc::kmajor_off(j, 32 * qq + 16 * c, BN)) = v4;
-        }
-      S.klossy[j][qq] = lmask;
-      if (qq == 0) {
+      for (int p = 0; p < NK; ++p) *(uint4*)(sK + p * K_PLANE + tc::kmajor_off(j, 16 * e8, BN)) = pl[p];
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, lmask, 1);
+      if ((e8 & 1) == 0) S.klossy[j][e8 >> 1] = lmask | (other << 16);
+      if (e8 == 0) {
         S.klsb[j] = lsb;
         S.kbad[j] = bad;
         S.vlossy[j] = 0;
       }
     }
     __syncthreads();
-    // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 32 (tid / 128) ..) ----
+    // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 16 (tid / 128) ..) ------
     {
-      const int c = tid & 127, kh = tid >> 7;
+      const int c = tid & 127, vq = tid >> 7;
       const int ve = S.ve[c];
       const int lsb = ve == INT32_MIN ? 0 : ve - FV;
-      uint32_t dig[NV][8];
+      uint32_t x[16];
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = 32 * kh + jj;
-        uint32_t b = (j0 + j < maxlen) ? (uint32_t)P.v[(base + j0 + j) * DV + c] : 0u;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 16 * vq + jj;
+        const uint32_t b = (j0 + j < maxlen) ? (uint32_t)P.v[(base + j0 + j) * DV + c] : 0u;
         int lost = 0, bad = 0;
         int32_t f = ve == INT32_MIN ? 0 : fixq(b, lsb, lost, bad);
-        if (bad) {
-          atomicOr(&S.kbad[j], 1);
-          f = 0;
-        }
-        if (lost) {
-          atomicOr(&S.vlossy[j], 1);
-        }
-        uint32_t u = (uint32_t)f;
-#pragma unroll
-        for (int p = 0; p < NV; ++p) {
-          uint32_t byte = (u >> (8 * p)) & 0xFFu;
-          if ((jj & 3) == 0) dig[p][jj >> 2] = byte;
-          else dig[p][jj >> 2] |= byte << (8 * (jj & 3));
-        }
+        if (bad) atomicOr(&S.kbad[j], 1);
+        if (lost) atomicOr(&S.vlossy[j], 1);
+        x[jj] = (uint32_t)f;
       }
+      uint4 pl[NV];
+      planes16<NV>(x, pl);
 #pragma unroll
-      for (int p = 0; p < NV; ++p)
-#pragma unroll
-        for (int q4 = 0; q4 < 2; ++q4) {
-          uint4 v4 = make_uint4(dig[p][4 * q4], dig[p][4 * q4 + 1], dig[p][4 * q4 + 2], dig[p][4 * q4 + 3]);
-          *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(c, 32 * kh + 16 * q4, DV)) = v4;
-        }
+      for (int p = 0; p < NV; ++p) *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(c, 16 * vq, DV)) = pl[p];
     }
     tc::fence_async_smem();
     __syncthreads();
@@ -410,7 +467,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t aq = tc::smem_u32(sQ), bk = tc::smem_u32(sK);
-      for (int g = 0; g < NQ + NK - 1; ++g) {
+      for (int g = 0; g < NGS; ++g) {
         bool first = true;
         for (int s = 0; s < NQ; ++s) {
           const int t = g - s;
@@ -437,29 +494,28 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
     tc::fence_after_sync();
 
-    // ---------------- pass 1: certified logits of (r, keys 32h ..) ----------------
+    // ---------------- pass 1: certified logits of (r, keys 16 u4 ..) ----------------
     {
       const int qlsb = S.qlsb[r];
       const bool qlossy = (S.qlossy[r][0] | S.qlossy[r][1] | S.qlossy[r][2] | S.qlossy[r][3]) != 0;
       int rstat = ST_OK;
 #pragma unroll 1
-      for (int c8 = 0; c8 < 4; ++c8) {
-        uint32_t dg[7][8];
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t dg[NGS][4];
 #pragma unroll
-        for (int g = 0; g < 7; ++g) tc::tmem_ld8(tlane + BN * g + 32 * h + 8 * c8, dg[g]);
+        for (int g = 0; g < NGS; ++g) tc::tmem_ld4(tlane + BN * g + 16 * u4 + 4 * c4, dg[g]);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int kj = 32 * h + 8 * c8 + u;
-          const int32_t key = j0 + kj;
+        for (int u = 0; u < 4; ++u) {
+          const int kj = 16 * u4 + 4 * c4 + u;
           uint32_t out = T_MASKED;
-          if (myrow >= 0 && key < mylen) {
+          if (myrow >= 0 && j0 + kj < mylen) {
             if (S.kbad[kj]) {
               rstat = ST_DOMAIN;
             } else {
               int64_t acc = 0;
 #pragma unroll
-              for (int g = 0; g < 7; ++g) acc += (int64_t)(int32_t)dg[g][u] * ((int64_t)1 << (8 * g));
+              for (int g = 0; g < NGS; ++g) acc += (int64_t)(int32_t)dg[g][u] << (8 * g);
               const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
               Rnd t = rnd_zero();
               int ls;
@@ -481,32 +537,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
 
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
-    for (int e0 = warp * 1024; e0 < (warp + 1) * 1024; e0 += 32) {
+    for (int e0 = warp * (BM * BN / NWARPS); e0 < (warp + 1) * (BM * BN / NWARPS); e0 += 32) {
       const int e = e0 + lane;
-      const int rr = e >> 6, kj = e & 63;
-      uint32_t hit = __ballot_sync(0xffffffffu, sT[rr * T_PITCH + kj] == T_UNCERT);
+      uint32_t hit = __ballot_sync(0xffffffffu, sT[(e >> 6) * T_PITCH + (e & 63)] == T_UNCERT);
       while (hit) {
         const int src = __ffs(hit) - 1;
         hit &= hit - 1;
         const int pr = (e0 + src) >> 6, pk = (e0 + src) & 63;
-        const int64_t qrow = S.rows[pr], krow = base + j0 + pk;
-        ExactScore sc;
-        score_clear(sc);
-#pragma unroll
-        for (int m4 = 0; m4 < D / 32; ++m4) {
-          const int i = lane + 32 * m4;
-          int32_t qm, qe, km, ke;
-          decode_bf16(P.q[qrow * D + i], qm, qe);
-          decode_bf16(P.k[krow * D + i], km, ke);
-          if (qm && km) score_add(sc, qm * km, qe + ke);
-        }
-#pragma unroll
-        for (int b = 0; b < SCORE_BINS; ++b)
-#pragma unroll
-          for (int o = 16; o; o >>= 1) sc.bins[b] += __shfl_xor_sync(0xffffffffu, sc.bins[b], o);
+        Rnd t = rnd_zero();
+        const int ls = warp_exact_logit(P, S.rows[pr], base + j0 + pk, t);
         if (lane == 0) {
-          Rnd t = rnd_zero();
-          int ls = logit_exact(sc, P.am, P.ae, t);
           if (ls == LOGIT_OK) {
             sT[pr * T_PITCH + pk] = rnd_to_f32_bits(t);
           } else {
@@ -520,35 +560,34 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
 
     // ---------------- pass 2: tile bound, weights, W digits ----------------
-    int32_t Rt;
     {
       // w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1): ceil of the exact fp32 t is exact
       int32_t rl = INT32_MIN;
-#pragma unroll 8
-      for (int u = 0; u < 32; ++u) {
-        const uint32_t tb = sT[r * T_PITCH + 32 * h + u];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint32_t tb = sT[r * T_PITCH + 16 * u4 + u];
         const float tf = __uint_as_float(tb);
         if (tb == T_MASKED || !(fabsf(tf) < 1073741824.0f)) continue;  // |t| >= 2^30: tier 3
         rl = max(rl, __float2int_ru(tf) + 1);
       }
-      S.rt[h][r] = rl;
+      S.rt[u4][r] = rl;
     }
     __syncthreads();
-    Rt = max(S.rt[0][r], S.rt[1][r]);
+    const int32_t Rt = max(max(S.rt[0][r], S.rt[1][r]), max(S.rt[2][r], S.rt[3][r]));
     {
       uint64_t wsum = 0, vwsum = 0;
       uint32_t nlw = 0;
       int rstat = ST_OK;
 #pragma unroll 1
-      for (int wd = 0; wd < 8; ++wd) {
-        uint32_t word[NW];
+      for (int wd = 0; wd < 4; ++wd) {
+        uint32_t wlo[4], whi[4];
 #pragma unroll
-        for (int u4 = 0; u4 < 4; ++u4) {
-          const int kj = 32 * h + 4 * wd + u4;
+        for (int u = 0; u < 4; ++u) {
+          const int kj = 16 * u4 + 4 * wd + u;
           const uint32_t tb = sT[r * T_PITCH + kj];
           uint64_t W = 0;
           if (tb != T_MASKED && Rt != INT32_MIN) {
-            Rnd t = rnd_from_f32(tb);
+            const Rnd t = rnd_from_f32(tb);
             uint32_t M;
             int64_t E;
             int ws = weight_from_logit(t, S.ta, S.tb, M, E);
@@ -564,7 +603,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
                 W = (uint64_t)M << sh;
               } else if (sh > -64) {
                 W = (uint64_t)M >> (-sh);
-                if ((W << (-sh)) != M) ++nlw;
+                nlw += (W << (-sh)) != M;
               } else {
                 ++nlw;
               }
@@ -572,19 +611,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
               if (S.vlossy[kj]) vwsum += W + 1;
             }
           }
-#pragma unroll
-          for (int p = 0; p < NW; ++p) {
-            uint32_t byte = (uint32_t)(W >> (8 * p)) & 0xFFu;
-            word[p] = u4 == 0 ? byte : (word[p] | (byte << (8 * u4)));
-          }
+          wlo[u] = (uint32_t)W;
+          whi[u] = (uint32_t)(W >> 32);
         }
-#pragma unroll
-        for (int p = 0; p < NW; ++p)
-          *(uint32_t*)(sW + p * W_PLANE + tc::kmajor_off(r, 32 * h + 4 * wd, BM)) = word[p];
+        uint8_t* dst = sW + tc::kmajor_off(r, 16 * u4 + 4 * wd, BM);
+        *(uint32_t*)(dst + 0 * W_PLANE) = pack4<0>(wlo[0], wlo[1], wlo[2], wlo[3]);
+        *(uint32_t*)(dst + 1 * W_PLANE) = pack4<1>(wlo[0], wlo[1], wlo[2], wlo[3]);
+        *(uint32_t*)(dst + 2 * W_PLANE) = pack4<2>(wlo[0], wlo[1], wlo[2], wlo[3]);
+        *(uint32_t*)(dst + 3 * W_PLANE) = pack4<3>(wlo[0], wlo[1], wlo[2], wlo[3]);
+        *(uint32_t*)(dst + 4 * W_PLANE) = pack4<0>(whi[0], whi[1], whi[2], whi[3]);
+        *(uint32_t*)(dst + 5 * W_PLANE) = pack4<1>(whi[0], whi[1], whi[2], whi[3]);
       }
-      S.zs[h][r] = wsum;
-      S.zl[h][r] = nlw;
-      S.vw[h][r] = vwsum;
+      S.zs[u4][r] = wsum;
+      S.zl[u4][r] = nlw;
+      S.vw[u4][r] = vwsum;
       if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
     }
     tc::fence_async_smem();
@@ -597,16 +637,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       if (R != R_EMPTY && Rn > R) {
         const int d = Rn - R;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) N[c] = shift_floor(N[c], -d);
+        for (int c = 0; c < 32; ++c) N[c] = shift_floor(N[c], -d);
         Nerr = scale_ceil(Nerr, -d) + 1;
         int lost;
         Z = floor_shift(Z, -d, lost);
         Zerr = scale_ceil(Zerr, -d) + (uint64_t)lost;
       }
       R = Rn;
-      const uint64_t zt = S.zs[0][r] + S.zs[1][r];
-      const uint64_t nlw = (uint64_t)S.zl[0][r] + S.zl[1][r];
-      const uint64_t vw = S.vw[0][r] + S.vw[1][r];
+      const uint64_t zt = S.zs[0][r] + S.zs[1][r] + S.zs[2][r] + S.zs[3][r];
+      const uint64_t nlw = (uint64_t)S.zl[0][r] + S.zl[1][r] + S.zl[2][r] + S.zl[3][r];
+      const uint64_t vw = S.vw[0][r] + S.vw[1][r] + S.vw[2][r] + S.vw[3][r];
       const int zsh = (Rt - FW) - (R - FZ);  // Z units
       int lost = 0;
       Z += floor_shift((int64_t)zt, zsh, lost);
@@ -617,14 +657,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       // truncated values (keys flagged lossy): < W + 1 W units times one V unit
       Nerr += scale_ceil(vw, sh_base);
       // floors of the group shifts
-      for (int g = 0; g < NW + NV - 1; ++g)
-        if (8 * g + sh_base < 0) Nerr += 1;
+#pragma unroll
+      for (int g = 0; g < NGP; ++g) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
     }
 
-    // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6), drained into N ----------------
+    // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6-7), drained into N ----------------
 #pragma unroll 1
     for (int rd = 0; rd < 3; ++rd) {
-      const int g_lo = 3 * rd, g_hi = rd == 2 ? NW + NV - 1 : 3 * rd + 3;
+      const int g_lo = 3 * rd, g_hi = rd == 2 ? NGP : 3 * rd + 3;
       if (tid == 0) {
         tc::fence_after_sync();
         const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
@@ -654,13 +694,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
       tc::fence_after_sync();
       {  // warp-collective loads: every lane takes part (rows without visible keys add zeros)
+        const int ng = g_hi - g_lo;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int c8 = 0; c8 < 4; ++c8) {
           uint32_t dg[3][8];
-          const int ng = g_hi - g_lo;
 #pragma unroll
           for (int gi = 0; gi < 3; ++gi)
-            if (gi < ng) tc::tmem_ld8(tlane + DV * gi + 64 * h + 8 * c8, dg[gi]);
+            if (gi < ng) tc::tmem_ld8(tlane + DV * gi + 32 * u4 + 8 * c8, dg[gi]);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int gi = 0; gi < 3; ++gi) {
@@ -680,50 +720,46 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   // ---------------- finalise ----------------
   {
     const int st = S.rst[r];
-    uint32_t outw[32];
-    bool ok = ok_wait && st == ST_OK;
-    const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
-    if (!P.fp32) {
+    uint32_t outw[16];
+    bool ok = ok_wait && st == ST_OK && !P.fp32;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        Rnd x = rnd_zero();
-        const int ve = S.ve[64 * h + c];
-        if (ok && R != R_EMPTY && ve != INT32_MIN) {
-          ok &= certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z,
-                                 Z + (int64_t)Zerr, (int64_t)R - FZ, p, qmin, 127, x);
-        }
-        uint32_t b = rnd_to_bf16_bits(x);
-        if (c & 1) outw[c >> 1] |= b << 16;
-        else outw[c >> 1] = b;
-      }
+    for (int c = 0; c < 32; ++c) {
+      Rnd x = rnd_zero();
+      const int ve = S.ve[32 * u4 + c];
+      if (ok && R != R_EMPTY && ve != INT32_MIN)
+        ok &= certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z,
+                               Z + (int64_t)Zerr, (int64_t)R - FZ, BF16_P, BF16_QMIN, 127, x);
+      const uint32_t b = rnd_to_bf16_bits(x);
+      if (c & 1) outw[c >> 1] |= b << 16;
+      else outw[c >> 1] = b;
     }
     if (!ok) atomicAnd(&S.rok[r], 0);
     __syncthreads();
     if (myrow >= 0) {
       const bool rowok = S.rok[r] != 0;
       if (st == ST_DOMAIN) {
-        uint16_t* o = (uint16_t*)P.out;
-        if (!P.fp32)
-          for (int c = 0; c < 64; ++c) o[(int64_t)myrow * DV + 64 * h + c] = 0;
-        if (h == 0) {
+        uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 32 * u4);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) o[q4] = make_uint4(0, 0, 0, 0);
+        if (u4 == 0) {
           P.flags[myrow] = 2;
           stat_add(P, STAT_DOMAIN_ROWS, 1);
         }
-      } else if (!rowok || P.fp32) {
-        if (h == 0) {
+      } else if (!rowok) {
+        if (u4 == 0) {
           push_tier3(P, myrow);
           stat_add(P, STAT_TIER3_ROWS, 1);
         }
       } else {
-        uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 64 * h);
+        uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 32 * u4);
 #pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) o[q4] = make_uint4(outw[4 * q4], outw[4 * q4 + 1], outw[4 * q4 + 2], outw[4 * q4 + 3]);
-        if (h == 0) P.flags[myrow] = 0;
+        for (int q4 = 0; q4 < 4; ++q4) o[q4] = make_uint4(outw[4 * q4], outw[4 * q4 + 1], outw[4 * q4 + 2], outw[4 * q4 + 3]);
+        if (u4 == 0) P.flags[myrow] = 0;
       }
     }
   }
-  n_exact = (unsigned long long)__reduce_add_sync(0xffffffffu, (unsigned)n_exact);
-  n_wide = (unsigned long long)__reduce_add_sync(0xffffffffu, (unsigned)n_wide);
+  n_exact = __reduce_add_sync(0xffffffffu, n_exact);
+  n_wide = __reduce_add_sync(0xffffffffu, n_wide);
   if (lane == 0) {
     stat_add(P, STAT_SCORE_EXACT, n_exact);
     stat_add(P, STAT_WEIGHT_WIDE, n_wide);

@@ -88,6 +88,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t* v) {
       : "r"(addr)
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld4(uint32_t addr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(addr)
+               : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------

@@ -59,6 +59,16 @@ int probe_logit_exact64(int64_t acc, int sexp, uint32_t alpha_bits, uint32_t* t_
   return s;
 }
 
+int probe_logit_i128(int64_t hi, uint64_t lo, int E, uint32_t alpha_bits, uint32_t* t_bits) {
+  int32_t am, ae;
+  decode_fp32(alpha_bits, am, ae);
+  Rnd t = rnd_zero();
+  i128 S = (i128)(((u128)(uint64_t)hi << 64) | lo);
+  int s = logit_i128(S, E, am, ae, t);
+  *t_bits = rnd_to_f32_bits(t);
+  return s;
+}
+
 // exact logit of a q row and a k row of d bf16 values
 int probe_logit_exact(const uint16_t* q, const uint16_t* k, int d, uint32_t alpha_bits, uint32_t* t_bits) {
   int32_t am, ae;

@@ -24,6 +24,7 @@ def P(probe_lib):
     L.probe_logit_interval.argtypes = [i64, u64, i32, u32, ctypes.POINTER(u32)]
     L.probe_logit_exact.argtypes = [ctypes.c_void_p, ctypes.c_void_p, i32, u32, ctypes.POINTER(u32)]
     L.probe_logit_exact64.argtypes = [i64, i32, u32, ctypes.POINTER(u32)]
+    L.probe_logit_i128.argtypes = [i64, u64, i32, u32, ctypes.POINTER(u32)]
     L.probe_certify_ratio.argtypes = [i64, u64, i64, i64, u64, i64, i32, ctypes.POINTER(u32)]
     return L
 
@@ -131,6 +132,24 @@ def test_logit_exact64_matches_oracle(P):
             try:
                 m, e = exact.round_dyadic(am * acc, ae + sexp, exact.FP32) if acc and am else (0, 0)
                 assert st == 0 and tb.value == _bits(m, e), (acc, sexp)
+            except exact.ExactAttentionDomainError:
+                assert st == 2
+
+
+def test_logit_i128_matches_oracle(P):
+    rng = np.random.default_rng(13)
+    for alpha in (exact.default_alpha(128), np.float32(-3.5e-39), np.float32(1.7e38)):
+        am, ae = exact.decode_fp32(alpha)
+        for _ in range(3000):
+            S = int(rng.integers(-2 ** 62, 2 ** 62)) << int(rng.integers(0, 62))
+            S += int(rng.integers(-3, 3))
+            S >>= int(rng.integers(0, 100))
+            E = int(rng.integers(-400, 50))
+            tb = u32()
+            st = P.probe_logit_i128(S >> 64, S & ((1 << 64) - 1), E, exact.f32_to_bits(alpha), tb)
+            try:
+                m, e = exact.round_dyadic(am * S, ae + E, exact.FP32) if S and am else (0, 0)
+                assert st == 0 and tb.value == _bits(m, e), (S, E)
             except exact.ExactAttentionDomainError:
                 assert st == 2
 
