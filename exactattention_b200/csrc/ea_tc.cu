@@ -82,6 +82,26 @@ struct Small {
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
+// Optional phase clocks (built with -DEA_PHASE_TIMERS): thread 0 of every CTA accumulates the
+// cycles between the barriers that separate the phases of the tile loop.
+#ifdef EA_PHASE_TIMERS
+__device__ unsigned long long g_phase_cycles[16];
+#define EA_PT_INIT long long pt_last = clock64(); long long pt_acc[16] = {0};
+#define EA_PT(i)                        \
+  if (tid == 0) {                       \
+    const long long pt_now = clock64(); \
+    pt_acc[i] += pt_now - pt_last;      \
+    pt_last = pt_now;                   \
+  }
+#define EA_PT_FLUSH \
+  if (tid == 0)     \
+    for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], (unsigned long long)pt_acc[i]);
+#else
+#define EA_PT_INIT
+#define EA_PT(i)
+#define EA_PT_FLUSH
+#endif
+
 constexpr uint32_t T_UNCERT = 0x7FC00001u;  // pass-1 markers in the logit table (t is never NaN)
 constexpr uint32_t T_MASKED = 0x7FC00002u;
 
@@ -368,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
   }
 
+  EA_PT_INIT
   const int r = 32 * (warp & 3) + lane, u4 = warp >> 2;
   const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
   const int32_t myrow = S.rows[r];
@@ -439,6 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
     }
     __syncthreads();
+    EA_PT(0)
     // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 16 (tid / 128) ..) ------
     {
       const int c = tid & 127, vq = tid >> 7;
@@ -462,6 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
     tc::fence_async_smem();
     __syncthreads();
+    EA_PT(1)
 
     // ---------------- score MMAs: 7 groups x 64 columns ----------------
     if (tid == 0) {
@@ -493,6 +516,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
     }
     tc::fence_after_sync();
+    EA_PT(2)
 
     // ---------------- pass 1: certified logits of (r, keys 16 u4 ..) ----------------
     {
@@ -535,6 +559,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
     tc::fence_before_sync();
     __syncthreads();
+    EA_PT(3)
 
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
     for (int e0 = warp * (BM * BN / NWARPS); e0 < (warp + 1) * (BM * BN / NWARPS); e0 += 32) {
@@ -558,6 +583,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
     }
     __syncthreads();
+    EA_PT(4)
 
     // ---------------- pass 2: tile bound, weights, W digits ----------------
     {
@@ -629,6 +655,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
     tc::fence_async_smem();
     __syncthreads();
+    EA_PT(5)
 
     // ---------------- merge Z, rescale N, bounds ----------------
     int sh_base = 0;  // (Rt - FW - FV) - (R - FN): shift of a W.Vfix unit into N units
@@ -661,6 +688,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       for (int g = 0; g < NGP; ++g) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
     }
 
+    EA_PT(6)
     // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6-7), drained into N ----------------
 #pragma unroll 1
     for (int rd = 0; rd < 3; ++rd) {
@@ -693,6 +721,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         }
       }
       tc::fence_after_sync();
+      EA_PT(7)
       {  // warp-collective loads: every lane takes part (rows without visible keys add zeros)
         const int ng = g_hi - g_lo;
 #pragma unroll
@@ -713,10 +742,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       }
       tc::fence_before_sync();
       __syncthreads();
+      EA_PT(8)
     }
     if (!ok_wait) break;  // uniform: set by the block vote
   }
 
+  EA_PT(9)
   // ---------------- finalise ----------------
   {
     const int st = S.rst[r];
@@ -771,6 +802,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     stat_add(P, STAT_TC_PAIRS, pairs);
     if (!ok_wait) stat_add(P, STAT_UNRESOLVED, 1000000);  // a bounded wait gave up: loud
   }
+  EA_PT(10)
+  EA_PT_FLUSH
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_free(tmem, TMEM_COLS);
@@ -787,5 +820,18 @@ cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t 
 }
 
 size_t tc_prefill_smem_bytes() { return tck::SMEM_BYTES; }
+
+}  // namespace ea
+
+#ifdef EA_PHASE_TIMERS
+// phase clocks of the tensor-core kernel (timer builds only): copies and clears the 16 counters
+extern "C" int ea_debug_phase_cycles(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, ea::tck::g_phase_cycles, sizeof(unsigned long long) * 16);
+  unsigned long long z[16] = {0};
+  return cudaMemcpyToSymbol(ea::tck::g_phase_cycles, z, sizeof(z)) == cudaSuccess ? 0 : -4;
+}
+#endif
+
+namespace ea {
 
 }  // namespace ea
