@@ -155,6 +155,17 @@ __device__ __forceinline__ int32_t fixq(uint32_t bits, int lsb, int& lost, int& 
   return m < 0 ? -f : f;
 }
 
+// sum_{g < n} D_g 2^(8g) exactly in int64 for n <= 4 int32 groups (|D_g| < 2^25): a chain of
+// 32 x 32 -> 64-bit multiply-adds
+template <int n>
+__device__ __forceinline__ int64_t recomb(const uint32_t* D) {
+  int64_t acc = (int64_t)(int32_t)D[0];
+  if (n > 1) acc += (int64_t)(int32_t)D[1] * 256;
+  if (n > 2) acc += (int64_t)(int32_t)D[2] * 65536;
+  if (n > 3) acc += (int64_t)(int32_t)D[3] * 16777216;
+  return acc;
+}
+
 // byte p of each of four words, packed into one word (byte permutes)
 template <int p>
 __device__ __forceinline__ uint32_t pack4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
@@ -537,9 +548,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             if (S.kbad[kj]) {
               rstat = ST_DOMAIN;
             } else {
-              int64_t acc = 0;
-#pragma unroll
-              for (int g = 0; g < NGS; ++g) acc += (int64_t)(int32_t)dg[g][u] << (8 * g);
+              const uint32_t lo4[4] = {dg[0][u], dg[1][u], dg[2][u], dg[3][u]};
+              const uint32_t hi3[3] = {dg[4][u], dg[5][u], dg[6][u]};
+              const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
               const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
               Rnd t = rnd_zero();
               int ls;
@@ -562,13 +573,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     EA_PT(3)
 
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
-    for (int e0 = warp * (BM * BN / NWARPS); e0 < (warp + 1) * (BM * BN / NWARPS); e0 += 32) {
-      const int e = e0 + lane;
+    // entry e = warp + 16 (32 it + lane): a row with many uncertified pairs spreads over every warp
+    for (int it = 0; it < BM * BN / (32 * NWARPS); ++it) {
+      const int e = warp + NWARPS * (32 * it + lane);
       uint32_t hit = __ballot_sync(0xffffffffu, sT[(e >> 6) * T_PITCH + (e & 63)] == T_UNCERT);
       while (hit) {
         const int src = __ffs(hit) - 1;
         hit &= hit - 1;
-        const int pr = (e0 + src) >> 6, pk = (e0 + src) & 63;
+        const int ee = warp + NWARPS * (32 * it + src);
+        const int pr = ee >> 6, pk = ee & 63;
         Rnd t = rnd_zero();
         const int ls = warp_exact_logit(P, S.rows[pr], base + j0 + pk, t);
         if (lane == 0) {
@@ -683,9 +696,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       Nerr += scale_ceil(nlw, sh_base + FV);
       // truncated values (keys flagged lossy): < W + 1 W units times one V unit
       Nerr += scale_ceil(vw, sh_base);
-      // floors of the group shifts
+      // floors of the per-round shifts (rounds start at groups 0, 3, 6)
 #pragma unroll
-      for (int g = 0; g < NGP; ++g) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
+      for (int g = 0; g < NGP; g += 3) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
     }
 
     EA_PT(6)
@@ -726,17 +739,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         const int ng = g_hi - g_lo;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
-          uint32_t dg[3][8];
+          uint32_t dg[3][8] = {};
 #pragma unroll
           for (int gi = 0; gi < 3; ++gi)
             if (gi < ng) tc::tmem_ld8(tlane + DV * gi + 32 * u4 + 8 * c8, dg[gi]);
           tc::tmem_wait_ld();
+          const int s = 8 * g_lo + sh_base;
 #pragma unroll
-          for (int gi = 0; gi < 3; ++gi) {
-            if (gi >= ng) continue;
-            const int s = 8 * (g_lo + gi) + sh_base;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) N[8 * c8 + u] += shift_floor((int64_t)(int32_t)dg[gi][u], s);
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t d3[3] = {dg[0][u], ng > 1 ? dg[1][u] : 0u, ng > 2 ? dg[2][u] : 0u};
+            N[8 * c8 + u] += shift_floor(recomb<3>(d3), s);
           }
         }
       }
