@@ -17,7 +17,8 @@ STAT_NAMES = ("score_exact", "weight_wide", "tier3_rows", "domain_rows", "unreso
 
 # Every symbol include/exactattn_cuda.h declares.
 EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda", "ea_launch_cuda",
-           "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error")
+           "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error", "ea_attention_cuda_noalloc",
+           "ea_noalloc_last_error")
 
 
 class LaunchArgs(ctypes.Structure):
@@ -61,6 +62,10 @@ def load(path: str | None = None):
     lib.ea_round_ratio_cuda.restype = ctypes.c_float
     lib.ea_launch_cuda.argtypes = [ctypes.POINTER(LaunchArgs), P]
     lib.ea_launch_cuda.restype = ctypes.c_int
+    lib.ea_attention_cuda_noalloc.argtypes = [ctypes.POINTER(LaunchArgs), P]
+    lib.ea_attention_cuda_noalloc.restype = ctypes.c_int
+    lib.ea_noalloc_last_error.argtypes = []
+    lib.ea_noalloc_last_error.restype = ctypes.c_char_p
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
     lib.ea_reserve_workspace.restype = ctypes.c_int
     lib.ea_cuda_release.argtypes = []

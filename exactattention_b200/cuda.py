@@ -100,7 +100,7 @@ def _ptr(t):
 
 def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
            seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-           out_tensor=None, flags=None, stats=None, stream=None, blocks=None):
+           out_tensor=None, flags=None, stats=None, stream=None, blocks=None, no_alloc=False):
     """Device-level launch, no host sync. q (rows, d), k, v: torch tensors of bf16 bits (any
     16-bit dtype) on one CUDA device. One mask: CSR (row_ptr, key_idx int64), RANGE
     (kv_base, kv_len int64: row r attends k rows kv_base[r] + [0, kv_len[r])), or PAGED
@@ -109,6 +109,8 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     or HYBRID (kv_base/kv_len and row_ptr/key_idx together: the range, then the CSR list).
     max_row_keys bounds every row's key count (required for RANGE/PAGED without a host sync).
     `blocks` (from row_blocks) lets RANGE masks with d = dv = 128 use the tensor-core kernel.
+    `no_alloc` calls ea_attention_cuda_noalloc instead: the library allocates no device memory for
+    the call (its scratch is a fixed static array; see include/exactattn_cuda.h for the limits).
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
     import torch
 
@@ -160,7 +162,13 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
         a.block_rows, a.nblocks = blocks.data_ptr(), blocks.shape[0]
     s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
-        _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
+        if no_alloc:
+            rc = lib.ea_attention_cuda_noalloc(ctypes.byref(a), ctypes.c_void_p(s))
+            if rc == -6:
+                raise ValueError(lib.ea_noalloc_last_error().decode())
+            _lib.check(rc, "ea_attention_cuda_noalloc")
+        else:
+            _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
     return out_tensor, flags
 
 

@@ -100,6 +100,19 @@ typedef struct ea_launch {
  * ea_reserve_workspace or on first use). The torch-tensor API builds on this. */
 int ea_launch_cuda(const ea_launch_t* args, void* stream);
 
+/* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
+ * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,
+ * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the
+ * reference. Its scratch (split partials, tier-3 work list, counters) is one static device array
+ * of EA_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until exit; a call needing
+ * more (rows x splits x (20 dv + 29) bytes plus 4 bytes per row, about) returns -6 with a message
+ * from ea_noalloc_last_error(). The first call on a device looks up the array's address: make it
+ * before any stream capture. Calls share the array, so calls on one device whose kernels may
+ * overlap race and must be serialised. CUDA-core kernels only (d <= 1024, dv <= 256). */
+#define EA_NOALLOC_SCRATCH_BYTES (32u << 20)
+int ea_attention_cuda_noalloc(const ea_launch_t* args, void* stream);
+const char* ea_noalloc_last_error(void);
+
 /* Sizes the workspace for up to `rows` rows, `splits` splits and dv channels on the current
  * device; call before capturing a launch in a CUDA graph. */
 int ea_reserve_workspace(int64_t rows, int splits, int dv);
