@@ -5,8 +5,10 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5] [--sp
 
 One step = one certified attention pass over the config's whole workload (c2 by default: the
 Qwen3-0.6B causal prefill, 16 q / 8 kv heads, 4096 tokens, d=128: 134,250,496 pairs).
-Under torchrun every rank runs its own copy of the workload (weak scaling: each GPU owns a batch
-element; the path has no data-path collective for these configs).
+Under torchrun, c2/c3/c4 run a full copy of the workload per rank (weak scaling; independent
+heads and sequences need no data-path collective), while c5 shards every (sequence, kv head) by
+key range over the ranks and merges the int64 row partials with two NCCL all-reduces (MAX of the
+exponents, SUM of the rescaled accumulators): strong scaling, the same bits at every N.
 
   value      pairs/s over all ranks, inputs resident in HBM; CUDA events around each step on the
              launch stream, L2 flushed (a 256 MiB write) between steps; max over ranks
@@ -177,9 +179,14 @@ def main():
     build.build()
     name = args.config
     splits = args.splits or default_splits(name)
-    case = workloads.device_case(name, dev)
+    # c5 shards every (sequence, kv head) by key range over the ranks and merges the row partials
+    # with NCCL all-reduces (strong scaling: the job is the same 2^20-key workload at every N);
+    # the other configs run a full copy per rank (weak scaling, no data-path collective)
+    kv_sharded = name == "c5" and world > 1
+    case = workloads.device_case(name, dev, shard=rank, nshards=world) if kv_sharded else workloads.device_case(name, dev)
     cfg = case["cfg"]
     pairs = cfg.pairs
+    job_pairs = pairs if kv_sharded else world * pairs
     q, k, v, kw = case["q"], case["k"], case["v"], case["kw"]
     stats = torch.zeros(8, dtype=torch.int64, device=dev)
     cuda.reserve_workspace(q.shape[0], splits, v.shape[-1])
@@ -188,8 +195,21 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
-        cuda.launch(q, k, v, cfg.alpha, splits=splits, out_tensor=out, flags=flags, stats=stats, **kw)
+    if kv_sharded:
+        from exactattention_b200 import dist as ea_dist
+
+        parts = cuda.Partials(q.shape[0], v.shape[-1], dev)
+        kw_local = dict(kw)
+        mrk = kw_local.pop("max_row_keys")
+
+        def step():
+            o, f = ea_dist.attention_kv_sharded(q, k, v, cfg.alpha, max_row_keys=mrk, splits=splits, stats=stats,
+                                                parts=parts, **kw_local)
+            out.copy_(o)
+            flags.copy_(f)
+    else:
+        def step():
+            cuda.launch(q, k, v, cfg.alpha, splits=splits, out_tensor=out, flags=flags, stats=stats, **kw)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -217,7 +237,7 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * pairs / (ms_max / 1000.0)
+    value = job_pairs / (ms_max / 1000.0)
 
     # ---- e2e through the host C ABI ----
     e2e = None
@@ -272,17 +292,21 @@ def main():
     line = {
         "metric": "certified QK pairs/s", "value": value, "unit": "pairs/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": name, "pairs_per_gpu": pairs, "rows": cfg.rows, "splits": splits,
-                   "heads": "16q/8kv", "head_dim": 128, "l2": "flushed (256 MiB write) between steps",
-                   "tokens_per_s": world * cfg.rows / (ms_max / 1000.0)},
+        "scaling": "strong" if kv_sharded else "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": name, "pairs_per_gpu": job_pairs // world, "job_pairs": job_pairs, "rows": cfg.rows,
+                   "splits": splits, "heads": "16q/8kv", "head_dim": 128,
+                   "l2": "flushed (256 MiB write) between steps",
+                   "parallelism": (f"kv-range shards x{world}, NCCL int64 MAX + SUM merge" if kv_sharded
+                                   else f"replicas x{world}"),
+                   "tokens_per_s": (1 if kv_sharded else world) * cfg.rows / (ms_max / 1000.0)},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak_tops, "unit": "TOPS(int8)",
                      "frac": achieved / int8_peak_tops, "traffic": traffic,
                      "kernel": kern + " (tier 1) with the tier-3 kernel in the same step",
                      "peak_source": f"2 x {pk['source']} bf16 {pk['bf16_tflops']} TFLOP/s"},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * (2 + (1 if splits > 1 and name != "c2" else 0)),
+        "gpu_launches": args.steps * ((2 if splits > 1 else 1) + 2 if kv_sharded
+                                      else 2 + (1 if splits > 1 and name != "c2" else 0)),
         "clocks": clk,
         "certified": {"flags_all_zero": ok, "score_exact": int(st[0]), "weight_wide": int(st[1]),
                       "tier3_rows": int(st[2]), "domain_rows": int(st[3]), "unresolved_rows": int(st[4]),

@@ -17,6 +17,8 @@ namespace ea {
 cudaError_t launch_simt(const Prob& P, cudaStream_t st);
 cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
 cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st);
+cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
+cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
 }  // namespace ea
 
 using namespace ea;
@@ -136,7 +138,7 @@ void ea_cuda_release(void) {
   cudaSetDevice(cur);
 }
 
-int ea_launch_cuda(const ea_launch_t* a, void* stream) {
+static int check_launch(const ea_launch_t* a) {
   if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->splits <= 0 || a->rows < 0) return -1;
   uint32_t ab;
   memcpy(&ab, &a->alpha, 4);
@@ -145,15 +147,16 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   if (a->mask_kind == EA_MASK_PAGED && (a->page_size <= 0 || a->q_heads <= 0 || a->kv_heads <= 0 ||
                                         a->q_heads % a->kv_heads != 0))
     return -5;
-  if (a->rows == 0) return 0;
-  std::lock_guard<std::mutex> lk(g_mu);
-  Workspace* w = workspace();
-  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-  int rc = reserve(w, a->rows, a->splits, a->dv);
-  if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
+  return 0;
+}
 
-  Prob P;
+// Problem description from the launch arguments, with the workspace's split buffers when
+// splits > 1.
+static void build_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
+  uint32_t ab;
+  memcpy(&ab, &a->alpha, 4);
+  int32_t am, ae;
+  decode_fp32(ab, am, ae);
   memset(&P, 0, sizeof(P));
   P.q = a->q;
   P.k = a->k;
@@ -202,12 +205,28 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
     P.pNR = (int32_t*)take(n * a->dv * 4);
     P.pSt = (uint8_t*)take(n);
   }
+}
+
+static bool tc_applicable(const ea_launch_t* a) {
+  return a->mask_kind == EA_MASK_RANGE && a->block_rows && a->nblocks > 0 && a->d == 128 && a->dv == 128 &&
+         !a->fp32_out && a->splits == 1 && ((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0;
+}
+
+int ea_launch_cuda(const ea_launch_t* a, void* stream) {
+  int rc = check_launch(a);
+  if (rc) return rc;
+  if (a->rows == 0) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  rc = reserve(w, a->rows, a->splits, a->dv);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  Prob P;
+  build_prob(a, w, P);
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
-  const bool tc_ok = a->mask_kind == EA_MASK_RANGE && a->block_rows && a->nblocks > 0 && a->d == 128 &&
-                     a->dv == 128 && !a->fp32_out && a->splits == 1 && ((uintptr_t)a->q & 15) == 0 &&
-                     ((uintptr_t)a->k & 15) == 0;
-  if (tc_ok)
+  if (tc_applicable(a))
     e = launch_tc_prefill(P, a->block_rows, a->nblocks, st);
   else
     e = launch_simt(P, st);
@@ -216,6 +235,74 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   e = launch_tier3(P, blocks, st);
   if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
   return 0;
+}
+
+static void set_export(Prob& P, const ea_partials_t* x) {
+  P.export_partials = 1;
+  P.xR = x->R;
+  P.xZ = x->Z;
+  P.xZe = (uint64_t*)x->Zerr;
+  P.xSt = x->status;
+  P.xNR = x->NR;
+  P.xN = x->N;
+  P.xNe = (uint64_t*)x->Nerr;
+}
+
+int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream) {
+  int rc = check_launch(a);
+  if (rc) return rc;
+  if (!x) return -1;
+  if (a->rows == 0) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  rc = reserve(w, a->rows, a->splits, a->dv);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  Prob P;
+  build_prob(a, w, P);
+  set_export(P, x);
+  cudaError_t e = tc_applicable(a) ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
+  if (e != cudaSuccess) return fail_cuda(e, "partials launch");
+  return 0;
+}
+
+int ea_partials_rescale_cuda(const ea_partials_t* x, const int32_t* R_global, const int32_t* NR_global,
+                             int64_t rows, int dv, void* stream) {
+  if (!x || rows < 0 || dv <= 0) return -1;
+  if (rows == 0) return 0;
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.rows = rows;
+  P.dv = dv;
+  set_export(P, x);
+  cudaError_t e = launch_partials_rescale(P, R_global, NR_global, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "rescale");
+}
+
+int ea_partials_finalize_cuda(const ea_partials_t* x, int64_t rows, int dv, int64_t max_row_keys, int fp32_out,
+                              void* out, uint8_t* flags, int64_t* stats, void* stream) {
+  if (!x || rows < 0 || dv <= 0 || !out || !flags) return -1;
+  if (rows == 0) return 0;
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace();
+    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  }
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.rows = rows;
+  P.dv = dv;
+  P.fp32 = fp32_out ? 1 : 0;
+  P.key_log2 = ceil_log2(max_row_keys < 2 ? 2 : max_row_keys);
+  P.FZ = 61 - P.key_log2;
+  P.out = out;
+  P.flags = flags;
+  P.stats = stats ? (unsigned long long*)stats : w->stats;
+  set_export(P, x);
+  cudaError_t e = launch_partials_finalize(P, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "finalize");
 }
 
 // Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back.

@@ -64,6 +64,16 @@ struct Prob {
   int32_t* pNR;
   int64_t* pN;
   uint64_t* pNe;
+  // export: write one partial per row instead of finalising (KV-sharded runs merge them across
+  // GPUs). Layout of ea_partials_t; N is one-sided: the value lies in [N, N + Nerr] units.
+  int export_partials;
+  int32_t* xR;
+  int64_t* xZ;
+  uint64_t* xZe;
+  int32_t* xSt;
+  int32_t* xNR;
+  int64_t* xN;
+  uint64_t* xNe;
   // bookkeeping
   unsigned long long* stats;
   int* t3_count;

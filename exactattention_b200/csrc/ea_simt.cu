@@ -126,6 +126,26 @@ __device__ void finalize_row(const Prob& P, int64_t r, int status, int32_t R, in
   if (lane == 0) P.flags[r] = 0;
 }
 
+// one row's partial into the export buffers (warp per row; NR/N/Ne hold channels lane + 32 i)
+template <int CPL>
+__device__ void export_row(const Prob& P, int64_t r, int status, int32_t R, int64_t Z, uint64_t Ze,
+                           const int32_t* NR, const int64_t* N, const uint64_t* Ne, int lane) {
+  if (lane == 0) {
+    P.xR[r] = R;
+    P.xZ[r] = Z;
+    P.xZe[r] = Ze;
+    P.xSt[r] = status;
+  }
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= P.dv) continue;
+    P.xNR[r * P.dv + c] = NR[i];
+    P.xN[r * P.dv + c] = N[i];
+    P.xNe[r * P.dv + c] = Ne[i];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // tier 1
 // ---------------------------------------------------------------------------
@@ -340,7 +360,10 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
   }
 
   if (S == 1) {
-    finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+    if (P.export_partials)
+      export_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+    else
+      finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
     return;
   }
   const int64_t pi = (int64_t)s * P.rows + r;
@@ -419,7 +442,91 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
     ok &= fits63(N[i], Ne[i]);
   }
   if (!__all_sync(0xffffffffu, ok) && status == ST_OK) status = ST_TIER3;
-  finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+  if (P.export_partials)
+    export_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+  else
+    finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+}
+
+// ---------------------------------------------------------------------------
+// partials of KV shards: re-express at the global exponents, then finalise after the sum
+// ---------------------------------------------------------------------------
+// Thread per (row, channel); channel 0's thread also handles Z. Exponents Rg/NRg come from an
+// all-reduce MAX over the shards; an empty partial (R_EMPTY) contributes zeros. After this every
+// shard's integers are in the same units, so their sum (an all-reduce SUM) is order-free.
+__global__ void partials_rescale_kernel(Prob P, const int32_t* Rg, const int32_t* NRg) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P.rows * P.dv) return;
+  const int64_t r = i / P.dv;
+  const int c = (int)(i - r * P.dv);
+  if (c == 0) {
+    const int32_t R = P.xR[r], G = Rg[r];
+    if (R == R_EMPTY) {
+      P.xZ[r] = 0;
+      P.xZe[r] = 0;
+    } else if (G != R_EMPTY && G > R) {
+      int64_t z = P.xZ[r];
+      uint64_t ze = P.xZe[r];
+      rescale(z, ze, G - R);
+      P.xZ[r] = z;
+      P.xZe[r] = ze;
+    }
+    P.xR[r] = G;
+  }
+  const int32_t NR = P.xNR[i], G = NRg[i];
+  if (NR == R_EMPTY) {
+    P.xN[i] = 0;
+    P.xNe[i] = 0;
+  } else if (G != R_EMPTY && G > NR) {
+    int64_t n = P.xN[i];
+    uint64_t ne = P.xNe[i];
+    rescale(n, ne, G - NR);
+    P.xN[i] = n;
+    P.xNe[i] = ne;
+  }
+  P.xNR[i] = G;
+}
+
+// Certified rounding of summed partials (warp per row). A row no tier-1 bound certifies is
+// flagged 1: the sharded wide tier is needed for it.
+template <int CPL>
+__global__ void __launch_bounds__(128) partials_finalize_kernel(Prob P) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= P.rows) return;
+  const int status = P.xSt[r];
+  const int32_t R = P.xR[r];
+  const int64_t Z = P.xZ[r];
+  const uint64_t Ze = P.xZe[r];
+  if (status == ST_DOMAIN) {
+    for (int c = lane; c < P.dv; c += 32) write_out(P, r, c, rnd_zero());
+    if (lane == 0) P.flags[r] = 2;
+    return;
+  }
+  bool ok = status == ST_OK && (R == R_EMPTY || fits63(Z, Ze));
+  Rnd res[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    res[i] = rnd_zero();
+    const int c = lane + 32 * i;
+    if (c >= P.dv || !ok || R == R_EMPTY) continue;
+    const int32_t NR = P.xNR[r * P.dv + c];
+    if (NR == R_EMPTY) continue;
+    const int64_t N = P.xN[r * P.dv + c];
+    const uint64_t Ne = P.xNe[r * P.dv + c];
+    const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+    ok &= fits63(N, Ne) && certify_ratio(N, Ne, (int64_t)NR - P.FZ, Z, Ze, (int64_t)R - P.FZ, p, qmin, 127, res[i]);
+  }
+  ok = __all_sync(0xffffffffu, ok);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < P.dv) write_out(P, r, c, ok ? res[i] : rnd_zero());
+  }
+  if (lane == 0) {
+    P.flags[r] = ok ? 0 : 1;
+    if (!ok) stat_add(P, STAT_UNRESOLVED, 1);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -696,6 +803,21 @@ cudaError_t launch_simt(const Prob& P, cudaStream_t st) {
   if (P.dv <= 64) return launch_simt_cpl<2>(P, warps, st);
   if (P.dv <= 128) return launch_simt_cpl<4>(P, warps, st);
   return launch_simt_cpl<8>(P, warps, st);
+}
+
+cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st) {
+  const int64_t n = P.rows * P.dv;
+  partials_rescale_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(P, Rg, NRg);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st) {
+  const unsigned g = (unsigned)((P.rows + 3) / 4);
+  if (P.dv <= 32) partials_finalize_kernel<1><<<g, 128, 0, st>>>(P);
+  else if (P.dv <= 64) partials_finalize_kernel<2><<<g, 128, 0, st>>>(P);
+  else if (P.dv <= 128) partials_finalize_kernel<4><<<g, 128, 0, st>>>(P);
+  else partials_finalize_kernel<8><<<g, 128, 0, st>>>(P);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st) {

@@ -760,8 +760,29 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   }
 
   EA_PT(9)
-  // ---------------- finalise ----------------
-  {
+  // ---------------- export (KV-sharded runs) or finalise ----------------
+  if (P.export_partials) {
+    // partials in the one-sided form [N, N + Nerr] of ea_partials_t: this kernel's N interval is
+    // [N - Nerr, N + Nerr], in units 2^(R + VE_c - FN) = 2^(NR - FZ) with NR = R + VE_c
+    if (myrow >= 0) {
+      const int st = ok_wait ? S.rst[r] : ST_TIER3;
+      if (u4 == 0) {
+        P.xR[myrow] = R;
+        P.xZ[myrow] = Z;
+        P.xZe[myrow] = Zerr;
+        P.xSt[myrow] = st;
+      }
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int ch = 32 * u4 + c, ve = S.ve[ch];
+        const int64_t o = (int64_t)myrow * DV + ch;
+        const bool empty = R == R_EMPTY || ve == INT32_MIN;
+        P.xNR[o] = empty ? R_EMPTY : R + ve;
+        P.xN[o] = empty ? 0 : N[c] - (int64_t)Nerr;
+        P.xNe[o] = empty ? 0 : 2 * Nerr;
+      }
+    }
+  } else {
     const int st = S.rst[r];
     uint32_t outw[16];
     bool ok = ok_wait && st == ST_OK && !P.fp32;

@@ -118,12 +118,35 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     dev = q.device
     if dev.type != "cuda":
         raise RuntimeError("launch needs CUDA tensors (there is no CPU path)")
-    rows, d = q.shape[0], q.shape[-1]
+    rows = q.shape[0]
     dv = v.shape[-1]
     if out_tensor is None:
         out_tensor = torch.empty((rows, dv), dtype=torch.int32 if out == "fp32" else torch.int16, device=dev)
     if flags is None:
         flags = torch.empty(rows, dtype=torch.uint8, device=dev)
+    a = _launch_args(q, k, v, alpha, row_ptr=row_ptr, key_idx=key_idx, kv_base=kv_base, kv_len=kv_len,
+                     page_table=page_table, seq_lens=seq_lens, page_size=page_size, q_heads=q_heads,
+                     kv_heads=kv_heads, max_row_keys=max_row_keys, splits=splits, out=out, blocks=blocks)
+    a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
+    a.stats = _ptr(stats)
+    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        if no_alloc:
+            rc = lib.ea_attention_cuda_noalloc(ctypes.byref(a), ctypes.c_void_p(s))
+            if rc == -6:
+                raise ValueError(lib.ea_noalloc_last_error().decode())
+            _lib.check(rc, "ea_attention_cuda_noalloc")
+        else:
+            _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
+    return out_tensor, flags
+
+
+def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
+                 seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
+                 blocks=None):
+    """ea_launch_t for `launch`'s inputs and mask (outputs left unset)."""
+    rows, d = q.shape[0], q.shape[-1]
+    dv = v.shape[-1]
     a = _lib.LaunchArgs()
     a.q, a.rows, a.d = q.data_ptr(), rows, d
     a.k, a.v, a.nkeys, a.dv = k.data_ptr(), v.data_ptr(), k.numel() // d, dv
@@ -156,20 +179,94 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     a.max_row_keys = int(max(1, max_row_keys))
     a.fp32_out = int(out == "fp32")
     a.splits = int(splits)
-    a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
-    a.stats = _ptr(stats)
     if blocks is not None:
         a.block_rows, a.nblocks = blocks.data_ptr(), blocks.shape[0]
-    s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+    return a
+
+
+class Partials:
+    """Row partials of one key range (ea_partials_t), as views into two flat device buffers so
+    that a merge needs one MAX all-reduce (`i32`: R, status, NR) and one SUM all-reduce (`i64`:
+    Z, Zerr, N, Nerr)."""
+
+    def __init__(self, rows: int, dv: int, device):
+        import torch
+
+        self.rows, self.dv = rows, dv
+        self.i32 = torch.empty(rows * (2 + dv), dtype=torch.int32, device=device)
+        self.i64 = torch.empty(rows * (2 + 2 * dv), dtype=torch.int64, device=device)
+        self.R, self.status = self.i32[:rows], self.i32[rows:2 * rows]
+        self.NR = self.i32[2 * rows:].view(rows, dv)
+        self.Z, self.Zerr = self.i64[:rows], self.i64[rows:2 * rows]
+        self.N = self.i64[2 * rows:(2 + dv) * rows].view(rows, dv)
+        self.Nerr = self.i64[(2 + dv) * rows:].view(rows, dv)
+
+    def struct(self) -> "_lib.PartialsArgs":
+        p = _lib.PartialsArgs()
+        p.R, p.Z, p.Zerr, p.status = (self.R.data_ptr(), self.Z.data_ptr(), self.Zerr.data_ptr(),
+                                      self.status.data_ptr())
+        p.NR, p.N, p.Nerr = self.NR.data_ptr(), self.N.data_ptr(), self.Nerr.data_ptr()
+        return p
+
+    def numpy(self) -> dict:
+        return {k: getattr(self, k).cpu().numpy() for k in ("R", "Z", "Zerr", "status", "NR", "N", "Nerr")}
+
+
+def _stream(dev, stream):
+    import torch
+
+    return stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+
+
+def partials(q, k, v, alpha, *, parts: Partials | None = None, stream=None, stats=None, **mask) -> Partials:
+    """Tier-1 partials of every row over its masked keys (ea_partials_cuda); `mask` takes
+    `launch`'s mask keywords (and `splits`, `blocks`). max_row_keys must bound the row's key count
+    over ALL key ranges that will be merged, and be the same for each of them."""
+    import torch
+
+    lib = _lib.load()
+    dev = q.device
+    if dev.type != "cuda":
+        raise RuntimeError("partials needs CUDA tensors (there is no CPU path)")
+    if mask.get("max_row_keys") is None:
+        raise ValueError("partials needs max_row_keys (the row's key count over all merged ranges)")
+    if parts is None:
+        parts = Partials(q.shape[0], v.shape[-1], dev)
+    a = _launch_args(q, k, v, alpha, **mask)
+    a.stats = _ptr(stats)
+    p = parts.struct()
     with torch.cuda.device(dev):
-        if no_alloc:
-            rc = lib.ea_attention_cuda_noalloc(ctypes.byref(a), ctypes.c_void_p(s))
-            if rc == -6:
-                raise ValueError(lib.ea_noalloc_last_error().decode())
-            _lib.check(rc, "ea_attention_cuda_noalloc")
-        else:
-            _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
-    return out_tensor, flags
+        _lib.check(lib.ea_partials_cuda(ctypes.byref(a), ctypes.byref(p), ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_partials_cuda")
+    return parts
+
+
+def rescale_partials(parts: Partials, R_global, NR_global, stream=None) -> None:
+    """Re-express `parts` at the merged exponents, in place (ea_partials_rescale_cuda)."""
+    import torch
+
+    p = parts.struct()
+    dev = parts.i32.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_partials_rescale_cuda(ctypes.byref(p), R_global.data_ptr(), NR_global.data_ptr(),
+                                                        parts.rows, parts.dv, ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_partials_rescale_cuda")
+
+
+def finalize_partials(parts: Partials, max_row_keys: int, out="bf16", stats=None, stream=None):
+    """Certified outputs from merged partials (ea_partials_finalize_cuda): (out bits, flags)."""
+    import torch
+
+    dev = parts.i32.device
+    o = torch.empty((parts.rows, parts.dv), dtype=torch.int32 if out == "fp32" else torch.int16, device=dev)
+    fl = torch.empty(parts.rows, dtype=torch.uint8, device=dev)
+    p = parts.struct()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_partials_finalize_cuda(ctypes.byref(p), parts.rows, parts.dv, int(max_row_keys),
+                                                         int(out == "fp32"), o.data_ptr(), fl.data_ptr(),
+                                                         _ptr(stats), ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_partials_finalize_cuda")
+    return o, fl
 
 
 def reserve_workspace(rows: int, splits: int, dv: int) -> None:

@@ -100,6 +100,42 @@ typedef struct ea_launch {
  * ea_reserve_workspace or on first use). The torch-tensor API builds on this. */
 int ea_launch_cuda(const ea_launch_t* args, void* stream);
 
+/* Per-row partial state of one key range (the split partial of the reference's certified
+ * split-KV kernel, cuda/exact_attention_kernel.cu, exported to device buffers so that partials
+ * computed on different GPUs can be merged). All device pointers; rows x dv for NR, N, Nerr.
+ *   R       row exponent: Z = Z_int * 2^(R - FZ); INT32_MIN for a row with no keys
+ *   Z, Zerr lower bound of the weight sum and its nonnegative error, in units 2^(R - FZ)
+ *   status  0 certified so far, 1 needs the exact tier (tier 3), 2 domain error
+ *   NR      per-channel exponent of the numerator (INT32_MIN: no contribution)
+ *   N, Nerr lower bound of the numerator and its error, units 2^(NR - FZ)
+ * FZ = 61 - ceil(log2(max_row_keys)) for the launch's max_row_keys (must be the same on every
+ * rank). Merging: R_g = max over ranks of R, NR_g = max of NR, status = max of status; every
+ * rank rescales to (R_g, NR_g) with ea_partials_rescale_cuda (floor shifts, error grown by one
+ * unit per shifted value); then Z, Zerr, N, Nerr are summed over ranks; the sum is finalised
+ * by ea_partials_finalize_cuda. Every step is order independent, so any all-reduce tree gives
+ * the same bits. No reference counterpart as a separate entry point: the reference merges
+ * split partials inside one launch (exact_attention_kernel.cu combine step). */
+typedef struct ea_partials {
+  int32_t* R;
+  int64_t* Z;
+  int64_t* Zerr;
+  int32_t* status;
+  int32_t* NR;
+  int64_t* N;
+  int64_t* Nerr;
+} ea_partials_t;
+
+/* Tier-1 pass of `args` (any mask, any splits; the tensor-core kernel where it applies) that
+ * writes the row partials instead of outputs. args->out/flags are not written. */
+int ea_partials_cuda(const ea_launch_t* args, const ea_partials_t* parts, void* stream);
+/* In-place rescale of `parts` to the global exponents R_global (rows) and NR_global (rows x dv). */
+int ea_partials_rescale_cuda(const ea_partials_t* parts, const int32_t* R_global, const int32_t* NR_global,
+                             int64_t rows, int dv, void* stream);
+/* Certified rounding of merged partials into out/flags (flag 1: not certifiable from the merged
+ * interval, the row needs the exact tier; flag 2: domain error). */
+int ea_partials_finalize_cuda(const ea_partials_t* parts, int64_t rows, int dv, int64_t max_row_keys,
+                              int fp32_out, void* out, uint8_t* flags, int64_t* stats, void* stream);
+
 /* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
  * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,
  * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the

@@ -5,6 +5,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 from exactattention_b200 import _lib
 
 ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
@@ -27,20 +29,21 @@ def test_library_exports_every_declared_symbol(cuda_lib):
     assert set(_lib.EXPORTS) <= names
 
 
-def test_launch_struct_layout_matches_header(cuda_lib, tmp_path):
-    """The ctypes mirror of ea_launch_t has the C compiler's size and field offsets."""
+@pytest.mark.parametrize("ctype,mirror", [("ea_launch_t", _lib.LaunchArgs), ("ea_partials_t", _lib.PartialsArgs)])
+def test_struct_layout_matches_header(cuda_lib, tmp_path, ctype, mirror):
+    """The ctypes mirrors of the header's structs have the C compiler's size and field offsets."""
     import subprocess
 
-    fields = [f[0] for f in _lib.LaunchArgs._fields_]
+    fields = [f[0] for f in mirror._fields_]
     src = tmp_path / "sz.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "exactattn_cuda.h"\nint main(void){'
-                   'printf("%zu", sizeof(ea_launch_t));'
-                   + "".join(f'printf(" %zu", offsetof(ea_launch_t, {f}));' for f in fields) + "return 0;}\n")
+                   f'printf("%zu", sizeof({ctype}));'
+                   + "".join(f'printf(" %zu", offsetof({ctype}, {f}));' for f in fields) + "return 0;}\n")
     exe = tmp_path / "sz"
     subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), "-o", str(exe), str(src)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(_lib.LaunchArgs)
-    assert vals[1:] == [getattr(_lib.LaunchArgs, f).offset for f in fields]
+    assert vals[0] == ctypes.sizeof(mirror)
+    assert vals[1:] == [getattr(mirror, f).offset for f in fields]
 
 
 def test_build_targets_sm100a():

@@ -1,0 +1,137 @@
+"""KV-range sharding on the GPU: partials of disjoint key ranges, merged max-then-sum, must give
+the bits of one launch over the whole range and of the oracle (B200 only).
+
+Ranks are emulated on one GPU (one partials call per key range, the collectives replaced by
+torch max / sum over the ranges); the NCCL form runs in test_gpu_multi.py when the box has two
+or more GPUs.
+"""
+
+import numpy as np
+import pytest
+
+from gen import bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(x, dev):
+    import torch
+
+    return torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)
+
+
+def merge_local(parts_list):
+    """The merge of exactattention_b200.dist.merge_partials over in-process ranges."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    mx = torch.stack([p.i32 for p in parts_list]).max(0).values
+    rows, dv = parts_list[0].rows, parts_list[0].dv
+    for p in parts_list:
+        cuda.rescale_partials(p, mx[:rows], mx[2 * rows:].view(rows, dv))
+    out = parts_list[0]
+    out.status.copy_(mx[rows:2 * rows])
+    for p in parts_list[1:]:
+        out.i64 += p.i64
+    return out
+
+
+def _bounds(n, shards):
+    return [(n * s // shards, n * (s + 1) // shards) for s in range(shards)]
+
+
+@pytest.mark.parametrize("kind,vkind,d", [("normal", "normal", 128), ("outlier", "wide", 128), ("wide", "normal", 64),
+                                          ("dupes", "dupes", 128)])
+@pytest.mark.parametrize("shards", [2, 3, 8])
+def test_kv_shards_simt_match_full_and_oracle(kind, vkind, d, shards):
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(hash((kind, vkind, d, shards)) & 0xFFFF)
+    rows, n = 12, 1500
+    Q, K, V = bf16(rng, (rows, d), kind), bf16(rng, (n, d), kind), bf16(rng, (n, d), vkind)
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(d)
+    kb = np.zeros(rows, np.int64)
+    kl = np.full(rows, n, np.int64)
+    kl[3] = 0
+    kl[5] = 700  # rows whose range ends inside a shard or before it: empty partials there
+    full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
+    parts = []
+    for i, (lo, hi) in enumerate(_bounds(n, shards)):
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
+                                   kv_len=_t(klen, dev), max_row_keys=n, splits=1 + i % 3))
+    merged = merge_local(parts)
+    out, flags = cuda.finalize_partials(merged, n)
+    torch.cuda.synchronize()
+    assert not flags.any().item() and not fflags.any().item()
+    assert torch.equal(out, full)
+    o = out.cpu().numpy().view(np.uint16)
+    for r in (0, 3, 5, rows - 1):
+        L = int(kl[r])
+        assert np.array_equal(o[r], exact.attention_row(Q[r], K[:L], V[:L], alpha)), r
+
+
+@pytest.mark.parametrize("shards", [2, 4])
+def test_kv_shards_tensor_core_match_full(shards):
+    """Causal rows through the tensor-core kernel's export: every shard's rows still form blocks
+    sharing a key range."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(40 + shards)
+    S, heads = 640, 2
+    Q = bf16(rng, (heads * S, 128), "outlier")
+    K, V = bf16(rng, (S, 128), "outlier"), bf16(rng, (S, 128), "wide")
+    kb = np.zeros(heads * S, np.int64)
+    kl = np.tile(np.arange(1, S + 1, dtype=np.int64), heads)
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(128)
+    full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
+                               blocks=_t(cuda.row_blocks(kb, kl), dev))
+    parts = []
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    for lo, hi in _bounds(S, shards):
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
+                                   kv_len=_t(klen, dev), max_row_keys=S, blocks=_t(cuda.row_blocks(kb, klen), dev),
+                                   stats=st))
+    out, flags = cuda.finalize_partials(merge_local(parts), S)
+    torch.cuda.synchronize()
+    assert st.cpu().numpy()[7] == int(kl.sum()), "the tensor-core kernel did not run"
+    assert not flags.any().item() and not fflags.any().item()
+    assert torch.equal(out, full)
+
+
+def test_kv_shards_domain_error_propagates():
+    """A NaN key in one shard makes the merged row a domain error (flag 2, zero output)."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(9)
+    rows, n, d = 6, 400, 64
+    Q, K, V = bf16(rng, (rows, d)), bf16(rng, (n, d)), bf16(rng, (n, d))
+    K[350, 3] = 0x7F80
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(d)
+    kb = np.zeros(rows, np.int64)
+    kl = np.array([n, 300, n, 351, 350, n], np.int64)
+    full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
+    parts = []
+    for lo, hi in _bounds(n, 2):
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
+                                   kv_len=_t(klen, dev), max_row_keys=n))
+    out, flags = cuda.finalize_partials(merge_local(parts), n)
+    torch.cuda.synchronize()
+    assert flags.cpu().numpy().tolist() == [2, 0, 2, 2, 0, 2]
+    assert torch.equal(flags, fflags) and torch.equal(out, full)

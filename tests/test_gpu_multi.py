@@ -1,0 +1,80 @@
+"""KV-range sharding over real ranks: one process per GPU, NCCL all-reduces (B200, >= 2 GPUs).
+
+Every rank holds a contiguous key range; dist.attention_kv_sharded must return, on every rank,
+the bits one single-GPU launch gives over all keys. Skipped when the box has one GPU.
+"""
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+from gen import bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(d=128):
+    rng = np.random.default_rng(515)
+    rows, n = 32, 6000
+    Q, K, V = bf16(rng, (rows, d), "outlier"), bf16(rng, (n, d), "outlier"), bf16(rng, (n, d), "wide")
+    kl = rng.integers(n // 2, n + 1, rows).astype(np.int64)
+    return Q, K, V, kl
+
+
+def _worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import dist as ea_dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        Q, K, V, kl = _case()
+        n = K.shape[0]
+        lo, hi = n * rank // world, n * (rank + 1) // world
+        t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        out, flags = ea_dist.attention_kv_sharded(t(Q), t(K[lo:hi]), t(V[lo:hi]), ea.default_alpha(128),
+                                                  max_row_keys=n, kv_base=t(np.zeros_like(kl)), kv_len=t(klen))
+        torch.cuda.synchronize(dev)
+        np.save(os.path.join(result_dir, f"out_{rank}.npy"), out.cpu().numpy())
+        np.save(os.path.join(result_dir, f"flags_{rank}.npy"), flags.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_nccl_kv_sharded_matches_single_gpu(world, tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    Q, K, V, kl = _case()
+    dev = torch.device("cuda", 0)
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    full, fflags = cuda.launch(t(Q), t(K), t(V), ea.default_alpha(128), kv_base=t(np.zeros_like(kl)), kv_len=t(kl))
+    full = full.cpu().numpy()
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"flags_{r}.npy"), fflags.cpu().numpy()), r
+        assert np.array_equal(np.load(tmp_path / f"out_{r}.npy"), full), r
