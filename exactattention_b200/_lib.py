@@ -18,7 +18,9 @@ STAT_NAMES = ("score_exact", "weight_wide", "tier3_rows", "domain_rows", "unreso
 # Every symbol include/exactattn_cuda.h declares.
 EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda", "ea_launch_cuda",
            "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error", "ea_attention_cuda_noalloc",
-           "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda")
+           "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
+           "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda")
+WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
 class LaunchArgs(ctypes.Structure):
@@ -45,6 +47,11 @@ class PartialsArgs(ctypes.Structure):
     _fields_ = [("R", ctypes.c_void_p), ("Z", ctypes.c_void_p), ("Zerr", ctypes.c_void_p),
                 ("status", ctypes.c_void_p), ("NR", ctypes.c_void_p), ("N", ctypes.c_void_p),
                 ("Nerr", ctypes.c_void_p)]
+
+
+class WidePartialsArgs(ctypes.Structure):
+    """ea_wide_partials_t (include/exactattn_cuda.h)."""
+    _fields_ = [("maxv", ctypes.c_void_p), ("sumv", ctypes.c_void_p)]
 
 
 def load(path: str | None = None):
@@ -80,6 +87,13 @@ def load(path: str | None = None):
     lib.ea_partials_finalize_cuda.argtypes = [ctypes.POINTER(PartialsArgs), ctypes.c_int64, ctypes.c_int,
                                               ctypes.c_int64, ctypes.c_int, P, P, P, P]
     lib.ea_partials_finalize_cuda.restype = ctypes.c_int
+    W = ctypes.POINTER(WidePartialsArgs)
+    lib.ea_wide_partials_cuda.argtypes = [ctypes.POINTER(LaunchArgs), P, ctypes.c_int, W, P]
+    lib.ea_wide_partials_cuda.restype = ctypes.c_int
+    lib.ea_wide_partials_rescale_cuda.argtypes = [W, P, ctypes.c_int, ctypes.c_int, P]
+    lib.ea_wide_partials_rescale_cuda.restype = ctypes.c_int
+    lib.ea_wide_partials_finalize_cuda.argtypes = [W, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P]
+    lib.ea_wide_partials_finalize_cuda.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
     lib.ea_reserve_workspace.restype = ctypes.c_int
     lib.ea_cuda_release.argtypes = []

@@ -19,6 +19,8 @@ cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
 cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st);
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
 cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
+cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
+cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 }  // namespace ea
 
 using namespace ea;
@@ -501,3 +503,66 @@ extern "C" float ea_round_ratio_cuda(uint64_t a_hi, uint64_t a_lo, uint64_t b_hi
   memcpy(&f, &h[0], 4);
   return f;
 }
+
+// wide (tier-3) partials of KV shards
+extern "C" {
+
+int ea_wide_partials_cuda(const ea_launch_t* a, const int32_t* rows, int n, const ea_wide_partials_t* x,
+                          void* stream) {
+  int rc = check_launch(a);
+  if (rc) return rc;
+  if (!x || n < 0 || a->dv > 256 || (n > 0 && !rows)) return -1;
+  if (n == 0 || a->rows == 0) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  Prob P;
+  build_prob(a, w, P);
+  P.export_partials = 1;
+  P.w3max = x->maxv;
+  P.w3sum = x->sumv;
+  P.t3_list = (int*)rows;
+  P.t3_fixed = n;
+  cudaError_t e = launch_tier3(P, n < 2 * w->sms ? n : 2 * w->sms, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "wide partials");
+}
+
+int ea_wide_partials_rescale_cuda(const ea_wide_partials_t* x, const int64_t* merged_max, int n, int dv,
+                                  void* stream) {
+  if (!x || !merged_max || n < 0 || dv <= 0 || dv > 256) return -1;
+  if (n == 0) return 0;
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.dv = dv;
+  P.w3max = x->maxv;
+  P.w3sum = x->sumv;
+  cudaError_t e = launch_wide_rescale(P, n, merged_max, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "wide rescale");
+}
+
+int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* x, const int64_t* merged_max, const int32_t* rows,
+                                   int n, int dv, int fp32_out, void* out, uint8_t* flags, int64_t* stats,
+                                   void* stream) {
+  if (!x || !merged_max || n < 0 || dv <= 0 || dv > 256 || !out || !flags || (n > 0 && !rows)) return -1;
+  if (n == 0) return 0;
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace();
+    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  }
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.dv = dv;
+  P.fp32 = fp32_out ? 1 : 0;
+  P.out = out;
+  P.flags = flags;
+  P.stats = stats ? (unsigned long long*)stats : w->stats;
+  P.w3max = x->maxv;
+  P.w3sum = x->sumv;
+  P.t3_list = (int*)rows;
+  cudaError_t e = launch_wide_finalize(P, n, merged_max, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "wide finalize");
+}
+
+}  // extern "C"

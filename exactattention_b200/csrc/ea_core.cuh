@@ -74,10 +74,16 @@ struct Prob {
   int32_t* xNR;
   int64_t* xN;
   uint64_t* xNe;
+  // wide (tier-3) partials of the rows in t3_list, when export_partials is set for tier 3:
+  // w3max (n x 4, merged by MAX): R, Emax, -Emin, status; w3sum (n x (dv + 1) x (LW + 1),
+  // merged by SUM): Z's LW digits and Zerr, then each channel's N digits and Nerr
+  int64_t* w3max;
+  int64_t* w3sum;
   // bookkeeping
   unsigned long long* stats;
   int* t3_count;
   int* t3_list;
+  int t3_fixed;  // > 0: number of listed rows (instead of *t3_count)
 };
 
 __device__ __forceinline__ int64_t row_len(const Prob& P, int64_t r) {

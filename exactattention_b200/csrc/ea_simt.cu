@@ -488,7 +488,7 @@ __global__ void partials_rescale_kernel(Prob P, const int32_t* Rg, const int32_t
 }
 
 // Certified rounding of summed partials (warp per row). A row no tier-1 bound certifies is
-// flagged 1: the sharded wide tier is needed for it.
+// flagged 1 (and counted as a tier-3 row): the sharded wide tier finishes it.
 template <int CPL>
 __global__ void __launch_bounds__(128) partials_finalize_kernel(Prob P) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(128) partials_finalize_kernel(Prob P) {
   }
   if (lane == 0) {
     P.flags[r] = ok ? 0 : 1;
-    if (!ok) stat_add(P, STAT_UNRESOLVED, 1);
+    if (!ok) stat_add(P, STAT_TIER3_ROWS, 1);
   }
 }
 
@@ -552,6 +552,46 @@ __device__ __forceinline__ int64_t block_max64(int64_t x, int64_t* red) {
   return m;
 }
 
+// RN of N / Z from the wide intervals N in [N, N + Nerr] (units 2^(R + 128 - FW)) and Z in
+// [Z, Z + Zerr] (units 2^(R - FW)), both normalised: true (and res) when both ends round alike.
+__device__ bool wide_round(const Prob& P, const Wide<LW>& Zw, uint64_t Zerr, const Wide<LW>& Nw, uint64_t Nerr,
+                           Rnd& res) {
+  uint32_t za[LW + 1], zb[LW + 1], na[LW + 1];
+  Zw.magnitude(za);
+  for (int i = 0; i <= LW; ++i) zb[i] = za[i];
+  big_add_u64(zb, LW + 1, Zerr);
+  bool nneg = Nw.magnitude(na);
+  uint32_t nlo[LW + 1], nhi[LW + 1];
+  const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+  Rnd rl, rh;
+  if (!nneg) {
+    for (int i = 0; i <= LW; ++i) nlo[i] = nhi[i] = na[i];
+    big_add_u64(nhi, LW + 1, Nerr);
+    rl = round_ratio_big<LW + 4>(nlo, zb, LW + 1, 128, 0, p, qmin, 127);
+    rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
+  } else {
+    // N = -|N|; the high end N + Nerr may cross zero
+    for (int i = 0; i <= LW; ++i) nlo[i] = na[i];
+    rl = round_ratio_big<LW + 4>(nlo, za, LW + 1, 128, 1, p, qmin, 127);
+    // |N| - Nerr, or Nerr - |N| if that is negative
+    uint32_t e[LW + 1];
+    for (int i = 0; i <= LW; ++i) e[i] = 0;
+    big_add_u64(e, LW + 1, Nerr);
+    if (big_cmp(na, e, LW + 1) >= 0) {
+      for (int i = 0; i <= LW; ++i) nhi[i] = na[i];
+      big_sub(nhi, e, LW + 1);
+      rh = round_ratio_big<LW + 4>(nhi, zb, LW + 1, 128, 1, p, qmin, 127);
+    } else {
+      for (int i = 0; i <= LW; ++i) nhi[i] = e[i];
+      big_sub(nhi, na, LW + 1);
+      rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
+    }
+  }
+  res = rl;
+  if (res.q == 0) res.neg = 0;
+  return rnd_eq(rl, rh);
+}
+
 __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
   __shared__ uint32_t sM[T3_THREADS];
   __shared__ int64_t sE[T3_THREADS];
@@ -561,7 +601,7 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
   const int tid = threadIdx.x;
   const int d = P.d, dv = P.dv;
   const int64_t FW = 32ll * LW - 64 - P.key_log2;
-  const int count = *P.t3_count;
+  const int count = P.t3_fixed > 0 ? P.t3_fixed : *P.t3_count;
 
   for (int item = blockIdx.x; item < count; item += gridDim.x) {
     const int64_t r = P.t3_list[item];
@@ -701,47 +741,36 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       __syncthreads();
       const int st = sStatus;
       __syncthreads();  // every thread has read sStatus before any finalisation writes it
+      if (P.export_partials) {
+        // this key range's wide partial (normalised digits), merged across GPUs by
+        // wide_rescale_kernel and an all-reduce SUM, finalised by wide_finalize_kernel
+        Zw.normalize();
+        Nw.normalize();
+        int64_t* base = P.w3sum + (int64_t)item * (dv + 1) * (LW + 1);
+        if (c0 == 0 && tid == 0) {
+          for (int i = 0; i < LW; ++i) base[i] = Zw.d[i];
+          base[LW] = (int64_t)Zerr;
+          int64_t* mx = P.w3max + (int64_t)item * 4;
+          mx[0] = R;
+          mx[1] = Emax;
+          mx[2] = Emin == INT64_MAX ? INT64_MIN : -Emin;
+          mx[3] = st;
+        }
+        if (c < dv) {
+          int64_t* o = base + (int64_t)(1 + c) * (LW + 1);
+          for (int i = 0; i < LW; ++i) o[i] = Nw.d[i];
+          o[LW] = (int64_t)Nerr;
+        }
+        __syncthreads();
+        continue;
+      }
       if (st == ST_OK && c < dv) {
         Rnd res = rnd_zero();
         bool ok = true;
         if (R != INT64_MIN && has_n) {
           Zw.normalize();
           Nw.normalize();
-          uint32_t za[LW + 1], zb[LW + 1], na[LW + 1];
-          Zw.magnitude(za);
-          for (int i = 0; i <= LW; ++i) zb[i] = za[i];
-          big_add_u64(zb, LW + 1, Zerr);
-          bool nneg = Nw.magnitude(na);
-          // N interval [N, N + Nerr]
-          uint32_t nlo[LW + 1], nhi[LW + 1];
-          const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
-          Rnd rl, rh;
-          if (!nneg) {
-            for (int i = 0; i <= LW; ++i) nlo[i] = nhi[i] = na[i];
-            big_add_u64(nhi, LW + 1, Nerr);
-            rl = round_ratio_big<LW + 4>(nlo, zb, LW + 1, 128, 0, p, qmin, 127);
-            rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
-          } else {
-            // N = -|N|; the high end N + Nerr may cross zero
-            for (int i = 0; i <= LW; ++i) nlo[i] = na[i];
-            rl = round_ratio_big<LW + 4>(nlo, za, LW + 1, 128, 1, p, qmin, 127);
-            // |N| - Nerr, or Nerr - |N| if that is negative
-            uint32_t e[LW + 1];
-            for (int i = 0; i <= LW; ++i) e[i] = 0;
-            big_add_u64(e, LW + 1, Nerr);
-            if (big_cmp(na, e, LW + 1) >= 0) {
-              for (int i = 0; i <= LW; ++i) nhi[i] = na[i];
-              big_sub(nhi, e, LW + 1);
-              rh = round_ratio_big<LW + 4>(nhi, zb, LW + 1, 128, 1, p, qmin, 127);
-            } else {
-              for (int i = 0; i <= LW; ++i) nhi[i] = e[i];
-              big_sub(nhi, na, LW + 1);
-              rh = round_ratio_big<LW + 4>(nhi, za, LW + 1, 128, 0, p, qmin, 127);
-            }
-          }
-          ok = rnd_eq(rl, rh);
-          res = rl;
-          if (res.q == 0) res.neg = 0;
+          ok = wide_round(P, Zw, Zerr, Nw, Nerr, res);
         }
         if (ok) {
           write_out(P, r, c, res);
@@ -755,6 +784,10 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       if (st2 != ST_OK) break;
     }
     __syncthreads();
+    if (P.export_partials) {
+      __syncthreads();  // the next row resets sStatus
+      continue;
+    }
     if (tid == 0) {
       const int st = sStatus;
       if (st == ST_DOMAIN) {
@@ -771,6 +804,93 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
     if (stf == ST_DOMAIN)
       for (int c = tid; c < dv; c += T3_THREADS) write_out(P, r, c, rnd_zero());
     __syncthreads();  // the next row resets sStatus
+  }
+}
+
+// ---------------------------------------------------------------------------
+// wide partials of KV shards (rows tier 1 could not certify after the merge)
+// ---------------------------------------------------------------------------
+// Thread per (listed row, j): j = 0 is Z, j = 1 + c is channel c's N. The wide windows of every
+// shard are shifted down to the merged reference exponent (floor; a dropped nonzero bit and the
+// shifted error's ceiling add to the error, as in tier3_kernel's re-anchoring), after which the
+// digit-wise SUM over shards is the exact sum of the shards' windows.
+__global__ void wide_rescale_kernel(Prob P, int n, const int64_t* gmax) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * (P.dv + 1)) return;
+  const int64_t item = i / (P.dv + 1);
+  int64_t* a = P.w3sum + i * (LW + 1);
+  const int64_t R = P.w3max[item * 4], G = gmax[item * 4];
+  if (R == INT64_MIN) {
+    for (int k = 0; k <= LW; ++k) a[k] = 0;
+    return;
+  }
+  if (G <= R) return;
+  Wide<LW> w;
+  for (int k = 0; k < LW; ++k) w.d[k] = a[k];
+  uint64_t err = (uint64_t)a[LW];
+  const int64_t sft = G - R;
+  const bool lost = w.shr(sft);
+  err = sft >= 64 ? (err != 0) : ((err >> sft) + ((err & ((1ull << sft) - 1)) != 0));
+  err += lost;
+  for (int k = 0; k < LW; ++k) a[k] = w.d[k];
+  a[LW] = (int64_t)err;
+}
+
+// Block per listed row: certified rounding of the merged wide sums into the row's outputs.
+__global__ void __launch_bounds__(T3_THREADS) wide_finalize_kernel(Prob P, int n, const int64_t* gmax) {
+  __shared__ int sOk;
+  const int item = blockIdx.x, tid = threadIdx.x;
+  if (item >= n) return;
+  const int64_t r = P.t3_list[item];
+  const int64_t* g = gmax + (int64_t)item * 4;
+  const int64_t R = g[0], Emax = g[1], Emin = g[2] == INT64_MIN ? INT64_MAX : -g[2];
+  int st = (int)g[3];
+  if (st == ST_OK && R != INT64_MIN && Emax - Emin > MAX_SPREAD) st = ST_DOMAIN;
+  if (tid == 0) sOk = 1;
+  __syncthreads();
+  bool ok = st == ST_OK;
+  const int64_t* base = P.w3sum + (int64_t)item * (P.dv + 1) * (LW + 1);
+  Wide<LW> Zw;
+  uint64_t Zerr = 0;
+  if (ok && R != INT64_MIN) {
+    for (int k = 0; k < LW; ++k) Zw.d[k] = base[k];
+    Zerr = (uint64_t)base[LW];
+    Zw.normalize();
+  }
+  constexpr int CPT = 256 / T3_THREADS;  // dv <= 256
+  Rnd res[CPT];
+  for (int i = 0; i < CPT; ++i) {
+    res[i] = rnd_zero();
+    const int c = tid + i * T3_THREADS;
+    if (!ok || c >= P.dv || R == INT64_MIN) continue;
+    const int64_t* o = base + (int64_t)(1 + c) * (LW + 1);
+    Wide<LW> Nw;
+    bool any = o[LW] != 0;
+    for (int k = 0; k < LW; ++k) {
+      Nw.d[k] = o[k];
+      any |= o[k] != 0;
+    }
+    if (!any) continue;
+    Nw.normalize();
+    ok &= wide_round(P, Zw, Zerr, Nw, (uint64_t)o[LW], res[i]);
+  }
+  if (st == ST_OK && !ok) atomicAnd(&sOk, 0);
+  __syncthreads();
+  const bool rowok = st == ST_OK && sOk != 0;
+  for (int i = 0; i < CPT; ++i) {
+    const int c = tid + i * T3_THREADS;
+    if (c < P.dv) write_out(P, r, c, rowok ? res[i] : rnd_zero());
+  }
+  if (tid == 0) {
+    if (st == ST_DOMAIN) {
+      P.flags[r] = 2;
+      stat_add(P, STAT_DOMAIN_ROWS, 1);
+    } else if (!rowok) {
+      P.flags[r] = 1;
+      stat_add(P, STAT_UNRESOLVED, 1);
+    } else {
+      P.flags[r] = 0;
+    }
   }
 }
 
@@ -817,6 +937,17 @@ cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st) {
   else if (P.dv <= 64) partials_finalize_kernel<2><<<g, 128, 0, st>>>(P);
   else if (P.dv <= 128) partials_finalize_kernel<4><<<g, 128, 0, st>>>(P);
   else partials_finalize_kernel<8><<<g, 128, 0, st>>>(P);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st) {
+  const int64_t m = (int64_t)n * (P.dv + 1);
+  wide_rescale_kernel<<<(unsigned)((m + 127) / 128), 128, 0, st>>>(P, n, gmax);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st) {
+  wide_finalize_kernel<<<n, T3_THREADS, 0, st>>>(P, n, gmax);
   return cudaGetLastError();
 }
 

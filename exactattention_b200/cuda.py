@@ -329,3 +329,68 @@ def row_blocks(kv_base: np.ndarray, kv_len: np.ndarray, bm: int = 128) -> np.nda
     arr = np.stack(out)
     first_len = kv_len[arr[:, 0]]
     return arr[np.argsort(-first_len, kind="stable")]
+
+
+class WidePartials:
+    """Wide (tier-3) partials of `n` listed rows (ea_wide_partials_t): `maxv` (n, 4) int64 merged
+    by MAX, `sumv` (n, dv + 1, WIDE_DIGITS + 1) int64 merged by SUM."""
+
+    def __init__(self, n: int, dv: int, device):
+        import torch
+
+        self.n, self.dv = n, dv
+        self.maxv = torch.empty((n, 4), dtype=torch.int64, device=device)
+        self.sumv = torch.empty((n, dv + 1, _lib.WIDE_DIGITS + 1), dtype=torch.int64, device=device)
+
+    def struct(self) -> "_lib.WidePartialsArgs":
+        w = _lib.WidePartialsArgs()
+        w.maxv, w.sumv = self.maxv.data_ptr(), self.sumv.data_ptr()
+        return w
+
+
+def wide_partials(q, k, v, alpha, rows, *, stream=None, stats=None, **mask) -> WidePartials:
+    """Wide partials over this key range of the rows listed in `rows` (int32 device tensor),
+    ea_wide_partials_cuda; `mask` as for `partials` (max_row_keys required)."""
+    import torch
+
+    lib = _lib.load()
+    dev = q.device
+    if mask.get("max_row_keys") is None:
+        raise ValueError("wide_partials needs max_row_keys (the row's key count over all merged ranges)")
+    rows = rows.to(device=dev, dtype=torch.int32).contiguous()
+    w = WidePartials(rows.numel(), v.shape[-1], dev)
+    mask = {k_: v_ for k_, v_ in mask.items() if k_ not in ("blocks", "splits")}
+    a = _launch_args(q, k, v, alpha, **mask)
+    a.stats = _ptr(stats)
+    ws = w.struct()
+    with torch.cuda.device(dev):
+        _lib.check(lib.ea_wide_partials_cuda(ctypes.byref(a), rows.data_ptr(), w.n, ctypes.byref(ws),
+                                             ctypes.c_void_p(_stream(dev, stream))), "ea_wide_partials_cuda")
+    return w
+
+
+def rescale_wide_partials(w: WidePartials, merged_max, stream=None) -> None:
+    import torch
+
+    ws = w.struct()
+    dev = w.maxv.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_wide_partials_rescale_cuda(ctypes.byref(ws), merged_max.data_ptr(), w.n, w.dv,
+                                                             ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_wide_partials_rescale_cuda")
+
+
+def finalize_wide_partials(w: WidePartials, merged_max, rows, out_tensor, flags, out="bf16", stats=None,
+                           stream=None) -> None:
+    """Writes the listed rows of out_tensor / flags from merged wide partials."""
+    import torch
+
+    ws = w.struct()
+    dev = w.maxv.device
+    rows = rows.to(device=dev, dtype=torch.int32).contiguous()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_wide_partials_finalize_cuda(ctypes.byref(ws), merged_max.data_ptr(), rows.data_ptr(),
+                                                              w.n, w.dv, int(out == "fp32"), out_tensor.data_ptr(),
+                                                              flags.data_ptr(), _ptr(stats),
+                                                              ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_wide_partials_finalize_cuda")

@@ -101,8 +101,9 @@ typedef struct ea_launch {
 int ea_launch_cuda(const ea_launch_t* args, void* stream);
 
 /* Per-row partial state of one key range (the split partial of the reference's certified
- * split-KV kernel, cuda/exact_attention_kernel.cu, exported to device buffers so that partials
- * computed on different GPUs can be merged). All device pointers; rows x dv for NR, N, Nerr.
+ * split-KV kernel, src/exactattn/triton_kernels.py:731 _split_program and _ea_combine_kernel
+ * :1081, and certified.py:213 `merge`), exported to device buffers so that partials computed on
+ * different GPUs can be merged. All device pointers; rows x dv for NR, N, Nerr.
  *   R       row exponent: Z = Z_int * 2^(R - FZ); INT32_MIN for a row with no keys
  *   Z, Zerr lower bound of the weight sum and its nonnegative error, in units 2^(R - FZ)
  *   status  0 certified so far, 1 needs the exact tier (tier 3), 2 domain error
@@ -114,7 +115,7 @@ int ea_launch_cuda(const ea_launch_t* args, void* stream);
  * unit per shifted value); then Z, Zerr, N, Nerr are summed over ranks; the sum is finalised
  * by ea_partials_finalize_cuda. Every step is order independent, so any all-reduce tree gives
  * the same bits. No reference counterpart as a separate entry point: the reference merges
- * split partials inside one launch (exact_attention_kernel.cu combine step). */
+ * split partials inside one launch (triton_kernels.py:1081 _ea_combine_kernel). */
 typedef struct ea_partials {
   int32_t* R;
   int64_t* Z;
@@ -132,9 +133,35 @@ int ea_partials_cuda(const ea_launch_t* args, const ea_partials_t* parts, void* 
 int ea_partials_rescale_cuda(const ea_partials_t* parts, const int32_t* R_global, const int32_t* NR_global,
                              int64_t rows, int dv, void* stream);
 /* Certified rounding of merged partials into out/flags (flag 1: not certifiable from the merged
- * interval, the row needs the exact tier; flag 2: domain error). */
+ * interval, the row needs the wide tier below, counted in stats[2]; flag 2: domain error). */
 int ea_partials_finalize_cuda(const ea_partials_t* parts, int64_t rows, int dv, int64_t max_row_keys,
                               int fp32_out, void* out, uint8_t* flags, int64_t* stats, void* stream);
+
+/* Wide (tier-3) partials for the rows ea_partials_finalize_cuda flagged 1, so that KV-sharded
+ * runs finish every row on the devices. Per listed row i (device pointers):
+ *   maxv[4 i + 0..3]  R (reference exponent, INT64_MIN: no keys), Emax, -Emin (weight exponent
+ *                     range), status; merged by MAX over ranks
+ *   sumv[((dv + 1) i + j) (EA_WIDE_DIGITS + 1) + ..]  j = 0: Z, j = 1 + c: channel c's N, as
+ *                     EA_WIDE_DIGITS signed 32-bit digits in int64 followed by the error bound;
+ *                     merged by SUM over ranks after ea_wide_partials_rescale_cuda.
+ * Merge: copy maxv, all-reduce MAX the copy (merged_max), rescale with it, all-reduce SUM sumv,
+ * finalise with merged_max. `rows` (n int32 row indices) must be the same on every rank. These
+ * carry the reference's exact big-integer sums (reference.py:146 attention_row) across devices; no
+ * reference counterpart as an entry point. */
+#define EA_WIDE_DIGITS 48
+typedef struct ea_wide_partials {
+  int64_t* maxv;
+  int64_t* sumv;
+} ea_wide_partials_t;
+int ea_wide_partials_cuda(const ea_launch_t* args, const int32_t* rows, int n, const ea_wide_partials_t* parts,
+                          void* stream);
+int ea_wide_partials_rescale_cuda(const ea_wide_partials_t* parts, const int64_t* merged_max, int n, int dv,
+                                  void* stream);
+/* Writes out/flags of the listed rows: flag 0 certified, 2 domain error, 1 unresolved (a
+ * 2^-97-probability event; counted in stats[4]). */
+int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* parts, const int64_t* merged_max, const int32_t* rows,
+                                   int n, int dv, int fp32_out, void* out, uint8_t* flags, int64_t* stats,
+                                   void* stream);
 
 /* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
  * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,

@@ -37,6 +37,28 @@ def merge_local(parts_list):
     return out
 
 
+def finish_local(shard_args, out, flags, max_row_keys, stats=None):
+    """The sharded wide tier (exactattention_b200.dist.wide_tier) over in-process ranges, for the
+    rows the merged tier-1 partials left at flag 1. shard_args: per range (q, k, v, alpha, mask)."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    need = flags == 1
+    if not int(need.sum().item()):
+        return 0
+    rows = need.nonzero().flatten().to(torch.int32)
+    ws = [cuda.wide_partials(q, k, v, a, rows, max_row_keys=max_row_keys, stats=stats, **m)
+          for (q, k, v, a, m) in shard_args]
+    gmax = torch.stack([w.maxv for w in ws]).max(0).values
+    for w in ws:
+        cuda.rescale_wide_partials(w, gmax)
+    for w in ws[1:]:
+        ws[0].sumv += w.sumv
+    cuda.finalize_wide_partials(ws[0], gmax, rows, out, flags, stats=stats)
+    return rows.numel()
+
+
 def _bounds(n, shards):
     return [(n * s // shards, n * (s + 1) // shards) for s in range(shards)]
 
@@ -61,13 +83,15 @@ def test_kv_shards_simt_match_full_and_oracle(kind, vkind, d, shards):
     kl[3] = 0
     kl[5] = 700  # rows whose range ends inside a shard or before it: empty partials there
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
-    parts = []
+    parts, shard_args = [], []
     for i, (lo, hi) in enumerate(_bounds(n, shards)):
         klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
-        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
-                                   kv_len=_t(klen, dev), max_row_keys=n, splits=1 + i % 3))
+        m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
+        shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, m))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, splits=1 + i % 3, **m))
     merged = merge_local(parts)
     out, flags = cuda.finalize_partials(merged, n)
+    finish_local(shard_args, out, flags, n)
     torch.cuda.synchronize()
     assert not flags.any().item() and not fflags.any().item()
     assert torch.equal(out, full)
@@ -96,14 +120,16 @@ def test_kv_shards_tensor_core_match_full(shards):
     alpha = ea.default_alpha(128)
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
                                blocks=_t(cuda.row_blocks(kb, kl), dev))
-    parts = []
+    parts, shard_args = [], []
     st = torch.zeros(8, dtype=torch.int64, device=dev)
     for lo, hi in _bounds(S, shards):
         klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
-        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
-                                   kv_len=_t(klen, dev), max_row_keys=S, blocks=_t(cuda.row_blocks(kb, klen), dev),
-                                   stats=st))
+        m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
+        shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, m))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=S, blocks=_t(cuda.row_blocks(kb, klen), dev),
+                                   stats=st, **m))
     out, flags = cuda.finalize_partials(merge_local(parts), S)
+    finish_local(shard_args, out, flags, S)
     torch.cuda.synchronize()
     assert st.cpu().numpy()[7] == int(kl.sum()), "the tensor-core kernel did not run"
     assert not flags.any().item() and not fflags.any().item()
@@ -126,12 +152,57 @@ def test_kv_shards_domain_error_propagates():
     kb = np.zeros(rows, np.int64)
     kl = np.array([n, 300, n, 351, 350, n], np.int64)
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
-    parts = []
+    parts, shard_args = [], []
     for lo, hi in _bounds(n, 2):
         klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
-        parts.append(cuda.partials(_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, kv_base=_t(kb, dev),
-                                   kv_len=_t(klen, dev), max_row_keys=n))
+        m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
+        shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, m))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
     out, flags = cuda.finalize_partials(merge_local(parts), n)
+    finish_local(shard_args, out, flags, n)
     torch.cuda.synchronize()
     assert flags.cpu().numpy().tolist() == [2, 0, 2, 2, 0, 2]
     assert torch.equal(flags, fflags) and torch.equal(out, full)
+
+
+def test_kv_shards_wide_tier_rows():
+    """Rows that only the wide tier certifies merge across shards to the single-launch bits: with
+    equal weights, +2^125 (key 0, shard 0) and -2^125 (key 500, shard 1) cancel exactly in
+    channel 0, so the int64 windows anchored at 2^125 keep nothing of the result."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(123)
+    rows, n, d = 8, 900, 64
+    Q = np.zeros((rows, d), np.uint16)          # zero scores: every weight is 1
+    K = bf16(rng, (n, d))
+    V = bf16(rng, (n, d))
+    V[0, 0] = 0x7E00                            # 2^125
+    V[500, 0] = 0xFE00                          # -2^125
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(d)
+    kb = np.zeros(rows, np.int64)
+    kl = np.full(rows, n, np.int64)
+    st_full = torch.zeros(8, dtype=torch.int64, device=dev)
+    full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
+                               stats=st_full)
+    parts, shard_args = [], []
+    for lo, hi in _bounds(n, 3):
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
+        shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, m))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
+    out, flags = cuda.finalize_partials(merge_local(parts), n)
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    n3 = finish_local(shard_args, out, flags, n, stats=st)
+    torch.cuda.synchronize()
+    assert st_full.cpu().numpy()[2] > 0, "the single launch should need the wide tier here"
+    assert n3 > 0
+    assert not flags.any().item() and not fflags.any().item()
+    assert st.cpu().numpy()[4] == 0
+    assert torch.equal(out, full)
+    o = out.cpu().numpy().view(np.uint16)
+    assert np.array_equal(o[0], exact.attention_row(Q[0], K, V, alpha))
