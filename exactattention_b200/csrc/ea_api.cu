@@ -19,6 +19,7 @@ cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
 cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st);
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
 cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
+cudaError_t launch_combine(const Prob& P, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 }  // namespace ea
@@ -68,10 +69,13 @@ Workspace* workspace() {
   return &g_ws.back();
 }
 
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// the split partial buffers as build_prob carves them: Z, Zerr, N, Nerr, R, NR, status
 size_t part_bytes(int64_t rows, int splits, int dv) {
   if (splits <= 1) return 0;
-  int64_t n = rows * (int64_t)splits;
-  return (size_t)n * (4 + 8 + 8 + 1 + 16) + (size_t)n * dv * (4 + 8 + 8) + 256;
+  const size_t n = (size_t)rows * (size_t)splits;
+  return 2 * align256(n * 8) + 2 * align256(n * dv * 8) + align256(n * 4) + align256(n * dv * 4) + align256(n * 4);
 }
 
 bool grow(void** p, size_t* cap, size_t need) {
@@ -205,13 +209,65 @@ static void build_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
     P.pNe = (uint64_t*)take(n * a->dv * 8);
     P.pR = (int32_t*)take(n * 4);
     P.pNR = (int32_t*)take(n * a->dv * 4);
-    P.pSt = (uint8_t*)take(n);
+    P.pSt = (int32_t*)take(n * 4);
   }
 }
 
+static bool tc_shape(const ea_launch_t* a) {
+  return a->block_rows && a->nblocks > 0 && a->d == 128 && a->dv == 128 && !a->fp32_out &&
+         ((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0;
+}
+
 static bool tc_applicable(const ea_launch_t* a) {
-  return a->mask_kind == EA_MASK_RANGE && a->block_rows && a->nblocks > 0 && a->d == 128 && a->dv == 128 &&
-         !a->fp32_out && a->splits == 1 && ((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0;
+  return a->mask_kind == EA_MASK_RANGE && a->splits == 1 && tc_shape(a);
+}
+
+// A HYBRID mask (shared key range + per-row list: tree verification) with row blocks: the range
+// part on the tensor cores and the list part on the CUDA cores, each exporting its partial into
+// one of two split slots, merged and finalised by the split combine (the merge of split
+// partials is exact, so this is the same as one pass over the row's keys).
+static bool hybrid_tc_applicable(const ea_launch_t* a) {
+  return a->mask_kind == EA_MASK_HYBRID && tc_shape(a);
+}
+
+static void export_to_split(Prob& X, const Prob& P, int s) {
+  const int64_t o = (int64_t)s * P.rows;
+  X.splits = 1;
+  X.export_partials = 1;
+  X.xR = P.pR + o;
+  X.xZ = P.pZ + o;
+  X.xZe = P.pZe + o;
+  X.xSt = P.pSt + o;
+  X.xNR = P.pNR + o * P.dv;
+  X.xN = P.pN + o * P.dv;
+  X.xNe = P.pNe + o * P.dv;
+}
+
+static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st) {
+  ea_launch_t a = *a0;
+  a.splits = 2;
+  int rc = reserve(w, a.rows, 2, a.dv);
+  if (rc) return rc;
+  Prob P;
+  build_prob(&a, w, P);
+  cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
+  if (e != cudaSuccess) return fail_cuda(e, "memset");
+  Prob P0 = P;
+  P0.kind = MASK_RANGE;
+  export_to_split(P0, P, 0);
+  e = launch_tc_prefill(P0, a.block_rows, a.nblocks, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-1 range launch");
+  Prob P1 = P;
+  P1.kind = MASK_CSR;
+  export_to_split(P1, P, 1);
+  e = launch_simt(P1, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-1 list launch");
+  e = launch_combine(P, st);
+  if (e != cudaSuccess) return fail_cuda(e, "combine");
+  int blocks = (int)(a.rows < 2 * w->sms ? a.rows : 2 * w->sms);
+  e = launch_tier3(P, blocks, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  return 0;
 }
 
 int ea_launch_cuda(const ea_launch_t* a, void* stream) {
@@ -221,9 +277,10 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* w = workspace();
   if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (hybrid_tc_applicable(a)) return launch_hybrid_tc(a, w, st);
   rc = reserve(w, a->rows, a->splits, a->dv);
   if (rc) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
   Prob P;
   build_prob(a, w, P);
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);

@@ -60,7 +60,7 @@ struct Prob {
   int32_t* pR;
   int64_t* pZ;
   uint64_t* pZe;
-  uint8_t* pSt;
+  int32_t* pSt;
   int32_t* pNR;
   int64_t* pN;
   uint64_t* pNe;

@@ -10,7 +10,7 @@
 //
 // Limits and rules:
 //   * the scratch holds EA_NOALLOC_SCRATCH_BYTES; a call that needs more (rows x splits x
-//     (20 dv + 29) bytes of partials plus 4 bytes per row) is rejected with -6 and an error
+//     (20 dv + 32) bytes of partials plus 4 bytes per row) is rejected with -6 and an error
 //     string, before anything is launched;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
 //     with that device current; make that first call before any stream capture;
@@ -57,7 +57,7 @@ size_t scratch_bytes(int64_t rows, int splits, int dv) {
   size_t b = align256(EA_STATS_LEN * 8) + align256(sizeof(int)) + align256((size_t)rows * 4);
   if (splits > 1) {
     size_t n = (size_t)rows * splits;
-    b += 2 * align256(n * 8) + 2 * align256(n * dv * 8) + align256(n * 4) + align256(n * dv * 4) + align256(n);
+    b += 2 * align256(n * 8) + 2 * align256(n * dv * 8) + 2 * align256(n * 4) + align256(n * dv * 4);
   }
   return b;
 }
@@ -141,7 +141,7 @@ extern "C" int ea_attention_cuda_noalloc(const ea_launch_t* a, void* stream) {
     P.pNe = (uint64_t*)take(n * a->dv * 8);
     P.pR = (int32_t*)take(n * 4);
     P.pNR = (int32_t*)take(n * a->dv * 4);
-    P.pSt = (uint8_t*)take(n);
+    P.pSt = (int32_t*)take(n * 4);
   }
   P.q = a->q;
   P.k = a->k;

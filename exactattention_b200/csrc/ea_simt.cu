@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
     P.pR[pi] = R;
     P.pZ[pi] = Z;
     P.pZe[pi] = Ze;
-    P.pSt[pi] = (uint8_t)status;
+    P.pSt[pi] = status;
   }
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {
@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
   int32_t R = R_EMPTY;
   for (int s = 0; s < S; ++s) {
     int64_t pi = (int64_t)s * P.rows + r;
-    status = max(status, (int)P.pSt[pi]);
+    status = max(status, P.pSt[pi]);
     if (P.pR[pi] != R_EMPTY) R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
   }
   int64_t Z = 0;
@@ -923,6 +923,15 @@ cudaError_t launch_simt(const Prob& P, cudaStream_t st) {
   if (P.dv <= 64) return launch_simt_cpl<2>(P, warps, st);
   if (P.dv <= 128) return launch_simt_cpl<4>(P, warps, st);
   return launch_simt_cpl<8>(P, warps, st);
+}
+
+cudaError_t launch_combine(const Prob& P, cudaStream_t st) {
+  const unsigned g = (unsigned)((P.rows + 3) / 4);
+  if (P.dv <= 32) combine_kernel<1><<<g, 128, 0, st>>>(P);
+  else if (P.dv <= 64) combine_kernel<2><<<g, 128, 0, st>>>(P);
+  else if (P.dv <= 128) combine_kernel<4><<<g, 128, 0, st>>>(P);
+  else combine_kernel<8><<<g, 128, 0, st>>>(P);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st) {

@@ -108,7 +108,9 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     laid out (pages, kv_heads, page_size, d); row r is sequence r // q_heads, head r % q_heads),
     or HYBRID (kv_base/kv_len and row_ptr/key_idx together: the range, then the CSR list).
     max_row_keys bounds every row's key count (required for RANGE/PAGED without a host sync).
-    `blocks` (from row_blocks) lets RANGE masks with d = dv = 128 use the tensor-core kernel.
+    `blocks` (from row_blocks; every row in some block) lets RANGE masks with d = dv = 128 use the
+    tensor-core kernel, and HYBRID masks run their shared range on it (the per-row lists on the
+    CUDA cores, the two partials merged exactly).
     `no_alloc` calls ea_attention_cuda_noalloc instead: the library allocates no device memory for
     the call (its scratch is a fixed static array; see include/exactattn_cuda.h for the limits).
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""

@@ -411,11 +411,14 @@ def device_case(name: str, device="cuda", shard: int = 0, nshards: int = 1) -> d
         kw = dict(kv_base=torch.from_numpy(base.astype(np.int64)).to(dev),
                   kv_len=torch.from_numpy(np.full(rows, Tn, np.int64)).to(dev), max_row_keys=T)
     elif name == "c4":
+        from .cuda import row_blocks
+
         tails = [np.array(cfg.ancestors(int(bb), int(tt)), np.int64) for bb, tt in zip(b, tok)]
         rp = np.concatenate([[0], np.cumsum([len(x) for x in tails])]).astype(np.int64)
         ki = np.concatenate([base[i] + cfg.prefix + tails[i] for i in range(rows)]).astype(np.int64)
+        plen = np.full(rows, cfg.prefix, np.int64)
         kw = dict(kv_base=torch.from_numpy(base.astype(np.int64)).to(dev),
-                  kv_len=torch.from_numpy(np.full(rows, cfg.prefix, np.int64)).to(dev),
+                  kv_len=torch.from_numpy(plen).to(dev),
                   row_ptr=torch.from_numpy(rp).to(dev), key_idx=torch.from_numpy(ki).to(dev),
-                  max_row_keys=cfg.prefix + 8)
+                  max_row_keys=cfg.prefix + 8, blocks=torch.from_numpy(row_blocks(base, plen)).to(dev))
     return dict(cfg=cfg, q=q, k=k.view(-1, D), v=v.view(-1, D), kw=kw)

@@ -88,9 +88,10 @@ typedef struct ea_launch {
   void* out;      /* (rows, dv) uint16 or float */
   uint8_t* flags; /* (rows,) */
   int64_t* stats; /* EA_STATS_LEN int64 counters, accumulated; may be NULL */
-  /* optional, RANGE masks: rows grouped into blocks of 128 that share kv_base (-1 pads a block),
-   * (nblocks, 128) int32. With it, d = dv = 128, bf16 output and splits == 1, the tensor-core
-   * kernel runs; any grouping gives the same bits. */
+  /* optional, RANGE and HYBRID masks: every row in one of the blocks of 128 rows that share
+   * kv_base (-1 pads a block), (nblocks, 128) int32. With it, d = dv = 128 and bf16 output, the
+   * tensor-core kernel runs (RANGE: when splits == 1; HYBRID: over the range part, with the
+   * per-row lists on the CUDA cores); any grouping gives the same bits. */
   const int32_t* block_rows;
   int64_t nblocks;
 } ea_launch_t;
@@ -168,7 +169,7 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* parts, const int64_
  * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the
  * reference. Its scratch (split partials, tier-3 work list, counters) is one static device array
  * of EA_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until exit; a call needing
- * more (rows x splits x (20 dv + 29) bytes plus 4 bytes per row, about) returns -6 with a message
+ * more (rows x splits x (20 dv + 32) bytes plus 4 bytes per row, about) returns -6 with a message
  * from ea_noalloc_last_error(). The first call on a device looks up the array's address: make it
  * before any stream capture. Calls share the array, so calls on one device whose kernels may
  * overlap race and must be serialised. CUDA-core kernels only (d <= 1024, dv <= 256). */

@@ -404,3 +404,48 @@ def test_tensor_core_ragged_blocks_and_nan(ea):
     assert torch.equal(f_tc, f_s)
     ok = torch.from_numpy(~sees).to(dev)
     assert torch.equal(o_tc[ok], o_s[ok])
+
+
+def test_tensor_core_hybrid_tree_mask(ea):
+    """HYBRID masks with row blocks: the shared prefix on the tensor cores, the ancestor lists on
+    the CUDA cores, merged; equal to the CUDA-core path and to sequential decode (oracle)."""
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(314)
+    P, nodes, heads = 500, 24, 2
+    parent = [-1] + [int(rng.integers(0, i)) for i in range(1, nodes)]
+    K = bf16(rng, (P + nodes, 128), "outlier")
+    V = bf16(rng, (P + nodes, 128))
+    Q = bf16(rng, (heads * nodes, 128), "outlier")
+    anc = []
+    for i in range(nodes):
+        a, x = [], i
+        while x >= 0:
+            a.append(x)
+            x = parent[x]
+        anc.append(sorted(a))
+    tails = [np.array(anc[r % nodes], np.int64) + P for r in range(heads * nodes)]
+    rp = np.concatenate([[0], np.cumsum([len(x) for x in tails])]).astype(np.int64)
+    ki = np.concatenate(tails).astype(np.int64)
+    kb = np.zeros(heads * nodes, np.int64)
+    kl = np.full(heads * nodes, P, np.int64)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), row_ptr=t(rp), key_idx=t(ki),
+                             stats=st, blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), row_ptr=t(rp), key_idx=t(ki))
+    torch.cuda.synchronize()
+    s = st.cpu().numpy()
+    assert s[7] == int(kl.sum()), "the tensor-core kernel did not run"
+    assert s[5] == int(kl.sum() + rp[-1])
+    assert not f_tc.any().item() and torch.equal(f_tc, f_s)
+    assert torch.equal(o_tc, o_s)
+    out = o_tc.cpu().numpy().view(np.uint16)
+    for r in (0, 5, nodes - 1, nodes + 7):
+        keys = np.concatenate([np.arange(P), tails[r]])
+        assert np.array_equal(out[r], exact.attention_row(Q[r], K[keys], V[keys], alpha)), r
