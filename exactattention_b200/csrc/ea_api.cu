@@ -20,6 +20,7 @@ cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t 
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
 cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
 cudaError_t launch_combine(const Prob& P, cudaStream_t st);
+cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 }  // namespace ea
@@ -230,6 +231,49 @@ static bool hybrid_tc_applicable(const ea_launch_t* a) {
   return a->mask_kind == EA_MASK_HYBRID && tc_shape(a);
 }
 
+// Decode shapes: a few rows per key sequence (a GQA group). PAGED masks form their segments from
+// the layout (sequence, kv head); RANGE masks need the caller's segment table.
+static bool decode_applicable(const ea_launch_t* a) {
+  if (a->d != 128 || a->dv != 128 || ((uintptr_t)a->q & 15) || ((uintptr_t)a->k & 15) || ((uintptr_t)a->v & 15))
+    return false;
+  if (a->mask_kind == EA_MASK_RANGE) return a->seg_rows && a->nsegs > 0;
+  if (a->mask_kind == EA_MASK_PAGED)
+    return a->q_heads > 0 && a->kv_heads > 0 && a->q_heads / a->kv_heads <= 8 && a->rows % a->q_heads == 0;
+  return false;
+}
+
+static int64_t decode_segments(const ea_launch_t* a) {
+  return a->mask_kind == EA_MASK_PAGED ? (a->rows / a->q_heads) * a->kv_heads : a->nsegs;
+}
+
+// the decode kernel writes split partials for splits >= 1: carve the split buffers for at least 2
+static int decode_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
+  ea_launch_t a2 = *a;
+  a2.splits = a->splits < 2 ? 2 : a->splits;
+  int rc = reserve(w, a2.rows, a2.splits, a2.dv);
+  if (rc) return rc;
+  build_prob(&a2, w, P);
+  P.splits = a->splits;
+  return 0;
+}
+
+static int launch_decode_tc(const ea_launch_t* a, Workspace* w, cudaStream_t st) {
+  Prob P;
+  int rc = decode_prob(a, w, P);
+  if (rc) return rc;
+  cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
+  if (e != cudaSuccess) return fail_cuda(e, "memset");
+  const int32_t* seg = a->mask_kind == EA_MASK_RANGE ? a->seg_rows : nullptr;
+  e = launch_tc_decode(P, seg, decode_segments(a), st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-1 decode launch");
+  e = launch_combine(P, st);
+  if (e != cudaSuccess) return fail_cuda(e, "combine");
+  int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
+  e = launch_tier3(P, blocks, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  return 0;
+}
+
 static void export_to_split(Prob& X, const Prob& P, int s) {
   const int64_t o = (int64_t)s * P.rows;
   X.splits = 1;
@@ -279,6 +323,7 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   if (!w) return fail_cuda(cudaGetLastError(), "workspace");
   cudaStream_t st = (cudaStream_t)stream;
   if (hybrid_tc_applicable(a)) return launch_hybrid_tc(a, w, st);
+  if (decode_applicable(a)) return launch_decode_tc(a, w, st);
   rc = reserve(w, a->rows, a->splits, a->dv);
   if (rc) return rc;
   Prob P;
@@ -315,10 +360,19 @@ int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream)
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* w = workspace();
   if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-  rc = reserve(w, a->rows, a->splits, a->dv);
-  if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   Prob P;
+  if (decode_applicable(a)) {
+    rc = decode_prob(a, w, P);
+    if (rc) return rc;
+    set_export(P, x);
+    const int32_t* seg = a->mask_kind == EA_MASK_RANGE ? a->seg_rows : nullptr;
+    cudaError_t e = launch_tc_decode(P, seg, decode_segments(a), st);
+    if (e == cudaSuccess) e = launch_combine(P, st);
+    return e == cudaSuccess ? 0 : fail_cuda(e, "partials decode launch");
+  }
+  rc = reserve(w, a->rows, a->splits, a->dv);
+  if (rc) return rc;
   build_prob(a, w, P);
   set_export(P, x);
   cudaError_t e = tc_applicable(a) ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);

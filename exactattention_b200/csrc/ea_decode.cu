@@ -1,0 +1,708 @@
+// Tensor-core (tcgen05 / TMEM) tier-1 kernel of certified ExactAttention for decode: a few query
+// rows (one GQA group of one sequence, at most 8) against a long key sequence, d = dv = 128.
+//
+// The prefill kernel puts 128 query rows on the MMA's M side; a decode group has 1-8 rows, so
+// here the KEYS take the M side and the rows' digits go to N:
+//   scores   S^T[key, (g, s)] = K_t . Q_s for key digit planes t (A, 128 keys x 128 dims) against
+//            one B tile holding every row's 4 query digit planes (N = 32 = 8 rows x 4 digits).
+//            Query digits are balanced (signed bytes) so one B tile has one signedness.
+//   P.V      O^T[c, (g, w)] = V_u . W_w for value digit planes u (A, 128 channels x 128 keys)
+//            against one B tile of every row's 6 weight digit planes (N = 48).
+// Digit products are grouped by digit position on the CUDA cores (int32 sums) and recombined
+// exactly in int64, with the same fixed-point windows, bounds and certification as the prefill
+// kernel. Each CTA takes one (segment, split): the split's 128-key tiles arrive by bulk copies
+// (cp.async.bulk, completing on an mbarrier) into a raw staging buffer one tile ahead of the
+// slicing. Every CTA writes its rows' split partials; the split combine merges them (any split
+// count gives the same bits) and sends uncertified rows to tier 3.
+//
+// Thread roles (256 threads): slicing uses all threads; TMEM lane quadrant = warp % 4, and the
+// two warpgroups take alternate rows (pass 1 / pass 2: lane = key; drain: lane = channel).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ea_core.cuh"
+#include "ea_numerics.h"
+#include "ea_tables.cuh"
+#include "ea_tc_common.cuh"
+#include "ea_tcgen05.cuh"
+
+namespace ea {
+namespace tcd {
+
+using namespace tcc;
+
+constexpr int BK = 128, D = 128, DV = 128, GD = 8;
+constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
+constexpr int FW = 48, FV = 23;
+constexpr int THREADS = 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
+constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
+constexpr uint32_t COL_O = 128;  // P.V accumulators: COL_O + 48 u + n (scores: 32 t + n)
+
+constexpr uint32_t RAW_K = BK * D * 2;  // 32768
+constexpr uint32_t K_PLANE = BK * D;    // 16384
+constexpr uint32_t V_PLANE = DV * BK;   // 16384
+constexpr uint32_t OFF_RAWK = 0;
+constexpr uint32_t OFF_RAWV = OFF_RAWK + RAW_K;
+constexpr uint32_t OFF_K = OFF_RAWV + RAW_K;
+constexpr uint32_t OFF_V = OFF_K + NK * K_PLANE;
+constexpr uint32_t OFF_Q = OFF_V + NV * V_PLANE;
+constexpr uint32_t OFF_W = OFF_Q + NSQ * D;
+constexpr uint32_t OFF_T = OFF_W + NSW * BK;
+constexpr uint32_t OFF_SMALL = OFF_T + GD * BK * 4;
+
+struct Small {
+  uint64_t ta[256];
+  uint64_t tb[256];
+  uint32_t klossy[BK][4];
+  int32_t qfix[GD][D];
+  int32_t klsb[BK];
+  int32_t kbad[BK];
+  int32_t vlossy[BK];
+  int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
+  int32_t ve4[4][DV];  // per key quarter maxima of the current tile
+  int32_t rows[GD];
+  int32_t len[GD];
+  int32_t qlsb[GD];
+  int32_t rst[GD];
+  uint32_t qlossy[GD][4];
+  int32_t rt[4][GD];
+  uint64_t zs[4][GD];
+  uint32_t zl[4][GD];
+  uint64_t vw[4][GD];
+  uint64_t bar_mma;
+  uint64_t bar_raw;
+  uint32_t tmem;
+  int32_t nrows;
+  int32_t maxlen;
+  int32_t row0;
+};
+
+constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(OFF_K % 1024 == 0 && OFF_Q % 16 == 0 && OFF_W % 16 == 0, "operand alignment");
+
+// first K/V row and the number of contiguous rows from the segment's key j on (RANGE: the rest
+// of the range; PAGED: the rest of the page)
+__device__ __forceinline__ int64_t run_start(const Prob& P, int32_t row0, int64_t j, int64_t& run) {
+  if (P.kind == MASK_RANGE) {
+    run = INT64_MAX;
+    return P.kv_base[row0] + j;
+  }
+  const int64_t b = row0 / P.hq;
+  const int kvh = (int)(row0 - b * P.hq) / P.group;
+  const int64_t page = P.page_table[b * P.max_pages + j / P.page_size];
+  run = P.page_size - j % P.page_size;
+  return (page * P.hkv + kvh) * P.page_size + (j % P.page_size);
+}
+
+// warp 0: bulk copies of keys [j0, j0 + n) of K and V into the raw tiles; lane 0 arms the barrier
+__device__ void fetch_tile(const Prob& P, int32_t row0, int64_t j0, int n, uint8_t* rawk, uint8_t* rawv,
+                           uint64_t* bar) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) tc::mbar_arrive_expect_tx(bar, (uint32_t)n * 2u * D * 2u);
+  __syncwarp();
+  // runs in key order; lane l issues runs l, l + 32, ...
+  int64_t j = 0;
+  int idx = 0;
+  while (j < n) {
+    int64_t run;
+    const int64_t kr = run_start(P, row0, j0 + j, run);
+    const int len = (int)(run < (int64_t)(n - j) ? run : (int64_t)(n - j));
+    if ((idx & 31) == lane) {
+      tc::bulk_g2s(rawk + j * (D * 2), P.k + kr * D, (uint32_t)len * D * 2, bar);
+      tc::bulk_g2s(rawv + j * (DV * 2), P.v + kr * DV, (uint32_t)len * DV * 2, bar);
+    }
+    j += len;
+    ++idx;
+  }
+}
+
+__device__ __forceinline__ int32_t lead_of_bits(uint32_t mag) {  // lead exponent of a nonzero |bf16|
+  int32_t m, e;
+  decode_bf16(mag, m, e);
+  return lead_of(m, e);
+}
+
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* rawk = smem + OFF_RAWK;
+  uint8_t* rawv = smem + OFF_RAWV;
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
+  uint8_t* sQ = smem + OFF_Q;
+  uint8_t* sW = smem + OFF_W;
+  uint32_t* sT = (uint32_t*)(smem + OFF_T);
+  Small& S = *(Small*)(smem + OFF_SMALL);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seg = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+
+  // ---------------- segment rows and this split's key range ----------------
+  if (tid < GD) {
+    int32_t row;
+    if (seg_rows) {
+      row = seg_rows[(int64_t)seg * GD + tid];
+    } else {  // PAGED: sequence seg / kv_heads, kv head seg % kv_heads, the group's q heads
+      const int b = seg / P.hkv, kvh = seg % P.hkv;
+      row = tid < P.group ? b * P.hq + kvh * P.group + tid : -1;
+    }
+    S.rows[tid] = row;
+    S.len[tid] = row >= 0 ? (int32_t)row_len(P, row) : 0;
+    S.rst[tid] = ST_OK;
+  }
+  for (int i = tid; i < 256; i += THREADS) {
+    S.ta[i] = g_ta64[i];
+    S.tb[i] = g_tb64[i];
+  }
+  for (int i = tid; i < DV; i += THREADS) S.ve[i] = INT32_MIN;
+  for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
+  if (tid == 0) {
+    tc::mbar_init(&S.bar_mma, 1);
+    tc::mbar_init(&S.bar_raw, 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int n = 0, m = 0, first = -1;
+    for (int g = 0; g < GD; ++g)
+      if (S.rows[g] >= 0) {
+        n = g + 1;
+        m = max(m, S.len[g]);
+        if (first < 0) first = S.rows[g];
+      }
+    S.nrows = n;
+    S.maxlen = m;
+    S.row0 = first;
+  }
+  __syncthreads();
+  const int nrows = S.nrows;
+  if (nrows == 0) return;  // uniform: an all-padding segment
+  const int32_t row0 = S.row0;  // the segment's rows share their keys: address them through this one
+  const int64_t maxlen = S.maxlen;
+  const int64_t kbeg = maxlen * split / nsplit, kend = maxlen * (split + 1) / nsplit;
+  if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
+  if (warp == 0 && kbeg < kend) fetch_tile(P, row0, kbeg, (int)min((int64_t)BK, kend - kbeg), rawk, rawv, &S.bar_raw);
+
+  // ---------------- query rows -> balanced digit planes (warp g: row g) ----------------
+  {
+    const int g = warp;
+    const int32_t row = S.rows[g];
+    uint32_t bits[4];
+    int lead = INT32_MIN, bad = 0;
+#pragma unroll
+    for (int m4 = 0; m4 < 4; ++m4) {
+      bits[m4] = row >= 0 ? (uint32_t)P.q[(int64_t)row * D + lane + 32 * m4] : 0u;
+      int32_t m, e;
+      if (!decode_bf16(bits[m4], m, e)) bad = 1;
+      if (m) lead = max(lead, lead_of(m, e));
+    }
+    lead = __reduce_max_sync(0xffffffffu, lead);
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+#pragma unroll
+    for (int m4 = 0; m4 < 4; ++m4) {
+      const int i = lane + 32 * m4;
+      int lost = 0, b2 = 0;
+      const int32_t x = (bad || lead == INT32_MIN) ? 0 : fixq(bits[m4], lsb, lost, b2);
+      S.qfix[g][i] = x;
+      const uint32_t lm = __ballot_sync(0xffffffffu, lost != 0);
+      if (lane == 0) S.qlossy[g][m4] = lm;
+      // balanced base-256 digits: x = sum_s d_s 256^s, d_s in [-128, 127] (|x| < 2^28)
+      int32_t y = x;
+#pragma unroll
+      for (int s = 0; s < NQ; ++s) {
+        const int32_t dg = s == NQ - 1 ? y : (int32_t)(int8_t)(y & 0xFF);
+        sQ[tc::kmajor_off(4 * g + s, i, NSQ)] = (uint8_t)(int8_t)dg;
+        y = (y - dg) >> 8;
+      }
+    }
+    if (lane == 0) {
+      S.qlsb[g] = lsb;
+      if (bad && row >= 0) S.rst[g] = ST_DOMAIN;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = S.tmem;
+
+  // ---------------- per-thread running state (drain role: channel c, rows h, h + 2, ..) ----------
+  const int h = warp >> 2, c = 32 * (warp & 3) + lane;
+  const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+  const int FN = P.FZ, FZ = P.FZ;
+  int32_t R[GD / 2];
+  int64_t Z[GD / 2], N[GD / 2];
+  uint64_t Zerr[GD / 2], Nerr[GD / 2];
+#pragma unroll
+  for (int i = 0; i < GD / 2; ++i) {
+    R[i] = R_EMPTY;
+    Z[i] = 0;
+    N[i] = 0;
+    Zerr[i] = 0;
+    Nerr[i] = 0;
+  }
+  int32_t vec = INT32_MIN;  // this channel's VE as last applied to N
+  uint32_t ph_raw = 0, ph_mma = 0;
+  bool ok_wait = true;
+  bool raw_pending = kbeg < kend, mma_pending = false;  // operations a timed-out exit must drain
+  unsigned n_exact = 0, n_wide = 0;
+
+  for (int64_t j0 = kbeg; j0 < kend; j0 += BK) {
+    const int nvalid = (int)min((int64_t)BK, kend - j0);
+    {
+      const bool okw = tc::mbar_wait(&S.bar_raw, ph_raw);
+      if (!__syncthreads_and(okw)) {
+        ok_wait = false;
+        break;
+      }
+      ph_raw ^= 1;
+      raw_pending = false;
+    }
+    // ---------------- K tile -> digit planes (8 elements per item, 16 lanes per key) ----------------
+#pragma unroll 1
+    for (int it = 0; it < 8; ++it) {
+      const int key = 16 * it + (tid >> 4), ch = tid & 15;
+      const bool valid = key < nvalid;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (valid) {
+        const uint4 x = *(const uint4*)(rawk + key * (D * 2) + ch * 16);
+        w[0] = x.x;
+        w[1] = x.y;
+        w[2] = x.z;
+        w[3] = x.w;
+      }
+      uint32_t mx = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                             __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+      mx = max(mx & 0xFFFFu, mx >> 16);
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const int bad = mx >= 0x7F80u;
+      const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
+      const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+      uint32_t xs[8];
+      uint32_t lm = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t b = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        int lost = 0, b2 = 0;
+        xs[e] = lead == INT32_MIN ? 0u : (uint32_t)fixq(b, lsb, lost, b2);
+        lm |= (uint32_t)(lost != 0) << e;
+      }
+#pragma unroll
+      for (int p = 0; p < NK; ++p) {
+        uint32_t lo, hi;
+        if (p == 0) { lo = pack4<0>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<0>(xs[4], xs[5], xs[6], xs[7]); }
+        else if (p == 1) { lo = pack4<1>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<1>(xs[4], xs[5], xs[6], xs[7]); }
+        else if (p == 2) { lo = pack4<2>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<2>(xs[4], xs[5], xs[6], xs[7]); }
+        else { lo = pack4<3>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<3>(xs[4], xs[5], xs[6], xs[7]); }
+        *(uint2*)(sK + p * K_PLANE + tc::kmajor_off(key, 8 * ch, BK)) = make_uint2(lo, hi);
+      }
+      // lossy mask of 32 elements (4 lanes) per word
+      uint32_t lw = lm << (8 * (ch & 3));
+      lw |= __shfl_xor_sync(0xffffffffu, lw, 1);
+      lw |= __shfl_xor_sync(0xffffffffu, lw, 2);
+      if ((ch & 3) == 0) S.klossy[key][ch >> 2] = lw;
+      if (ch == 0) {
+        S.klsb[key] = lsb;
+        S.kbad[key] = valid && bad;
+        S.vlossy[key] = 0;
+      }
+    }
+    __syncthreads();  // kbad / vlossy are reset above before the value checks below set them
+    // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
+    const int cp = tid & 63, kq = tid >> 6;
+    uint32_t vw32[32];
+    {
+      uint32_t mx = 0;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int key = 32 * kq + jj;
+        vw32[jj] = key < nvalid ? *(const uint32_t*)(rawv + key * (DV * 2) + cp * 4) : 0u;
+        mx = __vmaxu2(mx, vw32[jj] & 0x7FFF7FFFu);
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t m = (mx >> (16 * hh)) & 0xFFFFu;
+        if (m >= 0x7F80u) {  // a NaN / inf value: flag its keys (domain error for rows that see them)
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (((vw32[jj] >> (16 * hh)) & 0x7F80u) == 0x7F80u) atomicOr(&S.kbad[32 * kq + jj], 1);
+        }
+        S.ve4[kq][2 * cp + hh] = (m == 0 || m >= 0x7F80u) ? INT32_MIN : lead_of_bits(m) + 1;
+      }
+    }
+    __syncthreads();
+    if (tid < DV) {
+      const int vt = max(max(S.ve4[0][tid], S.ve4[1][tid]), max(S.ve4[2][tid], S.ve4[3][tid]));
+      S.ve[tid] = max(S.ve[tid], vt);
+    }
+    __syncthreads();
+    // ---------------- V tile -> digit planes against VE_c ----------------
+    {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int cc = 2 * cp + hh;
+        const int ve = S.ve[cc];
+        const int lsb = ve == INT32_MIN ? 0 : ve - FV;
+        uint32_t lossy = 0;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t x[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const uint32_t b = (vw32[16 * half + jj] >> (16 * hh)) & 0xFFFFu;
+            int lost = 0, bad = 0;
+            x[jj] = ve == INT32_MIN ? 0u : (uint32_t)fixq(b, lsb, lost, bad);
+            lossy |= (uint32_t)(lost != 0) << (16 * half + jj);
+          }
+          uint4 pl[NV];
+          planes16<NV>(x, pl);
+#pragma unroll
+          for (int p = 0; p < NV; ++p)
+            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(cc, 32 * kq + 16 * half, BK)) = pl[p];
+        }
+        for (uint32_t m = lossy; m; m &= m - 1) atomicOr(&S.vlossy[32 * kq + __ffs(m) - 1], 1);
+      }
+    }
+    tc::fence_async_smem();
+    __syncthreads();
+    // the raw tiles are consumed: bring in the next tile while this one is processed
+    if (j0 + BK < kend) {
+      raw_pending = true;
+      if (warp == 0) {
+        tc::fence_async_smem();
+        fetch_tile(P, row0, j0 + BK, (int)min((int64_t)BK, kend - j0 - BK), rawk, rawv, &S.bar_raw);
+      }
+    }
+
+    // ---------------- score MMAs: 4 key digits x (N = 32: row digits) ----------------
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
+      const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
+#pragma unroll 1
+      for (int t = 0; t < NK; ++t) {
+        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
+        for (int ks = 0; ks < D / 32; ++ks) {
+          const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
+          const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
+          tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar_mma));
+    }
+    mma_pending = true;
+    {
+      const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
+      if (!__syncthreads_and(okw)) {
+        ok_wait = false;
+        break;
+      }
+      ph_mma ^= 1;
+      mma_pending = false;
+    }
+    tc::fence_after_sync();
+
+    // ---------------- pass 1: certified logits (lane: key; rows h, h + 2, ..) ----------------
+    {
+      const int key = c;
+      const bool klossy = (S.klossy[key][0] | S.klossy[key][1] | S.klossy[key][2] | S.klossy[key][3]) != 0;
+#pragma unroll 1
+      for (int g = h; g < nrows; g += 2) {
+        uint32_t dg[NK][4];
+#pragma unroll
+        for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + 32 * t + 4 * g, dg[t]);
+        tc::tmem_wait_ld();
+        uint32_t out = T_MASKED;
+        if (key < nvalid && j0 + key < S.len[g] && S.rows[g] >= 0) {
+          if (S.kbad[key]) {
+            atomicMax(&S.rst[g], ST_DOMAIN);
+          } else {
+            // digit products (t, s) grouped by t + s: G_k = sum_{t + s = k} dg[t][s]
+            const int32_t G0 = (int32_t)dg[0][0];
+            const int32_t G1 = (int32_t)dg[0][1] + (int32_t)dg[1][0];
+            const int32_t G2 = (int32_t)dg[0][2] + (int32_t)dg[1][1] + (int32_t)dg[2][0];
+            const int32_t G3 = (int32_t)dg[0][3] + (int32_t)dg[1][2] + (int32_t)dg[2][1] + (int32_t)dg[3][0];
+            const int32_t G4 = (int32_t)dg[1][3] + (int32_t)dg[2][2] + (int32_t)dg[3][1];
+            const int32_t G5 = (int32_t)dg[2][3] + (int32_t)dg[3][2];
+            const int32_t G6 = (int32_t)dg[3][3];
+            const uint32_t lo4[4] = {(uint32_t)G0, (uint32_t)G1, (uint32_t)G2, (uint32_t)G3};
+            const uint32_t hi3[3] = {(uint32_t)G4, (uint32_t)G5, (uint32_t)G6};
+            const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
+            const bool qlossy = (S.qlossy[g][0] | S.qlossy[g][1] | S.qlossy[g][2] | S.qlossy[g][3]) != 0;
+            Rnd t = rnd_zero();
+            int ls;
+            if (qlossy || klossy) {
+              // |q k - Q K| <= |dq| |k| + |Q| |dk| over the lossy elements (units 2^(qlsb + klsb))
+              uint64_t err = 0;
+              for (int wd = 0; wd < 4; ++wd) {
+                const uint32_t ql = S.qlossy[g][wd], kl = S.klossy[key][wd];
+                for (uint32_t m = ql; m; m &= m - 1) {
+                  const int i = 32 * wd + __ffs(m) - 1;
+                  const int32_t kf = read_fix(sK, K_PLANE, key, i, BK);
+                  err += (uint64_t)(kf < 0 ? -kf : kf) + ((kl >> (i & 31)) & 1u);
+                }
+                for (uint32_t m = kl; m; m &= m - 1) {
+                  const int i = 32 * wd + __ffs(m) - 1;
+                  const int32_t qf = S.qfix[g][i];
+                  err += (uint64_t)(qf < 0 ? -qf : qf);
+                }
+              }
+              ls = logit_bounded(acc, err, S.qlsb[g] + S.klsb[key], P.am, P.ae, t);
+            } else {
+              ls = logit_exact64(acc, S.qlsb[g] + S.klsb[key], P.am, P.ae, t);
+            }
+            if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
+            else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
+            else atomicMax(&S.rst[g], ST_DOMAIN);
+          }
+        }
+        sT[g * BK + key] = out;
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+
+    // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
+    for (int e0 = 0; e0 < nrows * BK; e0 += THREADS) {
+      const int e = e0 + warp * 32 + lane;
+      const uint32_t hit = __ballot_sync(0xffffffffu, e < nrows * BK && sT[e] == T_UNCERT);
+      for (uint32_t m = hit; m; m &= m - 1) {
+        const int ee = e0 + warp * 32 + __ffs(m) - 1;
+        const int g = ee / BK, key = ee % BK;
+        int64_t run;
+        const int64_t kr = run_start(P, row0, j0 + key, run);
+        Rnd t = rnd_zero();
+        const int ls = warp_exact_logit(P, S.rows[g], kr, t);
+        if (lane == 0) {
+          if (ls == LOGIT_OK) {
+            sT[ee] = rnd_to_f32_bits(t);
+          } else {
+            sT[ee] = T_MASKED;
+            atomicMax(&S.rst[g], ST_DOMAIN);
+          }
+          ++n_exact;
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---------------- pass 2: tile bounds, weights, W digits ----------------
+#pragma unroll 1
+    for (int g = h; g < nrows; g += 2) {
+      const uint32_t tb = sT[g * BK + c];
+      const float tf = __uint_as_float(tb);
+      int32_t rl = INT32_MIN;
+      if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) rl = __float2int_ru(tf) + 1;
+      rl = __reduce_max_sync(0xffffffffu, rl);
+      if (lane == 0) S.rt[warp & 3][g] = rl;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int g = h; g < nrows; g += 2) {
+      const int key = c;
+      const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
+      const uint32_t tb = sT[g * BK + key];
+      uint64_t W = 0;
+      uint32_t lw = 0;
+      if (tb != T_MASKED && Rt != INT32_MIN) {
+        const Rnd t = rnd_from_f32(tb);
+        uint32_t M;
+        int64_t E;
+        int ws = weight_from_logit(t, S.ta, S.tb, M, E);
+        if (ws == W_RISKY) {
+          ++n_wide;
+          ws = wide_weight(t, M, E);
+        }
+        if (ws != W_OK) {
+          atomicMax(&S.rst[g], ST_TIER3);  // |t| >= 2^30 or a still-risky weight
+        } else {
+          const int sh = (int)(E + FW - Rt);
+          if (sh >= 0) {
+            W = (uint64_t)M << sh;
+          } else if (sh > -64) {
+            W = (uint64_t)M >> (-sh);
+            lw = (W << (-sh)) != M;
+          } else {
+            lw = 1;
+          }
+        }
+      }
+#pragma unroll
+      for (int wd = 0; wd < NW; ++wd) sW[tc::kmajor_off(6 * g + wd, key, NSW)] = (uint8_t)(W >> (8 * wd));
+      const uint64_t zs = warp_sum_u64(W);
+      const uint64_t vws = warp_sum_u64(S.vlossy[key] ? W + 1 : 0);
+      const uint32_t zl = __reduce_add_sync(0xffffffffu, lw);
+      if (lane == 0) {
+        S.zs[warp & 3][g] = zs;
+        S.zl[warp & 3][g] = zl;
+        S.vw[warp & 3][g] = vws;
+      }
+    }
+    tc::fence_async_smem();
+    __syncthreads();
+
+    // ---------------- P.V MMAs: 3 value digits x (N = 48: row weight digits) ----------------
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t av = tc::smem_u32(sV), bw = tc::smem_u32(sW);
+      const uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
+#pragma unroll 1
+      for (int u = 0; u < NV; ++u) {
+        const uint32_t idesc = tc::idesc_i8(128, NSW, u == NV - 1, false);
+        for (int ks = 0; ks < BK / 32; ++ks) {
+          const uint64_t ad = tc::smem_desc(av + u * V_PLANE + ks * 2 * lbo_a, lbo_a, 128);
+          const uint64_t bd = tc::smem_desc(bw + ks * 2 * lbo_b, lbo_b, 128);
+          tc::mma_i8(tmem + COL_O + NSW * u, ad, bd, idesc, ks > 0);
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar_mma));
+    }
+    // meanwhile: this channel's exponent change, the rows' merges and bounds (registers only)
+    const int ve_now = S.ve[c];
+    int sh_base[GD / 2];
+#pragma unroll
+    for (int i = 0; i < GD / 2; ++i) {
+      const int g = h + 2 * i;
+      sh_base[i] = INT32_MIN;
+      if (g >= nrows) continue;
+      if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
+        const int d = ve_now - vec;
+        N[i] = shift_floor(N[i], -d);
+        Nerr[i] = scale_ceil(Nerr[i], -d) + 1;
+      }
+      const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
+      if (Rt == INT32_MIN) continue;
+      const int32_t Rn = R[i] == R_EMPTY ? Rt : max(R[i], Rt);
+      if (R[i] != R_EMPTY && Rn > R[i]) {
+        const int d = Rn - R[i];
+        N[i] = shift_floor(N[i], -d);
+        Nerr[i] = scale_ceil(Nerr[i], -d) + 1;
+        int lost;
+        Z[i] = floor_shift(Z[i], -d, lost);
+        Zerr[i] = scale_ceil(Zerr[i], -d) + (uint64_t)lost;
+      }
+      R[i] = Rn;
+      const uint64_t zt = S.zs[0][g] + S.zs[1][g] + S.zs[2][g] + S.zs[3][g];
+      const uint64_t nlw = (uint64_t)S.zl[0][g] + S.zl[1][g] + S.zl[2][g] + S.zl[3][g];
+      const uint64_t vw = S.vw[0][g] + S.vw[1][g] + S.vw[2][g] + S.vw[3][g];
+      const int zsh = (Rt - FW) - (Rn - FZ);
+      int lost = 0;
+      Z[i] += floor_shift((int64_t)zt, zsh, lost);
+      Zerr[i] += scale_ceil(nlw, zsh) + (uint64_t)lost;
+      const int sb = (Rt - FW - FV) - (Rn - FN);
+      sh_base[i] = sb;
+      Nerr[i] += scale_ceil(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
+      Nerr[i] += scale_ceil(vw, sb);        // truncated values: < W + 1 W units times one V unit
+      Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
+    }
+    vec = ve_now;
+    mma_pending = true;
+    {
+      const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
+      if (!__syncthreads_and(okw)) {
+        ok_wait = false;
+        break;
+      }
+      ph_mma ^= 1;
+      mma_pending = false;
+    }
+    tc::fence_after_sync();
+    // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
+#pragma unroll
+    for (int i = 0; i < GD / 2; ++i) {
+      const int g = h + 2 * i;
+      if (g >= nrows) break;  // uniform across the warp
+      uint32_t d0[8], d1[8], d2[8];
+      tc::tmem_ld8(tlane + COL_O + 6 * g, d0);
+      tc::tmem_ld8(tlane + COL_O + NSW + 6 * g, d1);
+      tc::tmem_ld8(tlane + COL_O + 2 * NSW + 6 * g, d2);
+      tc::tmem_wait_ld();
+      if (sh_base[i] == INT32_MIN) continue;
+      const int32_t s0 = (int32_t)d0[0];
+      const int32_t s1 = (int32_t)d0[1] + (int32_t)d1[0];
+      const int32_t s2 = (int32_t)d0[2] + (int32_t)d1[1] + (int32_t)d2[0];
+      const int32_t s3 = (int32_t)d0[3] + (int32_t)d1[2] + (int32_t)d2[1];
+      const int32_t s4 = (int32_t)d0[4] + (int32_t)d1[3] + (int32_t)d2[2];
+      const int32_t s5 = (int32_t)d0[5] + (int32_t)d1[4] + (int32_t)d2[3];
+      const int32_t s6 = (int32_t)d1[5] + (int32_t)d2[4];
+      const int32_t s7 = (int32_t)d2[5];
+      const uint32_t r0[3] = {(uint32_t)s0, (uint32_t)s1, (uint32_t)s2};
+      const uint32_t r1[3] = {(uint32_t)s3, (uint32_t)s4, (uint32_t)s5};
+      const uint32_t r2[2] = {(uint32_t)s6, (uint32_t)s7};
+      const int sb = sh_base[i];
+      N[i] += shift_floor(recomb<3>(r0), sb) + shift_floor(recomb<3>(r1), 24 + sb) + shift_floor(recomb<2>(r2), 48 + sb);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+  }
+
+  // a wait that gave up: give the copies / MMAs still in flight another bounded wait before the
+  // shared memory and TMEM are released (uniform: the flags follow block votes)
+  if (raw_pending) tc::mbar_wait(&S.bar_raw, ph_raw);
+  if (mma_pending) tc::mbar_wait(&S.bar_mma, ph_mma);
+  // ---------------- split partials of this CTA's rows ----------------
+  __syncthreads();
+  const int64_t rows = P.rows;
+#pragma unroll
+  for (int i = 0; i < GD / 2; ++i) {
+    const int g = h + 2 * i;
+    if (g >= nrows) break;
+    const int32_t row = S.rows[g];
+    if (row < 0) continue;
+    const int64_t pi = (int64_t)split * rows + row;
+    const int st = ok_wait ? S.rst[g] : ST_TIER3;
+    if (c == 0) {
+      P.pR[pi] = R[i];
+      P.pZ[pi] = Z[i];
+      P.pZe[pi] = Zerr[i];
+      P.pSt[pi] = st;
+    }
+    const bool empty = R[i] == R_EMPTY || vec == INT32_MIN;
+    // this kernel's N interval is [N - Nerr, N + Nerr]; partials are one-sided [N, N + Nerr]
+    P.pNR[pi * DV + c] = empty ? R_EMPTY : R[i] + vec;
+    P.pN[pi * DV + c] = empty ? 0 : N[i] - (int64_t)Nerr[i];
+    P.pNe[pi * DV + c] = empty ? 0 : 2 * Nerr[i];
+  }
+  n_exact = __reduce_add_sync(0xffffffffu, n_exact);
+  n_wide = __reduce_add_sync(0xffffffffu, n_wide);
+  if (lane == 0) {
+    stat_add(P, STAT_SCORE_EXACT, n_exact);
+    stat_add(P, STAT_WEIGHT_WIDE, n_wide);
+  }
+  if (tid == 0) {
+    unsigned long long pairs = 0;
+    for (int g = 0; g < nrows; ++g) {
+      const int64_t l = S.rows[g] >= 0 ? S.len[g] : 0;
+      const int64_t a = kbeg, b = min(kend, l);
+      if (b > a) pairs += (unsigned long long)(b - a);
+    }
+    stat_add(P, STAT_PAIRS, pairs);
+    stat_add(P, STAT_TC_PAIRS, pairs);
+    if (!ok_wait) stat_add(P, STAT_UNRESOLVED, 1000000);  // a bounded wait gave up: loud
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_free(tmem, TMEM_COLS);
+}
+
+}  // namespace tcd
+
+// Grid (segments, splits); writes split partials (P.pR ..) for every listed row.
+cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(tcd::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)tcd::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)nseg, (unsigned)P.splits);
+  tcd::tc_decode_kernel<<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+  return cudaGetLastError();
+}
+
+}  // namespace ea

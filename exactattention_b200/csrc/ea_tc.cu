@@ -27,11 +27,14 @@
 #include "ea_core.cuh"
 #include "ea_numerics.h"
 #include "ea_tables.cuh"
+#include "ea_tc_common.cuh"
 #include "ea_tcgen05.cuh"
 
 namespace ea {
 
 namespace tck {
+
+using namespace tcc;
 
 constexpr int BM = 128, BN = 64, D = 128, DV = 128;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
@@ -102,102 +105,6 @@ __device__ unsigned long long g_phase_cycles[16];
 #define EA_PT_FLUSH
 #endif
 
-constexpr uint32_t T_UNCERT = 0x7FC00001u;  // pass-1 markers in the logit table (t is never NaN)
-constexpr uint32_t T_MASKED = 0x7FC00002u;
-
-__device__ __forceinline__ int32_t lead_of(int32_t m, int32_t e) {  // exponent of |m 2^e|'s leading bit
-  return e + bitlen64((uint64_t)(m < 0 ? -m : m)) - 1;
-}
-
-// floor(x * 2^s) of an int64 (s may be negative); callers keep left shifts in range
-__device__ __forceinline__ int64_t shift_floor(int64_t x, int s) {
-  if (s >= 0) return (int64_t)((uint64_t)x << s);
-  return s <= -63 ? (x < 0 ? -1 : 0) : (x >> (-s));
-}
-// ceil(u * 2^s): exact for s >= 0 (callers keep it in range), rounded up otherwise
-__device__ __forceinline__ uint64_t scale_ceil(uint64_t u, int s) {
-  if (s >= 0) return s >= 63 ? (u ? ~0ull >> 2 : 0) : (u << s);
-  int r = -s;
-  if (r >= 64) return u != 0;
-  return (u >> r) + ((u & ((1ull << r) - 1)) != 0);
-}
-
-__device__ __forceinline__ Rnd rnd_from_f32(uint32_t b) {
-  Rnd t = rnd_zero();
-  int32_t m, e;
-  decode_fp32(b, m, e);
-  t.q = (uint64_t)(m < 0 ? -m : m);
-  t.qe = e;
-  t.neg = m < 0;
-  if (t.q == 0) t.neg = 0;
-  return t;
-}
-
-// block fixed point of one bf16 element against lsb, as a two's complement int32
-__device__ __forceinline__ int32_t fixq(uint32_t bits, int lsb, int& lost, int& bad) {
-  int32_t m, e;
-  lost = 0;
-  if (!decode_bf16(bits, m, e)) {
-    bad = 1;
-    return 0;
-  }
-  if (!m) return 0;
-  int32_t mag = m < 0 ? -m : m;
-  int sh = e - lsb;
-  int32_t f;
-  if (sh >= 0) {
-    f = mag << sh;
-  } else {
-    int s = -sh;
-    f = s >= 31 ? 0 : (mag >> s);
-    lost = (s >= 31) ? 1 : ((f << s) != mag);
-  }
-  return m < 0 ? -f : f;
-}
-
-// sum_{g < n} D_g 2^(8g) exactly in int64 for n <= 4 int32 groups (|D_g| < 2^25): a chain of
-// 32 x 32 -> 64-bit multiply-adds
-template <int n>
-__device__ __forceinline__ int64_t recomb(const uint32_t* D) {
-  int64_t acc = (int64_t)(int32_t)D[0];
-  if (n > 1) acc += (int64_t)(int32_t)D[1] * 256;
-  if (n > 2) acc += (int64_t)(int32_t)D[2] * 65536;
-  if (n > 3) acc += (int64_t)(int32_t)D[3] * 16777216;
-  return acc;
-}
-
-// byte p of each of four words, packed into one word (byte permutes)
-template <int p>
-__device__ __forceinline__ uint32_t pack4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
-  constexpr uint32_t sel = (uint32_t)p | ((uint32_t)(p + 4) << 4);
-  return __byte_perm(__byte_perm(x0, x1, sel), __byte_perm(x2, x3, sel), 0x5410);
-}
-
-// 16 int32 values -> their byte planes 0 .. NP-1, each as one uint4 (16 bytes)
-template <int NP>
-__device__ __forceinline__ void planes16(const uint32_t* x, uint4* out) {
-#pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    uint32_t w[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t a = x[4 * c], b = x[4 * c + 1], cc = x[4 * c + 2], d = x[4 * c + 3];
-      w[c] = p == 0 ? pack4<0>(a, b, cc, d) : p == 1 ? pack4<1>(a, b, cc, d) : p == 2 ? pack4<2>(a, b, cc, d)
-                                                                                       : pack4<3>(a, b, cc, d);
-    }
-    out[p] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
-
-// int32 fixed-point value of digit planes at (row, byte k) of an R-row K-major tile
-__device__ __forceinline__ int32_t read_fix(const uint8_t* planes, uint32_t plane_bytes, uint32_t row, uint32_t k,
-                                            uint32_t R) {
-  uint32_t o = tc::kmajor_off(row, k, R);
-  uint32_t b0 = planes[o], b1 = planes[o + plane_bytes], b2 = planes[o + 2 * plane_bytes];
-  int32_t b3 = (int8_t)planes[o + 3 * plane_bytes];
-  return (int32_t)(b0 | (b1 << 8) | (b2 << 16)) + (b3 << 24);
-}
-
 // Truncation bound of one windowed score, in units 2^(qlsb + klsb): for the lossy elements only,
 // |q k - Q K| <= |dq| |k| + |Q| |dk| with |dq|, |dk| < 1 unit and |k| < |K| + 1 unit when k is lossy.
 __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, const uint8_t* sK, int r, int kj) {
@@ -216,75 +123,6 @@ __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, co
     }
   }
   return err;
-}
-
-__device__ __noinline__ int logit_bounded(int64_t acc, uint64_t err, int sexp, int32_t am, int32_t ae, Rnd& t) {
-  return logit_from_interval(acc, err, sexp, am, ae, t);
-}
-
-__device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_t& E) {
-  return weight_from_logit_wide(t, g_ta128, g_tb128, M, E);
-}
-
-// Exact logit of q row `qrow` and k row `krow`, by the whole warp; every lane returns it.
-// Products q_i k_i = m 2^e (|m| < 2^16) summed exactly in a 128-bit window whose unit is 118
-// bits below the largest product bound; if some product falls below the window, 576-bit bins.
-__device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow, int64_t krow, Rnd& t) {
-  const int lane = threadIdx.x & 31;
-  int32_t pm[4], pe[4];
-  int emax = INT32_MIN;
-#pragma unroll
-  for (int m4 = 0; m4 < 4; ++m4) {
-    const int i = lane + 32 * m4;
-    int32_t qm, qe, km, ke;
-    decode_bf16(P.q[qrow * D + i], qm, qe);
-    decode_bf16(P.k[krow * D + i], km, ke);
-    pm[m4] = qm * km;
-    pe[m4] = qe + ke;
-    if (pm[m4]) emax = max(emax, pe[m4] + 16);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
-  if (emax == INT32_MIN) {
-    t = rnd_zero();
-    return LOGIT_OK;
-  }
-  const int unit = emax - 118;
-  bool below = false;
-  i128 s = 0;
-#pragma unroll
-  for (int m4 = 0; m4 < 4; ++m4) {
-    if (!pm[m4]) continue;
-    const int sh = pe[m4] - unit;
-    if (sh < 0) below = true;
-    else s += (i128)pm[m4] << sh;
-  }
-  int ls;
-  if (!__any_sync(0xffffffffu, below)) {
-    uint64_t lo = (uint64_t)s;
-    int64_t hi = (int64_t)(s >> 64);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
-      const int64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
-      const uint64_t sum = lo + lo2;
-      hi = hi + hi2 + (sum < lo ? 1 : 0);
-      lo = sum;
-    }
-    ls = logit_i128((i128)(((u128)(uint64_t)hi << 64) | lo), unit, P.am, P.ae, t);
-  } else {
-    ExactScore sc;
-    score_clear(sc);
-#pragma unroll
-    for (int m4 = 0; m4 < 4; ++m4)
-      if (pm[m4]) score_add(sc, pm[m4], pe[m4]);
-#pragma unroll
-    for (int b = 0; b < SCORE_BINS; ++b)
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sc.bins[b] += __shfl_xor_sync(0xffffffffu, sc.bins[b], o);
-    ls = logit_exact(sc, P.am, P.ae, t);
-  }
-  return ls;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const int32_t* __restrict__ block_rows) {

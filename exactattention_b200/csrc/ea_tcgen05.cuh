@@ -96,6 +96,27 @@ __device__ __forceinline__ void tmem_ld4(uint32_t addr, uint32_t* v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_ld2(uint32_t addr, uint32_t* v) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "r"(addr) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// bulk copies global -> shared (the untiled TMA path), completing on an mbarrier
+// ---------------------------------------------------------------------------
+// The calling thread arrives on `bar` and adds `bytes` to the transaction count of its current
+// phase; the phase completes once that many bytes of bulk copies have landed.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// `bytes` (a multiple of 16) from global `src` to shared `dst`, both 16-byte aligned
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier with bounded waits
 // ---------------------------------------------------------------------------

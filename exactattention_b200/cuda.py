@@ -100,7 +100,7 @@ def _ptr(t):
 
 def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
            seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-           out_tensor=None, flags=None, stats=None, stream=None, blocks=None, no_alloc=False):
+           out_tensor=None, flags=None, stats=None, stream=None, blocks=None, segments=None, no_alloc=False):
     """Device-level launch, no host sync. q (rows, d), k, v: torch tensors of bf16 bits (any
     16-bit dtype) on one CUDA device. One mask: CSR (row_ptr, key_idx int64), RANGE
     (kv_base, kv_len int64: row r attends k rows kv_base[r] + [0, kv_len[r])), or PAGED
@@ -110,7 +110,9 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     max_row_keys bounds every row's key count (required for RANGE/PAGED without a host sync).
     `blocks` (from row_blocks; every row in some block) lets RANGE masks with d = dv = 128 use the
     tensor-core kernel, and HYBRID masks run their shared range on it (the per-row lists on the
-    CUDA cores, the two partials merged exactly).
+    CUDA cores, the two partials merged exactly). `segments` (from row_segments) runs RANGE masks
+    with d = dv = 128 through the tensor-core decode kernel (keys on the MMA's M side); PAGED masks
+    with d = dv = 128 and at most 8 q heads per kv head take it without a table.
     `no_alloc` calls ea_attention_cuda_noalloc instead: the library allocates no device memory for
     the call (its scratch is a fixed static array; see include/exactattn_cuda.h for the limits).
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
@@ -128,7 +130,8 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
         flags = torch.empty(rows, dtype=torch.uint8, device=dev)
     a = _launch_args(q, k, v, alpha, row_ptr=row_ptr, key_idx=key_idx, kv_base=kv_base, kv_len=kv_len,
                      page_table=page_table, seq_lens=seq_lens, page_size=page_size, q_heads=q_heads,
-                     kv_heads=kv_heads, max_row_keys=max_row_keys, splits=splits, out=out, blocks=blocks)
+                     kv_heads=kv_heads, max_row_keys=max_row_keys, splits=splits, out=out, blocks=blocks,
+                     segments=segments)
     a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
     a.stats = _ptr(stats)
     s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
@@ -145,7 +148,7 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
 
 def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
                  seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-                 blocks=None):
+                 blocks=None, segments=None):
     """ea_launch_t for `launch`'s inputs and mask (outputs left unset)."""
     rows, d = q.shape[0], q.shape[-1]
     dv = v.shape[-1]
@@ -183,6 +186,8 @@ def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv
     a.splits = int(splits)
     if blocks is not None:
         a.block_rows, a.nblocks = blocks.data_ptr(), blocks.shape[0]
+    if segments is not None:
+        a.seg_rows, a.nsegs = segments.data_ptr(), segments.shape[0]
     return a
 
 
@@ -310,6 +315,24 @@ def attention_cuda_ranges(q, k, v, alpha, kv_base, kv_len, max_row_keys=None, ou
     return res, flags
 
 
+def row_segments(kv_base: np.ndarray, width: int = 8) -> np.ndarray:
+    """Groups RANGE-mask rows that share kv_base into segments of at most `width` (8) rows, -1
+    padded: the (nsegs, 8) int32 `segments` argument of launch (decode: a GQA group per segment).
+    Any grouping gives the same bits."""
+    kv_base = np.asarray(kv_base, np.int64)
+    order = np.argsort(kv_base, kind="stable")
+    b = kv_base[order]
+    cuts = np.flatnonzero(np.diff(b)) + 1
+    out = []
+    for grp in np.split(order, cuts):
+        for c in range(0, len(grp), width):
+            seg = np.full(8, -1, np.int32)
+            part = grp[c:c + width]
+            seg[:len(part)] = part
+            out.append(seg)
+    return np.stack(out) if out else np.zeros((0, 8), np.int32)
+
+
 def row_blocks(kv_base: np.ndarray, kv_len: np.ndarray, bm: int = 128) -> np.ndarray:
     """Groups RANGE-mask rows that share kv_base into blocks of `bm` (longest rows first, blocks
     ordered longest first, -1 padding): the (nblocks, bm) int32 `blocks` argument of launch. The
@@ -361,7 +384,7 @@ def wide_partials(q, k, v, alpha, rows, *, stream=None, stats=None, **mask) -> W
         raise ValueError("wide_partials needs max_row_keys (the row's key count over all merged ranges)")
     rows = rows.to(device=dev, dtype=torch.int32).contiguous()
     w = WidePartials(rows.numel(), v.shape[-1], dev)
-    mask = {k_: v_ for k_, v_ in mask.items() if k_ not in ("blocks", "splits")}
+    mask = {k_: v_ for k_, v_ in mask.items() if k_ not in ("blocks", "segments", "splits")}
     a = _launch_args(q, k, v, alpha, **mask)
     a.stats = _ptr(stats)
     ws = w.struct()

@@ -408,8 +408,11 @@ def device_case(name: str, device="cuda", shard: int = 0, nshards: int = 1) -> d
                   kv_len=torch.from_numpy((tok + 1).astype(np.int64)).to(dev), max_row_keys=T,
                   blocks=torch.from_numpy(row_blocks(base, tok + 1)).to(dev))
     elif name == "c5":
+        from .cuda import row_segments
+
         kw = dict(kv_base=torch.from_numpy(base.astype(np.int64)).to(dev),
-                  kv_len=torch.from_numpy(np.full(rows, Tn, np.int64)).to(dev), max_row_keys=T)
+                  kv_len=torch.from_numpy(np.full(rows, Tn, np.int64)).to(dev), max_row_keys=T,
+                  segments=torch.from_numpy(row_segments(base)).to(dev))
     elif name == "c4":
         from .cuda import row_blocks
 

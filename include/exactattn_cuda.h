@@ -94,6 +94,12 @@ typedef struct ea_launch {
    * per-row lists on the CUDA cores); any grouping gives the same bits. */
   const int32_t* block_rows;
   int64_t nblocks;
+  /* optional, RANGE masks (decode): segments of up to 8 rows that share kv_base (-1 pads),
+   * (nsegs, 8) int32, every row in one segment. With it, d = dv = 128, the tensor-core decode
+   * kernel runs: keys on the MMA's M side, the segment's rows in N, `splits` CTAs per segment.
+   * PAGED masks with d = dv = 128 and q_heads / kv_heads <= 8 take that kernel without it. */
+  const int32_t* seg_rows;
+  int64_t nsegs;
 } ea_launch_t;
 
 /* Device-pointer entry point: asynchronous on `stream` (a cudaStream_t, NULL = default).
