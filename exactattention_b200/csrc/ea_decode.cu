@@ -236,7 +236,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   // ---------------- per-thread running state (drain role: channel c, rows h, h + 2, ..) ----------
   const int h = warp >> 2, c = 32 * (warp & 3) + lane;
   const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-  const int FN = P.FZ, FZ = P.FZ;
+  // Fraction bits of this CTA's Z and N windows: the headroom only has to cover the split's own
+  // keys (61 - ceil(log2 keys)), which keeps more bits than the row-wide P.FZ; the windows are
+  // converted to P.FZ units (interval ends rounded outwards) when the partials are written.
+  int klog = 1;
+  while (klog < 62 && ((int64_t)1 << klog) < kend - kbeg) ++klog;
+  const int FN = 61 - klog, FZ = FN;
   int32_t R[GD / 2];
   int64_t Z[GD / 2], N[GD / 2];
   uint64_t Zerr[GD / 2], Nerr[GD / 2];
@@ -660,16 +665,23 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     const int64_t pi = (int64_t)split * rows + row;
     const int st = ok_wait ? S.rst[g] : ST_TIER3;
     if (c == 0) {
+      const int dsh = FZ - P.FZ;
+      const int64_t zlo = shift_floor(Z[i], -dsh);
+      const int64_t zhi = -shift_floor(-(Z[i] + (int64_t)Zerr[i]), -dsh);
       P.pR[pi] = R[i];
-      P.pZ[pi] = Z[i];
-      P.pZe[pi] = Zerr[i];
+      P.pZ[pi] = zlo;
+      P.pZe[pi] = (uint64_t)(zhi - zlo);
       P.pSt[pi] = st;
     }
     const bool empty = R[i] == R_EMPTY || vec == INT32_MIN;
-    // this kernel's N interval is [N - Nerr, N + Nerr]; partials are one-sided [N, N + Nerr]
+    // this kernel's N interval is [N - Nerr, N + Nerr] in units 2^(R + VE_c - FN); partials are
+    // one-sided [N, N + Nerr] in units 2^(NR - P.FZ): floor the low end, ceil the high end
+    const int dsh = FN - P.FZ;
+    const int64_t nlo = shift_floor(N[i] - (int64_t)Nerr[i], -dsh);
+    const int64_t nhi = -shift_floor(-(N[i] + (int64_t)Nerr[i]), -dsh);
     P.pNR[pi * DV + c] = empty ? R_EMPTY : R[i] + vec;
-    P.pN[pi * DV + c] = empty ? 0 : N[i] - (int64_t)Nerr[i];
-    P.pNe[pi * DV + c] = empty ? 0 : 2 * Nerr[i];
+    P.pN[pi * DV + c] = empty ? 0 : nlo;
+    P.pNe[pi * DV + c] = empty ? 0 : (uint64_t)(nhi - nlo);
   }
   n_exact = __reduce_add_sync(0xffffffffu, n_exact);
   n_wide = __reduce_add_sync(0xffffffffu, n_wide);
