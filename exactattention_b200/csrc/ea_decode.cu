@@ -59,7 +59,7 @@ struct Small {
   int32_t qfix[GD][D];
   int32_t klsb[BK];
   int32_t kbad[BK];
-  int32_t vlossy[BK];
+  uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
   int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
   int32_t ve4[4][DV];  // per key quarter maxima of the current tile
   int32_t rows[GD];
@@ -70,7 +70,6 @@ struct Small {
   int32_t rt[4][GD];
   uint64_t zs[4][GD];
   uint32_t zl[4][GD];
-  uint64_t vw[4][GD];
   uint64_t bar_mma;
   uint64_t bar_raw;
   uint32_t tmem;
@@ -317,10 +316,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       if (ch == 0) {
         S.klsb[key] = lsb;
         S.kbad[key] = valid && bad;
-        S.vlossy[key] = 0;
       }
     }
-    __syncthreads();  // kbad / vlossy are reset above before the value checks below set them
+    __syncthreads();  // kbad is reset above before the value checks below set it
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
     uint32_t vw32[32];
@@ -373,7 +371,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           for (int p = 0; p < NV; ++p)
             *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(cc, 32 * kq + 16 * half, BK)) = pl[p];
         }
-        for (uint32_t m = lossy; m; m &= m - 1) atomicOr(&S.vlossy[32 * kq + __ffs(m) - 1], 1);
+        S.vlmask[cc][kq] = lossy;
       }
     }
     tc::fence_async_smem();
@@ -543,12 +541,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 #pragma unroll
       for (int wd = 0; wd < NW; ++wd) sW[tc::kmajor_off(6 * g + wd, key, NSW)] = (uint8_t)(W >> (8 * wd));
       const uint64_t zs = warp_sum_u64(W);
-      const uint64_t vws = warp_sum_u64(S.vlossy[key] ? W + 1 : 0);
       const uint32_t zl = __reduce_add_sync(0xffffffffu, lw);
       if (lane == 0) {
         S.zs[warp & 3][g] = zs;
         S.zl[warp & 3][g] = zl;
-        S.vw[warp & 3][g] = vws;
       }
     }
     tc::fence_async_smem();
@@ -597,7 +593,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       R[i] = Rn;
       const uint64_t zt = S.zs[0][g] + S.zs[1][g] + S.zs[2][g] + S.zs[3][g];
       const uint64_t nlw = (uint64_t)S.zl[0][g] + S.zl[1][g] + S.zl[2][g] + S.zl[3][g];
-      const uint64_t vw = S.vw[0][g] + S.vw[1][g] + S.vw[2][g] + S.vw[3][g];
       const int zsh = (Rt - FW) - (Rn - FZ);
       int lost = 0;
       Z[i] += floor_shift((int64_t)zt, zsh, lost);
@@ -605,7 +600,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int sb = (Rt - FW - FV) - (Rn - FN);
       sh_base[i] = sb;
       Nerr[i] += scale_ceil(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
-      Nerr[i] += scale_ceil(vw, sb);        // truncated values: < W + 1 W units times one V unit
+      // truncated values of this channel: < W + 1 W units times one V unit, per lossy key
+      uint64_t vw = 0;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4)
+        for (uint32_t m = S.vlmask[c][q4]; m; m &= m - 1) {
+          const int key = 32 * q4 + __ffs(m) - 1;
+          uint64_t W = 0;
+#pragma unroll
+          for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
+          vw += W + 1;
+        }
+      Nerr[i] += scale_ceil(vw, sb);
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
     vec = ve_now;
