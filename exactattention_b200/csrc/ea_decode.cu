@@ -124,6 +124,19 @@ __device__ __forceinline__ int32_t lead_of_bits(uint32_t mag) {  // lead exponen
   return lead_of(m, e);
 }
 
+// floor(x * 2^s) of an int128 (callers keep left shifts in range)
+__device__ __forceinline__ i128 shift_floor128(i128 x, int s) {
+  if (s >= 0) return (i128)((u128)x << s);
+  return s <= -127 ? (x < 0 ? -1 : 0) : (x >> (-s));
+}
+// ceil(u * 2^s) as a u128 (s < 64)
+__device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
+  if (s >= 0) return u << s;
+  const int r = -s;
+  if (r >= 128) return u != 0;
+  return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
+}
+
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -240,10 +253,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   // converted to P.FZ units (interval ends rounded outwards) when the partials are written.
   int klog = 1;
   while (klog < 62 && ((int64_t)1 << klog) < kend - kbeg) ++klog;
-  const int FN = 61 - klog, FZ = FN;
+  const int FZ = 61 - klog;
+  // N runs in int128 with 40 more fraction bits, so its precision is relative to its own size
+  // rather than to max weight x max |v|; the written partial takes the unit that its magnitude
+  // allows (below)
+  const int FN = FZ + 40;
   int32_t R[GD / 2];
-  int64_t Z[GD / 2], N[GD / 2];
-  uint64_t Zerr[GD / 2], Nerr[GD / 2];
+  int64_t Z[GD / 2];
+  i128 N[GD / 2];
+  uint64_t Zerr[GD / 2];
+  u128 Nerr[GD / 2];
 #pragma unroll
   for (int i = 0; i < GD / 2; ++i) {
     R[i] = R_EMPTY;
@@ -576,16 +595,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       if (g >= nrows) continue;
       if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
         const int d = ve_now - vec;
-        N[i] = shift_floor(N[i], -d);
-        Nerr[i] = scale_ceil(Nerr[i], -d) + 1;
+        N[i] = shift_floor128(N[i], -d);
+        Nerr[i] = scale_ceil128(Nerr[i], -d) + 1;
       }
       const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
       if (Rt == INT32_MIN) continue;
       const int32_t Rn = R[i] == R_EMPTY ? Rt : max(R[i], Rt);
       if (R[i] != R_EMPTY && Rn > R[i]) {
         const int d = Rn - R[i];
-        N[i] = shift_floor(N[i], -d);
-        Nerr[i] = scale_ceil(Nerr[i], -d) + 1;
+        N[i] = shift_floor128(N[i], -d);
+        Nerr[i] = scale_ceil128(Nerr[i], -d) + 1;
         int lost;
         Z[i] = floor_shift(Z[i], -d, lost);
         Zerr[i] = scale_ceil(Zerr[i], -d) + (uint64_t)lost;
@@ -599,7 +618,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       Zerr[i] += scale_ceil(nlw, zsh) + (uint64_t)lost;
       const int sb = (Rt - FW - FV) - (Rn - FN);
       sh_base[i] = sb;
-      Nerr[i] += scale_ceil(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
+      Nerr[i] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
       // truncated values of this channel: < W + 1 W units times one V unit, per lossy key
       uint64_t vw = 0;
 #pragma unroll 1
@@ -611,7 +630,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
           vw += W + 1;
         }
-      Nerr[i] += scale_ceil(vw, sb);
+      Nerr[i] += scale_ceil128(vw, sb);
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
     vec = ve_now;
@@ -649,7 +668,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const uint32_t r1[3] = {(uint32_t)s3, (uint32_t)s4, (uint32_t)s5};
       const uint32_t r2[2] = {(uint32_t)s6, (uint32_t)s7};
       const int sb = sh_base[i];
-      N[i] += shift_floor(recomb<3>(r0), sb) + shift_floor(recomb<3>(r1), 24 + sb) + shift_floor(recomb<2>(r2), 48 + sb);
+      N[i] += shift_floor128(recomb<3>(r0), sb) + shift_floor128(recomb<3>(r1), 24 + sb) +
+              shift_floor128(recomb<2>(r2), 48 + sb);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -681,11 +701,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     const bool empty = R[i] == R_EMPTY || vec == INT32_MIN;
     // this kernel's N interval is [N - Nerr, N + Nerr] in units 2^(R + VE_c - FN); partials are
-    // one-sided [N, N + Nerr] in units 2^(NR - P.FZ): floor the low end, ceil the high end
-    const int dsh = FN - P.FZ;
-    const int64_t nlo = shift_floor(N[i] - (int64_t)Nerr[i], -dsh);
-    const int64_t nhi = -shift_floor(-(N[i] + (int64_t)Nerr[i]), -dsh);
-    P.pNR[pi * DV + c] = empty ? R_EMPTY : R[i] + vec;
+    // one-sided [N, N + Nerr] in units 2^(NR - P.FZ) with |N| < 2^(P.FZ + klog - 2) < (this
+    // split's keys) 2^P.FZ, the bound the exact merge of partials relies on: take the finest unit
+    // 2^s (s >= 0) that keeps the interval ends below it, floor the low end, ceil the high end
+    const i128 lo = N[i] - (i128)Nerr[i], hi = N[i] + (i128)Nerr[i];
+    const u128 mag = (u128)(lo < 0 ? -lo : lo) > (u128)(hi < 0 ? -hi : hi) ? (u128)(lo < 0 ? -lo : lo)
+                                                                              : (u128)(hi < 0 ? -hi : hi);
+    const int sx = max(0, bitlen128(mag) + 1 - (P.FZ + klog - 2));
+    const int64_t nlo = (int64_t)shift_floor128(lo, -sx);
+    const int64_t nhi = (int64_t)(-shift_floor128(-hi, -sx));
+    P.pNR[pi * DV + c] = empty ? R_EMPTY : R[i] + vec - FN + P.FZ + sx;
     P.pN[pi * DV + c] = empty ? 0 : nlo;
     P.pNe[pi * DV + c] = empty ? 0 : (uint64_t)(nhi - nlo);
   }
