@@ -35,6 +35,7 @@ constexpr int BK = 128, D = 128, DV = 128, GD = 8;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
 constexpr int FW = 48, FV = 23;
 constexpr int THREADS = 256;
+constexpr uint32_t VLCAP = 512;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
 constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
@@ -60,6 +61,11 @@ struct Small {
   int32_t klsb[BK];
   int32_t kbad[BK];
   uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
+  // the values that lost bits, with their lost parts (units 2^(lsb_c - 24)), added back exactly
+  // in the drain: (channel | key << 8 | still-lossy << 16), part
+  uint32_t vl_n;
+  uint32_t vl_ck[512];
+  int32_t vl_dx[512];
   int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
   int32_t ve4[4][DV];  // per key quarter maxima of the current tile
   int32_t rows[GD];
@@ -135,6 +141,27 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   const int r = -s;
   if (r >= 128) return u != 0;
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
+}
+
+// The part of bf16 `bits` that fixq(bits, lsb) truncated away (toward zero), in units
+// 2^(lsb - 24), itself truncated toward zero; `lost2` when bits remain below that unit.
+__device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost2) {
+  int32_t m, e;
+  decode_bf16(bits, m, e);
+  lost2 = 0;
+  const uint32_t mag = (uint32_t)(m < 0 ? -m : m);
+  const int s = lsb - e;  // fixq kept mag >> s
+  if (s <= 0) return 0;
+  const uint32_t low = s >= 31 ? mag : (mag & ((1u << s) - 1));  // units 2^e, < 2^9
+  uint32_t dx;
+  if (s <= 24) {
+    dx = low << (24 - s);
+  } else {
+    const int r = s - 24;
+    dx = r >= 32 ? 0u : (low >> r);
+    lost2 = r >= 32 ? (low != 0) : ((dx << r) != low);
+  }
+  return m < 0 ? -(int32_t)dx : (int32_t)dx;
 }
 
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
@@ -336,6 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         S.klsb[key] = lsb;
         S.kbad[key] = valid && bad;
       }
+      if (tid == 0 && it == 0) S.vl_n = 0;
     }
     __syncthreads();  // kbad is reset above before the value checks below set it
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
@@ -383,6 +411,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             int lost = 0, bad = 0;
             x[jj] = ve == INT32_MIN ? 0u : (uint32_t)fixq(b, lsb, lost, bad);
             lossy |= (uint32_t)(lost != 0) << (16 * half + jj);
+            if (lost) {
+              int lost2 = 0;
+              const int32_t dx = lost_part24(b, lsb, lost2);
+              const uint32_t k = atomicAdd(&S.vl_n, 1u);
+              if (k < VLCAP) {
+                S.vl_ck[k] = (uint32_t)cc | ((uint32_t)(32 * kq + 16 * half + jj) << 8) | ((uint32_t)lost2 << 16);
+                S.vl_dx[k] = dx;
+              }
+            }
           }
           uint4 pl[NV];
           planes16<NV>(x, pl);
@@ -619,18 +656,40 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int sb = (Rt - FW - FV) - (Rn - FN);
       sh_base[i] = sb;
       Nerr[i] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
-      // truncated values of this channel: < W + 1 W units times one V unit, per lossy key
-      uint64_t vw = 0;
+      // values that lost bits in the V window: their lost parts times the weights, added exactly
+      // up to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W
+      // units times one V unit per lossy key
+      const uint32_t nl = S.vl_n;
+      if (nl <= VLCAP) {
+        i128 corr = 0;
+        u128 cerr = 0;
 #pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4)
-        for (uint32_t m = S.vlmask[c][q4]; m; m &= m - 1) {
-          const int key = 32 * q4 + __ffs(m) - 1;
+        for (uint32_t k = 0; k < nl; ++k) {
+          const uint32_t ck = S.vl_ck[k];
+          if ((int)(ck & 0xFFu) != c) continue;
+          const int key = (int)((ck >> 8) & 0xFFu);
           uint64_t W = 0;
 #pragma unroll
           for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-          vw += W + 1;
+          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[k], sb - 24);
+          cerr += (sb - 24 < 0) ? 1u : 0u;
+          if ((ck >> 16) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
         }
-      Nerr[i] += scale_ceil128(vw, sb);
+        N[i] += corr;
+        Nerr[i] += cerr;
+      } else {
+        uint64_t vw = 0;
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4)
+          for (uint32_t m = S.vlmask[c][q4]; m; m &= m - 1) {
+            const int key = 32 * q4 + __ffs(m) - 1;
+            uint64_t W = 0;
+#pragma unroll
+            for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
+            vw += W + 1;
+          }
+        Nerr[i] += scale_ceil128(vw, sb);
+      }
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
     vec = ve_now;

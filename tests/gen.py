@@ -21,6 +21,9 @@ def bf16(rng: np.random.Generator, shape, kind: str = "normal", scale: float = 1
         x = np.where(rng.random(shape) < 0.02, rng.standard_normal(shape) * 30 * scale, x)
     elif kind == "dupes":
         x = rng.choice(np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 2.0]) * scale, size=shape)
+    elif kind == "heavy":  # 1% of rows scaled by 32 (long-context stress: wide channel ranges)
+        x = rng.standard_normal(shape) * scale
+        x = x * np.where(rng.random(shape[:1]) < 0.01, 32.0, 1.0).reshape((-1,) + (1,) * (len(shape) - 1))
     elif kind == "subnormal":
         x = rng.standard_normal(shape) * 2.0 ** -130
     else:

@@ -27,7 +27,8 @@ def _range_case(rng, kind, vkind, nseg, group, L):
     return Q, K, V, kb, kl
 
 
-@pytest.mark.parametrize("kind,vkind", [(k, "normal") for k in KINDS] + [("outlier", "wide"), ("dupes", "dupes")])
+@pytest.mark.parametrize("kind,vkind", [(k, "normal") for k in KINDS] + [("outlier", "wide"), ("dupes", "dupes"),
+                                                                         ("heavy", "heavy")])
 @pytest.mark.parametrize("group,splits", [(2, 1), (2, 3), (1, 2), (5, 1), (8, 4)])
 def test_decode_range_matches_simt_and_oracle(kind, vkind, group, splits):
     import torch
