@@ -31,11 +31,15 @@ namespace tcd {
 
 using namespace tcc;
 
+#ifdef EA_PHASE_TIMERS
+__device__ unsigned long long g_phase_cycles[16];
+#endif
+
 constexpr int BK = 128, D = 128, DV = 128, GD = 8;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
 constexpr int FW = 48, FV = 23;
 constexpr int THREADS = 256;
-constexpr uint32_t VLCAP = 512;
+constexpr uint32_t VLCAP = 4;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
 constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
@@ -61,11 +65,11 @@ struct Small {
   int32_t klsb[BK];
   int32_t kbad[BK];
   uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
-  // the values that lost bits, with their lost parts (units 2^(lsb_c - 24)), added back exactly
-  // in the drain: (channel | key << 8 | still-lossy << 16), part
-  uint32_t vl_n;
-  uint32_t vl_ck[512];
-  int32_t vl_dx[512];
+  // per channel, up to VLCAP values that lost bits, with their lost parts (units
+  // 2^(lsb_c - 24)), added back exactly in the drain: (key | still-lossy << 8), part
+  uint32_t vl_n[DV];
+  uint32_t vl_k[DV][4];
+  int32_t vl_dx[DV][4];
   int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
   int32_t ve4[4][DV];  // per key quarter maxima of the current tile
   int32_t rows[GD];
@@ -304,6 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   bool raw_pending = kbeg < kend, mma_pending = false;  // operations a timed-out exit must drain
   unsigned n_exact = 0, n_wide = 0;
 
+  EA_PT_INIT
   for (int64_t j0 = kbeg; j0 < kend; j0 += BK) {
     const int nvalid = (int)min((int64_t)BK, kend - j0);
     {
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       ph_raw ^= 1;
       raw_pending = false;
     }
+    EA_PT(0)
     // ---------------- K tile -> digit planes (8 elements per item, 16 lanes per key) ----------------
 #pragma unroll 1
     for (int it = 0; it < 8; ++it) {
@@ -363,9 +369,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         S.klsb[key] = lsb;
         S.kbad[key] = valid && bad;
       }
-      if (tid == 0 && it == 0) S.vl_n = 0;
+      if (tid < DV && it == 0) S.vl_n[tid] = 0;
     }
     __syncthreads();  // kbad is reset above before the value checks below set it
+    EA_PT(1)
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
     uint32_t vw32[32];
@@ -394,6 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       S.ve[tid] = max(S.ve[tid], vt);
     }
     __syncthreads();
+    EA_PT(2)
     // ---------------- V tile -> digit planes against VE_c ----------------
     {
 #pragma unroll
@@ -414,10 +422,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             if (lost) {
               int lost2 = 0;
               const int32_t dx = lost_part24(b, lsb, lost2);
-              const uint32_t k = atomicAdd(&S.vl_n, 1u);
+              const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
               if (k < VLCAP) {
-                S.vl_ck[k] = (uint32_t)cc | ((uint32_t)(32 * kq + 16 * half + jj) << 8) | ((uint32_t)lost2 << 16);
-                S.vl_dx[k] = dx;
+                S.vl_k[cc][k] = (uint32_t)(32 * kq + 16 * half + jj) | ((uint32_t)lost2 << 8);
+                S.vl_dx[cc][k] = dx;
               }
             }
           }
@@ -432,6 +440,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     tc::fence_async_smem();
     __syncthreads();
+    EA_PT(3)
     // the raw tiles are consumed: bring in the next tile while this one is processed
     if (j0 + BK < kend) {
       raw_pending = true;
@@ -468,6 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       mma_pending = false;
     }
     tc::fence_after_sync();
+    EA_PT(4)
 
     // ---------------- pass 1: certified logits (lane: key; rows h, h + 2, ..) ----------------
     {
@@ -529,6 +539,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     tc::fence_before_sync();
     __syncthreads();
 
+    EA_PT(5)
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
     for (int e0 = 0; e0 < nrows * BK; e0 += THREADS) {
       const int e = e0 + warp * 32 + lane;
@@ -553,6 +564,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     __syncthreads();
 
+    EA_PT(6)
     // ---------------- pass 2: tile bounds, weights, W digits ----------------
 #pragma unroll 1
     for (int g = h; g < nrows; g += 2) {
@@ -606,6 +618,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     tc::fence_async_smem();
     __syncthreads();
 
+    EA_PT(7)
     // ---------------- P.V MMAs: 3 value digits x (N = 48: row weight digits) ----------------
     if (tid == 0) {
       tc::fence_after_sync();
@@ -659,21 +672,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       // values that lost bits in the V window: their lost parts times the weights, added exactly
       // up to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W
       // units times one V unit per lossy key
-      const uint32_t nl = S.vl_n;
+      const uint32_t nl = S.vl_n[c];
       if (nl <= VLCAP) {
         i128 corr = 0;
         u128 cerr = 0;
 #pragma unroll 1
         for (uint32_t k = 0; k < nl; ++k) {
-          const uint32_t ck = S.vl_ck[k];
-          if ((int)(ck & 0xFFu) != c) continue;
-          const int key = (int)((ck >> 8) & 0xFFu);
+          const uint32_t ck = S.vl_k[c][k];
+          const int key = (int)(ck & 0xFFu);
           uint64_t W = 0;
 #pragma unroll
           for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[k], sb - 24);
+          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);
           cerr += (sb - 24 < 0) ? 1u : 0u;
-          if ((ck >> 16) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
+          if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
         }
         N[i] += corr;
         Nerr[i] += cerr;
@@ -693,6 +705,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
     vec = ve_now;
+    EA_PT(8)
     mma_pending = true;
     {
       const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
@@ -704,6 +717,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       mma_pending = false;
     }
     tc::fence_after_sync();
+    EA_PT(9)
     // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
 #pragma unroll
     for (int i = 0; i < GD / 2; ++i) {
@@ -732,7 +746,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     tc::fence_before_sync();
     __syncthreads();
+    EA_PT(10)
   }
+  EA_PT_FLUSH
 
   // a wait that gave up: give the copies / MMAs still in flight another bounded wait before the
   // shared memory and TMEM are released (uniform: the flags follow block votes)
@@ -808,3 +824,12 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
 }
 
 }  // namespace ea
+
+#ifdef EA_PHASE_TIMERS
+// phase clocks of the decode kernel (timer builds only): copies and clears the 16 counters
+extern "C" int ea_debug_phase_cycles_decode(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, ea::tcd::g_phase_cycles, sizeof(unsigned long long) * 16);
+  unsigned long long z[16] = {0};
+  return cudaMemcpyToSymbol(ea::tcd::g_phase_cycles, z, sizeof(z)) == cudaSuccess ? 0 : -4;
+}
+#endif

@@ -85,24 +85,8 @@ struct Small {
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
-// Optional phase clocks (built with -DEA_PHASE_TIMERS): thread 0 of every CTA accumulates the
-// cycles between the barriers that separate the phases of the tile loop.
 #ifdef EA_PHASE_TIMERS
 __device__ unsigned long long g_phase_cycles[16];
-#define EA_PT_INIT long long pt_last = clock64(); long long pt_acc[16] = {0};
-#define EA_PT(i)                        \
-  if (tid == 0) {                       \
-    const long long pt_now = clock64(); \
-    pt_acc[i] += pt_now - pt_last;      \
-    pt_last = pt_now;                   \
-  }
-#define EA_PT_FLUSH \
-  if (tid == 0)     \
-    for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], (unsigned long long)pt_acc[i]);
-#else
-#define EA_PT_INIT
-#define EA_PT(i)
-#define EA_PT_FLUSH
 #endif
 
 // Truncation bound of one windowed score, in units 2^(qlsb + klsb): for the lossy elements only,

@@ -9,6 +9,26 @@
 #include "ea_tables.cuh"
 #include "ea_tcgen05.cuh"
 
+// Optional phase clocks (built with -DEA_PHASE_TIMERS): thread 0 of every CTA accumulates the
+// cycles between the barriers that separate the phases of the tile loop into the 16 counters
+// g_phase_cycles, which each kernel's translation unit defines in its own namespace.
+#ifdef EA_PHASE_TIMERS
+#define EA_PT_INIT long long pt_last = clock64(); long long pt_acc[16] = {0};
+#define EA_PT(i)                        \
+  if (tid == 0) {                       \
+    const long long pt_now = clock64(); \
+    pt_acc[i] += pt_now - pt_last;      \
+    pt_last = pt_now;                   \
+  }
+#define EA_PT_FLUSH \
+  if (tid == 0)     \
+    for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], (unsigned long long)pt_acc[i]);
+#else
+#define EA_PT_INIT
+#define EA_PT(i)
+#define EA_PT_FLUSH
+#endif
+
 namespace ea {
 namespace tcc {
 
