@@ -168,6 +168,40 @@ __device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost
   return m < 0 ? -(int32_t)dx : (int32_t)dx;
 }
 
+// shift that gives 0 for amounts of 32 or more (PTX shl clamps the amount)
+__device__ __forceinline__ uint32_t shl_clamp(uint32_t x, uint32_t s) {
+  uint32_t r;
+  asm("shl.b32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(s));
+  return r;
+}
+// Fixed point of the low / high bf16 of word w against ebase = lsb + 134: sign (frac | 0x80) <<
+// (E - ebase). Equal to fixq for a normal element with E >= ebase, and 0 for a zero element when
+// ebase >= 1 (the negative amount clamps the shift).
+__device__ __forceinline__ uint32_t fix_lo(uint32_t w, int ebase) {
+  const uint32_t mag = shl_clamp((w & 0x7Fu) | 0x80u, ((w >> 7) & 0xFFu) - (uint32_t)ebase);
+  const uint32_t sg = __byte_perm(w, 0u, 0x9999);  // bit 15 replicated
+  return (mag ^ sg) - sg;
+}
+__device__ __forceinline__ uint32_t fix_hi(uint32_t w, int ebase) {
+  const uint32_t mag = shl_clamp(((w >> 16) & 0x7Fu) | 0x80u, ((w >> 23) & 0xFFu) - (uint32_t)ebase);
+  const uint32_t sg = __byte_perm(w, 0u, 0xBBBB);  // bit 31 replicated
+  return (mag ^ sg) - sg;
+}
+// per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
+__device__ __forceinline__ uint32_t nz_mag_minus1(uint32_t w) {
+  return ((w & 0x7FFF7FFFu) + 0x7FFF7FFFu) ^ 0x80008000u;
+}
+// 4 x 4 byte transpose: p_k = bytes k of x0 .. x3
+__device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
+                                           uint32_t& p1, uint32_t& p2, uint32_t& p3) {
+  const uint32_t a = __byte_perm(x0, x1, 0x5140), b = __byte_perm(x0, x1, 0x7362);
+  const uint32_t c = __byte_perm(x2, x3, 0x5140), d = __byte_perm(x2, x3, 0x7362);
+  p0 = __byte_perm(a, c, 0x5410);
+  p1 = __byte_perm(a, c, 0x7632);
+  p2 = __byte_perm(b, d, 0x5410);
+  p3 = __byte_perm(b, d, 0x7632);
+}
+
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -321,78 +355,116 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       raw_pending = false;
     }
     EA_PT(0)
-    // ---------------- K tile -> digit planes (8 elements per item, 16 lanes per key) ----------------
+    // ---------------- K tile -> digit planes (16 elements per item, 8 lanes per key) ----------------
+    // Fast path (every nonzero element normal and at most W - 8 binades below the key's largest):
+    // x = sign (frac | 0x80) << (E - Ebase), zeros through the shift clamp; otherwise fixq with
+    // lossy masks. Lanes 4-7 of a key load their two 16-byte halves in swapped order, so the 8
+    // lanes' loads cover the 128 bytes of a bank row without conflicts.
 #pragma unroll 1
-    for (int it = 0; it < 8; ++it) {
-      const int key = 16 * it + (tid >> 4), ch = tid & 15;
+    for (int it = 0; it < 4; ++it) {
+      const int key = 32 * it + (tid >> 3), l8 = tid & 7, hsw = (l8 >> 2) & 1;
       const bool valid = key < nvalid;
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      if (valid) {
-        const uint4 x = *(const uint4*)(rawk + key * (D * 2) + ch * 16);
-        w[0] = x.x;
-        w[1] = x.y;
-        w[2] = x.z;
-        w[3] = x.w;
-      }
-      uint32_t mx = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
-                             __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
-      mx = max(mx & 0xFFFFu, mx >> 16);
+      uint32_t w[8];
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int i = 0; i < 8; ++i) w[i] = 0u;
+      if (valid) {
+        const uint8_t* src = rawk + key * (D * 2) + l8 * 32;
+        const uint4 a = *(const uint4*)(src + 16 * hsw);
+        const uint4 b = *(const uint4*)(src + 16 * (1 - hsw));
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+        w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+      }
+      uint32_t mx = 0, mn = 0xFFFFFFFFu;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx = __vmaxu2(mx, w[i] & 0x7FFF7FFFu);
+        mn = __vminu2(mn, nz_mag_minus1(w[i]));
+      }
+      mx = max(mx & 0xFFFFu, mx >> 16);
+      mn = min(mn & 0xFFFFu, mn >> 16);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      }
       const int bad = mx >= 0x7F80u;
       const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
-      uint32_t xs[8];
+      const int ebase = lsb + 134;  // x = (frac | 0x80) << (E - ebase) for a normal element
+      const bool fast = lead == INT32_MIN || (ebase >= 1 && mn + 1 >= ((uint32_t)ebase << 7));
+      uint32_t xs[16];
       uint32_t lm = 0;
+      if (lead == INT32_MIN) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t b = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-        int lost = 0, b2 = 0;
-        xs[e] = lead == INT32_MIN ? 0u : (uint32_t)fixq(b, lsb, lost, b2);
-        lm |= (uint32_t)(lost != 0) << e;
-      }
+        for (int e = 0; e < 16; ++e) xs[e] = 0u;
+      } else if (fast) {
 #pragma unroll
-      for (int p = 0; p < NK; ++p) {
-        uint32_t lo, hi;
-        if (p == 0) { lo = pack4<0>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<0>(xs[4], xs[5], xs[6], xs[7]); }
-        else if (p == 1) { lo = pack4<1>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<1>(xs[4], xs[5], xs[6], xs[7]); }
-        else if (p == 2) { lo = pack4<2>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<2>(xs[4], xs[5], xs[6], xs[7]); }
-        else { lo = pack4<3>(xs[0], xs[1], xs[2], xs[3]); hi = pack4<3>(xs[4], xs[5], xs[6], xs[7]); }
-        *(uint2*)(sK + p * K_PLANE + tc::kmajor_off(key, 8 * ch, BK)) = make_uint2(lo, hi);
+        for (int i = 0; i < 8; ++i) {
+          xs[2 * i] = fix_lo(w[i], ebase);
+          xs[2 * i + 1] = fix_hi(w[i], ebase);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const uint32_t b = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+          int lost = 0, b2 = 0;
+          xs[e] = (uint32_t)fixq(b, lsb, lost, b2);
+          lm |= (uint32_t)(lost != 0) << e;
+        }
       }
-      // lossy mask of 32 elements (4 lanes) per word
-      uint32_t lw = lm << (8 * (ch & 3));
-      lw |= __shfl_xor_sync(0xffffffffu, lw, 1);
-      lw |= __shfl_xor_sync(0xffffffffu, lw, 2);
-      if ((ch & 3) == 0) S.klossy[key][ch >> 2] = lw;
-      if (ch == 0) {
+      // elements 0-7 are dims 16 l8 + 8 hsw .., elements 8-15 the other half
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t p0a, p1a, p2a, p3a, p0b, p1b, p2b, p3b;
+        transpose4(xs[8 * hf], xs[8 * hf + 1], xs[8 * hf + 2], xs[8 * hf + 3], p0a, p1a, p2a, p3a);
+        transpose4(xs[8 * hf + 4], xs[8 * hf + 5], xs[8 * hf + 6], xs[8 * hf + 7], p0b, p1b, p2b, p3b);
+        const uint32_t off = tc::kmajor_off(key, 16 * l8 + 8 * (hf ^ hsw), BK);
+        *(uint2*)(sK + 0 * K_PLANE + off) = make_uint2(p0a, p0b);
+        *(uint2*)(sK + 1 * K_PLANE + off) = make_uint2(p1a, p1b);
+        *(uint2*)(sK + 2 * K_PLANE + off) = make_uint2(p2a, p2b);
+        *(uint2*)(sK + 3 * K_PLANE + off) = make_uint2(p3a, p3b);
+      }
+      // lossy mask in dim order: this lane's 16 dims, then 32 dims (2 lanes) per word
+      const uint32_t lm16 = hsw ? ((lm >> 8) | ((lm & 0xFFu) << 8)) : lm;
+      const uint32_t lw = (lm16 << (16 * (l8 & 1))) | (__shfl_xor_sync(0xffffffffu, lm16, 1) << (16 * (1 - (l8 & 1))));
+      if ((l8 & 1) == 0) S.klossy[key][l8 >> 1] = lw;
+      if (l8 == 0) {
         S.klsb[key] = lsb;
         S.kbad[key] = valid && bad;
       }
-      if (tid < DV && it == 0) S.vl_n[tid] = 0;
     }
+    if (tid < DV) S.vl_n[tid] = 0;
     __syncthreads();  // kbad is reset above before the value checks below set it
     EA_PT(1)
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
     uint32_t vw32[32];
+    uint32_t vmn;  // per channel (half) the smallest nonzero |v| - 1 over this thread's keys
     {
       uint32_t mx = 0;
+      vmn = 0xFFFFFFFFu;
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const int key = 32 * kq + jj;
         vw32[jj] = key < nvalid ? *(const uint32_t*)(rawv + key * (DV * 2) + cp * 4) : 0u;
         mx = __vmaxu2(mx, vw32[jj] & 0x7FFF7FFFu);
+        vmn = __vminu2(vmn, nz_mag_minus1(vw32[jj]));
       }
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t m = (mx >> (16 * hh)) & 0xFFFFu;
-        if (m >= 0x7F80u) {  // a NaN / inf value: flag its keys (domain error for rows that see them)
+        uint32_t m = (mx >> (16 * hh)) & 0xFFFFu;
+        if (m >= 0x7F80u) {
+          // a NaN / inf value: flag its keys (domain error for the rows that see them) and take the
+          // channel maximum over the finite values (the rows that do not see it use them)
+          m = 0;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj)
-            if (((vw32[jj] >> (16 * hh)) & 0x7F80u) == 0x7F80u) atomicOr(&S.kbad[32 * kq + jj], 1);
+          for (int jj = 0; jj < 32; ++jj) {
+            const uint32_t e = (vw32[jj] >> (16 * hh)) & 0x7FFFu;
+            if (e >= 0x7F80u) atomicOr(&S.kbad[32 * kq + jj], 1);
+            else m = max(m, e);
+          }
         }
-        S.ve4[kq][2 * cp + hh] = (m == 0 || m >= 0x7F80u) ? INT32_MIN : lead_of_bits(m) + 1;
+        S.ve4[kq][2 * cp + hh] = m == 0 ? INT32_MIN : lead_of_bits(m) + 1;
       }
     }
     __syncthreads();
@@ -409,31 +481,48 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         const int cc = 2 * cp + hh;
         const int ve = S.ve[cc];
         const int lsb = ve == INT32_MIN ? 0 : ve - FV;
+        const int ebase = lsb + 134;
+        const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
+        const bool fast = ve == INT32_MIN || (ebase >= 1 && mn + 1 >= ((uint32_t)ebase << 7));
         uint32_t lossy = 0;
+        uint32_t x[32];
+        if (ve == INT32_MIN) {
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t x[16];
+          for (int jj = 0; jj < 32; ++jj) x[jj] = 0u;
+        } else if (fast) {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const uint32_t b = (vw32[16 * half + jj] >> (16 * hh)) & 0xFFFFu;
+          for (int jj = 0; jj < 32; ++jj) x[jj] = hh ? fix_hi(vw32[jj], ebase) : fix_lo(vw32[jj], ebase);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
             int lost = 0, bad = 0;
-            x[jj] = ve == INT32_MIN ? 0u : (uint32_t)fixq(b, lsb, lost, bad);
-            lossy |= (uint32_t)(lost != 0) << (16 * half + jj);
+            x[jj] = (uint32_t)fixq(b, lsb, lost, bad);
+            lossy |= (uint32_t)(lost != 0) << jj;
             if (lost) {
               int lost2 = 0;
               const int32_t dx = lost_part24(b, lsb, lost2);
               const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
               if (k < VLCAP) {
-                S.vl_k[cc][k] = (uint32_t)(32 * kq + 16 * half + jj) | ((uint32_t)lost2 << 8);
+                S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
                 S.vl_dx[cc][k] = dx;
               }
             }
           }
-          uint4 pl[NV];
-          planes16<NV>(x, pl);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 2; ++q4) {
+          uint32_t pw[NV][4];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t p3;
+            transpose4(x[16 * q4 + 4 * c4], x[16 * q4 + 4 * c4 + 1], x[16 * q4 + 4 * c4 + 2], x[16 * q4 + 4 * c4 + 3],
+                       pw[0][c4], pw[1][c4], pw[2][c4], p3);
+          }
 #pragma unroll
           for (int p = 0; p < NV; ++p)
-            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(cc, 32 * kq + 16 * half, BK)) = pl[p];
+            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(cc, 32 * kq + 16 * q4, BK)) =
+                make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
         }
         S.vlmask[cc][kq] = lossy;
       }

@@ -123,6 +123,7 @@ def test_decode_nan_and_empty_rows():
     K, V = bf16(rng, (2 * L, 128)), bf16(rng, (2 * L, 128))
     Q = bf16(rng, (5, 128))
     V[300, 17] = 0x7FC0
+    V[299, 17] = 0x4280  # 64.0 next to it: the channel's range must come from the finite values
     kb = np.array([0, 0, 0, L, L], np.int64)
     kl = np.array([L, 300, 0, L, 250], np.int64)
     seg = np.full((3, 8), -1, np.int32)
