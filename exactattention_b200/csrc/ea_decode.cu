@@ -179,12 +179,12 @@ __device__ __forceinline__ uint32_t shl_clamp(uint32_t x, uint32_t s) {
 // ebase >= 1 (the negative amount clamps the shift).
 __device__ __forceinline__ uint32_t fix_lo(uint32_t w, int ebase) {
   const uint32_t mag = shl_clamp((w & 0x7Fu) | 0x80u, ((w >> 7) & 0xFFu) - (uint32_t)ebase);
-  const uint32_t sg = __byte_perm(w, 0u, 0x9999);  // bit 15 replicated
+  const uint32_t sg = (uint32_t)((int32_t)(w << 16) >> 31);  // bit 15 replicated
   return (mag ^ sg) - sg;
 }
 __device__ __forceinline__ uint32_t fix_hi(uint32_t w, int ebase) {
   const uint32_t mag = shl_clamp(((w >> 16) & 0x7Fu) | 0x80u, ((w >> 23) & 0xFFu) - (uint32_t)ebase);
-  const uint32_t sg = __byte_perm(w, 0u, 0xBBBB);  // bit 31 replicated
+  const uint32_t sg = (uint32_t)((int32_t)w >> 31);  // bit 31 replicated
   return (mag ^ sg) - sg;
 }
 // per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
