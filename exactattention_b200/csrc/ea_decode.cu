@@ -65,11 +65,11 @@ struct Small {
   int32_t klsb[BK];
   int32_t kbad[BK];
   uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
-  // per channel, up to VLCAP values that lost bits, with their lost parts (units
-  // 2^(lsb_c - 24)), added back exactly in the drain: (key | still-lossy << 8), part
+  // per channel, up to VLCAP values below the V window (their fast-path digits are 0), with their
+  // values in units 2^(lsb_c - 24), added back exactly in the drain: (key | still-lossy << 8), value
   uint32_t vl_n[DV];
   uint32_t vl_k[DV][4];
-  int32_t vl_dx[DV][4];
+  int64_t vl_dx[DV][4];
   int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
   int32_t ve4[4][DV];  // per key quarter maxima of the current tile
   int32_t rows[GD];
@@ -147,25 +147,23 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
 }
 
-// The part of bf16 `bits` that fixq(bits, lsb) truncated away (toward zero), in units
-// 2^(lsb - 24), itself truncated toward zero; `lost2` when bits remain below that unit.
-__device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost2) {
+// bf16 `bits` in units 2^(lsb - 24), truncated toward zero (|value| < 2^(lsb + 8) here, so the
+// result is below 2^32); `lost2` when nonzero bits remain below that unit.
+__device__ __forceinline__ int64_t value24(uint32_t bits, int lsb, int& lost2) {
   int32_t m, e;
   decode_bf16(bits, m, e);
   lost2 = 0;
   const uint32_t mag = (uint32_t)(m < 0 ? -m : m);
-  const int s = lsb - e;  // fixq kept mag >> s
-  if (s <= 0) return 0;
-  const uint32_t low = s >= 31 ? mag : (mag & ((1u << s) - 1));  // units 2^e, < 2^9
-  uint32_t dx;
-  if (s <= 24) {
-    dx = low << (24 - s);
+  const int sh = e - (lsb - 24);
+  uint64_t x;
+  if (sh >= 0) {
+    x = (uint64_t)mag << sh;
   } else {
-    const int r = s - 24;
-    dx = r >= 32 ? 0u : (low >> r);
-    lost2 = r >= 32 ? (low != 0) : ((dx << r) != low);
+    const int r = -sh;
+    x = r >= 32 ? 0u : (mag >> r);
+    lost2 = r >= 32 ? (mag != 0) : ((x << r) != mag);
   }
-  return m < 0 ? -(int32_t)dx : (int32_t)dx;
+  return m < 0 ? -(int64_t)x : (int64_t)x;
 }
 
 // shift that gives 0 for amounts of 32 or more (PTX shl clamps the amount)
@@ -175,8 +173,8 @@ __device__ __forceinline__ uint32_t shl_clamp(uint32_t x, uint32_t s) {
   return r;
 }
 // Fixed point of the low / high bf16 of word w against ebase = lsb + 134: sign (frac | 0x80) <<
-// (E - ebase). Equal to fixq for a normal element with E >= ebase, and 0 for a zero element when
-// ebase >= 1 (the negative amount clamps the shift).
+// (E - ebase). Equal to fixq for a normal element with E >= ebase, and 0 for a zero element or
+// one below the window (E < ebase) when ebase >= 1 (the negative amount clamps the shift).
 __device__ __forceinline__ uint32_t fix_lo(uint32_t w, int ebase) {
   const uint32_t mag = shl_clamp((w & 0x7Fu) | 0x80u, ((w >> 7) & 0xFFu) - (uint32_t)ebase);
   const uint32_t sg = (uint32_t)((int32_t)(w << 16) >> 31);  // bit 15 replicated
@@ -434,8 +432,27 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
     }
     if (tid < DV) S.vl_n[tid] = 0;
+    tc::fence_async_smem();
     __syncthreads();  // kbad is reset above before the value checks below set it
     EA_PT(1)
+    // the score MMAs run on the tensor cores while the V tile is sliced
+    // ---------------- score MMAs: 4 key digits x (N = 32: row digits) ----------------
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
+      const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
+#pragma unroll 1
+      for (int t = 0; t < NK; ++t) {
+        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
+        for (int ks = 0; ks < D / 32; ++ks) {
+          const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
+          const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
+          tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar_mma));
+    }
+    mma_pending = true;
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
     uint32_t vw32[32];
@@ -483,25 +500,26 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         const int lsb = ve == INT32_MIN ? 0 : ve - FV;
         const int ebase = lsb + 134;
         const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
-        const bool fast = ve == INT32_MIN || (ebase >= 1 && mn + 1 >= ((uint32_t)ebase << 7));
         uint32_t lossy = 0;
         uint32_t x[32];
         if (ve == INT32_MIN) {
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) x[jj] = 0u;
-        } else if (fast) {
+        } else if (ebase >= 1) {
+          // fast digits for every value; the values below the window (their digits come out 0)
+          // go to the channel's correction list
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) x[jj] = hh ? fix_hi(vw32[jj], ebase) : fix_lo(vw32[jj], ebase);
-        } else {
+          const uint32_t thr = (uint32_t)ebase << 7;
+          if (mn + 1 < thr) {
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
-            int lost = 0, bad = 0;
-            x[jj] = (uint32_t)fixq(b, lsb, lost, bad);
-            lossy |= (uint32_t)(lost != 0) << jj;
-            if (lost) {
+            for (int jj = 0; jj < 32; ++jj) {
+              const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
+              const uint32_t mg = b & 0x7FFFu;
+              if (mg == 0 || mg >= thr) continue;
+              lossy |= 1u << jj;
               int lost2 = 0;
-              const int32_t dx = lost_part24(b, lsb, lost2);
+              const int64_t dx = value24(b, lsb, lost2);
               const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
               if (k < VLCAP) {
                 S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
@@ -509,6 +527,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
               }
             }
           }
+        } else {
+          // a channel maximum near the bottom of the bf16 range: generic digits; whatever they
+          // lose is below 2^(lsb), bounded per value by the fallback bound
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
+            int lost = 0, bad = 0;
+            x[jj] = (uint32_t)fixq(b, lsb, lost, bad);
+            lossy |= (uint32_t)(lost != 0) << jj;
+          }
+          atomicAdd(&S.vl_n[cc], VLCAP + 1);  // use the bound for this channel
         }
 #pragma unroll
         for (int q4 = 0; q4 < 2; ++q4) {
@@ -539,23 +568,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
     }
 
-    // ---------------- score MMAs: 4 key digits x (N = 32: row digits) ----------------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
-      const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
-#pragma unroll 1
-      for (int t = 0; t < NK; ++t) {
-        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
-        for (int ks = 0; ks < D / 32; ++ks) {
-          const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
-          const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
-          tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
-        }
-      }
-      tc::mma_commit(tc::smem_u32(&S.bar_mma));
-    }
-    mma_pending = true;
     {
       const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
       if (!__syncthreads_and(okw)) {
@@ -758,9 +770,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int sb = (Rt - FW - FV) - (Rn - FN);
       sh_base[i] = sb;
       Nerr[i] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
-      // values that lost bits in the V window: their lost parts times the weights, added exactly
-      // up to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W
-      // units times one V unit per lossy key
+      // values below the V window: their values times the weights, added exactly up to a floor
+      // (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units times
+      // 2^8 V units per such value
       const uint32_t nl = S.vl_n[c];
       if (nl <= VLCAP) {
         i128 corr = 0;
@@ -772,7 +784,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           uint64_t W = 0;
 #pragma unroll
           for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);
+          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);  // |W dx| < 2^80
           cerr += (sb - 24 < 0) ? 1u : 0u;
           if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
         }
@@ -789,7 +801,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
             vw += W + 1;
           }
-        Nerr[i] += scale_ceil128(vw, sb);
+        Nerr[i] += scale_ceil128(vw, sb + 8);  // a listed value is below 2^(lsb + 8): < 2^8 V units
       }
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
