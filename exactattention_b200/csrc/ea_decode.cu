@@ -40,6 +40,7 @@ constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
 constexpr int FW = 48, FV = 23;
 constexpr int THREADS = 256;
 constexpr uint32_t VLCAP = 4;
+constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
 constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
@@ -455,17 +456,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     mma_pending = true;
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
-    uint32_t vw32[32];
+    const uint8_t* vsrc = rawv + (32 * kq) * (DV * 2) + cp * 4;  // word of key 32 kq + jj at jj * 256
+    const int nv = min(32, max(0, nvalid - 32 * kq));             // this thread's valid keys
     uint32_t vmn;  // per channel (half) the smallest nonzero |v| - 1 over this thread's keys
     {
       uint32_t mx = 0;
       vmn = 0xFFFFFFFFu;
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
-        const int key = 32 * kq + jj;
-        vw32[jj] = key < nvalid ? *(const uint32_t*)(rawv + key * (DV * 2) + cp * 4) : 0u;
-        mx = __vmaxu2(mx, vw32[jj] & 0x7FFF7FFFu);
-        vmn = __vminu2(vmn, nz_mag_minus1(vw32[jj]));
+        const uint32_t w = jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u;
+        mx = __vmaxu2(mx, w & 0x7FFF7FFFu);
+        vmn = __vminu2(vmn, nz_mag_minus1(w));
       }
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -474,9 +475,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           // a NaN / inf value: flag its keys (domain error for the rows that see them) and take the
           // channel maximum over the finite values (the rows that do not see it use them)
           m = 0;
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const uint32_t e = (vw32[jj] >> (16 * hh)) & 0x7FFFu;
+#pragma unroll 1
+          for (int jj = 0; jj < nv; ++jj) {
+            const uint32_t e = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0x7FFFu;
             if (e >= 0x7F80u) atomicOr(&S.kbad[32 * kq + jj], 1);
             else m = max(m, e);
           }
@@ -492,66 +493,68 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     __syncthreads();
     EA_PT(2)
     // ---------------- V tile -> digit planes against VE_c ----------------
+    // Fast digits for every value: x = sign (frac | 0x80) << (E - ebase), which is 0 for zeros and
+    // for the values below the window; those go to the channel's correction list (exact) or, past
+    // its capacity, to the bound. A channel whose maximum lies at the very bottom of the bf16 range
+    // (ebase < 1) keeps no digits at all and is bounded.
     {
+      int ebase2[2], lsb2[2];
+      uint32_t keep2[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int cc = 2 * cp + hh;
-        const int ve = S.ve[cc];
-        const int lsb = ve == INT32_MIN ? 0 : ve - FV;
-        const int ebase = lsb + 134;
-        const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
-        uint32_t lossy = 0;
-        uint32_t x[32];
-        if (ve == INT32_MIN) {
+        const int ve = S.ve[2 * cp + hh];
+        lsb2[hh] = ve == INT32_MIN ? 0 : ve - FV;
+        const int eb = lsb2[hh] + 134;
+        ebase2[hh] = ve == INT32_MIN ? 1 : max(eb, 1);
+        keep2[hh] = (ve == INT32_MIN || eb >= 1) ? 0xFFFFFFFFu : 0u;
+      }
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) x[jj] = 0u;
-        } else if (ebase >= 1) {
-          // fast digits for every value; the values below the window (their digits come out 0)
-          // go to the channel's correction list
+      for (int q4 = 0; q4 < 2; ++q4) {
+        uint32_t xa[16], xb[16];
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) x[jj] = hh ? fix_hi(vw32[jj], ebase) : fix_lo(vw32[jj], ebase);
-          const uint32_t thr = (uint32_t)ebase << 7;
-          if (mn + 1 < thr) {
-#pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
-              const uint32_t mg = b & 0x7FFFu;
-              if (mg == 0 || mg >= thr) continue;
-              lossy |= 1u << jj;
-              int lost2 = 0;
-              const int64_t dx = value24(b, lsb, lost2);
-              const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
-              if (k < VLCAP) {
-                S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
-                S.vl_dx[cc][k] = dx;
-              }
-            }
-          }
-        } else {
-          // a channel maximum near the bottom of the bf16 range: generic digits; whatever they
-          // lose is below 2^(lsb), bounded per value by the fallback bound
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const uint32_t b = (vw32[jj] >> (16 * hh)) & 0xFFFFu;
-            int lost = 0, bad = 0;
-            x[jj] = (uint32_t)fixq(b, lsb, lost, bad);
-            lossy |= (uint32_t)(lost != 0) << jj;
-          }
-          atomicAdd(&S.vl_n[cc], VLCAP + 1);  // use the bound for this channel
+        for (int jj = 0; jj < 16; ++jj) {
+          const uint32_t w = (16 * q4 + jj) < nv ? *(const uint32_t*)(vsrc + (16 * q4 + jj) * (DV * 2)) : 0u;
+          xa[jj] = fix_lo(w, ebase2[0]) & keep2[0];
+          xb[jj] = fix_hi(w, ebase2[1]) & keep2[1];
         }
 #pragma unroll
-        for (int q4 = 0; q4 < 2; ++q4) {
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t* x = hh ? xb : xa;
           uint32_t pw[NV][4];
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             uint32_t p3;
-            transpose4(x[16 * q4 + 4 * c4], x[16 * q4 + 4 * c4 + 1], x[16 * q4 + 4 * c4 + 2], x[16 * q4 + 4 * c4 + 3],
-                       pw[0][c4], pw[1][c4], pw[2][c4], p3);
+            transpose4(x[4 * c4], x[4 * c4 + 1], x[4 * c4 + 2], x[4 * c4 + 3], pw[0][c4], pw[1][c4], pw[2][c4], p3);
           }
 #pragma unroll
           for (int p = 0; p < NV; ++p)
-            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(cc, 32 * kq + 16 * q4, BK)) =
+            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(2 * cp + hh, 32 * kq + 16 * q4, BK)) =
                 make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int cc = 2 * cp + hh;
+        const uint32_t thr = keep2[hh] ? ((uint32_t)ebase2[hh] << 7) : 0x8000u;  // all values when bounded
+        const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
+        uint32_t lossy = 0;
+        if (mn + 1 < thr) {
+#pragma unroll 1
+          for (int jj = 0; jj < nv; ++jj) {
+            const uint32_t b = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0xFFFFu;
+            const uint32_t mg = b & 0x7FFFu;
+            if (mg == 0 || mg >= thr) continue;
+            lossy |= 1u << jj;
+            if (!keep2[hh]) continue;
+            int lost2 = 0;
+            const int64_t dx = value24(b, lsb2[hh], lost2);
+            const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
+            if (k < VLCAP) {
+              S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
+              S.vl_dx[cc][k] = dx;
+            }
+          }
+          if (!keep2[hh] && lossy) atomicAdd(&S.vl_n[cc], VL_BOUNDED);  // the whole channel is bounded
         }
         S.vlmask[cc][kq] = lossy;
       }
@@ -801,7 +804,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
             vw += W + 1;
           }
-        Nerr[i] += scale_ceil128(vw, sb + 8);  // a listed value is below 2^(lsb + 8): < 2^8 V units
+        // a value below the window is < 2^(lsb + 8): 2^8 V units; any value is < 2^VE_c: 2^FV units
+        Nerr[i] += scale_ceil128(vw, sb + (nl >= VL_BOUNDED ? FV : 8));
       }
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
