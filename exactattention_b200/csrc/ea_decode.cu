@@ -107,25 +107,35 @@ __device__ __forceinline__ int64_t run_start(const Prob& P, int32_t row0, int64_
   return (page * P.hkv + kvh) * P.page_size + (j % P.page_size);
 }
 
-// warp 0: bulk copies of keys [j0, j0 + n) of K and V into the raw tiles; lane 0 arms the barrier
-__device__ void fetch_tile(const Prob& P, int32_t row0, int64_t j0, int n, uint8_t* rawk, uint8_t* rawv,
-                           uint64_t* bar) {
+// warp 0: bulk copies of keys [j0, j0 + n) of K and V into the raw tiles; lane 0 arms the barrier.
+// RANGE: one contiguous run from `kvbase` (the segment's kv_base, read once per CTA). PAGED: one
+// run per page touched, run r issued by lane r % 32, each lane reading its own page-table entry
+// (or taking it from page_pref, read a tile ahead), so the lookups overlap instead of chaining.
+__device__ void fetch_tile(const Prob& P, int32_t row0, int64_t kvbase, int64_t j0, int n, uint8_t* rawk,
+                           uint8_t* rawv, uint64_t* bar, int64_t page_pref = -1) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) tc::mbar_arrive_expect_tx(bar, (uint32_t)n * 2u * D * 2u);
   __syncwarp();
-  // runs in key order; lane l issues runs l, l + 32, ...
-  int64_t j = 0;
-  int idx = 0;
-  while (j < n) {
-    int64_t run;
-    const int64_t kr = run_start(P, row0, j0 + j, run);
-    const int len = (int)(run < (int64_t)(n - j) ? run : (int64_t)(n - j));
-    if ((idx & 31) == lane) {
-      tc::bulk_g2s(rawk + j * (D * 2), P.k + kr * D, (uint32_t)len * D * 2, bar);
-      tc::bulk_g2s(rawv + j * (DV * 2), P.v + kr * DV, (uint32_t)len * DV * 2, bar);
+  if (P.kind == MASK_RANGE) {
+    if (lane == 0) {
+      tc::bulk_g2s(rawk, P.k + (kvbase + j0) * D, (uint32_t)n * D * 2, bar);
+      tc::bulk_g2s(rawv, P.v + (kvbase + j0) * DV, (uint32_t)n * DV * 2, bar);
     }
-    j += len;
-    ++idx;
+    return;
+  }
+  const int ps = P.page_size;
+  const int64_t b = row0 / P.hq;
+  const int kvh = (int)(row0 - b * P.hq) / P.group;
+  const int64_t p0 = j0 / ps, p1 = (j0 + n - 1) / ps;  // pages touched
+  for (int64_t pg = p0 + lane; pg <= p1; pg += 32) {
+    const int64_t ks = pg == p0 ? j0 : pg * ps;                  // first key of the run
+    const int64_t ke = min((pg + 1) * (int64_t)ps, j0 + n);      // one past its last key
+    // lane l's first page may have been read ahead (page_pref)
+    const int64_t page = (pg == p0 + lane && page_pref >= 0) ? page_pref : P.page_table[b * P.max_pages + pg];
+    const int64_t kr = (page * P.hkv + kvh) * ps + (ks - pg * ps);
+    const uint32_t len = (uint32_t)(ke - ks);
+    tc::bulk_g2s(rawk + (ks - j0) * (D * 2), P.k + kr * D, len * D * 2, bar);
+    tc::bulk_g2s(rawv + (ks - j0) * (DV * 2), P.v + kr * DV, len * DV * 2, bar);
   }
 }
 
@@ -264,7 +274,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   const int64_t maxlen = S.maxlen;
   const int64_t kbeg = maxlen * split / nsplit, kend = maxlen * (split + 1) / nsplit;
   if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
-  if (warp == 0 && kbeg < kend) fetch_tile(P, row0, kbeg, (int)min((int64_t)BK, kend - kbeg), rawk, rawv, &S.bar_raw);
+  const int64_t kvbase = P.kind == MASK_RANGE ? P.kv_base[row0] : 0;
+  if (warp == 0 && kbeg < kend)
+    fetch_tile(P, row0, kvbase, kbeg, (int)min((int64_t)BK, kend - kbeg), rawk, rawv, &S.bar_raw);
 
   // ---------------- query rows -> balanced digit planes (warp g: row g) ----------------
   {
@@ -354,6 +366,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       raw_pending = false;
     }
     EA_PT(0)
+    // warp 0 reads the next tile's page-table entries now; they are used when its fetch is issued
+    int64_t page_pref = -1;
+    if (P.kind == MASK_PAGED && warp == 0 && j0 + BK < kend) {
+      const int64_t pg = (j0 + BK) / P.page_size + lane;
+      const int64_t plast = (min(j0 + 2 * BK, kend) - 1) / P.page_size;
+      if (pg <= plast) page_pref = P.page_table[(int64_t)(row0 / P.hq) * P.max_pages + pg];
+    }
     // ---------------- K tile -> digit planes (16 elements per item, 8 lanes per key) ----------------
     // Fast path (every nonzero element normal and at most W - 8 binades below the key's largest):
     // x = sign (frac | 0x80) << (E - Ebase), zeros through the shift clamp; otherwise fixq with
@@ -567,7 +586,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       raw_pending = true;
       if (warp == 0) {
         tc::fence_async_smem();
-        fetch_tile(P, row0, j0 + BK, (int)min((int64_t)BK, kend - j0 - BK), rawk, rawv, &S.bar_raw);
+        fetch_tile(P, row0, kvbase, j0 + BK, (int)min((int64_t)BK, kend - j0 - BK), rawk, rawv, &S.bar_raw,
+                   page_pref);
       }
     }
 
