@@ -7,7 +7,8 @@
 //            one B tile holding every row's 4 query digit planes (N = 32 = 8 rows x 4 digits).
 //            Query digits are balanced (signed bytes) so one B tile has one signedness.
 //   P.V      O^T[c, (g, w)] = V_u . W_w for value digit planes u (A, 128 channels x 128 keys)
-//            against one B tile of every row's 6 weight digit planes (N = 48).
+//            against one B tile of every row's 6 weight digit planes (N = 48); values in a 31-bit
+//            window against the channel's running maximum, 4 digits.
 // Digit products are grouped by digit position on the CUDA cores (int32 sums) and recombined
 // exactly in int64, with the same fixed-point windows, bounds and certification as the prefill
 // kernel. Each CTA takes one (segment, split): the split's 128-key tiles arrive by bulk copies
@@ -36,8 +37,8 @@ __device__ unsigned long long g_phase_cycles[16];
 #endif
 
 constexpr int BK = 128, D = 128, DV = 128, GD = 8;
-constexpr int NQ = 4, NK = 4, NW = 6, NV = 3;
-constexpr int FW = 48, FV = 23;
+constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
+constexpr int FW = 48, FV = 31;  // V: 31-bit window, 4 digits (few values fall below it)
 constexpr int THREADS = 256;
 constexpr uint32_t VLCAP = 4;
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
@@ -62,7 +63,6 @@ struct Small {
   uint64_t ta[256];
   uint64_t tb[256];
   uint32_t klossy[BK][4];
-  int32_t qfix[GD][D];
   int32_t klsb[BK];
   int32_t kbad[BK];
   uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
@@ -211,6 +211,14 @@ __device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2
   p3 = __byte_perm(b, d, 0x7632);
 }
 
+// q row g's fixed-point element i from its balanced digit planes in the score B tile
+__device__ __forceinline__ int32_t q_fix(const uint8_t* sQ, int g, int i) {
+  int32_t x = 0;
+#pragma unroll
+  for (int t = NQ - 1; t >= 0; --t) x = x * 256 + (int32_t)(int8_t)sQ[tc::kmajor_off(4 * g + t, i, NSQ)];
+  return x;
+}
+
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -299,7 +307,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int i = lane + 32 * m4;
       int lost = 0, b2 = 0;
       const int32_t x = (bad || lead == INT32_MIN) ? 0 : fixq(bits[m4], lsb, lost, b2);
-      S.qfix[g][i] = x;
       const uint32_t lm = __ballot_sync(0xffffffffu, lost != 0);
       if (lane == 0) S.qlossy[g][m4] = lm;
       // balanced base-256 digits: x = sum_s d_s 256^s, d_s in [-128, 127] (|x| < 2^28)
@@ -541,10 +548,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           const uint32_t* x = hh ? xb : xa;
           uint32_t pw[NV][4];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t p3;
-            transpose4(x[4 * c4], x[4 * c4 + 1], x[4 * c4 + 2], x[4 * c4 + 3], pw[0][c4], pw[1][c4], pw[2][c4], p3);
-          }
+          for (int c4 = 0; c4 < 4; ++c4)
+            transpose4(x[4 * c4], x[4 * c4 + 1], x[4 * c4 + 2], x[4 * c4 + 3], pw[0][c4], pw[1][c4], pw[2][c4],
+                       pw[3][c4]);
 #pragma unroll
           for (int p = 0; p < NV; ++p)
             *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(2 * cp + hh, 32 * kq + 16 * q4, BK)) =
@@ -644,7 +650,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
                 }
                 for (uint32_t m = kl; m; m &= m - 1) {
                   const int i = 32 * wd + __ffs(m) - 1;
-                  const int32_t qf = S.qfix[g][i];
+                  const int32_t qf = q_fix(sQ, g, i);
                   err += (uint64_t)(qf < 0 ? -qf : qf);
                 }
               }
@@ -848,26 +854,29 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     for (int i = 0; i < GD / 2; ++i) {
       const int g = h + 2 * i;
       if (g >= nrows) break;  // uniform across the warp
-      uint32_t d0[8], d1[8], d2[8];
+      uint32_t d0[8], d1[8], d2[8], d3[8];
       tc::tmem_ld8(tlane + COL_O + 6 * g, d0);
       tc::tmem_ld8(tlane + COL_O + NSW + 6 * g, d1);
       tc::tmem_ld8(tlane + COL_O + 2 * NSW + 6 * g, d2);
+      tc::tmem_ld8(tlane + COL_O + 3 * NSW + 6 * g, d3);
       tc::tmem_wait_ld();
       if (sh_base[i] == INT32_MIN) continue;
+      // |D_u[w]| < 128 keys x 255 x 255 < 2^23, so each group (<= 4 terms) fits int32
       const int32_t s0 = (int32_t)d0[0];
       const int32_t s1 = (int32_t)d0[1] + (int32_t)d1[0];
       const int32_t s2 = (int32_t)d0[2] + (int32_t)d1[1] + (int32_t)d2[0];
-      const int32_t s3 = (int32_t)d0[3] + (int32_t)d1[2] + (int32_t)d2[1];
-      const int32_t s4 = (int32_t)d0[4] + (int32_t)d1[3] + (int32_t)d2[2];
-      const int32_t s5 = (int32_t)d0[5] + (int32_t)d1[4] + (int32_t)d2[3];
-      const int32_t s6 = (int32_t)d1[5] + (int32_t)d2[4];
-      const int32_t s7 = (int32_t)d2[5];
+      const int32_t s3 = (int32_t)d0[3] + (int32_t)d1[2] + (int32_t)d2[1] + (int32_t)d3[0];
+      const int32_t s4 = (int32_t)d0[4] + (int32_t)d1[3] + (int32_t)d2[2] + (int32_t)d3[1];
+      const int32_t s5 = (int32_t)d0[5] + (int32_t)d1[4] + (int32_t)d2[3] + (int32_t)d3[2];
+      const int32_t s6 = (int32_t)d1[5] + (int32_t)d2[4] + (int32_t)d3[3];
+      const int32_t s7 = (int32_t)d2[5] + (int32_t)d3[4];
+      const int32_t s8 = (int32_t)d3[5];
       const uint32_t r0[3] = {(uint32_t)s0, (uint32_t)s1, (uint32_t)s2};
       const uint32_t r1[3] = {(uint32_t)s3, (uint32_t)s4, (uint32_t)s5};
-      const uint32_t r2[2] = {(uint32_t)s6, (uint32_t)s7};
+      const uint32_t r2[3] = {(uint32_t)s6, (uint32_t)s7, (uint32_t)s8};
       const int sb = sh_base[i];
       N[i] += shift_floor128(recomb<3>(r0), sb) + shift_floor128(recomb<3>(r1), 24 + sb) +
-              shift_floor128(recomb<2>(r2), 48 + sb);
+              shift_floor128(recomb<3>(r2), 48 + sb);
     }
     tc::fence_before_sync();
     __syncthreads();
