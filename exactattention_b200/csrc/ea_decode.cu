@@ -16,8 +16,8 @@
 // slicing. Every CTA writes its rows' split partials; the split combine merges them (any split
 // count gives the same bits) and sends uncertified rows to tier 3.
 //
-// Thread roles (256 threads): slicing uses all threads; TMEM lane quadrant = warp % 4, and the
-// two warpgroups take alternate rows (pass 1 / pass 2: lane = key; drain: lane = channel).
+// Thread roles (512 threads): slicing uses all threads; TMEM lane quadrant = warp % 4, and the
+// four warpgroups take rows g = warpgroup + 4 i (pass 1 / pass 2: lane = key; drain: lane = channel).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -39,7 +39,8 @@ __device__ unsigned long long g_phase_cycles[16];
 constexpr int BK = 128, D = 128, DV = 128, GD = 8;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
 constexpr int FW = 48, FV = 31;  // V: 31-bit window, 4 digits (few values fall below it)
-constexpr int THREADS = 256;
+constexpr int THREADS = 512, NWG = THREADS / 128;  // NWG warpgroups share the TMEM lane quadrants
+constexpr int RPT = GD / NWG;                       // row slots per thread in the drain role
 constexpr uint32_t VLCAP = 4;
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
 constexpr uint32_t TMEM_COLS = 512;
@@ -72,13 +73,13 @@ struct Small {
   uint32_t vl_k[DV][4];
   int64_t vl_dx[DV][4];
   int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
-  int32_t ve4[4][DV];  // per key quarter maxima of the current tile
+  int32_t ve4[8][DV];  // per key eighth maxima of the current tile
   int32_t rows[GD];
   int32_t len[GD];
   int32_t qlsb[GD];
   int32_t rst[GD];
   uint32_t qlossy[GD][4];
-  int32_t rt[4][GD];
+  int32_t rt[4][GD];  // per lane quadrant
   uint64_t zs[4][GD];
   uint32_t zl[4][GD];
   uint64_t bar_mma;
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     fetch_tile(P, row0, kvbase, kbeg, (int)min((int64_t)BK, kend - kbeg), rawk, rawv, &S.bar_raw);
 
   // ---------------- query rows -> balanced digit planes (warp g: row g) ----------------
-  {
+  if (warp < GD) {
     const int g = warp;
     const int32_t row = S.rows[g];
     uint32_t bits[4];
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   tc::fence_after_sync();
   const uint32_t tmem = S.tmem;
 
-  // ---------------- per-thread running state (drain role: channel c, rows h, h + 2, ..) ----------
+  // ---------------- per-thread running state (drain role: channel c, rows h, h + NWG, ..) --------
   const int h = warp >> 2, c = 32 * (warp & 3) + lane;
   const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
   // Fraction bits of this CTA's Z and N windows: the headroom only has to cover the split's own
@@ -341,13 +342,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   // rather than to max weight x max |v|; the written partial takes the unit that its magnitude
   // allows (below)
   const int FN = FZ + 40;
-  int32_t R[GD / 2];
-  int64_t Z[GD / 2];
-  i128 N[GD / 2];
-  uint64_t Zerr[GD / 2];
-  u128 Nerr[GD / 2];
+  int32_t R[RPT];
+  int64_t Z[RPT];
+  i128 N[RPT];
+  uint64_t Zerr[RPT];
+  u128 Nerr[RPT];
 #pragma unroll
-  for (int i = 0; i < GD / 2; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     R[i] = R_EMPTY;
     Z[i] = 0;
     N[i] = 0;
@@ -380,35 +381,35 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int64_t plast = (min(j0 + 2 * BK, kend) - 1) / P.page_size;
       if (pg <= plast) page_pref = P.page_table[(int64_t)(row0 / P.hq) * P.max_pages + pg];
     }
-    // ---------------- K tile -> digit planes (16 elements per item, 8 lanes per key) ----------------
+    // ---------------- K tile -> digit planes (thread: key tid / 4, dims 32 (tid % 4) ..) ----------------
     // Fast path (every nonzero element normal and at most W - 8 binades below the key's largest):
     // x = sign (frac | 0x80) << (E - Ebase), zeros through the shift clamp; otherwise fixq with
-    // lossy masks. Lanes 4-7 of a key load their two 16-byte halves in swapped order, so the 8
-    // lanes' loads cover the 128 bytes of a bank row without conflicts.
-#pragma unroll 1
-    for (int it = 0; it < 4; ++it) {
-      const int key = 32 * it + (tid >> 3), l8 = tid & 7, hsw = (l8 >> 2) & 1;
+    // lossy masks. Step j reads 16-byte chunk cj = (j + l4 / 2 + 2 (key % 2)) % 4 of the lane's 64
+    // bytes, so the 8 lanes of a load phase (2 keys x 4 lanes) hit 8 distinct bank groups.
+    {
+      const int key = tid >> 2, l4 = tid & 3;
       const bool valid = key < nvalid;
-      uint32_t w[8];
+      const int rot = (l4 >> 1) + 2 * (key & 1);
+      uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = 0u;
-      if (valid) {
-        const uint8_t* src = rawk + key * (D * 2) + l8 * 32;
-        const uint4 a = *(const uint4*)(src + 16 * hsw);
-        const uint4 b = *(const uint4*)(src + 16 * (1 - hsw));
-        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-        w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+      for (int j = 0; j < 4; ++j) {
+        uint4 a = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) a = *(const uint4*)(rawk + key * (D * 2) + l4 * 64 + 16 * ((j + rot) & 3));
+        w[4 * j] = a.x;
+        w[4 * j + 1] = a.y;
+        w[4 * j + 2] = a.z;
+        w[4 * j + 3] = a.w;
       }
       uint32_t mx = 0, mn = 0xFFFFFFFFu;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 16; ++i) {
         mx = __vmaxu2(mx, w[i] & 0x7FFF7FFFu);
         mn = __vminu2(mn, nz_mag_minus1(w[i]));
       }
       mx = max(mx & 0xFFFFu, mx >> 16);
       mn = min(mn & 0xFFFFu, mn >> 16);
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
+      for (int o = 1; o < 4; o <<= 1) {
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
       }
@@ -417,48 +418,49 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
       const int ebase = lsb + 134;  // x = (frac | 0x80) << (E - ebase) for a normal element
       const bool fast = lead == INT32_MIN || (ebase >= 1 && mn + 1 >= ((uint32_t)ebase << 7));
-      uint32_t xs[16];
-      uint32_t lm = 0;
-      if (lead == INT32_MIN) {
+      uint32_t lm = 0;  // lossy elements, bit = dim - 32 l4
 #pragma unroll
-        for (int e = 0; e < 16; ++e) xs[e] = 0u;
-      } else if (fast) {
+      for (int j = 0; j < 4; ++j) {
+        const int cj = (j + rot) & 3;
+        uint32_t xs[8];
+        if (lead == INT32_MIN) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          xs[2 * i] = fix_lo(w[i], ebase);
-          xs[2 * i + 1] = fix_hi(w[i], ebase);
+          for (int e = 0; e < 8; ++e) xs[e] = 0u;
+        } else if (fast) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            xs[2 * i] = fix_lo(w[4 * j + i], ebase);
+            xs[2 * i + 1] = fix_hi(w[4 * j + i], ebase);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t b = (w[4 * j + (e >> 1)] >> (16 * (e & 1))) & 0xFFFFu;
+            int lost = 0, b2 = 0;
+            xs[e] = (uint32_t)fixq(b, lsb, lost, b2);
+            lm |= (uint32_t)(lost != 0) << (8 * cj + e);
+          }
         }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const uint32_t b = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-          int lost = 0, b2 = 0;
-          xs[e] = (uint32_t)fixq(b, lsb, lost, b2);
-          lm |= (uint32_t)(lost != 0) << e;
-        }
-      }
-      // elements 0-7 are dims 16 l8 + 8 hsw .., elements 8-15 the other half
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
         uint32_t p0a, p1a, p2a, p3a, p0b, p1b, p2b, p3b;
-        transpose4(xs[8 * hf], xs[8 * hf + 1], xs[8 * hf + 2], xs[8 * hf + 3], p0a, p1a, p2a, p3a);
-        transpose4(xs[8 * hf + 4], xs[8 * hf + 5], xs[8 * hf + 6], xs[8 * hf + 7], p0b, p1b, p2b, p3b);
-        const uint32_t off = tc::kmajor_off(key, 16 * l8 + 8 * (hf ^ hsw), BK);
+        transpose4(xs[0], xs[1], xs[2], xs[3], p0a, p1a, p2a, p3a);
+        transpose4(xs[4], xs[5], xs[6], xs[7], p0b, p1b, p2b, p3b);
+        const uint32_t off = tc::kmajor_off(key, 32 * l4 + 8 * cj, BK);
         *(uint2*)(sK + 0 * K_PLANE + off) = make_uint2(p0a, p0b);
         *(uint2*)(sK + 1 * K_PLANE + off) = make_uint2(p1a, p1b);
         *(uint2*)(sK + 2 * K_PLANE + off) = make_uint2(p2a, p2b);
         *(uint2*)(sK + 3 * K_PLANE + off) = make_uint2(p3a, p3b);
       }
-      // lossy mask in dim order: this lane's 16 dims, then 32 dims (2 lanes) per word
-      const uint32_t lm16 = hsw ? ((lm >> 8) | ((lm & 0xFFu) << 8)) : lm;
-      const uint32_t lw = (lm16 << (16 * (l8 & 1))) | (__shfl_xor_sync(0xffffffffu, lm16, 1) << (16 * (1 - (l8 & 1))));
-      if ((l8 & 1) == 0) S.klossy[key][l8 >> 1] = lw;
-      if (l8 == 0) {
+      S.klossy[key][l4] = lm;
+      if (l4 == 0) {
         S.klsb[key] = lsb;
         S.kbad[key] = valid && bad;
       }
     }
-    if (tid < DV) S.vl_n[tid] = 0;
+    if (tid < DV) {
+      S.vl_n[tid] = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) S.vlmask[tid][q] = 0;
+    }
     tc::fence_async_smem();
     __syncthreads();  // kbad is reset above before the value checks below set it
     EA_PT(1)
@@ -480,16 +482,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       tc::mma_commit(tc::smem_u32(&S.bar_mma));
     }
     mma_pending = true;
-    // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 32 kq ..) ------
+    // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 16 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
-    const uint8_t* vsrc = rawv + (32 * kq) * (DV * 2) + cp * 4;  // word of key 32 kq + jj at jj * 256
-    const int nv = min(32, max(0, nvalid - 32 * kq));             // this thread's valid keys
+    const uint8_t* vsrc = rawv + (16 * kq) * (DV * 2) + cp * 4;  // word of key 16 kq + jj at jj * 256
+    const int nv = min(16, max(0, nvalid - 16 * kq));             // this thread's valid keys
     uint32_t vmn;  // per channel (half) the smallest nonzero |v| - 1 over this thread's keys
     {
       uint32_t mx = 0;
       vmn = 0xFFFFFFFFu;
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
+      for (int jj = 0; jj < 16; ++jj) {
         const uint32_t w = jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u;
         mx = __vmaxu2(mx, w & 0x7FFF7FFFu);
         vmn = __vminu2(vmn, nz_mag_minus1(w));
@@ -504,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 #pragma unroll 1
           for (int jj = 0; jj < nv; ++jj) {
             const uint32_t e = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0x7FFFu;
-            if (e >= 0x7F80u) atomicOr(&S.kbad[32 * kq + jj], 1);
+            if (e >= 0x7F80u) atomicOr(&S.kbad[16 * kq + jj], 1);
             else m = max(m, e);
           }
         }
@@ -513,7 +515,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     __syncthreads();
     if (tid < DV) {
-      const int vt = max(max(S.ve4[0][tid], S.ve4[1][tid]), max(S.ve4[2][tid], S.ve4[3][tid]));
+      int vt = S.ve4[0][tid];
+#pragma unroll
+      for (int q = 1; q < 8; ++q) vt = max(vt, S.ve4[q][tid]);
       S.ve[tid] = max(S.ve[tid], vt);
     }
     __syncthreads();
@@ -534,12 +538,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         ebase2[hh] = ve == INT32_MIN ? 1 : max(eb, 1);
         keep2[hh] = (ve == INT32_MIN || eb >= 1) ? 0xFFFFFFFFu : 0u;
       }
-#pragma unroll
-      for (int q4 = 0; q4 < 2; ++q4) {
+      {
         uint32_t xa[16], xb[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
-          const uint32_t w = (16 * q4 + jj) < nv ? *(const uint32_t*)(vsrc + (16 * q4 + jj) * (DV * 2)) : 0u;
+          const uint32_t w = jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u;
           xa[jj] = fix_lo(w, ebase2[0]) & keep2[0];
           xb[jj] = fix_hi(w, ebase2[1]) & keep2[1];
         }
@@ -553,7 +556,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
                        pw[3][c4]);
 #pragma unroll
           for (int p = 0; p < NV; ++p)
-            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(2 * cp + hh, 32 * kq + 16 * q4, BK)) =
+            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(2 * cp + hh, 16 * kq, BK)) =
                 make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
         }
       }
@@ -575,13 +578,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             const int64_t dx = value24(b, lsb2[hh], lost2);
             const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
             if (k < VLCAP) {
-              S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
+              S.vl_k[cc][k] = (uint32_t)(16 * kq + jj) | ((uint32_t)lost2 << 8);
               S.vl_dx[cc][k] = dx;
             }
           }
           if (!keep2[hh] && lossy) atomicAdd(&S.vl_n[cc], VL_BOUNDED);  // the whole channel is bounded
         }
-        S.vlmask[cc][kq] = lossy;
+        if (lossy) atomicOr(&S.vlmask[cc][kq >> 1], lossy << (16 * (kq & 1)));
       }
     }
     tc::fence_async_smem();
@@ -609,12 +612,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     tc::fence_after_sync();
     EA_PT(4)
 
-    // ---------------- pass 1: certified logits (lane: key; rows h, h + 2, ..) ----------------
+    // ---------------- pass 1: certified logits (lane: key; rows h, h + NWG, ..) ----------------
     {
       const int key = c;
       const bool klossy = (S.klossy[key][0] | S.klossy[key][1] | S.klossy[key][2] | S.klossy[key][3]) != 0;
 #pragma unroll 1
-      for (int g = h; g < nrows; g += 2) {
+      for (int g = h; g < nrows; g += NWG) {
         uint32_t dg[NK][4];
 #pragma unroll
         for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + 32 * t + 4 * g, dg[t]);
@@ -697,7 +700,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     EA_PT(6)
     // ---------------- pass 2: tile bounds, weights, W digits ----------------
 #pragma unroll 1
-    for (int g = h; g < nrows; g += 2) {
+    for (int g = h; g < nrows; g += NWG) {
       const uint32_t tb = sT[g * BK + c];
       const float tf = __uint_as_float(tb);
       int32_t rl = INT32_MIN;
@@ -707,7 +710,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     __syncthreads();
 #pragma unroll 1
-    for (int g = h; g < nrows; g += 2) {
+    for (int g = h; g < nrows; g += NWG) {
       const int key = c;
       const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
       const uint32_t tb = sT[g * BK + key];
@@ -767,10 +770,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     // meanwhile: this channel's exponent change, the rows' merges and bounds (registers only)
     const int ve_now = S.ve[c];
-    int sh_base[GD / 2];
+    int sh_base[RPT];
 #pragma unroll
-    for (int i = 0; i < GD / 2; ++i) {
-      const int g = h + 2 * i;
+    for (int i = 0; i < RPT; ++i) {
+      const int g = h + NWG * i;
       sh_base[i] = INT32_MIN;
       if (g >= nrows) continue;
       if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
@@ -851,8 +854,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     EA_PT(9)
     // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
 #pragma unroll
-    for (int i = 0; i < GD / 2; ++i) {
-      const int g = h + 2 * i;
+    for (int i = 0; i < RPT; ++i) {
+      const int g = h + NWG * i;
       if (g >= nrows) break;  // uniform across the warp
       uint32_t d0[8], d1[8], d2[8], d3[8];
       tc::tmem_ld8(tlane + COL_O + 6 * g, d0);
@@ -892,8 +895,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   __syncthreads();
   const int64_t rows = P.rows;
 #pragma unroll
-  for (int i = 0; i < GD / 2; ++i) {
-    const int g = h + 2 * i;
+  for (int i = 0; i < RPT; ++i) {
+    const int g = h + NWG * i;
     if (g >= nrows) break;
     const int32_t row = S.rows[g];
     if (row < 0) continue;
