@@ -72,8 +72,9 @@ struct Small {
   uint32_t vl_n[DV];
   uint32_t vl_k[DV][4];
   int64_t vl_dx[DV][4];
-  int32_t ve[DV];      // running channel exponent VE_c: |v| < 2^VE_c over the keys so far
-  int32_t ve4[8][DV];  // per key eighth maxima of the current tile
+  int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
+  int32_t vbad[BK];    // a NaN / inf value in the key's V row
+  int16_t ve4[8][DV];  // per key eighth maxima of the current tile (INT16_MIN: none)
   int32_t rows[GD];
   int32_t len[GD];
   int32_t qlsb[GD];
@@ -257,7 +258,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     S.ta[i] = g_ta64[i];
     S.tb[i] = g_tb64[i];
   }
-  for (int i = tid; i < DV; i += THREADS) S.ve[i] = INT32_MIN;
+  for (int i = tid; i < DV; i += THREADS) S.ve[0][i] = S.ve[1][i] = INT32_MIN;
+  for (int i = tid; i < BK; i += THREADS) S.vbad[i] = 0;
   for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
   if (tid == 0) {
     tc::mbar_init(&S.bar_mma, 1);
@@ -362,17 +364,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   unsigned n_exact = 0, n_wide = 0;
 
   EA_PT_INIT
-  for (int64_t j0 = kbeg; j0 < kend; j0 += BK) {
+  int par = 0;  // tile parity: S.ve[par] receives this tile's channel exponents
+  for (int64_t j0 = kbeg; j0 < kend; j0 += BK, par ^= 1) {
     const int nvalid = (int)min((int64_t)BK, kend - j0);
-    {
-      const bool okw = tc::mbar_wait(&S.bar_raw, ph_raw);
-      if (!__syncthreads_and(okw)) {
-        ok_wait = false;
-        break;
-      }
-      ph_raw ^= 1;
-      raw_pending = false;
-    }
+    // Each thread waits for the raw tile; the block vote rides on the barrier after the slicing
+    // (after a wait that gave up, the slicing reads stale shared memory and the vote drops it).
+    // Five block barriers per tile: after the slicing (A), after the score MMAs (B), after pass 1
+    // (C), after the weights (E) and after the drain (F).
+    const bool ok_raw = tc::mbar_wait(&S.bar_raw, ph_raw);
     EA_PT(0)
     // warp 0 reads the next tile's page-table entries now; they are used when its fetch is issued
     int64_t page_pref = -1;
@@ -456,32 +455,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         S.kbad[key] = valid && bad;
       }
     }
-    if (tid < DV) {
-      S.vl_n[tid] = 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) S.vlmask[tid][q] = 0;
-    }
-    tc::fence_async_smem();
-    __syncthreads();  // kbad is reset above before the value checks below set it
-    EA_PT(1)
-    // the score MMAs run on the tensor cores while the V tile is sliced
-    // ---------------- score MMAs: 4 key digits x (N = 32: row digits) ----------------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
-      const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
-#pragma unroll 1
-      for (int t = 0; t < NK; ++t) {
-        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
-        for (int ks = 0; ks < D / 32; ++ks) {
-          const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
-          const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
-          tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
-        }
-      }
-      tc::mma_commit(tc::smem_u32(&S.bar_mma));
-    }
-    mma_pending = true;
     // ---------------- V tile: channel maxima (thread: channels 2 cp, 2 cp + 1; keys 16 kq ..) ------
     const int cp = tid & 63, kq = tid >> 6;
     const uint8_t* vsrc = rawv + (16 * kq) * (DV * 2) + cp * 4;  // word of key 16 kq + jj at jj * 256
@@ -506,22 +479,44 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 #pragma unroll 1
           for (int jj = 0; jj < nv; ++jj) {
             const uint32_t e = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0x7FFFu;
-            if (e >= 0x7F80u) atomicOr(&S.kbad[16 * kq + jj], 1);
+            if (e >= 0x7F80u) atomicOr(&S.vbad[16 * kq + jj], 1);
             else m = max(m, e);
           }
         }
-        S.ve4[kq][2 * cp + hh] = m == 0 ? INT32_MIN : lead_of_bits(m) + 1;
+        S.ve4[kq][2 * cp + hh] = (int16_t)(m == 0 ? INT16_MIN : lead_of_bits(m) + 1);
       }
     }
-    __syncthreads();
     if (tid < DV) {
-      int vt = S.ve4[0][tid];
+      S.vl_n[tid] = 0;
 #pragma unroll
-      for (int q = 1; q < 8; ++q) vt = max(vt, S.ve4[q][tid]);
-      S.ve[tid] = max(S.ve[tid], vt);
+      for (int q = 0; q < 4; ++q) S.vlmask[tid][q] = 0;
     }
-    __syncthreads();
-    EA_PT(2)
+    tc::fence_async_smem();
+    if (!__syncthreads_and(ok_raw)) {  // barrier A
+      ok_wait = false;
+      break;
+    }
+    ph_raw ^= 1;
+    raw_pending = false;
+    EA_PT(1)
+    // the score MMAs run on the tensor cores while the V tile is sliced
+    // ---------------- score MMAs: 4 key digits x (N = 32: row digits) ----------------
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
+      const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
+#pragma unroll 1
+      for (int t = 0; t < NK; ++t) {
+        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
+        for (int ks = 0; ks < D / 32; ++ks) {
+          const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
+          const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
+          tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar_mma));
+    }
+    mma_pending = true;
     // ---------------- V tile -> digit planes against VE_c ----------------
     // Fast digits for every value: x = sign (frac | 0x80) << (E - ebase), which is 0 for zeros and
     // for the values below the window; those go to the channel's correction list (exact) or, past
@@ -532,7 +527,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       uint32_t keep2[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int ve = S.ve[2 * cp + hh];
+        // running channel exponent: the previous tiles' and this tile's key eighths
+        int ve = S.ve[par ^ 1][2 * cp + hh];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (S.ve4[q][2 * cp + hh] != INT16_MIN) ve = max(ve, (int)S.ve4[q][2 * cp + hh]);
+        if (kq == 0) S.ve[par][2 * cp + hh] = ve;
         lsb2[hh] = ve == INT32_MIN ? 0 : ve - FV;
         const int eb = lsb2[hh] + 134;
         ebase2[hh] = ve == INT32_MIN ? 1 : max(eb, 1);
@@ -587,9 +587,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         if (lossy) atomicOr(&S.vlmask[cc][kq >> 1], lossy << (16 * (kq & 1)));
       }
     }
-    tc::fence_async_smem();
-    __syncthreads();
-    EA_PT(3)
+    {
+      const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);  // the score MMAs, issued before the V slicing
+      tc::fence_async_smem();
+      if (!__syncthreads_and(okw)) {  // barrier B
+        ok_wait = false;
+        break;
+      }
+      ph_mma ^= 1;
+      mma_pending = false;
+    }
+    tc::fence_after_sync();
+    EA_PT(2)
     // the raw tiles are consumed: bring in the next tile while this one is processed
     if (j0 + BK < kend) {
       raw_pending = true;
@@ -600,22 +609,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
     }
 
-    {
-      const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
-      if (!__syncthreads_and(okw)) {
-        ok_wait = false;
-        break;
-      }
-      ph_mma ^= 1;
-      mma_pending = false;
-    }
-    tc::fence_after_sync();
-    EA_PT(4)
 
     // ---------------- pass 1: certified logits (lane: key; rows h, h + NWG, ..) ----------------
+    bool unc = false;
     {
       const int key = c;
       const bool klossy = (S.klossy[key][0] | S.klossy[key][1] | S.klossy[key][2] | S.klossy[key][3]) != 0;
+      const bool kbad = S.kbad[key] | S.vbad[key];
 #pragma unroll 1
       for (int g = h; g < nrows; g += NWG) {
         uint32_t dg[NK][4];
@@ -624,7 +624,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         tc::tmem_wait_ld();
         uint32_t out = T_MASKED;
         if (key < nvalid && j0 + key < S.len[g] && S.rows[g] >= 0) {
-          if (S.kbad[key]) {
+          if (kbad) {
             atomicMax(&S.rst[g], ST_DOMAIN);
           } else {
             // digit products (t, s) grouped by t + s: G_k = sum_{t + s = k} dg[t][s]
@@ -667,13 +667,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           }
         }
         sT[g * BK + key] = out;
+        // tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1)
+        const float tf = __uint_as_float(out);
+        int32_t rl = INT32_MIN;
+        if (out != T_MASKED && out != T_UNCERT && fabsf(tf) < 1073741824.0f) rl = __float2int_ru(tf) + 1;
+        rl = __reduce_max_sync(0xffffffffu, rl);
+        if (lane == 0) S.rt[warp & 3][g] = rl;
+        unc |= out == T_UNCERT;
       }
     }
     tc::fence_before_sync();
-    __syncthreads();
-
-    EA_PT(5)
+    const int any_unc = __syncthreads_or(unc);  // barrier C
+    EA_PT(3)
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
+    if (any_unc) {
     for (int e0 = 0; e0 < nrows * BK; e0 += THREADS) {
       const int e = e0 + warp * 32 + lane;
       const uint32_t hit = __ballot_sync(0xffffffffu, e < nrows * BK && sT[e] == T_UNCERT);
@@ -696,9 +703,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
     }
     __syncthreads();
-
-    EA_PT(6)
-    // ---------------- pass 2: tile bounds, weights, W digits ----------------
+    // the tile bounds again, now over the exact logits too
 #pragma unroll 1
     for (int g = h; g < nrows; g += NWG) {
       const uint32_t tb = sT[g * BK + c];
@@ -709,6 +714,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       if (lane == 0) S.rt[warp & 3][g] = rl;
     }
     __syncthreads();
+    }  // any_unc
+    if (tid < BK) S.vbad[tid] = 0;  // read by pass 1 only; set again by the next tile's value checks
+    EA_PT(4)
+    // ---------------- pass 2: weights, W digits ----------------
 #pragma unroll 1
     for (int g = h; g < nrows; g += NWG) {
       const int key = c;
@@ -749,9 +758,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
     }
     tc::fence_async_smem();
-    __syncthreads();
-
-    EA_PT(7)
+    __syncthreads();  // barrier E
+    EA_PT(5)
     // ---------------- P.V MMAs: 3 value digits x (N = 48: row weight digits) ----------------
     if (tid == 0) {
       tc::fence_after_sync();
@@ -769,7 +777,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       tc::mma_commit(tc::smem_u32(&S.bar_mma));
     }
     // meanwhile: this channel's exponent change, the rows' merges and bounds (registers only)
-    const int ve_now = S.ve[c];
+    const int ve_now = S.ve[par][c];
     int sh_base[RPT];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
@@ -839,19 +847,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
     vec = ve_now;
-    EA_PT(8)
+    EA_PT(6)
     mma_pending = true;
-    {
-      const bool okw = tc::mbar_wait(&S.bar_mma, ph_mma);
-      if (!__syncthreads_and(okw)) {
-        ok_wait = false;
-        break;
-      }
-      ph_mma ^= 1;
-      mma_pending = false;
-    }
+    // each thread waits; after a wait that gave up the drain reads stale TMEM and the vote at
+    // barrier F drops the tile
+    const bool ok_pv = tc::mbar_wait(&S.bar_mma, ph_mma);
     tc::fence_after_sync();
-    EA_PT(9)
+    EA_PT(7)
     // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
@@ -882,8 +884,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
               shift_floor128(recomb<3>(r2), 48 + sb);
     }
     tc::fence_before_sync();
-    __syncthreads();
-    EA_PT(10)
+    if (!__syncthreads_and(ok_pv)) {  // barrier F
+      ok_wait = false;
+      break;
+    }
+    ph_mma ^= 1;
+    mma_pending = false;
+    EA_PT(8)
   }
   EA_PT_FLUSH
 
