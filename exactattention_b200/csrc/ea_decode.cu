@@ -67,11 +67,11 @@ struct Small {
   int32_t klsb[BK];
   int32_t kbad[BK];
   uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
-  // per channel, up to VLCAP values below the V window (their fast-path digits are 0), with their
-  // values in units 2^(lsb_c - 24), added back exactly in the drain: (key | still-lossy << 8), value
+  // per channel, up to VLCAP values that lost bits in the V window, with their lost parts (units
+  // 2^(lsb_c - 24)), added back exactly in the drain: (key | still-lossy << 8), part
   uint32_t vl_n[DV];
   uint32_t vl_k[DV][4];
-  int64_t vl_dx[DV][4];
+  int32_t vl_dx[DV][4];
   int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
   int32_t vbad[BK];    // a NaN / inf value in the key's V row
   int16_t ve4[8][DV];  // per key eighth maxima of the current tile (INT16_MIN: none)
@@ -160,23 +160,25 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
 }
 
-// bf16 `bits` in units 2^(lsb - 24), truncated toward zero (|value| < 2^(lsb + 8) here, so the
-// result is below 2^32); `lost2` when nonzero bits remain below that unit.
-__device__ __forceinline__ int64_t value24(uint32_t bits, int lsb, int& lost2) {
+// The part of bf16 `bits` that truncation toward zero to a multiple of 2^lsb dropped, in units
+// 2^(lsb - 24), itself truncated toward zero (< 2^24); `lost2` when bits remain below that unit.
+__device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost2) {
   int32_t m, e;
   decode_bf16(bits, m, e);
   lost2 = 0;
   const uint32_t mag = (uint32_t)(m < 0 ? -m : m);
-  const int sh = e - (lsb - 24);
-  uint64_t x;
-  if (sh >= 0) {
-    x = (uint64_t)mag << sh;
+  const int s = lsb - e;  // the kept part is mag >> s
+  if (s <= 0) return 0;
+  const uint32_t low = s >= 31 ? mag : (mag & ((1u << s) - 1));  // units 2^e, < 2^9
+  uint32_t dx;
+  if (s <= 24) {
+    dx = low << (24 - s);
   } else {
-    const int r = -sh;
-    x = r >= 32 ? 0u : (mag >> r);
-    lost2 = r >= 32 ? (mag != 0) : ((x << r) != mag);
+    const int r = s - 24;
+    dx = r >= 32 ? 0u : (low >> r);
+    lost2 = r >= 32 ? (low != 0) : ((dx << r) != low);
   }
-  return m < 0 ? -(int64_t)x : (int64_t)x;
+  return m < 0 ? -(int32_t)dx : (int32_t)dx;
 }
 
 // shift that gives 0 for amounts of 32 or more (PTX shl clamps the amount)
@@ -197,6 +199,16 @@ __device__ __forceinline__ uint32_t fix_hi(uint32_t w, int ebase) {
   const uint32_t mag = shl_clamp(((w >> 16) & 0x7Fu) | 0x80u, ((w >> 23) & 0xFFu) - (uint32_t)ebase);
   const uint32_t sg = (uint32_t)((int32_t)w >> 31);  // bit 31 replicated
   return (mag ^ sg) - sg;
+}
+// Fixed point of the low / high bf16 of word w at lsb, through fp32: the bf16 is exact in fp32,
+// the scale 2^-lsb is exact (lsb in [-126, 126]), and the conversion truncates toward zero as
+// fixq does; exact whenever |value| / 2^lsb < 2^31.
+__device__ __forceinline__ float scale_of(int lsb) { return __int_as_float((127 - lsb) << 23); }
+__device__ __forceinline__ uint32_t fixf_lo(uint32_t w, float sc) {
+  return (uint32_t)__float2int_rz(__uint_as_float(w << 16) * sc);
+}
+__device__ __forceinline__ uint32_t fixf_hi(uint32_t w, float sc) {
+  return (uint32_t)__float2int_rz(__uint_as_float(w & 0xFFFF0000u) * sc);
 }
 // per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
 __device__ __forceinline__ uint32_t nz_mag_minus1(uint32_t w) {
@@ -381,9 +393,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       if (pg <= plast) page_pref = P.page_table[(int64_t)(row0 / P.hq) * P.max_pages + pg];
     }
     // ---------------- K tile -> digit planes (thread: key tid / 4, dims 32 (tid % 4) ..) ----------------
-    // Fast path (every nonzero element normal and at most W - 8 binades below the key's largest):
-    // x = sign (frac | 0x80) << (E - Ebase), zeros through the shift clamp; otherwise fixq with
-    // lossy masks. Step j reads 16-byte chunk cj = (j + l4 / 2 + 2 (key % 2)) % 4 of the lane's 64
+    // Fast path (no element loses bits in the W-bit window): x = trunc(v 2^-lsb) through fp32;
+    // otherwise fixq with lossy masks. Step j reads 16-byte chunk cj = (j + l4 / 2 + 2 (key % 2)) % 4 of the lane's 64
     // bytes, so the 8 lanes of a load phase (2 keys x 4 lanes) hit 8 distinct bank groups.
     {
       const int key = tid >> 2, l4 = tid & 3;
@@ -415,8 +426,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int bad = mx >= 0x7F80u;
       const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
-      const int ebase = lsb + 134;  // x = (frac | 0x80) << (E - ebase) for a normal element
-      const bool fast = lead == INT32_MIN || (ebase >= 1 && mn + 1 >= ((uint32_t)ebase << 7));
+      const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
+      const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 && mn + 1 >= ((uint32_t)ebase << 7));
+      const float sc = scale_of(max(-126, min(126, lsb)));
       uint32_t lm = 0;  // lossy elements, bit = dim - 32 l4
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -428,8 +440,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         } else if (fast) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            xs[2 * i] = fix_lo(w[4 * j + i], ebase);
-            xs[2 * i + 1] = fix_hi(w[4 * j + i], ebase);
+            xs[2 * i] = fixf_lo(w[4 * j + i], sc);
+            xs[2 * i + 1] = fixf_hi(w[4 * j + i], sc);
           }
         } else {
 #pragma unroll
@@ -518,13 +530,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     mma_pending = true;
     // ---------------- V tile -> digit planes against VE_c ----------------
-    // Fast digits for every value: x = sign (frac | 0x80) << (E - ebase), which is 0 for zeros and
-    // for the values below the window; those go to the channel's correction list (exact) or, past
-    // its capacity, to the bound. A channel whose maximum lies at the very bottom of the bf16 range
-    // (ebase < 1) keeps no digits at all and is bounded.
+    // Digits of x = trunc(v 2^-lsb) through fp32 for every value. The values that lose bits (their
+    // exponent field below ebase = lsb + 134) go to the channel's correction list, which adds back
+    // exactly what the truncation dropped, or past its capacity to the bound. A channel whose
+    // maximum lies at the very bottom of the bf16 range (lsb < -126) keeps no digits and is bounded.
     {
       int ebase2[2], lsb2[2];
       uint32_t keep2[2];
+      float sc2[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         // running channel exponent: the previous tiles' and this tile's key eighths
@@ -534,17 +547,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           if (S.ve4[q][2 * cp + hh] != INT16_MIN) ve = max(ve, (int)S.ve4[q][2 * cp + hh]);
         if (kq == 0) S.ve[par][2 * cp + hh] = ve;
         lsb2[hh] = ve == INT32_MIN ? 0 : ve - FV;
-        const int eb = lsb2[hh] + 134;
-        ebase2[hh] = ve == INT32_MIN ? 1 : max(eb, 1);
-        keep2[hh] = (ve == INT32_MIN || eb >= 1) ? 0xFFFFFFFFu : 0u;
+        const bool in_range = ve == INT32_MIN || lsb2[hh] >= -126;  // lsb <= 127 - 31 always
+        ebase2[hh] = lsb2[hh] + 134;
+        keep2[hh] = in_range ? 0xFFFFFFFFu : 0u;
+        sc2[hh] = scale_of(in_range ? lsb2[hh] : 0);
       }
       {
         uint32_t xa[16], xb[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const uint32_t w = jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u;
-          xa[jj] = fix_lo(w, ebase2[0]) & keep2[0];
-          xb[jj] = fix_hi(w, ebase2[1]) & keep2[1];
+          xa[jj] = fixf_lo(w, sc2[0]) & keep2[0];
+          xb[jj] = fixf_hi(w, sc2[1]) & keep2[1];
         }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -563,7 +577,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int cc = 2 * cp + hh;
-        const uint32_t thr = keep2[hh] ? ((uint32_t)ebase2[hh] << 7) : 0x8000u;  // all values when bounded
+        const uint32_t thr = keep2[hh] ? ((uint32_t)max(ebase2[hh], 0) << 7) : 0x8000u;  // all, when bounded
         const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
         uint32_t lossy = 0;
         if (mn + 1 < thr) {
@@ -575,7 +589,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             lossy |= 1u << jj;
             if (!keep2[hh]) continue;
             int lost2 = 0;
-            const int64_t dx = value24(b, lsb2[hh], lost2);
+            const int32_t dx = lost_part24(b, lsb2[hh], lost2);
             const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
             if (k < VLCAP) {
               S.vl_k[cc][k] = (uint32_t)(16 * kq + jj) | ((uint32_t)lost2 << 8);
@@ -810,9 +824,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int sb = (Rt - FW - FV) - (Rn - FN);
       sh_base[i] = sb;
       Nerr[i] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
-      // values below the V window: their values times the weights, added exactly up to a floor
-      // (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units times
-      // 2^8 V units per such value
+      // values that lost bits in the V window: their lost parts times the weights, added exactly up
+      // to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units
+      // times one V unit per such value
       const uint32_t nl = S.vl_n[c];
       if (nl <= VLCAP) {
         i128 corr = 0;
@@ -824,7 +838,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           uint64_t W = 0;
 #pragma unroll
           for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);  // |W dx| < 2^80
+          corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);  // |W dx| < 2^72
           cerr += (sb - 24 < 0) ? 1u : 0u;
           if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
         }
@@ -841,8 +855,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
             vw += W + 1;
           }
-        // a value below the window is < 2^(lsb + 8): 2^8 V units; any value is < 2^VE_c: 2^FV units
-        Nerr[i] += scale_ceil128(vw, sb + (nl >= VL_BOUNDED ? FV : 8));
+        // a truncated value lost < 1 V unit; a bounded channel's values are < 2^VE_c: 2^FV units
+        Nerr[i] += scale_ceil128(vw, sb + (nl >= VL_BOUNDED ? FV : 0));
       }
       Nerr[i] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
     }
