@@ -15,8 +15,11 @@ exponents, SUM of the rescaled accumulators): strong scaling, the same bits at e
   e2e        the same metric through the host-pointer C ABI (ea_attention_cuda_ranges) from
              pinned host buffers: H2D of q, k, v and the masks, and D2H of the output and flags,
              inside the timed region
-  roofline   the tier-1 kernel against the int8 tensor-core roofline (SURVEY's 7,936 int8 ops per
-             pair) and its measured launch time
+  roofline   the hot (tier-1) kernel, timed live with CUDA events on the launch stream
+             (ea_kernel_timing): prefill shapes (c2, c4) against the int8 tensor-core roofline at
+             7,936 int8 ops per pair (the reference's 4 x 4 score and 5 x 3 P.V slice plan), decode
+             shapes (c3, c5) against HBM at 512 bytes of K and V per (kv head, key) plus q, outputs
+             and page-table entries
   cpu_baseline  the reference's C++ certified kernel (oracle/_ref, all host threads) on a bounded
              sample of the same workload, on this host
 `--impl reference` times only that CPU implementation, on the same config and metric.
@@ -37,8 +40,34 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-INT8_OPS_PER_PAIR = 7936        # QK 4x4 slices + P.V 5x3 slices at d = 128
+INT8_OPS_PER_PAIR = 7936        # QK 4x4 slices + P.V 5x3 slices at d = 128 (the reference's slice plan)
 BF16_EQUIV_FLOPS_PER_PAIR = 512  # 4 d
+KV_BYTES_PER_KEY = 512           # bf16 K and V rows of d = 128 for one kv head, read once
+
+
+def hot_kernel(name: str) -> str:
+    return {"c2": "tc_prefill_kernel", "c3": "tc_decode_kernel", "c4": "tc_prefill_kernel",
+            "c5": "tc_decode_kernel"}[name]
+
+
+def algorithmic(cfg, name: str, shards: int = 1) -> dict:
+    """The hot kernel's algorithmic work per launch (one rank): int8 tensor ops for the prefill
+    shapes, HBM bytes for decode (K + V of every (segment, visible key) once, q, outputs, and the
+    page-table entries read)."""
+    from exactattention_b200 import workloads as w
+
+    if name in ("c2", "c4"):
+        pairs = cfg.pairs if name == "c2" else cfg.rows * cfg.prefix  # c4: the prefix part runs on it
+        return {"bound": "tensor", "units": pairs * INT8_OPS_PER_PAIR / shards, "what": "int8 ops"}
+    rows, group = cfg.rows, w.HQ // w.HKV
+    if name == "c3":
+        keys = int(cfg.ctx.astype(np.int64).sum()) * w.HKV
+        extra = int(((cfg.ctx + cfg.page_size - 1) // cfg.page_size).sum()) * w.HKV * 4
+    else:
+        keys = cfg.batch * w.HKV * cfg.kv_tokens // shards
+        extra = 0
+    b = keys * KV_BYTES_PER_KEY + rows * 2 * w.D * 2 + extra
+    return {"bound": "hbm", "units": b, "what": "bytes", "keys_per_launch": keys, "group": group}
 
 
 def parse():
@@ -215,6 +244,7 @@ def main():
         step()
     torch.cuda.synchronize()
     stats.zero_()
+    cuda.kernel_timing(1)
     clocks = Clocks(local)
     clocks.start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -230,6 +260,9 @@ def main():
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
+    k_tot, k_n = cuda.kernel_timing(2)
+    cuda.kernel_timing(0)
+    kernel_ms = k_tot / max(1, k_n)
     ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
     st = stats.cpu().numpy()
     ok = bool(not flags.any().item())
@@ -276,11 +309,19 @@ def main():
         return
 
     pk = peaks()
-    int8_peak_tops = 2.0 * pk["bf16_tflops"]   # dense int8 = 2x dense bf16 on B200 (assumed from the nominal ratio)
-    achieved = pairs * INT8_OPS_PER_PAIR / (ms / 1000.0) / 1e12
-    kern = "tc_prefill_kernel" if name == "c2" else "simt_split_kernel"
+    kern = hot_kernel(name)
+    alg = algorithmic(cfg, name, world if kv_sharded else 1)
     prof = os.path.join(ROOT, "profiles", f"{kern}_{name}.json")
     traffic = json.load(open(prof)).get("dram_bytes_per_launch") if os.path.exists(prof) else None
+    if alg["bound"] == "tensor":
+        # dense int8 = 2x dense bf16 on B200 (the nominal ratio applied to the measured bf16 GEMM)
+        peak, unit = 2.0 * pk["bf16_tflops"], "TOPS(int8)"
+        achieved = alg["units"] / (kernel_ms / 1000.0) / 1e12
+        peak_source = f"2 x {pk['source']} bf16 {pk['bf16_tflops']} TFLOP/s"
+    else:
+        peak, unit = pk["hbm_gbs"], "GB/s"
+        achieved = alg["units"] / (kernel_ms / 1000.0) / 1e9
+        peak_source = f"{pk['source']} HBM copy {pk['hbm_gbs']} GB/s"
     cpu = None
     if not args.no_cpu and world == 1:
         from oracle import ref
@@ -299,14 +340,16 @@ def main():
                    "parallelism": (f"kv-range shards x{world}, NCCL int64 MAX + SUM merge" if kv_sharded
                                    else f"replicas x{world}"),
                    "tokens_per_s": (1 if kv_sharded else world) * cfg.rows / (ms_max / 1000.0)},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak_tops, "unit": "TOPS(int8)",
-                     "frac": achieved / int8_peak_tops, "traffic": traffic,
-                     "kernel": kern + " (tier 1) with the tier-3 kernel in the same step",
-                     "peak_source": f"2 x {pk['source']} bf16 {pk['bf16_tflops']} TFLOP/s"},
+        "roofline": {"bound": alg["bound"], "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "traffic": traffic, "kernel": kern,
+                     "kernel_ms": kernel_ms, "kernel_launches_timed": k_n,
+                     "algorithmic_per_launch": alg["units"], "algorithmic_unit": alg["what"],
+                     "peak_source": peak_source},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * ((2 if splits > 1 else 1) + 2 if kv_sharded
-                                      else 2 + (1 if splits > 1 and name != "c2" else 0)),
+        # ours per step: c2 prefill + tier 3; c3/c5 decode + combine + tier 3; c4 prefill + list
+        # kernel + combine + tier 3; sharded c5 decode + combine + rescale + finalize
+        "gpu_launches": args.steps * {"c2": 2, "c3": 3, "c4": 4, "c5": 4 if kv_sharded else 3}[name],
         "clocks": clk,
         "certified": {"flags_all_zero": ok, "score_exact": int(st[0]), "weight_wide": int(st[1]),
                       "tier3_rows": int(st[2]), "domain_rows": int(st[3]), "unresolved_rows": int(st[4]),

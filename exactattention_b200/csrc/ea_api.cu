@@ -145,6 +145,33 @@ void ea_cuda_release(void) {
   cudaSetDevice(cur);
 }
 
+// ---------------------------------------------------------------------------
+// optional timing of the tier-1 kernel: CUDA events recorded on the launch stream around it
+// ---------------------------------------------------------------------------
+struct KernelTiming {
+  bool on = false;
+  std::vector<cudaEvent_t> ev;  // pairs (start, end)
+  size_t used = 0;
+};
+static KernelTiming g_kt;
+
+// A tier-1 launch records its start/end events when timing is on (events come from a pool that
+// is created when timing is switched on, so nothing is allocated per launch).
+struct TimedLaunch {
+  cudaStream_t st;
+  cudaEvent_t end = nullptr;
+  explicit TimedLaunch(cudaStream_t s) : st(s) {
+    if (g_kt.on && g_kt.used + 2 <= g_kt.ev.size()) {
+      cudaEventRecord(g_kt.ev[g_kt.used], st);
+      end = g_kt.ev[g_kt.used + 1];
+      g_kt.used += 2;
+    }
+  }
+  ~TimedLaunch() {
+    if (end) cudaEventRecord(end, st);
+  }
+};
+
 static int check_launch(const ea_launch_t* a) {
   if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->splits <= 0 || a->rows < 0) return -1;
   uint32_t ab;
@@ -264,7 +291,10 @@ static int launch_decode_tc(const ea_launch_t* a, Workspace* w, cudaStream_t st)
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
   const int32_t* seg = a->mask_kind == EA_MASK_RANGE ? a->seg_rows : nullptr;
-  e = launch_tc_decode(P, seg, decode_segments(a), st);
+  {
+    TimedLaunch tl(st);
+    e = launch_tc_decode(P, seg, decode_segments(a), st);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 decode launch");
   e = launch_combine(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "combine");
@@ -299,7 +329,10 @@ static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st
   Prob P0 = P;
   P0.kind = MASK_RANGE;
   export_to_split(P0, P, 0);
-  e = launch_tc_prefill(P0, a.block_rows, a.nblocks, st);
+  {
+    TimedLaunch tl(st);
+    e = launch_tc_prefill(P0, a.block_rows, a.nblocks, st);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 range launch");
   Prob P1 = P;
   P1.kind = MASK_CSR;
@@ -330,10 +363,13 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   build_prob(a, w, P);
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
-  if (tc_applicable(a))
-    e = launch_tc_prefill(P, a->block_rows, a->nblocks, st);
-  else
-    e = launch_simt(P, st);
+  {
+    TimedLaunch tl(st);
+    if (tc_applicable(a))
+      e = launch_tc_prefill(P, a->block_rows, a->nblocks, st);
+    else
+      e = launch_simt(P, st);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 launch");
   int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
   e = launch_tier3(P, blocks, st);
@@ -677,3 +713,36 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* x, const int64_t* m
 }
 
 }  // extern "C"
+
+// Diagnostic: device time of the tier-1 kernel of each ea_launch_cuda call (the hot kernel:
+// tensor-core prefill / decode, or the CUDA-core split kernel with its combine).
+extern "C" int ea_kernel_timing(int mode, double* total_ms, int64_t* launches) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (mode == 1) {  // on, with a pool of 512 launches
+    if (g_kt.ev.empty()) {
+      g_kt.ev.resize(1024);
+      for (auto& e : g_kt.ev)
+        if (cudaEventCreate(&e) != cudaSuccess) return fail_cuda(cudaGetLastError(), "timing events");
+    }
+    g_kt.used = 0;
+    g_kt.on = true;
+    return 0;
+  }
+  if (mode == 2) {  // collect: wait for the recorded launches, sum, reset
+    double tot = 0;
+    int64_t n = 0;
+    for (size_t i = 0; i + 1 < g_kt.used; i += 2) {
+      if (cudaEventSynchronize(g_kt.ev[i + 1]) != cudaSuccess) return fail_cuda(cudaGetLastError(), "timing");
+      float ms = 0;
+      cudaEventElapsedTime(&ms, g_kt.ev[i], g_kt.ev[i + 1]);
+      tot += ms;
+      ++n;
+    }
+    if (total_ms) *total_ms = tot;
+    if (launches) *launches = n;
+    g_kt.used = 0;
+    return 0;
+  }
+  g_kt.on = false;
+  return 0;
+}

@@ -276,6 +276,13 @@ def finalize_partials(parts: Partials, max_row_keys: int, out="bf16", stats=None
     return o, fl
 
 
+def kernel_timing(mode: int) -> tuple[float, int]:
+    """ea_kernel_timing: 1 on, 2 collect (summed ms of the tier-1 kernel, launch count), 0 off."""
+    ms, n = ctypes.c_double(0), ctypes.c_int64(0)
+    _lib.check(_lib.load().ea_kernel_timing(mode, ctypes.byref(ms), ctypes.byref(n)), "ea_kernel_timing")
+    return ms.value, n.value
+
+
 def reserve_workspace(rows: int, splits: int, dv: int) -> None:
     _lib.check(_lib.load().ea_reserve_workspace(rows, splits, dv), "ea_reserve_workspace")
 

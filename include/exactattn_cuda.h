@@ -170,6 +170,13 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* parts, const int64_
                                    int n, int dv, int fp32_out, void* out, uint8_t* flags, int64_t* stats,
                                    void* stream);
 
+/* Diagnostic timing of the hot kernel: mode 1 switches it on (and clears it; no more than 512
+ * launches are recorded), mode 2 waits for the recorded launches and returns the summed device
+ * time (ms) of their tier-1 kernel (tensor-core prefill or decode, or the CUDA-core split kernel)
+ * and the count, then clears; mode 0 switches it off. CUDA events are recorded on the launch
+ * stream around that kernel. No reference counterpart (a measurement hook of this library). */
+int ea_kernel_timing(int mode, double* total_ms, int64_t* launches);
+
 /* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
  * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,
  * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the
