@@ -186,6 +186,52 @@ def run_reference(args):
     }))
 
 
+def e2e_decode(name, cfg, q, k, v, kw, splits, out, flags, steps, world, pairs):
+    """c3 / c5 end to end from pinned host buffers: ea_attention_cuda_paged (c3) or
+    ea_attention_cuda_ranges (c5), H2D of q, the K/V caches and the masks and D2H of the outputs
+    inside the timed region."""
+    import torch
+    import torch.distributed as dist
+
+    from exactattention_b200 import cuda
+
+    pin = lambda t: t.cpu().pin_memory().numpy()  # noqa: E731
+    qh, kh, vh = pin(q).view(np.uint16), pin(k).view(np.uint16), pin(v).view(np.uint16)
+    oh = torch.empty(out.shape, dtype=torch.int16).pin_memory().numpy().view(np.uint16)
+    fh = torch.empty(flags.shape, dtype=torch.uint8).pin_memory().numpy()
+    if name == "c3":
+        pt, sl = pin(kw["page_table"]), pin(kw["seq_lens"])
+
+        def call():
+            cuda.attention_cuda_paged(qh, kh, vh, cfg.alpha, pt, sl, kw["q_heads"], splits=splits, out_buf=oh,
+                                      flags_buf=fh)
+        h2d = qh.nbytes + kh.nbytes + vh.nbytes + pt.nbytes + sl.nbytes
+        path = "ea_attention_cuda_paged (host pointers, pinned)"
+    else:
+        kb, kl = pin(kw["kv_base"]), pin(kw["kv_len"])
+
+        def call():
+            cuda.attention_cuda_ranges(qh, kh, vh, cfg.alpha, kb, kl, kw["max_row_keys"], splits=splits, out_buf=oh,
+                                       flags_buf=fh)
+        h2d = qh.nbytes + kh.nbytes + vh.nbytes + kb.nbytes + kl.nbytes
+        path = "ea_attention_cuda_ranges (host pointers, pinned)"
+    for _ in range(2):
+        call()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    e_ms = (time.perf_counter() - t0) * 1000 / steps
+    te = torch.tensor([e_ms], dtype=torch.float64, device=q.device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    same = bool(np.array_equal(oh, out.cpu().numpy().view(np.uint16)))
+    return {"value": world * pairs / (float(te.item()) / 1000.0), "unit": "pairs/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(oh.nbytes + fh.nbytes), "ms_per_step": float(te.item()),
+            "matches_device_output": same, "path": path}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -274,6 +320,8 @@ def main():
 
     # ---- e2e through the host C ABI ----
     e2e = None
+    if not args.no_e2e and name in ("c3", "c5") and not kv_sharded:
+        e2e = e2e_decode(name, cfg, q, k, v, kw, splits, out, flags, args.steps, world, pairs)
     if not args.no_e2e and name == "c2":
         qh = q.cpu().pin_memory().numpy().view(np.uint16)
         kh = k.cpu().pin_memory().numpy().view(np.uint16)

@@ -20,7 +20,7 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error", "ea_attention_cuda_noalloc",
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
-           "ea_kernel_timing")
+           "ea_kernel_timing", "ea_attention_cuda_paged")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -96,6 +96,10 @@ def load(path: str | None = None):
     lib.ea_wide_partials_rescale_cuda.restype = ctypes.c_int
     lib.ea_wide_partials_finalize_cuda.argtypes = [W, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P]
     lib.ea_wide_partials_finalize_cuda.restype = ctypes.c_int
+    lib.ea_attention_cuda_paged.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int64,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, P, ctypes.c_int,
+                                            P, ctypes.c_int, ctypes.c_int, P, P, P]
+    lib.ea_attention_cuda_paged.restype = ctypes.c_int
     lib.ea_kernel_timing.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]
     lib.ea_kernel_timing.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]

@@ -473,9 +473,34 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   size_t orp = slot((size_t)(rows + 1) * 8), oki = slot((size_t)(row_ptr ? total : 0) * 8);
   size_t okb = slot((size_t)(row_ptr ? 0 : rows) * 8), okl = slot((size_t)(row_ptr ? 0 : rows) * 8);
   size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
-  // row blocks for the tensor-core kernel (range masks): rows sharing kv_base, longest first
-  std::vector<int32_t> blocks;
-  if (kv_len_h && d == 128 && dv == 128 && !fp32_out && splits == 1 && rows < (1ll << 31)) {
+  // Range masks at d = dv = 128: rows sharing kv_base either form decode segments (at most 8 rows
+  // per key range: the decode kernel) or 128-row blocks, longest first (the prefill kernel).
+  std::vector<int32_t> blocks, segs;
+  bool decode = false;
+  if (kv_len_h && d == 128 && dv == 128 && rows < (1ll << 31)) {
+    std::vector<int32_t> order(rows);
+    for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) { return kv_base_h[x] < kv_base_h[y]; });
+    int64_t gmax = 0;
+    for (int64_t i = 0; i < rows;) {
+      int64_t j = i;
+      while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
+      gmax = std::max(gmax, j - i);
+      i = j;
+    }
+    decode = gmax <= 8;
+    if (decode) {
+      for (int64_t i = 0; i < rows;) {
+        int64_t j = i;
+        while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
+        std::vector<int32_t> sgm(8, -1);
+        for (int64_t u = i; u < j; ++u) sgm[u - i] = order[u];
+        segs.insert(segs.end(), sgm.begin(), sgm.end());
+        i = j;
+      }
+    }
+  }
+  if (!decode && kv_len_h && d == 128 && dv == 128 && !fp32_out && splits == 1 && rows < (1ll << 31)) {
     std::vector<int32_t> order(rows);
     for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
     std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {
@@ -498,7 +523,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
     });
     for (auto& b : bl) blocks.insert(blocks.end(), b.begin(), b.end());
   }
-  size_t ob = slot(blocks.size() * 4);
+  size_t ob = slot(blocks.size() * 4), osg = slot(segs.size() * 4);
 
   Workspace* w;
   {
@@ -534,6 +559,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
     EA_CPY(okl, kl.data(), (size_t)rows * 8);
   }
   EA_CPY(ob, blocks.data(), blocks.size() * 4);
+  EA_CPY(osg, segs.data(), segs.size() * 4);
 #undef EA_CPY
   e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
@@ -561,6 +587,8 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.stats = (int64_t*)(base + os);
   a.block_rows = blocks.empty() ? nullptr : (const int32_t*)(base + ob);
   a.nblocks = (int64_t)(blocks.size() / 128);
+  a.seg_rows = segs.empty() ? nullptr : (const int32_t*)(base + osg);
+  a.nsegs = (int64_t)(segs.size() / 8);
   int rc = ea_launch_cuda(&a, st);
   if (rc) return rc;
   int64_t hs[EA_STATS_LEN];
@@ -744,5 +772,97 @@ extern "C" int ea_kernel_timing(int mode, double* total_ms, int64_t* launches) {
     return 0;
   }
   g_kt.on = false;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// host-pointer paged decode (staged copies, synchronous)
+// ---------------------------------------------------------------------------
+extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_heads, int d, const uint16_t* k_cache,
+                                       const uint16_t* v_cache, int64_t num_pages, int kv_heads, int page_size, int dv,
+                                       float alpha, const int32_t* page_table, int max_pages, const int32_t* seq_lens,
+                                       int fp32_out, int splits, void* out, uint8_t* flags, int64_t* stats) {
+  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || batch < 0 || num_pages < 0 || max_pages <= 0) return -1;
+  if (q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || page_size <= 0) return -5;
+  uint32_t ab;
+  memcpy(&ab, &alpha, 4);
+  int32_t am, ae;
+  if (!decode_fp32(ab, am, ae)) return -3;
+  const int64_t rows = batch * q_heads;
+  if (rows == 0) return 0;
+  int64_t maxn = 1;
+  for (int64_t b = 0; b < batch; ++b) maxn = std::max<int64_t>(maxn, seq_lens[b]);
+  const size_t osz = fp32_out ? 4 : 2;
+  const size_t cache = (size_t)num_pages * kv_heads * page_size;
+  size_t off = 0;
+  auto slot = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  size_t oq = slot((size_t)rows * d * 2), ok = slot(cache * d * 2), ov = slot(cache * dv * 2);
+  size_t opt = slot((size_t)batch * max_pages * 4), osl = slot((size_t)batch * 4);
+  size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace();
+    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+    if (!grow(&w->stage, &w->stage_bytes, off)) return fail_cuda(cudaErrorMemoryAllocation, "staging");
+    if (!w->stream && cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess)
+      return fail_cuda(cudaGetLastError(), "stream");
+  }
+  char* base = (char*)w->stage;
+  cudaStream_t st = w->stream;
+  cudaError_t e;
+  const struct {
+    size_t dst;
+    const void* src;
+    size_t n;
+  } h2d[] = {{oq, q, (size_t)rows * d * 2},
+             {ok, k_cache, cache * d * 2},
+             {ov, v_cache, cache * dv * 2},
+             {opt, page_table, (size_t)batch * max_pages * 4},
+             {osl, seq_lens, (size_t)batch * 4}};
+  for (const auto& c : h2d)
+    if (c.n && (e = cudaMemcpyAsync(base + c.dst, c.src, c.n, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+      return fail_cuda(e, "h2d");
+  if ((e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st)) != cudaSuccess) return fail_cuda(e, "memset");
+  ea_launch_t a;
+  memset(&a, 0, sizeof(a));
+  a.q = (const uint16_t*)(base + oq);
+  a.rows = rows;
+  a.d = d;
+  a.k = (const uint16_t*)(base + ok);
+  a.v = (const uint16_t*)(base + ov);
+  a.nkeys = (int64_t)cache;
+  a.dv = dv;
+  a.alpha = alpha;
+  a.mask_kind = EA_MASK_PAGED;
+  a.page_table = (const int32_t*)(base + opt);
+  a.seq_lens = (const int32_t*)(base + osl);
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.max_row_keys = maxn;
+  a.fp32_out = fp32_out;
+  a.splits = splits;
+  a.out = base + oo;
+  a.flags = (uint8_t*)(base + of);
+  a.stats = (int64_t*)(base + os);
+  int rc = ea_launch_cuda(&a, st);
+  if (rc) return rc;
+  int64_t hs[EA_STATS_LEN];
+  if ((e = cudaMemcpyAsync(out, base + oo, (size_t)rows * dv * osz, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(flags, base + of, (size_t)rows, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(hs, base + os, sizeof(hs), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+    return fail_cuda(e, "d2h");
+  if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e, "sync");
+  if (stats) {
+    stats[0] += hs[STAT_SCORE_EXACT];
+    stats[1] += hs[STAT_WEIGHT_WIDE];
+    stats[2] += hs[STAT_TIER3_ROWS];
+  }
   return 0;
 }

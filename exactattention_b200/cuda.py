@@ -322,6 +322,39 @@ def attention_cuda_ranges(q, k, v, alpha, kv_base, kv_len, max_row_keys=None, ou
     return res, flags
 
 
+def attention_cuda_paged(q, k_cache, v_cache, alpha, page_table, seq_lens, q_heads: int, out="bf16", splits=1,
+                         stats: CudaStats | None = None, out_buf=None, flags_buf=None):
+    """Host buffers through `ea_attention_cuda_paged`: q (batch * q_heads, d), caches
+    (num_pages, kv_heads, page_size, d), page_table (batch, max_pages) int32, seq_lens (batch,)
+    int32. Returns (out, flags); raises like attention_cuda."""
+    lib = _lib.load()
+    rows, d = q.shape
+    npg, hkv, ps, dv = v_cache.shape
+    batch = rows // q_heads
+    fp32 = out == "fp32"
+    res = out_buf if out_buf is not None else np.zeros((rows, dv), dtype=np.float32 if fp32 else np.uint16)
+    flags = flags_buf if flags_buf is not None else np.zeros(rows, dtype=np.uint8)
+    st = np.zeros(3, dtype=np.int64)
+    pt = np.ascontiguousarray(page_table, dtype=np.int32)
+    sl = np.ascontiguousarray(seq_lens, dtype=np.int32)
+    rc = lib.ea_attention_cuda_paged(q.ctypes.data, batch, q_heads, d, k_cache.ctypes.data, v_cache.ctypes.data, npg,
+                                     hkv, ps, dv, ctypes.c_float(float(np.float32(alpha))), pt.ctypes.data,
+                                     pt.shape[1], sl.ctypes.data, int(fp32), splits, res.ctypes.data,
+                                     flags.ctypes.data, st.ctypes.data)
+    _lib.check(rc, "ea_attention_cuda_paged")
+    if stats is not None:
+        stats.score_fallbacks += int(st[0])
+        stats.weight_fallbacks += int(st[1])
+        stats.final_fallbacks += int(st[2])
+        stats.rows += rows
+        stats.flagged_rows += int((flags != 0).sum())
+    if np.any(flags == 2):
+        raise ExactAttentionDomainError("non-finite input or logit overflow")
+    if np.any(flags == 1):
+        raise RuntimeError("rows left uncertified by every device tier (library bug)")
+    return res, flags
+
+
 def row_segments(kv_base: np.ndarray, width: int = 8) -> np.ndarray:
     """Groups RANGE-mask rows that share kv_base into segments of at most `width` (8) rows, -1
     padded: the (nsegs, 8) int32 `segments` argument of launch (decode: a GQA group per segment).

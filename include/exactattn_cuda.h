@@ -45,6 +45,16 @@ int ea_attention_cuda_ranges(const uint16_t* q, int64_t rows, int d, const uint1
                              int64_t max_row_keys, int fp32_out, int splits, void* out, uint8_t* flags,
                              int64_t* stats);
 
+/* Host-pointer paged decode: q (batch * q_heads, d) with row r = sequence r / q_heads, head
+ * r % q_heads; k_cache, v_cache (num_pages, kv_heads, page_size, d / dv); page_table (batch,
+ * max_pages) int32; seq_lens (batch,) int32. Staged to the device, synchronous; stats as
+ * ea_attention_cuda. The host form of the paged layout of ea_launch_cuda (the reference's C ABI
+ * has no paged entry; its paged callers build CSR key lists, which give the same outputs). */
+int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_heads, int d, const uint16_t* k_cache,
+                            const uint16_t* v_cache, int64_t num_pages, int kv_heads, int page_size, int dv,
+                            float alpha, const int32_t* page_table, int max_pages, const int32_t* seq_lens,
+                            int fp32_out, int splits, void* out, uint8_t* flags, int64_t* stats);
+
 /* RN-even of (a / b) * 2^E into fp32 (fp32 != 0) or bf16; a, b given as (hi, lo) 64-bit
  * halves. Mirrors the reference's test export ea_round_ratio
  * (csrc/exact_attention_cpu.cpp:630-638); evaluated on the GPU. */

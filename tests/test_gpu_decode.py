@@ -175,3 +175,33 @@ def test_decode_kv_sharded_partials():
     torch.cuda.synchronize()
     assert st.cpu().numpy()[7] == int(kl_full.sum())
     assert torch.equal(flags, fflags) and torch.equal(out, full)
+
+
+def test_host_entries_take_the_decode_kernel():
+    """Host-pointer entries: ea_attention_cuda_paged (paged caches) and ea_attention_cuda_ranges
+    (rows in groups of at most 8 per key range: decode segments built by the library) give the
+    device launch's bits."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(606)
+    B, hq, hkv, ps = 3, 4, 2, 16
+    Q, Kc, Vc, pt, ctx = _paged_case(rng, B, hq, hkv, ps, 100, 900)
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(128)
+    o_d, f_d = cuda.launch(_t(Q, dev), _t(Kc, dev), _t(Vc, dev), alpha, page_table=_t(pt, dev),
+                           seq_lens=_t(ctx.astype(np.int32), dev), page_size=ps, q_heads=hq, kv_heads=hkv, splits=3)
+    o_h, f_h = cuda.attention_cuda_paged(Q, Kc, Vc, alpha, pt, ctx.astype(np.int32), hq, splits=3)
+    assert np.array_equal(o_h, o_d.cpu().numpy().view(np.uint16)) and np.array_equal(f_h, f_d.cpu().numpy())
+
+    Q2, K2, V2, kb, kl = _range_case(rng, "outlier", "normal", 4, 2, 500)
+    o_d2, f_d2 = cuda.launch(_t(Q2, dev), _t(K2, dev), _t(V2, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
+                             splits=2)
+    cuda.kernel_timing(1)
+    o_h2, f_h2 = cuda.attention_cuda_ranges(Q2, K2, V2, alpha, kb, kl, splits=2)
+    ms, n = cuda.kernel_timing(2)
+    cuda.kernel_timing(0)
+    assert n == 1 and ms > 0
+    assert np.array_equal(o_h2, o_d2.cpu().numpy().view(np.uint16)) and np.array_equal(f_h2, f_d2.cpu().numpy())
