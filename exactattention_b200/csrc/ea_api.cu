@@ -403,7 +403,11 @@ int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream)
     if (rc) return rc;
     set_export(P, x);
     const int32_t* seg = a->mask_kind == EA_MASK_RANGE ? a->seg_rows : nullptr;
-    cudaError_t e = launch_tc_decode(P, seg, decode_segments(a), st);
+    cudaError_t e;
+    {
+      TimedLaunch tl(st);
+      e = launch_tc_decode(P, seg, decode_segments(a), st);
+    }
     if (e == cudaSuccess) e = launch_combine(P, st);
     return e == cudaSuccess ? 0 : fail_cuda(e, "partials decode launch");
   }
@@ -411,7 +415,11 @@ int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream)
   if (rc) return rc;
   build_prob(a, w, P);
   set_export(P, x);
-  cudaError_t e = tc_applicable(a) ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
+  cudaError_t e;
+  {
+    TimedLaunch tl(st);
+    e = tc_applicable(a) ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
+  }
   if (e != cudaSuccess) return fail_cuda(e, "partials launch");
   return 0;
 }
