@@ -78,3 +78,50 @@ def test_nccl_kv_sharded_matches_single_gpu(world, tmp_path):
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"flags_{r}.npy"), fflags.cpu().numpy()), r
         assert np.array_equal(np.load(tmp_path / f"out_{r}.npy"), full), r
+
+
+def _c5_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    from exactattention_b200 import dist as ea_dist, workloads as w
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        case = w.device_case("c5", dev, shard=rank, nshards=world)
+        kw = dict(case["kw"])
+        mrk = kw.pop("max_row_keys")
+        out, flags = ea_dist.attention_kv_sharded(case["q"], case["k"], case["v"], case["cfg"].alpha, max_row_keys=mrk,
+                                                  splits=64, **kw)
+        torch.cuda.synchronize(dev)
+        np.save(os.path.join(result_dir, f"c5_out_{rank}.npy"), out.cpu().numpy())
+        np.save(os.path.join(result_dir, f"c5_flags_{rank}.npy"), flags.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_c5_sharded_sha(tmp_path):
+    """Config 5 sharded by key range over the ranks: every rank's merged output has the
+    reference's SHA-256 (the bits do not depend on the GPU count)."""
+    import hashlib
+    import json
+
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "configs.json"))).get("c5")
+    if gold is None:
+        pytest.skip("no golden SHA for c5")
+    mp.start_processes(_c5_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        assert not np.load(tmp_path / f"c5_flags_{r}.npy").any()
+        out = np.load(tmp_path / f"c5_out_{r}.npy").view(np.uint16)
+        assert hashlib.sha256(np.ascontiguousarray(out).tobytes()).hexdigest() == gold, r
