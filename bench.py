@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kv-shard", default="", help="c5 on one GPU: only key range K of N (\"K/N\"), e.g. the "
+                    "share of one rank of an N-GPU run (a smaller case of the same kernel, for profiling)")
     return ap.parse_args()
 
 
@@ -263,9 +265,17 @@ def main():
     # with NCCL all-reduces (strong scaling: the job is the same 2^20-key workload at every N);
     # the other configs run a full copy per rank (weak scaling, no data-path collective)
     kv_sharded = name == "c5" and world > 1
-    case = workloads.device_case(name, dev, shard=rank, nshards=world) if kv_sharded else workloads.device_case(name, dev)
+    if args.kv_shard:
+        if name != "c5" or world > 1:
+            raise SystemExit("--kv-shard applies to c5 on one GPU")
+        ks, kn = (int(x) for x in args.kv_shard.split("/"))
+        case = workloads.device_case(name, dev, shard=ks, nshards=kn)
+    elif kv_sharded:
+        case = workloads.device_case(name, dev, shard=rank, nshards=world)
+    else:
+        case = workloads.device_case(name, dev)
     cfg = case["cfg"]
-    pairs = cfg.pairs
+    pairs = cfg.pairs // (int(args.kv_shard.split("/")[1]) if args.kv_shard else 1)
     job_pairs = pairs if kv_sharded else world * pairs
     q, k, v, kw = case["q"], case["k"], case["v"], case["kw"]
     stats = torch.zeros(8, dtype=torch.int64, device=dev)
@@ -363,7 +373,7 @@ def main():
 
     pk = peaks()
     kern = hot_kernel(name)
-    alg = algorithmic(cfg, name, world if kv_sharded else 1)
+    alg = algorithmic(cfg, name, world if kv_sharded else (int(args.kv_shard.split("/")[1]) if args.kv_shard else 1))
     prof = os.path.join(ROOT, "profiles", f"{kern}_{name}.json")
     traffic = json.load(open(prof)).get("dram_bytes_per_launch") if os.path.exists(prof) else None
     if alg["bound"] == "tensor":
@@ -387,7 +397,8 @@ def main():
         "metric": "certified QK pairs/s", "value": value, "unit": "pairs/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
         "scaling": "strong" if kv_sharded else "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": name, "pairs_per_gpu": job_pairs // world, "job_pairs": job_pairs, "rows": cfg.rows,
+        "config": {"workload": name + (f" key range {args.kv_shard}" if args.kv_shard else ""),
+                   "pairs_per_gpu": job_pairs // world, "job_pairs": job_pairs, "rows": cfg.rows,
                    "splits": splits, "heads": "16q/8kv", "head_dim": 128,
                    "l2": "flushed (256 MiB write) between steps",
                    "parallelism": (f"kv-range shards x{world}, NCCL int64 MAX + SUM merge" if kv_sharded
