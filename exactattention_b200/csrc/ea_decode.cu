@@ -430,6 +430,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     bool rk_pending = ntiles > 0, rv_pending = ntiles > 0;
     uint32_t rk_ph = 0, rv_ph = 0;  // phase of the fetch in flight
     int par = 0;
+    EA_PTW_INIT
     for (int i = 0; i < ntiles; ++i, par ^= 1) {
       const int64_t j0 = kbeg + (int64_t)i * BK;
       const int nvalid = (int)min((int64_t)BK, kend - j0);
@@ -445,6 +446,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         break;
       }
       rk_pending = false;
+      EA_PTW(THREADS / 2, 0)
 #pragma unroll 1
       for (int it = 0; it < 2; ++it) {
         const int key = 64 * it + (ptid >> 2), l4 = ptid & 3;
@@ -519,6 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
       tc::fence_async_smem();
       group_sync(2);
+      EA_PTW(THREADS / 2, 1)
       // score MMAs of tile i (the accumulators are free: pass 1 of tile i - 1 is done)
       if (ptid == 0) {
         tc::fence_after_sync();
@@ -554,6 +557,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         break;
       }
       rv_pending = false;
+      EA_PTW(THREADS / 2, 2)
       const int cp = ptid & 63, kq = ptid >> 6;
       const uint8_t* vsrc = rawv + (32 * kq) * (DV * 2) + cp * 4;  // word of key 32 kq + jj at jj * 256
       const int nv = min(32, max(0, nvalid - 32 * kq));             // this thread's valid keys
@@ -594,6 +598,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         for (int q = 0; q < 4; ++q) S.vlmask[ptid][q] = 0;
       }
       group_sync(2);
+      EA_PTW(THREADS / 2, 3)
       // Digits of x = trunc(v 2^-lsb) through fp32 for every value. The values that lose bits (their
       // exponent field below ebase = lsb + 134) go to the channel's correction list, which adds back
       // exactly what the truncation dropped, or past its capacity to the bound. A channel whose
@@ -669,6 +674,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
       tc::fence_async_smem();
       group_sync(2);
+      EA_PTW(THREADS / 2, 4)
       if (ptid == 0) mbar_arrive(&S.bar_vready);  // value digits and channel data of tile i
       // the raw V rows are consumed: fetch the next tile's
       if (pwarp == NWARPS / 2 - 2 && i + 1 < ntiles) {
@@ -680,6 +686,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         rv_ph = (uint32_t)(i + 1) & 1u;
       }
     }
+    EA_PTW_FLUSH(THREADS / 2)
     if (!ok_wait) S.abort = 1;
     // a wait that gave up: the copies still in flight get another bounded wait before the shared
     // memory is released

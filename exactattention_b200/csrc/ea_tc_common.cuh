@@ -23,10 +23,24 @@
 #define EA_PT_FLUSH \
   if (tid == 0)     \
     for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], (unsigned long long)pt_acc[i]);
+// the same, kept by thread `who` (a second role of a warp-specialised kernel) in counters 8-15
+#define EA_PTW_INIT long long ptw_last = clock64(); long long ptw_acc[8] = {0};
+#define EA_PTW(who, i)                   \
+  if (tid == (who)) {                    \
+    const long long pt_now = clock64();  \
+    ptw_acc[i] += pt_now - ptw_last;     \
+    ptw_last = pt_now;                   \
+  }
+#define EA_PTW_FLUSH(who) \
+  if (tid == (who))       \
+    for (int i = 0; i < 8; ++i) atomicAdd(&g_phase_cycles[8 + i], (unsigned long long)ptw_acc[i]);
 #else
 #define EA_PT_INIT
 #define EA_PT(i)
 #define EA_PT_FLUSH
+#define EA_PTW_INIT
+#define EA_PTW(who, i)
+#define EA_PTW_FLUSH(who)
 #endif
 
 namespace ea {
