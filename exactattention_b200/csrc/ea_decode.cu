@@ -21,8 +21,8 @@
 // TMEM lane quadrant = warp % 4) compute logits, weights and W digits, issue the P.V MMAs, and keep
 // the running sums (pass 1 / pass 2: lane = key; drain: lane = channel; rows g = warp / 4 + 2 i).
 // The slicing of tile i + 1 overlaps the epilogue of tile i; mbarriers carry the hand-offs (raw
-// K / V landed, score MMAs done, pass 1 done, value digits ready, tile done, P.V done) and every
-// wait is bounded.
+// K / V landed, score MMAs done, pass 1 done, value digits ready, P.V done) and every wait is
+// bounded.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -67,17 +67,17 @@ constexpr uint32_t OFF_T = OFF_W + NSW * BK;
 constexpr uint32_t OFF_SMALL = OFF_T + GD * BK * 4;
 
 struct Small {
-  uint64_t ta[256];
-  uint64_t tb[256];
   uint32_t klossy[BK][4];
   int32_t klsb[BK];
   int32_t kbad[BK];
-  uint32_t vlmask[DV][4];  // keys whose value in channel c lost bits in the V window
+  // value metadata of the last two tiles (by tile parity): the producers write tile i + 1's while
+  // the consumers still read tile i's
+  uint32_t vlmask[2][DV][4];  // keys whose value in channel c lost bits in the V window
   // per channel, up to VLCAP values that lost bits in the V window, with their lost parts (units
   // 2^(lsb_c - 24)), added back exactly in the drain: (key | still-lossy << 8), part
-  uint32_t vl_n[DV];
-  uint32_t vl_k[DV][4];
-  int32_t vl_dx[DV][4];
+  uint32_t vl_n[2][DV];
+  uint16_t vl_k[2][DV][4];
+  int32_t vl_dx[2][DV][4];
   int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
   int16_t ve4[4][DV];  // per key quarter maxima of the current tile (INT16_MIN: none)
   int32_t rows[GD];
@@ -89,8 +89,8 @@ struct Small {
   uint64_t zs[4][GD];
   uint32_t zl[4][GD];
   // producer -> consumer: raw K / V tiles landed (bulk copies), score MMAs done, value digits
-  // ready; consumer -> producer: pass 1 done, tile done; consumer: P.V MMAs done
-  uint64_t bar_rk, bar_rv, bar_smma, bar_vready, bar_p1, bar_cdone, bar_pv;
+  // ready; consumer -> producer: pass 1 done, P.V MMAs done
+  uint64_t bar_rk, bar_rv, bar_smma, bar_vready, bar_p1, bar_pv;
   int32_t abort;  // a bounded wait gave up in either role
   uint32_t tmem;
   int32_t nrows;
@@ -309,10 +309,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     S.len[tid] = row >= 0 ? (int32_t)row_len(P, row) : 0;
     S.rst[tid] = ST_OK;
   }
-  for (int i = tid; i < 256; i += THREADS) {
-    S.ta[i] = g_ta64[i];
-    S.tb[i] = g_tb64[i];
-  }
   for (int i = tid; i < DV; i += THREADS) S.ve[0][i] = S.ve[1][i] = INT32_MIN;
   for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
   if (tid == 0) {
@@ -322,7 +318,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     tc::mbar_init(&S.bar_pv, 1);
     tc::mbar_init(&S.bar_p1, 1);
     tc::mbar_init(&S.bar_vready, 1);
-    tc::mbar_init(&S.bar_cdone, 1);
     S.abort = 0;
   }
   __syncthreads();
@@ -548,10 +543,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         rk_ph = (uint32_t)(i + 1) & 1u;
       }
 
-      // ---- V(i): needs its raw rows, and tile i - 1 finished by the consumers (its P.V MMAs read
-      //      the value digits, its merge read the channel exponents and corrections) ----
+      // ---- V(i): needs its raw rows, and the P.V MMAs of tile i - 1 done with the value digits. The
+      //      channel data of tile i - 1 stay in the other parity buffer until the consumers' merge;
+      //      the P.V MMAs of tile i + 1 (after that merge) gate the next rewrite of this one ----
       okw = tc::mbar_wait(&S.bar_rv, ph);
-      if (i > 0) okw &= tc::mbar_wait(&S.bar_cdone, php);
+      if (i > 0) okw &= tc::mbar_wait(&S.bar_pv, php);
       if (!group_sync_and(2, okw)) {
         ok_wait = false;
         break;
@@ -593,9 +589,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         }
       }
       if (ptid < DV) {
-        S.vl_n[ptid] = 0;
+        S.vl_n[par][ptid] = 0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) S.vlmask[ptid][q] = 0;
+        for (int q = 0; q < 4; ++q) S.vlmask[par][ptid][q] = 0;
       }
       group_sync(2);
       EA_PTW(THREADS / 2, 3)
@@ -661,15 +657,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
               if (!keep2[hh]) continue;
               int lost2 = 0;
               const int32_t dx = lost_part24(b, lsb2[hh], lost2);
-              const uint32_t k = atomicAdd(&S.vl_n[cc], 1u);
+              const uint32_t k = atomicAdd(&S.vl_n[par][cc], 1u);
               if (k < VLCAP) {
-                S.vl_k[cc][k] = (uint32_t)(32 * kq + jj) | ((uint32_t)lost2 << 8);
-                S.vl_dx[cc][k] = dx;
+                S.vl_k[par][cc][k] = (uint16_t)((32 * kq + jj) | (lost2 << 8));
+                S.vl_dx[par][cc][k] = dx;
               }
             }
-            if (!keep2[hh] && lossy) atomicAdd(&S.vl_n[cc], VL_BOUNDED);  // the whole channel is bounded
+            if (!keep2[hh] && lossy) atomicAdd(&S.vl_n[par][cc], VL_BOUNDED);  // the whole channel is bounded
           }
-          S.vlmask[cc][kq] = lossy;
+          S.vlmask[par][cc][kq] = lossy;
         }
       }
       tc::fence_async_smem();
@@ -831,7 +827,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           const Rnd t = rnd_from_f32(tb);
           uint32_t M;
           int64_t E;
-          int ws = weight_from_logit(t, S.ta, S.tb, M, E);
+          int ws = weight_from_logit(t, g_ta64, g_tb64, M, E);  // 2 x 2 KB tables, L1-resident
           if (ws == W_RISKY) {
             ++n_wide;
             ws = wide_weight(t, M, E);
@@ -921,18 +917,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         // values that lost bits in the V window: their lost parts times the weights, added exactly up
         // to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units
         // times one V unit per such value
-        const uint32_t nl = S.vl_n[c];
+        const uint32_t nl = S.vl_n[par][c];
         if (nl <= VLCAP) {
           i128 corr = 0;
           u128 cerr = 0;
 #pragma unroll 1
           for (uint32_t k = 0; k < nl; ++k) {
-            const uint32_t ck = S.vl_k[c][k];
+            const uint32_t ck = S.vl_k[par][c][k];
             const int key = (int)(ck & 0xFFu);
             uint64_t W = 0;
 #pragma unroll
             for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-            corr += shift_floor128((i128)(int64_t)W * S.vl_dx[c][k], sb - 24);  // |W dx| < 2^72
+            corr += shift_floor128((i128)(int64_t)W * S.vl_dx[par][c][k], sb - 24);  // |W dx| < 2^72
             cerr += (sb - 24 < 0) ? 1u : 0u;
             if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
           }
@@ -942,7 +938,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           uint64_t vw = 0;
 #pragma unroll 1
           for (int q4 = 0; q4 < 4; ++q4)
-            for (uint32_t m = S.vlmask[c][q4]; m; m &= m - 1) {
+            for (uint32_t m = S.vlmask[par][c][q4]; m; m &= m - 1) {
               const int key = 32 * q4 + __ffs(m) - 1;
               uint64_t W = 0;
 #pragma unroll
@@ -996,7 +992,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         break;
       }
       pv_pending = false;
-      if (tid == 0) mbar_arrive(&S.bar_cdone);  // tile i is finished: the producers may reuse its data
       EA_PT(6)
     }
     EA_PT_FLUSH
