@@ -880,6 +880,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
       pv_pending = true;
       pv_ph = ph;
+      EA_PT(7)
       // meanwhile: this channel's exponent change, the rows' merges and bounds (registers only)
       const int ve_now = S.ve[par][c];
       int sh_base[RPT];
