@@ -520,16 +520,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       // score MMAs of tile i (the accumulators are free: pass 1 of tile i - 1 is done)
       if (ptid == 0) {
         tc::fence_after_sync();
-        const uint32_t ak = tc::smem_u32(sK), bq = tc::smem_u32(sQ);
-        const uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
-#pragma unroll 1
+        // descriptors: the base ones once, then constant start-address offsets (16-byte units)
+        constexpr uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
+        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sK), lbo_a, 128);
+        const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sQ), lbo_b, 128);
+#pragma unroll
         for (int t = 0; t < NK; ++t) {
           const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
-          for (int ks = 0; ks < D / 32; ++ks) {
-            const uint64_t ad = tc::smem_desc(ak + t * K_PLANE + ks * 2 * lbo_a, lbo_a, 128);
-            const uint64_t bd = tc::smem_desc(bq + ks * 2 * lbo_b, lbo_b, 128);
-            tc::mma_i8(tmem + 32 * t, ad, bd, idesc, ks > 0);
-          }
+#pragma unroll
+          for (int ks = 0; ks < D / 32; ++ks)
+            tc::mma_i8(tmem + 32 * t, ad0 + ((t * K_PLANE + ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
+                       ks > 0);
         }
         tc::mma_commit(tc::smem_u32(&S.bar_smma));
       }
@@ -865,16 +866,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       // ---------------- P.V MMAs: 4 value digits x (N = 48: row weight digits) ----------------
       if (tid == 0) {
         tc::fence_after_sync();
-        const uint32_t av = tc::smem_u32(sV), bw = tc::smem_u32(sW);
-        const uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
-#pragma unroll 1
+        constexpr uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
+        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sV), lbo_a, 128);
+        const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sW), lbo_b, 128);
+#pragma unroll
         for (int u = 0; u < NV; ++u) {
           const uint32_t idesc = tc::idesc_i8(128, NSW, u == NV - 1, false);
-          for (int ks = 0; ks < BK / 32; ++ks) {
-            const uint64_t ad = tc::smem_desc(av + u * V_PLANE + ks * 2 * lbo_a, lbo_a, 128);
-            const uint64_t bd = tc::smem_desc(bw + ks * 2 * lbo_b, lbo_b, 128);
-            tc::mma_i8(tmem + COL_O + NSW * u, ad, bd, idesc, ks > 0);
-          }
+#pragma unroll
+          for (int ks = 0; ks < BK / 32; ++ks)
+            tc::mma_i8(tmem + COL_O + NSW * u, ad0 + ((u * V_PLANE + ks * 2 * lbo_a) >> 4),
+                       bd0 + ((ks * 2 * lbo_b) >> 4), idesc, ks > 0);
         }
         tc::mma_commit(tc::smem_u32(&S.bar_pv));
       }
