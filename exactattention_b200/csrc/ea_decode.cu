@@ -314,8 +314,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   if (tid == 0) {
     tc::mbar_init(&S.bar_rk, 1);
     tc::mbar_init(&S.bar_rv, 1);
-    tc::mbar_init(&S.bar_smma, 1);
-    tc::mbar_init(&S.bar_pv, 1);
+    tc::mbar_init(&S.bar_smma, NK);  // one commit per key digit's issuer
+    tc::mbar_init(&S.bar_pv, NV);    // one commit per value digit's issuer
     tc::mbar_init(&S.bar_p1, 1);
     tc::mbar_init(&S.bar_vready, 1);
     S.abort = 0;
@@ -517,21 +517,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       tc::fence_async_smem();
       group_sync(2);
       EA_PTW(THREADS / 2, 1)
-      // score MMAs of tile i (the accumulators are free: pass 1 of tile i - 1 is done)
-      if (ptid == 0) {
+      // score MMAs of tile i (the accumulators are free: pass 1 of tile i - 1 is done). Key digit t
+      // goes to its own accumulator and is issued by lane 0 of producer warp t: an issuing thread
+      // waits while the tensor core takes its operands, so four issuers share that wait.
+      if (lane == 0 && pwarp < NK) {
+        const int t = pwarp;
         tc::fence_after_sync();
-        // descriptors: the base ones once, then constant start-address offsets (16-byte units)
+        // descriptors: the base ones, then constant start-address offsets (16-byte units)
         constexpr uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
-        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sK), lbo_a, 128);
+        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sK + t * K_PLANE), lbo_a, 128);
         const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sQ), lbo_b, 128);
+        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
 #pragma unroll
-        for (int t = 0; t < NK; ++t) {
-          const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
-#pragma unroll
-          for (int ks = 0; ks < D / 32; ++ks)
-            tc::mma_i8(tmem + 32 * t, ad0 + ((t * K_PLANE + ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
-                       ks > 0);
-        }
+        for (int ks = 0; ks < D / 32; ++ks)
+          tc::mma_i8(tmem + 32 * t, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc, ks > 0);
         tc::mma_commit(tc::smem_u32(&S.bar_smma));
       }
       // the raw K rows are consumed: fetch the next tile's
@@ -864,19 +863,18 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
       EA_PT(3)
       // ---------------- P.V MMAs: 4 value digits x (N = 48: row weight digits) ----------------
-      if (tid == 0) {
+      // value digit u to its own accumulator, issued by lane 0 of consumer warp u
+      if (lane == 0 && warp < NV) {
+        const int u = warp;
         tc::fence_after_sync();
         constexpr uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
-        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sV), lbo_a, 128);
+        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sV + u * V_PLANE), lbo_a, 128);
         const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sW), lbo_b, 128);
+        const uint32_t idesc = tc::idesc_i8(128, NSW, u == NV - 1, false);
 #pragma unroll
-        for (int u = 0; u < NV; ++u) {
-          const uint32_t idesc = tc::idesc_i8(128, NSW, u == NV - 1, false);
-#pragma unroll
-          for (int ks = 0; ks < BK / 32; ++ks)
-            tc::mma_i8(tmem + COL_O + NSW * u, ad0 + ((u * V_PLANE + ks * 2 * lbo_a) >> 4),
-                       bd0 + ((ks * 2 * lbo_b) >> 4), idesc, ks > 0);
-        }
+        for (int ks = 0; ks < BK / 32; ++ks)
+          tc::mma_i8(tmem + COL_O + NSW * u, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
+                     ks > 0);
         tc::mma_commit(tc::smem_u32(&S.bar_pv));
       }
       pv_pending = true;
