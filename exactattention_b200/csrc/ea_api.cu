@@ -125,7 +125,8 @@ int ea_reserve_workspace(int64_t rows, int splits, int dv) {
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* w = workspace();
   if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-  return reserve(w, rows, splits, dv);
+  // the tree-mask and decode paths keep split partials even at one split: reserve for two
+  return reserve(w, rows, splits < 2 ? 2 : splits, dv);
 }
 
 void ea_cuda_release(void) {

@@ -1059,9 +1059,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 
 // Grid (segments, splits); writes split partials (P.pR ..) for every listed row.
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(tcd::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)tcd::SMEM_BYTES);
-  if (e != cudaSuccess) return e;
+  // the shared-memory opt-in is a property of the function on a device: set it once per device
+  // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tcd::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
   tcd::tc_decode_kernel<<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
   return cudaGetLastError();

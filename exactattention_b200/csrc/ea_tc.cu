@@ -667,9 +667,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 }  // namespace tck
 
 cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(tck::tc_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)tck::SMEM_BYTES);
-  if (e != cudaSuccess) return e;
+  // the shared-memory opt-in is a property of the function on a device: set it once per device
+  // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tck::tc_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tck::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
   tck::tc_prefill_kernel<<<(unsigned)nblocks, tck::THREADS, tck::SMEM_BYTES, st>>>(P, block_rows);
   return cudaGetLastError();
 }
