@@ -20,7 +20,7 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error", "ea_attention_cuda_noalloc",
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
-           "ea_kernel_timing", "ea_attention_cuda_paged")
+           "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -54,6 +54,15 @@ class PartialsArgs(ctypes.Structure):
 class WidePartialsArgs(ctypes.Structure):
     """ea_wide_partials_t (include/exactattn_cuda.h)."""
     _fields_ = [("maxv", ctypes.c_void_p), ("sumv", ctypes.c_void_p)]
+
+
+class KvAppendArgs(ctypes.Structure):
+    """ea_kv_append_t (include/exactattn_cuda.h)."""
+    _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p), ("page_table", ctypes.c_void_p),
+                ("seq_lens", ctypes.c_void_p), ("new_k", ctypes.c_void_p), ("new_v", ctypes.c_void_p),
+                ("k_meta", ctypes.c_void_p), ("batch", ctypes.c_int64), ("kv_heads", ctypes.c_int),
+                ("page_size", ctypes.c_int), ("max_pages", ctypes.c_int), ("n_new", ctypes.c_int),
+                ("d", ctypes.c_int), ("advance_lens", ctypes.c_int)]
 
 
 def load(path: str | None = None):
@@ -100,6 +109,8 @@ def load(path: str | None = None):
                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, P, ctypes.c_int,
                                             P, ctypes.c_int, ctypes.c_int, P, P, P]
     lib.ea_attention_cuda_paged.restype = ctypes.c_int
+    lib.ea_kv_append_cuda.argtypes = [ctypes.POINTER(KvAppendArgs), P]
+    lib.ea_kv_append_cuda.restype = ctypes.c_int
     lib.ea_kernel_timing.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]
     lib.ea_kernel_timing.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]

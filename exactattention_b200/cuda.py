@@ -276,6 +276,28 @@ def finalize_partials(parts: Partials, max_row_keys: int, out="bf16", stats=None
     return o, fl
 
 
+def kv_append(k_cache, v_cache, page_table, seq_lens, new_k, new_v, k_meta=None, advance_lens=True,
+              stream=None) -> None:
+    """Appends new_k / new_v (batch, kv_heads, n_new, d) at positions seq_lens[b] .. of the paged
+    caches (pages, kv_heads, page_size, d), through ea_kv_append_cuda; optionally fills k_meta
+    (pages, kv_heads, page_size) uint32 (max |k| bits | min nonzero |k| bits << 16) and advances
+    seq_lens. All tensors on one CUDA device; no host synchronisation."""
+    import torch
+
+    a = _lib.KvAppendArgs()
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.page_table, a.seq_lens = page_table.data_ptr(), seq_lens.data_ptr()
+    a.new_k, a.new_v = new_k.contiguous().data_ptr(), new_v.contiguous().data_ptr()
+    a.k_meta = _ptr(k_meta)
+    a.batch, a.kv_heads, a.n_new, a.d = new_k.shape[0], new_k.shape[1], new_k.shape[2], new_k.shape[3]
+    a.page_size, a.max_pages = k_cache.shape[2], page_table.shape[1]
+    a.advance_lens = int(advance_lens)
+    dev = k_cache.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_kv_append_cuda(ctypes.byref(a), ctypes.c_void_p(_stream(dev, stream))),
+                   "ea_kv_append_cuda")
+
+
 def kernel_timing(mode: int) -> tuple[float, int]:
     """ea_kernel_timing: 1 on, 2 collect (summed ms of the tier-1 kernel, launch count), 0 off."""
     ms, n = ctypes.c_double(0), ctypes.c_int64(0)

@@ -55,6 +55,30 @@ int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_heads, int d
                             float alpha, const int32_t* page_table, int max_pages, const int32_t* seq_lens,
                             int fp32_out, int splits, void* out, uint8_t* flags, int64_t* stats);
 
+/* KV-cache write path (paged storage, the layout of EA_MASK_PAGED): append n_new tokens of every
+ * (sequence b, kv head h) at positions seq_lens[b] .. seq_lens[b] + n_new - 1; the pages those
+ * positions fall in must already be in page_table (the caller's page allocator assigns them).
+ * new_k, new_v: (batch, kv_heads, n_new, d) bf16 bits, device pointers, 16-byte aligned; d a
+ * multiple of 8 up to 128. advance_lens != 0 adds n_new to seq_lens after the copy (same
+ * stream). k_meta (optional, (pages, kv_heads, page_size) uint32): per written key, the largest
+ * |k| as bf16 magnitude bits (>= 0x7F80: NaN / inf in the row) | the smallest nonzero |k| << 16
+ * (0xFFFF: all zero). The reference slices its cache into int8 planes at this point
+ * (triton_kernels.py:1183-1268, 1,053 bytes per key); this library keeps bf16 rows and slices in
+ * the kernels. Asynchronous on `stream`. */
+typedef struct ea_kv_append {
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+  const int32_t* page_table; /* (batch, max_pages) */
+  int32_t* seq_lens;         /* (batch,) */
+  const uint16_t* new_k;
+  const uint16_t* new_v;
+  uint32_t* k_meta; /* optional */
+  int64_t batch;
+  int kv_heads, page_size, max_pages, n_new, d;
+  int advance_lens;
+} ea_kv_append_t;
+int ea_kv_append_cuda(const ea_kv_append_t* args, void* stream);
+
 /* RN-even of (a / b) * 2^E into fp32 (fp32 != 0) or bf16; a, b given as (hi, lo) 64-bit
  * halves. Mirrors the reference's test export ea_round_ratio
  * (csrc/exact_attention_cpu.cpp:630-638); evaluated on the GPU. */

@@ -29,7 +29,9 @@ def test_library_exports_every_declared_symbol(cuda_lib):
     assert set(_lib.EXPORTS) <= names
 
 
-@pytest.mark.parametrize("ctype,mirror", [("ea_launch_t", _lib.LaunchArgs), ("ea_partials_t", _lib.PartialsArgs)])
+@pytest.mark.parametrize("ctype,mirror", [("ea_launch_t", _lib.LaunchArgs), ("ea_partials_t", _lib.PartialsArgs),
+                                          ("ea_wide_partials_t", _lib.WidePartialsArgs),
+                                          ("ea_kv_append_t", _lib.KvAppendArgs)])
 def test_struct_layout_matches_header(cuda_lib, tmp_path, ctype, mirror):
     """The ctypes mirrors of the header's structs have the C compiler's size and field offsets."""
     import subprocess
