@@ -287,7 +287,8 @@ def kv_append(k_cache, v_cache, page_table, seq_lens, new_k, new_v, k_meta=None,
     a = _lib.KvAppendArgs()
     a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
     a.page_table, a.seq_lens = page_table.data_ptr(), seq_lens.data_ptr()
-    a.new_k, a.new_v = new_k.contiguous().data_ptr(), new_v.contiguous().data_ptr()
+    nk, nv = new_k.contiguous(), new_v.contiguous()  # kept alive until the launch is enqueued
+    a.new_k, a.new_v = nk.data_ptr(), nv.data_ptr()
     a.k_meta = _ptr(k_meta)
     a.batch, a.kv_heads, a.n_new, a.d = new_k.shape[0], new_k.shape[1], new_k.shape[2], new_k.shape[3]
     a.page_size, a.max_pages = k_cache.shape[2], page_table.shape[1]
