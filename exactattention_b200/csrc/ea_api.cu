@@ -243,8 +243,8 @@ static void build_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
 }
 
 static bool tc_shape(const ea_launch_t* a) {
-  return a->block_rows && a->nblocks > 0 && a->d == 128 && a->dv == 128 && !a->fp32_out &&
-         ((uintptr_t)a->q & 15) == 0 && ((uintptr_t)a->k & 15) == 0;
+  return a->block_rows && a->nblocks > 0 && a->d == 128 && a->dv == 128 && ((uintptr_t)a->q & 15) == 0 &&
+         ((uintptr_t)a->k & 15) == 0;
 }
 
 static bool tc_applicable(const ea_launch_t* a) {
@@ -509,7 +509,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
       }
     }
   }
-  if (!decode && kv_len_h && d == 128 && dv == 128 && !fp32_out && splits == 1 && rows < (1ll << 31)) {
+  if (!decode && kv_len_h && d == 128 && dv == 128 && splits == 1 && rows < (1ll << 31)) {
     std::vector<int32_t> order(rows);
     for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
     std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {

@@ -606,15 +606,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
   } else {
     const int st = S.rst[r];
-    uint32_t outw[16];
-    bool ok = ok_wait && st == ST_OK && !P.fp32;
+    const int prec = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+    uint32_t outw[16];  // bf16 results, two per word (fp32 results are recomputed when stored)
+    bool ok = ok_wait && st == ST_OK;
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
       Rnd x = rnd_zero();
       const int ve = S.ve[32 * u4 + c];
       if (ok && R != R_EMPTY && ve != INT32_MIN)
         ok &= certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z,
-                               Z + (int64_t)Zerr, (int64_t)R - FZ, BF16_P, BF16_QMIN, 127, x);
+                               Z + (int64_t)Zerr, (int64_t)R - FZ, prec, qmin, 127, x);
       const uint32_t b = rnd_to_bf16_bits(x);
       if (c & 1) outw[c >> 1] |= b << 16;
       else outw[c >> 1] = b;
@@ -624,9 +625,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     if (myrow >= 0) {
       const bool rowok = S.rok[r] != 0;
       if (st == ST_DOMAIN) {
-        uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 32 * u4);
+        if (P.fp32) {
+          uint4* o = (uint4*)((uint32_t*)P.out + (int64_t)myrow * DV + 32 * u4);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) o[q4] = make_uint4(0, 0, 0, 0);
+          for (int q8 = 0; q8 < 8; ++q8) o[q8] = make_uint4(0, 0, 0, 0);
+        } else {
+          uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 32 * u4);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) o[q4] = make_uint4(0, 0, 0, 0);
+        }
         if (u4 == 0) {
           P.flags[myrow] = 2;
           stat_add(P, STAT_DOMAIN_ROWS, 1);
@@ -636,6 +643,25 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           push_tier3(P, myrow);
           stat_add(P, STAT_TIER3_ROWS, 1);
         }
+      } else if (P.fp32) {
+        // every channel certified: round again, now keeping the fp32 results (4 per store)
+        uint32_t* o = (uint32_t*)P.out + (int64_t)myrow * DV + 32 * u4;
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          uint32_t f[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = 4 * c4 + u;
+            Rnd x = rnd_zero();
+            const int ve = S.ve[32 * u4 + c];
+            if (R != R_EMPTY && ve != INT32_MIN)
+              certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z, Z + (int64_t)Zerr,
+                               (int64_t)R - FZ, FP32_P, FP32_QMIN, 127, x);
+            f[u] = rnd_to_f32_bits(x);
+          }
+          *(uint4*)(o + 4 * c4) = make_uint4(f[0], f[1], f[2], f[3]);
+        }
+        if (u4 == 0) P.flags[myrow] = 0;
       } else {
         uint4* o = (uint4*)((uint16_t*)P.out + (int64_t)myrow * DV + 32 * u4);
 #pragma unroll

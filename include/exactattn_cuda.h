@@ -123,9 +123,9 @@ typedef struct ea_launch {
   uint8_t* flags; /* (rows,) */
   int64_t* stats; /* EA_STATS_LEN int64 counters, accumulated; may be NULL */
   /* optional, RANGE and HYBRID masks: every row in one of the blocks of 128 rows that share
-   * kv_base (-1 pads a block), (nblocks, 128) int32. With it, d = dv = 128 and bf16 output, the
-   * tensor-core kernel runs (RANGE: when splits == 1; HYBRID: over the range part, with the
-   * per-row lists on the CUDA cores); any grouping gives the same bits. */
+   * kv_base (-1 pads a block), (nblocks, 128) int32. With it and d = dv = 128 (bf16 or fp32
+   * output), the tensor-core kernel runs (RANGE: when splits == 1; HYBRID: over the range part,
+   * with the per-row lists on the CUDA cores); any grouping gives the same bits. */
   const int32_t* block_rows;
   int64_t nblocks;
   /* optional, RANGE masks (decode): segments of up to 8 rows that share kv_base (-1 pads),

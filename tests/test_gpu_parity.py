@@ -449,3 +449,31 @@ def test_tensor_core_hybrid_tree_mask(ea):
     for r in (0, 5, nodes - 1, nodes + 7):
         keys = np.concatenate([np.arange(P), tails[r]])
         assert np.array_equal(out[r], exact.attention_row(Q[r], K[keys], V[keys], alpha)), r
+
+
+def test_tensor_core_prefill_fp32_output(ea):
+    """fp32 outputs from the tensor-core prefill kernel equal the CUDA-core kernel's and the
+    oracle's."""
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(3232)
+    S = 260
+    Q, K, V, kb, kl = _causal_case(rng, S, "outlier", "wide")
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st, out="fp32",
+                             blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), out="fp32")
+    torch.cuda.synchronize()
+    assert st.cpu().numpy()[7] == int(kl.sum()), "the tensor-core kernel did not run"
+    assert torch.equal(f_tc, f_s) and torch.equal(o_tc, o_s)
+    out = o_tc.cpu().numpy().view(np.uint32)
+    for r in (0, 9, S - 1, 2 * S - 1):
+        L = int(kl[r])
+        exp = exact.attention_row(Q[r], K[:L], V[:L], alpha, out="fp32")
+        assert np.array_equal(out[r], np.asarray(exp).view(np.uint32)), r
