@@ -75,3 +75,21 @@ def default_alpha(d: int) -> np.float32:
         if a == b:
             return np.float32(a[0] * 2.0 ** a[1])
         w *= 2
+
+
+@lru_cache(maxsize=None)
+def alpha_for(scaling: float) -> np.float32:
+    """alpha = RN_fp32(scaling / ln 2) for a model's softmax scaling (a double), decided exactly:
+    the base-2 logit multiplier that makes 2^(alpha s) the model's exp(scaling s) up to rounding
+    (the reference's scripts/validate_model.py:35-40 `alpha_for`)."""
+    num, den = float(scaling).as_integer_ratio()
+    if num <= 0:
+        raise ValueError("scaling must be positive")
+    w = 96
+    while True:
+        lo, hi = _ln2_bounds(w)
+        a = _rn_fp32_ratio(num << w, den * hi)
+        b = _rn_fp32_ratio(num << w, den * lo)
+        if a == b:
+            return np.float32(a[0] * 2.0 ** a[1])
+        w *= 2
