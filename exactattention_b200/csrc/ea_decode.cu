@@ -27,6 +27,7 @@
 #include <stdint.h>
 
 #include "ea_core.cuh"
+#include "ea_fast64.cuh"
 #include "ea_numerics.h"
 #include "ea_tables.cuh"
 #include "ea_tc_common.cuh"
@@ -392,6 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   const uint32_t tmem = S.tmem;
   unsigned n_exact = 0, n_wide = 0;
   bool ok_wait = true;
+  const double am_d = (double)P.am;
   // consumer state (rows h, h + NWGC, .. of channel c), live until the partials are written
   const int h = warp >> 2, c = 32 * (warp & 3) + lane;
   // Fraction bits of this CTA's Z and N windows: the headroom only has to cover the split's own
@@ -737,11 +739,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
               const uint32_t hi3[3] = {(uint32_t)G4, (uint32_t)G5, (uint32_t)G6};
               const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
               const bool qlossy = (S.qlossy[g][0] | S.qlossy[g][1] | S.qlossy[g][2] | S.qlossy[g][3]) != 0;
-              Rnd t = rnd_zero();
-              int ls;
+              const int sexp = S.qlsb[g] + S.klsb[key];
+              uint32_t fb;
+              bool done = false, differ = false;
+              uint64_t err = 0;
               if (qlossy || klossy) {
                 // |q k - Q K| <= |dq| |k| + |Q| |dk| over the lossy elements (units 2^(qlsb + klsb))
-                uint64_t err = 0;
                 for (int wd = 0; wd < 4; ++wd) {
                   const uint32_t ql = S.qlossy[g][wd], kl = S.klossy[key][wd];
                   for (uint32_t m = ql; m; m &= m - 1) {
@@ -755,13 +758,23 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
                     err += (uint64_t)(qf < 0 ? -qf : qf);
                   }
                 }
-                ls = logit_bounded(acc, err, S.qlsb[g] + S.klsb[key], P.am, P.ae, t);
+                done = f64::logit_interval_f64(acc, err, sexp, am_d, P.ae, fb, differ);
               } else {
-                ls = logit_exact64(acc, S.qlsb[g] + S.klsb[key], P.am, P.ae, t);
+                done = f64::logit_f64(acc, sexp, am_d, P.ae, fb);
               }
-              if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
-              else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
-              else atomicMax(&S.rst[g], ST_DOMAIN);
+              // the binary64 fast path first; the integer evaluation decides what it cannot certify
+              if (done) {
+                out = fb;
+              } else if (differ) {
+                out = T_UNCERT;
+              } else {
+                Rnd t = rnd_zero();
+                const int ls = (qlossy || klossy) ? logit_bounded(acc, err, sexp, P.am, P.ae, t)
+                                                  : logit_exact64(acc, sexp, P.am, P.ae, t);
+                if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
+                else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
+                else atomicMax(&S.rst[g], ST_DOMAIN);
+              }
             }
           }
           sT[g * BK + key] = out;
@@ -824,16 +837,30 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         uint64_t W = 0;
         uint32_t lw = 0;
         if (tb != T_MASKED && Rt != INT32_MIN) {
-          const Rnd t = rnd_from_f32(tb);
           uint32_t M;
           int64_t E;
-          int ws = weight_from_logit(t, g_ta64, g_tb64, M, E);  // 2 x 2 KB tables, L1-resident
-          if (ws == W_RISKY) {
-            ++n_wide;
-            ws = wide_weight(t, M, E);
+          int ws = W_OK;
+          const float tf = __uint_as_float(tb);
+          int32_t Ef;
+          // w < 2^(t + 1) <= 2^(Rt - 48): W = 0, a truncated (nonzero) weight
+          const bool tiny = tf > -1073741824.0f && (double)tf < (double)Rt - 49.0;
+          if (tiny) {
+            M = 0;
+            E = 0;
+          } else if (f64::weight_f64(tb, f64::g_exp2_d64, M, Ef)) {  // 2 KB table, L1-resident
+            E = Ef;
+          } else {
+            const Rnd t = rnd_from_f32(tb);
+            ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
+            if (ws == W_RISKY) {
+              ++n_wide;
+              ws = wide_weight(t, M, E);
+            }
           }
           if (ws != W_OK) {
             atomicMax(&S.rst[g], ST_TIER3);  // |t| >= 2^30 or a still-risky weight
+          } else if (tiny) {
+            lw = 1;
           } else {
             const int sh = (int)(E + FW - Rt);
             if (sh >= 0) {

@@ -1,0 +1,112 @@
+// Certified binary64 fast paths of the two per-pair roundings (device only):
+//   logit   t = RN32(alpha * s) for an exactly known integer score s = acc * 2^sexp
+//   weight  w = RN24(2^t) for an fp32 logit t
+// Each evaluates the real value in binary64 with a proven error bound and returns the rounded
+// result only when no rounding midpoint lies within that bound of the computed value; otherwise
+// it returns false and the caller takes the exact integer path (logit_exact64 / logit_from_interval,
+// weight_from_logit). A certified result therefore equals the exact one: the fast paths change
+// how fast the bits are found, never which bits.
+//
+// Rounding to p bits from binary64 drops 53 - p significand bits. For p = 24 those are the low 29
+// bits, all in the low word; their distance from the midpoint 2^28, in units of the binary64 ulp,
+// is compared with the bound (MARGIN ulps). Within a binade the rounding is monotone and its
+// result only changes at midpoints, so a computed value y with |y - x| <= bound and a distance
+// above the bound rounds as x does (also when x lies in the neighbouring binade: the midpoints
+// next to a power of two are 2^-25 relative away from it).
+#pragma once
+#include <stdint.h>
+
+#include "ea_numerics.h"
+#include "exp2_tables.h"
+
+namespace ea {
+namespace f64 {
+
+static __device__ const uint64_t g_exp2_d64[256] = EA_EXP2_D64_INIT;
+
+constexpr int MARGIN = 4;  // ulps; both error bounds below are under 2.1 ulps
+
+// distance of the dropped 29 bits (low word `lo`) from their midpoint, signed
+__device__ __forceinline__ int32_t mid_dist29(uint32_t lo) { return (int32_t)(lo & 0x1FFFFFFFu) - 0x10000000; }
+__device__ __forceinline__ bool clear_of_mid(int32_t d) { return d > MARGIN || d < -MARGIN; }
+
+// The alpha of a launch as a binary64 (am exact: |am| < 2^24).
+__device__ __forceinline__ double alpha_mantissa(int32_t am) { return (double)am; }
+
+// t = RN32(am 2^ae * acc 2^sexp) as fp32 bits, for a normal fp32 result.
+//   x = RN64(RN64(acc) * am) * 2^(ae + sexp): two roundings of relative size <= 2^-53 each, so
+//   |x - t_exact| <= (2^-52 + 2^-106) |t_exact| < 2.01 ulps of x (the power of two is applied to
+//   the exponent field, exactly). am != 0.
+__device__ __forceinline__ bool logit_f64(int64_t acc, int sexp, double am_d, int32_t ae, uint32_t& bits) {
+  if (acc == 0) {
+    bits = 0u;
+    return true;
+  }
+  const double x = __dmul_rn(__ll2double_rn(acc), am_d);
+  const uint32_t hi = (uint32_t)__double2hiint(x), lo = (uint32_t)__double2loint(x);
+  const int32_t e32 = (int32_t)((hi >> 20) & 0x7FFu) - (1023 - 127) + ae + sexp;  // biased fp32 exponent
+  const int32_t d = mid_dist29(lo);
+  if (e32 < 1 || e32 > 253 || !clear_of_mid(d)) return false;
+  const uint32_t mant = ((hi & 0xFFFFFu) << 3) | (lo >> 29);
+  bits = (hi & 0x80000000u) | (((uint32_t)e32 << 23) + mant + (d > 0 ? 1u : 0u));
+  return true;
+}
+
+// The score interval [acc - err, acc + err] * 2^sexp: certified when both ends are and round to
+// the same fp32 value; `differ` reports two certified, different ends (an uncertified logit).
+__device__ __forceinline__ bool logit_interval_f64(int64_t acc, uint64_t err, int sexp, double am_d, int32_t ae,
+                                                   uint32_t& bits, bool& differ) {
+  uint32_t b0, b1;
+  differ = false;
+  if (!logit_f64(acc - (int64_t)err, sexp, am_d, ae, b0) || !logit_f64(acc + (int64_t)err, sexp, am_d, ae, b1))
+    return false;
+  differ = b0 != b1;
+  bits = b0;
+  return !differ;
+}
+
+// w = RN24(2^t) = M 2^E (2^23 <= M < 2^24) for the fp32 logit with bits tb, |t| < 2^22.
+//   |t| < 2^-27: w = 1 (2^t lies strictly inside the rounding interval of 1).
+//   J = floor(256 t), n = floor(t) = J >> 8, j = J mod 256, r = t - J / 256 in [0, 2^-8) (exact:
+//   t is a multiple of 2^-50 here). 2^t = 2^n * 2^(j/256) * 2^r with
+//   p = r (c1 + r (c2 + r (c3 + r (c4 + r c5)))) ~ 2^r - 1 (Taylor to degree 5; remainder
+//   < 2^-60.7) and y = RN(T_j + T_j p), T_j = RN64(2^(j/256)):
+//     |p - (2^r - 1)| < 2^-8.53 * 2.74 * 2^-53 + 2^-60.7 < 2^-59.3
+//     |y - 2^(j/256 + r)| < 2^-53 * (1 + 2^-8.5) + 2 * 2^-59.3 + 2^-53 < 2.1 * 2^-53 (1.05 ulps)
+//   and y < 2 (2^f <= 2^(1 - 2^-50) < 2 - 2^-49.4).
+__device__ __forceinline__ bool weight_f64(uint32_t tb, const uint64_t* tab, uint32_t& M, int32_t& E) {
+  const float tf = __uint_as_float(tb);
+  const float at = fabsf(tf);
+  if (!(at < 4194304.0f)) return false;  // |t| >= 2^22, or NaN
+  if (at < 7.450580596923828125e-9f) {    // 2^-27
+    M = 1u << 23;
+    E = -23;
+    return true;
+  }
+  const double t = (double)tf;
+  constexpr double K = 6755399441055744.0;  // 1.5 * 2^52: its low word is zero
+  const double u = __fma_rd(t, 256.0, K);  // K + floor(256 t), exactly
+  const int32_t J = (int32_t)__double2loint(u);
+  const double r = __fma_rn(u - K, -0.00390625, t);
+  double p = __fma_rn(r, __longlong_as_double((long long)EA_EXP2_C5), __longlong_as_double((long long)EA_EXP2_C4));
+  p = __fma_rn(r, p, __longlong_as_double((long long)EA_EXP2_C3));
+  p = __fma_rn(r, p, __longlong_as_double((long long)EA_EXP2_C2));
+  p = __fma_rn(r, p, __longlong_as_double((long long)EA_EXP2_C1));
+  p = __dmul_rn(r, p);
+  const double T = __longlong_as_double((long long)tab[J & 255]);
+  const double y = __fma_rn(T, p, T);
+  const uint32_t hi = (uint32_t)__double2hiint(y), lo = (uint32_t)__double2loint(y);
+  const int32_t d = mid_dist29(lo);
+  if (!clear_of_mid(d)) return false;
+  uint32_t m = ((1u << 23) | ((hi & 0xFFFFFu) << 3) | (lo >> 29)) + (d > 0 ? 1u : 0u);
+  E = (J >> 8) - 23 + (int32_t)((hi >> 20) & 0x7FFu) - 1023;
+  if (m == (1u << 24)) {
+    m = 1u << 23;
+    E += 1;
+  }
+  M = m;
+  return true;
+}
+
+}  // namespace f64
+}  // namespace ea

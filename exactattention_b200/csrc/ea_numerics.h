@@ -205,22 +205,26 @@ EA_HD int logit_from_interval(int64_t acc, uint64_t err, int sexp, int32_t am, i
   return LOGIT_OK;
 }
 
-// t = RN32(alpha * acc * 2^sexp) for an exactly known score (err == 0), in 64-bit arithmetic:
-// with L = bitlen(|acc|), the top min(L, 40) bits A of |acc| times |am| < 2^24 fit in 64 bits;
-// the bits of |acc| below A only act as a sticky bit, because they change the product by less
-// than 2^24 units of A's last bit, while the rounding point lies at least 39 bits above it.
+// Exact product of a 128-bit magnitude and a 64-bit one (at most 192 bits), rounded: when it
+// exceeds 128 bits its low 64 bits act only as a sticky bit (the rounding point lies far above
+// them, and they are the exact low bits of the product, so nothing carries out of them).
+EA_HD Rnd round_mul128(u128 a, uint64_t m, int E, int neg, int p, int qmin, int emax) {
+  const u128 lo = (u128)(uint64_t)a * m, hi = (u128)(uint64_t)(a >> 64) * m;
+  const u128 mid = (lo >> 64) + (u128)(uint64_t)hi;  // < 2^65
+  const uint64_t w0 = (uint64_t)lo, w1 = (uint64_t)mid, w2 = (uint64_t)(hi >> 64) + (uint64_t)(mid >> 64);
+  if (w2 == 0) return round_u128(((u128)w1 << 64) | w0, E, neg, p, qmin, emax);
+  return round_u128(((u128)w2 << 64) | w1, E + 64, neg, p, qmin, emax, w0 != 0);
+}
+
+// t = RN32(alpha * acc * 2^sexp) for an exactly known score (err == 0): the exact product
+// |acc| |am| (< 2^87) rounded once. (Dropping low bits of |acc| before the multiplication would
+// not be exact: their product with am can carry across the rounding midpoint.)
 EA_HD int logit_exact64(int64_t acc, int sexp, int32_t am, int32_t ae, Rnd& t) {
   if (am == 0 || acc == 0) {
     t = rnd_zero();
     return LOGIT_OK;
   }
-  const uint64_t a = uabs64(acc);
-  const int L = bitlen64(a);
-  const int drop = L > 40 ? L - 40 : 0;
-  const uint64_t top = a >> drop;
-  const bool sticky = drop ? (a & ((1ull << drop) - 1)) != 0 : false;
-  const uint64_t P = top * uabs64(am);  // < 2^64
-  t = round_u64(P, ae + sexp + drop, (am < 0) != (acc < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  t = round_u128((u128)uabs64(acc) * uabs64(am), ae + sexp, (am < 0) != (acc < 0), FP32_P, FP32_QMIN, FP32_EMAX);
   if (t.ovf) return LOGIT_OVERFLOW;
   if (t.q == 0) t.neg = 0;
   return LOGIT_OK;
@@ -484,11 +488,7 @@ EA_HD int logit_i128(i128 S, int E, int32_t am, int32_t ae, Rnd& t) {
   }
   const int neg = (S < 0) != (am < 0);
   const u128 a = S < 0 ? (u128)(-S) : (u128)S;
-  const int L = bitlen128(a);
-  const int drop = L > 40 ? L - 40 : 0;
-  const uint64_t top = (uint64_t)(a >> drop);
-  const bool sticky = drop ? (a & (((u128)1 << drop) - 1)) != 0 : false;
-  t = round_u64(top * uabs64(am), ae + E + drop, neg, FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  t = round_mul128(a, uabs64(am), ae + E, neg, FP32_P, FP32_QMIN, FP32_EMAX);
   if (t.ovf) return LOGIT_OVERFLOW;
   if (t.q == 0) t.neg = 0;
   return LOGIT_OK;
@@ -551,15 +551,26 @@ EA_HD int logit_exact(ExactScore& s, int32_t am, int32_t ae, Rnd& t) {
     t = rnd_zero();
     return LOGIT_OK;
   }
-  // take the top 64 bits (aligned at the leading bit) and a sticky bit for the rest
-  int lb = 31 - (bitlen64(mag[top]) - 1);   // leading zeros in the top digit
-  uint64_t w2 = (uint64_t)mag[top] << 32 | (top >= 1 ? mag[top - 1] : 0u);
-  uint32_t w0 = top >= 2 ? mag[top - 2] : 0u;
+  // the exact product |S| |am| in 32-bit digits (one more digit than S), then its top 64 bits
+  // (aligned at the leading bit) with a sticky bit for the exact bits below them
+  uint32_t prod[SCORE_BINS + 1];
+  const uint64_t am_mag = uabs64(am);
+  uint64_t cy = 0;
+  for (int i = 0; i <= top; ++i) {
+    const uint64_t x = (uint64_t)mag[i] * am_mag + cy;  // < 2^56 + 2^24
+    prod[i] = (uint32_t)x;
+    cy = x >> 32;
+  }
+  int ptop = top;
+  if (cy) prod[++ptop] = (uint32_t)cy;
+  int lb = 31 - (bitlen64(prod[ptop]) - 1);   // leading zeros in the top digit
+  uint64_t w2 = (uint64_t)prod[ptop] << 32 | (ptop >= 1 ? prod[ptop - 1] : 0u);
+  uint32_t w0 = ptop >= 2 ? prod[ptop - 2] : 0u;
   uint64_t hi64 = lb ? (w2 << lb) | ((uint64_t)w0 >> (32 - lb)) : w2;
   bool sticky = (lb ? (uint32_t)(w0 << lb) != 0u : w0 != 0u);
-  for (int i = top - 3; i >= 0 && !sticky; --i) sticky = mag[i] != 0u;
-  int e_hi = (top - 1) * 32 - lb - SCORE_BIAS;  // exponent of hi64's last bit
-  t = round_u128((u128)uabs64(am) * hi64, ae + e_hi, neg != (am < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
+  for (int i = ptop - 3; i >= 0 && !sticky; --i) sticky = prod[i] != 0u;
+  int e_hi = (ptop - 1) * 32 - lb - SCORE_BIAS;  // exponent of hi64's last bit
+  t = round_u64(hi64, ae + e_hi, neg != (am < 0), FP32_P, FP32_QMIN, FP32_EMAX, sticky);
   if (t.ovf) return LOGIT_OVERFLOW;
   if (t.q == 0) t.neg = 0;
   return LOGIT_OK;

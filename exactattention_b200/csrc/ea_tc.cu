@@ -25,6 +25,7 @@
 #include <stdint.h>
 
 #include "ea_core.cuh"
+#include "ea_fast64.cuh"
 #include "ea_numerics.h"
 #include "ea_tables.cuh"
 #include "ea_tc_common.cuh"
@@ -74,8 +75,7 @@ struct Small {
   int32_t vlossy[BN];
   int32_t ve[DV];
   int32_t ve4[4][DV];
-  uint64_t ta[256];
-  uint64_t tb[256];
+  uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
   uint64_t bar;
   uint32_t tmem;
   int32_t maxlen;
@@ -129,10 +129,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     S.rst[tid] = ST_OK;
     S.rok[tid] = 1;
   }
-  if (tid < 256) {
-    S.ta[tid] = g_ta64[tid];
-    S.tb[tid] = g_tb64[tid];
-  }
+  if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
     tc::mbar_init(&S.bar, 1);
     S.base = P.kv_base[block_rows[(int64_t)blk * BM]];
@@ -236,6 +233,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   uint32_t phase = 0;
   bool ok_wait = true;
   unsigned n_exact = 0, n_wide = 0;
+  const double am_d = (double)P.am;
 
   for (int32_t j0 = 0; j0 < maxlen; j0 += BN) {
     // ---------------- K tile -> digit planes (thread: key tid / 8, elements 16 (tid % 8) ..) --------
@@ -374,15 +372,29 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
               const uint32_t hi3[3] = {dg[4][u], dg[5][u], dg[6][u]};
               const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
               const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
-              Rnd t = rnd_zero();
-              int ls;
-              if (qlossy || klossy)
-                ls = logit_bounded(acc, score_err(S, sQ, sK, r, kj), qlsb + S.klsb[kj], P.am, P.ae, t);
-              else
-                ls = logit_exact64(acc, qlsb + S.klsb[kj], P.am, P.ae, t);
-              if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
-              else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
-              else rstat = ST_DOMAIN;
+              const int sexp = qlsb + S.klsb[kj];
+              // binary64 fast path first; the integer evaluation decides what it cannot certify
+              uint32_t fb;
+              bool done = false, differ = false;
+              uint64_t err = 0;
+              if (qlossy || klossy) {
+                err = score_err(S, sQ, sK, r, kj);
+                done = f64::logit_interval_f64(acc, err, sexp, am_d, P.ae, fb, differ);
+              } else {
+                done = f64::logit_f64(acc, sexp, am_d, P.ae, fb);
+              }
+              if (done) {
+                out = fb;
+              } else if (differ) {
+                out = T_UNCERT;
+              } else {
+                Rnd t = rnd_zero();
+                const int ls = (qlossy || klossy) ? logit_bounded(acc, err, sexp, P.am, P.ae, t)
+                                                  : logit_exact64(acc, sexp, P.am, P.ae, t);
+                if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
+                else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
+                else rstat = ST_DOMAIN;
+              }
             }
           }
           sT[r * T_PITCH + kj] = out;
@@ -448,16 +460,31 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const uint32_t tb = sT[r * T_PITCH + kj];
           uint64_t W = 0;
           if (tb != T_MASKED && Rt != INT32_MIN) {
-            const Rnd t = rnd_from_f32(tb);
             uint32_t M;
             int64_t E;
-            int ws = weight_from_logit(t, S.ta, S.tb, M, E);
-            if (ws == W_RISKY) {
-              ++n_wide;
-              ws = wide_weight(t, M, E);
+            int ws = W_OK;
+            const float tf = __uint_as_float(tb);
+            int32_t Ef;
+            // w < 2^(t + 1) <= 2^(Rt - 48): W = 0, a truncated (nonzero) weight
+            const bool tiny = tf > -1073741824.0f && (double)tf < (double)Rt - 49.0;
+            if (tiny) {
+              M = 0;
+              E = 0;
+            } else if (f64::weight_f64(tb, S.td, M, Ef)) {
+              E = Ef;
+            } else {
+              const Rnd t = rnd_from_f32(tb);
+              ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
+              if (ws == W_RISKY) {
+                ++n_wide;
+                ws = wide_weight(t, M, E);
+              }
             }
             if (ws != W_OK) {
               rstat = ST_TIER3;
+            } else if (tiny) {
+              ++nlw;
+              if (S.vlossy[kj]) vwsum += 1;
             } else {
               const int sh = (int)(E + FW - Rt);
               if (sh >= 0) {

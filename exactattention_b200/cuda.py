@@ -306,6 +306,13 @@ def kernel_timing(mode: int) -> tuple[float, int]:
     return ms.value, n.value
 
 
+def selftest_fast64(mode: int, seed: int, n: int, stride: int = 1) -> tuple[int, int, int, int]:
+    """ea_selftest_fast64: (cases, certified by the binary64 fast path, mismatches, a bad input)."""
+    out = (ctypes.c_int64 * 4)()
+    _lib.check(_lib.load().ea_selftest_fast64(mode, seed, stride, n, out), "ea_selftest_fast64")
+    return tuple(int(x) for x in out)
+
+
 def reserve_workspace(rows: int, splits: int, dv: int) -> None:
     _lib.check(_lib.load().ea_reserve_workspace(rows, splits, dv), "ea_reserve_workspace")
 

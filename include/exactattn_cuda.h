@@ -211,6 +211,14 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* parts, const int64_
  * stream around that kernel. No reference counterpart (a measurement hook of this library). */
 int ea_kernel_timing(int mode, double* total_ms, int64_t* launches);
 
+/* Self-test of the binary64 fast paths of the per-pair roundings against their exact integer
+ * evaluations, on the current device (no reference counterpart: the reference has one exact
+ * evaluation). mode 0: weights RN24(2^t) for n logits t, fp32 bit patterns from `seed` with step
+ * `stride`, both signs, |t| < 2^22; mode 1: logits RN32(alpha s) for n splitmix64 cases from
+ * `seed`. out[0..3] = cases, cases the fast path certified, mismatches (must be 0), the input of
+ * a mismatch. Returns 0, or -1 / -4 for bad arguments / a CUDA error. */
+int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int64_t n, int64_t* out);
+
 /* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
  * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,
  * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the

@@ -116,8 +116,8 @@ def test_logit_interval_exact_point(P):
 
 
 def test_logit_exact64_matches_oracle(P):
-    """The 64-bit fast path (top 40 bits of the score and a sticky bit) rounds like the exact
-    product, including the subnormal range, ties and overflow."""
+    """The exact-product rounding of a 64-bit score, including the subnormal range, ties and
+    overflow."""
     rng = np.random.default_rng(12)
     for alpha in (exact.default_alpha(128), np.float32(0.0883883), np.float32(-3.5e-39), np.float32(1.7e38)):
         am, ae = exact.decode_fp32(alpha)
@@ -134,6 +134,42 @@ def test_logit_exact64_matches_oracle(P):
                 assert st == 0 and tb.value == _bits(m, e), (acc, sexp)
             except exact.ExactAttentionDomainError:
                 assert st == 2
+
+
+def _carry_cases(am, n, seed):
+    """Scores whose product with am rounds differently when the bits of the score below its top
+    40 are dropped before the multiplication (kept only as a sticky bit): the dropped part times
+    am carries across the rounding midpoint. These need the exact product."""
+    rng = np.random.default_rng(seed)
+    out = []
+    a = abs(am)
+    while len(out) < n:
+        acc = int(rng.integers(1 << 54, 1 << 62)) | 1
+        drop = acc.bit_length() - 40
+        top = acc >> drop
+        p_top, p_ex = top * a, acc * a
+        sh_t = p_top.bit_length() - 24
+        sh_e = p_ex.bit_length() - 24
+        rt = (p_top >> sh_t) + (((p_top >> (sh_t - 1)) & 1) if sh_t > 0 else 0)
+        re = (p_ex >> sh_e) + (((p_ex >> (sh_e - 1)) & 1) if sh_e > 0 else 0)
+        if rt << (sh_t + drop) != re << sh_e:
+            out.append(acc)
+    return out
+
+
+def test_logit_exact64_carry_across_midpoint(P):
+    alpha = exact.default_alpha(128)
+    am, ae = exact.decode_fp32(alpha)
+    for acc in _carry_cases(am, 6, 21):
+        for sg in (1, -1):
+            tb = u32()
+            st = P.probe_logit_exact64(sg * acc, -40, exact.f32_to_bits(alpha), tb)
+            m, e = exact.round_dyadic(am * sg * acc, ae - 40, exact.FP32)
+            assert st == 0 and tb.value == _bits(m, e), acc
+            S = sg * acc << 50
+            st = P.probe_logit_i128(S >> 64, S & ((1 << 64) - 1), -90, exact.f32_to_bits(alpha), tb)
+            m, e = exact.round_dyadic(am * S, ae - 90, exact.FP32)
+            assert st == 0 and tb.value == _bits(m, e), acc
 
 
 def test_logit_i128_matches_oracle(P):
