@@ -36,20 +36,18 @@ __device__ __forceinline__ double alpha_mantissa(int32_t am) { return (double)am
 // t = RN32(am 2^ae * acc 2^sexp) as fp32 bits, for a normal fp32 result.
 //   x = RN64(RN64(acc) * am) * 2^(ae + sexp): two roundings of relative size <= 2^-53 each, so
 //   |x - t_exact| <= (2^-52 + 2^-106) |t_exact| < 2.01 ulps of x (the power of two is applied to
-//   the exponent field, exactly). am != 0.
+//   the exponent field, exactly). am != 0. Straight-line code (selects, no branches), so that a
+//   caller's unrolled loop can interleave several evaluations.
 __device__ __forceinline__ bool logit_f64(int64_t acc, int sexp, double am_d, int32_t ae, uint32_t& bits) {
-  if (acc == 0) {
-    bits = 0u;
-    return true;
-  }
   const double x = __dmul_rn(__ll2double_rn(acc), am_d);
   const uint32_t hi = (uint32_t)__double2hiint(x), lo = (uint32_t)__double2loint(x);
   const int32_t e32 = (int32_t)((hi >> 20) & 0x7FFu) - (1023 - 127) + ae + sexp;  // biased fp32 exponent
   const int32_t d = mid_dist29(lo);
-  if (e32 < 1 || e32 > 253 || !clear_of_mid(d)) return false;
   const uint32_t mant = ((hi & 0xFFFFFu) << 3) | (lo >> 29);
-  bits = (hi & 0x80000000u) | (((uint32_t)e32 << 23) + mant + (d > 0 ? 1u : 0u));
-  return true;
+  const uint32_t b = (hi & 0x80000000u) | (((uint32_t)e32 << 23) + mant + (d > 0 ? 1u : 0u));
+  const bool zero = acc == 0;
+  bits = zero ? 0u : b;
+  return zero || (e32 >= 1 && e32 <= 253 && clear_of_mid(d));
 }
 
 // The score interval [acc - err, acc + err] * 2^sexp: certified when both ends are and round to
@@ -74,16 +72,13 @@ __device__ __forceinline__ bool logit_interval_f64(int64_t acc, uint64_t err, in
 //     |p - (2^r - 1)| < 2^-8.53 * 2.74 * 2^-53 + 2^-60.7 < 2^-59.3
 //     |y - 2^(j/256 + r)| < 2^-53 * (1 + 2^-8.5) + 2 * 2^-59.3 + 2^-53 < 2.1 * 2^-53 (1.05 ulps)
 //   and y < 2 (2^f <= 2^(1 - 2^-50) < 2 - 2^-49.4).
+// Straight-line code, as logit_f64.
 __device__ __forceinline__ bool weight_f64(uint32_t tb, const uint64_t* tab, uint32_t& M, int32_t& E) {
   const float tf = __uint_as_float(tb);
   const float at = fabsf(tf);
-  if (!(at < 4194304.0f)) return false;  // |t| >= 2^22, or NaN
-  if (at < 7.450580596923828125e-9f) {    // 2^-27
-    M = 1u << 23;
-    E = -23;
-    return true;
-  }
-  const double t = (double)tf;
+  const bool in_range = at < 4194304.0f;            // |t| < 2^22 (false for NaN)
+  const bool one = at < 7.450580596923828125e-9f;   // |t| < 2^-27: w = 1
+  const double t = (double)(in_range ? tf : 0.0f);
   constexpr double K = 6755399441055744.0;  // 1.5 * 2^52: its low word is zero
   const double u = __fma_rd(t, 256.0, K);  // K + floor(256 t), exactly
   const int32_t J = (int32_t)__double2loint(u);
@@ -97,15 +92,12 @@ __device__ __forceinline__ bool weight_f64(uint32_t tb, const uint64_t* tab, uin
   const double y = __fma_rn(T, p, T);
   const uint32_t hi = (uint32_t)__double2hiint(y), lo = (uint32_t)__double2loint(y);
   const int32_t d = mid_dist29(lo);
-  if (!clear_of_mid(d)) return false;
-  uint32_t m = ((1u << 23) | ((hi & 0xFFFFFu) << 3) | (lo >> 29)) + (d > 0 ? 1u : 0u);
-  E = (J >> 8) - 23 + (int32_t)((hi >> 20) & 0x7FFu) - 1023;
-  if (m == (1u << 24)) {
-    m = 1u << 23;
-    E += 1;
-  }
-  M = m;
-  return true;
+  const uint32_t m = ((1u << 23) | ((hi & 0xFFFFFu) << 3) | (lo >> 29)) + (d > 0 ? 1u : 0u);
+  const bool carry = m == (1u << 24);
+  const int32_t e = (J >> 8) - 23 + (int32_t)((hi >> 20) & 0x7FFu) - 1023 + (carry ? 1 : 0);
+  M = one ? (1u << 23) : (carry ? (1u << 23) : m);
+  E = one ? -23 : e;
+  return in_range && (one || clear_of_mid(d));
 }
 
 }  // namespace f64

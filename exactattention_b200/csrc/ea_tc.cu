@@ -73,6 +73,7 @@ struct Small {
   uint32_t klossy[BN][4];
   int32_t kbad[BN];
   int32_t vlossy[BN];
+  uint32_t kmeta[BN];  // per key, for pass 1: klsb (low 16 bits, signed) | lossy << 16 | bad << 17
   int32_t ve[DV];
   int32_t ve4[4][DV];
   uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
@@ -317,6 +318,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
     EA_PT(1)
 
+    if (tid < BN)
+      S.kmeta[tid] = ((uint32_t)S.klsb[tid] & 0xFFFFu) |
+                     ((S.klossy[tid][0] | S.klossy[tid][1] | S.klossy[tid][2] | S.klossy[tid][3]) ? 1u << 16 : 0u) |
+                     (S.kbad[tid] ? 1u << 17 : 0u);
     // ---------------- score MMAs: 7 groups x 64 columns ----------------
     if (tid == 0) {
       tc::fence_after_sync();
@@ -360,45 +365,57 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
         for (int g = 0; g < NGS; ++g) tc::tmem_ld4(tlane + BN * g + 16 * u4 + 4 * c4, dg[g]);
         tc::tmem_wait_ld();
+        // the binary64 fast path for the four keys (straight-line, interleaved), then the rare keys
+        // it leaves to the integer evaluation: NaN/inf keys, lossy windows, results it cannot certify
+        int64_t acc[4];
+        uint32_t outv[4], slow = 0;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int kj = 16 * u4 + 4 * c4 + u;
+          const uint32_t km = S.kmeta[kj];
+          const uint32_t lo4[4] = {dg[0][u], dg[1][u], dg[2][u], dg[3][u]};
+          const uint32_t hi3[3] = {dg[4][u], dg[5][u], dg[6][u]};
+          acc[u] = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
+          uint32_t fb;
+          const bool ok = f64::logit_f64(acc[u], qlsb + (int32_t)(int16_t)(km & 0xFFFFu), am_d, P.ae, fb);
+          const bool live = myrow >= 0 && j0 + kj < mylen;
+          outv[u] = live ? fb : T_MASKED;
+          if (live && (!ok || qlossy || (km >> 16) != 0)) slow |= 1u << u;
+        }
+        for (uint32_t m = slow; m; m &= m - 1) {
+          const int u = __ffs(m) - 1;
+          const int kj = 16 * u4 + 4 * c4 + u;
+          const uint32_t km = S.kmeta[kj];
           uint32_t out = T_MASKED;
-          if (myrow >= 0 && j0 + kj < mylen) {
-            if (S.kbad[kj]) {
-              rstat = ST_DOMAIN;
+          if ((km >> 17) & 1u) {
+            rstat = ST_DOMAIN;
+          } else {
+            const bool klossy = ((km >> 16) & 1u) != 0;
+            const int sexp = qlsb + (int32_t)(int16_t)(km & 0xFFFFu);
+            uint32_t fb;
+            bool done = false, differ = false;
+            uint64_t err = 0;
+            if (qlossy || klossy) {
+              err = score_err(S, sQ, sK, r, kj);
+              done = f64::logit_interval_f64(acc[u], err, sexp, am_d, P.ae, fb, differ);
+            }
+            if (done) {
+              out = fb;
+            } else if (differ) {
+              out = T_UNCERT;
             } else {
-              const uint32_t lo4[4] = {dg[0][u], dg[1][u], dg[2][u], dg[3][u]};
-              const uint32_t hi3[3] = {dg[4][u], dg[5][u], dg[6][u]};
-              const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
-              const bool klossy = (S.klossy[kj][0] | S.klossy[kj][1] | S.klossy[kj][2] | S.klossy[kj][3]) != 0;
-              const int sexp = qlsb + S.klsb[kj];
-              // binary64 fast path first; the integer evaluation decides what it cannot certify
-              uint32_t fb;
-              bool done = false, differ = false;
-              uint64_t err = 0;
-              if (qlossy || klossy) {
-                err = score_err(S, sQ, sK, r, kj);
-                done = f64::logit_interval_f64(acc, err, sexp, am_d, P.ae, fb, differ);
-              } else {
-                done = f64::logit_f64(acc, sexp, am_d, P.ae, fb);
-              }
-              if (done) {
-                out = fb;
-              } else if (differ) {
-                out = T_UNCERT;
-              } else {
-                Rnd t = rnd_zero();
-                const int ls = (qlossy || klossy) ? logit_bounded(acc, err, sexp, P.am, P.ae, t)
-                                                  : logit_exact64(acc, sexp, P.am, P.ae, t);
-                if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
-                else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
-                else rstat = ST_DOMAIN;
-              }
+              Rnd t = rnd_zero();
+              const int ls = (qlossy || klossy) ? logit_bounded(acc[u], err, sexp, P.am, P.ae, t)
+                                                : logit_exact64(acc[u], sexp, P.am, P.ae, t);
+              if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
+              else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
+              else rstat = ST_DOMAIN;
             }
           }
-          sT[r * T_PITCH + kj] = out;
+          outv[u] = out;
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sT[r * T_PITCH + 16 * u4 + 4 * c4 + u] = outv[u];
       }
       if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
     }
@@ -435,15 +452,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     // ---------------- pass 2: tile bound, weights, W digits ----------------
     {
       // w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1): ceil of the exact fp32 t is exact
-      int32_t rl = INT32_MIN;
+      // (ceil is monotone: the ceiling of the largest logit)
+      float tmax = -INFINITY;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         const uint32_t tb = sT[r * T_PITCH + 16 * u4 + u];
         const float tf = __uint_as_float(tb);
-        if (tb == T_MASKED || !(fabsf(tf) < 1073741824.0f)) continue;  // |t| >= 2^30: tier 3
-        rl = max(rl, __float2int_ru(tf) + 1);
+        if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);  // |t| >= 2^30: tier 3
       }
-      S.rt[u4][r] = rl;
+      S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
     }
     __syncthreads();
     const int32_t Rt = max(max(S.rt[0][r], S.rt[1][r]), max(S.rt[2][r], S.rt[3][r]));
@@ -453,54 +470,66 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       int rstat = ST_OK;
 #pragma unroll 1
       for (int wd = 0; wd < 4; ++wd) {
-        uint32_t wlo[4], whi[4];
+        // the binary64 fast path for the four keys (straight-line, interleaved); the integer
+        // evaluation for the rare ones it leaves (|t| >= 2^22, or too close to a midpoint)
+        uint64_t Wv[4];
+        uint32_t slow = 0, counted = 0;  // keys for the integer path; keys that enter the sums
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int kj = 16 * u4 + 4 * wd + u;
           const uint32_t tb = sT[r * T_PITCH + kj];
+          const float tf = __uint_as_float(tb);
+          uint32_t M;
+          int32_t E;
+          const bool ok = f64::weight_f64(tb, S.td, M, E);
+          const bool live = tb != T_MASKED && Rt != INT32_MIN;
+          // w < 2^(t + 1) <= 2^(Rt - 48): W = 0, a truncated (nonzero) weight
+          const bool tiny = tf > -1073741824.0f && (double)tf < (double)Rt - 49.0;
+          const int sh = E + FW - Rt;  // <= 24 for a certified weight (w < 2^Rt)
+          const uint64_t W = sh >= 0 ? (uint64_t)M << min(sh, 40)
+                                     : (sh > -64 ? (uint64_t)M >> (-sh) : 0ull);
+          const bool lost = sh < 0 && (sh <= -64 || (W << (-sh)) != (uint64_t)M);
+          Wv[u] = (live && !tiny && ok) ? W : 0ull;
+          if (live && (tiny || (ok && lost))) ++nlw;
+          if (live && !tiny && !ok) slow |= 1u << u;
+          if (live && (tiny || ok)) counted |= 1u << u;
+        }
+        for (uint32_t m = slow; m; m &= m - 1) {
+          const int u = __ffs(m) - 1;
+          const Rnd t = rnd_from_f32(sT[r * T_PITCH + 16 * u4 + 4 * wd + u]);
+          uint32_t M;
+          int64_t E;
+          int ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
+          if (ws == W_RISKY) {
+            ++n_wide;
+            ws = wide_weight(t, M, E);
+          }
           uint64_t W = 0;
-          if (tb != T_MASKED && Rt != INT32_MIN) {
-            uint32_t M;
-            int64_t E;
-            int ws = W_OK;
-            const float tf = __uint_as_float(tb);
-            int32_t Ef;
-            // w < 2^(t + 1) <= 2^(Rt - 48): W = 0, a truncated (nonzero) weight
-            const bool tiny = tf > -1073741824.0f && (double)tf < (double)Rt - 49.0;
-            if (tiny) {
-              M = 0;
-              E = 0;
-            } else if (f64::weight_f64(tb, S.td, M, Ef)) {
-              E = Ef;
+          if (ws != W_OK) {
+            rstat = ST_TIER3;
+          } else {
+            counted |= 1u << u;
+            const int sh = (int)(E + FW - Rt);
+            if (sh >= 0) {
+              W = (uint64_t)M << sh;
+            } else if (sh > -64) {
+              W = (uint64_t)M >> (-sh);
+              nlw += (W << (-sh)) != M;
             } else {
-              const Rnd t = rnd_from_f32(tb);
-              ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
-              if (ws == W_RISKY) {
-                ++n_wide;
-                ws = wide_weight(t, M, E);
-              }
-            }
-            if (ws != W_OK) {
-              rstat = ST_TIER3;
-            } else if (tiny) {
               ++nlw;
-              if (S.vlossy[kj]) vwsum += 1;
-            } else {
-              const int sh = (int)(E + FW - Rt);
-              if (sh >= 0) {
-                W = (uint64_t)M << sh;
-              } else if (sh > -64) {
-                W = (uint64_t)M >> (-sh);
-                nlw += (W << (-sh)) != M;
-              } else {
-                ++nlw;
-              }
-              wsum += W;
-              if (S.vlossy[kj]) vwsum += W + 1;
             }
           }
-          wlo[u] = (uint32_t)W;
-          whi[u] = (uint32_t)(W >> 32);
+          Wv[u] = W;
+        }
+        uint32_t wlo[4], whi[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if ((counted >> u) & 1u) {
+            wsum += Wv[u];
+            if (S.vlossy[16 * u4 + 4 * wd + u]) vwsum += Wv[u] + 1;
+          }
+          wlo[u] = (uint32_t)Wv[u];
+          whi[u] = (uint32_t)(Wv[u] >> 32);
         }
         uint8_t* dst = sW + tc::kmajor_off(r, 16 * u4 + 4 * wd, BM);
         *(uint32_t*)(dst + 0 * W_PLANE) = pack4<0>(wlo[0], wlo[1], wlo[2], wlo[3]);
