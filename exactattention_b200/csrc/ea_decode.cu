@@ -185,12 +185,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ int32_t lead_of_bits(uint32_t mag) {  // lead exponent of a nonzero |bf16|
-  int32_t m, e;
-  decode_bf16(mag, m, e);
-  return lead_of(m, e);
-}
-
 // floor(x * 2^s) of an int128 (callers keep left shifts in range)
 __device__ __forceinline__ i128 shift_floor128(i128 x, int s) {
   if (s >= 0) return (i128)((u128)x << s);
@@ -223,50 +217,6 @@ __device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost
     lost2 = r >= 32 ? (low != 0) : ((dx << r) != low);
   }
   return m < 0 ? -(int32_t)dx : (int32_t)dx;
-}
-
-// shift that gives 0 for amounts of 32 or more (PTX shl clamps the amount)
-__device__ __forceinline__ uint32_t shl_clamp(uint32_t x, uint32_t s) {
-  uint32_t r;
-  asm("shl.b32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(s));
-  return r;
-}
-// Fixed point of the low / high bf16 of word w against ebase = lsb + 134: sign (frac | 0x80) <<
-// (E - ebase). Equal to fixq for a normal element with E >= ebase, and 0 for a zero element or
-// one below the window (E < ebase) when ebase >= 1 (the negative amount clamps the shift).
-__device__ __forceinline__ uint32_t fix_lo(uint32_t w, int ebase) {
-  const uint32_t mag = shl_clamp((w & 0x7Fu) | 0x80u, ((w >> 7) & 0xFFu) - (uint32_t)ebase);
-  const uint32_t sg = (uint32_t)((int32_t)(w << 16) >> 31);  // bit 15 replicated
-  return (mag ^ sg) - sg;
-}
-__device__ __forceinline__ uint32_t fix_hi(uint32_t w, int ebase) {
-  const uint32_t mag = shl_clamp(((w >> 16) & 0x7Fu) | 0x80u, ((w >> 23) & 0xFFu) - (uint32_t)ebase);
-  const uint32_t sg = (uint32_t)((int32_t)w >> 31);  // bit 31 replicated
-  return (mag ^ sg) - sg;
-}
-// Fixed point of the low / high bf16 of word w at lsb, through fp32: the bf16 is exact in fp32,
-// the scale 2^-lsb is exact (lsb in [-126, 126]), and the conversion truncates toward zero as
-// fixq does; exact whenever |value| / 2^lsb < 2^31.
-__device__ __forceinline__ float scale_of(int lsb) { return __int_as_float((127 - lsb) << 23); }
-__device__ __forceinline__ uint32_t fixf_lo(uint32_t w, float sc) {
-  return (uint32_t)__float2int_rz(__uint_as_float(w << 16) * sc);
-}
-__device__ __forceinline__ uint32_t fixf_hi(uint32_t w, float sc) {
-  return (uint32_t)__float2int_rz(__uint_as_float(w & 0xFFFF0000u) * sc);
-}
-// per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
-__device__ __forceinline__ uint32_t nz_mag_minus1(uint32_t w) {
-  return ((w & 0x7FFF7FFFu) + 0x7FFF7FFFu) ^ 0x80008000u;
-}
-// 4 x 4 byte transpose: p_k = bytes k of x0 .. x3
-__device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
-                                           uint32_t& p1, uint32_t& p2, uint32_t& p3) {
-  const uint32_t a = __byte_perm(x0, x1, 0x5140), b = __byte_perm(x0, x1, 0x7362);
-  const uint32_t c = __byte_perm(x2, x3, 0x5140), d = __byte_perm(x2, x3, 0x7362);
-  p0 = __byte_perm(a, c, 0x5410);
-  p1 = __byte_perm(a, c, 0x7632);
-  p2 = __byte_perm(b, d, 0x5410);
-  p3 = __byte_perm(b, d, 0x7632);
 }
 
 // q row g's fixed-point element i from its balanced digit planes in the score B tile

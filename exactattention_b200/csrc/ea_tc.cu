@@ -203,19 +203,49 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       if (bad && row >= 0) S.rst[i] = ST_DOMAIN;
     }
   }
-  // channel exponents over the block's keys: VE_c = max (lead(v) + 1), or INT32_MIN if all zero
+  // channel exponents over the block's keys: VE_c = max (lead(v) + 1) over the finite values, or
+  // INT32_MIN if all are zero. Thread: 16-byte piece q = tid % 16 (channels 8q .. 8q + 7) of keys
+  // tid / 16, + 32, ..; NaN / inf values are caught per tile.
   {
-    const int c = tid & 127, part = tid >> 7;
-    int ve = INT32_MIN;
-    for (int64_t j = part; j < maxlen; j += 4) {
-      int32_t m, e;
-      const uint16_t b = P.v[(base + j) * DV + c];
-      decode_bf16(b, m, e);  // NaN/inf keys are caught per tile
-      if (m && ((b >> 7) & 0xFF) != 0xFF) ve = max(ve, lead_of(m, e) + 1);
+    const int q = tid & 15;
+    uint32_t mx[4] = {0u, 0u, 0u, 0u};
+#pragma unroll 4
+    for (int64_t j = tid >> 4; j < maxlen; j += THREADS / 16) {
+      const uint4 x = *(const uint4*)(P.v + (base + j) * DV + 8 * q);
+      mx[0] = __vmaxu2(mx[0], x.x & 0x7FFF7FFFu);
+      mx[1] = __vmaxu2(mx[1], x.y & 0x7FFF7FFFu);
+      mx[2] = __vmaxu2(mx[2], x.z & 0x7FFF7FFFu);
+      mx[3] = __vmaxu2(mx[3], x.w & 0x7FFF7FFFu);
     }
-    S.ve4[part][c] = ve;
+    // a channel that saw a NaN / inf: its largest finite magnitude, rescanned (rare)
+    if (__vcmpgeu2(__vmaxu2(__vmaxu2(mx[0], mx[1]), __vmaxu2(mx[2], mx[3])), 0x7F807F80u)) {
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        if (((mx[h >> 1] >> (16 * (h & 1))) & 0xFFFFu) < 0x7F80u) continue;
+        uint32_t m = 0;
+        for (int64_t j = tid >> 4; j < maxlen; j += THREADS / 16) {
+          const uint32_t e = P.v[(base + j) * DV + 8 * q + h] & 0x7FFFu;
+          if (e < 0x7F80u) m = max(m, e);
+        }
+        mx[h >> 1] = (mx[h >> 1] & ~(0xFFFFu << (16 * (h & 1)))) | (m << (16 * (h & 1)));
+      }
+    }
+    uint32_t* part = sT;  // [16 warps][128 channels], free until the first tile's pass 1
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t o = __vmaxu2(mx[w], __shfl_xor_sync(0xffffffffu, mx[w], 16));  // keys of the other half-warp
+      if (lane < 16) {
+        part[warp * DV + 8 * q + 2 * w] = o & 0xFFFFu;
+        part[warp * DV + 8 * q + 2 * w + 1] = o >> 16;
+      }
+    }
     __syncthreads();
-    if (tid < DV) S.ve[tid] = max(max(S.ve4[0][tid], S.ve4[1][tid]), max(S.ve4[2][tid], S.ve4[3][tid]));
+    if (tid < DV) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int w = 0; w < NWARPS; ++w) m = max(m, part[w * DV + tid]);
+      S.ve[tid] = m == 0 ? INT32_MIN : lead_of_bits(m) + 1;
+    }
     __syncthreads();
   }
 
@@ -238,46 +268,59 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 
   for (int32_t j0 = 0; j0 < maxlen; j0 += BN) {
     // ---------------- K tile -> digit planes (thread: key tid / 8, elements 16 (tid % 8) ..) --------
+    // The block exponent comes from the key's largest |k|. When no nonzero element lies below the
+    // window (smallest nonzero |k| has an exponent field >= ebase), every element converts exactly
+    // through fp32 (x = trunc(k 2^-lsb), |x| < 2^W); otherwise element by element with loss flags.
     {
       const int j = tid >> 3, e8 = tid & 7;
       const bool valid = j0 + j < maxlen;
-      uint32_t bits[16];
-      int lead = INT32_MIN, bad = 0;
+      uint32_t w[8];
       if (valid) {
         const uint4* src = (const uint4*)(P.k + (base + j0 + j) * D + 16 * e8);
+        const uint4 a = src[0], b = src[1];
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+        w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+      } else {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint4 x = src[c];
-          const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+        for (int i = 0; i < 8; ++i) w[i] = 0u;
+      }
+      uint32_t mx = 0, mn = 0xFFFFFFFFu;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            bits[8 * c + 2 * u] = w4[u] & 0xFFFFu;
-            bits[8 * c + 2 * u + 1] = w4[u] >> 16;
-          }
-        }
+      for (int i = 0; i < 8; ++i) {
+        mx = __vmaxu2(mx, w[i] & 0x7FFF7FFFu);
+        mn = __vminu2(mn, nz_mag_minus1(w[i]));
+      }
+      mx = max(mx & 0xFFFFu, mx >> 16);
+      mn = min(mn & 0xFFFFu, mn >> 16);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          int32_t m, ex;
-          if (!decode_bf16(bits[e], m, ex)) bad = 1;
-          if (m) lead = max(lead, lead_of(m, ex));
+      for (int o = 1; o < 8; o <<= 1) {
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      }
+      const int bad = mx >= 0x7F80u;
+      const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
+      const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+      const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
+      const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 && mn + 1 >= ((uint32_t)ebase << 7));
+      uint32_t lmask = 0;
+      uint32_t x[16];
+      if (lead == INT32_MIN) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = 0u;
+      } else if (fast) {
+        const float sc = scale_of(lsb);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          x[2 * i] = fixf_lo(w[i], sc);
+          x[2 * i + 1] = fixf_hi(w[i], sc);
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) bits[e] = 0;
-      }
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        lead = max(lead, __shfl_xor_sync(0xffffffffu, lead, o));
-        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-      }
-      const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
-      uint32_t lmask = 0;
-      uint32_t x[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        int lost = 0, b2 = 0;
-        x[e] = (bad || lead == INT32_MIN) ? 0u : (uint32_t)fixq(bits[e], lsb, lost, b2);
-        if (lost) lmask |= 1u << e;
+        for (int e = 0; e < 16; ++e) {
+          int lost = 0, b2 = 0;
+          x[e] = (uint32_t)fixq((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, lsb, lost, b2);
+          if (lost) lmask |= 1u << e;
+        }
       }
       uint4 pl[NK];
       planes16<NK>(x, pl);
@@ -287,27 +330,46 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       if ((e8 & 1) == 0) S.klossy[j][e8 >> 1] = lmask | (other << 16);
       if (e8 == 0) {
         S.klsb[j] = lsb;
-        S.kbad[j] = bad;
+        S.kbad[j] = valid && bad;
         S.vlossy[j] = 0;
       }
     }
     __syncthreads();
     EA_PT(0)
     // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 16 (tid / 128) ..) ------
+    // Against the block's channel exponent: through fp32 unless some value is NaN / inf or loses
+    // bits below the window (then element by element, flagging its key).
     {
       const int c = tid & 127, vq = tid >> 7;
       const int ve = S.ve[c];
       const int lsb = ve == INT32_MIN ? 0 : ve - FV;
-      uint32_t x[16];
+      const uint32_t thr = (uint32_t)max(lsb + 134, 0) << 7;  // nonzero |v| bits below this lose bits
+      uint32_t b16[16];
+      uint32_t flag = 0;
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj) {
         const int j = 16 * vq + jj;
-        const uint32_t b = (j0 + j < maxlen) ? (uint32_t)P.v[(base + j0 + j) * DV + c] : 0u;
-        int lost = 0, bad = 0;
-        int32_t f = ve == INT32_MIN ? 0 : fixq(b, lsb, lost, bad);
-        if (bad) atomicOr(&S.kbad[j], 1);
-        if (lost) atomicOr(&S.vlossy[j], 1);
-        x[jj] = (uint32_t)f;
+        b16[jj] = (j0 + j < maxlen) ? (uint32_t)P.v[(base + j0 + j) * DV + c] : 0u;
+        const uint32_t u = b16[jj] & 0x7FFFu;
+        flag |= (uint32_t)(u >= 0x7F80u) | (uint32_t)(u - 1u < thr - 1u);
+      }
+      uint32_t x[16];
+      // (a channel without finite nonzero values has lsb 0: zeros convert exactly, NaN / inf go
+      // to the flagged path)
+      if (!flag && lsb >= -126) {
+        const float sc = scale_of(lsb);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) x[jj] = fixf_lo(b16[jj], sc);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = 16 * vq + jj;
+          int lost = 0, bad = 0;
+          const int32_t f = fixq(b16[jj], lsb, lost, bad);
+          if (bad) atomicOr(&S.kbad[j], 1);
+          if (lost) atomicOr(&S.vlossy[j], 1);
+          x[jj] = (uint32_t)f;
+        }
       }
       uint4 pl[NV];
       planes16<NV>(x, pl);

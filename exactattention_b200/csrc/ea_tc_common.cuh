@@ -99,6 +99,37 @@ __device__ __forceinline__ int32_t fixq(uint32_t bits, int lsb, int& lost, int& 
   return m < 0 ? -f : f;
 }
 
+__device__ __forceinline__ int32_t lead_of_bits(uint32_t mag) {  // lead exponent of a nonzero |bf16|
+  int32_t m, e;
+  decode_bf16(mag, m, e);
+  return lead_of(m, e);
+}
+
+// Fixed point of the low / high bf16 of word w at lsb, through fp32: the bf16 is exact in fp32,
+// the scale 2^-lsb is exact (lsb in [-126, 126]), and the conversion truncates toward zero as
+// fixq does; exact whenever |value| / 2^lsb < 2^31.
+__device__ __forceinline__ float scale_of(int lsb) { return __int_as_float((127 - lsb) << 23); }
+__device__ __forceinline__ uint32_t fixf_lo(uint32_t w, float sc) {
+  return (uint32_t)__float2int_rz(__uint_as_float(w << 16) * sc);
+}
+__device__ __forceinline__ uint32_t fixf_hi(uint32_t w, float sc) {
+  return (uint32_t)__float2int_rz(__uint_as_float(w & 0xFFFF0000u) * sc);
+}
+// per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
+__device__ __forceinline__ uint32_t nz_mag_minus1(uint32_t w) {
+  return ((w & 0x7FFF7FFFu) + 0x7FFF7FFFu) ^ 0x80008000u;
+}
+// 4 x 4 byte transpose: p_k = bytes k of x0 .. x3
+__device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
+                                           uint32_t& p1, uint32_t& p2, uint32_t& p3) {
+  const uint32_t a = __byte_perm(x0, x1, 0x5140), b = __byte_perm(x0, x1, 0x7362);
+  const uint32_t c = __byte_perm(x2, x3, 0x5140), d = __byte_perm(x2, x3, 0x7362);
+  p0 = __byte_perm(a, c, 0x5410);
+  p1 = __byte_perm(a, c, 0x7632);
+  p2 = __byte_perm(b, d, 0x5410);
+  p3 = __byte_perm(b, d, 0x7632);
+}
+
 // sum_{g < n} D_g 2^(8g) exactly in int64 for n <= 4 int32 groups (|D_g| < 2^25): a chain of
 // 32 x 32 -> 64-bit multiply-adds
 template <int n>
@@ -120,17 +151,12 @@ __device__ __forceinline__ uint32_t pack4(uint32_t x0, uint32_t x1, uint32_t x2,
 // 16 int32 values -> their byte planes 0 .. NP-1, each as one uint4 (16 bytes)
 template <int NP>
 __device__ __forceinline__ void planes16(const uint32_t* x, uint4* out) {
+  uint32_t w[4][4];  // [plane][word]
 #pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    uint32_t w[4];
+  for (int c = 0; c < 4; ++c)
+    transpose4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3], w[0][c], w[1][c], w[2][c], w[3][c]);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t a = x[4 * c], b = x[4 * c + 1], cc = x[4 * c + 2], d = x[4 * c + 3];
-      w[c] = p == 0 ? pack4<0>(a, b, cc, d) : p == 1 ? pack4<1>(a, b, cc, d) : p == 2 ? pack4<2>(a, b, cc, d)
-                                                                                       : pack4<3>(a, b, cc, d);
-    }
-    out[p] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
+  for (int p = 0; p < NP; ++p) out[p] = make_uint4(w[p][0], w[p][1], w[p][2], w[p][3]);
 }
 
 // int32 fixed-point value of digit planes at (row, byte k) of an R-row K-major tile

@@ -406,6 +406,41 @@ def test_tensor_core_ragged_blocks_and_nan(ea):
     assert torch.equal(o_tc[ok], o_s[ok])
 
 
+def test_tensor_core_value_channel_edges(ea):
+    """Value channels the tensor-core kernel must not take the fast conversion for: all zeros but
+    one NaN (seen by some rows only), a subnormal next to normal values (bits below the window),
+    an infinity; against the CUDA-core path, flags included."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(78)
+    n = 400
+    K, V = bf16(rng, (n, 128), "outlier"), bf16(rng, (n, 128))
+    Q = bf16(rng, (300, 128), "outlier")
+    V[:, 7] = 0
+    V[300, 7] = 0x7FC0     # NaN in an otherwise zero channel
+    V[40, 9] = 0x0001      # subnormal among normal values
+    V[41, 9] = 0x8003
+    V[200, 11] = 0xFF80    # -inf
+    kb = np.zeros(300, np.int64)
+    kl = rng.integers(1, n + 1, size=300).astype(np.int64)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st,
+                             blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
+    torch.cuda.synchronize()
+    assert st.cpu().numpy()[7] == int(kl.sum())
+    sees = kl > 200
+    assert np.array_equal(f_tc.cpu().numpy() == 2, sees)
+    assert torch.equal(f_tc, f_s)
+    ok = torch.from_numpy(~sees).to(dev)
+    assert torch.equal(o_tc[ok], o_s[ok])
+
+
 def test_tensor_core_hybrid_tree_mask(ea):
     """HYBRID masks with row blocks: the shared prefix on the tensor cores, the ancestor lists on
     the CUDA cores, merged; equal to the CUDA-core path and to sequential decode (oracle)."""
