@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   uint8_t* sW = smem + OFF_W;
   uint32_t* sT = (uint32_t*)(smem + OFF_T);
   Small& S = *(Small*)(smem + OFF_SMALL);
+  EA_PT_DECL
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int seg = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;

@@ -50,6 +50,34 @@ __device__ __forceinline__ bool logit_f64(int64_t acc, int sexp, double am_d, in
   return zero || (e32 >= 1 && e32 <= 253 && clear_of_mid(d));
 }
 
+// t = RN32(am 2^ae * (acc 2^sexp + c)) for a score known exactly up to a small correction c (the
+// parts of lossy window elements), given as corr with |corr - c| <= corr_err. With u = 2^-53:
+//   s = RN(RN(acc) 2^sexp + corr), x = RN(s am): |x - am S| <= |am| (u |acc| 2^sexp + corr_err +
+//   u |s|) + u |x| =: B (evaluated with a relative margin); certified when the nearest fp32
+//   midpoint lies farther than B from x.
+__device__ __forceinline__ bool logit_f64_corr(int64_t acc, int sexp, double corr, double corr_err, double am_d,
+                                               int32_t ae, uint32_t& bits) {
+  if (sexp < -1000 || sexp > 1000) return false;
+  const double u = 1.1102230246251565e-16;  // 2^-53
+  const double a = __ll2double_rn(acc);
+  const double p2 = __hiloint2double((sexp + 1023) << 20, 0);
+  const double s = __fma_rn(a, p2, corr);
+  const double x = __dmul_rn(s, am_d);
+  const double B = (fabs(am_d) * (u * fabs(a) * p2 + corr_err + u * fabs(s)) + u * fabs(x)) * 1.000001;
+  const uint32_t hi = (uint32_t)__double2hiint(x), lo = (uint32_t)__double2loint(x);
+  const int32_t ex = (int32_t)((hi >> 20) & 0x7FFu);
+  const int32_t e32 = ex - (1023 - 127) + ae;
+  // (B far below the fp32 spacing also keeps the interval away from the finer spacing of the
+  // binade below a power of two)
+  if (s == 0.0 || ex <= 53 || e32 < 1 || e32 > 253 || !(B < fabs(x) * 9.313225746154785e-10)) return false;  // 2^-30
+  const double ulp = __hiloint2double((ex - 52) << 20, 0);
+  const int32_t d = mid_dist29(lo);
+  if (!((double)(d < 0 ? -d : d) * ulp > B)) return false;
+  const uint32_t mant = ((hi & 0xFFFFFu) << 3) | (lo >> 29);
+  bits = (hi & 0x80000000u) | (((uint32_t)e32 << 23) + mant + (d > 0 ? 1u : 0u));
+  return true;
+}
+
 // The score interval [acc - err, acc + err] * 2^sexp: certified when both ends are and round to
 // the same fp32 value; `differ` reports two certified, different ends (an uncertified logit).
 __device__ __forceinline__ bool logit_interval_f64(int64_t acc, uint64_t err, int sexp, double am_d, int32_t ae,

@@ -110,6 +110,34 @@ __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, co
   return err;
 }
 
+// The exact correction of one windowed score for its lossy elements, in binary64: with
+// q = Q 2^qlsb + dq and k = K 2^klsb + dk (dq, dk: the parts truncation dropped, exact),
+// q k - Q K 2^(qlsb + klsb) = Q 2^qlsb dk + dq k, one rounding per element (an fma of exact
+// products), then a sum of n terms: |corr - c| <= (n + 1) 2^-53 sum |terms| (returned in err).
+__device__ __noinline__ double score_corr(const Small& S, const uint8_t* sQ, const uint8_t* sK, int r, int kj,
+                                          const uint16_t* qrow, const uint16_t* krow, int qlsb, int klsb,
+                                          double& err) {
+  const double pq = __hiloint2double((qlsb + 1023) << 20, 0), pk = __hiloint2double((klsb + 1023) << 20, 0);
+  double c = 0.0, a = 0.0;
+  int n = 0;
+  for (int w = 0; w < 4; ++w) {
+    for (uint32_t m = S.qlossy[r][w] | S.klossy[kj][w]; m; m &= m - 1) {
+      const int i = 32 * w + __ffs(m) - 1;
+      // a bf16 is exact as the fp32 with its bits on top, and so in binary64
+      const double q = (double)__uint_as_float((uint32_t)qrow[i] << 16);
+      const double k = (double)__uint_as_float((uint32_t)krow[i] << 16);
+      const double Qs = (double)read_fix(sQ, Q_PLANE, r, i, BM) * pq;
+      const double Ks = (double)read_fix(sK, K_PLANE, kj, i, BN) * pk;
+      const double t = __fma_rn(Qs, k - Ks, (q - Qs) * k);
+      c += t;
+      a += fabs(t);
+      ++n;
+    }
+  }
+  err = (double)(n + 2) * 1.1102230246251565e-16 * a * 1.000001;
+  return c;
+}
+
 __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const int32_t* __restrict__ block_rows) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* sQ = smem + OFF_Q;
@@ -118,6 +146,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   uint8_t* sW = smem + OFF_W;
   uint32_t* sT = (uint32_t*)(smem + OFF_T);
   Small& S = *(Small*)(smem + OFF_SMALL);
+  EA_PT_DECL
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int blk = blockIdx.x;
@@ -458,8 +487,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             bool done = false, differ = false;
             uint64_t err = 0;
             if (qlossy || klossy) {
-              err = score_err(S, sQ, sK, r, kj);
-              done = f64::logit_interval_f64(acc[u], err, sexp, am_d, P.ae, fb, differ);
+              // first the exact correction of the lossy elements, then the truncation bound
+              double cerr;
+              const double corr = score_corr(S, sQ, sK, r, kj, P.q + (int64_t)myrow * D, P.k + (base + j0 + kj) * D,
+                                             qlsb, sexp - qlsb, cerr);
+              done = sexp - qlsb >= -1000 && qlsb >= -1000 &&
+                     f64::logit_f64_corr(acc[u], sexp, corr, cerr, am_d, P.ae, fb);
+              if (!done) {
+                err = score_err(S, sQ, sK, r, kj);
+                done = f64::logit_interval_f64(acc[u], err, sexp, am_d, P.ae, fb, differ);
+              }
             }
             if (done) {
               out = fb;
@@ -525,6 +562,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
     }
     __syncthreads();
+    EA_PT(11)
     const int32_t Rt = max(max(S.rt[0][r], S.rt[1][r]), max(S.rt[2][r], S.rt[3][r]));
     {
       uint64_t wsum = 0, vwsum = 0;
@@ -601,6 +639,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         *(uint32_t*)(dst + 4 * W_PLANE) = pack4<0>(whi[0], whi[1], whi[2], whi[3]);
         *(uint32_t*)(dst + 5 * W_PLANE) = pack4<1>(whi[0], whi[1], whi[2], whi[3]);
       }
+      EA_PT(12)
       S.zs[u4][r] = wsum;
       S.zl[u4][r] = nlw;
       S.vw[u4][r] = vwsum;

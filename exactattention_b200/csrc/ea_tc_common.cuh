@@ -13,28 +13,33 @@
 // cycles between the barriers that separate the phases of the tile loop into the 16 counters
 // g_phase_cycles, which each kernel's translation unit defines in its own namespace.
 #ifdef EA_PHASE_TIMERS
-#define EA_PT_INIT long long pt_last = clock64(); long long pt_acc[16] = {0};
+// EA_PT_DECL goes before a block-wide barrier at the start of the kernel
+#define EA_PT_DECL                                 \
+  __shared__ unsigned long long ea_pt_acc[16];     \
+  if (threadIdx.x < 16) ea_pt_acc[threadIdx.x] = 0;
+#define EA_PT_INIT long long pt_last = clock64();
 #define EA_PT(i)                        \
   if (tid == 0) {                       \
     const long long pt_now = clock64(); \
-    pt_acc[i] += pt_now - pt_last;      \
+    ea_pt_acc[i] += pt_now - pt_last;   \
     pt_last = pt_now;                   \
   }
 #define EA_PT_FLUSH \
   if (tid == 0)     \
-    for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], (unsigned long long)pt_acc[i]);
+    for (int i = 0; i < 16; ++i) atomicAdd(&g_phase_cycles[i], ea_pt_acc[i]);
 // the same, kept by thread `who` (a second role of a warp-specialised kernel) in counters 8-15
-#define EA_PTW_INIT long long ptw_last = clock64(); long long ptw_acc[8] = {0};
+#define EA_PTW_INIT long long ptw_last = clock64();
 #define EA_PTW(who, i)                   \
   if (tid == (who)) {                    \
     const long long pt_now = clock64();  \
-    ptw_acc[i] += pt_now - ptw_last;     \
+    ea_pt_acc[8 + (i)] += pt_now - ptw_last; \
     ptw_last = pt_now;                   \
   }
 #define EA_PTW_FLUSH(who) \
   if (tid == (who))       \
-    for (int i = 0; i < 8; ++i) atomicAdd(&g_phase_cycles[8 + i], (unsigned long long)ptw_acc[i]);
+    for (int i = 0; i < 8; ++i) atomicAdd(&g_phase_cycles[8 + i], ea_pt_acc[8 + i]);
 #else
+#define EA_PT_DECL
 #define EA_PT_INIT
 #define EA_PT(i)
 #define EA_PT_FLUSH
