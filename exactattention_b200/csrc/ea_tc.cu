@@ -77,7 +77,8 @@ struct Small {
   int32_t ve[DV];
   int32_t ve4[4][DV];
   uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
-  uint64_t bar;
+  uint64_t bar;        // score MMAs
+  uint64_t bar_pv[2];  // P.V rounds, by round parity
   uint32_t tmem;
   int32_t maxlen;
   int64_t base;
@@ -162,6 +163,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
     tc::mbar_init(&S.bar, 1);
+    tc::mbar_init(&S.bar_pv[0], 1);
+    tc::mbar_init(&S.bar_pv[1], 1);
     S.base = P.kv_base[block_rows[(int64_t)blk * BM]];
   }
   if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
@@ -291,6 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
   for (int c = 0; c < 32; ++c) N[c] = 0;
   uint32_t phase = 0;
+  uint32_t pv_phase = 0, pv_pending = 0;  // P.V barriers: phase bits, commits in flight (by parity)
   bool ok_wait = true;
   unsigned n_exact = 0, n_wide = 0;
   const double am_d = (double)P.am;
@@ -363,8 +367,30 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         S.vlossy[j] = 0;
       }
     }
+    tc::fence_async_smem();
     __syncthreads();
     EA_PT(0)
+    // ---------------- score MMAs: 7 groups x 64 columns (they run while the values are sliced) ----
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t aq = tc::smem_u32(sQ), bk = tc::smem_u32(sK);
+      for (int g = 0; g < NGS; ++g) {
+        bool first = true;
+        for (int s = 0; s < NQ; ++s) {
+          const int t = g - s;
+          if (t < 0 || t >= NK) continue;
+          const uint32_t idesc = tc::idesc_i8(128, BN, s == NQ - 1, t == NK - 1);
+          for (int ks = 0; ks < D / 32; ++ks) {
+            uint64_t ad = tc::smem_desc(aq + s * Q_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
+            uint64_t bd = tc::smem_desc(bk + t * K_PLANE + ks * 2 * (BN / 8) * 128, (BN / 8) * 128, 128);
+            tc::mma_i8(tmem + BN * g, ad, bd, idesc, !first);
+            first = false;
+          }
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar));
+    }
+
     // ---------------- V tile -> digit planes (thread: channel tid % 128, keys 16 (tid / 128) ..) ------
     // Against the block's channel exponent: through fp32 unless some value is NaN / inf or loses
     // bits below the window (then element by element, flagging its key).
@@ -413,26 +439,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       S.kmeta[tid] = ((uint32_t)S.klsb[tid] & 0xFFFFu) |
                      ((S.klossy[tid][0] | S.klossy[tid][1] | S.klossy[tid][2] | S.klossy[tid][3]) ? 1u << 16 : 0u) |
                      (S.kbad[tid] ? 1u << 17 : 0u);
-    // ---------------- score MMAs: 7 groups x 64 columns ----------------
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t aq = tc::smem_u32(sQ), bk = tc::smem_u32(sK);
-      for (int g = 0; g < NGS; ++g) {
-        bool first = true;
-        for (int s = 0; s < NQ; ++s) {
-          const int t = g - s;
-          if (t < 0 || t >= NK) continue;
-          const uint32_t idesc = tc::idesc_i8(128, BN, s == NQ - 1, t == NK - 1);
-          for (int ks = 0; ks < D / 32; ++ks) {
-            uint64_t ad = tc::smem_desc(aq + s * Q_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
-            uint64_t bd = tc::smem_desc(bk + t * K_PLANE + ks * 2 * (BN / 8) * 128, (BN / 8) * 128, 128);
-            tc::mma_i8(tmem + BN * g, ad, bd, idesc, !first);
-            first = false;
-          }
-        }
-      }
-      tc::mma_commit(tc::smem_u32(&S.bar));
-    }
     {
       const bool okw = tc::mbar_wait(&S.bar, phase);
       phase ^= 1;
@@ -675,38 +681,45 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       Nerr += scale_ceil(nlw, sh_base + FV);
       // truncated values (keys flagged lossy): < W + 1 W units times one V unit
       Nerr += scale_ceil(vw, sh_base);
-      // floors of the per-round shifts (rounds start at groups 0, 3, 6)
+      // floors of the per-round shifts (rounds start at groups 0, 2, 4, 6)
 #pragma unroll
-      for (int g = 0; g < NGP; g += 3) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
+      for (int g = 0; g < NGP; g += 2) Nerr += (8 * g + sh_base < 0) ? 1 : 0;
     }
 
     EA_PT(6)
-    // ---------------- P.V MMAs in three rounds (groups 0-2, 3-5, 6-7), drained into N ----------------
-#pragma unroll 1
-    for (int rd = 0; rd < 3; ++rd) {
-      const int g_lo = 3 * rd, g_hi = rd == 2 ? NGP : 3 * rd + 3;
-      if (tid == 0) {
-        tc::fence_after_sync();
-        const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
-        for (int g = g_lo; g < g_hi; ++g) {
-          bool first = true;
-          for (int s = 0; s < NW; ++s) {
-            const int t = g - s;
-            if (t < 0 || t >= NV) continue;
-            const uint32_t idesc = tc::idesc_i8(128, DV, false, t == NV - 1);
-            for (int ks = 0; ks < BN / 32; ++ks) {
-              uint64_t ad = tc::smem_desc(aw + s * W_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
-              uint64_t bd = tc::smem_desc(bv + t * V_PLANE + ks * 2 * (DV / 8) * 128, (DV / 8) * 128, 128);
-              tc::mma_i8(tmem + DV * (g - g_lo), ad, bd, idesc, !first);
-              first = false;
-            }
+    // ---------------- P.V MMAs in four rounds of two groups, drained into N ----------------
+    // Round rd (groups 2 rd, 2 rd + 1) accumulates in TMEM columns 256 (rd % 2) ..; round rd + 1 is
+    // issued before round rd is drained, so the tensor cores work while the CUDA cores drain. Its
+    // commit goes to the barrier of its parity (each completes once before it is waited on).
+    auto issue_pv = [&](int rd) {
+      if (tid != 0) return;
+      tc::fence_after_sync();
+      const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
+      for (int g = 2 * rd; g < 2 * rd + 2; ++g) {
+        bool first = true;
+        for (int s = 0; s < NW; ++s) {
+          const int t = g - s;
+          if (t < 0 || t >= NV) continue;
+          const uint32_t idesc = tc::idesc_i8(128, DV, false, t == NV - 1);
+          for (int ks = 0; ks < BN / 32; ++ks) {
+            uint64_t ad = tc::smem_desc(aw + s * W_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
+            uint64_t bd = tc::smem_desc(bv + t * V_PLANE + ks * 2 * (DV / 8) * 128, (DV / 8) * 128, 128);
+            tc::mma_i8(tmem + 256 * (rd & 1) + DV * (g - 2 * rd), ad, bd, idesc, !first);
+            first = false;
           }
         }
-        tc::mma_commit(tc::smem_u32(&S.bar));
       }
+      tc::mma_commit(tc::smem_u32(&S.bar_pv[rd & 1]));
+    };
+    issue_pv(0);
+    issue_pv(1);
+    pv_pending = 3;  // bit b: the barrier of parity b has a commit in flight
+#pragma unroll 1
+    for (int rd = 0; rd < 4; ++rd) {
       {
-        const bool okw = tc::mbar_wait(&S.bar, phase);
-        phase ^= 1;
+        const bool okw = tc::mbar_wait(&S.bar_pv[rd & 1], (pv_phase >> (rd & 1)) & 1u);
+        pv_phase ^= 1u << (rd & 1);
+        pv_pending &= ~(1u << (rd & 1));
         if (!__syncthreads_and(okw)) {
           ok_wait = false;
           break;
@@ -715,27 +728,38 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       tc::fence_after_sync();
       EA_PT(7)
       {  // warp-collective loads: every lane takes part (rows without visible keys add zeros)
-        const int ng = g_hi - g_lo;
+        // floor(X 2^s) as (X << l) >> r: s <= 38 and the round's |X| < 2^33 (so X 2^l < 2^63), and
+        // a right shift clamped to 63 still floors
+        const int s = 16 * rd + sh_base;
+        const int l = max(s, 0), rr = min(max(-s, 0), 63);
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
-          uint32_t dg[3][8] = {};
-#pragma unroll
-          for (int gi = 0; gi < 3; ++gi)
-            if (gi < ng) tc::tmem_ld8(tlane + DV * gi + 32 * u4 + 8 * c8, dg[gi]);
+          uint32_t dg[2][8];
+          tc::tmem_ld8(tlane + 256 * (rd & 1) + 32 * u4 + 8 * c8, dg[0]);
+          tc::tmem_ld8(tlane + 256 * (rd & 1) + DV + 32 * u4 + 8 * c8, dg[1]);
           tc::tmem_wait_ld();
-          const int s = 8 * g_lo + sh_base;
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const uint32_t d3[3] = {dg[0][u], ng > 1 ? dg[1][u] : 0u, ng > 2 ? dg[2][u] : 0u};
-            N[8 * c8 + u] += shift_floor(recomb<3>(d3), s);
+            const uint32_t d2[2] = {dg[0][u], dg[1][u]};
+            N[8 * c8 + u] += (int64_t)((uint64_t)recomb<2>(d2) << l) >> rr;
           }
         }
       }
       tc::fence_before_sync();
       __syncthreads();
       EA_PT(8)
+      if (rd + 2 < 4) {
+        issue_pv(rd + 2);
+        pv_pending |= 1u << (rd & 1);
+      }
     }
     if (!ok_wait) break;  // uniform: set by the block vote
+  }
+  if (!ok_wait) {
+    // a wait that gave up: the MMAs still in flight get a bounded wait before TMEM is released
+    tc::mbar_wait(&S.bar, phase ^ 1u);
+    for (int b = 0; b < 2; ++b)
+      if ((pv_pending >> b) & 1u) tc::mbar_wait(&S.bar_pv[b], (pv_phase >> b) & 1u);
   }
 
   EA_PT(9)
