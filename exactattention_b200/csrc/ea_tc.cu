@@ -452,10 +452,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     EA_PT(2)
 
     // ---------------- pass 1: certified logits of (r, keys 16 u4 ..) ----------------
+    bool any_unc = false;
     {
       const int qlsb = S.qlsb[r];
       const bool qlossy = (S.qlossy[r][0] | S.qlossy[r][1] | S.qlossy[r][2] | S.qlossy[r][3]) != 0;
       int rstat = ST_OK;
+      // the tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1),
+      // and ceil is monotone (the ceiling of the largest logit); |t| >= 2^30 goes to tier 3
+      float tmax = -INFINITY;
 #pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t dg[NGS][4];
@@ -520,54 +524,60 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           outv[u] = out;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) sT[r * T_PITCH + 16 * u4 + 4 * c4 + u] = outv[u];
+        for (int u = 0; u < 4; ++u) {
+          sT[r * T_PITCH + 16 * u4 + 4 * c4 + u] = outv[u];
+          const float tf = __uint_as_float(outv[u]);
+          if (fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);  // false for the NaN markers
+          any_unc |= outv[u] == T_UNCERT;
+        }
       }
       if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
+      S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
     }
     tc::fence_before_sync();
-    __syncthreads();
+    const bool tile_unc = __syncthreads_or(any_unc);
     EA_PT(3)
 
     // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
-    // entry e = warp + 16 (32 it + lane): a row with many uncertified pairs spreads over every warp
-    for (int it = 0; it < BM * BN / (32 * NWARPS); ++it) {
-      const int e = warp + NWARPS * (32 * it + lane);
-      uint32_t hit = __ballot_sync(0xffffffffu, sT[(e >> 6) * T_PITCH + (e & 63)] == T_UNCERT);
-      while (hit) {
-        const int src = __ffs(hit) - 1;
-        hit &= hit - 1;
-        const int ee = warp + NWARPS * (32 * it + src);
-        const int pr = ee >> 6, pk = ee & 63;
-        Rnd t = rnd_zero();
-        const int ls = warp_exact_logit(P, S.rows[pr], base + j0 + pk, t);
-        if (lane == 0) {
-          if (ls == LOGIT_OK) {
-            sT[pr * T_PITCH + pk] = rnd_to_f32_bits(t);
-          } else {
-            sT[pr * T_PITCH + pk] = T_MASKED;
-            atomicMax(&S.rst[pr], ST_DOMAIN);
+    // entry e = warp + 16 (32 it + lane): a row with many uncertified pairs spreads over every warp.
+    // Then the tile bounds again, over the exact logits too.
+    if (tile_unc) {
+      for (int it = 0; it < BM * BN / (32 * NWARPS); ++it) {
+        const int e = warp + NWARPS * (32 * it + lane);
+        uint32_t hit = __ballot_sync(0xffffffffu, sT[(e >> 6) * T_PITCH + (e & 63)] == T_UNCERT);
+        while (hit) {
+          const int src = __ffs(hit) - 1;
+          hit &= hit - 1;
+          const int ee = warp + NWARPS * (32 * it + src);
+          const int pr = ee >> 6, pk = ee & 63;
+          Rnd t = rnd_zero();
+          const int ls = warp_exact_logit(P, S.rows[pr], base + j0 + pk, t);
+          if (lane == 0) {
+            if (ls == LOGIT_OK) {
+              sT[pr * T_PITCH + pk] = rnd_to_f32_bits(t);
+            } else {
+              sT[pr * T_PITCH + pk] = T_MASKED;
+              atomicMax(&S.rst[pr], ST_DOMAIN);
+            }
+            ++n_exact;
           }
-          ++n_exact;
         }
       }
+      __syncthreads();
+      {
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float tf = __uint_as_float(sT[r * T_PITCH + 16 * u4 + u]);
+          if (fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);
+        }
+        S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
+      }
+      __syncthreads();
     }
-    __syncthreads();
     EA_PT(4)
 
-    // ---------------- pass 2: tile bound, weights, W digits ----------------
-    {
-      // w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1): ceil of the exact fp32 t is exact
-      // (ceil is monotone: the ceiling of the largest logit)
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const uint32_t tb = sT[r * T_PITCH + 16 * u4 + u];
-        const float tf = __uint_as_float(tb);
-        if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);  // |t| >= 2^30: tier 3
-      }
-      S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
-    }
-    __syncthreads();
+    // ---------------- pass 2: weights, W digits ----------------
     EA_PT(11)
     const int32_t Rt = max(max(S.rt[0][r], S.rt[1][r]), max(S.rt[2][r], S.rt[3][r]));
     {
