@@ -43,6 +43,7 @@ constexpr int NGS = NQ + NK - 1;  // score groups
 constexpr int NGP = NW + NV - 1;  // P.V groups
 constexpr int FW = 48, FV = 23;
 constexpr int THREADS = 512, NWARPS = THREADS / 32;
+constexpr int LCAP = 4;  // window elements per q row / key whose lost parts are kept for the correction
 constexpr uint32_t TMEM_COLS = 512;
 
 // shared memory map (bytes)
@@ -74,8 +75,16 @@ struct Small {
   int32_t kbad[BN];
   int32_t vlossy[BN];
   uint32_t kmeta[BN];  // per key, for pass 1: klsb (low 16 bits, signed) | lossy << 16 | bad << 17
+  // the window elements of each q row (key of the tile) that lost bits, up to LCAP, with their
+  // lost parts dq = q - Q 2^qlsb (dk = k - K 2^klsb): at most 8 significant bits at or above the
+  // bf16 subnormal unit 2^-133, so exact in fp32; count > LCAP: the list is incomplete
+  float qc_d[BM][LCAP];
+  float kc_d[BN][LCAP];
+  uint8_t qc_i[BM][LCAP];
+  uint8_t kc_i[BN][LCAP];
+  uint8_t qc_n[BM];
+  uint8_t kc_n[BN];
   int32_t ve[DV];
-  int32_t ve4[4][DV];
   uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
   uint64_t bar;        // score MMAs
   uint64_t bar_pv[2];  // P.V rounds, by round parity
@@ -137,6 +146,41 @@ __device__ __noinline__ double score_corr(const Small& S, const uint8_t* sQ, con
   }
   err = (double)(n + 2) * 1.1102230246251565e-16 * a * 1.000001;
   return c;
+}
+
+// As score_corr, from the per-row and per-key lists of lost parts kept in shared memory (no
+// global loads): for an element lossy in q only, the term is dq k with k = K 2^klsb exact; for one
+// lossy in k only, Q 2^qlsb dk (exact); for one lossy in both, Q 2^qlsb dk + dq k (one rounding).
+// False when a list is incomplete.
+__device__ __forceinline__ bool score_corr_cached(const Small& S, const uint8_t* sQ, const uint8_t* sK, int r, int kj,
+                                                  int qlsb, int klsb, double& corr, double& err) {
+  const int nq = S.qc_n[r], nk = S.kc_n[kj];
+  if (nq > LCAP || nk > LCAP) return false;
+  const double pq = __hiloint2double((qlsb + 1023) << 20, 0), pk = __hiloint2double((klsb + 1023) << 20, 0);
+  double c = 0.0, a = 0.0;
+  for (int e = 0; e < nq; ++e) {
+    const int i = S.qc_i[r][e];
+    double dk = 0.0;
+    for (int f = 0; f < nk; ++f)
+      if (S.kc_i[kj][f] == i) dk = (double)S.kc_d[kj][f];
+    const double k = (double)read_fix(sK, K_PLANE, kj, i, BN) * pk + dk;  // the element itself, exact
+    const double Qs = dk != 0.0 ? (double)read_fix(sQ, Q_PLANE, r, i, BM) * pq : 0.0;
+    const double t = __fma_rn(Qs, dk, (double)S.qc_d[r][e] * k);
+    c += t;
+    a += fabs(t);
+  }
+  for (int f = 0; f < nk; ++f) {
+    const int i = S.kc_i[kj][f];
+    bool inq = false;
+    for (int e = 0; e < nq; ++e) inq |= S.qc_i[r][e] == i;
+    if (inq) continue;
+    const double t = (double)read_fix(sQ, Q_PLANE, r, i, BM) * pq * (double)S.kc_d[kj][f];  // exact
+    c += t;
+    a += fabs(t);
+  }
+  corr = c;
+  err = (double)(nq + nk + 2) * 1.1102230246251565e-16 * a * 1.000001;
+  return true;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const int32_t* __restrict__ block_rows) {
@@ -281,6 +325,26 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
   }
 
+  // the q rows' lists of lost window parts (the planes and the lossy masks are complete here)
+  if (tid < BM) {
+    const int32_t row = S.rows[tid];
+    const int qlsb = S.qlsb[tid];
+    const double pq = __hiloint2double((qlsb + 1023) << 20, 0);
+    int n = 0;
+    for (int w = 0; w < 4; ++w)
+      for (uint32_t m = S.qlossy[tid][w]; m; m &= m - 1) {
+        const int i = 32 * w + __ffs(m) - 1;
+        if (n < LCAP) {
+          const double q = (double)__uint_as_float((uint32_t)P.q[(int64_t)row * D + i] << 16);
+          S.qc_d[tid][n] = (float)(q - (double)read_fix(sQ, Q_PLANE, tid, i, BM) * pq);  // exact
+          S.qc_i[tid][n] = (uint8_t)i;
+        }
+        ++n;
+      }
+    S.qc_n[tid] = (uint8_t)min(n, 255);
+  }
+  __syncthreads();
+
   EA_PT_INIT
   const int r = 32 * (warp & 3) + lane, u4 = warp >> 2;
   const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
@@ -370,6 +434,24 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     tc::fence_async_smem();
     __syncthreads();
     EA_PT(0)
+    // the keys' lists of lost window parts (threads 64 .. 127; read in pass 1, after the next barrier)
+    if (tid >= 64 && tid < 64 + BN) {
+      const int jj = tid - 64;
+      const int klsb = S.klsb[jj];
+      const double pk = __hiloint2double((klsb + 1023) << 20, 0);
+      int n = 0;
+      for (int w = 0; w < 4; ++w)
+        for (uint32_t m = S.klossy[jj][w]; m; m &= m - 1) {
+          const int i = 32 * w + __ffs(m) - 1;
+          if (n < LCAP) {
+            const double k = (double)__uint_as_float((uint32_t)P.k[(base + j0 + jj) * D + i] << 16);
+            S.kc_d[jj][n] = (float)(k - (double)read_fix(sK, K_PLANE, jj, i, BN) * pk);  // exact
+            S.kc_i[jj][n] = (uint8_t)i;
+          }
+          ++n;
+        }
+      S.kc_n[jj] = (uint8_t)min(n, 255);
+    }
     // ---------------- score MMAs: 7 groups x 64 columns (they run while the values are sliced) ----
     if (tid == 0) {
       tc::fence_after_sync();
@@ -498,9 +580,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             uint64_t err = 0;
             if (qlossy || klossy) {
               // first the exact correction of the lossy elements, then the truncation bound
-              double cerr;
-              const double corr = score_corr(S, sQ, sK, r, kj, P.q + (int64_t)myrow * D, P.k + (base + j0 + kj) * D,
-                                             qlsb, sexp - qlsb, cerr);
+              double cerr, corr;
+              if (!score_corr_cached(S, sQ, sK, r, kj, qlsb, sexp - qlsb, corr, cerr))
+                corr = score_corr(S, sQ, sK, r, kj, P.q + (int64_t)myrow * D, P.k + (base + j0 + kj) * D, qlsb,
+                                  sexp - qlsb, cerr);
               done = sexp - qlsb >= -1000 && qlsb >= -1000 &&
                      f64::logit_f64_corr(acc[u], sexp, corr, cerr, am_d, P.ae, fb);
               if (!done) {
