@@ -128,5 +128,61 @@ __device__ __forceinline__ bool weight_f64(uint32_t tb, const uint64_t* tab, uin
   return in_range && (one || clear_of_mid(d));
 }
 
+// RN_p(a / b * 2^sh) for a < 2^63, 0 < b < 2^63, the result a normal number of the target
+// format: x = RN(RN(a) / RN(b)) has relative error below 3.01 u (u = 2^-53), about 6 ulps of x;
+// certified when the 53 - p dropped bits lie more than 8 ulps from their midpoint. 0: certain
+// (a == 0), 1: certified, -1: the integer division decides.
+__device__ __forceinline__ int ratio_f64(uint64_t a, uint64_t b, int sh, int neg, int p, int qmin, int emax,
+                                         Rnd& out) {
+  out = rnd_zero();
+  out.neg = neg;
+  if (a == 0) return 0;
+  const double x = __ddiv_rn(__ull2double_rn(a), __ull2double_rn(b));
+  const uint64_t bits = (uint64_t)__double_as_longlong(x);
+  const int K = (int)((bits >> 52) & 0x7FF) - 1023 + sh;  // 2^K <= value < 2^(K + 1), up to the error
+  if (K - (p - 1) <= qmin || K >= emax) return -1;
+  const int Dr = 53 - p;  // dropped bits (29 for fp32, 45 for bf16)
+  const uint64_t mant = bits & ((1ull << 52) - 1);
+  const int64_t dropped = (int64_t)(mant & ((1ull << Dr) - 1)), half = (int64_t)1 << (Dr - 1);
+  const int64_t d = dropped - half;
+  if (d <= 8 && d >= -8) return -1;
+  uint64_t q = ((mant >> Dr) | (1ull << (p - 1))) + (d > 0 ? 1u : 0u);
+  int qe = K - (p - 1);
+  if (q == (1ull << p)) {
+    q >>= 1;
+    ++qe;
+  }
+  out.q = q;
+  out.qe = qe;
+  return 1;
+}
+
+// certify_ratio_lh through ratio_f64: 1 certified (out set), 0 not certifiable (the ends differ),
+// -1 the integer evaluation decides.
+__device__ __forceinline__ int certify_ratio_f64(int64_t nlo, int64_t nhi, int64_t nunit, int64_t zlo, int64_t zhi,
+                                                 int64_t zunit, int p, int qmin, int emax, Rnd& out) {
+  if (zlo <= 0 || zhi < zlo || nhi < nlo) return -1;
+  const int64_t sh64 = nunit - zunit;
+  if (sh64 > 100000 || sh64 < -100000) return -1;
+  const int sh = (int)sh64;
+  uint64_t ln, ld, hn, hd;
+  int lneg, hneg;
+  if (nlo >= 0) {
+    ln = (uint64_t)nlo; ld = (uint64_t)zhi; hn = (uint64_t)nhi; hd = (uint64_t)zlo; lneg = 0; hneg = 0;
+  } else if (nhi <= 0) {
+    ln = (uint64_t)(-nlo); ld = (uint64_t)zlo; hn = (uint64_t)(-nhi); hd = (uint64_t)zhi; lneg = 1; hneg = 1;
+  } else {
+    return -1;  // the interval holds zero: the integer evaluation
+  }
+  Rnd rl, rh;
+  const int cl = ratio_f64(ln, ld, sh, lneg, p, qmin, emax, rl);
+  const int ch = ratio_f64(hn, hd, sh, hneg, p, qmin, emax, rh);
+  if (cl < 0 || ch < 0) return -1;
+  if (!rnd_eq(rl, rh)) return 0;
+  out = rl;
+  if (out.q == 0) out.neg = 0;
+  return 1;
+}
+
 }  // namespace f64
 }  // namespace ea

@@ -548,6 +548,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
         for (int g = 0; g < NGS; ++g) tc::tmem_ld4(tlane + BN * g + 16 * u4 + 4 * c4, dg[g]);
         tc::tmem_wait_ld();
+        EA_PT(13)
         // the binary64 fast path for the four keys (straight-line, interleaved), then the rare keys
         // it leaves to the integer evaluation: NaN/inf keys, lossy windows, results it cannot certify
         int64_t acc[4];
@@ -565,6 +566,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           outv[u] = live ? fb : T_MASKED;
           if (live && (!ok || qlossy || (km >> 16) != 0)) slow |= 1u << u;
         }
+        EA_PT(14)
         for (uint32_t m = slow; m; m &= m - 1) {
           const int u = __ffs(m) - 1;
           const int kj = 16 * u4 + 4 * c4 + u;
@@ -606,6 +608,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           }
           outv[u] = out;
         }
+        EA_PT(15)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           sT[r * T_PITCH + 16 * u4 + 4 * c4 + u] = outv[u];
@@ -684,10 +687,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const bool live = tb != T_MASKED && Rt != INT32_MIN;
           // w < 2^(t + 1) <= 2^(Rt - 48): W = 0, a truncated (nonzero) weight
           const bool tiny = tf > -1073741824.0f && (double)tf < (double)Rt - 49.0;
-          const int sh = E + FW - Rt;  // <= 24 for a certified weight (w < 2^Rt)
-          const uint64_t W = sh >= 0 ? (uint64_t)M << min(sh, 40)
-                                     : (sh > -64 ? (uint64_t)M >> (-sh) : 0ull);
-          const bool lost = sh < 0 && (sh <= -64 || (W << (-sh)) != (uint64_t)M);
+          // W = floor(M 2^sh) with M < 2^24 and sh <= 24 (w < 2^Rt): a left shift fits in 48 bits,
+          // a right shift stays in 32 (clamped to 31 below 2^-31, which the lost flag covers)
+          const int sh = E + FW - Rt;
+          const int rs = min(max(-sh, 0), 31);
+          const uint32_t Wr = sh <= -32 ? 0u : M >> rs;
+          const uint64_t W = sh >= 0 ? (uint64_t)M << min(sh, 24) : (uint64_t)Wr;
+          const bool lost = sh < 0 && (sh <= -32 || (M & ((1u << rs) - 1u)) != 0u);
           Wv[u] = (live && !tiny && ok) ? W : 0ull;
           if (live && (tiny || (ok && lost))) ++nlw;
           if (live && !tiny && !ok) slow |= 1u << u;
@@ -753,9 +759,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     if (Rt != INT32_MIN) {
       const int32_t Rn = R == R_EMPTY ? Rt : max(R, Rt);
       if (R != R_EMPTY && Rn > R) {
-        const int d = Rn - R;
+        const int d = Rn - R, dc = min(d, 63);  // d > 0: an arithmetic right shift is the floor
 #pragma unroll
-        for (int c = 0; c < 32; ++c) N[c] = shift_floor(N[c], -d);
+        for (int c = 0; c < 32; ++c) N[c] >>= dc;
         Nerr = scale_ceil(Nerr, -d) + 1;
         int lost;
         Z = floor_shift(Z, -d, lost);
@@ -887,9 +893,14 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     for (int c = 0; c < 32; ++c) {
       Rnd x = rnd_zero();
       const int ve = S.ve[32 * u4 + c];
-      if (ok && R != R_EMPTY && ve != INT32_MIN)
-        ok &= certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z,
-                               Z + (int64_t)Zerr, (int64_t)R - FZ, prec, qmin, 127, x);
+      if (ok && R != R_EMPTY && ve != INT32_MIN) {
+        // binary64 first; the integer division decides what it cannot certify
+        const int64_t nl = N[c] - (int64_t)Nerr, nh = N[c] + (int64_t)Nerr;
+        const int64_t nu = (int64_t)R + ve - FN, zu = (int64_t)R - FZ;
+        const int cf = f64::certify_ratio_f64(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, prec, qmin, 127, x);
+        if (cf == 0) ok = false;
+        else if (cf < 0) ok &= certify_ratio_lh(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, prec, qmin, 127, x);
+      }
       const uint32_t b = rnd_to_bf16_bits(x);
       if (c & 1) outw[c >> 1] |= b << 16;
       else outw[c >> 1] = b;
@@ -928,9 +939,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             const int c = 4 * c4 + u;
             Rnd x = rnd_zero();
             const int ve = S.ve[32 * u4 + c];
-            if (R != R_EMPTY && ve != INT32_MIN)
-              certify_ratio_lh(N[c] - (int64_t)Nerr, N[c] + (int64_t)Nerr, (int64_t)R + ve - FN, Z, Z + (int64_t)Zerr,
-                               (int64_t)R - FZ, FP32_P, FP32_QMIN, 127, x);
+            if (R != R_EMPTY && ve != INT32_MIN) {
+              const int64_t nl = N[c] - (int64_t)Nerr, nh = N[c] + (int64_t)Nerr;
+              const int64_t nu = (int64_t)R + ve - FN, zu = (int64_t)R - FZ;
+              if (f64::certify_ratio_f64(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, FP32_P, FP32_QMIN, 127, x) < 0)
+                certify_ratio_lh(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, FP32_P, FP32_QMIN, 127, x);
+            }
             f[u] = rnd_to_f32_bits(x);
           }
           *(uint4*)(o + 4 * c4) = make_uint4(f[0], f[1], f[2], f[3]);
