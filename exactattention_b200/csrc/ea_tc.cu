@@ -206,9 +206,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   }
   if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
-    tc::mbar_init(&S.bar, 1);
-    tc::mbar_init(&S.bar_pv[0], 1);
-    tc::mbar_init(&S.bar_pv[1], 1);
+    tc::mbar_init(&S.bar, NGS);        // one commit per score group's issuer
+    tc::mbar_init(&S.bar_pv[0], 2);    // one commit per P.V group's issuer (two groups a round)
+    tc::mbar_init(&S.bar_pv[1], 2);
     S.base = P.kv_base[block_rows[(int64_t)blk * BM]];
   }
   if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
@@ -453,10 +453,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       S.kc_n[jj] = (uint8_t)min(n, 255);
     }
     // ---------------- score MMAs: 7 groups x 64 columns (they run while the values are sliced) ----
-    if (tid == 0) {
+    // Group g is issued by lane 0 of warp 2 g + 1: an issuing thread waits while the tensor core
+    // takes its operands, so the groups' issuers share that wait (each commits to the barrier).
+    if (lane == 0 && (warp & 1) && (warp >> 1) < NGS) {
       tc::fence_after_sync();
       const uint32_t aq = tc::smem_u32(sQ), bk = tc::smem_u32(sK);
-      for (int g = 0; g < NGS; ++g) {
+      {
+        const int g = warp >> 1;
         bool first = true;
         for (int s = 0; s < NQ; ++s) {
           const int t = g - s;
@@ -538,6 +541,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     {
       const int qlsb = S.qlsb[r];
       const bool qlossy = (S.qlossy[r][0] | S.qlossy[r][1] | S.qlossy[r][2] | S.qlossy[r][3]) != 0;
+      const int nqc = S.qc_n[r];
+      const bool qlist = nqc <= LCAP && qlsb >= -1000;  // the row's lost parts are all listed
       int rstat = ST_OK;
       // the tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1),
       // and ceil is monotone (the ceiling of the largest logit); |t| >= 2^30 goes to tier 3
@@ -565,6 +570,36 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const bool live = myrow >= 0 && j0 + kj < mylen;
           outv[u] = live ? fb : T_MASKED;
           if (live && (!ok || qlossy || (km >> 16) != 0)) slow |= 1u << u;
+        }
+        // a q row whose window lost bits, against keys that lost none: its exact correction
+        // sum_e dq_e K_(key, i_e) 2^klsb for the four keys together (interleaved), from the row's list
+        if (qlossy && qlist) {
+          double cr[4] = {0.0, 0.0, 0.0, 0.0}, ca[4] = {0.0, 0.0, 0.0, 0.0};
+          for (int e = 0; e < nqc; ++e) {
+            const int i = S.qc_i[r][e];
+            const double dq = (double)S.qc_d[r][e];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int kj = 16 * u4 + 4 * c4 + u;
+              const int klsb = (int32_t)(int16_t)(S.kmeta[kj] & 0xFFFFu);
+              const double t = dq * ((double)read_fix(sK, K_PLANE, kj, i, BN) * __hiloint2double((klsb + 1023) << 20, 0));
+              cr[u] += t;  // dq K 2^klsb: exact products (at most 8 x 27 bits), one rounding per sum
+              ca[u] += fabs(t);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int kj = 16 * u4 + 4 * c4 + u;
+            const uint32_t km = S.kmeta[kj];
+            if (!((slow >> u) & 1u) || (km >> 16) != 0) continue;  // lossy keys: the general path
+            uint32_t fb;
+            const double cerr = (double)(nqc + 2) * 1.1102230246251565e-16 * ca[u] * 1.000001;
+            const int sexp = qlsb + (int32_t)(int16_t)(km & 0xFFFFu);
+            if (sexp - qlsb >= -1000 && f64::logit_f64_corr(acc[u], sexp, cr[u], cerr, am_d, P.ae, fb)) {
+              outv[u] = fb;
+              slow &= ~(1u << u);
+            }
+          }
         }
         EA_PT(14)
         for (uint32_t m = slow; m; m &= m - 1) {
@@ -790,11 +825,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     // Round rd (groups 2 rd, 2 rd + 1) accumulates in TMEM columns 256 (rd % 2) ..; round rd + 1 is
     // issued before round rd is drained, so the tensor cores work while the CUDA cores drain. Its
     // commit goes to the barrier of its parity (each completes once before it is waited on).
+    // group 2 rd + i is issued by lane 0 of warp 4 rd + 2 i (as the score groups)
     auto issue_pv = [&](int rd) {
-      if (tid != 0) return;
+      if (lane != 0 || (warp >> 2) != rd || (warp & 1)) return;
       tc::fence_after_sync();
       const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
-      for (int g = 2 * rd; g < 2 * rd + 2; ++g) {
+      {
+        const int g = 2 * rd + ((warp >> 1) & 1);
         bool first = true;
         for (int s = 0; s < NW; ++s) {
           const int t = g - s;

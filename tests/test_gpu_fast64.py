@@ -33,3 +33,14 @@ def test_logit_fast_path_matches_integer(seed):
     # not certified: results outside the normal fp32 range, exact ties (short scores times alpha
     # often have exactly 25 significant bits), and values within 4 ulps of a midpoint
     assert cert >= cases * 0.95
+
+
+@pytest.mark.parametrize("seed", [4, 5])
+def test_ratio_fast_path_matches_integer(seed):
+    from exactattention_b200 import cuda
+
+    n = 1 << 24
+    cases, cert, bad, what = cuda.selftest_fast64(2, seed, n)
+    assert cases == n
+    assert bad == 0, what
+    assert cert >= cases * 0.9  # the rest: results near the subnormal or overflow range, near midpoints
