@@ -20,7 +20,7 @@ cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t 
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
 cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
 cudaError_t launch_combine(const Prob& P, cudaStream_t st);
-cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, cudaStream_t st);
+cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 }  // namespace ea
@@ -274,6 +274,11 @@ static int64_t decode_segments(const ea_launch_t* a) {
   return a->mask_kind == EA_MASK_PAGED ? (a->rows / a->q_heads) * a->kv_heads : a->nsegs;
 }
 
+// rows per decode segment: the GQA group of a paged layout; a segment table may fill all 8 slots
+static int decode_max_rows(const ea_launch_t* a) {
+  return a->mask_kind == EA_MASK_PAGED ? a->q_heads / a->kv_heads : 8;
+}
+
 // the decode kernel writes split partials for splits >= 1: carve the split buffers for at least 2
 static int decode_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
   ea_launch_t a2 = *a;
@@ -294,7 +299,7 @@ static int launch_decode_tc(const ea_launch_t* a, Workspace* w, cudaStream_t st)
   const int32_t* seg = a->mask_kind == EA_MASK_RANGE ? a->seg_rows : nullptr;
   {
     TimedLaunch tl(st);
-    e = launch_tc_decode(P, seg, decode_segments(a), st);
+    e = launch_tc_decode(P, seg, decode_segments(a), decode_max_rows(a), st);
   }
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 decode launch");
   e = launch_combine(P, st);
@@ -407,7 +412,7 @@ int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream)
     cudaError_t e;
     {
       TimedLaunch tl(st);
-      e = launch_tc_decode(P, seg, decode_segments(a), st);
+      e = launch_tc_decode(P, seg, decode_segments(a), decode_max_rows(a), st);
     }
     if (e == cudaSuccess) e = launch_combine(P, st);
     return e == cudaSuccess ? 0 : fail_cuda(e, "partials decode launch");

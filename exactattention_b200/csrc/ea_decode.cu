@@ -47,7 +47,7 @@ constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
 constexpr int FW = 48, FV = 31;  // V: 31-bit window, 4 digits (few values fall below it)
 constexpr int THREADS = 512, NWARPS = THREADS / 32;
 constexpr int NWGC = 2;         // consumer warpgroups (warps 0-7); warps 8-15 are the producers
-constexpr int RPT = GD / NWGC;  // row slots per consumer thread
+constexpr int RPT_MAX = GD / NWGC;  // row slots per consumer thread for a full segment of GD rows
 constexpr uint32_t VLCAP = 4;
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
 constexpr uint32_t TMEM_COLS = 512;
@@ -81,6 +81,7 @@ struct Small {
   int32_t vl_dx[2][DV][4];
   int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
   int16_t ve4[4][DV];  // per key quarter maxima of the current tile (INT16_MIN: none)
+  uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
   int32_t rows[GD];
   int32_t len[GD];
   int32_t qlsb[GD];
@@ -233,6 +234,9 @@ __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
   return x;
 }
 
+// RPT: row slots per consumer thread (rows h, h + NWGC, ..): segments of at most NWGC RPT rows.
+// A smaller RPT keeps fewer running sums in registers (GQA groups of 2 need one slot).
+template <int RPT>
 __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* rawk = smem + OFF_RAWK;
@@ -263,6 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   }
   for (int i = tid; i < DV; i += THREADS) S.ve[0][i] = S.ve[1][i] = INT32_MIN;
   for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
+  if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
     tc::mbar_init(&S.bar_rk, 1);
     tc::mbar_init(&S.bar_rv, 1);
@@ -288,6 +293,28 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   __syncthreads();
   const int nrows = S.nrows;
   if (nrows == 0) return;  // uniform: an all-padding segment
+  if (nrows > NWGC * RPT) {
+    // more rows than this instantiation keeps sums for (a launch error): every row of the segment
+    // goes to the exact tier, and the run is flagged
+    for (int i = tid; i < nrows * (DV + 1); i += THREADS) {
+      const int g = i / (DV + 1), ch = i % (DV + 1);
+      const int32_t row = S.rows[g];
+      if (row < 0) continue;
+      const int64_t pi = (int64_t)split * P.rows + row;
+      if (ch == DV) {
+        P.pR[pi] = R_EMPTY;
+        P.pZ[pi] = 0;
+        P.pZe[pi] = 0;
+        P.pSt[pi] = ST_TIER3;
+      } else {
+        P.pNR[pi * DV + ch] = R_EMPTY;
+        P.pN[pi * DV + ch] = 0;
+        P.pNe[pi * DV + ch] = 0;
+      }
+    }
+    if (tid == 0) stat_add(P, STAT_UNRESOLVED, 1000000);
+    return;
+  }
   const int32_t row0 = S.row0;  // the segment's rows share their keys: address them through this one
   const int64_t maxlen = S.maxlen;
   const int64_t kbeg = maxlen * split / nsplit, kend = maxlen * (split + 1) / nsplit;
@@ -798,15 +825,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           if (tiny) {
             M = 0;
             E = 0;
-          } else if (f64::weight_f64(tb, f64::g_exp2_d64, M, Ef)) {  // 2 KB table, L1-resident
+          } else if (f64::weight_f64(tb, S.td, M, Ef)) {
             E = Ef;
           } else {
+            // (separate variables for the out-of-line call: M and E keep no address)
             const Rnd t = rnd_from_f32(tb);
-            ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
+            uint32_t Mi;
+            int64_t Ei;
+            ws = weight_from_logit(t, g_ta64, g_tb64, Mi, Ei);
             if (ws == W_RISKY) {
               ++n_wide;
-              ws = wide_weight(t, M, E);
+              ws = wide_weight(t, Mi, Ei);
             }
+            M = Mi;
+            E = Ei;
           }
           if (ws != W_OK) {
             atomicMax(&S.rst[g], ST_TIER3);  // |t| >= 2^30 or a still-risky weight
@@ -1035,20 +1067,32 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 
 }  // namespace tcd
 
-// Grid (segments, splits); writes split partials (P.pR ..) for every listed row.
-cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, cudaStream_t st) {
+// Grid (segments, splits); writes split partials (P.pR ..) for every listed row. max_rows: the
+// most rows any segment holds (1..8; 8 when unknown).
+cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st) {
   // the shared-memory opt-in is a property of the function on a device: set it once per device
   // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
-  static bool attr_set[64] = {};
+  static bool attr_set[64][3] = {};
+  const int v = max_rows <= tcd::NWGC ? 0 : max_rows <= 2 * tcd::NWGC ? 1 : 2;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(tcd::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
+  if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
+    cudaError_t e = v == 0 ? cudaFuncSetAttribute(tcd::tc_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  (int)tcd::SMEM_BYTES)
+                    : v == 1 ? cudaFuncSetAttribute(tcd::tc_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    (int)tcd::SMEM_BYTES)
+                             : cudaFuncSetAttribute(tcd::tc_decode_kernel<tcd::RPT_MAX>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
   }
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
-  tcd::tc_decode_kernel<<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+  if (v == 0)
+    tcd::tc_decode_kernel<1><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+  else if (v == 1)
+    tcd::tc_decode_kernel<2><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+  else
+    tcd::tc_decode_kernel<tcd::RPT_MAX><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
   return cudaGetLastError();
 }
 

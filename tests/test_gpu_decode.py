@@ -76,7 +76,8 @@ def _paged_case(rng, B, hq, hkv, ps, lo, hi, kind="outlier"):
     return Q, Kc, Vc, pt, ctx
 
 
-@pytest.mark.parametrize("hq,hkv,ps,splits", [(4, 2, 16, 1), (4, 2, 16, 4), (8, 1, 5, 2), (3, 3, 32, 1)])
+@pytest.mark.parametrize("hq,hkv,ps,splits", [(4, 2, 16, 1), (4, 2, 16, 4), (8, 1, 5, 2), (3, 3, 32, 1), (8, 2, 16, 3),
+                                             (12, 4, 8, 1)])
 def test_decode_paged_matches_csr_and_oracle(hq, hkv, ps, splits):
     import torch
 
