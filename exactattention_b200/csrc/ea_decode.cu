@@ -437,14 +437,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           w[4 * j + 2] = a.z;
           w[4 * j + 3] = a.w;
         }
-        uint32_t mx = 0, mn = 0xFFFFFFFFu;
+        uint32_t mx = 0, mk = NZ_NONE;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
-          mx = __vmaxu2(mx, w[q] & 0x7FFF7FFFu);
-          mn = __vminu2(mn, nz_mag_minus1(w[q]));
+          const uint32_t m = w[q] & 0x7FFF7FFFu;
+          mx = __vmaxu2(mx, m);
+          mk = __vmins2(mk, nz_key(m));
         }
         mx = max(mx & 0xFFFFu, mx >> 16);
-        mn = min(mn & 0xFFFFu, mn >> 16);
+        int32_t mn = nz_key_min(mk);
 #pragma unroll
         for (int o = 1; o < 4; o <<= 1) {
           mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -454,7 +455,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
         const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
         const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
-        const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 && mn + 1 >= ((uint32_t)ebase << 7));
+        const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 &&
+                                                (mn == 32767 || nz_key_mag(mn) >= ((uint32_t)ebase << 7)));
         const float sc = scale_of(max(-126, min(126, lsb)));
         uint32_t lm = 0;  // lossy elements, bit = dim - 32 l4
 #pragma unroll
@@ -537,15 +539,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int cp = ptid & 63, kq = ptid >> 6;
       const uint8_t* vsrc = rawv + (32 * kq) * (DV * 2) + cp * 4;  // word of key 32 kq + jj at jj * 256
       const int nv = min(32, max(0, nvalid - 32 * kq));             // this thread's valid keys
-      uint32_t vmn;  // per channel (half) the smallest nonzero |v| - 1 over this thread's keys
+      uint32_t vmn;  // per channel (half) the key of the smallest nonzero |v| over this thread's keys
       {
         uint32_t mx = 0;
-        vmn = 0xFFFFFFFFu;
+        vmn = NZ_NONE;
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) {
-          const uint32_t w = jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u;
-          mx = __vmaxu2(mx, w & 0x7FFF7FFFu);
-          vmn = __vminu2(vmn, nz_mag_minus1(w));
+          const uint32_t m = (jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u) & 0x7FFF7FFFu;
+          mx = __vmaxu2(mx, m);
+          vmn = __vmins2(vmn, nz_key(m));
         }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -625,9 +627,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         for (int hh = 0; hh < 2; ++hh) {
           const int cc = 2 * cp + hh;
           const uint32_t thr = keep2[hh] ? ((uint32_t)max(ebase2[hh], 0) << 7) : 0x8000u;  // all, when bounded
-          const uint32_t mn = (vmn >> (16 * hh)) & 0xFFFFu;
+          const int32_t mk = (int32_t)(int16_t)((vmn >> (16 * hh)) & 0xFFFFu);
           uint32_t lossy = 0;
-          if (mn + 1 < thr) {
+          if (mk != 32767 && nz_key_mag(mk) < thr) {
 #pragma unroll 1
             for (int jj = 0; jj < nv; ++jj) {
               const uint32_t b = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0xFFFFu;

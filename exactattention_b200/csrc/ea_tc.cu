@@ -381,14 +381,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
         for (int i = 0; i < 8; ++i) w[i] = 0u;
       }
-      uint32_t mx = 0, mn = 0xFFFFFFFFu;
+      uint32_t mx = 0, mk = NZ_NONE;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        mx = __vmaxu2(mx, w[i] & 0x7FFF7FFFu);
-        mn = __vminu2(mn, nz_mag_minus1(w[i]));
+        const uint32_t m = w[i] & 0x7FFF7FFFu;
+        mx = __vmaxu2(mx, m);
+        mk = __vmins2(mk, nz_key(m));
       }
       mx = max(mx & 0xFFFFu, mx >> 16);
-      mn = min(mn & 0xFFFFu, mn >> 16);
+      int32_t mn = nz_key_min(mk);
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
         mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -398,7 +399,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
       const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
-      const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 && mn + 1 >= ((uint32_t)ebase << 7));
+      const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 &&
+                                              (mn == 32767 || nz_key_mag(mn) >= ((uint32_t)ebase << 7)));
       uint32_t lmask = 0;
       uint32_t x[16];
       if (lead == INT32_MIN) {

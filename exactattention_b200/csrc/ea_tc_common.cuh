@@ -120,10 +120,16 @@ __device__ __forceinline__ uint32_t fixf_lo(uint32_t w, float sc) {
 __device__ __forceinline__ uint32_t fixf_hi(uint32_t w, float sc) {
   return (uint32_t)__float2int_rz(__uint_as_float(w & 0xFFFF0000u) * sc);
 }
-// per 16-bit half: |bf16| - 1, with 0xFFFF for a zero (so a min finds the smallest nonzero)
-__device__ __forceinline__ uint32_t nz_mag_minus1(uint32_t w) {
-  return ((w & 0x7FFF7FFFu) + 0x7FFF7FFFu) ^ 0x80008000u;
-}
+// Smallest nonzero magnitude of bf16 halves with one signed 16x2 min per word: a nonzero
+// magnitude m (1 .. 0x7FFF) maps to m + 0x7FFF (0x8000 .. 0xFFFE, i.e. -32768 .. -2 as signed
+// halves, increasing with m) and zero to 0x7FFF (+32767, larger than every nonzero one); the
+// 32-bit add cannot carry between halves. NZ_NONE is the start value and the "all zero" result.
+constexpr uint32_t NZ_NONE = 0x7FFF7FFFu;
+__device__ __forceinline__ uint32_t nz_key(uint32_t mag2) { return mag2 + 0x7FFF7FFFu; }  // mag2 = w & 0x7FFF7FFF
+// the smaller of the two halves' keys, as a signed int (32767: no nonzero magnitude)
+__device__ __forceinline__ int32_t nz_key_min(uint32_t k) { return min((int32_t)(int16_t)(k & 0xFFFFu), (int32_t)(int16_t)(k >> 16)); }
+// the magnitude a key (< 32767) stands for
+__device__ __forceinline__ uint32_t nz_key_mag(int32_t k) { return (uint32_t)(k + 32769); }
 // 4 x 4 byte transpose: p_k = bytes k of x0 .. x3
 __device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
                                            uint32_t& p1, uint32_t& p2, uint32_t& p3) {
