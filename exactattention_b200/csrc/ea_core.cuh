@@ -16,6 +16,14 @@ enum MaskKind { MASK_CSR = 0, MASK_RANGE = 1, MASK_PAGED = 2, MASK_HYBRID = 3 };
 enum Status { ST_OK = 0, ST_TIER3 = 1, ST_DOMAIN = 2 };
 
 constexpr int32_t R_EMPTY = INT32_MIN;
+// The reference refuses rows whose weight exponents spread over more than 2^20
+// (reference.py:30, 116-118). Tier 1 sends a row to tier 3 (which decides the spread exactly)
+// when one unit of work sees its logits span more than SPREAD_CHECK (R - lowest floor(t)), and
+// the merge of units does when a unit's R lies more than SPREAD_CHECK below the row's: together
+// these cover every spread above 2^20 - 16. A KV shard marks a far-below partial by adding
+// SPREAD_MARK to its Zerr (a legitimate Zerr stays below 2^40), which survives the sum.
+constexpr int32_t SPREAD_CHECK = (1 << 19) - 8;
+constexpr uint64_t SPREAD_MARK = 1ull << 56;
 
 // Device statistics counters (accumulated, never reset by a launch).
 enum Stat {

@@ -87,7 +87,8 @@ struct Small {
   int32_t qlsb[GD];
   int32_t rst[GD];
   uint32_t qlossy[GD][4];
-  int32_t rt[4][GD];  // per lane quadrant
+  int32_t rt[4][GD];    // per lane quadrant
+  int32_t rtlo[4][GD];  // lowest floor(t) per lane quadrant (the exponent-spread check)
   uint64_t zs[4][GD];
   uint32_t zl[4][GD];
   // producer -> consumer: raw K / V tiles landed (bulk copies), score MMAs done, value digits
@@ -385,6 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   // allows (below)
   const int FN = FZ + 40;
   int32_t R[RPT];
+  int32_t Tlo[RPT];  // lowest floor(t) of the row's keys in this split
   int64_t Z[RPT];
   i128 N[RPT];
   uint64_t Zerr[RPT];
@@ -392,6 +394,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     R[i] = R_EMPTY;
+    Tlo[i] = INT32_MAX;
     Z[i] = 0;
     N[i] = 0;
     Zerr[i] = 0;
@@ -760,10 +763,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           sT[g * BK + key] = out;
           // tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1)
           const float tf = __uint_as_float(out);
-          int32_t rl = INT32_MIN;
-          if (out != T_MASKED && out != T_UNCERT && fabsf(tf) < 1073741824.0f) rl = __float2int_ru(tf) + 1;
+          int32_t rl = INT32_MIN, ll = INT32_MAX;
+          if (out != T_MASKED && out != T_UNCERT && fabsf(tf) < 1073741824.0f) {
+            rl = __float2int_ru(tf) + 1;
+            ll = __float2int_rd(tf);
+          }
           rl = __reduce_max_sync(0xffffffffu, rl);
-          if (lane == 0) S.rt[warp & 3][g] = rl;
+          ll = __reduce_min_sync(0xffffffffu, ll);
+          if (lane == 0) {
+            S.rt[warp & 3][g] = rl;
+            S.rtlo[warp & 3][g] = ll;
+          }
           unc |= out == T_UNCERT;
         }
       }
@@ -800,10 +810,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         for (int g = h; g < nrows; g += NWGC) {
           const uint32_t tb = sT[g * BK + c];
           const float tf = __uint_as_float(tb);
-          int32_t rl = INT32_MIN;
-          if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) rl = __float2int_ru(tf) + 1;
+          int32_t rl = INT32_MIN, ll = INT32_MAX;
+          if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) {
+            rl = __float2int_ru(tf) + 1;
+            ll = __float2int_rd(tf);
+          }
           rl = __reduce_max_sync(0xffffffffu, rl);
-          if (lane == 0) S.rt[warp & 3][g] = rl;
+          ll = __reduce_min_sync(0xffffffffu, ll);
+          if (lane == 0) {
+            S.rt[warp & 3][g] = rl;
+            S.rtlo[warp & 3][g] = ll;
+          }
         }
         group_sync(1);
       }
@@ -907,6 +924,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         }
         const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
         if (Rt == INT32_MIN) continue;
+        Tlo[ii] = min(Tlo[ii], min(min(S.rtlo[0][g], S.rtlo[1][g]), min(S.rtlo[2][g], S.rtlo[3][g])));
         const int32_t Rn = R[ii] == R_EMPTY ? Rt : max(R[ii], Rt);
         if (R[ii] != R_EMPTY && Rn > R[ii]) {
           const int d = Rn - R[ii];
@@ -1027,7 +1045,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int32_t row = S.rows[g];
       if (row < 0) continue;
       const int64_t pi = (int64_t)split * P.rows + row;
-      const int st = S.abort ? ST_TIER3 : S.rst[g];
+      int st = S.abort ? ST_TIER3 : S.rst[g];
+      // logits spanning more than SPREAD_CHECK below the bound: tier 3 decides the reference's
+      // exponent-spread rule
+      if (st == ST_OK && R[ii] != R_EMPTY && Tlo[ii] != INT32_MAX && (int64_t)R[ii] - Tlo[ii] > SPREAD_CHECK)
+        st = ST_TIER3;
       if (c == 0) {
         const int dsh = FZ - P.FZ;
         const int64_t zlo = shift_floor(Z[ii], -dsh);

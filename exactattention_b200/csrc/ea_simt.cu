@@ -51,6 +51,11 @@ __device__ __forceinline__ int warp_max32(int x) {
   for (int o = 16; o; o >>= 1) x = max(x, __shfl_xor_sync(0xffffffffu, x, o));
   return x;
 }
+__device__ __forceinline__ int warp_min32(int x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x = min(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
 
 // Block fixed point of one bf16 value at lsb: sign * trunc(|m| 2^(e - lsb)), and whether bits
 // were dropped. Callers guarantee e - lsb <= W - bitlen(|m|) (the value fits the window).
@@ -202,6 +207,7 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
   __syncwarp();
 
   int32_t R = R_EMPTY;
+  int32_t Rlo = INT32_MAX;  // lowest E + 24 seen (the logit spread check)
   int64_t Z = 0;
   uint64_t Ze = 0;
   int32_t NR[CPL];
@@ -302,6 +308,7 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
     }
     // ---- tile partial: Z ----
     int32_t Rt = warp_max32(valid ? E + 24 : INT32_MIN);
+    Rlo = min(Rlo, warp_min32(valid ? E + 24 : INT32_MAX));
     int64_t zt = 0;
     int zl = 0;
     if (valid) zt = floor_shift((int64_t)M, E + FZ - Rt, zl);
@@ -359,6 +366,7 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
     stat_add(P, STAT_PAIRS, (unsigned long long)(j1 - j0));
   }
 
+  if (status == ST_OK && R != R_EMPTY && Rlo != INT32_MAX && (int64_t)R - Rlo > SPREAD_CHECK) status = ST_TIER3;
   if (S == 1) {
     if (P.export_partials)
       export_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
@@ -393,12 +401,18 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
   if (r >= P.rows) return;
   const int S = P.splits, dv = P.dv;
   int status = ST_OK;
-  int32_t R = R_EMPTY;
+  int32_t R = R_EMPTY, Rmin = INT32_MAX;
   for (int s = 0; s < S; ++s) {
     int64_t pi = (int64_t)s * P.rows + r;
     status = max(status, P.pSt[pi]);
-    if (P.pR[pi] != R_EMPTY) R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
+    if (P.pR[pi] != R_EMPTY) {
+      R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
+      Rmin = min(Rmin, P.pR[pi]);
+    }
   }
+  // a split far below the row's largest weights: the exponent spread may exceed the reference's
+  // limit (tier 3 decides)
+  if (status == ST_OK && R != R_EMPTY && (int64_t)R - Rmin > SPREAD_CHECK) status = ST_TIER3;
   int64_t Z = 0;
   uint64_t Ze = 0;
   bool ok = true;
@@ -468,6 +482,7 @@ __global__ void partials_rescale_kernel(Prob P, const int32_t* Rg, const int32_t
       int64_t z = P.xZ[r];
       uint64_t ze = P.xZe[r];
       rescale(z, ze, G - R);
+      if ((int64_t)G - R > SPREAD_CHECK) ze += SPREAD_MARK;  // far below the row's maximum: mark
       P.xZ[r] = z;
       P.xZe[r] = ze;
     }
@@ -503,7 +518,8 @@ __global__ void __launch_bounds__(128) partials_finalize_kernel(Prob P) {
     if (lane == 0) P.flags[r] = 2;
     return;
   }
-  bool ok = status == ST_OK && (R == R_EMPTY || fits63(Z, Ze));
+  // (a shard marked its partial far below the row's maximum: the wide tier decides the spread)
+  bool ok = status == ST_OK && (R == R_EMPTY || (fits63(Z, Ze) && Ze < SPREAD_MARK));
   Rnd res[CPL];
 #pragma unroll
   for (int i = 0; i < CPL; ++i) {

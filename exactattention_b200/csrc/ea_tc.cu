@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
   for (int c = 0; c < 32; ++c) N[c] = 0;
   uint32_t phase = 0;
+  float tlo = INFINITY;  // this thread's lowest certified logit (the exponent-spread check)
   uint32_t pv_phase = 0, pv_pending = 0;  // P.V barriers: phase bits, commits in flight (by parity)
   bool ok_wait = true;
   unsigned n_exact = 0, n_wide = 0;
@@ -548,7 +549,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       int rstat = ST_OK;
       // the tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1),
       // and ceil is monotone (the ceiling of the largest logit); |t| >= 2^30 goes to tier 3
-      float tmax = -INFINITY;
+      float tmax = -INFINITY, tmin = INFINITY;
 #pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t dg[NGS][4];
@@ -650,12 +651,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         for (int u = 0; u < 4; ++u) {
           sT[r * T_PITCH + 16 * u4 + 4 * c4 + u] = outv[u];
           const float tf = __uint_as_float(outv[u]);
-          if (fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);  // false for the NaN markers
+          if (fabsf(tf) < 1073741824.0f) {  // false for the NaN markers
+            tmax = fmaxf(tmax, tf);
+            tmin = fminf(tmin, tf);
+          }
           any_unc |= outv[u] == T_UNCERT;
         }
       }
       if (rstat != ST_OK) atomicMax(&S.rst[r], rstat);
       S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
+      tlo = fminf(tlo, tmin);
     }
     tc::fence_before_sync();
     const bool tile_unc = __syncthreads_or(any_unc);
@@ -692,7 +697,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
           const float tf = __uint_as_float(sT[r * T_PITCH + 16 * u4 + u]);
-          if (fabsf(tf) < 1073741824.0f) tmax = fmaxf(tmax, tf);
+          if (fabsf(tf) < 1073741824.0f) {
+            tmax = fmaxf(tmax, tf);
+            tlo = fminf(tlo, tf);
+          }
         }
         S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;
       }
@@ -901,6 +909,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   }
 
   EA_PT(9)
+  // the row's logits spanning more than SPREAD_CHECK below its bound: tier 3 decides the
+  // reference's exponent-spread rule (the four threads of a row pool their lowest logits)
+  S.rt[u4][r] = tlo == INFINITY ? INT32_MAX : __float2int_rd(tlo);
+  __syncthreads();
+  if (u4 == 0 && R != R_EMPTY) {
+    const int32_t lo = min(min(S.rt[0][r], S.rt[1][r]), min(S.rt[2][r], S.rt[3][r]));
+    if (lo != INT32_MAX && (int64_t)R - lo > SPREAD_CHECK) atomicMax(&S.rst[r], ST_TIER3);
+  }
+  __syncthreads();
   // ---------------- export (KV-sharded runs) or finalise ----------------
   if (P.export_partials) {
     // partials in the one-sided form [N, N + Nerr] of ea_partials_t: this kernel's N interval is

@@ -206,3 +206,36 @@ def test_kv_shards_wide_tier_rows():
     assert torch.equal(out, full)
     o = out.cpu().numpy().view(np.uint16)
     assert np.array_equal(o[0], exact.attention_row(Q[0], K, V, alpha))
+
+
+def test_spread_across_shards_is_a_domain_error():
+    """Each shard's logits span little, but one shard's lie 2^21 below the other's: the merged row
+    breaks the reference's exponent-spread rule (reference.py:30, 116-118) and must be flagged."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    f2b = lambda x: np.uint16(exact.f32_to_bits(np.float32(x)) >> 16)  # noqa: E731
+    rng = np.random.default_rng(91)
+    n, rows = 400, 4
+    K, V = bf16(rng, (n, 128)), bf16(rng, (n, 128))
+    Q = bf16(rng, (rows, 128))
+    Q[:, 0] = f2b(64.0)
+    K[:, 0] = 0
+    K[200:, 0] = f2b(-262144.0)  # every key of the second half: t ~ -2^21
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    kl = np.array([150, 400, 300, 199], np.int64)
+    sees = (kl > 200)
+    parts, shard_args = [], []
+    for lo, hi in [(0, 200), (200, n)]:
+        m = dict(kv_base=t(np.zeros(rows, np.int64)), kv_len=t(np.clip(kl - lo, 0, hi - lo)))
+        shard_args.append((t(Q), t(K[lo:hi]), t(V[lo:hi]), alpha, m))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
+    out, flags = cuda.finalize_partials(merge_local(parts), n)
+    finish_local(shard_args, out, flags, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(flags.cpu().numpy() == 2, sees)

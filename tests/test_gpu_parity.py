@@ -512,3 +512,45 @@ def test_tensor_core_prefill_fp32_output(ea):
         L = int(kl[r])
         exp = exact.attention_row(Q[r], K[:L], V[:L], alpha, out="fp32")
         assert np.array_equal(out[r], np.asarray(exp).view(np.uint32)), r
+
+
+def test_weight_exponent_spread_is_a_domain_error(ea):
+    """A row whose logits span more than 2^20 (so its weights' exponents do) is a domain error in
+    the reference (reference.py:30, 116-118), also when the small weights are negligible: every
+    tier-1 path must flag it, not round it."""
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    f2b = lambda x: np.uint16(exact.f32_to_bits(np.float32(x)) >> 16)  # noqa: E731
+    rng = np.random.default_rng(90)
+    n, rows = 300, 16
+    K, V = bf16(rng, (n, 128)), bf16(rng, (n, 128))
+    Q = bf16(rng, (rows, 128))
+    Q[:, 0] = f2b(64.0)
+    K[:, 0] = 0
+    K[150, 0] = f2b(-262144.0)  # t ~ -2^21 for every row that sees key 150
+    kb = np.zeros(rows, np.int64)
+    kl = np.array([100, 200, 300, 151] * 4, np.int64)
+    sees = kl > 150
+    for r in (0, 1):
+        L = int(kl[r])
+        try:
+            exact.attention_row(Q[r], K[:L], V[:L], ea.default_alpha(128))
+            assert not sees[r]
+        except exact.ExactAttentionDomainError:
+            assert sees[r]
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    paths = {
+        "simt": dict(),
+        "tc_prefill": dict(blocks=t(cuda.row_blocks(kb, kl))),
+        "decode": dict(segments=t(cuda.row_segments(kb)), splits=2),
+    }
+    for name, extra in paths.items():
+        o, f = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), **extra)
+        torch.cuda.synchronize()
+        assert np.array_equal(f.cpu().numpy() == 2, sees), name
+        assert not o[torch.from_numpy(sees).to(dev)].any().item(), name
