@@ -20,7 +20,8 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_reserve_workspace", "ea_cuda_release", "ea_cuda_last_error", "ea_attention_cuda_noalloc",
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
-           "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda", "ea_selftest_fast64")
+           "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda", "ea_selftest_fast64",
+           "ea_merge_partials_nccl")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -115,6 +116,8 @@ def load(path: str | None = None):
     lib.ea_kernel_timing.restype = ctypes.c_int
     lib.ea_selftest_fast64.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int64, P]
     lib.ea_selftest_fast64.restype = ctypes.c_int
+    lib.ea_merge_partials_nccl.argtypes = [ctypes.POINTER(PartialsArgs), ctypes.c_int64, ctypes.c_int, P, P]
+    lib.ea_merge_partials_nccl.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
     lib.ea_reserve_workspace.restype = ctypes.c_int
     lib.ea_cuda_release.argtypes = []

@@ -11,7 +11,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libexactattn_cuda.so")
 SOURCES = ["ea_simt.cu", "ea_tc.cu", "ea_decode.cu", "ea_api.cu", "ea_synth.cu", "ea_noalloc.cu", "ea_cache.cu",
-           "ea_selftest.cu"]
+           "ea_selftest.cu", "ea_nccl.cu"]
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-shared"]
 

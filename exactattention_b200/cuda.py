@@ -260,6 +260,18 @@ def rescale_partials(parts: Partials, R_global, NR_global, stream=None) -> None:
                    "ea_partials_rescale_cuda")
 
 
+def merge_partials_nccl(parts: Partials, nccl_comm: int, stream=None) -> None:
+    """The KV-shard merge over a raw NCCL communicator (an ncclComm_t address), in place
+    (ea_merge_partials_nccl): the C form of exactattention_b200.dist.merge_partials."""
+    import torch
+
+    p = parts.struct()
+    dev = parts.i32.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_merge_partials_nccl(ctypes.byref(p), parts.rows, parts.dv, ctypes.c_void_p(nccl_comm),
+                                                      ctypes.c_void_p(_stream(dev, stream))), "ea_merge_partials_nccl")
+
+
 def finalize_partials(parts: Partials, max_row_keys: int, out="bf16", stats=None, stream=None):
     """Certified outputs from merged partials (ea_partials_finalize_cuda): (out bits, flags)."""
     import torch

@@ -178,6 +178,16 @@ int ea_partials_rescale_cuda(const ea_partials_t* parts, const int32_t* R_global
 int ea_partials_finalize_cuda(const ea_partials_t* parts, int64_t rows, int dv, int64_t max_row_keys,
                               int fp32_out, void* out, uint8_t* flags, int64_t* stats, void* stream);
 
+/* The whole KV-shard merge of `parts` over the caller's NCCL communicator (an ncclComm_t passed
+ * as void*), on `stream`: all-reduce MAX of R, status and NR, ea_partials_rescale_cuda, all-reduce
+ * SUM of Z, Zerr, N and Nerr; then ea_partials_finalize_cuda gives every rank the same rows. Every
+ * rank calls it with the same rows and dv (also rows = 0). NCCL (libnccl.so.2) is loaded at run
+ * time, preferring a copy the process already loaded, so the communicator must come from that
+ * library. Returns 0, -1 bad arguments, -4 CUDA error, -7 NCCL not found, -8 an NCCL call failed.
+ * The Python form is exactattention_b200/dist.py (torch.distributed). No reference counterpart
+ * (the reference runs on one device). */
+int ea_merge_partials_nccl(const ea_partials_t* parts, int64_t rows, int dv, void* nccl_comm, void* stream);
+
 /* Wide (tier-3) partials for the rows ea_partials_finalize_cuda flagged 1, so that KV-sharded
  * runs finish every row on the devices. Per listed row i (device pointers):
  *   maxv[4 i + 0..3]  R (reference exponent, INT64_MIN: no keys), Emax, -Emin (weight exponent

@@ -125,3 +125,73 @@ def test_nccl_c5_sharded_sha(tmp_path):
         assert not np.load(tmp_path / f"c5_flags_{r}.npy").any()
         out = np.load(tmp_path / f"c5_out_{r}.npy").view(np.uint16)
         assert hashlib.sha256(np.ascontiguousarray(out).tobytes()).hexdigest() == gold, r
+
+
+def _raw_comm_worker(rank, world, port, result_dir):
+    """ea_merge_partials_nccl on a communicator made directly with NCCL's C API (as a C / C++
+    server would hold one), the unique id exchanged through the process group's store; the same
+    partials merged by dist.merge_partials (torch.distributed) must come out bit for bit equal."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda, dist as ea_dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    nccl = ctypes.CDLL("libnccl.so.2")
+
+    class UniqueId(ctypes.Structure):
+        _fields_ = [("internal", ctypes.c_byte * 128)]
+
+    uid = UniqueId()
+    idt = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        assert nccl.ncclGetUniqueId(ctypes.byref(uid)) == 0
+        idt.copy_(torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(uid), 128)), dtype=torch.uint8))
+    dist.broadcast(idt, 0)
+    ctypes.memmove(ctypes.addressof(uid), bytes(idt.cpu().numpy().tobytes()), 128)
+    comm = ctypes.c_void_p()
+    nccl.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, UniqueId, ctypes.c_int]
+    assert nccl.ncclCommInitRank(ctypes.byref(comm), world, uid, rank) == 0
+    try:
+        Q, K, V, kl = _case()
+        n = K.shape[0]
+        lo, hi = n * rank // world, n * (rank + 1) // world
+        t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        args = (t(Q), t(K[lo:hi]), t(V[lo:hi]), ea.default_alpha(128))
+        mask = dict(kv_base=t(np.zeros_like(kl)), kv_len=t(klen))
+        pa = cuda.partials(*args, max_row_keys=n, **mask)
+        pb = cuda.partials(*args, max_row_keys=n, **mask)
+        ea_dist.merge_partials(pa)
+        cuda.merge_partials_nccl(pb, comm.value)
+        torch.cuda.synchronize(dev)
+        same = torch.equal(pa.i32, pb.i32) and torch.equal(pa.i64, pb.i64)
+        oa, fa = cuda.finalize_partials(pa, n)
+        ob, fb = cuda.finalize_partials(pb, n)
+        torch.cuda.synchronize(dev)
+        same = same and torch.equal(oa, ob) and torch.equal(fa, fb)
+        np.save(os.path.join(result_dir, f"raw_same_{rank}.npy"), np.array([same]))
+        dist.barrier()
+    finally:
+        nccl.ncclCommDestroy(comm)
+        dist.destroy_process_group()
+
+
+def test_merge_partials_nccl_raw_communicator(tmp_path):
+    """The C-ABI merge over a raw NCCL communicator equals the torch.distributed merge."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_raw_comm_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        assert bool(np.load(tmp_path / f"raw_same_{r}.npy")[0]), r
