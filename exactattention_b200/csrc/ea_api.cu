@@ -5,6 +5,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <deque>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -23,6 +24,7 @@ cudaError_t launch_combine(const Prob& P, cudaStream_t st);
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
+void nccl_release_scratch();  // ea_nccl.cu
 }  // namespace ea
 
 using namespace ea;
@@ -36,9 +38,14 @@ int fail_cuda(cudaError_t e, const char* where) {
   return -4;
 }
 
-// Grow-only device buffers of one device.
+// Grow-only device buffers of one device. Each device has two: one for the device-pointer entry
+// points (callers order their launches on one device) and one for the synchronous host-pointer
+// entry points, whose calls host_mu serialises, so that concurrent host calls (the reference's C
+// entry is reentrant) never share staging or partial buffers with work in flight.
 struct Workspace {
   int device = -1;
+  bool host = false;
+  std::mutex host_mu;
   int sms = 148;
   unsigned long long* stats = nullptr;  // STAT_LEN
   int* t3_count = nullptr;
@@ -46,28 +53,41 @@ struct Workspace {
   int64_t t3_cap = 0;
   void* part = nullptr;
   size_t part_bytes = 0;
-  // staging for the host-pointer entry point
+  // staging for the host-pointer entry point, and the row lists it builds on the host (pinned)
+  // and copies (device)
   void* stage = nullptr;
   size_t stage_bytes = 0;
+  int32_t* lists_h = nullptr;
+  size_t lists_h_bytes = 0;
+  void* lists = nullptr;
+  size_t lists_bytes = 0;
   cudaStream_t stream = nullptr;
 };
 
 std::mutex g_mu;
-std::vector<Workspace> g_ws;
+std::deque<Workspace> g_ws;  // a deque: workspaces never move once made
 
-Workspace* workspace() {
+// the current device's workspace (call with g_mu held)
+Workspace* workspace(bool host = false) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
   for (auto& w : g_ws)
-    if (w.device == dev) return &w;
-  Workspace w;
+    if (w.device == dev && w.host == host) return &w;
+  unsigned long long* stats = nullptr;
+  int* t3_count = nullptr;
+  if (cudaMalloc(&stats, STAT_LEN * sizeof(unsigned long long)) != cudaSuccess) return nullptr;
+  if (cudaMalloc(&t3_count, sizeof(int)) != cudaSuccess) {
+    cudaFree(stats);
+    return nullptr;
+  }
+  cudaMemset(stats, 0, STAT_LEN * sizeof(unsigned long long));
+  Workspace& w = g_ws.emplace_back();
   w.device = dev;
+  w.host = host;
   cudaDeviceGetAttribute(&w.sms, cudaDevAttrMultiProcessorCount, dev);
-  if (cudaMalloc(&w.stats, STAT_LEN * sizeof(unsigned long long)) != cudaSuccess) return nullptr;
-  if (cudaMalloc(&w.t3_count, sizeof(int)) != cudaSuccess) return nullptr;
-  cudaMemset(w.stats, 0, STAT_LEN * sizeof(unsigned long long));
-  g_ws.push_back(w);
-  return &g_ws.back();
+  w.stats = stats;
+  w.t3_count = t3_count;
+  return &w;
 }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -130,6 +150,7 @@ int ea_reserve_workspace(int64_t rows, int splits, int dv) {
 }
 
 void ea_cuda_release(void) {
+  nccl_release_scratch();
   std::lock_guard<std::mutex> lk(g_mu);
   int cur = 0;
   cudaGetDevice(&cur);
@@ -140,6 +161,8 @@ void ea_cuda_release(void) {
     if (w.t3_list) cudaFree(w.t3_list);
     if (w.part) cudaFree(w.part);
     if (w.stage) cudaFree(w.stage);
+    if (w.lists) cudaFree(w.lists);
+    if (w.lists_h) cudaFreeHost(w.lists_h);
     if (w.stream) cudaStreamDestroy(w.stream);
   }
   g_ws.clear();
@@ -353,14 +376,9 @@ static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st
   return 0;
 }
 
-int ea_launch_cuda(const ea_launch_t* a, void* stream) {
-  int rc = check_launch(a);
-  if (rc) return rc;
-  if (a->rows == 0) return 0;
-  std::lock_guard<std::mutex> lk(g_mu);
-  Workspace* w = workspace();
-  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-  cudaStream_t st = (cudaStream_t)stream;
+// the launch sequence of one problem on workspace w (g_mu held)
+static int launch_on(const ea_launch_t* a, Workspace* w, cudaStream_t st) {
+  int rc;
   if (hybrid_tc_applicable(a)) return launch_hybrid_tc(a, w, st);
   if (decode_applicable(a)) return launch_decode_tc(a, w, st);
   rc = reserve(w, a->rows, a->splits, a->dv);
@@ -381,6 +399,49 @@ int ea_launch_cuda(const ea_launch_t* a, void* stream) {
   e = launch_tier3(P, blocks, st);
   if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
   return 0;
+}
+
+int ea_launch_cuda(const ea_launch_t* a, void* stream) {
+  int rc = check_launch(a);
+  if (rc) return rc;
+  if (a->rows == 0) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace* w = workspace();
+  if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  return launch_on(a, w, (cudaStream_t)stream);
+}
+
+// The host-pointer entry points' workspace with its call lock taken: staging grown to `bytes`
+// and a library stream. Returns nullptr after recording the error.
+static Workspace* host_workspace(size_t bytes, std::unique_lock<std::mutex>& call) {
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace(true);
+    if (!w) {
+      fail_cuda(cudaGetLastError(), "workspace");
+      return nullptr;
+    }
+  }
+  call = std::unique_lock<std::mutex>(w->host_mu);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!grow(&w->stage, &w->stage_bytes, bytes)) {
+    fail_cuda(cudaErrorMemoryAllocation, "staging");
+    return nullptr;
+  }
+  if (!w->stream && cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    fail_cuda(cudaGetLastError(), "stream");
+    return nullptr;
+  }
+  return w;
+}
+
+// ea_launch_cuda on the host-pointer workspace (its call lock held)
+static int launch_host(const ea_launch_t* a, Workspace* w) {
+  int rc = check_launch(a);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return launch_on(a, w, w->stream);
 }
 
 static void set_export(Prob& P, const ea_partials_t* x) {
@@ -468,6 +529,39 @@ int ea_partials_finalize_cuda(const ea_partials_t* x, int64_t rows, int dv, int6
   return e == cudaSuccess ? 0 : fail_cuda(e, "finalize");
 }
 
+// Rows grouped by kv_base: `order` lists the rows group by group (increasing kv_base, a group's
+// rows in input order), group g being order[gstart[g] .. gstart[g + 1]). Rows already in
+// non-decreasing kv_base order (the usual layout) take one pass; others one stable sort.
+static void group_rows(const int64_t* kv_base, int64_t rows, std::vector<int32_t>& order,
+                       std::vector<int64_t>& gstart) {
+  order.resize((size_t)rows);
+  for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
+  bool sorted = true;
+  for (int64_t i = 1; i < rows && sorted; ++i) sorted = kv_base[i] >= kv_base[i - 1];
+  if (!sorted)
+    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) { return kv_base[x] < kv_base[y]; });
+  gstart.clear();
+  for (int64_t i = 0; i < rows; ++i)
+    if (i == 0 || kv_base[order[i]] != kv_base[order[i - 1]]) gstart.push_back(i);
+  gstart.push_back(rows);
+}
+
+// Rows [r0, r1) by decreasing kv_len, ties in their current order: a non-increasing run stays, a
+// strictly increasing one (causal rows) is reversed, anything else is stably sorted.
+static void order_by_len_desc(const int64_t* kv_len, int32_t* r0, int32_t* r1) {
+  bool noninc = true, inc = true;
+  for (int32_t* p = r0 + 1; p < r1; ++p) {
+    noninc = noninc && kv_len[p[0]] <= kv_len[p[-1]];
+    inc = inc && kv_len[p[0]] > kv_len[p[-1]];
+  }
+  if (noninc) return;
+  if (inc) {
+    std::reverse(r0, r1);
+    return;
+  }
+  std::stable_sort(r0, r1, [&](int32_t x, int32_t y) { return kv_len[x] > kv_len[y]; });
+}
+
 // Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back.
 // Exactly one of (row_ptr, key_idx) or (kv_base, kv_len) is used; neither: every key.
 static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v, int64_t nkeys,
@@ -476,7 +570,8 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
                     int64_t* stats) {
   int64_t total = row_ptr ? row_ptr[rows] : 0;
   const size_t osz = fp32_out ? 4 : 2;
-  // staging layout: q | k | v | mask | out | flags | stats
+  // staging layout: q | k | v | mask | out | flags | stats; the copies start before the host
+  // builds the row lists (blocks / segments) of a range mask
   size_t off = 0;
   auto slot = [&](size_t bytes) {
     size_t o = off;
@@ -487,74 +582,22 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   size_t orp = slot((size_t)(rows + 1) * 8), oki = slot((size_t)(row_ptr ? total : 0) * 8);
   size_t okb = slot((size_t)(row_ptr ? 0 : rows) * 8), okl = slot((size_t)(row_ptr ? 0 : rows) * 8);
   size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
-  // Range masks at d = dv = 128: rows sharing kv_base either form decode segments (at most 8 rows
-  // per key range: the decode kernel) or 128-row blocks, longest first (the prefill kernel).
-  std::vector<int32_t> blocks, segs;
-  bool decode = false;
-  if (kv_len_h && d == 128 && dv == 128 && rows < (1ll << 31)) {
-    std::vector<int32_t> order(rows);
-    for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
-    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) { return kv_base_h[x] < kv_base_h[y]; });
-    int64_t gmax = 0;
-    for (int64_t i = 0; i < rows;) {
-      int64_t j = i;
-      while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
-      gmax = std::max(gmax, j - i);
-      i = j;
-    }
-    decode = gmax <= 8;
-    if (decode) {
-      for (int64_t i = 0; i < rows;) {
-        int64_t j = i;
-        while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
-        std::vector<int32_t> sgm(8, -1);
-        for (int64_t u = i; u < j; ++u) sgm[u - i] = order[u];
-        segs.insert(segs.end(), sgm.begin(), sgm.end());
-        i = j;
-      }
-    }
-  }
-  if (!decode && kv_len_h && d == 128 && dv == 128 && splits == 1 && rows < (1ll << 31)) {
-    std::vector<int32_t> order(rows);
-    for (int64_t i = 0; i < rows; ++i) order[i] = (int32_t)i;
-    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) {
-      if (kv_base_h[x] != kv_base_h[y]) return kv_base_h[x] < kv_base_h[y];
-      return kv_len_h[x] > kv_len_h[y];
-    });
-    std::vector<std::vector<int32_t>> bl;
-    for (int64_t i = 0; i < rows;) {
-      int64_t j = i;
-      while (j < rows && kv_base_h[order[j]] == kv_base_h[order[i]]) ++j;
-      for (int64_t c = i; c < j; c += 128) {
-        std::vector<int32_t> b(128, -1);
-        for (int64_t u = c; u < j && u < c + 128; ++u) b[u - c] = order[u];
-        bl.push_back(b);
-      }
-      i = j;
-    }
-    std::stable_sort(bl.begin(), bl.end(), [&](const std::vector<int32_t>& x, const std::vector<int32_t>& y) {
-      return kv_len_h[x[0]] > kv_len_h[y[0]];
-    });
-    for (auto& b : bl) blocks.insert(blocks.end(), b.begin(), b.end());
-  }
-  size_t ob = slot(blocks.size() * 4), osg = slot(segs.size() * 4);
 
-  Workspace* w;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    w = workspace();
-    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-    if (!grow(&w->stage, &w->stage_bytes, off)) return fail_cuda(cudaErrorMemoryAllocation, "staging");
-    if (!w->stream && cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess)
-      return fail_cuda(cudaGetLastError(), "stream");
-  }
+  std::unique_lock<std::mutex> call;
+  Workspace* w = host_workspace(off, call);
+  if (!w) return -4;
   char* base = (char*)w->stage;
   cudaStream_t st = w->stream;
   cudaError_t e;
+  // an error after the first copy waits for the copies in flight before the call returns
+  auto fail = [&](cudaError_t err, const char* where) {
+    cudaStreamSynchronize(st);
+    return fail_cuda(err, where);
+  };
 #define EA_CPY(dst, src, n)                                                    \
   if ((n) > 0) {                                                              \
     e = cudaMemcpyAsync(base + (dst), (src), (n), cudaMemcpyHostToDevice, st); \
-    if (e != cudaSuccess) return fail_cuda(e, "h2d");                         \
+    if (e != cudaSuccess) return fail(e, "h2d");                              \
   }
   EA_CPY(oq, q, (size_t)rows * d * 2);
   EA_CPY(ok, k, (size_t)nkeys * d * 2);
@@ -572,11 +615,65 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
     EA_CPY(okb, kb.data(), (size_t)rows * 8);
     EA_CPY(okl, kl.data(), (size_t)rows * 8);
   }
-  EA_CPY(ob, blocks.data(), blocks.size() * 4);
-  EA_CPY(osg, segs.data(), segs.size() * 4);
 #undef EA_CPY
+  // Range masks at d = dv = 128: rows sharing kv_base either form decode segments (at most 8 rows
+  // per key range: the decode kernel) or 128-row blocks, longest first (the prefill kernel),
+  // built while the copies above run.
+  std::vector<int32_t> blocks, segs;
+  bool decode = false;
+  if (kv_len_h && d == 128 && dv == 128 && rows < (1ll << 31)) {
+    std::vector<int32_t> order;
+    std::vector<int64_t> gstart;
+    group_rows(kv_base_h, rows, order, gstart);
+    const int64_t ng = (int64_t)gstart.size() - 1;
+    int64_t gmax = 0;
+    for (int64_t g = 0; g < ng; ++g) gmax = std::max(gmax, gstart[g + 1] - gstart[g]);
+    decode = gmax <= 8;
+    if (decode) {
+      segs.assign((size_t)ng * 8, -1);
+      for (int64_t g = 0; g < ng; ++g)
+        for (int64_t u = gstart[g]; u < gstart[g + 1]; ++u) segs[(size_t)(8 * g + u - gstart[g])] = order[u];
+    } else if (splits == 1) {
+      // rows of a group by decreasing kv_len, cut into 128-row blocks; blocks by decreasing
+      // length of their first (longest) row
+      std::vector<int64_t> bst;  // first position in `order` of each block
+      for (int64_t g = 0; g < ng; ++g) {
+        order_by_len_desc(kv_len_h, order.data() + gstart[g], order.data() + gstart[g + 1]);
+        for (int64_t c = gstart[g]; c < gstart[g + 1]; c += 128) bst.push_back(c);
+      }
+      std::stable_sort(bst.begin(), bst.end(),
+                       [&](int64_t x, int64_t y) { return kv_len_h[order[x]] > kv_len_h[order[y]]; });
+      blocks.assign(bst.size() * 128, -1);
+      for (size_t i = 0; i < bst.size(); ++i) {
+        const int64_t c = bst[i];
+        const int64_t gend = gstart[std::upper_bound(gstart.begin(), gstart.end(), c) - gstart.begin()];
+        std::copy(order.begin() + c, order.begin() + std::min(c + 128, gend), blocks.begin() + 128 * i);
+      }
+    }
+  }
+  const size_t nlist = blocks.size() + segs.size();
+  if (nlist) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (w->lists_h_bytes < nlist * 4) {
+      if (w->lists_h) cudaFreeHost(w->lists_h);
+      w->lists_h = nullptr;
+      w->lists_h_bytes = 0;
+      if (cudaHostAlloc((void**)&w->lists_h, nlist * 4, cudaHostAllocDefault) != cudaSuccess)
+        return fail(cudaErrorMemoryAllocation, "row lists");
+      w->lists_h_bytes = nlist * 4;
+    }
+    if (!grow(&w->lists, &w->lists_bytes, nlist * 4)) return fail(cudaErrorMemoryAllocation, "row lists");
+  }
+  // the previous call's copy out of lists_h ended with its stream synchronisation
+  int32_t* lists_d = (int32_t*)w->lists;
+  if (nlist) {
+    std::copy(blocks.begin(), blocks.end(), w->lists_h);
+    std::copy(segs.begin(), segs.end(), w->lists_h + blocks.size());
+    e = cudaMemcpyAsync(lists_d, w->lists_h, nlist * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return fail(e, "h2d");
+  }
   e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st);
-  if (e != cudaSuccess) return fail_cuda(e, "memset");
+  if (e != cudaSuccess) return fail(e, "memset");
 
   ea_launch_t a;
   memset(&a, 0, sizeof(a));
@@ -599,17 +696,20 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.out = base + oo;
   a.flags = (uint8_t*)(base + of);
   a.stats = (int64_t*)(base + os);
-  a.block_rows = blocks.empty() ? nullptr : (const int32_t*)(base + ob);
+  a.block_rows = blocks.empty() ? nullptr : lists_d;
   a.nblocks = (int64_t)(blocks.size() / 128);
-  a.seg_rows = segs.empty() ? nullptr : (const int32_t*)(base + osg);
+  a.seg_rows = segs.empty() ? nullptr : lists_d + blocks.size();
   a.nsegs = (int64_t)(segs.size() / 8);
-  int rc = ea_launch_cuda(&a, st);
-  if (rc) return rc;
+  int rc = launch_host(&a, w);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
   int64_t hs[EA_STATS_LEN];
   if ((e = cudaMemcpyAsync(out, base + oo, (size_t)rows * dv * osz, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(flags, base + of, (size_t)rows, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(hs, base + os, sizeof(hs), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
-    return fail_cuda(e, "d2h");
+    return fail(e, "d2h");
   if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e, "sync");
   if (stats) {
     stats[0] += hs[STAT_SCORE_EXACT];
@@ -817,18 +917,17 @@ extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_h
   size_t oq = slot((size_t)rows * d * 2), ok = slot(cache * d * 2), ov = slot(cache * dv * 2);
   size_t opt = slot((size_t)batch * max_pages * 4), osl = slot((size_t)batch * 4);
   size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
-  Workspace* w;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    w = workspace();
-    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
-    if (!grow(&w->stage, &w->stage_bytes, off)) return fail_cuda(cudaErrorMemoryAllocation, "staging");
-    if (!w->stream && cudaStreamCreateWithFlags(&w->stream, cudaStreamNonBlocking) != cudaSuccess)
-      return fail_cuda(cudaGetLastError(), "stream");
-  }
+  std::unique_lock<std::mutex> call;
+  Workspace* w = host_workspace(off, call);
+  if (!w) return -4;
   char* base = (char*)w->stage;
   cudaStream_t st = w->stream;
   cudaError_t e;
+  // an error after the first copy waits for the copies in flight before the call returns
+  auto fail = [&](cudaError_t err, const char* where) {
+    cudaStreamSynchronize(st);
+    return fail_cuda(err, where);
+  };
   const struct {
     size_t dst;
     const void* src;
@@ -840,8 +939,8 @@ extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_h
              {osl, seq_lens, (size_t)batch * 4}};
   for (const auto& c : h2d)
     if (c.n && (e = cudaMemcpyAsync(base + c.dst, c.src, c.n, cudaMemcpyHostToDevice, st)) != cudaSuccess)
-      return fail_cuda(e, "h2d");
-  if ((e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st)) != cudaSuccess) return fail_cuda(e, "memset");
+      return fail(e, "h2d");
+  if ((e = cudaMemsetAsync(base + os, 0, EA_STATS_LEN * 8, st)) != cudaSuccess) return fail(e, "memset");
   ea_launch_t a;
   memset(&a, 0, sizeof(a));
   a.q = (const uint16_t*)(base + oq);
@@ -865,13 +964,16 @@ extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_h
   a.out = base + oo;
   a.flags = (uint8_t*)(base + of);
   a.stats = (int64_t*)(base + os);
-  int rc = ea_launch_cuda(&a, st);
-  if (rc) return rc;
+  int rc = launch_host(&a, w);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
+  }
   int64_t hs[EA_STATS_LEN];
   if ((e = cudaMemcpyAsync(out, base + oo, (size_t)rows * dv * osz, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(flags, base + of, (size_t)rows, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
       (e = cudaMemcpyAsync(hs, base + os, sizeof(hs), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
-    return fail_cuda(e, "d2h");
+    return fail(e, "d2h");
   if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return fail_cuda(e, "sync");
   if (stats) {
     stats[0] += hs[STAT_SCORE_EXACT];

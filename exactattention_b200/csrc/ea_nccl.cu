@@ -42,9 +42,9 @@ const NcclApi& nccl_api() {
   return api;
 }
 
-// per-device scratch for the global exponents (grow only)
+// per-device scratch for the global exponents (grow only); calls on one device share it, so a
+// caller orders its merges on one device (one stream, or events between streams)
 struct MergeScratch {
-  int device = -1;
   int32_t* buf = nullptr;
   size_t n = 0;
 };
@@ -67,6 +67,24 @@ int32_t* scratch(size_t n) {
 }
 
 }  // namespace
+
+namespace ea {
+// frees the merge scratch of every device (ea_cuda_release)
+void nccl_release_scratch() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (int d = 0; d < 64; ++d) {
+    MergeScratch& s = g_scratch[d];
+    if (!s.buf) continue;
+    cudaSetDevice(d);
+    cudaFree(s.buf);
+    s.buf = nullptr;
+    s.n = 0;
+  }
+  cudaSetDevice(cur);
+}
+}  // namespace ea
 
 extern "C" int ea_merge_partials_nccl(const ea_partials_t* parts, int64_t rows, int dv, void* nccl_comm,
                                       void* stream) {

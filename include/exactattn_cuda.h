@@ -30,7 +30,8 @@ extern "C" {
  * depend on them. splits partitions each row's keys into KV splits merged exactly.
  * out: rows x dv uint16 (bf16) or float (fp32_out). flags: rows bytes.
  * stats[0..2] += (scores recomputed exactly, weights recomputed with the 128-bit exp2,
- * rows sent to the wide tier). Synchronous. */
+ * rows sent to the wide tier). Synchronous and thread-safe: the host-pointer entry points share
+ * one staging workspace per device, and concurrent calls on one device run one after another. */
 int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
                       int64_t nkeys, int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx,
                       int fp32_out, int acc_bits, int tile, int splits, uint64_t order_seed, int nthreads,
@@ -138,7 +139,10 @@ typedef struct ea_launch {
 
 /* Device-pointer entry point: asynchronous on `stream` (a cudaStream_t, NULL = default).
  * Uses a library-owned workspace on the current device (grown outside any stream capture by
- * ea_reserve_workspace or on first use). The torch-tensor API builds on this. */
+ * ea_reserve_workspace or on first use). The device-pointer entry points of one device share it
+ * (split partials, tier-3 work list): launches on different streams of one device must be ordered
+ * (one stream, or events between streams), as with one cuBLAS handle. The host-pointer entry
+ * points use a workspace of their own. The torch-tensor API builds on this. */
 int ea_launch_cuda(const ea_launch_t* args, void* stream);
 
 /* Per-row partial state of one key range (the split partial of the reference's certified
@@ -184,7 +188,8 @@ int ea_partials_finalize_cuda(const ea_partials_t* parts, int64_t rows, int dv, 
  * rank calls it with the same rows and dv (also rows = 0). NCCL (libnccl.so.2) is loaded at run
  * time, preferring a copy the process already loaded, so the communicator must come from that
  * library. Returns 0, -1 bad arguments, -4 CUDA error, -7 NCCL not found, -8 an NCCL call failed.
- * The Python form is exactattention_b200/dist.py (torch.distributed). No reference counterpart
+ * Calls on one device share a scratch array (rows x (dv + 1) int32), so they are ordered like
+ * ea_launch_cuda's. The Python form is exactattention_b200/dist.py (torch.distributed). No reference counterpart
  * (the reference runs on one device). */
 int ea_merge_partials_nccl(const ea_partials_t* parts, int64_t rows, int dv, void* nccl_comm, void* stream);
 

@@ -406,6 +406,61 @@ def test_tensor_core_ragged_blocks_and_nan(ea):
     assert torch.equal(o_tc[ok], o_s[ok])
 
 
+def test_host_ranges_row_orders_and_threads(ea):
+    """ea_attention_cuda_ranges builds the prefill row blocks itself: rows in causal order (one
+    pass), rows permuted (sorted), and ragged ranges give the device launch's bits; calls from
+    several threads at once (the host entry is reentrant, as the reference's is) give each
+    call's sequential result."""
+    import threading
+
+    import torch
+
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(515)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    cases = []
+    for S, heads in ((300, 2), (520, 3)):
+        Q, K, V, kb, kl = _causal_case(rng, S, "outlier", "normal", heads)
+        cases.append((Q, K, V, kb, kl))
+    perm = rng.permutation(len(cases[0][0]))
+    Q, K, V, kb, kl = cases[0]
+    cases.append((Q[perm].copy(), K, V, kb[perm].copy(), kl[perm].copy()))
+    n = 700
+    K3, V3 = bf16(rng, (n, 128), "outlier"), bf16(rng, (n, 128))
+    kb3 = rng.choice([0, 90, 200, 350], size=400).astype(np.int64)
+    kl3 = rng.integers(1, n - 350, size=400).astype(np.int64)
+    cases.append((bf16(rng, (400, 128), "outlier"), K3, V3, kb3, kl3))
+    ref = []
+    for Q, K, V, kb, kl in cases:
+        o_d, f_d = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
+        ref.append((o_d.cpu().numpy().view(np.uint16), f_d.cpu().numpy()))
+        o_h, f_h = cuda.attention_cuda_ranges(Q, K, V, alpha, kb, kl)
+        assert np.array_equal(o_h, ref[-1][0]) and np.array_equal(f_h, ref[-1][1])
+    o0 = ref[0][0]
+    assert np.array_equal(ref[2][0], o0[perm])
+    res = [None] * 12
+    errs = []
+
+    def work(i):
+        try:
+            Q, K, V, kb, kl = cases[i % len(cases)]
+            res[i] = cuda.attention_cuda_ranges(Q, K, V, alpha, kb, kl)
+        except Exception as e:  # noqa: BLE001 - reported below
+            errs.append(repr(e))
+
+    th = [threading.Thread(target=work, args=(i,)) for i in range(len(res))]
+    for x in th:
+        x.start()
+    for x in th:
+        x.join()
+    assert not errs, errs
+    for i, (o, f) in enumerate(res):
+        assert np.array_equal(o, ref[i % len(cases)][0]) and np.array_equal(f, ref[i % len(cases)][1]), i
+
+
 def test_tensor_core_value_channel_edges(ea):
     """Value channels the tensor-core kernel must not take the fast conversion for: all zeros but
     one NaN (seen by some rows only), a subnormal next to normal values (bits below the window),
