@@ -799,6 +799,36 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     __syncthreads();
     EA_PT(5)
 
+    // ---------------- P.V MMAs in four rounds of two groups, drained into N ----------------
+    // Round rd (groups 2 rd, 2 rd + 1) accumulates in TMEM columns 256 (rd % 2) ..; round rd + 1 is
+    // issued before round rd is drained, so the tensor cores work while the CUDA cores drain, and
+    // rounds 0 and 1 go out before the merge below, which they overlap. A round's commit goes to
+    // the barrier of its parity (each completes once before it is waited on).
+    // group 2 rd + i is issued by lane 0 of warp 4 rd + 2 i (as the score groups)
+    auto issue_pv = [&](int rd) {
+      if (lane != 0 || (warp >> 2) != rd || (warp & 1)) return;
+      tc::fence_after_sync();
+      const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
+      {
+        const int g = 2 * rd + ((warp >> 1) & 1);
+        bool first = true;
+        for (int s = 0; s < NW; ++s) {
+          const int t = g - s;
+          if (t < 0 || t >= NV) continue;
+          const uint32_t idesc = tc::idesc_i8(128, DV, false, t == NV - 1);
+          for (int ks = 0; ks < BN / 32; ++ks) {
+            uint64_t ad = tc::smem_desc(aw + s * W_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
+            uint64_t bd = tc::smem_desc(bv + t * V_PLANE + ks * 2 * (DV / 8) * 128, (DV / 8) * 128, 128);
+            tc::mma_i8(tmem + 256 * (rd & 1) + DV * (g - 2 * rd), ad, bd, idesc, !first);
+            first = false;
+          }
+        }
+      }
+      tc::mma_commit(tc::smem_u32(&S.bar_pv[rd & 1]));
+    };
+    issue_pv(0);
+    issue_pv(1);
+    pv_pending = 3;  // bit b: the barrier of parity b has a commit in flight
     // ---------------- merge Z, rescale N, bounds ----------------
     int sh_base = 0;  // (Rt - FW - FV) - (R - FN): shift of a W.Vfix unit into N units
     if (Rt != INT32_MIN) {
@@ -831,35 +861,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     }
 
     EA_PT(6)
-    // ---------------- P.V MMAs in four rounds of two groups, drained into N ----------------
-    // Round rd (groups 2 rd, 2 rd + 1) accumulates in TMEM columns 256 (rd % 2) ..; round rd + 1 is
-    // issued before round rd is drained, so the tensor cores work while the CUDA cores drain. Its
-    // commit goes to the barrier of its parity (each completes once before it is waited on).
-    // group 2 rd + i is issued by lane 0 of warp 4 rd + 2 i (as the score groups)
-    auto issue_pv = [&](int rd) {
-      if (lane != 0 || (warp >> 2) != rd || (warp & 1)) return;
-      tc::fence_after_sync();
-      const uint32_t aw = tc::smem_u32(sW), bv = tc::smem_u32(sV);
-      {
-        const int g = 2 * rd + ((warp >> 1) & 1);
-        bool first = true;
-        for (int s = 0; s < NW; ++s) {
-          const int t = g - s;
-          if (t < 0 || t >= NV) continue;
-          const uint32_t idesc = tc::idesc_i8(128, DV, false, t == NV - 1);
-          for (int ks = 0; ks < BN / 32; ++ks) {
-            uint64_t ad = tc::smem_desc(aw + s * W_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
-            uint64_t bd = tc::smem_desc(bv + t * V_PLANE + ks * 2 * (DV / 8) * 128, (DV / 8) * 128, 128);
-            tc::mma_i8(tmem + 256 * (rd & 1) + DV * (g - 2 * rd), ad, bd, idesc, !first);
-            first = false;
-          }
-        }
-      }
-      tc::mma_commit(tc::smem_u32(&S.bar_pv[rd & 1]));
-    };
-    issue_pv(0);
-    issue_pv(1);
-    pv_pending = 3;  // bit b: the barrier of parity b has a commit in flight
 #pragma unroll 1
     for (int rd = 0; rd < 4; ++rd) {
       {
