@@ -546,11 +546,20 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       {
         uint32_t mx = 0;
         vmn = NZ_NONE;
+        if (nv == 32) {  // a full key quarter: no bounds test per load
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const uint32_t m = (jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u) & 0x7FFF7FFFu;
-          mx = __vmaxu2(mx, m);
-          vmn = __vmins2(vmn, nz_key(m));
+          for (int jj = 0; jj < 32; ++jj) {
+            const uint32_t m = *(const uint32_t*)(vsrc + jj * (DV * 2)) & 0x7FFF7FFFu;
+            mx = __vmaxu2(mx, m);
+            vmn = __vmins2(vmn, nz_key(m));
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const uint32_t m = (jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u) & 0x7FFF7FFFu;
+            mx = __vmaxu2(mx, m);
+            vmn = __vmins2(vmn, nz_key(m));
+          }
         }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -602,15 +611,25 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
           keep2[hh] = in_range ? 0xFFFFFFFFu : 0u;
           sc2[hh] = scale_of(in_range ? lsb2[hh] : 0);
         }
+        const bool plain = nv == 32 && (keep2[0] & keep2[1]) != 0u;
 #pragma unroll 1
         for (int q4 = 0; q4 < 2; ++q4) {
           uint32_t xa[16], xb[16];
+          if (plain) {  // the usual case: 32 valid keys, both channels keep digits
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int kk = 16 * q4 + jj;
-            const uint32_t w = kk < nv ? *(const uint32_t*)(vsrc + kk * (DV * 2)) : 0u;
-            xa[jj] = fixf_lo(w, sc2[0]) & keep2[0];
-            xb[jj] = fixf_hi(w, sc2[1]) & keep2[1];
+            for (int jj = 0; jj < 16; ++jj) {
+              const uint32_t w = *(const uint32_t*)(vsrc + (16 * q4 + jj) * (DV * 2));
+              xa[jj] = fixf_lo(w, sc2[0]);
+              xb[jj] = fixf_hi(w, sc2[1]);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int kk = 16 * q4 + jj;
+              const uint32_t w = kk < nv ? *(const uint32_t*)(vsrc + kk * (DV * 2)) : 0u;
+              xa[jj] = fixf_lo(w, sc2[0]) & keep2[0];
+              xb[jj] = fixf_hi(w, sc2[1]) & keep2[1];
+            }
           }
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
