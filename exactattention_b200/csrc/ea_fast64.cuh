@@ -128,16 +128,11 @@ __device__ __forceinline__ bool weight_f64(uint32_t tb, const uint64_t* tab, uin
   return in_range && (one || clear_of_mid(d));
 }
 
-// RN_p(a / b * 2^sh) for a < 2^63, 0 < b < 2^63, the result a normal number of the target
-// format: x = RN(RN(a) / RN(b)) has relative error below 3.01 u (u = 2^-53), about 6 ulps of x;
-// certified when the 53 - p dropped bits lie more than 8 ulps from their midpoint. 0: certain
-// (a == 0), 1: certified, -1: the integer division decides.
-__device__ __forceinline__ int ratio_f64(uint64_t a, uint64_t b, int sh, int neg, int p, int qmin, int emax,
-                                         Rnd& out) {
-  out = rnd_zero();
-  out.neg = neg;
-  if (a == 0) return 0;
-  const double x = __ddiv_rn(__ull2double_rn(a), __ull2double_rn(b));
+// RN_p of a binary64 estimate x of a ratio times 2^sh, the result a normal number of the target
+// format, given that |x - ratio| stays within 4.01 u |ratio| (u = 2^-53), i.e. a few ulps of x:
+// certified when the 53 - p dropped bits of x lie more than 8 ulps from their midpoint.
+// 1: certified (out set), -1: the integer division decides.
+__device__ __forceinline__ int round_ratio_estimate(double x, int sh, int p, int qmin, int emax, Rnd& out) {
   const uint64_t bits = (uint64_t)__double_as_longlong(x);
   const int K = (int)((bits >> 52) & 0x7FF) - 1023 + sh;  // 2^K <= value < 2^(K + 1), up to the error
   if (K - (p - 1) <= qmin || K >= emax) return -1;
@@ -155,6 +150,31 @@ __device__ __forceinline__ int ratio_f64(uint64_t a, uint64_t b, int sh, int neg
   out.q = q;
   out.qe = qe;
   return 1;
+}
+
+// RN_p(a / b * 2^sh) for a < 2^63, 0 < b < 2^63: x = RN(RN(a) / RN(b)) has relative error below
+// 3.01 u. 0: certain (a == 0), 1: certified, -1: the integer division decides.
+__device__ __forceinline__ int ratio_f64(uint64_t a, uint64_t b, int sh, int neg, int p, int qmin, int emax,
+                                         Rnd& out) {
+  out = rnd_zero();
+  out.neg = neg;
+  if (a == 0) return 0;
+  return round_ratio_estimate(__ddiv_rn(__ull2double_rn(a), __ull2double_rn(b)), sh, p, qmin, emax, out);
+}
+
+// The same from a reciprocal of the divisor shared by many ratios, rb = RN(1 / RN(b)):
+// x = RN(RN(a) rb) carries four roundings, relative error below (1 + u)^3 / (1 - u) - 1 < 4.01 u.
+__device__ __forceinline__ int ratio_f64_rcp(uint64_t a, double rb, int sh, int neg, int p, int qmin, int emax,
+                                             Rnd& out) {
+  out = rnd_zero();
+  out.neg = neg;
+  if (a == 0) return 0;
+  return round_ratio_estimate(__dmul_rn(__ull2double_rn(a), rb), sh, p, qmin, emax, out);
+}
+
+// RN(1 / RN(b)) for ratio_f64_rcp (b > 0), and 0 for b <= 0 (which the callers never divide by)
+__device__ __forceinline__ double recip_f64(int64_t b) {
+  return b > 0 ? __drcp_rn(__ull2double_rn((uint64_t)b)) : 0.0;
 }
 
 // certify_ratio_lh through ratio_f64: 1 certified (out set), 0 not certifiable (the ends differ),
@@ -177,6 +197,33 @@ __device__ __forceinline__ int certify_ratio_f64(int64_t nlo, int64_t nhi, int64
   Rnd rl, rh;
   const int cl = ratio_f64(ln, ld, sh, lneg, p, qmin, emax, rl);
   const int ch = ratio_f64(hn, hd, sh, hneg, p, qmin, emax, rh);
+  if (cl < 0 || ch < 0) return -1;
+  if (!rnd_eq(rl, rh)) return 0;
+  out = rl;
+  if (out.q == 0) out.neg = 0;
+  return 1;
+}
+
+// certify_ratio_f64 with the divisors' reciprocals given (rzlo = recip_f64(zlo), rzhi =
+// recip_f64(zhi)): a row's channels share one Z interval, so one pair of reciprocals serves all.
+__device__ __forceinline__ int certify_ratio_f64_rcp(int64_t nlo, int64_t nhi, int64_t nunit, int64_t zlo, int64_t zhi,
+                                                     double rzlo, double rzhi, int64_t zunit, int p, int qmin,
+                                                     int emax, Rnd& out) {
+  if (zlo <= 0 || zhi < zlo || nhi < nlo) return -1;
+  const int64_t sh64 = nunit - zunit;
+  if (sh64 > 100000 || sh64 < -100000) return -1;
+  const int sh = (int)sh64;
+  Rnd rl, rh;
+  int cl, ch;
+  if (nlo >= 0) {
+    cl = ratio_f64_rcp((uint64_t)nlo, rzhi, sh, 0, p, qmin, emax, rl);
+    ch = ratio_f64_rcp((uint64_t)nhi, rzlo, sh, 0, p, qmin, emax, rh);
+  } else if (nhi <= 0) {
+    cl = ratio_f64_rcp((uint64_t)(-nlo), rzlo, sh, 1, p, qmin, emax, rl);
+    ch = ratio_f64_rcp((uint64_t)(-nhi), rzhi, sh, 1, p, qmin, emax, rh);
+  } else {
+    return -1;  // the interval holds zero: the integer evaluation
+  }
   if (cl < 0 || ch < 0) return -1;
   if (!rnd_eq(rl, rh)) return 0;
   out = rl;

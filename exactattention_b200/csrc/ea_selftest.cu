@@ -7,6 +7,7 @@
 //     exponents from a splitmix64 stream; every certified fast logit must equal logit_exact64.
 //   mode 2 (output ratios): a / b * 2^sh for random a, b < 2^63 of random lengths, rounded to bf16
 //     and to fp32; every certified fast ratio must equal round_ratio64.
+//   mode 3: the same through the shared-reciprocal form (ratio_f64_rcp).
 // out[0] cases checked, out[1] certified by the fast path, out[2] mismatches, out[3] the input of
 // one mismatch (the fp32 bits of t, or the case index).
 #include <cuda_runtime.h>
@@ -81,7 +82,7 @@ __global__ void selftest_logit_kernel(uint64_t seed, int64_t n, unsigned long lo
   }
 }
 
-__global__ void selftest_ratio_kernel(uint64_t seed, int64_t n, unsigned long long* acc) {
+__global__ void selftest_ratio_kernel(uint64_t seed, int64_t n, int rcp, unsigned long long* acc) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const uint64_t h0 = mix64(seed ^ (uint64_t)i), h1 = mix64(h0), h2 = mix64(h1), h3 = mix64(h2);
     const uint64_t a = h1 >> (1 + h0 % 63), b = (h2 >> (1 + (h0 >> 8) % 63)) | 1u;
@@ -90,7 +91,8 @@ __global__ void selftest_ratio_kernel(uint64_t seed, int64_t n, unsigned long lo
     const bool f32 = (h3 >> 1) & 1;
     const int p = f32 ? FP32_P : BF16_P, qmin = f32 ? FP32_QMIN : BF16_QMIN;
     Rnd rf;
-    const int c = f64::ratio_f64(a, b, sh, neg, p, qmin, 127, rf);
+    const int c = rcp ? f64::ratio_f64_rcp(a, f64::recip_f64((int64_t)b), sh, neg, p, qmin, 127, rf)
+                      : f64::ratio_f64(a, b, sh, neg, p, qmin, 127, rf);
     bool bad = false;
     if (c >= 0) {
       const Rnd re = round_ratio64(a, b, sh, neg, p, qmin, 127);
@@ -104,7 +106,7 @@ __global__ void selftest_ratio_kernel(uint64_t seed, int64_t n, unsigned long lo
 }  // namespace ea
 
 extern "C" int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int64_t n, int64_t* out) {
-  if (!out || n < 0 || mode < 0 || mode > 2) return -1;
+  if (!out || n < 0 || mode < 0 || mode > 3) return -1;
   unsigned long long* d = nullptr;
   if (cudaMalloc(&d, 4 * sizeof(unsigned long long)) != cudaSuccess) return -4;
   cudaMemset(d, 0, 4 * sizeof(unsigned long long));
@@ -116,7 +118,7 @@ extern "C" int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int6
   else if (mode == 1)
     ea::selftest_logit_kernel<<<8 * sms, 256>>>(seed, n, d);
   else
-    ea::selftest_ratio_kernel<<<8 * sms, 256>>>(seed, n, d);
+    ea::selftest_ratio_kernel<<<8 * sms, 256>>>(seed, n, mode == 3, d);
   cudaError_t e = cudaGetLastError();
   unsigned long long h[4] = {0, 0, 0, 0};
   if (e == cudaSuccess) e = cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);

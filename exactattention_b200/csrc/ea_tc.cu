@@ -946,6 +946,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     const int prec = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
     uint32_t outw[16];  // bf16 results, two per word (fp32 results are recomputed when stored)
     bool ok = ok_wait && st == ST_OK;
+    // one pair of divisor reciprocals for the row's channels
+    const double rzl = f64::recip_f64(Z), rzh = f64::recip_f64(Z + (int64_t)Zerr);
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
       Rnd x = rnd_zero();
@@ -954,7 +956,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         // binary64 first; the integer division decides what it cannot certify
         const int64_t nl = N[c] - (int64_t)Nerr, nh = N[c] + (int64_t)Nerr;
         const int64_t nu = (int64_t)R + ve - FN, zu = (int64_t)R - FZ;
-        const int cf = f64::certify_ratio_f64(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, prec, qmin, 127, x);
+        const int cf = f64::certify_ratio_f64_rcp(nl, nh, nu, Z, Z + (int64_t)Zerr, rzl, rzh, zu, prec, qmin, 127, x);
         if (cf == 0) ok = false;
         else if (cf < 0) ok &= certify_ratio_lh(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, prec, qmin, 127, x);
       }
@@ -999,7 +1001,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             if (R != R_EMPTY && ve != INT32_MIN) {
               const int64_t nl = N[c] - (int64_t)Nerr, nh = N[c] + (int64_t)Nerr;
               const int64_t nu = (int64_t)R + ve - FN, zu = (int64_t)R - FZ;
-              if (f64::certify_ratio_f64(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, FP32_P, FP32_QMIN, 127, x) < 0)
+              if (f64::certify_ratio_f64_rcp(nl, nh, nu, Z, Z + (int64_t)Zerr, rzl, rzh, zu, FP32_P, FP32_QMIN, 127,
+                                             x) < 0)
                 certify_ratio_lh(nl, nh, nu, Z, Z + (int64_t)Zerr, zu, FP32_P, FP32_QMIN, 127, x);
             }
             f[u] = rnd_to_f32_bits(x);

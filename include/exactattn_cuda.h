@@ -230,7 +230,8 @@ int ea_kernel_timing(int mode, double* total_ms, int64_t* launches);
  * evaluations, on the current device (no reference counterpart: the reference has one exact
  * evaluation). mode 0: weights RN24(2^t) for n logits t, fp32 bit patterns from `seed` with step
  * `stride`, both signs, |t| < 2^22; mode 1: logits RN32(alpha s) for n splitmix64 cases from
- * `seed`; mode 2: output ratios RN(a / b 2^sh) to bf16 and fp32 for n splitmix64 cases.
+ * `seed`; mode 2: output ratios RN(a / b 2^sh) to bf16 and fp32 for n splitmix64 cases; mode 3:
+ * the same ratios through one reciprocal of b (the form the prefill kernel uses per row).
  * out[0..3] = cases, cases the fast path certified, mismatches (must be 0), the input of a
  * mismatch. Returns 0, or -1 / -4 for bad arguments / a CUDA error. */
 int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int64_t n, int64_t* out);

@@ -35,12 +35,13 @@ def test_logit_fast_path_matches_integer(seed):
     assert cert >= cases * 0.95
 
 
+@pytest.mark.parametrize("mode", [2, 3])  # 3: through one shared reciprocal of the divisor
 @pytest.mark.parametrize("seed", [4, 5])
-def test_ratio_fast_path_matches_integer(seed):
+def test_ratio_fast_path_matches_integer(seed, mode):
     from exactattention_b200 import cuda
 
     n = 1 << 24
-    cases, cert, bad, what = cuda.selftest_fast64(2, seed, n)
+    cases, cert, bad, what = cuda.selftest_fast64(mode, seed, n)
     assert cases == n
     assert bad == 0, what
     assert cert >= cases * 0.9  # the rest: results near the subnormal or overflow range, near midpoints
