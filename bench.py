@@ -131,7 +131,7 @@ class Clocks:
 
 
 def default_splits(name: str) -> int:
-    return {"c2": 1, "c3": 4, "c4": 1, "c5": 64}[name]
+    return {"c2": 1, "c3": 4, "c4": 1, "c5": 32}[name]
 
 
 def cpu_reference_step(name: str, budget_s: float = 12.0):
