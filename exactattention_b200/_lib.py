@@ -11,9 +11,11 @@ LIB_PATH = os.path.join(_HERE, "libexactattn_cuda.so")
 _lib = None
 
 EA_MASK_CSR, EA_MASK_RANGE, EA_MASK_PAGED, EA_MASK_HYBRID = 0, 1, 2, 3
-EA_STATS_LEN = 8
-STAT_NAMES = ("score_exact", "weight_wide", "tier3_rows", "domain_rows", "unresolved_rows", "pairs",
-              "host_fallbacks", "tc_pairs")
+EA_STATS_LEN = 12
+STAT_NAMES = ("score_exact", "weight_wide", "tier1_uncertified", "domain_rows", "unresolved_rows", "pairs",
+              "host_fallbacks", "tc_pairs", "waits_expired", "tier2_uncertified", "tier2_pairs", "forced_rows")
+# return codes (include/exactattn_cuda.h)
+RC_WAIT_EXPIRED = -5
 
 # Every symbol include/exactattn_cuda.h declares.
 EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda", "ea_launch_cuda",
@@ -21,7 +23,7 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
            "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda", "ea_selftest_fast64",
-           "ea_merge_partials_nccl")
+           "ea_merge_partials_nccl", "ea_set_test_hooks")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -55,6 +57,11 @@ class PartialsArgs(ctypes.Structure):
 class WidePartialsArgs(ctypes.Structure):
     """ea_wide_partials_t (include/exactattn_cuda.h)."""
     _fields_ = [("maxv", ctypes.c_void_p), ("sumv", ctypes.c_void_p)]
+
+
+class TestHooks(ctypes.Structure):
+    """ea_test_hooks_t (include/exactattn_cuda.h)."""
+    _fields_ = [("force_stride", ctypes.c_int), ("force_tier", ctypes.c_int), ("wait_debug", ctypes.c_int)]
 
 
 class KvAppendArgs(ctypes.Structure):
@@ -118,6 +125,8 @@ def load(path: str | None = None):
     lib.ea_selftest_fast64.restype = ctypes.c_int
     lib.ea_merge_partials_nccl.argtypes = [ctypes.POINTER(PartialsArgs), ctypes.c_int64, ctypes.c_int, P, P]
     lib.ea_merge_partials_nccl.restype = ctypes.c_int
+    lib.ea_set_test_hooks.argtypes = [ctypes.POINTER(TestHooks)]
+    lib.ea_set_test_hooks.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
     lib.ea_reserve_workspace.restype = ctypes.c_int
     lib.ea_cuda_release.argtypes = []
@@ -127,6 +136,11 @@ def load(path: str | None = None):
     if path is None:
         _lib = lib
     return lib
+
+
+class WaitExpiredWarning(RuntimeWarning):
+    """A bounded device wait gave up during a synchronous call (code -5): the GPU stalled. The
+    affected rows were recomputed by the later tiers, so the call's outputs are exact."""
 
 
 def check(rc: int, what: str) -> None:
@@ -140,6 +154,20 @@ def check(rc: int, what: str) -> None:
         raise ValueError(f"{what}: acc_bits must be 64 or 128 (code -2)")
     if rc == -3:
         raise ValueError(f"{what}: alpha is not finite (code -3)")
-    if rc == -5:
-        raise ValueError(f"{what}: unsupported layout (code -5)")
+    if rc == RC_WAIT_EXPIRED:
+        import warnings
+
+        warnings.warn(f"{what}: {msg} (code -5)", WaitExpiredWarning, stacklevel=3)
+        return
+    if rc == -9:
+        raise ValueError(f"{what}: unsupported layout (code -9)")
     raise RuntimeError(f"{what}: CUDA error (code {rc}): {msg}")
+
+
+def set_test_hooks(force_stride: int = 0, force_tier: int = 0, wait_debug: int = 0) -> None:
+    """ea_set_test_hooks (tests only): force rows out of tier 1 (and tier 2), or make the bounded
+    waits of the tensor-core kernels report expiry. All zero restores production behaviour."""
+    h = TestHooks(force_stride, force_tier, wait_debug)
+    rc = load().ea_set_test_hooks(ctypes.byref(h))
+    if rc:
+        raise ValueError("invalid test hooks")

@@ -24,14 +24,20 @@ cudaError_t launch_combine(const Prob& P, cudaStream_t st);
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
+cudaError_t launch_list_all_rows(const Prob& P, cudaStream_t st);
 void nccl_release_scratch();  // ea_nccl.cu
 }  // namespace ea
 
 using namespace ea;
 
+static_assert(EA_STATS_LEN == STAT_LEN, "the C ABI's stats length and the device counters agree");
+
 namespace {
 
 thread_local std::string g_err;
+
+// test hooks (ea_set_test_hooks), copied into every launch's problem description
+ea_test_hooks_t g_hooks = {0, 0, 0};
 
 int fail_cuda(cudaError_t e, const char* where) {
   g_err = std::string(where) + ": " + cudaGetErrorString(e);
@@ -197,14 +203,15 @@ struct TimedLaunch {
 };
 
 static int check_launch(const ea_launch_t* a) {
-  if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->splits <= 0 || a->rows < 0) return -1;
+  if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->splits <= 0 || a->splits > 65535 || a->rows < 0) return -1;
   uint32_t ab;
   memcpy(&ab, &a->alpha, 4);
   int32_t am, ae;
   if (!decode_fp32(ab, am, ae)) return -3;
+  if (a->mask_kind < EA_MASK_CSR || a->mask_kind > EA_MASK_HYBRID) return -9;
   if (a->mask_kind == EA_MASK_PAGED && (a->page_size <= 0 || a->q_heads <= 0 || a->kv_heads <= 0 ||
                                         a->q_heads % a->kv_heads != 0))
-    return -5;
+    return -9;
   return 0;
 }
 
@@ -247,6 +254,10 @@ static void build_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
   P.stats = a->stats ? (unsigned long long*)a->stats : w->stats;
   P.t3_count = w->t3_count;
   P.t3_list = w->t3_list;
+  P.tier = 1;
+  P.force_stride = g_hooks.force_stride;
+  P.force_tier = g_hooks.force_tier;
+  P.wait_debug = g_hooks.wait_debug;
   if (a->splits > 1) {
     int64_t n = a->rows * (int64_t)a->splits;
     char* p = (char*)w->part;
@@ -376,9 +387,27 @@ static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st
   return 0;
 }
 
+// More than 256 value channels (beyond what the tier-1 and tier-2 kernels keep per thread): every
+// row goes straight to the wide tier 3, which loops over channel blocks of any width.
+static int launch_wide_all(const ea_launch_t* a0, Workspace* w, cudaStream_t st) {
+  ea_launch_t a = *a0;
+  a.splits = 1;
+  int rc = reserve(w, a.rows, 1, a.dv);
+  if (rc) return rc;
+  Prob P;
+  build_prob(&a, w, P);
+  cudaError_t e = launch_list_all_rows(P, st);
+  if (e != cudaSuccess) return fail_cuda(e, "row list");
+  int blocks = (int)(a.rows < 2 * w->sms ? a.rows : 2 * w->sms);
+  e = launch_tier3(P, blocks, st);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  return 0;
+}
+
 // the launch sequence of one problem on workspace w (g_mu held)
 static int launch_on(const ea_launch_t* a, Workspace* w, cudaStream_t st) {
   int rc;
+  if (a->dv > 256) return launch_wide_all(a, w, st);
   if (hybrid_tc_applicable(a)) return launch_hybrid_tc(a, w, st);
   if (decode_applicable(a)) return launch_decode_tc(a, w, st);
   rc = reserve(w, a->rows, a->splits, a->dv);
@@ -458,7 +487,7 @@ static void set_export(Prob& P, const ea_partials_t* x) {
 int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream) {
   int rc = check_launch(a);
   if (rc) return rc;
-  if (!x) return -1;
+  if (!x || a->dv > 256) return -1;
   if (a->rows == 0) return 0;
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace* w = workspace();
@@ -560,6 +589,16 @@ static void order_by_len_desc(const int64_t* kv_len, int32_t* r0, int32_t* r1) {
     return;
   }
   std::stable_sort(r0, r1, [&](int32_t x, int32_t y) { return kv_len[x] > kv_len[y]; });
+}
+
+// -5 when a bounded wait of a tensor-core kernel gave up during the call (a stalled GPU): the
+// affected rows were recomputed by the later tiers, so out and flags are complete and exact.
+static int wait_status(const int64_t* hs) {
+  if (hs[STAT_WAIT_EXPIRED] == 0) return 0;
+  g_err = std::to_string(hs[STAT_WAIT_EXPIRED]) +
+          " CTA(s) of a tensor-core kernel gave up a bounded wait; their rows were recomputed by the "
+          "wide tier and the outputs are exact";
+  return -5;
 }
 
 // Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back.
@@ -714,9 +753,9 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   if (stats) {
     stats[0] += hs[STAT_SCORE_EXACT];
     stats[1] += hs[STAT_WEIGHT_WIDE];
-    stats[2] += hs[STAT_TIER3_ROWS];
+    stats[2] += hs[STAT_TIER1_UNCERT];
   }
-  return 0;
+  return wait_status(hs);
 }
 
 int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
@@ -725,7 +764,7 @@ int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k,
                       void* out, uint8_t* flags, int64_t* stats) {
   (void)order_seed;
   (void)nthreads;
-  if (d <= 0 || d > 1024 || dv <= 0 || tile <= 0 || splits <= 0) return -1;
+  if (d <= 0 || d > 1024 || dv <= 0 || tile <= 0 || splits <= 0 || splits > 65535) return -1;
   if (acc_bits != 64 && acc_bits != 128) return -2;
   uint32_t ab;
   memcpy(&ab, &alpha, 4);
@@ -749,7 +788,7 @@ int ea_attention_cuda_ranges(const uint16_t* q, int64_t rows, int d, const uint1
                              int64_t nkeys, int dv, float alpha, const int64_t* kv_base, const int64_t* kv_len,
                              int64_t max_row_keys, int fp32_out, int splits, void* out, uint8_t* flags,
                              int64_t* stats) {
-  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || !kv_base || !kv_len) return -1;
+  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || splits > 65535 || !kv_base || !kv_len) return -1;
   uint32_t ab;
   memcpy(&ab, &alpha, 4);
   int32_t am, ae;
@@ -856,6 +895,17 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* x, const int64_t* m
 
 }  // extern "C"
 
+extern "C" int ea_set_test_hooks(const ea_test_hooks_t* h) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!h) {
+    g_hooks = {0, 0, 0};
+    return 0;
+  }
+  if (h->force_stride < 0 || h->force_tier < 0 || h->force_tier > 2) return -1;
+  g_hooks = *h;
+  return 0;
+}
+
 // Diagnostic: device time of the tier-1 kernel of each ea_launch_cuda call (the hot kernel:
 // tensor-core prefill / decode, or the CUDA-core split kernel with its combine).
 extern "C" int ea_kernel_timing(int mode, double* total_ms, int64_t* launches) {
@@ -896,8 +946,9 @@ extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_h
                                        const uint16_t* v_cache, int64_t num_pages, int kv_heads, int page_size, int dv,
                                        float alpha, const int32_t* page_table, int max_pages, const int32_t* seq_lens,
                                        int fp32_out, int splits, void* out, uint8_t* flags, int64_t* stats) {
-  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || batch < 0 || num_pages < 0 || max_pages <= 0) return -1;
-  if (q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || page_size <= 0) return -5;
+  if (d <= 0 || d > 1024 || dv <= 0 || splits <= 0 || splits > 65535 || batch < 0 || num_pages < 0 || max_pages <= 0)
+    return -1;
+  if (q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || page_size <= 0) return -9;
   uint32_t ab;
   memcpy(&ab, &alpha, 4);
   int32_t am, ae;
@@ -978,7 +1029,7 @@ extern "C" int ea_attention_cuda_paged(const uint16_t* q, int64_t batch, int q_h
   if (stats) {
     stats[0] += hs[STAT_SCORE_EXACT];
     stats[1] += hs[STAT_WEIGHT_WIDE];
-    stats[2] += hs[STAT_TIER3_ROWS];
+    stats[2] += hs[STAT_TIER1_UNCERT];
   }
-  return 0;
+  return wait_status(hs);
 }

@@ -417,8 +417,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int64_t pref = pwarp >= NWARPS / 2 - 2 ? page_ahead(P, row0, j0 + BK, kend) : -1;
       // ---- K(i): needs its raw rows, and pass 1 of tile i - 1 done with the digits, the lossy
       //      masks and the score accumulators ----
-      bool okw = tc::mbar_wait(&S.bar_rk, ph);
-      if (i > 0) okw &= tc::mbar_wait(&S.bar_p1, php);
+      bool okw = tc::mbar_wait(&S.bar_rk, ph, P.wait_debug);
+      if (i > 0) okw &= tc::mbar_wait(&S.bar_p1, php, P.wait_debug);
       if (!group_sync_and(2, okw)) {
         ok_wait = false;
         break;
@@ -531,8 +531,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       // ---- V(i): needs its raw rows, and the P.V MMAs of tile i - 1 done with the value digits. The
       //      channel data of tile i - 1 stay in the other parity buffer until the consumers' merge;
       //      the P.V MMAs of tile i + 1 (after that merge) gate the next rewrite of this one ----
-      okw = tc::mbar_wait(&S.bar_rv, ph);
-      if (i > 0) okw &= tc::mbar_wait(&S.bar_pv, php);
+      okw = tc::mbar_wait(&S.bar_rv, ph, P.wait_debug);
+      if (i > 0) okw &= tc::mbar_wait(&S.bar_pv, php, P.wait_debug);
       if (!group_sync_and(2, okw)) {
         ok_wait = false;
         break;
@@ -690,8 +690,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     if (!ok_wait) S.abort = 1;
     // a wait that gave up: the copies still in flight get another bounded wait before the shared
     // memory is released
-    if (rk_pending) tc::mbar_wait(&S.bar_rk, rk_ph);
-    if (rv_pending) tc::mbar_wait(&S.bar_rv, rv_ph);
+    if (rk_pending) tc::mbar_wait(&S.bar_rk, rk_ph, P.wait_debug);
+    if (rv_pending) tc::mbar_wait(&S.bar_rv, rv_ph, P.wait_debug);
   } else {
     // ======================= consumer warpgroups: logits, weights, P.V, merges =======================
     const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
@@ -704,7 +704,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int nvalid = (int)min((int64_t)BK, kend - j0);
       const uint32_t ph = (uint32_t)i & 1u;
       {
-        const bool okw = tc::mbar_wait(&S.bar_smma, ph);  // the score MMAs of tile i
+        const bool okw = tc::mbar_wait(&S.bar_smma, ph, P.wait_debug);  // the score MMAs of tile i
         if (!group_sync_and(1, okw && !*(volatile int*)&S.abort)) {
           ok_wait = false;
           break;
@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         }
       }
       tc::fence_async_smem();
-      bool okw = tc::mbar_wait(&S.bar_vready, ph);  // the producers' value digits of tile i
+      bool okw = tc::mbar_wait(&S.bar_vready, ph, P.wait_debug);  // the producers' value digits of tile i
       if (!group_sync_and(1, okw)) {
         ok_wait = false;
         break;
@@ -1003,7 +1003,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       EA_PT(4)
       // each thread waits; after a wait that gave up the drain reads stale TMEM and the vote at
       // the end of the tile drops it
-      const bool ok_pv = tc::mbar_wait(&S.bar_pv, ph);
+      const bool ok_pv = tc::mbar_wait(&S.bar_pv, ph, P.wait_debug);
       tc::fence_after_sync();
       EA_PT(5)
       // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
@@ -1045,7 +1045,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     EA_PT_FLUSH
     if (!ok_wait) S.abort = 1;
-    if (pv_pending) tc::mbar_wait(&S.bar_pv, pv_ph);
+    if (pv_pending) tc::mbar_wait(&S.bar_pv, pv_ph, P.wait_debug);
     n_exact = __reduce_add_sync(0xffffffffu, n_exact);
     n_wide = __reduce_add_sync(0xffffffffu, n_wide);
     if (lane == 0) {
@@ -1103,7 +1103,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
     stat_add(P, STAT_PAIRS, pairs);
     stat_add(P, STAT_TC_PAIRS, pairs);
-    if (S.abort) stat_add(P, STAT_UNRESOLVED, 1000000);  // a bounded wait gave up: loud
+    if (S.abort) stat_add(P, STAT_WAIT_EXPIRED, 1);  // a bounded wait gave up
   }
   if (warp == 0) tc::tmem_free(tmem, TMEM_COLS);
 }

@@ -1,16 +1,16 @@
 // ea_attention_cuda_noalloc: the device-pointer entry point without any device allocation.
 //
-// Some callers cannot allocate device memory at the moment they need attention: code running
-// while a stream is being captured into a CUDA graph (a cudaMalloc there is not part of the
-// graph and may be refused), serving processes whose allocator owns the whole device and
-// forbids allocations behind its back, or latency-bound decode loops that cannot afford the
-// stall of a first-call allocation. This entry point serves them: the split partials, the
-// tier-3 work list and the counters live in one file-scope __device__ array of fixed size,
-// reserved when the library is loaded (every GPU that loads the library keeps it until exit).
+// Some callers cannot allocate device memory at the moment they need attention: serving
+// processes whose memory pool owns the whole device and forbids allocations behind its back,
+// and latency-bound decode loops that cannot afford the stall (and the implicit device
+// synchronisation) of a first-call cudaMalloc. This entry point serves them: the split
+// partials, the tier-3 work list and the counters live in one file-scope __device__ array of
+// fixed size, reserved when the library is loaded (every GPU that loads the library keeps it
+// until exit).
 //
 // Limits and rules:
-//   * the scratch holds EA_NOALLOC_SCRATCH_BYTES; a call that needs more (rows x splits x
-//     (20 dv + 32) bytes of partials plus 4 bytes per row) is rejected with -6 and an error
+//   * the scratch holds EA_NOALLOC_SCRATCH_BYTES; a call that needs more (the exact formula is in
+//     scratch_bytes below and in include/exactattn_cuda.h) is rejected with -6 and an error
 //     string, before anything is launched;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
 //     with that device current; make that first call before any stream capture;
@@ -52,7 +52,8 @@ thread_local std::string g_err;
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// bytes of scratch one call needs (same layout as the carve-up below)
+// bytes of scratch one call needs (same layout as the carve-up below); callers have checked
+// rows <= SCRATCH / 4 and rows x splits <= SCRATCH / 4, so no product here overflows
 size_t scratch_bytes(int64_t rows, int splits, int dv) {
   size_t b = align256(EA_STATS_LEN * 8) + align256(sizeof(int)) + align256((size_t)rows * 4);
   if (splits > 1) {
@@ -73,32 +74,39 @@ int ceil_log2(int64_t n) {
 extern "C" const char* ea_noalloc_last_error(void) { return g_err.c_str(); }
 
 extern "C" int ea_attention_cuda_noalloc(const ea_launch_t* a, void* stream) {
-  if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->dv > 256 || a->splits <= 0 || a->rows < 0) {
-    g_err = "invalid dimensions";
+  if (!a || a->d <= 0 || a->d > 1024 || a->dv <= 0 || a->dv > 256 || a->splits <= 0 || a->splits > 65535 ||
+      a->rows < 0) {
+    g_err = "ea_attention_cuda_noalloc: invalid dimensions (d <= 1024, dv <= 256, 1 <= splits <= 65535)";
     return -1;
   }
   uint32_t ab;
   memcpy(&ab, &a->alpha, 4);
   int32_t am, ae;
   if (!decode_fp32(ab, am, ae)) {
-    g_err = "alpha is not finite";
+    g_err = "ea_attention_cuda_noalloc: alpha is not finite";
     return -3;
   }
-  if (a->mask_kind == EA_MASK_PAGED && (a->page_size <= 0 || a->q_heads <= 0 || a->kv_heads <= 0 ||
-                                        a->q_heads % a->kv_heads != 0)) {
-    g_err = "unsupported paged layout";
-    return -5;
+  if (a->mask_kind < EA_MASK_CSR || a->mask_kind > EA_MASK_HYBRID ||
+      (a->mask_kind == EA_MASK_PAGED && (a->page_size <= 0 || a->q_heads <= 0 || a->kv_heads <= 0 ||
+                                         a->q_heads % a->kv_heads != 0))) {
+    g_err = "ea_attention_cuda_noalloc: unsupported layout";
+    return -9;
   }
   if (a->rows == 0) return 0;
-  const size_t need = scratch_bytes(a->rows, a->splits, a->dv);
-  if (need > (size_t)EA_NOALLOC_SCRATCH_BYTES) {
-    g_err = "ea_attention_cuda_noalloc: needs " + std::to_string(need) + " bytes of scratch, the maximum is " +
-            std::to_string((size_t)EA_NOALLOC_SCRATCH_BYTES) + " (use fewer rows or splits per call)";
+  // every row takes 4 bytes of the work list and every (row, split) at least 4 bytes of
+  // partials: bounding both first keeps the size arithmetic below free of overflow
+  constexpr int64_t cap4 = (int64_t)EA_NOALLOC_SCRATCH_BYTES / 4;
+  const bool too_many = a->rows > cap4 || (a->splits > 1 && a->rows > cap4 / a->splits);
+  const size_t need = too_many ? 0 : scratch_bytes(a->rows, a->splits, a->dv);
+  if (too_many || need > (size_t)EA_NOALLOC_SCRATCH_BYTES) {
+    g_err = "ea_attention_cuda_noalloc: needs " + (too_many ? std::string("more") : std::to_string(need)) +
+            " bytes of scratch, the maximum is " + std::to_string((size_t)EA_NOALLOC_SCRATCH_BYTES) +
+            " (use fewer rows or splits per call)";
     return -6;
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
-    g_err = "no current CUDA device";
+    g_err = "ea_attention_cuda_noalloc: no current CUDA device";
     return -4;
   }
   unsigned char* base;
@@ -110,7 +118,7 @@ extern "C" int ea_attention_cuda_noalloc(const ea_launch_t* a, void* stream) {
       void* p = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
       if (e != cudaSuccess || !p) {
-        g_err = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e);
+        g_err = std::string("ea_attention_cuda_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e);
         return -4;
       }
       int n = 148;

@@ -116,11 +116,9 @@ __device__ void finalize_row(const Prob& P, int64_t r, int status, int32_t R, in
     }
   }
   ok = __all_sync(0xffffffffu, ok);
-  if (!ok) {
-    if (lane == 0) {
-      push_tier3(P, r);
-      stat_add(P, STAT_TIER3_ROWS, 1);
-    }
+  const bool forced = ok && forced_uncertified(P, r);
+  if (!ok || forced) {
+    if (lane == 0) leave_tier(P, r, forced);
     return;
   }
 #pragma unroll
@@ -152,22 +150,36 @@ __device__ void export_row(const Prob& P, int64_t r, int status, int32_t R, int6
 }
 
 // ---------------------------------------------------------------------------
-// tier 1
+// tier 1 (and tier 2): one warp over a key range of one row
 // ---------------------------------------------------------------------------
+// The int64 partial of a key range: lane holds channels lane + 32 i.
 template <int CPL>
-__global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  uint64_t* sTA = (uint64_t*)smem;
-  uint64_t* sTB = sTA + 256;
+struct SimtPart {
+  int status;
+  int32_t R, Rlo;  // running reference exponent; lowest E + 24 seen (the logit spread check)
+  int64_t Z;
+  uint64_t Ze;
+  int32_t NR[CPL];
+  int64_t N[CPL];
+  uint64_t Ne[CPL];
+};
+
+// the exp2 tables of the 64-bit weight path into shared memory (4 KB at the start of smem)
+__device__ __forceinline__ void load_exp2_tables(uint64_t* sTA, uint64_t* sTB) {
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
     sTA[i] = g_ta64[i];
     sTB[i] = g_tb64[i];
   }
-  __syncthreads();
+}
 
+// Row r's keys [j0, j1) by one warp on the CUDA cores; ws is the warp's shared workspace
+// (simt_warp_bytes). Counts exact scores and wide weights into n_exact / n_wide (this lane).
+template <int CPL>
+__device__ __forceinline__ void simt_range(const Prob& P, int64_t r, int64_t j0, int64_t j1, const uint64_t* sTA,
+                                           const uint64_t* sTB, unsigned char* ws, SimtPart<CPL>& out,
+                                           unsigned long long& n_exact, unsigned long long& n_wide) {
+  const int lane = threadIdx.x & 31;
   const int d = P.d, dv = P.dv, nw = simt_words(d);
-  unsigned char* ws = smem + 4096 + (size_t)warp * simt_warp_bytes(d, dv);
   uint16_t* qbits = (uint16_t*)ws;
   int32_t* qfix = (int32_t*)(ws + align16((size_t)d * 2));
   uint8_t* qlost = (uint8_t*)((unsigned char*)qfix + align16((size_t)d * 4));
@@ -177,12 +189,6 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
   uint16_t* vtile = (uint16_t*)tile;
   uint32_t* sM = (uint32_t*)(tile + align16(kt > vt ? kt : vt));
   int32_t* sE = (int32_t*)(sM + 32);
-
-  const int64_t r = (int64_t)blockIdx.x * nwarps + warp;
-  if (r >= P.rows) return;
-  const int S = P.splits, s = blockIdx.y;
-  const int64_t L = row_len(P, r);
-  const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
 
   // ---- q row: decode, leading exponent, block fixed point ----
   int status = ST_OK;
@@ -220,7 +226,6 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
     Ne[i] = 0;
   }
   const int FZ = P.FZ;
-  unsigned long long n_exact = 0, n_wide = 0;
 
   for (int64_t t0 = j0; t0 < j1 && status == ST_OK; t0 += 32) {
     const int nt = (int)min((int64_t)32, j1 - t0);
@@ -358,15 +363,80 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
     __syncwarp();
   }
   status = warp_max32(status);
+  if (status == ST_OK && R != R_EMPTY && Rlo != INT32_MAX && (int64_t)R - Rlo > SPREAD_CHECK) status = ST_TIER3;
+  out.status = status;
+  out.R = R;
+  out.Rlo = Rlo;
+  out.Z = Z;
+  out.Ze = Ze;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    out.NR[i] = NR[i];
+    out.N[i] = N[i];
+    out.Ne[i] = Ne[i];
+  }
+}
+
+// the counters of one warp's range (lane 0 adds the warp's sums)
+__device__ __forceinline__ void simt_stats(const Prob& P, unsigned long long n_exact, unsigned long long n_wide,
+                                           unsigned long long pairs, int pairs_slot) {
   n_exact = (unsigned long long)warp_sum64((int64_t)n_exact);
   n_wide = (unsigned long long)warp_sum64((int64_t)n_wide);
-  if (lane == 0) {
+  if ((threadIdx.x & 31) == 0) {
     stat_add(P, STAT_SCORE_EXACT, n_exact);
     stat_add(P, STAT_WEIGHT_WIDE, n_wide);
-    stat_add(P, STAT_PAIRS, (unsigned long long)(j1 - j0));
+    stat_add(P, pairs_slot, pairs);
   }
+}
 
-  if (status == ST_OK && R != R_EMPTY && Rlo != INT32_MAX && (int64_t)R - Rlo > SPREAD_CHECK) status = ST_TIER3;
+// one partial into slot pi of the split (or unit) buffers P.p*
+template <int CPL>
+__device__ __forceinline__ void write_split_partial(const Prob& P, int64_t pi, const SimtPart<CPL>& o) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) {
+    P.pR[pi] = o.R;
+    P.pZ[pi] = o.Z;
+    P.pZe[pi] = o.Ze;
+    P.pSt[pi] = o.status;
+  }
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= P.dv) continue;
+    P.pNR[pi * P.dv + c] = o.NR[i];
+    P.pN[pi * P.dv + c] = o.N[i];
+    P.pNe[pi * P.dv + c] = o.Ne[i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// tier 1: one warp per (row, KV split)
+// ---------------------------------------------------------------------------
+template <int CPL>
+__global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  uint64_t* sTA = (uint64_t*)smem;
+  uint64_t* sTB = sTA + 256;
+  load_exp2_tables(sTA, sTB);
+  __syncthreads();
+  unsigned char* ws = smem + 4096 + (size_t)warp * simt_warp_bytes(P.d, P.dv);
+  const int64_t r = (int64_t)blockIdx.x * nwarps + warp;
+  if (r >= P.rows) return;
+  const int S = P.splits, s = blockIdx.y;
+  const int64_t L = row_len(P, r);
+  const int64_t j0 = L * s / S, j1 = L * (s + 1) / S;
+  SimtPart<CPL> o;
+  unsigned long long n_exact = 0, n_wide = 0;
+  simt_range<CPL>(P, r, j0, j1, sTA, sTB, ws, o, n_exact, n_wide);
+  simt_stats(P, n_exact, n_wide, (unsigned long long)(j1 - j0), STAT_PAIRS);
+  const int status = o.status;
+  const int32_t R = o.R;
+  const int64_t Z = o.Z;
+  const uint64_t Ze = o.Ze;
+  const int32_t* NR = o.NR;
+  const int64_t* N = o.N;
+  const uint64_t* Ne = o.Ne;
   if (S == 1) {
     if (P.export_partials)
       export_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
@@ -374,36 +444,23 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
       finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
     return;
   }
-  const int64_t pi = (int64_t)s * P.rows + r;
-  if (lane == 0) {
-    P.pR[pi] = R;
-    P.pZ[pi] = Z;
-    P.pZe[pi] = Ze;
-    P.pSt[pi] = status;
-  }
-#pragma unroll
-  for (int i = 0; i < CPL; ++i) {
-    int c = lane + 32 * i;
-    if (c >= dv) continue;
-    P.pNR[pi * dv + c] = NR[i];
-    P.pN[pi * dv + c] = N[i];
-    P.pNe[pi * dv + c] = Ne[i];
-  }
+  write_split_partial<CPL>(P, (int64_t)s * P.rows + r, o);
+  (void)lane;
 }
 
 // ---------------------------------------------------------------------------
 // split combine: max reference exponent, rescale, integer sum (order-independent)
 // ---------------------------------------------------------------------------
+// Merge of the partials in slots first + s * stride (s < S), one warp: the largest reference
+// exponents, every partial re-expressed at them, integer sums (order-free), the spread check.
 template <int CPL>
-__global__ void __launch_bounds__(128) combine_kernel(Prob P) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
-  if (r >= P.rows) return;
-  const int S = P.splits, dv = P.dv;
+__device__ __forceinline__ void merge_slots(const Prob& P, int64_t first, int64_t stride, int S, SimtPart<CPL>& o) {
+  const int lane = threadIdx.x & 31;
+  const int dv = P.dv;
   int status = ST_OK;
   int32_t R = R_EMPTY, Rmin = INT32_MAX;
   for (int s = 0; s < S; ++s) {
-    int64_t pi = (int64_t)s * P.rows + r;
+    int64_t pi = first + (int64_t)s * stride;
     status = max(status, P.pSt[pi]);
     if (P.pR[pi] != R_EMPTY) {
       R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
@@ -418,7 +475,7 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
   bool ok = true;
   if (status == ST_OK && R != R_EMPTY) {
     for (int s = 0; s < S; ++s) {
-      int64_t pi = (int64_t)s * P.rows + r;
+      int64_t pi = first + (int64_t)s * stride;
       if (P.pR[pi] == R_EMPTY) continue;
       int64_t z = P.pZ[pi];
       uint64_t ze = P.pZe[pi];
@@ -439,12 +496,12 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
     int c = lane + 32 * i;
     if (c >= dv || status != ST_OK) continue;
     for (int s = 0; s < S; ++s) {
-      int32_t x = P.pNR[((int64_t)s * P.rows + r) * dv + c];
+      int32_t x = P.pNR[(first + (int64_t)s * stride) * dv + c];
       if (x != R_EMPTY) NR[i] = NR[i] == R_EMPTY ? x : max(NR[i], x);
     }
     if (NR[i] == R_EMPTY) continue;
     for (int s = 0; s < S; ++s) {
-      int64_t pc = ((int64_t)s * P.rows + r) * dv + c;
+      int64_t pc = (first + (int64_t)s * stride) * dv + c;
       int32_t x = P.pNR[pc];
       if (x == R_EMPTY) continue;
       int64_t n = P.pN[pc];
@@ -456,10 +513,30 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
     ok &= fits63(N[i], Ne[i]);
   }
   if (!__all_sync(0xffffffffu, ok) && status == ST_OK) status = ST_TIER3;
+  o.status = status;
+  o.R = R;
+  o.Rlo = Rmin;
+  o.Z = Z;
+  o.Ze = Ze;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    o.NR[i] = NR[i];
+    o.N[i] = N[i];
+    o.Ne[i] = Ne[i];
+  }
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(128) combine_kernel(Prob P) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= P.rows) return;
+  SimtPart<CPL> o;
+  merge_slots<CPL>(P, r, P.rows, P.splits, o);
   if (P.export_partials)
-    export_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+    export_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
   else
-    finalize_row<CPL>(P, r, status, R, Z, Ze, NR, N, Ne, lane);
+    finalize_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -973,6 +1050,30 @@ cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaS
 
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st) {
   wide_finalize_kernel<<<n, T3_THREADS, 0, st>>>(P, n, gmax);
+  return cudaGetLastError();
+}
+
+// Every row on the tier-3 list (value rows wider than the tier-1 kernels take), with the pair count.
+__global__ void list_all_rows_kernel(Prob P) {
+  __shared__ unsigned long long pairs;
+  if (threadIdx.x == 0) pairs = 0;
+  __syncthreads();
+  unsigned long long mine = 0;
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < P.rows; r += (int64_t)gridDim.x * blockDim.x) {
+    P.t3_list[r] = (int)r;
+    mine += (unsigned long long)row_len(P, r);
+  }
+  atomicAdd(&pairs, mine);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    stat_add(P, STAT_PAIRS, pairs);
+    if (blockIdx.x == 0) *P.t3_count = (int)P.rows;
+  }
+}
+
+cudaError_t launch_list_all_rows(const Prob& P, cudaStream_t st) {
+  const int64_t b = (P.rows + 255) / 256;
+  list_all_rows_kernel<<<(unsigned)(b < 1024 ? b : 1024), 256, 0, st>>>(P);
   return cudaGetLastError();
 }
 

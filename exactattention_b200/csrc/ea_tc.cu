@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
                      ((S.klossy[tid][0] | S.klossy[tid][1] | S.klossy[tid][2] | S.klossy[tid][3]) ? 1u << 16 : 0u) |
                      (S.kbad[tid] ? 1u << 17 : 0u);
     {
-      const bool okw = tc::mbar_wait(&S.bar, phase);
+      const bool okw = tc::mbar_wait(&S.bar, phase, P.wait_debug);
       phase ^= 1;
       // block-wide vote: a wait that gave up ends the tile loop for every thread together
       if (!__syncthreads_and(okw)) {
@@ -864,7 +864,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
 #pragma unroll 1
     for (int rd = 0; rd < 4; ++rd) {
       {
-        const bool okw = tc::mbar_wait(&S.bar_pv[rd & 1], (pv_phase >> (rd & 1)) & 1u);
+        const bool okw = tc::mbar_wait(&S.bar_pv[rd & 1], (pv_phase >> (rd & 1)) & 1u, P.wait_debug);
         pv_phase ^= 1u << (rd & 1);
         pv_pending &= ~(1u << (rd & 1));
         if (!__syncthreads_and(okw)) {
@@ -904,9 +904,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   }
   if (!ok_wait) {
     // a wait that gave up: the MMAs still in flight get a bounded wait before TMEM is released
-    tc::mbar_wait(&S.bar, phase ^ 1u);
+    tc::mbar_wait(&S.bar, phase ^ 1u, P.wait_debug);
     for (int b = 0; b < 2; ++b)
-      if ((pv_pending >> b) & 1u) tc::mbar_wait(&S.bar_pv[b], (pv_phase >> b) & 1u);
+      if ((pv_pending >> b) & 1u) tc::mbar_wait(&S.bar_pv[b], (pv_phase >> b) & 1u, P.wait_debug);
   }
 
   EA_PT(9)
@@ -982,11 +982,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           P.flags[myrow] = 2;
           stat_add(P, STAT_DOMAIN_ROWS, 1);
         }
-      } else if (!rowok) {
-        if (u4 == 0) {
-          push_tier3(P, myrow);
-          stat_add(P, STAT_TIER3_ROWS, 1);
-        }
+      } else if (!rowok || forced_uncertified(P, myrow)) {
+        if (u4 == 0) leave_tier(P, myrow, rowok);
       } else if (P.fp32) {
         // every channel certified: round again, now keeping the fp32 results (4 per store)
         uint32_t* o = (uint32_t*)P.out + (int64_t)myrow * DV + 32 * u4;
@@ -1029,7 +1026,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
     for (int i = 0; i < BM; ++i) pairs += (unsigned long long)S.len[i];
     stat_add(P, STAT_PAIRS, pairs);
     stat_add(P, STAT_TC_PAIRS, pairs);
-    if (!ok_wait) stat_add(P, STAT_UNRESOLVED, 1000000);  // a bounded wait gave up: loud
+    if (!ok_wait) stat_add(P, STAT_WAIT_EXPIRED, 1);  // a bounded wait gave up
   }
   EA_PT(10)
   EA_PT_FLUSH

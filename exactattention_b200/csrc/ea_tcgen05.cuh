@@ -132,10 +132,14 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // Waits for the phase with the given parity to complete. Returns false after 2 s (or 2^26
-// polls) without completion; callers then record an error and skip the dependent work.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// polls) without completion; callers then record an error, skip the dependent work and drain
+// what they still have in flight before the CTA exits.
+// debug != 0 (a test hook): the wait still waits for the phase (20 ms at most) but then reports
+// expiry, so that the callers' abort and drain path runs with nothing left in flight.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int debug = 0) {
   const uint32_t a = smem_u32(bar);
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = debug ? 20000000ull : 2000000000ull;
   for (uint32_t i = 0; i < (1u << 26); ++i) {
     uint32_t done;
     asm volatile(
@@ -145,8 +149,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "=r"(done)
         : "r"(a), "r"(parity), "r"(10000u)  // suspend up to 10 us per try (woken by the phase)
         : "memory");
-    if (done) return true;
-    if ((i & 255u) == 255u && globaltimer() - t0 > 2000000000ull) return false;
+    if (done) return debug == 0;
+    if ((i & 255u) == 255u && globaltimer() - t0 > limit) return false;
   }
   return false;
 }

@@ -27,7 +27,7 @@ class CudaStats:
     """Per-call counters (the reference's CpuStats, cpu.py:54-59, plus the device tiers)."""
     score_fallbacks: int = 0      # scores the window could not certify, recomputed exactly
     weight_fallbacks: int = 0     # weights recomputed by the 128-bit exp2
-    final_fallbacks: int = 0      # rows sent to the wide-integer tier
+    final_fallbacks: int = 0      # rows the fast tier left uncertified (rerun by tiers 2 and 3)
     rows: int = 0
     flagged_rows: int = 0         # rows with flag != 0 (domain errors)
     host_fallbacks: int = 0       # always 0
@@ -81,6 +81,13 @@ def attention_cuda(q, k, v, alpha, row_ptr=None, key_idx=None, out="bf16", acc_b
     return res, flags
 
 
+def new_stats(device="cuda"):
+    """A zeroed device counter array of EA_STATS_LEN int64 (the `stats` argument of launch)."""
+    import torch
+
+    return torch.zeros(_lib.EA_STATS_LEN, dtype=torch.int64, device=device)
+
+
 def round_ratio(a: int, b: int, E: int, neg: bool, fp32: bool) -> tuple[float, bool]:
     """The reference's `cpu.round_ratio` (cpu.py:112-117), evaluated by the device helper."""
     lib = _lib.load()
@@ -114,7 +121,7 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     with d = dv = 128 through the tensor-core decode kernel (keys on the MMA's M side); PAGED masks
     with d = dv = 128 and at most 8 q heads per kv head take it without a table.
     `no_alloc` calls ea_attention_cuda_noalloc instead: the library allocates no device memory for
-    the call (its scratch is a fixed static array; see include/exactattn_cuda.h for the limits).
+    the call (its scratch is a fixed static array of EA_NOALLOC_SCRATCH_BYTES; larger calls raise).
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
     import torch
 
@@ -138,9 +145,9 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     with torch.cuda.device(dev):
         if no_alloc:
             rc = lib.ea_attention_cuda_noalloc(ctypes.byref(a), ctypes.c_void_p(s))
-            if rc == -6:
-                raise ValueError(lib.ea_noalloc_last_error().decode())
-            _lib.check(rc, "ea_attention_cuda_noalloc")
+            if rc != 0:
+                msg = lib.ea_noalloc_last_error().decode(errors="replace")
+                raise (RuntimeError if rc == -4 else ValueError)(f"{msg} (code {rc})")
         else:
             _lib.check(lib.ea_launch_cuda(ctypes.byref(a), ctypes.c_void_p(s)), "ea_launch_cuda")
     return out_tensor, flags

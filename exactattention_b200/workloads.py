@@ -92,10 +92,46 @@ def draw_scales(rng: np.random.Generator, heads: int, d: int = D) -> Scale:
     return Scale.from_f32(s.astype(np.float32))
 
 
+_host_gen = None
+
+
+def _host_generator():
+    """The C form of this generator (csrc/ea_synth_host.c, all host threads), or None when it is
+    not built; both give the same bits."""
+    global _host_gen
+    if _host_gen is None:
+        import ctypes
+        import os
+
+        p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libea_synth_host.so")
+        if not os.path.exists(p):
+            return None
+        lib = ctypes.CDLL(p)
+        P, I64 = ctypes.c_void_p, ctypes.c_int64
+        lib.ea_synth_rows_host.argtypes = [P, ctypes.c_uint64, ctypes.c_uint64, I64, I64, I64, I64, I64, I64, I64,
+                                           P, P, ctypes.c_int]
+        lib.ea_synth_rows_host.restype = ctypes.c_int
+        _host_gen = lib
+    return _host_gen
+
+
 def synth_rows(seed: int, tensor_id: int, shape, g: int, h: int, t0: int, t1: int, scale: Scale | None = None,
-               heavy_permille: int = 0, chunk: int = 1 << 22) -> np.ndarray:
+               heavy_permille: int = 0, chunk: int = 1 << 22, use_host_lib: bool = True) -> np.ndarray:
     """Rows [g, h, t0:t1, :] of the logical (G, H, T, D) tensor, as uint16 bf16 bits."""
     G, H, T, Dd = shape
+    lib = _host_generator() if use_host_lib else None
+    if lib is not None:
+        out = np.empty((t1 - t0, Dd), np.uint16)
+        sm = se = None
+        if scale is not None:
+            sm = np.ascontiguousarray(scale.m, np.int32)
+            se = np.ascontiguousarray(scale.e, np.int32)
+        rc = lib.ea_synth_rows_host(out.ctypes.data, seed, tensor_id, H, T, Dd, g, h, t0, t1,
+                                    sm.ctypes.data if sm is not None else None,
+                                    se.ctypes.data if se is not None else None, heavy_permille)
+        if rc != 0:
+            raise RuntimeError("ea_synth_rows_host failed")
+        return out
     base = _sm_scalar((seed << 20) ^ tensor_id)
     hbase = _sm_scalar(base ^ 0x5555555555555555)
     out = np.empty((t1 - t0) * Dd, np.uint16)

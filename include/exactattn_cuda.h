@@ -4,10 +4,20 @@
  * per-row domain-error flag. Rows that the fast tier cannot certify are recomputed on the GPU
  * (a wide-integer tier); nothing falls back to the CPU.
  *
- * Return codes: 0 OK; -1 bad dimensions; -2 acc_bits not 64/128; -3 non-finite alpha;
- * -4 CUDA error; -5 unsupported layout.
+ * Return codes: 0 OK; -1 bad dimensions; -2 acc_bits not 64/128; -3 non-finite alpha (these
+ * three as the reference's csrc/exact_attention_cpu.cpp:589-592); -4 CUDA error; -5 a bounded
+ * device wait gave up (a stalled GPU; returned by the synchronous host-pointer entry points after
+ * the affected rows were recomputed by the later tiers: out and flags are complete and exact);
+ * -6 the allocation-free entry point's scratch is too small for the call; -7 NCCL not found;
+ * -8 an NCCL call failed; -9 unsupported layout (mask kind or paged shape).
  * Per-row flags: 0 certified, 2 NaN/inf input or an fp32 logit overflow (the reference raises
  * ExactAttentionDomainError), 1 never expected (no device tier certified the row).
+ *
+ * Tiers (all on the GPU): tier 1 (tensor-core kernels, or the CUDA-core split kernel) certifies
+ * almost every row; the rows it cannot certify are rerun by tier 2 (int64 fixed point on the CUDA
+ * cores, each row's keys split into chunks over the whole GPU from a device work list); what
+ * tier 2 cannot certify is computed by tier 3 (1536-bit integer windows, also split by key
+ * chunks). Value rows wider than 256 channels go straight to tier 3.
  */
 #ifndef EXACTATTN_CUDA_H
 #define EXACTATTN_CUDA_H
@@ -30,7 +40,7 @@ extern "C" {
  * depend on them. splits partitions each row's keys into KV splits merged exactly.
  * out: rows x dv uint16 (bf16) or float (fp32_out). flags: rows bytes.
  * stats[0..2] += (scores recomputed exactly, weights recomputed with the 128-bit exp2,
- * rows sent to the wide tier). Synchronous and thread-safe: the host-pointer entry points share
+ * rows the fast tier left uncertified). Synchronous and thread-safe: the host-pointer entry points share
  * one staging workspace per device, and concurrent calls on one device run one after another. */
 int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
                       int64_t nkeys, int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx,
@@ -91,11 +101,14 @@ float ea_round_ratio_cuda(uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t 
  * (a shared prefix plus a per-row list: tree verification). */
 enum { EA_MASK_CSR = 0, EA_MASK_RANGE = 1, EA_MASK_PAGED = 2, EA_MASK_HYBRID = 3 };
 
-#define EA_STATS_LEN 8
+#define EA_STATS_LEN 12
 /* stats slots (int64, accumulated): 0 scores recomputed exactly, 1 weights by the 128-bit exp2,
- * 2 rows sent to the wide tier, 3 domain-error rows, 4 unresolved rows (flag 1; never
- * expected), 5 (row, key) pairs processed, 6 host fallbacks (always 0), 7 pairs processed by the
- * tensor-core kernel. */
+ * 2 rows tier 1 left uncertified (rerun by tier 2), 3 domain-error rows, 4 unresolved rows
+ * (flag 1; never expected), 5 (row, key) pairs processed by tier 1, 6 host fallbacks (always 0),
+ * 7 pairs processed by the tensor-core kernels, 8 CTAs whose bounded wait gave up (their rows are
+ * recomputed by the later tiers; the host-pointer entry points then return -5), 9 rows tier 2
+ * left uncertified (computed by tier 3), 10 (row, key) pairs rerun by tier 2, 11 rows the test
+ * hook forced out of tier 1. */
 
 typedef struct ea_launch {
   /* inputs, device pointers */
@@ -237,17 +250,39 @@ int ea_kernel_timing(int mode, double* total_ms, int64_t* launches);
 int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int64_t n, int64_t* out);
 
 /* Allocation-free form of ea_launch_cuda, for callers that cannot allocate device memory when
- * they run attention (while capturing a CUDA graph, under an allocator that owns the whole GPU,
- * or in a latency-bound loop that cannot stall on a first allocation). No counterpart in the
- * reference. Its scratch (split partials, tier-3 work list, counters) is one static device array
- * of EA_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until exit; a call needing
- * more (rows x splits x (20 dv + 32) bytes plus 4 bytes per row, about) returns -6 with a message
- * from ea_noalloc_last_error(). The first call on a device looks up the array's address: make it
- * before any stream capture. Calls share the array, so calls on one device whose kernels may
- * overlap race and must be serialised. CUDA-core kernels only (d <= 1024, dv <= 256). */
+ * they run attention: a serving process whose memory pool owns the whole GPU and forbids
+ * allocations behind its back, or a latency-bound loop that cannot stall on a first cudaMalloc.
+ * No counterpart in the reference. Its scratch (split partials, tier-3 work list, counters) is one
+ * static device array of EA_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * exit. A call needs, with A(x) = x rounded up to a multiple of 256 and n = rows x splits,
+ *   A(8 EA_STATS_LEN) + A(4) + A(4 rows)
+ *   + (splits > 1 ? 2 A(8 n) + 2 A(8 n dv) + 2 A(4 n) + A(4 n dv) : 0)
+ * bytes; a call needing more returns -6. Every failure's message is in ea_noalloc_last_error().
+ * The first call on a device looks up the array's address (cudaGetSymbolAddress with that device
+ * current): make that first call before any stream capture. Calls share the array, which keeps the
+ * previous call's contents (each call clears what must start at zero), so calls on one device
+ * whose kernels may overlap race and must be serialised. CUDA-core kernels only (d <= 1024,
+ * dv <= 256, splits <= 65535); the test hooks do not apply. */
 #define EA_NOALLOC_SCRATCH_BYTES (32u << 20)
 int ea_attention_cuda_noalloc(const ea_launch_t* args, void* stream);
 const char* ea_noalloc_last_error(void);
+
+/* Test hooks, for tests of this library (all zero in production). force_stride > 0: every row r
+ * with r % force_stride == 0 that tier 1 certified is treated as uncertified, so it runs through
+ * tier 2, and with force_tier == 2 through tier 3 as well (stats[11] counts the rows); the output
+ * bits must not change. wait_debug != 0: every bounded wait of the tensor-core kernels reports
+ * expiry once its phase has completed (or after 20 ms), so their abort path runs with nothing left
+ * in flight: stats[8] counts the CTAs, their rows are recomputed by the later tiers, and the
+ * host-pointer entry points return -5. Applies to every device, to launches made after the call;
+ * NULL resets. Returns 0 or -1. No reference counterpart as an entry point: the reference drives
+ * its fallback tiers in tests by narrowing its windows (Config(acc_bits=34),
+ * tests/test_certified.py:129-139). */
+typedef struct ea_test_hooks {
+  int force_stride;
+  int force_tier;
+  int wait_debug;
+} ea_test_hooks_t;
+int ea_set_test_hooks(const ea_test_hooks_t* hooks);
 
 /* Sizes the workspace for up to `rows` rows, `splits` splits and dv channels on the current
  * device; call before capturing a launch in a CUDA graph. */

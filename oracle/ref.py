@@ -19,12 +19,42 @@ import numpy as np
 from . import exact
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_ref", "libexactattn_cpu.so")
+_VARIANTS = (("x86-64-v4", "libexactattn_cpu_v4.so", {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"}),
+             ("x86-64-v3", "libexactattn_cpu_v3.so", {"avx2", "bmi2", "fma", "movbe"}),
+             ("x86-64-v2", "libexactattn_cpu.so", set()))
 _lib = None
+
+
+def _cpu_flags() -> set:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("flags"):
+                return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def _pick() -> tuple[str, str]:
+    """The most capable build of the reference kernel this CPU runs (the reference builds with
+    -march=native; oracle/Makefile builds the x86-64 levels)."""
+    flags = _cpu_flags()
+    for name, so, need in _VARIANTS:
+        p = os.path.join(_HERE, "_ref", so)
+        if os.path.exists(p) and need <= flags:
+            return name, p
+    return _VARIANTS[-1][0], os.path.join(_HERE, "_ref", _VARIANTS[-1][1])
+
+
+LIB_VARIANT, LIB_PATH = _pick()
 
 
 def available() -> bool:
     return os.path.exists(LIB_PATH)
+
+
+def build_variant() -> str:
+    return LIB_VARIANT
 
 
 def _load():

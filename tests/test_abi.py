@@ -31,7 +31,8 @@ def test_library_exports_every_declared_symbol(cuda_lib):
 
 @pytest.mark.parametrize("ctype,mirror", [("ea_launch_t", _lib.LaunchArgs), ("ea_partials_t", _lib.PartialsArgs),
                                           ("ea_wide_partials_t", _lib.WidePartialsArgs),
-                                          ("ea_kv_append_t", _lib.KvAppendArgs)])
+                                          ("ea_kv_append_t", _lib.KvAppendArgs),
+                                          ("ea_test_hooks_t", _lib.TestHooks)])
 def test_struct_layout_matches_header(cuda_lib, tmp_path, ctype, mirror):
     """The ctypes mirrors of the header's structs have the C compiler's size and field offsets."""
     import subprocess
@@ -52,3 +53,21 @@ def test_build_targets_sm100a():
     from exactattention_b200 import build
 
     assert "arch=compute_100a,code=sm_100a" in build.FLAGS
+
+
+def test_exactattn_import_name():
+    """The reference's import name serves the same functions (no GPU call)."""
+    import exactattn
+    import exactattention_b200 as ea
+    from exactattn.cuda import attention_cuda
+    from exactattn.torch_impl import attention_torch
+
+    assert exactattn.attention is ea.attention
+    assert attention_cuda is ea.cuda.attention_cuda
+    assert attention_torch is ea.torch_impl.attention_torch
+    assert exactattn.default_alpha(64) == ea.default_alpha(64)
+
+
+def test_stats_length_matches_header():
+    src = open(os.path.join(ROOT, "include", "exactattn_cuda.h")).read()
+    assert int(re.search(r"#define EA_STATS_LEN (\d+)", src).group(1)) == _lib.EA_STATS_LEN == len(_lib.STAT_NAMES)

@@ -42,7 +42,7 @@ def test_decode_range_matches_simt_and_oracle(kind, vkind, group, splits):
     Q, K, V, kb, kl = _range_case(rng, kind, vkind, nseg, group, L)
     dev = torch.device("cuda")
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_d, f_d = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
                            splits=splits, stats=st, segments=_t(cuda.row_segments(kb), dev))
     o_s, f_s = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
@@ -90,7 +90,7 @@ def test_decode_paged_matches_csr_and_oracle(hq, hkv, ps, splits):
     Q, Kc, Vc, pt, ctx = _paged_case(rng, B, hq, hkv, ps, 1, 600)
     dev = torch.device("cuda")
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_p, f_p = cuda.launch(_t(Q, dev), _t(Kc, dev), _t(Vc, dev), alpha, page_table=_t(pt, dev),
                            seq_lens=_t(ctx.astype(np.int32), dev), page_size=ps, q_heads=hq, kv_heads=hkv,
                            splits=splits, stats=st)
@@ -161,7 +161,7 @@ def test_decode_kv_sharded_partials():
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb_full, dev),
                                kv_len=_t(kl_full, dev))
     parts, shard_args = [], []
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     for lo, hi in [(0, 1000), (1000, 1900), (1900, n)]:
         Ks = np.concatenate([K[lo:hi], K[n + lo:n + hi]])
         Vs = np.concatenate([V[lo:hi], V[n + lo:n + hi]])

@@ -121,7 +121,7 @@ def test_kv_shards_tensor_core_match_full(shards):
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
                                blocks=_t(cuda.row_blocks(kb, kl), dev))
     parts, shard_args = [], []
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     for lo, hi in _bounds(S, shards):
         klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
         m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
@@ -186,7 +186,7 @@ def test_kv_shards_wide_tier_rows():
     alpha = ea.default_alpha(d)
     kb = np.zeros(rows, np.int64)
     kl = np.full(rows, n, np.int64)
-    st_full = torch.zeros(8, dtype=torch.int64, device=dev)
+    st_full = torch.zeros(12, dtype=torch.int64, device=dev)
     full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev),
                                stats=st_full)
     parts, shard_args = [], []
@@ -196,7 +196,7 @@ def test_kv_shards_wide_tier_rows():
         shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha, m))
         parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
     out, flags = cuda.finalize_partials(merge_local(parts), n)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     n3 = finish_local(shard_args, out, flags, n, stats=st)
     torch.cuda.synchronize()
     assert st_full.cpu().numpy()[2] > 0, "the single launch should need the wide tier here"

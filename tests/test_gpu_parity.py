@@ -324,7 +324,7 @@ def test_config_sha(ea, name, splits):
     if name not in gold:
         pytest.skip(f"no golden SHA for {name}")
     case = w.device_case(name)
-    stats = torch.zeros(8, dtype=torch.int64, device="cuda")
+    stats = torch.zeros(12, dtype=torch.int64, device="cuda")
     out, flags = cuda.launch(case["q"], case["k"], case["v"], case["cfg"].alpha, splits=splits, stats=stats,
                              **case["kw"])
     torch.cuda.synchronize()
@@ -362,7 +362,7 @@ def test_tensor_core_prefill_matches_simt_and_oracle(ea, kind, vkind):
     dev = torch.device("cuda")
     t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
     alpha = ea.default_alpha(128)
-    st_tc = torch.zeros(8, dtype=torch.int64, device=dev)
+    st_tc = torch.zeros(12, dtype=torch.int64, device=dev)
     o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st_tc,
                              blocks=t(cuda.row_blocks(kb, kl)))
     o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
@@ -393,7 +393,7 @@ def test_tensor_core_ragged_blocks_and_nan(ea):
     dev = torch.device("cuda")
     t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st,
                              blocks=t(cuda.row_blocks(kb, kl)))
     o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
@@ -483,7 +483,7 @@ def test_tensor_core_value_channel_edges(ea):
     dev = torch.device("cuda")
     t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st,
                              blocks=t(cuda.row_blocks(kb, kl)))
     o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
@@ -525,7 +525,7 @@ def test_tensor_core_hybrid_tree_mask(ea):
     dev = torch.device("cuda")
     t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), row_ptr=t(rp), key_idx=t(ki),
                              stats=st, blocks=t(cuda.row_blocks(kb, kl)))
     o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), row_ptr=t(rp), key_idx=t(ki))
@@ -555,7 +555,7 @@ def test_tensor_core_prefill_fp32_output(ea):
     dev = torch.device("cuda")
     t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
     alpha = ea.default_alpha(128)
-    st = torch.zeros(8, dtype=torch.int64, device=dev)
+    st = torch.zeros(12, dtype=torch.int64, device=dev)
     o_tc, f_tc = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), stats=st, out="fp32",
                              blocks=t(cuda.row_blocks(kb, kl)))
     o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), out="fp32")
