@@ -53,7 +53,7 @@ DEFAULT_SPLITS = {"c2": 1, "c3": 4, "c4": 1, "c5": 32}
 # our kernel launches per step: tier 1, split combine / list kernel, and the fallback tiers'
 # fixed launches (they run on device-side counts, so they launch every step); KV-sharded c5 adds
 # the rescale and finalize kernels
-LAUNCHES = {"c2": 2, "c3": 3, "c4": 4, "c5": 3, "c5-sharded": 4}
+LAUNCHES = {"c2": 9, "c3": 10, "c4": 11, "c5": 10, "c5-sharded": 4}
 
 
 def parse():

@@ -23,7 +23,7 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
            "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda", "ea_selftest_fast64",
-           "ea_merge_partials_nccl", "ea_set_test_hooks")
+           "ea_merge_partials_nccl", "ea_set_test_hooks", "ea_last_host_stats")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -125,6 +125,8 @@ def load(path: str | None = None):
     lib.ea_selftest_fast64.restype = ctypes.c_int
     lib.ea_merge_partials_nccl.argtypes = [ctypes.POINTER(PartialsArgs), ctypes.c_int64, ctypes.c_int, P, P]
     lib.ea_merge_partials_nccl.restype = ctypes.c_int
+    lib.ea_last_host_stats.argtypes = [P]
+    lib.ea_last_host_stats.restype = ctypes.c_int
     lib.ea_set_test_hooks.argtypes = [ctypes.POINTER(TestHooks)]
     lib.ea_set_test_hooks.restype = ctypes.c_int
     lib.ea_reserve_workspace.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int]
@@ -171,3 +173,12 @@ def set_test_hooks(force_stride: int = 0, force_tier: int = 0, wait_debug: int =
     rc = load().ea_set_test_hooks(ctypes.byref(h))
     if rc:
         raise ValueError("invalid test hooks")
+
+
+def last_host_stats() -> dict:
+    """The full counters of this thread's last host-pointer call (ea_last_host_stats)."""
+    import numpy as np
+
+    out = np.zeros(EA_STATS_LEN, np.int64)
+    load().ea_last_host_stats(out.ctypes.data)
+    return dict(zip(STAT_NAMES, (int(x) for x in out)))

@@ -25,6 +25,9 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_wide_finalize(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
 cudaError_t launch_list_all_rows(const Prob& P, cudaStream_t st);
+cudaError_t launch_fallback(const Prob& P, const FallbackBufs& F, int sms, cudaStream_t st);
+size_t fallback_bytes(int dv);
+void fallback_carve(void* base, int dv, FallbackBufs& F);
 void nccl_release_scratch();  // ea_nccl.cu
 }  // namespace ea
 
@@ -35,6 +38,9 @@ static_assert(EA_STATS_LEN == STAT_LEN, "the C ABI's stats length and the device
 namespace {
 
 thread_local std::string g_err;
+
+// the full counters of this thread's last host-pointer call (ea_last_host_stats)
+thread_local int64_t g_last_host_stats[EA_STATS_LEN] = {0};
 
 // test hooks (ea_set_test_hooks), copied into every launch's problem description
 ea_test_hooks_t g_hooks = {0, 0, 0};
@@ -57,6 +63,12 @@ struct Workspace {
   int* t3_count = nullptr;
   int* t3_list = nullptr;
   int64_t t3_cap = 0;
+  // the fallback tiers: tier 3's row list (capacity t3_cap, after the count in list3_blk) and
+  // the fixed-size tier-2 / tier-3 buffers for fb_dv channels
+  void* list3_blk = nullptr;
+  void* fb = nullptr;
+  int fb_dv = 0;
+  FallbackBufs F{};
   void* part = nullptr;
   size_t part_bytes = 0;
   // staging for the host-pointer entry point, and the row lists it builds on the host (pinned)
@@ -119,9 +131,24 @@ bool grow(void** p, size_t* cap, size_t need) {
 int reserve(Workspace* w, int64_t rows, int splits, int dv) {
   if (rows > w->t3_cap) {
     if (w->t3_list) cudaFree(w->t3_list);
+    if (w->list3_blk) cudaFree(w->list3_blk);
     w->t3_list = nullptr;
+    w->list3_blk = nullptr;
+    w->t3_cap = 0;
     if (cudaMalloc(&w->t3_list, (size_t)rows * sizeof(int)) != cudaSuccess) return fail_cuda(cudaErrorMemoryAllocation, "t3_list");
+    if (cudaMalloc(&w->list3_blk, 256 + (size_t)rows * sizeof(int)) != cudaSuccess)
+      return fail_cuda(cudaErrorMemoryAllocation, "tier-3 list");
     w->t3_cap = rows;
+    w->F.count3 = (int*)w->list3_blk;
+    w->F.list3 = (int*)((char*)w->list3_blk + 256);
+  }
+  const int fdv = dv <= 32 ? 32 : dv <= 64 ? 64 : dv <= 128 ? 128 : 256;  // the fallback buffers' width
+  if (dv <= 256 && fdv > w->fb_dv) {
+    if (w->fb) cudaFree(w->fb);
+    w->fb = nullptr;
+    w->fb_dv = 0;
+    if (cudaMalloc(&w->fb, fallback_bytes(fdv)) != cudaSuccess) return fail_cuda(cudaErrorMemoryAllocation, "fallback");
+    w->fb_dv = fdv;
   }
   if (!grow(&w->part, &w->part_bytes, part_bytes(rows, splits, dv)))
     return fail_cuda(cudaErrorMemoryAllocation, "partials");
@@ -165,6 +192,8 @@ void ea_cuda_release(void) {
     if (w.stats) cudaFree(w.stats);
     if (w.t3_count) cudaFree(w.t3_count);
     if (w.t3_list) cudaFree(w.t3_list);
+    if (w.list3_blk) cudaFree(w.list3_blk);
+    if (w.fb) cudaFree(w.fb);
     if (w.part) cudaFree(w.part);
     if (w.stage) cudaFree(w.stage);
     if (w.lists) cudaFree(w.lists);
@@ -213,6 +242,13 @@ static int check_launch(const ea_launch_t* a) {
                                         a->q_heads % a->kv_heads != 0))
     return -9;
   return 0;
+}
+
+// The fallback buffers of workspace w carved for dv channels (reserve() sized them).
+static FallbackBufs fallback_bufs(Workspace* w, int dv) {
+  FallbackBufs F = w->F;
+  fallback_carve(w->fb, dv, F);
+  return F;
 }
 
 // Problem description from the launch arguments, with the workspace's split buffers when
@@ -281,8 +317,10 @@ static bool tc_shape(const ea_launch_t* a) {
          ((uintptr_t)a->k & 15) == 0;
 }
 
+// RANGE masks with row blocks: the tensor-core prefill kernel (KV splits on its grid's y, merged
+// by the split combine)
 static bool tc_applicable(const ea_launch_t* a) {
-  return a->mask_kind == EA_MASK_RANGE && a->splits == 1 && tc_shape(a);
+  return a->mask_kind == EA_MASK_RANGE && tc_shape(a);
 }
 
 // A HYBRID mask (shared key range + per-row list: tree verification) with row blocks: the range
@@ -338,9 +376,8 @@ static int launch_decode_tc(const ea_launch_t* a, Workspace* w, cudaStream_t st)
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 decode launch");
   e = launch_combine(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "combine");
-  int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
-  e = launch_tier3(P, blocks, st);
-  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  e = launch_fallback(P, fallback_bufs(w, a->dv), w->sms, st);
+  if (e != cudaSuccess) return fail_cuda(e, "fallback tiers");
   return 0;
 }
 
@@ -381,9 +418,8 @@ static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 list launch");
   e = launch_combine(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "combine");
-  int blocks = (int)(a.rows < 2 * w->sms ? a.rows : 2 * w->sms);
-  e = launch_tier3(P, blocks, st);
-  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  e = launch_fallback(P, fallback_bufs(w, a.dv), w->sms, st);
+  if (e != cudaSuccess) return fail_cuda(e, "fallback tiers");
   return 0;
 }
 
@@ -416,17 +452,15 @@ static int launch_on(const ea_launch_t* a, Workspace* w, cudaStream_t st) {
   build_prob(a, w, P);
   cudaError_t e = cudaMemsetAsync(w->t3_count, 0, sizeof(int), st);
   if (e != cudaSuccess) return fail_cuda(e, "memset");
+  const bool tc = tc_applicable(a);
   {
     TimedLaunch tl(st);
-    if (tc_applicable(a))
-      e = launch_tc_prefill(P, a->block_rows, a->nblocks, st);
-    else
-      e = launch_simt(P, st);
+    e = tc ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
   }
+  if (e == cudaSuccess && tc && a->splits > 1) e = launch_combine(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 launch");
-  int blocks = (int)(a->rows < 2 * w->sms ? a->rows : 2 * w->sms);
-  e = launch_tier3(P, blocks, st);
-  if (e != cudaSuccess) return fail_cuda(e, "tier-3 launch");
+  e = launch_fallback(P, fallback_bufs(w, a->dv), w->sms, st);
+  if (e != cudaSuccess) return fail_cuda(e, "fallback tiers");
   return 0;
 }
 
@@ -512,10 +546,12 @@ int ea_partials_cuda(const ea_launch_t* a, const ea_partials_t* x, void* stream)
   build_prob(a, w, P);
   set_export(P, x);
   cudaError_t e;
+  const bool tc = tc_applicable(a);
   {
     TimedLaunch tl(st);
-    e = tc_applicable(a) ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
+    e = tc ? launch_tc_prefill(P, a->block_rows, a->nblocks, st) : launch_simt(P, st);
   }
+  if (e == cudaSuccess && tc && a->splits > 1) e = launch_combine(P, st);  // split partials -> export
   if (e != cudaSuccess) return fail_cuda(e, "partials launch");
   return 0;
 }
@@ -594,6 +630,7 @@ static void order_by_len_desc(const int64_t* kv_len, int32_t* r0, int32_t* r1) {
 // -5 when a bounded wait of a tensor-core kernel gave up during the call (a stalled GPU): the
 // affected rows were recomputed by the later tiers, so out and flags are complete and exact.
 static int wait_status(const int64_t* hs) {
+  memcpy(g_last_host_stats, hs, sizeof(g_last_host_stats));
   if (hs[STAT_WAIT_EXPIRED] == 0) return 0;
   g_err = std::to_string(hs[STAT_WAIT_EXPIRED]) +
           " CTA(s) of a tensor-core kernel gave up a bounded wait; their rows were recomputed by the "
@@ -601,13 +638,40 @@ static int wait_status(const int64_t* hs) {
   return -5;
 }
 
-// Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back.
-// Exactly one of (row_ptr, key_idx) or (kv_base, kv_len) is used; neither: every key.
+// KV splits the host entries choose for the tensor-core kernels when the caller leaves the
+// schedule to the library (the reference's C entry takes `splits` for its CPU threads; the bits
+// never depend on it): prefill a split per block unless the blocks are too few to fill the GPU;
+// decode enough splits for about eight CTAs per SM, each at least 1024 keys.
+static int auto_splits(bool decode, int64_t units, int64_t maxlen, int sms) {
+  if (units <= 0) return 1;
+  int64_t sp;
+  if (decode) {
+    sp = (8 * (int64_t)sms + units - 1) / units;
+    sp = std::min<int64_t>(sp, std::max<int64_t>(1, maxlen / 1024));
+  } else {
+    if (units >= sms) return 1;
+    sp = (sms + units - 1) / units;
+    sp = std::min<int64_t>(sp, std::max<int64_t>(1, maxlen / 512));
+  }
+  return (int)std::max<int64_t>(1, std::min<int64_t>(sp, 64));
+}
+
+// Copies host inputs to the workspace, runs ea_launch_cuda, copies the results back. The mask:
+// (row_ptr, key_idx) CSR; (kv_base, kv_len) ranges; both: HYBRID (the range, then the list);
+// neither: every key. auto_sched: the library picks the KV splits of the tensor-core kernels.
 static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v, int64_t nkeys,
                     int dv, float alpha, const int64_t* row_ptr, const int64_t* key_idx, const int64_t* kv_base_h,
                     const int64_t* kv_len_h, int64_t maxn, int fp32_out, int splits, void* out, uint8_t* flags,
-                    int64_t* stats) {
+                    int64_t* stats, bool auto_sched = false) {
   int64_t total = row_ptr ? row_ptr[rows] : 0;
+  std::vector<int64_t> kb, kl;
+  if (!row_ptr && !kv_len_h) {  // every key: one range shared by all rows
+    kb.assign(rows, 0);
+    kl.assign(rows, nkeys);
+    kv_base_h = kb.data();
+    kv_len_h = kl.data();
+  }
+  const bool hybrid = row_ptr && kv_len_h;
   const size_t osz = fp32_out ? 4 : 2;
   // staging layout: q | k | v | mask | out | flags | stats; the copies start before the host
   // builds the row lists (blocks / segments) of a range mask
@@ -619,7 +683,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   };
   size_t oq = slot((size_t)rows * d * 2), ok = slot((size_t)nkeys * d * 2), ov = slot((size_t)nkeys * dv * 2);
   size_t orp = slot((size_t)(rows + 1) * 8), oki = slot((size_t)(row_ptr ? total : 0) * 8);
-  size_t okb = slot((size_t)(row_ptr ? 0 : rows) * 8), okl = slot((size_t)(row_ptr ? 0 : rows) * 8);
+  size_t okb = slot((size_t)(kv_len_h ? rows : 0) * 8), okl = slot((size_t)(kv_len_h ? rows : 0) * 8);
   size_t oo = slot((size_t)rows * dv * osz), of = slot((size_t)rows), os = slot(EA_STATS_LEN * 8);
 
   std::unique_lock<std::mutex> call;
@@ -641,38 +705,35 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   EA_CPY(oq, q, (size_t)rows * d * 2);
   EA_CPY(ok, k, (size_t)nkeys * d * 2);
   EA_CPY(ov, v, (size_t)nkeys * dv * 2);
-  std::vector<int64_t> kb, kl;
   if (row_ptr) {
     EA_CPY(orp, row_ptr, (size_t)(rows + 1) * 8);
     EA_CPY(oki, key_idx, (size_t)total * 8);
-  } else if (kv_len_h) {
+  }
+  if (kv_len_h) {
     EA_CPY(okb, kv_base_h, (size_t)rows * 8);
     EA_CPY(okl, kv_len_h, (size_t)rows * 8);
-  } else {
-    kb.assign(rows, 0);
-    kl.assign(rows, nkeys);
-    EA_CPY(okb, kb.data(), (size_t)rows * 8);
-    EA_CPY(okl, kl.data(), (size_t)rows * 8);
   }
 #undef EA_CPY
   // Range masks at d = dv = 128: rows sharing kv_base either form decode segments (at most 8 rows
   // per key range: the decode kernel) or 128-row blocks, longest first (the prefill kernel),
-  // built while the copies above run.
+  // built while the copies above run. HYBRID masks take blocks (their range part).
   std::vector<int32_t> blocks, segs;
   bool decode = false;
+  int64_t range_max = 0;
   if (kv_len_h && d == 128 && dv == 128 && rows < (1ll << 31)) {
+    for (int64_t r = 0; r < rows; ++r) range_max = std::max(range_max, kv_len_h[r]);
     std::vector<int32_t> order;
     std::vector<int64_t> gstart;
     group_rows(kv_base_h, rows, order, gstart);
     const int64_t ng = (int64_t)gstart.size() - 1;
     int64_t gmax = 0;
     for (int64_t g = 0; g < ng; ++g) gmax = std::max(gmax, gstart[g + 1] - gstart[g]);
-    decode = gmax <= 8;
+    decode = gmax <= 8 && !hybrid;
     if (decode) {
       segs.assign((size_t)ng * 8, -1);
       for (int64_t g = 0; g < ng; ++g)
         for (int64_t u = gstart[g]; u < gstart[g + 1]; ++u) segs[(size_t)(8 * g + u - gstart[g])] = order[u];
-    } else if (splits == 1) {
+    } else {
       // rows of a group by decreasing kv_len, cut into 128-row blocks; blocks by decreasing
       // length of their first (longest) row
       std::vector<int64_t> bst;  // first position in `order` of each block
@@ -724,7 +785,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.nkeys = nkeys;
   a.dv = dv;
   a.alpha = alpha;
-  a.mask_kind = row_ptr ? EA_MASK_CSR : EA_MASK_RANGE;
+  a.mask_kind = hybrid ? EA_MASK_HYBRID : row_ptr ? EA_MASK_CSR : EA_MASK_RANGE;
   a.row_ptr = (const int64_t*)(base + orp);
   a.key_idx = (const int64_t*)(base + oki);
   a.kv_base = (const int64_t*)(base + okb);
@@ -739,6 +800,8 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.nblocks = (int64_t)(blocks.size() / 128);
   a.seg_rows = segs.empty() ? nullptr : lists_d + blocks.size();
   a.nsegs = (int64_t)(segs.size() / 8);
+  if (auto_sched && (a.nblocks > 0 || a.nsegs > 0))
+    a.splits = auto_splits(a.nsegs > 0, a.nsegs > 0 ? a.nsegs : a.nblocks, range_max, w->sms);
   int rc = launch_host(&a, w);
   if (rc) {
     cudaStreamSynchronize(st);
@@ -772,16 +835,44 @@ int ea_attention_cuda(const uint16_t* q, int64_t rows, int d, const uint16_t* k,
   if (!decode_fp32(ab, am, ae)) return -3;
   if (rows <= 0) return 0;
   int64_t maxn = 1;
-  if (row_ptr) {
-    for (int64_t r = 0; r < rows; ++r) {
-      int64_t n = row_ptr[r + 1] - row_ptr[r];
-      if (n > maxn) maxn = n;
-    }
-  } else {
-    maxn = nkeys;
+  if (!row_ptr) {
+    return run_host(q, rows, d, k, v, nkeys, dv, alpha, nullptr, nullptr, nullptr, nullptr, std::max<int64_t>(1, nkeys),
+                    fp32_out, splits, out, flags, stats, true);
   }
-  return run_host(q, rows, d, k, v, nkeys, dv, alpha, row_ptr, key_idx, nullptr, nullptr, maxn, fp32_out, splits,
-                  out, flags, stats);
+  for (int64_t r = 0; r < rows; ++r) maxn = std::max(maxn, row_ptr[r + 1] - row_ptr[r]);
+  // The reference's callers pass CSR lists that are mostly runs of consecutive keys (causal and
+  // prefix masks, tree masks as prefix + ancestors): each row's leading ascending run becomes a
+  // key range, the rest stays a list. All runs: a RANGE mask; mostly runs (at d = dv = 128): a
+  // HYBRID mask (the ranges on the tensor cores, the lists on the CUDA cores, merged exactly).
+  // The same keys in a different layout give the same bits.
+  std::vector<int64_t> kb((size_t)rows), kl((size_t)rows);
+  int64_t tail = 0;
+  for (int64_t r = 0; r < rows; ++r) {
+    const int64_t p0 = row_ptr[r], p1 = row_ptr[r + 1];
+    int64_t m = 0;
+    kb[r] = p1 > p0 ? key_idx[p0] : 0;
+    if (p1 > p0)
+      for (m = 1; p0 + m < p1 && key_idx[p0 + m] == kb[r] + m;) ++m;
+    kl[r] = m;
+    tail += (p1 - p0) - m;
+  }
+  const int64_t total = row_ptr[rows] - row_ptr[0];
+  if (tail == 0)
+    return run_host(q, rows, d, k, v, nkeys, dv, alpha, nullptr, nullptr, kb.data(), kl.data(), maxn, fp32_out, splits,
+                    out, flags, stats, true);
+  if (d == 128 && dv == 128 && 4 * tail <= total) {
+    std::vector<int64_t> trp((size_t)rows + 1), tki;
+    tki.reserve((size_t)tail);
+    for (int64_t r = 0; r < rows; ++r) {
+      trp[r] = (int64_t)tki.size();
+      tki.insert(tki.end(), key_idx + row_ptr[r] + kl[r], key_idx + row_ptr[r + 1]);
+    }
+    trp[rows] = (int64_t)tki.size();
+    return run_host(q, rows, d, k, v, nkeys, dv, alpha, trp.data(), tki.data(), kb.data(), kl.data(), maxn, fp32_out,
+                    splits, out, flags, stats, true);
+  }
+  return run_host(q, rows, d, k, v, nkeys, dv, alpha, row_ptr, key_idx, nullptr, nullptr, maxn, fp32_out, splits, out,
+                  flags, stats, true);
 }
 
 int ea_attention_cuda_ranges(const uint16_t* q, int64_t rows, int d, const uint16_t* k, const uint16_t* v,
@@ -894,6 +985,12 @@ int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* x, const int64_t* m
 }
 
 }  // extern "C"
+
+extern "C" int ea_last_host_stats(int64_t* out) {
+  if (!out) return -1;
+  memcpy(out, g_last_host_stats, sizeof(g_last_host_stats));
+  return 0;
+}
 
 extern "C" int ea_set_test_hooks(const ea_test_hooks_t* h) {
   std::lock_guard<std::mutex> lk(g_mu);

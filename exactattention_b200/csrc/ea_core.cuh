@@ -192,6 +192,7 @@ struct FallbackBufs {
   int32_t* pNR;
   int64_t* pN;
   uint64_t* pNe;
+  int32_t* pRlo;  // a merged group's lowest exponent, at its head slot (the spread check)
   // tier-3 unit wide partials (T3_UNITS slots)
   int64_t* w3max;
   int64_t* w3sum;

@@ -453,8 +453,11 @@ __global__ void __launch_bounds__(128) simt_split_kernel(Prob P) {
 // ---------------------------------------------------------------------------
 // Merge of the partials in slots first + s * stride (s < S), one warp: the largest reference
 // exponents, every partial re-expressed at them, integer sums (order-free), the spread check.
+// pRlo (optional): per slot the lowest reference exponent among the partials merged into it
+// before (a two-level merge), so that the spread check sees every original partial.
 template <int CPL>
-__device__ __forceinline__ void merge_slots(const Prob& P, int64_t first, int64_t stride, int S, SimtPart<CPL>& o) {
+__device__ __forceinline__ void merge_slots(const Prob& P, int64_t first, int64_t stride, int S, SimtPart<CPL>& o,
+                                            const int32_t* pRlo = nullptr) {
   const int lane = threadIdx.x & 31;
   const int dv = P.dv;
   int status = ST_OK;
@@ -464,7 +467,7 @@ __device__ __forceinline__ void merge_slots(const Prob& P, int64_t first, int64_
     status = max(status, P.pSt[pi]);
     if (P.pR[pi] != R_EMPTY) {
       R = (R == R_EMPTY) ? P.pR[pi] : max(R, P.pR[pi]);
-      Rmin = min(Rmin, P.pR[pi]);
+      Rmin = min(Rmin, pRlo ? pRlo[pi] : P.pR[pi]);
     }
   }
   // a split far below the row's largest weights: the exponent spread may exceed the reference's
@@ -537,6 +540,166 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
     export_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
   else
     finalize_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
+}
+
+// ---------------------------------------------------------------------------
+// tier 2: the rows tier 1 left uncertified, int64 fixed point on the CUDA cores, each row's keys
+// cut into chunks over the whole GPU (the reference reruns its uncertified pairs with int64 P.V
+// from a device work list: triton_kernels.py:1046-1067, 1498-1515)
+// ---------------------------------------------------------------------------
+// Plan of a split-K fallback tier, one block of 1024 threads, from device-side counts only (no host
+// synchronisation): the rows in_list[0 .. n) with n = min(*in_count, max_rows) get units of
+// `chunk` keys, chunk >= min_chunk chosen so that every unit fits ucap; u_off[i] is row i's first
+// unit, u_off[n] the unit count; u_n = {n, units, chunk, mode}. Rows past max_rows: mode 0 (tier
+// 2) appends them to (over_list, over_count) for tier 3; mode 1 (tier 3) plans no units and marks
+// the run as one block per whole row (u_n = {count, count, 0, 1}).
+__global__ void __launch_bounds__(1024) fallback_plan_kernel(Prob P, const int* in_list, const int* in_count,
+                                                              int max_rows, int ucap, int64_t min_chunk, int* u_off,
+                                                              int64_t* u_n, int* over_list, int* over_count,
+                                                              int mode) {
+  __shared__ int64_t wsum[32];
+  __shared__ int64_t s_chunk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int count = *in_count;
+  if (mode == 1 && count > max_rows) {
+    if (tid == 0) {
+      u_n[0] = count;
+      u_n[1] = count;
+      u_n[2] = 0;
+      u_n[3] = 1;
+    }
+    return;
+  }
+  const int n = min(count, max_rows);
+  for (int i = n + tid; i < count; i += blockDim.x) {
+    const int k = atomicAdd(over_count, 1);
+    over_list[k] = in_list[i];
+  }
+  if (tid == 0 && count > n) stat_add(P, STAT_TIER2_UNCERT, (unsigned long long)(count - n));
+  // total keys of the planned rows
+  int64_t t = 0;
+  for (int i = tid; i < n; i += blockDim.x) t += row_len(P, in_list[i]);
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (lane == 0) wsum[warp] = t;
+  __syncthreads();
+  if (tid == 0) {
+    int64_t tot = 0;
+    for (int w = 0; w < 32; ++w) tot += wsum[w];
+    const int64_t room = max(1, ucap - n);
+    s_chunk = max(min_chunk, (tot + room - 1) / room);
+  }
+  __syncthreads();
+  const int64_t chunk = s_chunk;
+  // units per row, exclusive scan over contiguous per-thread ranges (sum <= ucap: ceil(L / chunk)
+  // <= L / chunk + 1 and the keys fill at most ucap - n chunks)
+  const int per = (n + 1023) / 1024;
+  const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+  int64_t mine = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int64_t L = row_len(P, in_list[i]);
+    mine += L > chunk ? (L + chunk - 1) / chunk : 1;
+  }
+  int64_t inc = mine;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int64_t base = inc - mine;
+  for (int w = 0; w < warp; ++w) base += wsum[w];
+  for (int i = i0; i < i1; ++i) {
+    u_off[i] = (int)base;
+    const int64_t L = row_len(P, in_list[i]);
+    base += L > chunk ? (L + chunk - 1) / chunk : 1;
+  }
+  if (tid == 1023) {
+    u_off[n] = (int)base;  // the last thread's running sum is the total
+    u_n[0] = n;
+    u_n[1] = base;
+    u_n[2] = chunk;
+    u_n[3] = 0;
+  }
+}
+
+// the listed row (index into u_rows) that unit u belongs to: the last i with u_off[i] <= u
+__device__ __forceinline__ int unit_row(const int* u_off, int n, int64_t u) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (u_off[mid] <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Tier-2 units: warp per (row, key chunk), the tier-1 CUDA-core arithmetic over the chunk; the
+// partial goes to the unit's slot of P.p* (grid-stride over the planned units).
+template <int CPL>
+__global__ void __launch_bounds__(128) tier2_units_kernel(Prob P) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  uint64_t* sTA = (uint64_t*)smem;
+  uint64_t* sTB = sTA + 256;
+  load_exp2_tables(sTA, sTB);
+  __syncthreads();
+  unsigned char* ws = smem + 4096 + (size_t)warp * simt_warp_bytes(P.d, P.dv);
+  const int n = (int)P.u_n[0];
+  const int64_t units = P.u_n[1], chunk = P.u_n[2];
+  for (int64_t u = (int64_t)blockIdx.x * nwarps + warp; u < units; u += (int64_t)gridDim.x * nwarps) {
+    const int i = unit_row(P.u_off, n, u);
+    const int64_t r = P.u_rows[i];
+    const int64_t L = row_len(P, r);
+    const int64_t j0 = min(L, (u - P.u_off[i]) * chunk), j1 = min(L, j0 + chunk);
+    SimtPart<CPL> o;
+    unsigned long long n_exact = 0, n_wide = 0;
+    simt_range<CPL>(P, r, j0, j1, sTA, sTB, ws, o, n_exact, n_wide);
+    simt_stats(P, n_exact, n_wide, (unsigned long long)(j1 - j0), STAT_TIER2_PAIRS);
+    write_split_partial<CPL>(P, u, o);
+    __syncwarp();
+  }
+}
+
+// The merge of a row's units runs in two levels so that a long row's thousands of units are
+// merged in parallel: groups of GROUP consecutive units are merged in place into their first
+// unit's slot (warp per group), then each row merges its group heads. Re-expressing at a group's
+// largest exponent and then at the row's is the same floor as one shift (only the error bounds,
+// which can only decide whether a row certifies, gain their rounding units).
+constexpr int T2_GROUP = 64, T3_GROUP = 16;
+
+// Level 1 of the tier-2 merge: warp per group head (unit u with (u - u_off[i]) % T2_GROUP == 0).
+// pRlo[u] keeps the group's lowest exponent for the spread check.
+template <int CPL>
+__global__ void __launch_bounds__(128) tier2_group_kernel(Prob P, int32_t* pRlo) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int n = (int)P.u_n[0];
+  const int64_t units = P.u_n[1];
+  for (int64_t u = (int64_t)blockIdx.x * nwarps + warp; u < units; u += (int64_t)gridDim.x * nwarps) {
+    const int i = unit_row(P.u_off, n, u);
+    if ((u - P.u_off[i]) % T2_GROUP != 0) continue;  // uniform across the warp
+    const int cnt = (int)min((int64_t)T2_GROUP, (int64_t)P.u_off[i + 1] - u);
+    SimtPart<CPL> o;
+    merge_slots<CPL>(P, u, 1, cnt, o);
+    __syncwarp();  // every lane has read the group's slots before the head is overwritten
+    write_split_partial<CPL>(P, u, o);
+    if (lane == 0) pRlo[u] = o.Rlo;
+  }
+}
+
+// Tier-2 merge, level 2: warp per planned row, its group heads merged exactly and the row
+// certified; what still fails goes on to tier 3's list (P.t3_list; P.tier == 2).
+template <int CPL>
+__global__ void __launch_bounds__(128) tier2_merge_kernel(Prob P, const int32_t* pRlo) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n = P.u_n[0];
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; i < n; i += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t r = P.u_rows[i];
+    const int u0 = P.u_off[i], u1 = P.u_off[i + 1];
+    SimtPart<CPL> o;
+    merge_slots<CPL>(P, u0, T2_GROUP, (u1 - u0 + T2_GROUP - 1) / T2_GROUP, o, pRlo);
+    finalize_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -694,11 +857,26 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
   const int tid = threadIdx.x;
   const int d = P.d, dv = P.dv;
   const int64_t FW = 32ll * LW - 64 - P.key_log2;
-  const int count = P.t3_fixed > 0 ? P.t3_fixed : *P.t3_count;
+  // planned run (after tier 2): u_n[3] == 0 split-K units (item = unit, its key chunk, a wide
+  // partial per unit for tier3_merge_kernel), 1 one item per listed row; otherwise the list
+  // (t3_list, t3_count or t3_fixed) with whole rows
+  const bool planned = P.u_n != nullptr;
+  const bool split = planned && P.u_n[3] == 0;
+  const bool exporting = P.export_partials || split;
+  const int count = planned ? (int)P.u_n[1] : P.t3_fixed > 0 ? P.t3_fixed : *P.t3_count;
 
   for (int item = blockIdx.x; item < count; item += gridDim.x) {
-    const int64_t r = P.t3_list[item];
-    const int64_t L = row_len(P, r);
+    int64_t r, j0 = 0, j1;
+    if (split) {
+      const int i = unit_row(P.u_off, (int)P.u_n[0], item);
+      r = P.u_rows[i];
+      const int64_t L = row_len(P, r);
+      j0 = min(L, (item - P.u_off[i]) * P.u_n[2]);
+      j1 = min(L, j0 + P.u_n[2]);
+    } else {
+      r = planned ? P.u_rows[item] : P.t3_list[item];
+      j1 = row_len(P, r);
+    }
     // q row
     int qlead = INT32_MIN;
     int qbad = 0;
@@ -721,8 +899,8 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       bool has_n = false;
       // sStatus is written only between the top of an iteration and its first barrier, and read
       // only after that barrier, so every thread sees the same value and leaves together.
-      for (int64_t t0 = 0; t0 < L; t0 += T3_THREADS) {
-        const int nt = (int)min((int64_t)T3_THREADS, L - t0);
+      for (int64_t t0 = j0; t0 < j1; t0 += T3_THREADS) {
+        const int nt = (int)min((int64_t)T3_THREADS, j1 - t0);
         int st = ST_OK;
         int64_t E = 0;
         uint32_t M = 0;
@@ -834,7 +1012,7 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       __syncthreads();
       const int st = sStatus;
       __syncthreads();  // every thread has read sStatus before any finalisation writes it
-      if (P.export_partials) {
+      if (exporting) {
         // this key range's wide partial (normalised digits), merged across GPUs by
         // wide_rescale_kernel and an all-reduce SUM, finalised by wide_finalize_kernel
         Zw.normalize();
@@ -877,7 +1055,7 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       if (st2 != ST_OK) break;
     }
     __syncthreads();
-    if (P.export_partials) {
+    if (exporting) {
       __syncthreads();  // the next row resets sStatus
       continue;
     }
@@ -929,20 +1107,17 @@ __global__ void wide_rescale_kernel(Prob P, int n, const int64_t* gmax) {
   a[LW] = (int64_t)err;
 }
 
-// Block per listed row: certified rounding of the merged wide sums into the row's outputs.
-__global__ void __launch_bounds__(T3_THREADS) wide_finalize_kernel(Prob P, int n, const int64_t* gmax) {
-  __shared__ int sOk;
-  const int item = blockIdx.x, tid = threadIdx.x;
-  if (item >= n) return;
-  const int64_t r = P.t3_list[item];
-  const int64_t* g = gmax + (int64_t)item * 4;
+// Certified rounding of one row's merged wide sums (base: Z then every channel's N, digits and
+// error; g: merged R, Emax, -Emin, status) into its outputs and flag; a block of T3_THREADS.
+__device__ void wide_finalize_row(const Prob& P, const int64_t* base, const int64_t* g, int64_t r, int* sOkp) {
+  int& sOk = *sOkp;
+  const int tid = threadIdx.x;
   const int64_t R = g[0], Emax = g[1], Emin = g[2] == INT64_MIN ? INT64_MAX : -g[2];
   int st = (int)g[3];
   if (st == ST_OK && R != INT64_MIN && Emax - Emin > MAX_SPREAD) st = ST_DOMAIN;
   if (tid == 0) sOk = 1;
   __syncthreads();
   bool ok = st == ST_OK;
-  const int64_t* base = P.w3sum + (int64_t)item * (P.dv + 1) * (LW + 1);
   Wide<LW> Zw;
   uint64_t Zerr = 0;
   if (ok && R != INT64_MIN) {
@@ -984,6 +1159,110 @@ __global__ void __launch_bounds__(T3_THREADS) wide_finalize_kernel(Prob P, int n
     } else {
       P.flags[r] = 0;
     }
+  }
+}
+
+// Block per listed row: certified rounding of the merged wide sums into the row's outputs.
+__global__ void __launch_bounds__(T3_THREADS) wide_finalize_kernel(Prob P, int n, const int64_t* gmax) {
+  __shared__ int sOk;
+  const int item = blockIdx.x;
+  if (item >= n) return;
+  wide_finalize_row(P, P.w3sum + (int64_t)item * (P.dv + 1) * (LW + 1), gmax + (int64_t)item * 4, P.t3_list[item],
+                    &sOk);
+}
+
+// Merge of the wide partials in slots first + s * stride (s < cnt) into slot `first` (a block of
+// T3_THREADS): MAX of the exponent records, every window floor-shifted to the largest R (the
+// error grows by the shift's rounding), digit-wise SUM, as the KV-sharded wide tier does across
+// GPUs. The merged record goes to g (which may be the first slot's own record).
+__device__ void wide_merge_slots(const Prob& P, int64_t first, int64_t stride, int cnt, int64_t* g, int64_t* red) {
+  const int tid = threadIdx.x, dv = P.dv;
+  int64_t R = INT64_MIN, Emax = INT64_MIN, nEmin = INT64_MIN, st = ST_OK;
+  for (int s = tid; s < cnt; s += T3_THREADS) {
+    const int64_t* m = P.w3max + (first + (int64_t)s * stride) * 4;
+    R = max(R, m[0]);
+    Emax = max(Emax, m[1]);
+    nEmin = max(nEmin, m[2]);
+    st = max(st, m[3]);
+  }
+  R = block_max64(R, red);
+  Emax = block_max64(Emax, red);
+  nEmin = block_max64(nEmin, red);
+  st = block_max64(st, red);
+  for (int j = tid; j <= dv; j += T3_THREADS) {
+    int64_t acc[LW];
+    for (int k = 0; k < LW; ++k) acc[k] = 0;
+    uint64_t err = 0;
+    for (int s = 0; s < cnt; ++s) {
+      const int64_t u = first + (int64_t)s * stride;
+      const int64_t Ru = P.w3max[u * 4];
+      if (Ru == INT64_MIN) continue;  // no keys in this slot
+      const int64_t* a = P.w3sum + (u * (dv + 1) + j) * (LW + 1);
+      Wide<LW> w;
+      for (int k = 0; k < LW; ++k) w.d[k] = a[k];
+      uint64_t e = (uint64_t)a[LW];
+      if (R > Ru) {
+        const int64_t sft = R - Ru;
+        const bool lost = w.shr(sft);
+        e = sft >= 64 ? (e != 0) : ((e >> sft) + ((e & ((1ull << sft) - 1)) != 0));
+        e += lost;
+      }
+      for (int k = 0; k < LW; ++k) acc[k] += w.d[k];
+      err += e;
+    }
+    int64_t* o = P.w3sum + (first * (dv + 1) + j) * (LW + 1);
+    for (int k = 0; k < LW; ++k) o[k] = acc[k];
+    o[LW] = (int64_t)err;
+  }
+  __syncthreads();  // every slot's record and windows have been read
+  if (tid == 0) {
+    g[0] = R;
+    g[1] = Emax;
+    g[2] = nEmin;
+    g[3] = st;
+  }
+  __syncthreads();
+}
+
+// Level 1 of the tier-3 merge (split mode only): block per group head of T3_GROUP units, merged in
+// place into the head's slot; the digit sums are renormalised before level 2 adds them up again.
+__global__ void __launch_bounds__(T3_THREADS) tier3_group_kernel(Prob P) {
+  __shared__ int64_t red[T3_THREADS / 32];
+  if (P.u_n[3] != 0) return;
+  const int n = (int)P.u_n[0], dv = P.dv;
+  const int64_t units = P.u_n[1];
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const int i = unit_row(P.u_off, n, u);
+    if ((u - P.u_off[i]) % T3_GROUP != 0) continue;  // uniform across the block
+    const int cnt = (int)min((int64_t)T3_GROUP, (int64_t)P.u_off[i + 1] - u);
+    wide_merge_slots(P, u, 1, cnt, P.w3max + u * 4, red);
+    // normalise the head's windows (each digit back to 32 bits) for the next level's shifts
+    for (int j = threadIdx.x; j <= dv; j += T3_THREADS) {
+      int64_t* a = P.w3sum + (u * (dv + 1) + j) * (LW + 1);
+      if (P.w3max[u * 4] == INT64_MIN) continue;
+      Wide<LW> w;
+      for (int k = 0; k < LW; ++k) w.d[k] = a[k];
+      w.normalize();
+      for (int k = 0; k < LW; ++k) a[k] = w.d[k];
+    }
+    __syncthreads();
+  }
+}
+
+// Tier-3 merge of a split-K run, level 2 (nothing to do in whole-row mode): block per planned row,
+// its group heads merged into its first slot, then certified. g3: merged records (T3_SPLIT_ROWS x 4).
+__global__ void __launch_bounds__(T3_THREADS) tier3_merge_kernel(Prob P, int64_t* g3) {
+  __shared__ int64_t red[T3_THREADS / 32];
+  __shared__ int sOk;
+  if (P.u_n[3] != 0) return;
+  const int n = (int)P.u_n[0], tid = threadIdx.x, dv = P.dv;
+  for (int i = blockIdx.x; i < n; i += gridDim.x) {
+    const int u0 = P.u_off[i], u1 = P.u_off[i + 1];
+    int64_t* g = g3 + (int64_t)i * 4;
+    wide_merge_slots(P, u0, T3_GROUP, (u1 - u0 + T3_GROUP - 1) / T3_GROUP, g, red);
+    wide_finalize_row(P, P.w3sum + (int64_t)u0 * (dv + 1) * (LW + 1), g, P.u_rows[i], &sOk);
+    __syncthreads();
+    (void)tid;
   }
 }
 
@@ -1079,6 +1358,105 @@ cudaError_t launch_list_all_rows(const Prob& P, cudaStream_t st) {
 
 cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st) {
   tier3_kernel<<<blocks, T3_THREADS, 0, st>>>(P);
+  return cudaGetLastError();
+}
+
+size_t fallback_bytes(int dv) {
+  auto a = [](size_t x) { return (x + 255) & ~(size_t)255; };
+  return a((T2_MAX_ROWS + 1) * 4) + a((T3_SPLIT_ROWS + 1) * 4) + 2 * a(4 * 8) + a((size_t)T3_SPLIT_ROWS * 4 * 8) +
+         3 * a((size_t)T2_UNITS * 4) + 2 * a((size_t)T2_UNITS * 8) + a((size_t)T2_UNITS * dv * 4) +
+         2 * a((size_t)T2_UNITS * dv * 8) + a((size_t)T3_UNITS * 4 * 8) + a((size_t)T3_UNITS * (dv + 1) * (LW + 1) * 8);
+}
+
+// carves a fallback_bytes(dv) block into the fallback buffers (list3 / count3 come separately)
+void fallback_carve(void* base, int dv, FallbackBufs& F) {
+  char* p = (char*)base;
+  auto take = [&](size_t bytes) {
+    char* r = p;
+    p += (bytes + 255) & ~(size_t)255;
+    return (void*)r;
+  };
+  F.u2_off = (int*)take((T2_MAX_ROWS + 1) * 4);
+  F.u3_off = (int*)take((T3_SPLIT_ROWS + 1) * 4);
+  F.u2_n = (int64_t*)take(4 * 8);
+  F.u3_n = (int64_t*)take(4 * 8);
+  F.g3 = (int64_t*)take((size_t)T3_SPLIT_ROWS * 4 * 8);
+  F.pR = (int32_t*)take((size_t)T2_UNITS * 4);
+  F.pSt = (int32_t*)take((size_t)T2_UNITS * 4);
+  F.pRlo = (int32_t*)take((size_t)T2_UNITS * 4);
+  F.pZ = (int64_t*)take((size_t)T2_UNITS * 8);
+  F.pZe = (uint64_t*)take((size_t)T2_UNITS * 8);
+  F.pNR = (int32_t*)take((size_t)T2_UNITS * dv * 4);
+  F.pN = (int64_t*)take((size_t)T2_UNITS * dv * 8);
+  F.pNe = (uint64_t*)take((size_t)T2_UNITS * dv * 8);
+  F.w3max = (int64_t*)take((size_t)T3_UNITS * 4 * 8);
+  F.w3sum = (int64_t*)take((size_t)T3_UNITS * (dv + 1) * (LW + 1) * 8);
+}
+
+template <int CPL>
+static cudaError_t launch_tier2_cpl(const Prob& P2, int32_t* pRlo, int sms, cudaStream_t st) {
+  const int warps = simt_warps_for(P2.d, P2.dv);
+  const size_t smem = simt_smem_bytes(P2.d, P2.dv, warps);
+  cudaError_t e = cudaFuncSetAttribute(tier2_units_kernel<CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int gu = min((T2_UNITS + warps - 1) / warps, 4 * sms);
+  tier2_units_kernel<CPL><<<gu, warps * 32, smem, st>>>(P2);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  tier2_group_kernel<CPL><<<min(T2_UNITS / 4, 4 * sms), 128, 0, st>>>(P2, pRlo);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  tier2_merge_kernel<CPL><<<min(T2_MAX_ROWS / 4, 2 * sms), 128, 0, st>>>(P2, pRlo);
+  return cudaGetLastError();
+}
+
+// The fallback tiers after a tier-1 launch of P (dv <= 256): tier 2 reruns the rows tier 1
+// listed (P.t3_list, *P.t3_count), tier 3 computes what tier 2 could not certify (split by key
+// chunks when few rows are left). Fixed launches that read their work from device memory, so
+// nothing waits on the host and the sequence can be captured in a CUDA graph.
+cudaError_t launch_fallback(const Prob& P, const FallbackBufs& F, int sms, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(F.count3, 0, sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  fallback_plan_kernel<<<1, 1024, 0, st>>>(P, P.t3_list, P.t3_count, T2_MAX_ROWS, T2_UNITS, T2_MIN_CHUNK, F.u2_off,
+                                           F.u2_n, F.list3, F.count3, 0);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  Prob P2 = P;
+  P2.tier = 2;
+  P2.splits = 1;
+  P2.export_partials = 0;
+  P2.t3_fixed = 0;
+  P2.u_off = F.u2_off;
+  P2.u_n = F.u2_n;
+  P2.u_rows = P.t3_list;
+  P2.t3_list = F.list3;
+  P2.t3_count = F.count3;
+  P2.pR = F.pR;
+  P2.pZ = F.pZ;
+  P2.pZe = F.pZe;
+  P2.pSt = F.pSt;
+  P2.pNR = F.pNR;
+  P2.pN = F.pN;
+  P2.pNe = F.pNe;
+  if (P.dv <= 32) e = launch_tier2_cpl<1>(P2, F.pRlo, sms, st);
+  else if (P.dv <= 64) e = launch_tier2_cpl<2>(P2, F.pRlo, sms, st);
+  else if (P.dv <= 128) e = launch_tier2_cpl<4>(P2, F.pRlo, sms, st);
+  else e = launch_tier2_cpl<8>(P2, F.pRlo, sms, st);
+  if (e != cudaSuccess) return e;
+  fallback_plan_kernel<<<1, 1024, 0, st>>>(P, F.list3, F.count3, T3_SPLIT_ROWS, T3_UNITS, T3_MIN_CHUNK, F.u3_off,
+                                           F.u3_n, nullptr, nullptr, 1);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  Prob P3 = P;
+  P3.tier = 3;
+  P3.export_partials = 0;
+  P3.t3_fixed = 0;
+  P3.u_off = F.u3_off;
+  P3.u_n = F.u3_n;
+  P3.u_rows = F.list3;
+  P3.w3max = F.w3max;
+  P3.w3sum = F.w3sum;
+  tier3_kernel<<<2 * sms, T3_THREADS, 0, st>>>(P3);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  tier3_group_kernel<<<min(T3_UNITS, 2 * sms), T3_THREADS, 0, st>>>(P3);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  tier3_merge_kernel<<<min(T3_SPLIT_ROWS, 2 * sms), T3_THREADS, 0, st>>>(P3, F.g3);
   return cudaGetLastError();
 }
 

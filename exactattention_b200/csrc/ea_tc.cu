@@ -90,6 +90,7 @@ struct Small {
   uint64_t bar_pv[2];  // P.V rounds, by round parity
   uint32_t tmem;
   int32_t maxlen;
+  int32_t ka, kb;  // this KV split's keys of the block's range
   int64_t base;
 };
 
@@ -216,7 +217,23 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   if (tid == 0) {
     int32_t m = 0;
     for (int i = 0; i < BM; ++i) m = max(m, S.len[i]);
+    // KV split blockIdx.y of gridDim.y: keys [ka, kb) of the block's range, the cut points
+    // rounded down to whole tiles; every row keeps its keys below kb, from ka on
+    int32_t ka = 0, kb = m;
+    if (gridDim.y > 1) {
+      const int64_t sp = blockIdx.y, ns = gridDim.y;
+      ka = (int32_t)(((int64_t)m * sp / ns) & ~(int64_t)(BN - 1));
+      kb = sp + 1 == ns ? m : (int32_t)(((int64_t)m * (sp + 1) / ns) & ~(int64_t)(BN - 1));
+      S.base += ka;
+      m = max(0, kb - ka);
+    }
+    S.ka = ka;
+    S.kb = kb;
     S.maxlen = m;
+  }
+  if (gridDim.y > 1) {
+    __syncthreads();
+    if (tid < BM) S.len[tid] = max(0, min(S.len[tid], S.kb) - S.ka);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -920,25 +937,36 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
   }
   __syncthreads();
   // ---------------- export (KV-sharded runs) or finalise ----------------
-  if (P.export_partials) {
+  // KV splits (gridDim.y > 1) write split partials, merged exactly by the split combine; a
+  // KV-sharded run exports its partials in the same one-sided form
+  const bool exporting = P.export_partials || gridDim.y > 1;
+  const int64_t so = (int64_t)blockIdx.y * P.rows;
+  int32_t* xR = gridDim.y > 1 ? P.pR + so : P.xR;
+  int64_t* xZ = gridDim.y > 1 ? P.pZ + so : P.xZ;
+  uint64_t* xZe = gridDim.y > 1 ? P.pZe + so : P.xZe;
+  int32_t* xSt = gridDim.y > 1 ? P.pSt + so : P.xSt;
+  int32_t* xNR = gridDim.y > 1 ? P.pNR + so * DV : P.xNR;
+  int64_t* xN = gridDim.y > 1 ? P.pN + so * DV : P.xN;
+  uint64_t* xNe = gridDim.y > 1 ? P.pNe + so * DV : P.xNe;
+  if (exporting) {
     // partials in the one-sided form [N, N + Nerr] of ea_partials_t: this kernel's N interval is
     // [N - Nerr, N + Nerr], in units 2^(R + VE_c - FN) = 2^(NR - FZ) with NR = R + VE_c
     if (myrow >= 0) {
       const int st = ok_wait ? S.rst[r] : ST_TIER3;
       if (u4 == 0) {
-        P.xR[myrow] = R;
-        P.xZ[myrow] = Z;
-        P.xZe[myrow] = Zerr;
-        P.xSt[myrow] = st;
+        xR[myrow] = R;
+        xZ[myrow] = Z;
+        xZe[myrow] = Zerr;
+        xSt[myrow] = st;
       }
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const int ch = 32 * u4 + c, ve = S.ve[ch];
         const int64_t o = (int64_t)myrow * DV + ch;
         const bool empty = R == R_EMPTY || ve == INT32_MIN;
-        P.xNR[o] = empty ? R_EMPTY : R + ve;
-        P.xN[o] = empty ? 0 : N[c] - (int64_t)Nerr;
-        P.xNe[o] = empty ? 0 : 2 * Nerr;
+        xNR[o] = empty ? R_EMPTY : R + ve;
+        xN[o] = empty ? 0 : N[c] - (int64_t)Nerr;
+        xNe[o] = empty ? 0 : 2 * Nerr;
       }
     }
   } else {
@@ -1048,7 +1076,9 @@ cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t 
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  tck::tc_prefill_kernel<<<(unsigned)nblocks, tck::THREADS, tck::SMEM_BYTES, st>>>(P, block_rows);
+  // KV splits on grid.y (the split partials are merged by the split combine)
+  dim3 grid((unsigned)nblocks, (unsigned)(P.splits > 1 ? P.splits : 1));
+  tck::tc_prefill_kernel<<<grid, tck::THREADS, tck::SMEM_BYTES, st>>>(P, block_rows);
   return cudaGetLastError();
 }
 

@@ -404,6 +404,56 @@ def attention_cuda_paged(q, k_cache, v_cache, alpha, page_table, seq_lens, q_hea
     return res, flags
 
 
+def split_runs(row_ptr: np.ndarray, key_idx: np.ndarray):
+    """CSR rows of ascending, distinct keys (the rows of a boolean mask) as a leading run of
+    consecutive keys plus a tail list: (kv_base, kv_len, tail_row_ptr, tail_key_idx). Causal and
+    prefix rows are one run with an empty tail; tree rows are the prefix run plus the ancestors.
+    The same keys in either layout give the same bits."""
+    row_ptr = np.asarray(row_ptr, np.int64)
+    key_idx = np.asarray(key_idx, np.int64)
+    rows = len(row_ptr) - 1
+    counts = np.diff(row_ptr)
+    kb = np.zeros(rows, np.int64)
+    nz = counts > 0
+    kb[nz] = key_idx[row_ptr[:-1][nz]]
+    rowid = np.repeat(np.arange(rows), counts)
+    offs = np.arange(len(key_idx), dtype=np.int64) - np.repeat(row_ptr[:-1], counts)
+    # keys ascending and distinct: key - (first + offset) never decreases along a row, so the
+    # positions still in the run are a prefix of the row
+    inrun = key_idx == kb[rowid] + offs
+    kl = np.bincount(rowid[inrun], minlength=rows).astype(np.int64)
+    tail = key_idx[~inrun]
+    trp = np.concatenate([[0], np.cumsum(counts - kl)]).astype(np.int64)
+    return kb, kl, trp, tail
+
+
+def mask_launch_kwargs(row_ptr: np.ndarray, key_idx: np.ndarray, d: int, dv: int, device):
+    """`launch` mask keywords for a CSR mask of ascending, distinct keys: RANGE when every row is
+    one run of consecutive keys, HYBRID when runs hold at least three quarters of the keys (at
+    d = dv = 128), CSR otherwise; with the row blocks or decode segments that put RANGE and HYBRID
+    masks on the tensor-core kernels."""
+    import torch
+
+    kb, kl, trp, tail = split_runs(row_ptr, key_idx)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(device)  # noqa: E731
+    counts = np.diff(np.asarray(row_ptr, np.int64))
+    mk = int(counts.max(initial=1))
+    tc = d == 128 and dv == 128
+    if len(tail) == 0:
+        kw = dict(kv_base=t(kb), kv_len=t(kl), max_row_keys=mk)
+        if tc:
+            groups = np.unique(kb, return_counts=True)[1]
+            if len(groups) and groups.max() <= 8:
+                kw["segments"] = t(row_segments(kb))
+            else:
+                kw["blocks"] = t(row_blocks(kb, kl))
+        return kw
+    if tc and 4 * len(tail) <= len(key_idx):
+        return dict(kv_base=t(kb), kv_len=t(kl), row_ptr=t(trp), key_idx=t(tail), max_row_keys=mk,
+                    blocks=t(row_blocks(kb, kl)))
+    return dict(row_ptr=t(np.asarray(row_ptr, np.int64)), key_idx=t(np.asarray(key_idx, np.int64)), max_row_keys=mk)
+
+
 def row_segments(kv_base: np.ndarray, width: int = 8) -> np.ndarray:
     """Groups RANGE-mask rows that share kv_base into segments of at most `width` (8) rows, -1
     padded: the (nsegs, 8) int32 `segments` argument of launch (decode: a GQA group per segment).

@@ -64,8 +64,14 @@ def main(argv=None) -> int:
         h = sha(out)
         match = h == info["sha256"]
         ok &= match
+        extra = ""
+        if args.backend == "cuda":
+            from ._lib import last_host_stats
+
+            st = last_host_stats()
+            extra = f", {st['tc_pairs']} of {st['pairs']} pairs on the tensor cores"
         print(f"head {key}: {'MATCH' if match else 'MISMATCH'} sha256 {h[:16]}  ({dt:.2f}s, "
-              f"{int((flags != 0).sum())} flagged rows, 0 host fallbacks)", flush=True)
+              f"{int((flags != 0).sum())} flagged rows, 0 host fallbacks{extra})", flush=True)
     print("ALL MATCH" if ok else "MISMATCH")
     return 0 if ok else 1
 

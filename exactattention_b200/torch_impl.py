@@ -42,9 +42,9 @@ def attention_torch(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, 
         return torch.from_numpy(x.view(dt) if x.dtype == np.uint16 else x).to(dev)
 
     Q, K, V = t(q, np.int16), t(k, np.int16), t(v, np.int16)
-    RP, KI = t(row_ptr, None), t(key_idx, None)
-    o, fl = cuda.launch(Q, K, V, alpha, row_ptr=RP, key_idx=KI, max_row_keys=int(counts.max(initial=1)),
-                        out=out)
+    # causal / prefix rows as key ranges, tree rows as a range plus a list: the tensor-core kernels
+    mask_kw = cuda.mask_launch_kwargs(row_ptr, key_idx, q.shape[1], v.shape[1], dev)
+    o, fl = cuda.launch(Q, K, V, alpha, out=out, **mask_kw)
     o = o.cpu().numpy()
     flags = fl.cpu().numpy().astype(np.uint8)
     res = o.view(np.float32).copy() if out == "fp32" else o.view(np.uint16).copy()

@@ -267,6 +267,12 @@ int ea_selftest_fast64(int mode, uint64_t seed, uint32_t stride, int64_t n, int6
 int ea_attention_cuda_noalloc(const ea_launch_t* args, void* stream);
 const char* ea_noalloc_last_error(void);
 
+/* The EA_STATS_LEN counters of the calling thread's last successful host-pointer call
+ * (ea_attention_cuda, _ranges, _paged): the reference's C entry reports three counters through its
+ * `stats` argument; this gives the rest (pairs on the tensor cores, tier-2 work, ...). No reference
+ * counterpart. Returns 0, or -1 for a NULL out. */
+int ea_last_host_stats(int64_t* out);
+
 /* Test hooks, for tests of this library (all zero in production). force_stride > 0: every row r
  * with r % force_stride == 0 that tier 1 certified is treated as uncertified, so it runs through
  * tier 2, and with force_tier == 2 through tier 3 as well (stats[11] counts the rows); the output

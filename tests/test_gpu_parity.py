@@ -76,6 +76,93 @@ def test_fixture_heads_sha(ea, splits):
         out, flags = attention_cuda(q, k, v, a, rp, ki, splits=splits, stats=st)
         assert sha(out) == info["sha256"], key
         assert not flags.any() and st.host_fallbacks == 0
+        from exactattention_b200 import _lib
+
+        full = _lib.last_host_stats()
+        assert full["tc_pairs"] == full["pairs"] == int(kv.sum()), full  # every pair on the tensor cores
+
+
+def _csr(rows_keys):
+    rp = np.concatenate([[0], np.cumsum([len(x) for x in rows_keys])]).astype(np.int64)
+    ki = np.concatenate(rows_keys).astype(np.int64)
+    return rp, ki
+
+
+def test_csr_entry_reaches_tensor_cores(ea):
+    """The reference's C entry with CSR lists (ea_attention_cuda): causal rows run on the
+    tensor-core prefill kernel, tree rows (prefix + ancestors) on it plus the CUDA-core list
+    kernel, a GQA decode group on the decode kernel. Bits equal the CUDA-core CSR path and the
+    oracle."""
+    import torch
+
+    from exactattention_b200 import _lib, cuda
+    from exactattention_b200.cuda import attention_cuda
+    from oracle import exact
+
+    rng = np.random.default_rng(21)
+    alpha = ea.default_alpha(128)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    cases = []
+    S = 300  # causal prefill, two heads
+    cases.append(("causal", bf16(rng, (2 * S, 128), "outlier"), bf16(rng, (S, 128), "outlier"),
+                  bf16(rng, (S, 128)), [np.arange(r % S + 1) for r in range(2 * S)], 2 * (S * (S + 1) // 2)))
+    P, T = 500, 40  # tree verification: prefix + ancestors, node keys after the prefix
+    parent = [-1] + [int(rng.integers(0, i)) for i in range(1, T)]
+    tree_rows = []
+    for h in range(2):
+        for i in range(T):
+            path, x = [], i
+            while x != -1:
+                path.append(P + x)
+                x = parent[x]
+            tree_rows.append(np.concatenate([np.arange(P), np.sort(np.array(path))]))
+    cases.append(("tree", bf16(rng, (2 * T, 128)), bf16(rng, (P + T, 128), "outlier"), bf16(rng, (P + T, 128)),
+                  tree_rows, None))
+    n = 700  # one GQA decode group
+    cases.append(("decode", bf16(rng, (2, 128)), bf16(rng, (n, 128), "heavy"), bf16(rng, (n, 128)),
+                  [np.arange(n), np.arange(n)], 2 * n))
+    for name, Q, K, V, rows_keys, tc_pairs in cases:
+        rp, ki = _csr(rows_keys)
+        out, flags = attention_cuda(Q, K, V, alpha, rp, ki, splits=8)
+        st = _lib.last_host_stats()
+        assert not flags.any()
+        if tc_pairs is not None:
+            assert st["tc_pairs"] == tc_pairs == st["pairs"], (name, st)
+        else:
+            assert st["tc_pairs"] >= 2 * T * (P - 64), (name, st)  # the prefix part
+        o_s, _ = cuda.launch(t(Q), t(K), t(V), alpha, row_ptr=t(rp), key_idx=t(ki))  # CUDA-core CSR kernel
+        assert np.array_equal(out, o_s.cpu().numpy().view(np.uint16)), name
+        for r in (0, len(rows_keys) // 2, len(rows_keys) - 1):
+            sel = rows_keys[r]
+            assert np.array_equal(out[r], exact.attention_row(Q[r], K[sel], V[sel], alpha)), (name, r)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5, 16])
+def test_tensor_core_prefill_kv_splits(ea, splits):
+    """The prefill kernel's KV splits (grid y, tile-aligned key ranges, exact split combine) give
+    the same bits at every split count, all pairs on the tensor cores."""
+    import torch
+
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(31)
+    S = 700
+    Q = bf16(rng, (2 * S, 128), "outlier")
+    K, V = bf16(rng, (S, 128), "outlier"), bf16(rng, (S, 128), "wide")
+    kb = np.zeros(2 * S, np.int64)
+    kl = np.tile(np.arange(1, S + 1, dtype=np.int64), 2)
+    dev = torch.device("cuda")
+    t = lambda x: torch.from_numpy(x.view(np.int16) if x.dtype == np.uint16 else x).to(dev)  # noqa: E731
+    alpha = ea.default_alpha(128)
+    st = cuda.new_stats(dev)
+    o, f = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl), splits=splits, stats=st,
+                       blocks=t(cuda.row_blocks(kb, kl)))
+    o_s, f_s = cuda.launch(t(Q), t(K), t(V), alpha, kv_base=t(kb), kv_len=t(kl))
+    torch.cuda.synchronize()
+    assert not f.any().item()
+    assert st.cpu().numpy()[7] == int(kl.sum())
+    assert torch.equal(o, o_s)
 
 
 # ---------------------------------------------------------------------------

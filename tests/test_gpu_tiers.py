@@ -143,3 +143,63 @@ def test_value_rows_wider_than_256(ea, dv):
     assert not f.cpu().numpy().any()
     ref32 = exact.attention(Q, K, V, alpha, out="fp32")
     assert np.array_equal(o.cpu().numpy().view(np.uint32), ref32.view(np.uint32))
+
+
+def _golden_configs():
+    import json
+    import os
+
+    p = os.path.join(os.path.dirname(__file__), "golden", "configs.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+@pytest.mark.parametrize("name,stride,tier", [("c5", 64, 1), ("c5", 64, 2), ("c2", 100, 1), ("c2", 100, 2)])
+def test_config_with_forced_rows_keeps_sha(ea, hooks, name, stride, tier):
+    """About 1% of a full configuration's rows forced out of tier 1 (and tier 2): the SHA-256 of
+    the outputs is still the reference's, tier 2 (and tier 3) count their work, and on config 5
+    (one forced row of 2^20 keys) the step costs less than twice the clean step (the rows are
+    split by key chunks over the whole GPU instead of one block per row)."""
+    import hashlib
+
+    import torch
+
+    from exactattention_b200 import cuda, workloads as w
+
+    gold = _golden_configs().get(name)
+    if gold is None:
+        pytest.skip(f"no golden SHA for {name}")
+    case = w.device_case(name)
+    splits = 32 if name == "c5" else 1
+
+    def run(st):
+        return cuda.launch(case["q"], case["k"], case["v"], case["cfg"].alpha, splits=splits, stats=st, **case["kw"])
+
+    def timed(n=3):
+        ts = []
+        for _ in range(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            run(cuda.new_stats())
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return sorted(ts)[n // 2]
+
+    run(cuda.new_stats())
+    clean_ms = timed()
+    hooks(stride, tier, 0)
+    st = cuda.new_stats()
+    out, flags = run(st)
+    torch.cuda.synchronize()
+    s = st.cpu().numpy()
+    forced = len(range(0, case["cfg"].rows, stride))
+    assert not flags.any().item()
+    assert hashlib.sha256(out.cpu().numpy().view(np.uint16).tobytes()).hexdigest() == gold
+    assert s[11] == forced and s[2] == forced
+    assert s[10] > 0  # tier 2 ran on the forced rows' keys
+    if tier == 2:
+        assert s[9] == forced
+    forced_ms = timed()
+    print(f"{name} forced tier {tier}: clean {clean_ms:.2f} ms, with {forced} forced rows {forced_ms:.2f} ms")
+    if name == "c5":
+        assert forced_ms < 2 * clean_ms, (clean_ms, forced_ms)
