@@ -550,7 +550,7 @@ def e2e(R: Runner, name: str, case: dict, splits: int, out_dev, kv_sharded: bool
             o, f = ea_dist.attention_kv_sharded(dev["q"], dev["k"], dev["v"], cfg.alpha,
                                                 max_row_keys=kw["max_row_keys"], splits=splits, parts=parts,
                                                 kv_base=dev["kv_base"], kv_len=dev["kv_len"],
-                                                segments=dev["segments"])
+                                                segments=dev["segments"], segment_width=kw.get("segment_width", 0))
             oh.copy_(o, non_blocking=True)
             fh.copy_(f, non_blocking=True)
             torch.cuda.current_stream(R.dev).synchronize()

@@ -43,7 +43,7 @@ class LaunchArgs(ctypes.Structure):
         ("fp32_out", ctypes.c_int), ("splits", ctypes.c_int),
         ("out", ctypes.c_void_p), ("flags", ctypes.c_void_p), ("stats", ctypes.c_void_p),
         ("block_rows", ctypes.c_void_p), ("nblocks", ctypes.c_int64),
-        ("seg_rows", ctypes.c_void_p), ("nsegs", ctypes.c_int64),
+        ("seg_rows", ctypes.c_void_p), ("nsegs", ctypes.c_int64), ("seg_width", ctypes.c_int),
     ]
 
 

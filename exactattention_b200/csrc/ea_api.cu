@@ -348,7 +348,8 @@ static int64_t decode_segments(const ea_launch_t* a) {
 
 // rows per decode segment: the GQA group of a paged layout; a segment table may fill all 8 slots
 static int decode_max_rows(const ea_launch_t* a) {
-  return a->mask_kind == EA_MASK_PAGED ? a->q_heads / a->kv_heads : 8;
+  if (a->mask_kind == EA_MASK_PAGED) return a->q_heads / a->kv_heads;
+  return a->seg_width >= 1 && a->seg_width <= 8 ? a->seg_width : 8;
 }
 
 // the decode kernel writes split partials for splits >= 1: carve the split buffers for at least 2
@@ -719,6 +720,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   // built while the copies above run. HYBRID masks take blocks (their range part).
   std::vector<int32_t> blocks, segs;
   bool decode = false;
+  int seg_width = 8;
   int64_t range_max = 0;
   if (kv_len_h && d == 128 && dv == 128 && rows < (1ll << 31)) {
     for (int64_t r = 0; r < rows; ++r) range_max = std::max(range_max, kv_len_h[r]);
@@ -733,6 +735,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
       segs.assign((size_t)ng * 8, -1);
       for (int64_t g = 0; g < ng; ++g)
         for (int64_t u = gstart[g]; u < gstart[g + 1]; ++u) segs[(size_t)(8 * g + u - gstart[g])] = order[u];
+      seg_width = (int)gmax;
     } else {
       // rows of a group by decreasing kv_len, cut into 128-row blocks; blocks by decreasing
       // length of their first (longest) row
@@ -800,6 +803,7 @@ static int run_host(const uint16_t* q, int64_t rows, int d, const uint16_t* k, c
   a.nblocks = (int64_t)(blocks.size() / 128);
   a.seg_rows = segs.empty() ? nullptr : lists_d + blocks.size();
   a.nsegs = (int64_t)(segs.size() / 8);
+  a.seg_width = seg_width;
   if (auto_sched && (a.nblocks > 0 || a.nsegs > 0))
     a.splits = auto_splits(a.nsegs > 0, a.nsegs > 0 ? a.nsegs : a.nblocks, range_max, w->sms);
   int rc = launch_host(&a, w);

@@ -107,7 +107,8 @@ def _ptr(t):
 
 def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
            seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-           out_tensor=None, flags=None, stats=None, stream=None, blocks=None, segments=None, no_alloc=False):
+           out_tensor=None, flags=None, stats=None, stream=None, blocks=None, segments=None, segment_width=0,
+           no_alloc=False):
     """Device-level launch, no host sync. q (rows, d), k, v: torch tensors of bf16 bits (any
     16-bit dtype) on one CUDA device. One mask: CSR (row_ptr, key_idx int64), RANGE
     (kv_base, kv_len int64: row r attends k rows kv_base[r] + [0, kv_len[r])), or PAGED
@@ -118,8 +119,10 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     `blocks` (from row_blocks; every row in some block) lets RANGE masks with d = dv = 128 use the
     tensor-core kernel, and HYBRID masks run their shared range on it (the per-row lists on the
     CUDA cores, the two partials merged exactly). `segments` (from row_segments) runs RANGE masks
-    with d = dv = 128 through the tensor-core decode kernel (keys on the MMA's M side); PAGED masks
-    with d = dv = 128 and at most 8 q heads per kv head take it without a table.
+    with d = dv = 128 through the tensor-core decode kernel (keys on the MMA's M side);
+    `segment_width` (optional) is the most rows any segment holds (row_segments' width; a GQA
+    group of 2 keeps fewer running sums per thread). PAGED masks with d = dv = 128 and at most 8 q
+    heads per kv head take that kernel without a table.
     `no_alloc` calls ea_attention_cuda_noalloc instead: the library allocates no device memory for
     the call (its scratch is a fixed static array of EA_NOALLOC_SCRATCH_BYTES; larger calls raise).
     Returns (out (rows, dv) int16/int32 bit patterns, flags (rows,) uint8)."""
@@ -138,7 +141,7 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
     a = _launch_args(q, k, v, alpha, row_ptr=row_ptr, key_idx=key_idx, kv_base=kv_base, kv_len=kv_len,
                      page_table=page_table, seq_lens=seq_lens, page_size=page_size, q_heads=q_heads,
                      kv_heads=kv_heads, max_row_keys=max_row_keys, splits=splits, out=out, blocks=blocks,
-                     segments=segments)
+                     segments=segments, segment_width=segment_width)
     a.out, a.flags = out_tensor.data_ptr(), flags.data_ptr()
     a.stats = _ptr(stats)
     s = stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
@@ -155,7 +158,7 @@ def launch(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=N
 
 def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv_len=None, page_table=None,
                  seq_lens=None, page_size=0, q_heads=0, kv_heads=0, max_row_keys=None, splits=1, out="bf16",
-                 blocks=None, segments=None):
+                 blocks=None, segments=None, segment_width=0):
     """ea_launch_t for `launch`'s inputs and mask (outputs left unset)."""
     rows, d = q.shape[0], q.shape[-1]
     dv = v.shape[-1]
@@ -195,6 +198,7 @@ def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv
         a.block_rows, a.nblocks = blocks.data_ptr(), blocks.shape[0]
     if segments is not None:
         a.seg_rows, a.nsegs = segments.data_ptr(), segments.shape[0]
+        a.seg_width = int(segment_width)
     return a
 
 
@@ -445,6 +449,7 @@ def mask_launch_kwargs(row_ptr: np.ndarray, key_idx: np.ndarray, d: int, dv: int
             groups = np.unique(kb, return_counts=True)[1]
             if len(groups) and groups.max() <= 8:
                 kw["segments"] = t(row_segments(kb))
+                kw["segment_width"] = int(groups.max())
             else:
                 kw["blocks"] = t(row_blocks(kb, kl))
         return kw
@@ -523,7 +528,7 @@ def wide_partials(q, k, v, alpha, rows, *, stream=None, stats=None, **mask) -> W
         raise ValueError("wide_partials needs max_row_keys (the row's key count over all merged ranges)")
     rows = rows.to(device=dev, dtype=torch.int32).contiguous()
     w = WidePartials(rows.numel(), v.shape[-1], dev)
-    mask = {k_: v_ for k_, v_ in mask.items() if k_ not in ("blocks", "segments", "splits")}
+    mask = {k_: v_ for k_, v_ in mask.items() if k_ not in ("blocks", "segments", "segment_width", "splits")}
     a = _launch_args(q, k, v, alpha, **mask)
     a.stats = _ptr(stats)
     ws = w.struct()

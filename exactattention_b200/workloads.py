@@ -448,7 +448,7 @@ def device_case(name: str, device="cuda", shard: int = 0, nshards: int = 1) -> d
 
         kw = dict(kv_base=torch.from_numpy(base.astype(np.int64)).to(dev),
                   kv_len=torch.from_numpy(np.full(rows, Tn, np.int64)).to(dev), max_row_keys=T,
-                  segments=torch.from_numpy(row_segments(base)).to(dev))
+                  segments=torch.from_numpy(row_segments(base)).to(dev), segment_width=GROUP)
     elif name == "c4":
         from .cuda import row_blocks
 

@@ -148,6 +148,9 @@ typedef struct ea_launch {
    * PAGED masks with d = dv = 128 and q_heads / kv_heads <= 8 take that kernel without it. */
   const int32_t* seg_rows;
   int64_t nsegs;
+  /* optional: the most rows any segment of seg_rows holds (1..8; 0 = up to 8). Segments of a GQA
+   * group of 2 (or 4) let the decode kernel keep fewer running sums per thread. */
+  int seg_width;
 } ea_launch_t;
 
 /* Device-pointer entry point: asynchronous on `stream` (a cudaStream_t, NULL = default).
