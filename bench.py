@@ -5,9 +5,9 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5|c2|c3|c4] [--ex
 
 The headline (`value`) is config 5: batch 4 x 16 q / 8 kv heads x one query token against 2^20
 keys (67,108,864 certified pairs per step). On one GPU it is the whole job; under torchrun every
-(sequence, kv head) is sharded by key range over the ranks and the int64 row partials are merged
-by two NCCL all-reduces (MAX of the exponents, SUM of the rescaled integers): strong scaling, the
-same bits at every N. In the same run configs 2, 3 and 4 are measured into `extra.configs` (at
+(sequence, kv head) is sharded by key range over the ranks, one NCCL all-gather brings every rank
+all ranks' int64 row partials, and one kernel merges them exactly (MAX of the exponents, SUM of
+the rescaled integers) and rounds: strong scaling, the same bits at every N. In the same run configs 2, 3 and 4 are measured into `extra.configs` (at
 N > 1 sharded by (sequence, kv head) segments: every rank a contiguous share of the rows, no
 data-path collective, outputs gathered for the hash). Every config's output is hashed (SHA-256 of
 the bf16 bits in canonical row order) and compared with tests/golden/configs.json (`sha_ok`).
@@ -51,9 +51,10 @@ HOT_KERNEL = {"c2": "tc_prefill_kernel", "c3": "tc_decode_kernel", "c4": "tc_pre
               "c5": "tc_decode_kernel"}
 DEFAULT_SPLITS = {"c2": 1, "c3": 4, "c4": 1, "c5": 32}
 # our kernel launches per step: tier 1, split combine / list kernel, and the fallback tiers'
-# fixed launches (they run on device-side counts, so they launch every step); KV-sharded c5 adds
-# the rescale and finalize kernels
-LAUNCHES = {"c2": 9, "c3": 10, "c4": 11, "c5": 10, "c5-sharded": 4}
+# fixed launches (they run on device-side counts, so they launch every step); KV-sharded c5: the
+# decode kernel, the split combine (export), the gathered merge, and the fixed-capacity wide tier
+# (wide partials, rescale, finalize; empty slots)
+LAUNCHES = {"c2": 9, "c3": 10, "c4": 11, "c5": 10, "c5-sharded": 7}
 
 
 def parse():
@@ -432,7 +433,7 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
 
         def step():
             o, f = ea_dist.attention_kv_sharded(q, k, v, cfg.alpha, max_row_keys=mrk, splits=splits, stats=stats,
-                                                parts=parts, **kwl)
+                                                parts=parts, sync=False, **kwl)
             out.copy_(o)
             flags.copy_(f)
     else:
@@ -474,7 +475,7 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     rec = {
         "value": job_pairs / (ms / 1000.0), "unit": "pairs/s", "ms_per_step": ms, "job_pairs": job_pairs,
         "rows": cfg.rows, "rows_per_rank": rows, "splits": splits,
-        "parallelism": (f"kv-range shards x{world}, NCCL int64 MAX + SUM merge" if kv_sharded and world > 1 else
+        "parallelism": (f"kv-range shards x{world}, one NCCL all-gather of the int64 partials, exact merge" if kv_sharded and world > 1 else
                         f"(sequence, kv head) shards x{world}, outputs gathered for the hash" if world > 1 else
                         "1 GPU"),
         "decode_tokens_per_s": (tokens / (ms / 1000.0)) if tokens else None,

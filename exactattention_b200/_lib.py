@@ -23,7 +23,8 @@ EXPORTS = ("ea_attention_cuda", "ea_attention_cuda_ranges", "ea_round_ratio_cuda
            "ea_noalloc_last_error", "ea_partials_cuda", "ea_partials_rescale_cuda", "ea_partials_finalize_cuda",
            "ea_wide_partials_cuda", "ea_wide_partials_rescale_cuda", "ea_wide_partials_finalize_cuda",
            "ea_kernel_timing", "ea_attention_cuda_paged", "ea_kv_append_cuda", "ea_selftest_fast64",
-           "ea_merge_partials_nccl", "ea_set_test_hooks", "ea_last_host_stats")
+           "ea_merge_partials_nccl", "ea_set_test_hooks", "ea_last_host_stats",
+           "ea_partials_merge_gathered_cuda")
 WIDE_DIGITS = 48  # EA_WIDE_DIGITS
 
 
@@ -125,6 +126,9 @@ def load(path: str | None = None):
     lib.ea_selftest_fast64.restype = ctypes.c_int
     lib.ea_merge_partials_nccl.argtypes = [ctypes.POINTER(PartialsArgs), ctypes.c_int64, ctypes.c_int, P, P]
     lib.ea_merge_partials_nccl.restype = ctypes.c_int
+    lib.ea_partials_merge_gathered_cuda.argtypes = [P, ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int64,
+                                                    ctypes.c_int, P, P, P, P, P, P]
+    lib.ea_partials_merge_gathered_cuda.restype = ctypes.c_int
     lib.ea_last_host_stats.argtypes = [P]
     lib.ea_last_host_stats.restype = ctypes.c_int
     lib.ea_set_test_hooks.argtypes = [ctypes.POINTER(TestHooks)]

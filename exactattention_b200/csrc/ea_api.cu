@@ -20,6 +20,8 @@ cudaError_t launch_tier3(const Prob& P, int blocks, cudaStream_t st);
 cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t nblocks, cudaStream_t st);
 cudaError_t launch_partials_rescale(const Prob& P, const int32_t* Rg, const int32_t* NRg, cudaStream_t st);
 cudaError_t launch_partials_finalize(const Prob& P, cudaStream_t st);
+cudaError_t launch_gathered_merge(const Prob& P, const void* g, int world, int64_t stride, int* wide_rows,
+                                  int* wide_count, cudaStream_t st);
 cudaError_t launch_combine(const Prob& P, cudaStream_t st);
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st);
 cudaError_t launch_wide_rescale(const Prob& P, int n, const int64_t* gmax, cudaStream_t st);
@@ -593,6 +595,33 @@ int ea_partials_finalize_cuda(const ea_partials_t* x, int64_t rows, int dv, int6
   set_export(P, x);
   cudaError_t e = launch_partials_finalize(P, (cudaStream_t)stream);
   return e == cudaSuccess ? 0 : fail_cuda(e, "finalize");
+}
+
+int ea_partials_merge_gathered_cuda(const void* gathered, int world, int64_t rows, int dv, int64_t max_row_keys,
+                                    int fp32_out, void* out, uint8_t* flags, int32_t* wide_rows, int32_t* wide_count,
+                                    int64_t* stats, void* stream) {
+  if (!gathered || world <= 0 || rows < 0 || dv <= 0 || dv > 256 || !out || !flags || !wide_rows || !wide_count)
+    return -1;
+  if (rows == 0) return 0;
+  Workspace* w;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    w = workspace();
+    if (!w) return fail_cuda(cudaGetLastError(), "workspace");
+  }
+  Prob P;
+  memset(&P, 0, sizeof(P));
+  P.rows = rows;
+  P.dv = dv;
+  P.fp32 = fp32_out ? 1 : 0;
+  P.key_log2 = ceil_log2(max_row_keys < 2 ? 2 : max_row_keys);
+  P.FZ = 61 - P.key_log2;
+  P.out = out;
+  P.flags = flags;
+  P.stats = stats ? (unsigned long long*)stats : w->stats;
+  const int64_t stride = (int64_t)EA_PARTIALS_FLAT_BYTES(rows, dv);
+  cudaError_t e = launch_gathered_merge(P, gathered, world, stride, wide_rows, wide_count, (cudaStream_t)stream);
+  return e == cudaSuccess ? 0 : fail_cuda(e, "gathered merge");
 }
 
 // Rows grouped by kv_base: `order` lists the rows group by group (increasing kv_base, a group's

@@ -786,6 +786,142 @@ __global__ void __launch_bounds__(128) partials_finalize_kernel(Prob P) {
 }
 
 // ---------------------------------------------------------------------------
+// the one-collective KV-shard merge: every rank's partials gathered back to back, merged and
+// rounded in one kernel (warp per row)
+// ---------------------------------------------------------------------------
+// Flat layout of one rank's partials (rows, dv): int64 Z[rows], Zerr[rows], N[rows dv],
+// Nerr[rows dv], then int32 R[rows], status[rows], NR[rows dv]; stride: the padded rank size.
+template <int CPL>
+__global__ void __launch_bounds__(128) gathered_merge_kernel(Prob P, const unsigned char* g, int world,
+                                                              int64_t stride, int* wide_rows, int* wide_count) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (r >= P.rows) return;
+  const int64_t rows = P.rows;
+  const int dv = P.dv;
+  const int64_t oZe = 8 * rows, oN = 16 * rows, oNe = oN + 8 * rows * dv, oR = oNe + 8 * rows * dv;
+  const int64_t oSt = oR + 4 * rows, oNR = oSt + 4 * rows;
+  auto i64 = [&](int s, int64_t off, int64_t i) { return ((const int64_t*)(g + s * stride + off))[i]; };
+  auto i32 = [&](int s, int64_t off, int64_t i) { return ((const int32_t*)(g + s * stride + off))[i]; };
+  int status = ST_OK;
+  int32_t R = R_EMPTY, Rmin = INT32_MAX;
+  for (int s = 0; s < world; ++s) {
+    status = max(status, i32(s, oSt, r));
+    const int32_t Rs = i32(s, oR, r);
+    if (Rs != R_EMPTY) {
+      R = R == R_EMPTY ? Rs : max(R, Rs);
+      Rmin = min(Rmin, Rs);
+    }
+  }
+  // a shard far below the row's largest weights: the wide tier decides the exponent spread
+  if (status == ST_OK && R != R_EMPTY && (int64_t)R - Rmin > SPREAD_CHECK) status = ST_TIER3;
+  int64_t Z = 0;
+  uint64_t Ze = 0;
+  bool ok = true;
+  if (status == ST_OK && R != R_EMPTY) {
+    for (int s = 0; s < world; ++s) {
+      const int32_t Rs = i32(s, oR, r);
+      if (Rs == R_EMPTY) continue;
+      int64_t z = i64(s, 0, r);
+      uint64_t ze = (uint64_t)i64(s, oZe, r);
+      rescale(z, ze, R - Rs);
+      Z += z;
+      Ze += ze;
+    }
+    ok &= fits63(Z, Ze);
+  }
+  Rnd res[CPL];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    res[i] = rnd_zero();
+    const int c = lane + 32 * i;
+    if (c >= dv || status != ST_OK || R == R_EMPTY) continue;
+    int32_t NR = R_EMPTY;
+    for (int s = 0; s < world; ++s) {
+      const int32_t x = i32(s, oNR, r * dv + c);
+      if (x != R_EMPTY) NR = NR == R_EMPTY ? x : max(NR, x);
+    }
+    if (NR == R_EMPTY) continue;
+    int64_t N = 0;
+    uint64_t Ne = 0;
+    for (int s = 0; s < world; ++s) {
+      const int32_t x = i32(s, oNR, r * dv + c);
+      if (x == R_EMPTY) continue;
+      int64_t n = i64(s, oN, r * dv + c);
+      uint64_t ne = (uint64_t)i64(s, oNe, r * dv + c);
+      rescale(n, ne, NR - x);
+      N += n;
+      Ne += ne;
+    }
+    const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+    ok &= fits63(N, Ne) && certify_ratio(N, Ne, (int64_t)NR - P.FZ, Z, Ze, (int64_t)R - P.FZ, p, qmin, 127, res[i]);
+  }
+  if (status == ST_DOMAIN) {
+    for (int c = lane; c < dv; c += 32) write_out(P, r, c, rnd_zero());
+    if (lane == 0) {
+      P.flags[r] = 2;
+      stat_add(P, STAT_DOMAIN_ROWS, 1);
+    }
+    return;
+  }
+  ok = __all_sync(0xffffffffu, ok && status == ST_OK);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < dv) write_out(P, r, c, ok ? res[i] : rnd_zero());
+  }
+  if (lane == 0) {
+    P.flags[r] = ok ? 0 : 1;
+    if (!ok) stat_add(P, STAT_TIER1_UNCERT, 1);
+  }
+}
+
+// The rows flagged 1, in increasing row order (every rank must list the wide tier's rows in the
+// same order: its SUM all-reduce adds the ranks' partials slot by slot), then -1 in every unused
+// slot up to `rows`. One block; a block-wide prefix count per chunk of rows.
+__global__ void __launch_bounds__(1024) list_flagged_kernel(const uint8_t* flags, int64_t rows, int* list, int* count) {
+  __shared__ int wsum[32];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int64_t r0 = 0; r0 < rows; r0 += 1024) {
+    const int64_t r = r0 + tid;
+    const bool f = r < rows && flags[r] == 1;
+    const unsigned b = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) wsum[warp] = __popc(b);
+    __syncthreads();
+    int before = s_base;
+    for (int w = 0; w < warp; ++w) before += wsum[w];
+    if (f) list[before + __popc(b & ((1u << lane) - 1))] = (int)r;
+    __syncthreads();
+    if (tid == 0) {
+      int t = 0;
+      for (int w = 0; w < 32; ++w) t += wsum[w];
+      s_base += t;
+    }
+    __syncthreads();
+  }
+  const int n = s_base;
+  for (int64_t i = n + tid; i < rows; i += 1024) list[i] = -1;
+  if (tid == 0) *count = n;
+}
+
+cudaError_t launch_gathered_merge(const Prob& P, const void* g, int world, int64_t stride, int* wide_rows,
+                                  int* wide_count, cudaStream_t st) {
+  const unsigned gr = (unsigned)((P.rows + 3) / 4);
+  const unsigned char* gb = (const unsigned char*)g;
+  if (P.dv <= 32) gathered_merge_kernel<1><<<gr, 128, 0, st>>>(P, gb, world, stride, wide_rows, wide_count);
+  else if (P.dv <= 64) gathered_merge_kernel<2><<<gr, 128, 0, st>>>(P, gb, world, stride, wide_rows, wide_count);
+  else if (P.dv <= 128) gathered_merge_kernel<4><<<gr, 128, 0, st>>>(P, gb, world, stride, wide_rows, wide_count);
+  else gathered_merge_kernel<8><<<gr, 128, 0, st>>>(P, gb, world, stride, wide_rows, wide_count);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  list_flagged_kernel<<<1, 1024, 0, st>>>(P.flags, P.rows, wide_rows, wide_count);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // tier 3: one block per listed row, wide fixed point over every key of the row
 // ---------------------------------------------------------------------------
 // Weights: the same certified logit (exact score when the window does not decide) and the
@@ -875,6 +1011,14 @@ __global__ void __launch_bounds__(T3_THREADS) tier3_kernel(Prob P) {
       j1 = min(L, j0 + P.u_n[2]);
     } else {
       r = planned ? P.u_rows[item] : P.t3_list[item];
+      if (r < 0) {  // an unused slot of a fixed-capacity list (KV-shard wide tier): an empty partial
+        if (exporting) {
+          int64_t* b = P.w3sum + (int64_t)item * (dv + 1) * (LW + 1);
+          for (int64_t i = tid; i < (int64_t)(dv + 1) * (LW + 1); i += T3_THREADS) b[i] = 0;
+          if (tid < 4) P.w3max[(int64_t)item * 4 + tid] = tid == 3 ? ST_OK : INT64_MIN;
+        }
+        continue;  // uniform across the block
+      }
       j1 = row_len(P, r);
     }
     // q row
@@ -1166,7 +1310,7 @@ __device__ void wide_finalize_row(const Prob& P, const int64_t* base, const int6
 __global__ void __launch_bounds__(T3_THREADS) wide_finalize_kernel(Prob P, int n, const int64_t* gmax) {
   __shared__ int sOk;
   const int item = blockIdx.x;
-  if (item >= n) return;
+  if (item >= n || P.t3_list[item] < 0) return;  // (an unused slot of a fixed-capacity list)
   wide_finalize_row(P, P.w3sum + (int64_t)item * (P.dv + 1) * (LW + 1), gmax + (int64_t)item * 4, P.t3_list[item],
                     &sOk);
 }

@@ -203,16 +203,22 @@ def _launch_args(q, k, v, alpha, *, row_ptr=None, key_idx=None, kv_base=None, kv
 
 
 class Partials:
-    """Row partials of one key range (ea_partials_t), as views into two flat device buffers so
-    that a merge needs one MAX all-reduce (`i32`: R, status, NR) and one SUM all-reduce (`i64`:
-    Z, Zerr, N, Nerr)."""
+    """Row partials of one key range (ea_partials_t) in one flat buffer, the layout of
+    EA_PARTIALS_FLAT_BYTES: `i64` (Z, Zerr, N, Nerr) then `i32` (R, status, NR). The flat buffer is
+    what one all-gather moves for the merge (ea_partials_merge_gathered_cuda); the two views are
+    what the MAX / SUM all-reduce form of the merge reduces."""
 
     def __init__(self, rows: int, dv: int, device):
         import torch
 
         self.rows, self.dv = rows, dv
-        self.i32 = torch.empty(rows * (2 + dv), dtype=torch.int32, device=device)
-        self.i64 = torch.empty(rows * (2 + 2 * dv), dtype=torch.int64, device=device)
+        n64, n32 = rows * (2 + 2 * dv), rows * (2 + dv)
+        self.flat = torch.empty(n64 + (n32 + 1) // 2, dtype=torch.int64, device=device)
+        self.i64 = self.flat[:n64]
+        self.i32 = self.flat[n64:].view(torch.int32)[:n32]
+        self._gathered = None
+        self.wide_rows = torch.empty(max(1, rows), dtype=torch.int32, device=device)
+        self.wide_count = torch.zeros(1, dtype=torch.int32, device=device)
         self.R, self.status = self.i32[:rows], self.i32[rows:2 * rows]
         self.NR = self.i32[2 * rows:].view(rows, dv)
         self.Z, self.Zerr = self.i64[:rows], self.i64[rows:2 * rows]
@@ -228,6 +234,14 @@ class Partials:
 
     def numpy(self) -> dict:
         return {k: getattr(self, k).cpu().numpy() for k in ("R", "Z", "Zerr", "status", "NR", "N", "Nerr")}
+
+    def gathered(self, world: int):
+        """The receive buffer of the all-gather of `world` flat buffers (kept between calls)."""
+        import torch
+
+        if self._gathered is None or self._gathered.numel() != world * self.flat.numel():
+            self._gathered = torch.empty(world * self.flat.numel(), dtype=torch.int64, device=self.flat.device)
+        return self._gathered
 
 
 def _stream(dev, stream):
@@ -269,6 +283,24 @@ def rescale_partials(parts: Partials, R_global, NR_global, stream=None) -> None:
         _lib.check(_lib.load().ea_partials_rescale_cuda(ctypes.byref(p), R_global.data_ptr(), NR_global.data_ptr(),
                                                         parts.rows, parts.dv, ctypes.c_void_p(_stream(dev, stream))),
                    "ea_partials_rescale_cuda")
+
+
+def merge_gathered(gathered, world: int, parts: Partials, max_row_keys: int, out="bf16", stats=None, stream=None):
+    """Merge and certified rounding of `world` ranks' gathered flat partials
+    (ea_partials_merge_gathered_cuda): (out bits, flags, wide_rows, wide_count) on the device; rows
+    flagged 1 are listed in increasing order in wide_rows[:wide_count] (the same list on every
+    rank), every later slot -1, for the sharded wide tier."""
+    import torch
+
+    dev = parts.flat.device
+    o = torch.empty((parts.rows, parts.dv), dtype=torch.int32 if out == "fp32" else torch.int16, device=dev)
+    fl = torch.empty(parts.rows, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ea_partials_merge_gathered_cuda(
+            gathered.data_ptr(), world, parts.rows, parts.dv, int(max_row_keys), int(out == "fp32"), o.data_ptr(),
+            fl.data_ptr(), parts.wide_rows.data_ptr(), parts.wide_count.data_ptr(), _ptr(stats),
+            ctypes.c_void_p(_stream(dev, stream))), "ea_partials_merge_gathered_cuda")
+    return o, fl, parts.wide_rows, parts.wide_count
 
 
 def merge_partials_nccl(parts: Partials, nccl_comm: int, stream=None) -> None:

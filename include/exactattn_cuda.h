@@ -198,6 +198,25 @@ int ea_partials_rescale_cuda(const ea_partials_t* parts, const int32_t* R_global
 int ea_partials_finalize_cuda(const ea_partials_t* parts, int64_t rows, int dv, int64_t max_row_keys,
                               int fp32_out, void* out, uint8_t* flags, int64_t* stats, void* stream);
 
+/* The one-collective form of the KV-shard merge. Each rank keeps its partials in one flat buffer
+ * of EA_PARTIALS_FLAT_BYTES(rows, dv) bytes (int64 Z[rows], Zerr[rows], N[rows dv], Nerr[rows dv],
+ * then int32 R[rows], status[rows], NR[rows dv], padded to a multiple of 8 bytes; an ea_partials_t
+ * pointing into it is filled by ea_partials_cuda as usual). After an all-gather of those buffers
+ * (rank order does not matter), `gathered` holds world buffers back to back; this merges them (MAX
+ * of the exponents, every partial re-expressed at them, SUM: order-free) and rounds every row,
+ * writing out and flags on every rank alike. Rows the merged interval cannot certify get flag 1 and
+ * are listed in increasing row order in wide_rows (capacity rows; every slot past the count holds
+ * -1; the count in the device int *wide_count), the same list on every rank, for the sharded wide
+ * tier (ea_wide_partials_cuda and the following entries, which pair the ranks' partials slot by
+ * slot). Replaces
+ * ea_partials_rescale_cuda + a SUM all-reduce + ea_partials_finalize_cuda: one collective instead of
+ * two, one kernel. No reference counterpart (the reference runs on one device). */
+#define EA_PARTIALS_FLAT_BYTES(rows, dv) \
+  ((((size_t)(rows) * (16 + 16 * (size_t)(dv)) + (size_t)(rows) * (8 + 4 * (size_t)(dv))) + 7) & ~(size_t)7)
+int ea_partials_merge_gathered_cuda(const void* gathered, int world, int64_t rows, int dv, int64_t max_row_keys,
+                                    int fp32_out, void* out, uint8_t* flags, int32_t* wide_rows, int32_t* wide_count,
+                                    int64_t* stats, void* stream);
+
 /* The whole KV-shard merge of `parts` over the caller's NCCL communicator (an ncclComm_t passed
  * as void*), on `stream`: all-reduce MAX of R, status and NR, ea_partials_rescale_cuda, all-reduce
  * SUM of Z, Zerr, N and Nerr; then ea_partials_finalize_cuda gives every rank the same rows. Every
@@ -230,7 +249,9 @@ int ea_wide_partials_cuda(const ea_launch_t* args, const int32_t* rows, int n, c
 int ea_wide_partials_rescale_cuda(const ea_wide_partials_t* parts, const int64_t* merged_max, int n, int dv,
                                   void* stream);
 /* Writes out/flags of the listed rows: flag 0 certified, 2 domain error, 1 unresolved (a
- * 2^-97-probability event; counted in stats[4]). */
+ * 2^-97-probability event; counted in stats[4]). A row index below 0 in `rows` marks an unused slot
+ * of a fixed-capacity list (an empty partial, nothing written): a caller can then run these calls
+ * with a fixed n every step, without reading the wide-row count on the host. */
 int ea_wide_partials_finalize_cuda(const ea_wide_partials_t* parts, const int64_t* merged_max, const int32_t* rows,
                                    int n, int dv, int fp32_out, void* out, uint8_t* flags, int64_t* stats,
                                    void* stream);

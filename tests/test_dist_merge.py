@@ -144,3 +144,54 @@ def test_merge_single_rank_is_identity_up_to_rescale():
     before = p.i64.clone()
     sequential_merge([p])
     assert torch.equal(p.i64, before)
+
+
+def _gather_worker(rank: int, world: int, port: int, rows: int, dv: int, seeds, result_dir: str):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        p = make_parts(seeds[rank], rows, dv)
+        g, w = ea_dist.gather_partials(p)
+        assert w == world
+        np.save(os.path.join(result_dir, f"g_{rank}.npy"), g.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_is_every_flat_buffer_in_rank_order(world, tmp_path):
+    """The one-collective merge's gather: every rank holds every rank's flat partials in rank
+    order, in the flat layout (the merge kernel then reads rank s's fields at s x the flat size),
+    and merging them gives the same partials as the MAX / rescale / SUM form."""
+    import torch.multiprocessing as mp
+
+    rows, dv = 23, 8
+    seeds = [300 + r for r in range(world)]
+    mp.start_processes(_gather_worker, args=(world, _free_port(), rows, dv, seeds, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    gs = [np.load(tmp_path / f"g_{r}.npy") for r in range(world)]
+    for r in range(1, world):
+        assert np.array_equal(gs[0], gs[r])
+    flat = np.concatenate([make_parts(s, rows, dv).flat.numpy() for s in seeds])
+    assert np.array_equal(gs[0], flat)
+    # the layout: rank s's partials read back from its slice of the gathered buffer
+    n_flat = make_parts(seeds[0], rows, dv).flat.numel()
+    views = []
+    for s in range(world):
+        p = cuda.Partials(rows, dv, "cpu")
+        p.flat.copy_(torch.from_numpy(gs[0][s * n_flat:(s + 1) * n_flat]))
+        views.append(p)
+    merged = sequential_merge(views)
+    ref = sequential_merge([make_parts(s, rows, dv) for s in seeds])
+    assert np.array_equal(merged.i32.numpy(), ref.i32.numpy()) and np.array_equal(merged.i64.numpy(), ref.i64.numpy())
+
+
+def test_flat_layout_matches_header():
+    """The flat buffer's size is EA_PARTIALS_FLAT_BYTES(rows, dv) of include/exactattn_cuda.h."""
+    for rows, dv in ((1, 1), (7, 3), (64, 128), (5, 256)):
+        p = cuda.Partials(rows, dv, "cpu")
+        want = (rows * (16 + 16 * dv) + rows * (8 + 4 * dv) + 7) & ~7
+        assert p.flat.numel() * 8 == want
+        assert p.R.data_ptr() - p.flat.data_ptr() == 8 * rows * (2 + 2 * dv)

@@ -239,3 +239,59 @@ def test_spread_across_shards_is_a_domain_error():
     finish_local(shard_args, out, flags, n)
     torch.cuda.synchronize()
     assert np.array_equal(flags.cpu().numpy() == 2, sees)
+
+
+def gathered_local(parts_list):
+    """The flat buffers of in-process ranges, concatenated (what the all-gather gives every rank)."""
+    import torch
+
+    return torch.cat([p.flat for p in parts_list])
+
+
+@pytest.mark.parametrize("kind,vkind,shards,decode", [("normal", "normal", 3, False), ("outlier", "wide", 8, False),
+                                                      ("normal", "heavy", 4, True)])
+def test_gathered_merge_equals_two_collective_merge(kind, vkind, shards, decode):
+    """The one-collective merge (gather the flat partials, merge and round in one kernel) gives the
+    same bits and flags as MAX / rescale / SUM / finalize, and as one launch over all keys; the wide
+    rows it lists are exactly the ones the older form flags."""
+    import torch
+
+    import exactattention_b200 as ea
+    from exactattention_b200 import cuda
+
+    rng = np.random.default_rng(hash((kind, vkind, shards)) & 0xFFFF)
+    rows, n = (4, 4000) if decode else (12, 1500)
+    Q, K, V = bf16(rng, (rows, 128), kind), bf16(rng, (n, 128), kind), bf16(rng, (n, 128), vkind)
+    dev = torch.device("cuda")
+    alpha = ea.default_alpha(128)
+    kb = np.zeros(rows, np.int64)
+    kl = np.full(rows, n, np.int64)
+    if not decode:
+        kl[3], kl[5] = 0, 700
+    full, fflags = cuda.launch(_t(Q, dev), _t(K, dev), _t(V, dev), alpha, kv_base=_t(kb, dev), kv_len=_t(kl, dev))
+    parts, parts2, shard_args = [], [], []
+    for lo, hi in _bounds(n, shards):
+        klen = np.clip(kl - lo, 0, hi - lo).astype(np.int64)
+        m = dict(kv_base=_t(kb, dev), kv_len=_t(klen, dev))
+        if decode:
+            m.update(segments=_t(cuda.row_segments(kb), dev), segment_width=rows, splits=3)
+        shard_args.append((_t(Q, dev), _t(K[lo:hi], dev), _t(V[lo:hi], dev), alpha,
+                           {k_: v_ for k_, v_ in m.items() if k_ in ("kv_base", "kv_len")}))
+        parts.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
+        parts2.append(cuda.partials(*shard_args[-1][:4], max_row_keys=n, **m))
+    out_g, fl_g, wrows, wcount = cuda.merge_gathered(gathered_local(parts), shards, parts[0], n)
+    torch.cuda.synchronize()
+    out_m, fl_m = cuda.finalize_partials(merge_local(parts2), n)
+    torch.cuda.synchronize()
+    assert torch.equal(fl_g, fl_m)
+    wl = wrows.cpu().numpy()
+    nw = int(wcount.item())
+    # the wide tier pairs the ranks' partials slot by slot: the list is in row order, then -1
+    assert wl[:nw].tolist() == torch.nonzero(fl_m == 1).flatten().cpu().numpy().tolist()
+    assert (wl[nw:] == -1).all()
+    ok = fl_g == 0
+    assert torch.equal(out_g[ok], out_m[ok])
+    finish_local(shard_args, out_g, fl_g, n)
+    torch.cuda.synchronize()
+    assert not fl_g.any().item() and not fflags.any().item()
+    assert torch.equal(out_g, full)

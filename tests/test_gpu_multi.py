@@ -94,11 +94,12 @@ def _c5_worker(rank, world, port, result_dir):
         case = w.device_case("c5", dev, shard=rank, nshards=world)
         kw = dict(case["kw"])
         mrk = kw.pop("max_row_keys")
-        out, flags = ea_dist.attention_kv_sharded(case["q"], case["k"], case["v"], case["cfg"].alpha, max_row_keys=mrk,
-                                                  splits=64, **kw)
-        torch.cuda.synchronize(dev)
-        np.save(os.path.join(result_dir, f"c5_out_{rank}.npy"), out.cpu().numpy())
-        np.save(os.path.join(result_dir, f"c5_flags_{rank}.npy"), flags.cpu().numpy())
+        for sync in (True, False):  # host-read wide-row count / fixed-capacity wide tier, no host sync
+            out, flags = ea_dist.attention_kv_sharded(case["q"], case["k"], case["v"], case["cfg"].alpha,
+                                                      max_row_keys=mrk, splits=32, sync=sync, **kw)
+            torch.cuda.synchronize(dev)
+            np.save(os.path.join(result_dir, f"c5_out_{rank}_{int(sync)}.npy"), out.cpu().numpy())
+            np.save(os.path.join(result_dir, f"c5_flags_{rank}_{int(sync)}.npy"), flags.cpu().numpy())
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -122,9 +123,10 @@ def test_nccl_c5_sharded_sha(tmp_path):
     mp.start_processes(_c5_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
-        assert not np.load(tmp_path / f"c5_flags_{r}.npy").any()
-        out = np.load(tmp_path / f"c5_out_{r}.npy").view(np.uint16)
-        assert hashlib.sha256(np.ascontiguousarray(out).tobytes()).hexdigest() == gold, r
+        for sync in (1, 0):
+            assert not np.load(tmp_path / f"c5_flags_{r}_{sync}.npy").any()
+            out = np.load(tmp_path / f"c5_out_{r}_{sync}.npy").view(np.uint16)
+            assert hashlib.sha256(np.ascontiguousarray(out).tobytes()).hexdigest() == gold, (r, sync)
 
 
 def _raw_comm_worker(rank, world, port, result_dir):
