@@ -49,7 +49,7 @@ BF16_EQUIV_FLOPS_PER_PAIR = 512  # 4 d
 KV_BYTES_PER_KEY = 512           # bf16 K and V rows of d = 128 for one kv head, read once
 HOT_KERNEL = {"c2": "tc_prefill_kernel", "c3": "tc_decode_kernel", "c4": "tc_prefill_kernel",
               "c5": "tc_decode_kernel"}
-DEFAULT_SPLITS = {"c2": 1, "c3": 4, "c4": 1, "c5": 32}
+DEFAULT_SPLITS = {"c2": 1, "c3": 6, "c4": 1, "c5": 32}
 # our kernel launches per step: tier 1, split combine / list kernel, and the fallback tiers'
 # fixed launches (they run on device-side counts, so they launch every step); KV-sharded c5: the
 # decode kernel, the split combine (export), the gathered merge, and the fixed-capacity wide tier
@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kv-shard", default="", help="c5 on one GPU: only key range K of N (\"K/N\"), the share of "
                     "one rank of an N-GPU run (a smaller case of the same kernel, for profiling)")
+    ap.add_argument("--seqs", type=int, default=0, help="c3 / c4 on one GPU: only the first SEQS sequences (a smaller "
+                    "case of the same kernels, for profiling)")
     return ap.parse_args()
 
 
@@ -394,6 +396,16 @@ class Runner:
         return self.max(ms), (k_tot / k_n if k_n else None), k_n, rec
 
 
+def config_splits(name: str, case: dict, sms: int) -> int:
+    """KV splits of a config's rank share: c4's prefix blocks (128 rows each) are too few to fill
+    the GPU, so each takes enough KV splits for about 1.5 waves; the others use their measured
+    best (c2 1, c3 6, c5 32)."""
+    if name == "c4":
+        nb = int(case["kw"]["blocks"].shape[0])
+        return max(1, -(-3 * sms // (2 * nb)))
+    return DEFAULT_SPLITS[name]
+
+
 def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     """Measures one config on this rank (its share at N > 1); returns the config's record (rank 0
     fills in the hash check)."""
@@ -402,7 +414,6 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     from exactattention_b200 import cuda, workloads
 
     world, rank = R.world, R.rank
-    splits = (args.splits if headline and args.splits else 0) or DEFAULT_SPLITS[name]
     kv_sharded = name == "c5" and (world > 1 or bool(args.kv_shard))
     ks, kn = rank, world
     if args.kv_shard and headline:
@@ -414,11 +425,15 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     else:
         full = workloads.device_case(name, R.dev)
         r0, r1 = row_share(name, full["cfg"], rank, world)
-        case = slice_case(name, full, r0, r1) if world > 1 else full
+        if headline and args.seqs and name in ("c3", "c4") and world == 1:
+            r0, r1 = 0, args.seqs * workloads.HQ * full["cfg"].q_tokens
+        case = slice_case(name, full, r0, r1) if (r0, r1) != (0, full["cfg"].rows) else full
         del full
     cfg = case["cfg"]
     q, k, v, kw = case["q"], case["k"], case["v"], case["kw"]
     rows = q.shape[0]
+    sms = torch.cuda.get_device_properties(R.dev).multi_processor_count
+    splits = (args.splits if headline and args.splits else 0) or config_splits(name, case, sms)
     stats = cuda.new_stats(R.dev)
     cuda.reserve_workspace(rows, splits, 128)
     out = torch.empty((rows, 128), dtype=torch.int16, device=R.dev)
@@ -449,10 +464,8 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     ok = R.max(0.0 if ok_local else 1.0) == 0.0
 
     # the job's output in canonical row order, hashed on rank 0
-    if kv_sharded and not args.kv_shard:
-        full_out = out  # every rank holds every row after the merge
-    elif name == "c5":
-        full_out = out
+    if name == "c5" or (headline and args.seqs):
+        full_out = out  # c5: every rank holds every row after the merge
     else:
         full_out = R.gather_rows(out, cfg.rows)
     sha = hashlib.sha256(full_out.cpu().numpy().view(np.uint16).tobytes()).hexdigest() if rank == 0 else None
@@ -471,6 +484,9 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     kern = HOT_KERNEL[name]
     rl = roofline(alg, kernel_ms if kernel_ms else ms, peaks(), kern, k_n, profile_traffic(kern, name))
     job_pairs = cfg.pairs if not args.kv_shard else cfg.pairs // kn
+    partial_job = bool(args.kv_shard) or (headline and bool(args.seqs))
+    if headline and args.seqs:
+        job_pairs = int(cfg.row_keys()[:rows].sum())  # the first rows in canonical order
     tokens = cfg.rows if name in ("c3", "c5") else None  # decode: one query token per (sequence, q head) row
     rec = {
         "value": job_pairs / (ms / 1000.0), "unit": "pairs/s", "ms_per_step": ms, "job_pairs": job_pairs,
@@ -481,7 +497,7 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
         "decode_tokens_per_s": (tokens / (ms / 1000.0)) if tokens else None,
         "query_rows_per_s": cfg.rows / (ms / 1000.0),
         "roofline": rl,
-        "flags_all_zero": ok, "sha256": sha, "sha_ok": (sha == gold) if (rank == 0 and gold and not args.kv_shard) else None,
+        "flags_all_zero": ok, "sha256": sha, "sha_ok": (sha == gold) if (rank == 0 and gold and not partial_job) else None,
         "certified_per_step": {"tier1_uncertified_rows": int(st[2]), "tier2_uncertified_rows": int(st[9]),
                                "tier2_pairs": int(st[10]), "domain_rows": int(st[3]), "unresolved_rows": int(st[4]),
                                "waits_expired": int(st[8]), "host_fallbacks": int(st[6]),
@@ -490,7 +506,7 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
         "clocks": clk,
         "launches_per_step": LAUNCHES["c5-sharded" if kv_sharded else name],
     }
-    if headline and not args.no_e2e and not args.kv_shard:
+    if headline and not args.no_e2e and not partial_job:
         rec["e2e"] = e2e(R, name, case, splits, out, kv_sharded, job_pairs)
     del case, q, k, v, kw
     torch.cuda.empty_cache()
@@ -584,7 +600,7 @@ def main():
     name = args.config
     head = run_config(R, name, args, headline=True)
     extras = {}
-    if args.extras != "none" and not args.kv_shard:
+    if args.extras != "none" and not args.kv_shard and not args.seqs:
         for x in [s for s in args.extras.split(",") if s and s != name]:
             extras[x] = run_config(R, x, args, headline=False)
     clk = head.pop("clocks")
@@ -597,7 +613,7 @@ def main():
         return
 
     cpu = None
-    if not args.no_cpu and R.world == 1 and not args.kv_shard:
+    if not args.no_cpu and R.world == 1 and not args.kv_shard and not args.seqs:
         from oracle import ref
 
         if ref.available():
@@ -613,7 +629,8 @@ def main():
         "steps": steps_all, "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "decode_tokens_per_s": head["decode_tokens_per_s"],
-        "config": {"workload": name + (f" key range {args.kv_shard}" if args.kv_shard else ""),
+        "config": {"workload": name + (f" key range {args.kv_shard}" if args.kv_shard else "") + (
+                       f" first {args.seqs} sequences" if args.seqs else ""),
                    "job_pairs": head["job_pairs"], "rows": head["rows"],
                    "splits": head["splits"], "heads": "16q/8kv", "head_dim": 128, "keys_per_sequence": 1 << 20,
                    "l2": "flushed (256 MiB write) between steps", "parallelism": head["parallelism"],

@@ -82,6 +82,10 @@ struct Workspace {
   void* lists = nullptr;
   size_t lists_bytes = 0;
   cudaStream_t stream = nullptr;
+  // a side stream and fork / join events for work that can overlap on one launch (the tree
+  // mask's list part beside the tensor-core range part)
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 std::mutex g_mu;
@@ -105,6 +109,10 @@ Workspace* workspace(bool host = false) {
   w.device = dev;
   w.host = host;
   cudaDeviceGetAttribute(&w.sms, cudaDevAttrMultiProcessorCount, dev);
+  if (cudaStreamCreateWithFlags(&w.side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&w.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&w.join, cudaEventDisableTiming) != cudaSuccess)
+    w.side = nullptr;  // (then the list part runs on the launch stream)
   w.stats = stats;
   w.t3_count = t3_count;
   return &w;
@@ -201,6 +209,9 @@ void ea_cuda_release(void) {
     if (w.lists) cudaFree(w.lists);
     if (w.lists_h) cudaFreeHost(w.lists_h);
     if (w.stream) cudaStreamDestroy(w.stream);
+    if (w.side) cudaStreamDestroy(w.side);
+    if (w.fork) cudaEventDestroy(w.fork);
+    if (w.join) cudaEventDestroy(w.join);
   }
   g_ws.clear();
   cudaSetDevice(cur);
@@ -397,10 +408,13 @@ static void export_to_split(Prob& X, const Prob& P, int s) {
   X.xNe = P.pNe + o * P.dv;
 }
 
+// The range part runs in a0->splits KV splits on the tensor cores (split slots 0 .. S - 1), the
+// per-row lists on the CUDA cores (slot S); one exact combine merges the S + 1 slots.
 static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st) {
+  const int S = a0->splits;
   ea_launch_t a = *a0;
-  a.splits = 2;
-  int rc = reserve(w, a.rows, 2, a.dv);
+  a.splits = S + 1;
+  int rc = reserve(w, a.rows, S + 1, a.dv);
   if (rc) return rc;
   Prob P;
   build_prob(&a, w, P);
@@ -408,17 +422,26 @@ static int launch_hybrid_tc(const ea_launch_t* a0, Workspace* w, cudaStream_t st
   if (e != cudaSuccess) return fail_cuda(e, "memset");
   Prob P0 = P;
   P0.kind = MASK_RANGE;
-  export_to_split(P0, P, 0);
+  if (S == 1)
+    export_to_split(P0, P, 0);
+  else
+    P0.splits = S;  // the kernel's grid.y: split y writes split slot y
+  // the list part (its own split slot) runs beside the range part, on the side stream
+  Prob P1 = P;
+  P1.kind = MASK_CSR;
+  export_to_split(P1, P, S);
+  cudaStream_t ls = st;
+  if (w->side && cudaEventRecord(w->fork, st) == cudaSuccess && cudaStreamWaitEvent(w->side, w->fork, 0) == cudaSuccess)
+    ls = w->side;
+  e = launch_simt(P1, ls);
+  if (e != cudaSuccess) return fail_cuda(e, "tier-1 list launch");
+  if (ls != st && ((e = cudaEventRecord(w->join, ls)) != cudaSuccess)) return fail_cuda(e, "join");
   {
     TimedLaunch tl(st);
     e = launch_tc_prefill(P0, a.block_rows, a.nblocks, st);
   }
   if (e != cudaSuccess) return fail_cuda(e, "tier-1 range launch");
-  Prob P1 = P;
-  P1.kind = MASK_CSR;
-  export_to_split(P1, P, 1);
-  e = launch_simt(P1, st);
-  if (e != cudaSuccess) return fail_cuda(e, "tier-1 list launch");
+  if (ls != st && (e = cudaStreamWaitEvent(st, w->join, 0)) != cudaSuccess) return fail_cuda(e, "join");
   e = launch_combine(P, st);
   if (e != cudaSuccess) return fail_cuda(e, "combine");
   e = launch_fallback(P, fallback_bufs(w, a.dv), w->sms, st);
