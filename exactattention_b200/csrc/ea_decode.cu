@@ -124,7 +124,7 @@ __device__ __forceinline__ int64_t run_start(const Prob& P, int32_t row0, int64_
 // kv_base, read once per CTA). PAGED: one run per page touched, run r issued by lane r % 32, each
 // lane reading its own page-table entry (or taking it from page_pref, read a tile ahead), so the
 // lookups overlap instead of chaining.
-__device__ void fetch_rows(const Prob& P, const uint16_t* src, int32_t row0, int64_t kvbase, int64_t j0, int n,
+__device__ __forceinline__ void fetch_rows(const Prob& P, const uint16_t* src, int32_t row0, int64_t kvbase, int64_t j0, int n,
                            uint8_t* raw, uint64_t* bar, int64_t page_pref = -1) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) tc::mbar_arrive_expect_tx(bar, (uint32_t)n * D * 2u);
@@ -811,7 +811,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             int64_t run;
             const int64_t kr = run_start(P, row0, j0 + key, run);
             Rnd t = rnd_zero();
-            const int ls = warp_exact_logit(P, S.rows[g], kr, t);
+            const int ls = warp_exact_logit(P.q, P.k, P.am, P.ae, S.rows[g], kr, t);
             if (lane == 0) {
               if (ls == LOGIT_OK) {
                 sT[ee] = rnd_to_f32_bits(t);

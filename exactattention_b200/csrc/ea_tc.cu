@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const int ee = warp + NWARPS * (32 * it + src);
           const int pr = ee >> 6, pk = ee & 63;
           Rnd t = rnd_zero();
-          const int ls = warp_exact_logit(P, S.rows[pr], base + j0 + pk, t);
+          const int ls = warp_exact_logit(P.q, P.k, P.am, P.ae, S.rows[pr], base + j0 + pk, t);
           if (lane == 0) {
             if (ls == LOGIT_OK) {
               sT[pr * T_PITCH + pk] = rnd_to_f32_bits(t);

@@ -190,7 +190,10 @@ static __device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_
 // Exact logit of q row `qrow` and k row `krow`, by the whole warp; every lane returns it.
 // Products q_i k_i = m 2^e (|m| < 2^16) summed exactly in a 128-bit window whose unit is 118
 // bits below the largest product bound; if some product falls below the window, 576-bit bins.
-static __device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow, int64_t krow, Rnd& t) {
+// (Plain arguments, not the kernel's Prob: taking the parameter struct's address would make every
+// thread keep a copy of it in local memory.)
+static __device__ __noinline__ int warp_exact_logit(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
+                                                    int32_t am, int32_t ae, int64_t qrow, int64_t krow, Rnd& t) {
   const int lane = threadIdx.x & 31;
   int32_t pm[4], pe[4];
   int emax = INT32_MIN;
@@ -198,8 +201,8 @@ static __device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow,
   for (int m4 = 0; m4 < 4; ++m4) {
     const int i = lane + 32 * m4;
     int32_t qm, qe, km, ke;
-    decode_bf16(P.q[qrow * 128 + i], qm, qe);
-    decode_bf16(P.k[krow * 128 + i], km, ke);
+    decode_bf16(q[qrow * 128 + i], qm, qe);
+    decode_bf16(k[krow * 128 + i], km, ke);
     pm[m4] = qm * km;
     pe[m4] = qe + ke;
     if (pm[m4]) emax = max(emax, pe[m4] + 16);
@@ -232,7 +235,7 @@ static __device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow,
       hi = hi + hi2 + (sum < lo ? 1 : 0);
       lo = sum;
     }
-    ls = logit_i128((i128)(((u128)(uint64_t)hi << 64) | lo), unit, P.am, P.ae, t);
+    ls = logit_i128((i128)(((u128)(uint64_t)hi << 64) | lo), unit, am, ae, t);
   } else {
     ExactScore sc;
     score_clear(sc);
@@ -243,7 +246,7 @@ static __device__ __noinline__ int warp_exact_logit(const Prob& P, int64_t qrow,
     for (int b = 0; b < SCORE_BINS; ++b)
 #pragma unroll
       for (int o = 16; o; o >>= 1) sc.bins[b] += __shfl_xor_sync(0xffffffffu, sc.bins[b], o);
-    ls = logit_exact(sc, P.am, P.ae, t);
+    ls = logit_exact(sc, am, ae, t);
   }
   return ls;
 }
