@@ -291,6 +291,7 @@ static void build_prob(const ea_launch_t* a, Workspace* w, Prob& P) {
   P.seq_lens = a->seq_lens;
   P.page_size = a->page_size;
   P.max_pages = a->max_pages;
+  P.krows = a->nkeys;
   P.hq = a->q_heads;
   P.hkv = a->kv_heads;
   P.group = a->kv_heads > 0 ? a->q_heads / a->kv_heads : 1;

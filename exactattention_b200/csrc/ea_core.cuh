@@ -63,6 +63,7 @@ struct Prob {
   const int32_t* page_table;
   const int32_t* seq_lens;
   int page_size, max_pages, hq, group, hkv;
+  int64_t krows;  // rows of the K (and V) tensor: keys (CSR / RANGE) or pages x kv heads x page size
   // schedule / headroom
   int splits;
   int key_log2;

@@ -3,27 +3,46 @@
 //
 // The prefill kernel puts 128 query rows on the MMA's M side; a decode group has 1-8 rows, so
 // here the KEYS take the M side and the rows' digits go to N:
-//   scores   S^T[key, (g, s)] = K_t . Q_s for key digit planes t (A, 128 keys x 128 dims) against
-//            one B tile holding every row's 4 query digit planes (N = 32 = 8 rows x 4 digits).
-//            Query digits are balanced (signed bytes) so one B tile has one signedness.
-//   P.V      O^T[c, (g, w)] = V_u . W_w for value digit planes u (A, 128 channels x 128 keys)
-//            against one B tile of every row's 6 weight digit planes (N = 48); values in a 31-bit
-//            window against the channel's running maximum, 4 digits.
+//   scores   S^T[key, (g, s)] = K_t . Q_s for key digit planes t (A, 128 keys x 128 dims, held in
+//            TENSOR MEMORY: key r in TMEM lane r) against one B tile holding every row's 4 query
+//            digit planes (N = 4 x rows). Query digits are balanced (signed bytes) so one B tile
+//            has one signedness.
+//   P.V      O^T[c, (g, w)] = V_u . W_w for value digit planes u (A, 128 channels x 128 keys, in
+//            shared memory) against one B tile of every row's 6 weight digit planes (N = 6 x
+//            rows); values in a 30-bit window against the channel's running maximum, as four
+//            unsigned digits of x + 2^30 (a low byte and three OFFSET-BINARY bytes), the offset
+//            removed exactly with the tile's weight sum.
 // Digit products are grouped by digit position on the CUDA cores (int32 sums) and recombined
-// exactly in int64, with the same fixed-point windows, bounds and certification as the prefill
-// kernel. Each CTA takes one (segment, split): the split's 128-key tiles arrive by bulk copies
-// (cp.async.bulk, completing on an mbarrier) into a raw staging buffer one tile ahead of the
-// slicing. Every CTA writes its rows' split partials; the split combine merges them (any split
-// count gives the same bits) and sends uncertified rows to tier 3.
+// exactly in int64 / int128, with the same fixed-point windows, bounds and certification as the
+// prefill kernel. Each CTA takes one (segment, split): the split's 128-key tiles arrive by bulk
+// copies (cp.async.bulk, completing on mbarriers) into two raw staging buffers per tensor, so
+// the copies of tile i + 1 land while tile i is sliced. Every CTA writes its rows' split
+// partials; the split combine merges them (any split count gives the same bits).
 //
-// Thread roles (512 threads, warp-specialised): warps 8-15 (producers) turn the raw tiles into
-// digit planes, issue the score MMAs and the next tiles' bulk copies; warps 0-7 (consumers, the
-// TMEM lane quadrant = warp % 4) compute logits, weights and W digits, issue the P.V MMAs, and keep
-// the running sums (pass 1 / pass 2: lane = key; drain: lane = channel; rows g = warp / 4 + 2 i).
-// The slicing of tile i + 1 overlaps the epilogue of tile i; mbarriers carry the hand-offs (raw
-// K / V landed, score MMAs done, pass 1 done, value digits ready, P.V done) and every wait is
-// bounded.
+// Thread roles (512 threads, warp-specialised, one warp of each producer role per SM sub-
+// partition so the roles overlap):
+//   warps 8-11 (K producers): one key per thread, which is also the key's TMEM lane. The raw K
+//     tile arrives through a 2D TMA tensor map as two 64-dimension halves of 128-byte rows with
+//     the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), so the 32 threads of
+//     a warp read 32 rows without bank conflicts (page sizes that do not tile 128 keys take dense
+//     bulk copies instead). Each thread turns its key into 4 digit planes (27-bit two's complement window,
+//     exact through fp32), stores them into tensor memory and its warp's lane 0 issues the score
+//     MMAs of one key digit plane (A from TMEM, B = the query digits in shared memory). It also
+//     keeps the key's fixed-point values at the few dimensions where some query row lost bits
+//     (the consumers' error bound), so the raw rows are free once sliced and the next tiles'
+//     copies run two tiles ahead.
+//   warps 12-15 (V producers): 4 channels x 32 keys per thread; value digits by round-toward-zero
+//     fused multiply-adds (the scale and the conversion to offset-binary integer bits in one
+//     instruction: one for the high three bytes, one on a clamped copy for the low byte, which
+//     only values at the bottom of the window have).
+//   warps 0-7 (consumers, the TMEM lane quadrant = warp % 4): logits, weights and W digits, the
+//     P.V MMAs (lane 0 of warp u issues value digit plane u), the running sums (pass 1 / pass 2:
+//     lane = key; drain: lane = channel; rows g = warp / 4 + 2 i).
+// mbarriers carry the hand-offs (raw K / V landed per buffer, score MMAs done, pass 1 done, value
+// digits ready, P.V done) and every wait is bounded.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 
 #include "ea_core.cuh"
@@ -33,6 +52,8 @@
 #include "ea_tc_common.cuh"
 #include "ea_tcgen05.cuh"
 
+#include <cstring>
+
 namespace ea {
 namespace tcd {
 
@@ -40,48 +61,85 @@ using namespace tcc;
 
 #ifdef EA_PHASE_TIMERS
 __device__ unsigned long long g_phase_cycles[16];
+// the counters live in the dynamic shared memory (no static shared memory moves its base)
+#undef EA_PT_DECL
+#define EA_PT_DECL                    \
+  unsigned long long* ea_pt_acc = S.pt_acc; \
+  if (threadIdx.x < 16) ea_pt_acc[threadIdx.x] = 0;
+// K producers (thread 256) keep counters 8-11, V producers (thread 384) counters 12-15
+#define EA_PTK_INIT long long ptk_last = clock64();
+#define EA_PTK(i)                          \
+  if (tid == 256) {                        \
+    const long long pt_now = clock64();    \
+    ea_pt_acc[8 + (i)] += pt_now - ptk_last; \
+    ptk_last = pt_now;                     \
+  }
+#define EA_PTV_INIT long long ptv_last = clock64();
+#define EA_PTV(i)                           \
+  if (tid == 384) {                         \
+    const long long pt_now = clock64();     \
+    ea_pt_acc[12 + (i)] += pt_now - ptv_last; \
+    ptv_last = pt_now;                      \
+  }
+#define EA_PT_FLUSH_RANGE(who, lo, hi) \
+  if (tid == (who))                    \
+    for (int i = (lo); i < (hi); ++i) atomicAdd(&g_phase_cycles[i], ea_pt_acc[i]);
+#else
+#define EA_PTK_INIT
+#define EA_PTK(i)
+#define EA_PTV_INIT
+#define EA_PTV(i)
+#define EA_PT_FLUSH_RANGE(who, lo, hi)
 #endif
 
 constexpr int BK = 128, D = 128, DV = 128, GD = 8;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
-constexpr int FW = 48, FV = 31;  // V: 31-bit window, 4 digits (few values fall below it)
-constexpr int THREADS = 512, NWARPS = THREADS / 32;
-constexpr int NWGC = 2;         // consumer warpgroups (warps 0-7); warps 8-15 are the producers
+constexpr int FW = 48, FV = 30;  // V: 30-bit window, 4 digits (very few values fall below it)
+constexpr float V_MAGIC = 12582912.0f;  // 1.5 x 2^23: y + V_MAGIC has y + 2^22 in its low 23 bits
+constexpr int THREADS = 512;
+constexpr int KW0 = 8, VW0 = 12;  // first K / V producer warp
+constexpr int NWGC = 2;           // consumer warpgroups (warps 0-7)
 constexpr int RPT_MAX = GD / NWGC;  // row slots per consumer thread for a full segment of GD rows
-constexpr uint32_t VLCAP = 4;
+constexpr uint32_t VLCAP = 2;
+constexpr int NQL = 4;  // dimensions whose k values the K producers keep for the consumers' bound
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
 constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
-constexpr uint32_t COL_O = 128;  // P.V accumulators: COL_O + 48 u + n (scores: 32 t + n)
+// TMEM columns: K digit planes (A of the scores; plane t at COL_K + 32 t, 4 bytes a column),
+// score accumulators (plane t at COL_S + 32 t + n), P.V accumulators (plane u at COL_O + 48 u + n)
+constexpr uint32_t COL_K = 0, COL_S = 128, COL_O = 256;
+static_assert(COL_O + NV * NSW <= TMEM_COLS, "tensor memory budget");
 
-constexpr uint32_t RAW_K = BK * D * 2;  // 32768
-constexpr uint32_t K_PLANE = BK * D;    // 16384
-constexpr uint32_t V_PLANE = DV * BK;   // 16384
+constexpr uint32_t RAWK_BUF = BK * D * 2;   // 32768: two swizzled halves of 128 x 128 bytes, or 128 dense rows
+constexpr uint32_t KHALF = BK * 128;         // 16384
+constexpr uint32_t RAWV_BUF = BK * DV * 2;   // 32768
+constexpr uint32_t V_PLANE = DV * BK;            // 16384
 constexpr uint32_t OFF_RAWK = 0;
-constexpr uint32_t OFF_RAWV = OFF_RAWK + RAW_K;
-constexpr uint32_t OFF_K = OFF_RAWV + RAW_K;
-constexpr uint32_t OFF_V = OFF_K + NK * K_PLANE;
+constexpr uint32_t OFF_RAWV = OFF_RAWK + 2 * RAWK_BUF;
+constexpr uint32_t OFF_V = OFF_RAWV + 2 * RAWV_BUF;
 constexpr uint32_t OFF_Q = OFF_V + NV * V_PLANE;
 constexpr uint32_t OFF_W = OFF_Q + NSQ * D;
 constexpr uint32_t OFF_T = OFF_W + NSW * BK;
 constexpr uint32_t OFF_SMALL = OFF_T + GD * BK * 4;
 
 struct Small {
-  uint32_t klossy[BK][4];
-  int32_t klsb[BK];
-  int32_t kbad[BK];
-  // value metadata of the last two tiles (by tile parity): the producers write tile i + 1's while
-  // the consumers still read tile i's
-  uint32_t vlmask[2][DV][4];  // keys whose value in channel c lost bits in the V window
-  // per channel, up to VLCAP values that lost bits in the V window, with their lost parts (units
-  // 2^(lsb_c - 24)), added back exactly in the drain: (key | still-lossy << 8), part
+  // key metadata by tile parity (the K producers write tile i + 1's while the consumers read i's)
+  uint32_t klossy[2][BK][4];
+  int32_t kqv[2][BK][NQL];  // fixed-point k at the listed dimensions where some q row is lossy
+  int16_t klsb[2][BK];
+  uint8_t kbad[2][BK];
+  // value metadata of the last two tiles (by tile parity): per channel, up to VLCAP values that
+  // lost bits in the V window, with their lost parts (units 2^(lsb_c - 24), floored, >= 0), added
+  // back exactly in the drain: (key | still-lossy << 8), part
   uint32_t vl_n[2][DV];
-  uint16_t vl_k[2][DV][4];
-  int32_t vl_dx[2][DV][4];
+  uint16_t vl_k[2][DV][VLCAP];
+  int32_t vl_dx[2][DV][VLCAP];
   int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
-  int16_t ve4[4][DV];  // per key quarter maxima of the current tile (INT16_MIN: none)
-  uint64_t td[256];  // binary64 2^(j/256) of the fast weight path
+  int16_t ve4[2][DV];  // per key half maxima of the current tile (INT16_MIN: none)
+  uint64_t td[256];    // binary64 2^(j/256) of the fast weight path
+  int32_t qlk[NQL];    // the dimensions where some query row of the segment lost bits, ascending
+  int32_t nqlk;        // their number, or -1 when there are more than NQL
   int32_t rows[GD];
   int32_t len[GD];
   int32_t qlsb[GD];
@@ -91,11 +149,14 @@ struct Small {
   int32_t rtlo[4][GD];  // lowest floor(t) per lane quadrant (the exponent-spread check)
   uint64_t zs[4][GD];
   uint32_t zl[4][GD];
-  // producer -> consumer: raw K / V tiles landed (bulk copies), score MMAs done, value digits
-  // ready; consumer -> producer: pass 1 done, P.V MMAs done
-  uint64_t bar_rk, bar_rv, bar_smma, bar_vready, bar_p1, bar_pv;
-  int32_t abort;  // a bounded wait gave up in either role
+  // raw K / V tiles landed (per buffer); score MMAs done; pass 1 done; value digits and channel
+  // data ready; P.V MMAs done
+  uint64_t bar_rk[2], bar_rv[2], bar_smma, bar_p1, bar_vready, bar_pv;
+  int32_t abort;  // a bounded wait gave up in some role
   uint32_t tmem;
+#ifdef EA_PHASE_TIMERS
+  unsigned long long pt_acc[16];
+#endif
   int32_t nrows;
   int32_t maxlen;
   int32_t row0;
@@ -103,7 +164,11 @@ struct Small {
 
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-static_assert(OFF_K % 1024 == 0 && OFF_Q % 16 == 0 && OFF_W % 16 == 0, "operand alignment");
+static_assert(OFF_V % 1024 == 0 && OFF_Q % 16 == 0 && OFF_W % 16 == 0 && OFF_RAWV % 1024 == 0, "operand alignment");
+// K fetch modes: 0 dense bulk copies of contiguous runs; 1 RANGE through the tensor map (one box
+// of 128 rows per half); 2 PAGED through the tensor map (boxes of `kbox` rows, a page or a
+// 128-row part of one; tiles start on page boundaries)
+constexpr int KM_DENSE = 0, KM_RANGE = 1, KM_PAGED = 2;
 
 // first K/V row and the number of contiguous rows from the segment's key j on (RANGE: the rest
 // of the range; PAGED: the rest of the page)
@@ -119,13 +184,13 @@ __device__ __forceinline__ int64_t run_start(const Prob& P, int32_t row0, int64_
   return (page * P.hkv + kvh) * P.page_size + (j % P.page_size);
 }
 
-// One warp: bulk copies of keys [j0, j0 + n) of `src` (K or V, 128 bf16 per row) into the raw
-// tile `raw`; lane 0 arms the barrier. RANGE: one contiguous run from `kvbase` (the segment's
-// kv_base, read once per CTA). PAGED: one run per page touched, run r issued by lane r % 32, each
-// lane reading its own page-table entry (or taking it from page_pref, read a tile ahead), so the
-// lookups overlap instead of chaining.
-__device__ __forceinline__ void fetch_rows(const Prob& P, const uint16_t* src, int32_t row0, int64_t kvbase, int64_t j0, int n,
-                           uint8_t* raw, uint64_t* bar, int64_t page_pref = -1) {
+// One warp: bulk copies of keys [j0, j0 + n) of V (128 bf16 per row) into the dense raw tile
+// `raw`; lane 0 arms the barrier. RANGE: one contiguous run from `kvbase` (the segment's kv_base,
+// read once per CTA). PAGED: one run per page touched, run r issued by lane r % 32, each lane
+// reading its own page-table entry (or taking it from page_pref, read ahead), so the lookups
+// overlap instead of chaining.
+__device__ __forceinline__ void fetch_rows(const Prob& P, const uint16_t* src, int32_t row0, int64_t kvbase,
+                                           int64_t j0, int n, uint8_t* raw, uint64_t* bar, int64_t page_pref = -1) {
   const int lane = threadIdx.x & 31;
   if (lane == 0) tc::mbar_arrive_expect_tx(bar, (uint32_t)n * D * 2u);
   __syncwarp();
@@ -155,32 +220,74 @@ __device__ __forceinline__ int64_t page_ahead(const Prob& P, int32_t row0, int64
   return pg <= plast ? (int64_t)P.page_table[(int64_t)(row0 / P.hq) * P.max_pages + pg] : -1;
 }
 
-// Named barrier over one warpgroup pair (256 threads) with an AND vote.
-__device__ __forceinline__ bool group_sync_and(int id, bool p) {
+// The page-table entry of box `lane` of the K tile at j0 (KM_PAGED; -1 when the box lies past kend)
+__device__ __forceinline__ int64_t kbox_page(const Prob& P, int32_t row0, int64_t j0, int64_t kend, int kbox) {
+  const int64_t j = j0 + (int64_t)(threadIdx.x & 31) * kbox;
+  if (j >= kend || j >= j0 + BK) return -1;
+  return (int64_t)P.page_table[(int64_t)(row0 / P.hq) * P.max_pages + j / P.page_size];
+}
+
+// One warp: the K rows of keys [j0, j0 + n) into raw tile `raw`; lane 0 arms the barrier.
+// KM_RANGE / KM_PAGED: 2D tensor-map boxes into the two swizzled halves (a box's rows land at its
+// tile rows, so each 8-row group starts on a 1024-byte boundary); `pref`: kbox_page of this
+// lane's box. KM_DENSE: contiguous runs into 256-byte rows (fetch_rows; `pref` its page_ahead).
+__device__ __forceinline__ void fetch_k(const Prob& P, const CUtensorMap* tm, int kmode, int kbox, int32_t row0,
+                                        int64_t kvbase, int64_t j0, int n, uint8_t* raw, uint64_t* bar, int64_t pref) {
+  const int lane = threadIdx.x & 31;
+  if (kmode == KM_RANGE) {
+    if (lane == 0) {
+      tc::mbar_arrive_expect_tx(bar, 2u * KHALF);
+      const int y = (int)(kvbase + j0);
+      tc::tma_load_2d(raw, tm, 0, y, bar);
+      tc::tma_load_2d(raw + KHALF, tm, 64, y, bar);
+    }
+    return;
+  }
+  if (kmode == KM_PAGED) {
+    const int nbox = (n + kbox - 1) / kbox;
+    if (lane == 0) tc::mbar_arrive_expect_tx(bar, (uint32_t)nbox * 2u * (uint32_t)kbox * 128u);
+    __syncwarp();
+    if (lane < nbox) {
+      const int64_t b = row0 / P.hq;
+      const int kvh = (int)(row0 - b * P.hq) / P.group;
+      const int64_t j = j0 + (int64_t)lane * kbox;
+      const int y = (int)((pref * P.hkv + kvh) * P.page_size + j % P.page_size);
+      tc::tma_load_2d(raw + lane * kbox * 128, tm, 0, y, bar);
+      tc::tma_load_2d(raw + KHALF + lane * kbox * 128, tm, 64, y, bar);
+    }
+    return;
+  }
+  fetch_rows(P, P.k, row0, kvbase, j0, n, raw, bar, pref);
+}
+
+// Named barrier over `n` threads with an AND / OR vote.
+__device__ __forceinline__ bool group_sync_and(int id, int n, bool p) {
   int r;
   asm volatile(
       "{\n\t.reg .pred q, rr;\n\t"
       "setp.ne.s32 q, %1, 0;\n\t"
-      "bar.red.and.pred rr, %2, 256, q;\n\t"
+      "bar.red.and.pred rr, %2, %3, q;\n\t"
       "selp.s32 %0, 1, 0, rr;\n\t}\n"
       : "=r"(r)
-      : "r"((int)p), "r"(id)
+      : "r"((int)p), "r"(id), "r"(n)
       : "memory");
   return r != 0;
 }
-__device__ __forceinline__ bool group_sync_or(int id, bool p) {
+__device__ __forceinline__ bool group_sync_or(int id, int n, bool p) {
   int r;
   asm volatile(
       "{\n\t.reg .pred q, rr;\n\t"
       "setp.ne.s32 q, %1, 0;\n\t"
-      "bar.red.or.pred rr, %2, 256, q;\n\t"
+      "bar.red.or.pred rr, %2, %3, q;\n\t"
       "selp.s32 %0, 1, 0, rr;\n\t}\n"
       : "=r"(r)
-      : "r"((int)p), "r"(id)
+      : "r"((int)p), "r"(id), "r"(n)
       : "memory");
   return r != 0;
 }
-__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+__device__ __forceinline__ void group_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// named barriers: 1 consumers (256 threads), 2 K producers (128), 3 V producers (128)
+constexpr int BAR_C = 1, BAR_K = 2, BAR_V = 3;
 
 // an mbarrier arrival by one thread
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -200,25 +307,36 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
 }
 
-// The part of bf16 `bits` that truncation toward zero to a multiple of 2^lsb dropped, in units
-// 2^(lsb - 24), itself truncated toward zero (< 2^24); `lost2` when bits remain below that unit.
+// The part of bf16 `bits` (value v) that FLOORING v 2^-lsb to an integer dropped, v 2^-lsb -
+// floor(v 2^-lsb) in [0, 1), in units 2^-24, itself floored (< 2^24); `lost2` when bits remain
+// below that unit.
 __device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost2) {
   int32_t m, e;
   decode_bf16(bits, m, e);
   lost2 = 0;
   const uint32_t mag = (uint32_t)(m < 0 ? -m : m);
-  const int s = lsb - e;  // the kept part is mag >> s
-  if (s <= 0) return 0;
-  const uint32_t low = s >= 31 ? mag : (mag & ((1u << s) - 1));  // units 2^e, < 2^9
-  uint32_t dx;
-  if (s <= 24) {
-    dx = low << (24 - s);
-  } else {
-    const int r = s - 24;
-    dx = r >= 32 ? 0u : (low >> r);
-    lost2 = r >= 32 ? (low != 0) : ((dx << r) != low);
+  const int s = lsb - e;  // the bits of mag below the unit 2^lsb
+  if (s <= 0 || mag == 0) return 0;
+  const uint32_t low = s >= 32 ? mag : (mag & ((1u << s) - 1));  // units 2^e, < 2^9
+  if (low == 0) return 0;
+  // the dropped fraction is low / 2^s for v >= 0 and 1 - low / 2^s for v < 0
+  if (s <= 24) return (int32_t)((m < 0 ? (1u << s) - low : low) << (24 - s));
+  const int r = s - 24;
+  if (m >= 0) {
+    if (r >= 32) {
+      lost2 = 1;
+      return 0;
+    }
+    const uint32_t dx = low >> r;
+    lost2 = (dx << r) != low;
+    return (int32_t)dx;
   }
-  return m < 0 ? -(int32_t)dx : (int32_t)dx;
+  // floor((2^s - low) / 2^r) = 2^24 - ceil(low / 2^r); a remainder iff low is not a multiple of 2^r
+  lost2 = 1;
+  if (r >= 32) return (1 << 24) - 1;
+  const uint64_t rm = ((uint64_t)1 << r) - 1;
+  lost2 = (low & rm) != 0;
+  return (int32_t)((1u << 24) - (uint32_t)(((uint64_t)low + rm) >> r));
 }
 
 // q row g's fixed-point element i from its balanced digit planes in the score B tile
@@ -235,14 +353,25 @@ __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
   return x;
 }
 
+// bytes 0, 1, 2 of four words as three words (byte k of word j -> byte j of output k)
+__device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
+                                           uint32_t& p1, uint32_t& p2) {
+  const uint32_t a = __byte_perm(x0, x1, 0x5140), c = __byte_perm(x2, x3, 0x5140);
+  const uint32_t b = __byte_perm(x0, x1, 0x7362), d = __byte_perm(x2, x3, 0x7362);
+  p0 = __byte_perm(a, c, 0x5410);
+  p1 = __byte_perm(a, c, 0x7632);
+  p2 = __byte_perm(b, d, 0x5410);
+}
+
 // RPT: row slots per consumer thread (rows h, h + NWGC, ..): segments of at most NWGC RPT rows.
 // A smaller RPT keeps fewer running sums in registers (GQA groups of 2 need one slot).
 template <int RPT>
-__global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows) {
+__global__ void __launch_bounds__(THREADS, 1)
+    tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows, const __grid_constant__ CUtensorMap tmk, int kmode,
+                     int kbox) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* rawk = smem + OFF_RAWK;
   uint8_t* rawv = smem + OFF_RAWV;
-  uint8_t* sK = smem + OFF_K;
   uint8_t* sV = smem + OFF_V;
   uint8_t* sQ = smem + OFF_Q;
   uint8_t* sW = smem + OFF_W;
@@ -252,6 +381,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int seg = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
+  // the swizzled tensor-map boxes land on 1024-byte boundaries of the shared window
+  if (tc::smem_u32(smem) & 1023u) kmode = KM_DENSE;
 
   // ---------------- segment rows and this split's key range ----------------
   if (tid < GD) {
@@ -270,8 +401,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
   if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
-    tc::mbar_init(&S.bar_rk, 1);
-    tc::mbar_init(&S.bar_rv, 1);
+    tc::mbar_init(&S.bar_rk[0], 1);
+    tc::mbar_init(&S.bar_rk[1], 1);
+    tc::mbar_init(&S.bar_rv[0], 1);
+    tc::mbar_init(&S.bar_rv[1], 1);
     tc::mbar_init(&S.bar_smma, NK);  // one commit per key digit's issuer
     tc::mbar_init(&S.bar_pv, NV);    // one commit per value digit's issuer
     tc::mbar_init(&S.bar_p1, 1);
@@ -318,15 +451,29 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   }
   const int32_t row0 = S.row0;  // the segment's rows share their keys: address them through this one
   const int64_t maxlen = S.maxlen;
-  const int64_t kbeg = maxlen * split / nsplit, kend = maxlen * (split + 1) / nsplit;
+  // split s covers keys [kbeg, kend): cut points rounded down to whole 128-key tiles, so tiles of
+  // a paged sequence start on page boundaries (any split layout gives the same bits)
+  const int64_t kbeg = (maxlen * split / nsplit) & ~(int64_t)(BK - 1);
+  const int64_t kend = split + 1 == nsplit ? maxlen : ((maxlen * (split + 1) / nsplit) & ~(int64_t)(BK - 1));
   const int ntiles = (int)((kend - kbeg + BK - 1) / BK);
   const int64_t kvbase = P.kind == MASK_RANGE ? P.kv_base[row0] : 0;
+  // MMA N sizes for this segment's rows (4 query digits and 6 weight digits a row)
+  const int nsq = nrows <= 2 ? 8 : nrows <= 4 ? 16 : 32;
+  const int npv = nrows <= 2 ? 16 : nrows <= 4 ? 32 : 48;
   if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
-  // the first tile's K (warp 15) and V (warp 14) fetches
-  if (warp == NWARPS - 1 && ntiles > 0)
-    fetch_rows(P, P.k, row0, kvbase, kbeg, (int)min((int64_t)BK, kend - kbeg), rawk, &S.bar_rk);
-  if (warp == NWARPS - 2 && ntiles > 0)
-    fetch_rows(P, P.v, row0, kvbase, kbeg, (int)min((int64_t)BK, kend - kbeg), rawv, &S.bar_rv);
+  // the first two tiles' K (warp 11) and V (warp 15) fetches
+  if (warp == KW0 + 3)
+    for (int t = 0; t < 2 && t < ntiles; ++t) {
+      const int64_t j0 = kbeg + (int64_t)t * BK;
+      const int64_t pref = kmode == KM_PAGED ? kbox_page(P, row0, j0, kend, kbox) : page_ahead(P, row0, j0, kend);
+      fetch_k(P, &tmk, kmode, kbox, row0, kvbase, j0, (int)min((int64_t)BK, kend - j0), rawk + t * RAWK_BUF,
+              &S.bar_rk[t], pref);
+    }
+  if (warp == VW0 + 3)
+    for (int t = 0; t < 2 && t < ntiles; ++t) {
+      const int64_t j0 = kbeg + (int64_t)t * BK;
+      fetch_rows(P, P.v, row0, kvbase, j0, (int)min((int64_t)BK, kend - j0), rawv + t * RAWV_BUF, &S.bar_rv[t]);
+    }
 
   // ---------------- query rows -> balanced digit planes (warp g: row g) ----------------
   if (warp < GD) {
@@ -365,6 +512,19 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       if (bad && row >= 0) S.rst[g] = ST_DOMAIN;
     }
   }
+  __syncthreads();
+  if (tid == 0) {  // the dimensions where some query row lost bits (usually none)
+    int n = 0;
+    for (int wd = 0; wd < 4; ++wd) {
+      uint32_t u = 0;
+      for (int g = 0; g < nrows; ++g) u |= S.qlossy[g][wd];
+      for (; u; u &= u - 1) {
+        if (n < NQL) S.qlk[n] = 32 * wd + __ffs(u) - 1;
+        ++n;
+      }
+    }
+    S.nqlk = n <= NQL ? n : -1;
+  }
   tc::fence_async_smem();
   tc::fence_before_sync();
   __syncthreads();
@@ -402,298 +562,377 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
   }
   int32_t vec = INT32_MIN;  // this channel's VE as last applied to N
 
-  if (warp >= NWARPS / 2) {
-    // ======================= producer warpgroups: slicing and the score MMAs =======================
-    const int ptid = tid - THREADS / 2, pwarp = warp - NWARPS / 2;
-    bool rk_pending = ntiles > 0, rv_pending = ntiles > 0;
-    uint32_t rk_ph = 0, rv_ph = 0;  // phase of the fetch in flight
-    int par = 0;
-    EA_PTW_INIT
-    for (int i = 0; i < ntiles; ++i, par ^= 1) {
+  if (warp >= KW0 && warp < VW0) {
+    // ======================= K producers: one key per thread, digits into TMEM =======================
+    const int kw = warp - KW0;
+    const int key = 32 * kw + lane;
+    const int nqlk = max(S.nqlk, 0);
+    const uint32_t tq = tmem + ((uint32_t)(32 * kw) << 16);  // this warp's TMEM lane quadrant
+    int waited = 0, issued = min(ntiles, 2);  // tiles [waited, issued) have fetches in flight
+    bool mma_pend = false;
+    uint32_t mma_ph = 0;
+    // byte offset of 16-byte chunk c (dims 8c .. 8c + 7) of this thread's raw row: in the swizzled
+    // halves (c / 8) * KHALF + 128 key + ((c % 8) ^ (key % 8)) 16, in dense rows 256 key + 16 c
+    const bool swz = kmode != KM_DENSE;
+    const uint32_t rbase = swz ? (uint32_t)key * 128u : (uint32_t)key * 256u;
+    const uint32_t hstep = swz ? KHALF : 128u;
+    const uint32_t x7 = swz ? (uint32_t)(key & 7) : 0u;
+    int64_t kpref = -1;
+    EA_PTK_INIT
+    for (int i = 0; i < ntiles; ++i) {
+      const int b = i & 1;
       const int64_t j0 = kbeg + (int64_t)i * BK;
       const int nvalid = (int)min((int64_t)BK, kend - j0);
-      const uint32_t ph = (uint32_t)i & 1u, php = (uint32_t)(i - 1) & 1u;
-      // the next tile's page-table entries, read now for its fetches below
-      const int64_t pref = pwarp >= NWARPS / 2 - 2 ? page_ahead(P, row0, j0 + BK, kend) : -1;
-      // ---- K(i): needs its raw rows, and pass 1 of tile i - 1 done with the digits, the lossy
-      //      masks and the score accumulators ----
-      bool okw = tc::mbar_wait(&S.bar_rk, ph, P.wait_debug);
-      if (i > 0) okw &= tc::mbar_wait(&S.bar_p1, php, P.wait_debug);
-      if (!group_sync_and(2, okw)) {
+      bool okw = tc::mbar_wait(&S.bar_rk[b], (uint32_t)(i >> 1) & 1u, P.wait_debug);
+      if (!group_sync_and(BAR_K, 128, okw && !*(volatile int*)&S.abort)) {
         ok_wait = false;
         break;
       }
-      rk_pending = false;
-      EA_PTW(THREADS / 2, 0)
+      waited = i + 1;
+      // page-table entries of tile i + 2, read now for its fetch below
+      if (warp == KW0 + 3 && i + 2 < ntiles)
+        kpref = kmode == KM_PAGED ? kbox_page(P, row0, j0 + 2 * BK, kend, kbox) : page_ahead(P, row0, j0 + 2 * BK, kend);
+      EA_PTK(0)
+      const uint8_t* rawb = rawk + b * RAWK_BUF + rbase;
+#define KCHUNK(c) (rawb + ((c) >> 3) * hstep + ((((uint32_t)(c) & 7u) ^ x7) << 4))
+      const bool valid = key < nvalid;
+      // pass A: the key's largest magnitude and its smallest nonzero one (two chains)
+      uint32_t mx0 = 0, mx1 = 0, mk0 = NZ_NONE, mk1 = NZ_NONE;
+      if (valid) {
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          const uint4 a = *(const uint4*)KCHUNK(cc);
+          const uint32_t m0 = a.x & 0x7FFF7FFFu, m1 = a.y & 0x7FFF7FFFu;
+          const uint32_t m2 = a.z & 0x7FFF7FFFu, m3 = a.w & 0x7FFF7FFFu;
+          mx0 = __vmaxu2(mx0, __vmaxu2(m0, m1));
+          mx1 = __vmaxu2(mx1, __vmaxu2(m2, m3));
+          mk0 = __vmins2(mk0, __vmins2(nz_key(m0), nz_key(m1)));
+          mk1 = __vmins2(mk1, __vmins2(nz_key(m2), nz_key(m3)));
+        }
+      }
+      uint32_t mx = __vmaxu2(mx0, mx1);
+      mx = max(mx & 0xFFFFu, mx >> 16);
+      const int32_t mn = nz_key_min(__vmins2(mk0, mk1));
+      const int bad = mx >= 0x7F80u;
+      const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
+      const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
+      const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
+      const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 &&
+                                              (mn == 32767 || nz_key_mag(mn) >= ((uint32_t)ebase << 7)));
+      const float sc = scale_of(max(-126, min(126, lsb)));
+      // the score MMAs of tile i - 1 are done reading the K digits in tensor memory
+      if (i > 0) {
+        okw = tc::mbar_wait(&S.bar_smma, (uint32_t)(i - 1) & 1u, P.wait_debug);
+        if (!group_sync_and(BAR_K, 128, okw)) {
+          ok_wait = false;
+          break;
+        }
+        mma_pend = false;
+      }
+      tc::fence_after_sync();
+      EA_PTK(1)
+      // pass B: digits of 32 dims at a time (4 planes x 8 columns), stored to this key's TMEM lane.
+      // x = trunc(k 2^-lsb) through fp32 is exact for every finite element when lsb lies in
+      // [-126, 126] (the product is exact or below 1); a key whose largest element is below
+      // 2^-100 (lsb < -126) takes the integer conversion.
+      const bool norm = lead == INT32_MIN || lsb >= -126;
 #pragma unroll 1
-      for (int it = 0; it < 2; ++it) {
-        const int key = 64 * it + (ptid >> 2), l4 = ptid & 3;
-        const bool valid = key < nvalid;
-        const int rot = (l4 >> 1) + 2 * (key & 1);
-        uint32_t w[16];
+      for (int blk = 0; blk < 4; ++blk) {
+        uint32_t pl[NK][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int g4 = 0; g4 < 4; ++g4) {
           uint4 a = make_uint4(0u, 0u, 0u, 0u);
-          if (valid) a = *(const uint4*)(rawk + key * (D * 2) + l4 * 64 + 16 * ((j + rot) & 3));
-          w[4 * j] = a.x;
-          w[4 * j + 1] = a.y;
-          w[4 * j + 2] = a.z;
-          w[4 * j + 3] = a.w;
-        }
-        uint32_t mx = 0, mk = NZ_NONE;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const uint32_t m = w[q] & 0x7FFF7FFFu;
-          mx = __vmaxu2(mx, m);
-          mk = __vmins2(mk, nz_key(m));
-        }
-        mx = max(mx & 0xFFFFu, mx >> 16);
-        int32_t mn = nz_key_min(mk);
-#pragma unroll
-        for (int o = 1; o < 4; o <<= 1) {
-          mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        }
-        const int bad = mx >= 0x7F80u;
-        const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
-        const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
-        const int ebase = lsb + 134;  // an element with exponent field E >= ebase loses no bits
-        const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 &&
-                                                (mn == 32767 || nz_key_mag(mn) >= ((uint32_t)ebase << 7)));
-        const float sc = scale_of(max(-126, min(126, lsb)));
-        uint32_t lm = 0;  // lossy elements, bit = dim - 32 l4
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int cj = (j + rot) & 3;
+          if (valid && lead != INT32_MIN) a = *(const uint4*)KCHUNK(4 * blk + g4);
+          const uint32_t w[4] = {a.x, a.y, a.z, a.w};
           uint32_t xs[8];
-          if (lead == INT32_MIN) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) xs[e] = 0u;
-          } else if (fast) {
+          if (norm) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              xs[2 * q] = fixf_lo(w[4 * j + q], sc);
-              xs[2 * q + 1] = fixf_hi(w[4 * j + q], sc);
+              xs[2 * q] = fixf_lo(w[q], sc);
+              xs[2 * q + 1] = fixf_hi(w[q], sc);
             }
           } else {
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const uint32_t b = (w[4 * j + (e >> 1)] >> (16 * (e & 1))) & 0xFFFFu;
               int lost = 0, b2 = 0;
-              xs[e] = (uint32_t)fixq(b, lsb, lost, b2);
-              lm |= (uint32_t)(lost != 0) << (8 * cj + e);
+              xs[e] = (uint32_t)fixq((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, lsb, lost, b2);
             }
           }
-          uint32_t p0a, p1a, p2a, p3a, p0b, p1b, p2b, p3b;
-          transpose4(xs[0], xs[1], xs[2], xs[3], p0a, p1a, p2a, p3a);
-          transpose4(xs[4], xs[5], xs[6], xs[7], p0b, p1b, p2b, p3b);
-          const uint32_t off = tc::kmajor_off(key, 32 * l4 + 8 * cj, BK);
-          *(uint2*)(sK + 0 * K_PLANE + off) = make_uint2(p0a, p0b);
-          *(uint2*)(sK + 1 * K_PLANE + off) = make_uint2(p1a, p1b);
-          *(uint2*)(sK + 2 * K_PLANE + off) = make_uint2(p2a, p2b);
-          *(uint2*)(sK + 3 * K_PLANE + off) = make_uint2(p3a, p3b);
+          transpose4(xs[0], xs[1], xs[2], xs[3], pl[0][2 * g4], pl[1][2 * g4], pl[2][2 * g4], pl[3][2 * g4]);
+          transpose4(xs[4], xs[5], xs[6], xs[7], pl[0][2 * g4 + 1], pl[1][2 * g4 + 1], pl[2][2 * g4 + 1],
+                     pl[3][2 * g4 + 1]);
         }
-        S.klossy[key][l4] = lm;
-        if (l4 == 0) {
-          S.klsb[key] = lsb;
-          S.kbad[key] = valid && bad;
-        }
-      }
-      tc::fence_async_smem();
-      group_sync(2);
-      EA_PTW(THREADS / 2, 1)
-      // score MMAs of tile i (the accumulators are free: pass 1 of tile i - 1 is done). Key digit t
-      // goes to its own accumulator and is issued by lane 0 of producer warp t: an issuing thread
-      // waits while the tensor core takes its operands, so four issuers share that wait.
-      if (lane == 0 && pwarp < NK) {
-        const int t = pwarp;
-        tc::fence_after_sync();
-        // descriptors: the base ones, then constant start-address offsets (16-byte units)
-        constexpr uint32_t lbo_a = (BK / 8) * 128, lbo_b = (NSQ / 8) * 128;
-        const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sK + t * K_PLANE), lbo_a, 128);
-        const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sQ), lbo_b, 128);
-        const uint32_t idesc = tc::idesc_i8(128, NSQ, t == NK - 1, true);
 #pragma unroll
-        for (int ks = 0; ks < D / 32; ++ks)
-          tc::mma_i8(tmem + 32 * t, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc, ks > 0);
-        tc::mma_commit(tc::smem_u32(&S.bar_smma));
+        for (int t = 0; t < NK; ++t) tc::tmem_st8(tq + COL_K + 32 * t + 8 * blk, pl[t]);
       }
-      // the raw K rows are consumed: fetch the next tile's
-      if (pwarp == NWARPS / 2 - 1 && i + 1 < ntiles) {
-        tc::fence_async_smem();
-        fetch_rows(P, P.k, row0, kvbase, j0 + BK, (int)min((int64_t)BK, kend - j0 - BK), rawk, &S.bar_rk, pref);
+      // the elements that lost bits (exponent field below ebase), for the consumers' error bound
+      uint32_t lmk[4] = {0u, 0u, 0u, 0u};
+      if (!fast && valid) {
+        const uint32_t thr = (uint32_t)max(ebase, 0) << 7;
+#pragma unroll 1
+        for (int cc = 0; cc < 16; ++cc) {
+          const uint4 a = *(const uint4*)KCHUNK(cc);
+          const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+          uint32_t bits = 0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t mg = (w[e >> 1] >> (16 * (e & 1))) & 0x7FFFu;
+            bits |= (uint32_t)(mg != 0 && mg < thr) << e;
+          }
+          lmk[cc >> 2] |= bits << (8 * (cc & 3));
+        }
       }
-      if (i + 1 < ntiles) {
-        rk_pending = true;
-        rk_ph = (uint32_t)(i + 1) & 1u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) S.klossy[b][key][q] = lmk[q];
+      S.klsb[b][key] = (int16_t)lsb;
+      S.kbad[b][key] = (uint8_t)(valid && bad);
+      // the key's fixed-point values where some query row is lossy (the consumers' error bound)
+      for (int n = 0; n < nqlk; ++n) {
+        int lost = 0, b2 = 0;
+        const int ii = S.qlk[n];
+        const uint32_t kb = valid ? *(const uint16_t*)(KCHUNK(ii >> 3) + 2 * (ii & 7)) : 0u;
+        S.kqv[b][key][n] = lead == INT32_MIN ? 0 : fixq(kb, lsb, lost, b2);
       }
-
-      // ---- V(i): needs its raw rows, and the P.V MMAs of tile i - 1 done with the value digits. The
-      //      channel data of tile i - 1 stay in the other parity buffer until the consumers' merge;
-      //      the P.V MMAs of tile i + 1 (after that merge) gate the next rewrite of this one ----
-      okw = tc::mbar_wait(&S.bar_rv, ph, P.wait_debug);
-      if (i > 0) okw &= tc::mbar_wait(&S.bar_pv, php, P.wait_debug);
-      if (!group_sync_and(2, okw)) {
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      EA_PTK(2)
+      // every K thread is done with the raw rows of tile i: fetch tile i + 2 into them
+      group_sync(BAR_K, 128);
+      if (i + 2 < ntiles) {
+        if (warp == KW0 + 3)
+          fetch_k(P, &tmk, kmode, kbox, row0, kvbase, j0 + 2 * BK, (int)min((int64_t)BK, kend - j0 - 2 * BK),
+                  rawk + b * RAWK_BUF, &S.bar_rk[b], kpref);
+        issued = i + 3;
+      }
+      // the consumers are done with the score accumulators of tile i - 1
+      okw = i > 0 ? tc::mbar_wait(&S.bar_p1, (uint32_t)(i - 1) & 1u, P.wait_debug) : true;
+      if (!group_sync_and(BAR_K, 128, okw)) {
         ok_wait = false;
         break;
       }
-      rv_pending = false;
-      EA_PTW(THREADS / 2, 2)
-      const int cp = ptid & 63, kq = ptid >> 6;
-      const uint8_t* vsrc = rawv + (32 * kq) * (DV * 2) + cp * 4;  // word of key 32 kq + jj at jj * 256
-      const int nv = min(32, max(0, nvalid - 32 * kq));             // this thread's valid keys
-      uint32_t vmn;  // per channel (half) the key of the smallest nonzero |v| over this thread's keys
-      {
-        uint32_t mx = 0;
-        vmn = NZ_NONE;
-        if (nv == 32) {  // a full key quarter: no bounds test per load
+      EA_PTK(3)
+      // score MMAs of tile i: key digit plane t (A in TMEM) by lane 0 of K warp t; an issuing
+      // thread waits while the tensor core takes its operands, so four issuers share that wait
+      if (lane == 0) {
+        const int t = kw;
+        tc::fence_after_sync();
+        constexpr uint32_t lbo_b = (NSQ / 8) * 128;
+        const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sQ), lbo_b, 128);
+        const uint32_t idesc = tc::idesc_i8(128, nsq, t == NK - 1, true);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const uint32_t m = *(const uint32_t*)(vsrc + jj * (DV * 2)) & 0x7FFF7FFFu;
-            mx = __vmaxu2(mx, m);
-            vmn = __vmins2(vmn, nz_key(m));
+        for (int ks = 0; ks < D / 32; ++ks)
+          tc::mma_i8_tmem_a(tmem + COL_S + 32 * t, tmem + COL_K + 32 * t + 8 * ks, bd0 + ((ks * 2 * lbo_b) >> 4),
+                            idesc, ks > 0);
+        tc::mma_commit(tc::smem_u32(&S.bar_smma));
+      }
+      mma_pend = true;
+      mma_ph = (uint32_t)i & 1u;
+    }
+#undef KCHUNK
+    EA_PT_FLUSH_RANGE(256, 8, 12)
+    if (!ok_wait) S.abort = 1;
+    // what this role still has in flight gets a bounded wait before shared and tensor memory go
+    for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rk[t & 1], (uint32_t)(t >> 1) & 1u, P.wait_debug);
+    if (mma_pend) tc::mbar_wait(&S.bar_smma, mma_ph, P.wait_debug);
+  } else if (warp >= VW0) {
+    // ======================= V producers: value digits into shared memory =======================
+    const int vt = tid - VW0 * 32;
+    const int cp = vt & 63, kh = vt >> 6;  // channels 2 cp, 2 cp + 1; keys 64 kh .. 64 kh + 63
+    // Slot s of this thread holds channel 2 cp + (s ^ swp): a quarter warp's digit stores then
+    // cover all 8 16-byte slots of a core matrix (no bank conflicts). The slot's value is taken out
+    // of the 32-bit word of both channels by one byte permute (which also zeroes it for a channel
+    // without digits).
+    const int swp = (cp >> 2) & 1;
+    int waited = 0, issued = min(ntiles, 2);  // tiles [waited, issued) have fetches in flight
+    EA_PTV_INIT
+    for (int i = 0; i < ntiles; ++i) {
+      const int b = i & 1, par = b;
+      const int64_t j0 = kbeg + (int64_t)i * BK;
+      const int nvalid = (int)min((int64_t)BK, kend - j0);
+      const int64_t pref = warp == VW0 + 3 ? page_ahead(P, row0, j0 + 2 * BK, kend) : -1;
+      bool okw = tc::mbar_wait(&S.bar_rv[b], (uint32_t)(i >> 1) & 1u, P.wait_debug);
+      if (!group_sync_and(BAR_V, 128, okw && !*(volatile int*)&S.abort)) {
+        ok_wait = false;
+        break;
+      }
+      waited = i + 1;
+      EA_PTV(0)
+      const uint8_t* vsrc = rawv + b * RAWV_BUF + (64 * kh) * (DV * 2) + cp * 4;  // key 64 kh + jj at jj * 256
+      const int nv = min(64, max(0, nvalid - 64 * kh));  // this thread's valid keys
+      // per channel (16-bit half) the largest magnitude and the key of the smallest nonzero one
+      uint32_t mxw, mnw;
+      {
+        uint32_t x0 = 0, x1 = 0, x2 = 0, x3 = 0;
+        uint32_t n0 = NZ_NONE, n1 = NZ_NONE, n2 = NZ_NONE, n3 = NZ_NONE;
+        if (nv == 64) {  // full: no bounds test per load
+#pragma unroll 4
+          for (int jj = 0; jj < 64; jj += 4) {
+            const uint32_t a0 = *(const uint32_t*)(vsrc + jj * (DV * 2)) & 0x7FFF7FFFu;
+            const uint32_t a1 = *(const uint32_t*)(vsrc + (jj + 1) * (DV * 2)) & 0x7FFF7FFFu;
+            const uint32_t a2 = *(const uint32_t*)(vsrc + (jj + 2) * (DV * 2)) & 0x7FFF7FFFu;
+            const uint32_t a3 = *(const uint32_t*)(vsrc + (jj + 3) * (DV * 2)) & 0x7FFF7FFFu;
+            x0 = __vmaxu2(x0, a0);
+            x1 = __vmaxu2(x1, a1);
+            x2 = __vmaxu2(x2, a2);
+            x3 = __vmaxu2(x3, a3);
+            n0 = __vmins2(n0, nz_key(a0));
+            n1 = __vmins2(n1, nz_key(a1));
+            n2 = __vmins2(n2, nz_key(a2));
+            n3 = __vmins2(n3, nz_key(a3));
           }
         } else {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const uint32_t m = (jj < nv ? *(const uint32_t*)(vsrc + jj * (DV * 2)) : 0u) & 0x7FFF7FFFu;
-            mx = __vmaxu2(mx, m);
-            vmn = __vmins2(vmn, nz_key(m));
+#pragma unroll 4
+          for (int jj = 0; jj < nv; ++jj) {
+            const uint32_t a0 = *(const uint32_t*)(vsrc + jj * (DV * 2)) & 0x7FFF7FFFu;
+            x0 = __vmaxu2(x0, a0);
+            n0 = __vmins2(n0, nz_key(a0));
           }
         }
+        mxw = __vmaxu2(__vmaxu2(x0, x1), __vmaxu2(x2, x3));
+        mnw = __vmins2(__vmins2(n0, n1), __vmins2(n2, n3));
+      }
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t m = (mx >> (16 * hh)) & 0xFFFFu;
-          if (m >= 0x7F80u) {
-            // a NaN / inf value: a domain error for the rows that see its key; the channel's range
-            // comes from the finite values (the rows that do not see it use them)
-            m = 0;
+      for (int h = 0; h < 2; ++h) {  // physical channel 2 cp + h
+        uint32_t m = (mxw >> (16 * h)) & 0xFFFFu;
+        if (m >= 0x7F80u) {
+          // a NaN / inf value: a domain error for the rows that see its key; the channel's range
+          // comes from the finite values (the rows that do not see it use them)
+          m = 0;
 #pragma unroll 1
-            for (int jj = 0; jj < nv; ++jj) {
-              const uint32_t e = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0x7FFFu;
-              if (e >= 0x7F80u) {
-                for (int g = 0; g < nrows; ++g)
-                  if (S.rows[g] >= 0 && j0 + 32 * kq + jj < S.len[g]) atomicMax(&S.rst[g], ST_DOMAIN);
-              } else {
-                m = max(m, e);
-              }
+          for (int jj = 0; jj < nv; ++jj) {
+            const uint32_t e = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * h)) & 0x7FFFu;
+            if (e >= 0x7F80u) {
+              for (int g = 0; g < nrows; ++g)
+                if (S.rows[g] >= 0 && j0 + 64 * kh + jj < S.len[g]) atomicMax(&S.rst[g], ST_DOMAIN);
+            } else {
+              m = max(m, e);
             }
           }
-          S.ve4[kq][2 * cp + hh] = (int16_t)(m == 0 ? INT16_MIN : lead_of_bits(m) + 1);
+        }
+        S.ve4[kh][2 * cp + h] = (int16_t)(m == 0 ? INT16_MIN : lead_of_bits(m) + 1);
+      }
+      S.vl_n[par][vt] = 0;
+      group_sync(BAR_V, 128);
+      EA_PTV(1)
+      // running exponents of this thread's channels: the previous tiles' and this tile's
+      int lsbh[2], keeph[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ch = 2 * cp + h;
+        int ve = S.ve[par ^ 1][ch];
+        if (S.ve4[0][ch] != INT16_MIN) ve = max(ve, (int)S.ve4[0][ch]);
+        if (S.ve4[1][ch] != INT16_MIN) ve = max(ve, (int)S.ve4[1][ch]);
+        if (kh == 0) S.ve[par][ch] = ve;
+        lsbh[h] = ve == INT32_MIN ? 0 : ve - FV;
+        // a channel whose maximum lies at the very bottom of the bf16 range keeps no digits
+        keeph[h] = (ve == INT32_MIN || lsbh[h] >= -126) ? 1 : 0;
+      }
+      // per slot: the channel, the byte permute that places its bf16 in the high half of a zero
+      // word (all zero without digits), and the scales of the two fused multiply-adds
+      int chs[2];
+      uint32_t sels[2];
+      float schi[2], sclo[2], clampv[2];
+#pragma unroll
+      for (int sl = 0; sl < 2; ++sl) {
+        const int h = sl ^ swp;
+        const int keep = h ? keeph[1] : keeph[0];
+        const int l = keep ? (h ? lsbh[1] : lsbh[0]) : 0;
+        chs[sl] = 2 * cp + h;
+        sels[sl] = keep ? (h ? 0x3244u : 0x1044u) : 0x4444u;
+        schi[sl] = scale_of(l + 8);       // 2^-(lsb + 8): the high part floor(x / 256)
+        sclo[sl] = scale_of(l);           // 2^-lsb
+        clampv[sl] = scale_of(-(l + 15));  // 2^(lsb + 15): above it x is a multiple of 256
+      }
+      // the P.V MMAs of tile i - 1 are done reading the value digit planes
+      if (i > 0) {
+        okw = tc::mbar_wait(&S.bar_pv, (uint32_t)(i - 1) & 1u, P.wait_debug);
+        if (!group_sync_and(BAR_V, 128, okw)) {
+          ok_wait = false;
+          break;
         }
       }
-      if (ptid < DV) {
-        S.vl_n[par][ptid] = 0;
+      EA_PTV(2)
+      // Digits of x = floor(v 2^-lsb) (|x| < 2^30) = 256 h + l: fmaf_rz(v, 2^-(lsb + 8), 1.5 2^23) is
+      // 1.5 2^23 + h exactly (the product is exact, the sum positive, rounding toward zero is the
+      // floor), whose low three bytes are h + 2^22; the same on v clamped to +-2^(lsb + 15) with
+      // the scale 2^-lsb gives l = x mod 256 in the low byte (a value of magnitude 2^(lsb + 15) or
+      // more is a multiple of 2^(lsb + 8), so l = 0 for it and for the clamp bound alike). The
+      // digits are l and the three bytes of h + 2^22, i.e. of x + 2^30. Values of a channel
+      // without digits count as 0. Sixteen keys per step, both slots from the same words.
+#pragma unroll 1
+      for (int ck = 0; ck < 4; ++ck) {
+        uint32_t w[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) S.vlmask[par][ptid][q] = 0;
+        for (int jj = 0; jj < 16; ++jj) w[jj] = *(const uint32_t*)(vsrc + (16 * ck + jj) * (DV * 2));
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          uint32_t pw[NV][4];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t fh[4], fl[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float f = __uint_as_float(__byte_perm(w[4 * c4 + e], 0u, sels[sl]));
+              fh[e] = __float_as_uint(__fmaf_rz(f, schi[sl], V_MAGIC));
+              fl[e] = __float_as_uint(__fmaf_rz(fminf(fmaxf(f, -clampv[sl]), clampv[sl]), sclo[sl], V_MAGIC));
+            }
+            transpose3(fh[0], fh[1], fh[2], fh[3], pw[1][c4], pw[2][c4], pw[3][c4]);
+            pw[0][c4] = __byte_perm(__byte_perm(fl[0], fl[1], 0x0040), __byte_perm(fl[2], fl[3], 0x0040), 0x5410);
+          }
+#pragma unroll
+          for (int p = 0; p < NV; ++p)
+            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(chs[sl], 64 * kh + 16 * ck, BK)) =
+                make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
+        }
       }
-      group_sync(2);
-      EA_PTW(THREADS / 2, 3)
-      // Digits of x = trunc(v 2^-lsb) through fp32 for every value. The values that lose bits (their
-      // exponent field below ebase = lsb + 134) go to the channel's correction list, which adds back
-      // exactly what the truncation dropped, or past its capacity to the bound. A channel whose
-      // maximum lies at the very bottom of the bf16 range (lsb < -126) keeps no digits and is bounded.
-      {
-        int ebase2[2], lsb2[2];
-        uint32_t keep2[2];
-        float sc2[2];
+      // Values below the V window (an exponent field under lsb + 134): each goes to its channel's
+      // correction list with the exact part the floor dropped, or past the list's capacity to the
+      // bound; in a channel without digits every nonzero value is bounded.
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          // running channel exponent: the previous tiles' and this tile's key quarters
-          int ve = S.ve[par ^ 1][2 * cp + hh];
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (S.ve4[q][2 * cp + hh] != INT16_MIN) ve = max(ve, (int)S.ve4[q][2 * cp + hh]);
-          if (kq == 0) S.ve[par][2 * cp + hh] = ve;
-          lsb2[hh] = ve == INT32_MIN ? 0 : ve - FV;
-          const bool in_range = ve == INT32_MIN || lsb2[hh] >= -126;  // lsb <= 127 - 31 always
-          ebase2[hh] = lsb2[hh] + 134;
-          keep2[hh] = in_range ? 0xFFFFFFFFu : 0u;
-          sc2[hh] = scale_of(in_range ? lsb2[hh] : 0);
-        }
-        const bool plain = nv == 32 && (keep2[0] & keep2[1]) != 0u;
+      for (int h = 0; h < 2; ++h) {  // physical channel 2 cp + h
+        const int cc = 2 * cp + h;
+        const int keep = keeph[h], lsb = lsbh[h];
+        const uint32_t thr = keep ? ((uint32_t)max(lsb + 134, 0) << 7) : 0x8000u;  // all, when bounded
+        const int32_t mk = (int32_t)(int16_t)((mnw >> (16 * h)) & 0xFFFFu);
+        if (mk != 32767 && nz_key_mag(mk) < thr) {
+          bool any = false;
 #pragma unroll 1
-        for (int q4 = 0; q4 < 2; ++q4) {
-          uint32_t xa[16], xb[16];
-          if (plain) {  // the usual case: 32 valid keys, both channels keep digits
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const uint32_t w = *(const uint32_t*)(vsrc + (16 * q4 + jj) * (DV * 2));
-              xa[jj] = fixf_lo(w, sc2[0]);
-              xb[jj] = fixf_hi(w, sc2[1]);
-            }
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int kk = 16 * q4 + jj;
-              const uint32_t w = kk < nv ? *(const uint32_t*)(vsrc + kk * (DV * 2)) : 0u;
-              xa[jj] = fixf_lo(w, sc2[0]) & keep2[0];
-              xb[jj] = fixf_hi(w, sc2[1]) & keep2[1];
+          for (int jj = 0; jj < nv; ++jj) {
+            const uint32_t bb = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * h)) & 0xFFFFu;
+            const uint32_t mg = bb & 0x7FFFu;
+            if (mg == 0 || mg >= thr) continue;
+            any = true;
+            if (!keep) continue;
+            int lost2 = 0;
+            const int32_t dx = lost_part24(bb, lsb, lost2);
+            const uint32_t k = atomicAdd(&S.vl_n[par][cc], 1u);
+            if (k < VLCAP) {
+              S.vl_k[par][cc][k] = (uint16_t)((64 * kh + jj) | (lost2 << 8));
+              S.vl_dx[par][cc][k] = dx;
             }
           }
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t* x = hh ? xb : xa;
-            uint32_t pw[NV][4];
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4)
-              transpose4(x[4 * c4], x[4 * c4 + 1], x[4 * c4 + 2], x[4 * c4 + 3], pw[0][c4], pw[1][c4], pw[2][c4],
-                         pw[3][c4]);
-#pragma unroll
-            for (int p = 0; p < NV; ++p)
-              *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(2 * cp + hh, 32 * kq + 16 * q4, BK)) =
-                  make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
-          }
-        }
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int cc = 2 * cp + hh;
-          const uint32_t thr = keep2[hh] ? ((uint32_t)max(ebase2[hh], 0) << 7) : 0x8000u;  // all, when bounded
-          const int32_t mk = (int32_t)(int16_t)((vmn >> (16 * hh)) & 0xFFFFu);
-          uint32_t lossy = 0;
-          if (mk != 32767 && nz_key_mag(mk) < thr) {
-#pragma unroll 1
-            for (int jj = 0; jj < nv; ++jj) {
-              const uint32_t b = (*(const uint32_t*)(vsrc + jj * (DV * 2)) >> (16 * hh)) & 0xFFFFu;
-              const uint32_t mg = b & 0x7FFFu;
-              if (mg == 0 || mg >= thr) continue;
-              lossy |= 1u << jj;
-              if (!keep2[hh]) continue;
-              int lost2 = 0;
-              const int32_t dx = lost_part24(b, lsb2[hh], lost2);
-              const uint32_t k = atomicAdd(&S.vl_n[par][cc], 1u);
-              if (k < VLCAP) {
-                S.vl_k[par][cc][k] = (uint16_t)((32 * kq + jj) | (lost2 << 8));
-                S.vl_dx[par][cc][k] = dx;
-              }
-            }
-            if (!keep2[hh] && lossy) atomicAdd(&S.vl_n[par][cc], VL_BOUNDED);  // the whole channel is bounded
-          }
-          S.vlmask[par][cc][kq] = lossy;
+          if (!keep && any) atomicAdd(&S.vl_n[par][cc], VL_BOUNDED);  // the whole channel is bounded
         }
       }
       tc::fence_async_smem();
-      group_sync(2);
-      EA_PTW(THREADS / 2, 4)
-      if (ptid == 0) mbar_arrive(&S.bar_vready);  // value digits and channel data of tile i
-      // the raw V rows are consumed: fetch the next tile's
-      if (pwarp == NWARPS / 2 - 2 && i + 1 < ntiles) {
-        tc::fence_async_smem();
-        fetch_rows(P, P.v, row0, kvbase, j0 + BK, (int)min((int64_t)BK, kend - j0 - BK), rawv, &S.bar_rv, pref);
-      }
-      if (i + 1 < ntiles) {
-        rv_pending = true;
-        rv_ph = (uint32_t)(i + 1) & 1u;
+      group_sync(BAR_V, 128);
+      EA_PTV(3)
+      if (vt == 0) mbar_arrive(&S.bar_vready);  // value digits and channel data of tile i
+      // the raw V rows of tile i are consumed: fetch tile i + 2 into them
+      if (i + 2 < ntiles) {
+        if (warp == VW0 + 3) {
+          tc::fence_async_smem();
+          fetch_rows(P, P.v, row0, kvbase, j0 + 2 * BK, (int)min((int64_t)BK, kend - j0 - 2 * BK), rawv + b * RAWV_BUF,
+                     &S.bar_rv[b], pref);
+        }
+        issued = i + 3;
       }
     }
-    EA_PTW_FLUSH(THREADS / 2)
+    EA_PT_FLUSH_RANGE(384, 12, 16)
     if (!ok_wait) S.abort = 1;
-    // a wait that gave up: the copies still in flight get another bounded wait before the shared
-    // memory is released
-    if (rk_pending) tc::mbar_wait(&S.bar_rk, rk_ph, P.wait_debug);
-    if (rv_pending) tc::mbar_wait(&S.bar_rv, rv_ph, P.wait_debug);
+    for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rv[t & 1], (uint32_t)(t >> 1) & 1u, P.wait_debug);
   } else {
-    // ======================= consumer warpgroups: logits, weights, P.V, merges =======================
+    // ======================= consumer warpgroups: logits, weights, merges, drains =======================
     const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     int par = 0;
     bool pv_pending = false;
@@ -703,9 +942,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const int64_t j0 = kbeg + (int64_t)i * BK;
       const int nvalid = (int)min((int64_t)BK, kend - j0);
       const uint32_t ph = (uint32_t)i & 1u;
+      const int b = i & 1;
       {
         const bool okw = tc::mbar_wait(&S.bar_smma, ph, P.wait_debug);  // the score MMAs of tile i
-        if (!group_sync_and(1, okw && !*(volatile int*)&S.abort)) {
+        if (!group_sync_and(BAR_C, 256, okw && !*(volatile int*)&S.abort)) {
           ok_wait = false;
           break;
         }
@@ -716,13 +956,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       bool unc = false;
       {
         const int key = c;
-        const bool klossy = (S.klossy[key][0] | S.klossy[key][1] | S.klossy[key][2] | S.klossy[key][3]) != 0;
-        const bool kbad = S.kbad[key];
+        const uint32_t* kl4 = S.klossy[b][key];
+        const bool klossy = (kl4[0] | kl4[1] | kl4[2] | kl4[3]) != 0;
+        const bool kbad = S.kbad[b][key];
+        const int klsb = S.klsb[b][key];
+        const int nqlk = S.nqlk;
 #pragma unroll 1
         for (int g = h; g < nrows; g += NWGC) {
           uint32_t dg[NK][4];
 #pragma unroll
-          for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + 32 * t + 4 * g, dg[t]);
+          for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + COL_S + 32 * t + 4 * g, dg[t]);
           tc::tmem_wait_ld();
           uint32_t out = T_MASKED;
           if (key < nvalid && j0 + key < S.len[g] && S.rows[g] >= 0) {
@@ -741,19 +984,26 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
               const uint32_t hi3[3] = {(uint32_t)G4, (uint32_t)G5, (uint32_t)G6};
               const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
               const bool qlossy = (S.qlossy[g][0] | S.qlossy[g][1] | S.qlossy[g][2] | S.qlossy[g][3]) != 0;
-              const int sexp = S.qlsb[g] + S.klsb[key];
+              const int sexp = S.qlsb[g] + klsb;
               uint32_t fb;
               bool done = false, differ = false;
               uint64_t err = 0;
               if (qlossy || klossy) {
-                // |q k - Q K| <= |dq| |k| + |Q| |dk| over the lossy elements (units 2^(qlsb + klsb))
-                for (int wd = 0; wd < 4; ++wd) {
-                  const uint32_t ql = S.qlossy[g][wd], kl = S.klossy[key][wd];
-                  for (uint32_t m = ql; m; m &= m - 1) {
-                    const int ii = 32 * wd + __ffs(m) - 1;
-                    const int32_t kf = read_fix(sK, K_PLANE, key, ii, BK);
-                    err += (uint64_t)(kf < 0 ? -kf : kf) + ((kl >> (ii & 31)) & 1u);
+                // |q k - Q K| <= |dq| |k| + |Q| |dk| over the lossy elements (units 2^(qlsb + klsb));
+                // |k|'s fixed point as the K producers kept it (beyond their list: |K| < 2^W),
+                // |Q| from the query digits
+                if (nqlk >= 0) {
+                  for (int n = 0; n < nqlk; ++n) {
+                    const int ii = S.qlk[n];
+                    if (!((S.qlossy[g][ii >> 5] >> (ii & 31)) & 1u)) continue;
+                    const int32_t kf = S.kqv[b][key][n];
+                    err += (uint64_t)(kf < 0 ? -kf : kf) + ((kl4[ii >> 5] >> (ii & 31)) & 1u);
                   }
+                } else {
+                  for (int wd = 0; wd < 4; ++wd) err += (uint64_t)__popc(S.qlossy[g][wd]) * ((1ull << P.W) + 1);
+                }
+                for (int wd = 0; wd < 4; ++wd) {
+                  const uint32_t kl = kl4[wd];
                   for (uint32_t m = kl; m; m &= m - 1) {
                     const int ii = 32 * wd + __ffs(m) - 1;
                     const int32_t qf = q_fix(sQ, g, ii);
@@ -797,8 +1047,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         }
       }
       tc::fence_before_sync();
-      const bool any_unc = group_sync_or(1, unc);
-      if (tid == 0) mbar_arrive(&S.bar_p1);  // the key digits, masks and score accumulators are free
+      const bool any_unc = group_sync_or(BAR_C, 256, unc);
+      if (tid == 0) mbar_arrive(&S.bar_p1);  // the score accumulators and the raw K rows are free
       EA_PT(1)
       // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
       if (any_unc) {
@@ -823,7 +1073,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             }
           }
         }
-        group_sync(1);
+        group_sync(BAR_C, 256);
         // the tile bounds again, now over the exact logits too
 #pragma unroll 1
         for (int g = h; g < nrows; g += NWGC) {
@@ -841,7 +1091,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             S.rtlo[warp & 3][g] = ll;
           }
         }
-        group_sync(1);
+        group_sync(BAR_C, 256);
       }
       EA_PT(2)
       // ---------------- pass 2: weights, W digits ----------------
@@ -905,12 +1155,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       }
       tc::fence_async_smem();
       bool okw = tc::mbar_wait(&S.bar_vready, ph, P.wait_debug);  // the producers' value digits of tile i
-      if (!group_sync_and(1, okw)) {
+      if (!group_sync_and(BAR_C, 256, okw)) {
         ok_wait = false;
         break;
       }
       EA_PT(3)
-      // ---------------- P.V MMAs: 4 value digits x (N = 48: row weight digits) ----------------
+      // ---------------- P.V MMAs: 4 value digits x (N: the rows' weight digits) ----------------
       // value digit u to its own accumulator, issued by lane 0 of consumer warp u
       if (lane == 0 && warp < NV) {
         const int u = warp;
@@ -918,7 +1168,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         constexpr uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
         const uint64_t ad0 = tc::smem_desc(tc::smem_u32(sV + u * V_PLANE), lbo_a, 128);
         const uint64_t bd0 = tc::smem_desc(tc::smem_u32(sW), lbo_b, 128);
-        const uint32_t idesc = tc::idesc_i8(128, NSW, u == NV - 1, false);
+        const uint32_t idesc = tc::idesc_i8(128, npv, false, false);
 #pragma unroll
         for (int ks = 0; ks < BK / 32; ++ks)
           tc::mma_i8(tmem + COL_O + NSW * u, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
@@ -928,13 +1178,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       pv_pending = true;
       pv_ph = ph;
       EA_PT(7)
-      // meanwhile: this channel's exponent change, the rows' merges and bounds (registers only)
+      // this channel's exponent change, the rows' merges and bounds (registers only) while the P.V
+      // MMAs run
       const int ve_now = S.ve[par][c];
       int sh_base[RPT];
+      uint64_t ztile[RPT];
 #pragma unroll
       for (int ii = 0; ii < RPT; ++ii) {
         const int g = h + NWGC * ii;
         sh_base[ii] = INT32_MIN;
+        ztile[ii] = 0;
         if (g >= nrows) continue;
         if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
           const int d = ve_now - vec;
@@ -955,6 +1208,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         }
         R[ii] = Rn;
         const uint64_t zt = S.zs[0][g] + S.zs[1][g] + S.zs[2][g] + S.zs[3][g];
+        ztile[ii] = zt;
         const uint64_t nlw = (uint64_t)S.zl[0][g] + S.zl[1][g] + S.zl[2][g] + S.zl[3][g];
         const int zsh = (Rt - FW) - (Rn - FZ);
         int lost = 0;
@@ -977,27 +1231,19 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
             uint64_t W = 0;
 #pragma unroll
             for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-            corr += shift_floor128((i128)(int64_t)W * S.vl_dx[par][c][k], sb - 24);  // |W dx| < 2^72
+            corr += shift_floor128((i128)(int64_t)W * S.vl_dx[par][c][k], sb - 24);  // 0 <= W dx < 2^72
             cerr += (sb - 24 < 0) ? 1u : 0u;
             if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
           }
           N[ii] += corr;
           Nerr[ii] += cerr;
         } else {
-          uint64_t vw = 0;
-#pragma unroll 1
-          for (int q4 = 0; q4 < 4; ++q4)
-            for (uint32_t m = S.vlmask[par][c][q4]; m; m &= m - 1) {
-              const int key = 32 * q4 + __ffs(m) - 1;
-              uint64_t W = 0;
-#pragma unroll
-              for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
-              vw += W + 1;
-            }
-          // a truncated value lost < 1 V unit; a bounded channel's values are < 2^VE_c: 2^FV units
-          Nerr[ii] += scale_ceil128(vw, sb + (nl >= VL_BOUNDED ? FV : 0));
+          // more such values than the list holds (or a channel without digits): each lost < 1 V
+          // unit (a bounded channel's values are < 2^VE_c: 2^FV units) times < W + 1 W units,
+          // bounded over every key of the tile: sum (W + 1) = Z_tile + 128
+          Nerr[ii] += scale_ceil128((u128)zt + BK, sb + (nl >= VL_BOUNDED ? FV : 0));
         }
-        Nerr[ii] += (sb < 0) + (24 + sb < 0) + (48 + sb < 0);  // floors of the three round shifts
+        Nerr[ii] += (sb < 0);  // the floor of the tile's one shift into N
       }
       vec = ve_now;
       EA_PT(4)
@@ -1006,7 +1252,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
       const bool ok_pv = tc::mbar_wait(&S.bar_pv, ph, P.wait_debug);
       tc::fence_after_sync();
       EA_PT(5)
-      // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k, G_k = sum_{u + w = k} D_u[w] ----------------
+      // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k - 2^30 Z_tile, G_k = sum_{u + w = k} D_u[w] ----------------
 #pragma unroll
       for (int ii = 0; ii < RPT; ++ii) {
         const int g = h + NWGC * ii;
@@ -1018,32 +1264,31 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
         tc::tmem_ld8(tlane + COL_O + 3 * NSW + 6 * g, d3);
         tc::tmem_wait_ld();
         if (sh_base[ii] == INT32_MIN) continue;
-        // |D_u[w]| < 128 keys x 255 x 255 < 2^23, so each group (<= 4 terms) fits int32
-        const int32_t s0 = (int32_t)d0[0];
-        const int32_t s1 = (int32_t)d0[1] + (int32_t)d1[0];
-        const int32_t s2 = (int32_t)d0[2] + (int32_t)d1[1] + (int32_t)d2[0];
-        const int32_t s3 = (int32_t)d0[3] + (int32_t)d1[2] + (int32_t)d2[1] + (int32_t)d3[0];
-        const int32_t s4 = (int32_t)d0[4] + (int32_t)d1[3] + (int32_t)d2[2] + (int32_t)d3[1];
-        const int32_t s5 = (int32_t)d0[5] + (int32_t)d1[4] + (int32_t)d2[3] + (int32_t)d3[2];
-        const int32_t s6 = (int32_t)d1[5] + (int32_t)d2[4] + (int32_t)d3[3];
-        const int32_t s7 = (int32_t)d2[5] + (int32_t)d3[4];
-        const int32_t s8 = (int32_t)d3[5];
-        const uint32_t r0[3] = {(uint32_t)s0, (uint32_t)s1, (uint32_t)s2};
-        const uint32_t r1[3] = {(uint32_t)s3, (uint32_t)s4, (uint32_t)s5};
-        const uint32_t r2[3] = {(uint32_t)s6, (uint32_t)s7, (uint32_t)s8};
-        const int sb = sh_base[ii];
-        N[ii] += shift_floor128(recomb<3>(r0), sb) + shift_floor128(recomb<3>(r1), 24 + sb) +
-                 shift_floor128(recomb<3>(r2), 48 + sb);
+        // unsigned digits: 0 <= D_u[w] < 128 keys x 255 x 255 < 2^23, each group (<= 4 terms) < 2^25
+        const int64_t s0 = (int64_t)d0[0];
+        const int64_t s1 = (int64_t)d0[1] + d1[0];
+        const int64_t s2 = (int64_t)d0[2] + d1[1] + d2[0];
+        const int64_t s3 = (int64_t)d0[3] + d1[2] + d2[1] + d3[0];
+        const int64_t s4 = (int64_t)d0[4] + d1[3] + d2[2] + d3[1];
+        const int64_t s5 = (int64_t)d0[5] + d1[4] + d2[3] + d3[2];
+        const int64_t s6 = (int64_t)d1[5] + d2[4] + d3[3];
+        const int64_t s7 = (int64_t)d2[5] + d3[4];
+        const int64_t s8 = (int64_t)d3[5];
+        const int64_t lo = s0 + (s1 << 8) + (s2 << 16) + (s3 << 24);  // < 2^50
+        const int64_t hi = s4 + (s5 << 8) + (s6 << 16) + (s7 << 24);
+        // sum_keys W (x + 2^30) - 2^30 sum_keys W = sum_keys W x, exactly
+        const i128 T = (i128)lo + ((i128)hi << 32) + ((i128)s8 << 64) - ((i128)ztile[ii] << 30);
+        N[ii] += shift_floor128(T, sh_base[ii]);
       }
       tc::fence_before_sync();
-      if (!group_sync_and(1, ok_pv)) {
+      if (!group_sync_and(BAR_C, 256, ok_pv)) {
         ok_wait = false;
         break;
       }
       pv_pending = false;
       EA_PT(6)
     }
-    EA_PT_FLUSH
+    EA_PT_FLUSH_RANGE(0, 0, 8)
     if (!ok_wait) S.abort = 1;
     if (pv_pending) tc::mbar_wait(&S.bar_pv, pv_ph, P.wait_debug);
     n_exact = __reduce_add_sync(0xffffffffu, n_exact);
@@ -1054,9 +1299,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
     }
   }
   tc::fence_before_sync();
-  __syncthreads();  // both roles are done: row status (also set by the producers) is final
-  // ---------------- split partials of this CTA's rows (after both roles are done) ----------------
-  if (warp < NWARPS / 2) {
+  __syncthreads();  // every role is done: row status (also set by the producers) is final
+  // ---------------- split partials of this CTA's rows (after every role is done) ----------------
+  if (warp < KW0) {
 #pragma unroll
     for (int ii = 0; ii < RPT; ++ii) {
       const int g = h + NWGC * ii;
@@ -1110,6 +1355,52 @@ __global__ void __launch_bounds__(THREADS, 1) tc_decode_kernel(Prob P, const int
 
 }  // namespace tcd
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda)
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)f;
+  }
+  return fn;
+}
+
+// The K fetch mode of a launch and its tensor map: 2D (128 dims x krows rows of bf16), boxes of 64
+// dims x `box` rows, 128-byte swizzle. RANGE tiles are 128 consecutive rows; PAGED tiles start on
+// page boundaries, so pages of 8..128 keys that divide 128, or multiples of 128, map onto whole
+// boxes. Anything else (or a tensor too tall for 32-bit coordinates) takes dense bulk copies.
+static int k_fetch_mode(const Prob& P, CUtensorMap* tm, int* kbox) {
+  *kbox = 0;
+  std::memset(tm, 0, sizeof(*tm));
+  int mode = tcd::KM_DENSE, box = 0;
+  if (P.kind == MASK_RANGE) {
+    mode = tcd::KM_RANGE;
+    box = tcd::BK;
+  } else if (P.kind == MASK_PAGED && P.page_size > 0) {
+    if (P.page_size % tcd::BK == 0) box = tcd::BK;
+    else if (tcd::BK % P.page_size == 0 && P.page_size >= 8) box = P.page_size;
+    if (box) mode = tcd::KM_PAGED;
+  }
+  if (mode == tcd::KM_DENSE || P.krows <= 0 || P.krows + tcd::BK >= ((int64_t)1 << 31) || ((uintptr_t)P.k & 15)) return tcd::KM_DENSE;
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return tcd::KM_DENSE;
+  const cuuint64_t gdim[2] = {(cuuint64_t)tcd::D, (cuuint64_t)P.krows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)tcd::D * 2};
+  const cuuint32_t bdim[2] = {64u, (cuuint32_t)box};
+  const cuuint32_t estr[2] = {1u, 1u};
+  if (enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void*)P.k, gdim, gstride, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return tcd::KM_DENSE;
+  *kbox = box;
+  return mode;
+}
+
 // Grid (segments, splits); writes split partials (P.pR ..) for every listed row. max_rows: the
 // most rows any segment holds (1..8; 8 when unknown).
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st) {
@@ -1129,13 +1420,16 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
   }
+  CUtensorMap tm;
+  int kbox = 0;
+  const int kmode = k_fetch_mode(P, &tm, &kbox);
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
   if (v == 0)
-    tcd::tc_decode_kernel<1><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+    tcd::tc_decode_kernel<1><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
   else if (v == 1)
-    tcd::tc_decode_kernel<2><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+    tcd::tc_decode_kernel<2><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
   else
-    tcd::tc_decode_kernel<tcd::RPT_MAX><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows);
+    tcd::tc_decode_kernel<tcd::RPT_MAX><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
   return cudaGetLastError();
 }
 
