@@ -97,9 +97,7 @@ constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
 constexpr int FW = 48, FV = 30;  // V: 30-bit window, 4 digits (very few values fall below it)
 constexpr float V_MAGIC = 12582912.0f;  // 1.5 x 2^23: y + V_MAGIC has y + 2^22 in its low 23 bits
 constexpr int THREADS = 512;
-constexpr int KW0 = 8, VW0 = 12;  // first K / V producer warp
-constexpr int NWGC = 2;           // consumer warpgroups (warps 0-7)
-constexpr int RPT_MAX = GD / NWGC;  // row slots per consumer thread for a full segment of GD rows
+constexpr int VW0 = 12;  // first V producer warp; the consumers take warps 0 .. NC - 1, the K producers NC .. 11
 constexpr uint32_t VLCAP = 2;
 constexpr int NQL = 4;  // dimensions whose k values the K producers keep for the consumers' bound
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
@@ -138,6 +136,7 @@ struct Small {
   int32_t ve[2][DV];   // running channel exponent VE_c (|v| < 2^VE_c so far), by tile parity
   int16_t ve4[2][DV];  // per key half maxima of the current tile (INT16_MIN: none)
   uint64_t td[256];    // binary64 2^(j/256) of the fast weight path
+  uint32_t kscan[2][BK][2];  // with two K threads a key: each half's largest magnitude and nonzero-minimum key
   int32_t qlk[NQL];    // the dimensions where some query row of the segment lost bits, ascending
   int32_t nqlk;        // their number, or -1 when there are more than NQL
   int32_t rows[GD];
@@ -363,12 +362,18 @@ __device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2
   p2 = __byte_perm(b, d, 0x5410);
 }
 
-// RPT: row slots per consumer thread (rows h, h + NWGC, ..): segments of at most NWGC RPT rows.
-// A smaller RPT keeps fewer running sums in registers (GQA groups of 2 need one slot).
-template <int RPT>
+// RPT: row slots per consumer thread (rows h, h + NWG, ..): segments of at most NWG RPT rows.
+// NC: consumer warps (8: two warpgroups, rows split between them; 4: one warpgroup with every row,
+// which leaves 8 K producer warps, two threads a key, for segments of at most 2 rows).
+template <int RPT, int NC>
 __global__ void __launch_bounds__(THREADS, 1)
     tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows, const __grid_constant__ CUtensorMap tmk, int kmode,
                      int kbox) {
+  constexpr int NWG = NC / 4;          // consumer warpgroups
+  constexpr int KW0 = NC;              // first K producer warp
+  constexpr int KWN = VW0 - NC;        // K producer warps: 4 or 8
+  constexpr int KH = KWN / 4;          // K threads a key (each takes D / KH dimensions)
+  constexpr int BLKS = 4 / KH;         // 32-dimension blocks a K thread slices
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* rawk = smem + OFF_RAWK;
   uint8_t* rawv = smem + OFF_RAWV;
@@ -427,7 +432,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   const int nrows = S.nrows;
   if (nrows == 0) return;  // uniform: an all-padding segment
-  if (nrows > NWGC * RPT) {
+  if (nrows > NWG * RPT) {
     // more rows than this instantiation keeps sums for (a launch error): every row of the segment
     // goes to the exact tier, and the run is flagged
     for (int i = tid; i < nrows * (DV + 1); i += THREADS) {
@@ -462,7 +467,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int npv = nrows <= 2 ? 16 : nrows <= 4 ? 32 : 48;
   if (warp == 0) tc::tmem_alloc(&S.tmem, TMEM_COLS);
   // the first two tiles' K (warp 11) and V (warp 15) fetches
-  if (warp == KW0 + 3)
+  if (warp == VW0 - 1)
     for (int t = 0; t < 2 && t < ntiles; ++t) {
       const int64_t j0 = kbeg + (int64_t)t * BK;
       const int64_t pref = kmode == KM_PAGED ? kbox_page(P, row0, j0, kend, kbox) : page_ahead(P, row0, j0, kend);
@@ -533,7 +538,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   unsigned n_exact = 0, n_wide = 0;
   bool ok_wait = true;
   const double am_d = (double)P.am;
-  // consumer state (rows h, h + NWGC, .. of channel c), live until the partials are written
+  // consumer state (rows h, h + NWG, .. of channel c), live until the partials are written
   const int h = warp >> 2, c = 32 * (warp & 3) + lane;
   // Fraction bits of this CTA's Z and N windows: the headroom only has to cover the split's own
   // keys (61 - ceil(log2 keys)), which keeps more bits than the row-wide P.FZ; the windows are
@@ -565,9 +570,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp >= KW0 && warp < VW0) {
     // ======================= K producers: one key per thread, digits into TMEM =======================
     const int kw = warp - KW0;
-    const int key = 32 * kw + lane;
+    const int khf = kw >> 2;  // which D / KH dimensions of the key this thread takes
+    const int key = 32 * (warp & 3) + lane;
     const int nqlk = max(S.nqlk, 0);
-    const uint32_t tq = tmem + ((uint32_t)(32 * kw) << 16);  // this warp's TMEM lane quadrant
+    const uint32_t tq = tmem + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's TMEM lane quadrant
     int waited = 0, issued = min(ntiles, 2);  // tiles [waited, issued) have fetches in flight
     bool mma_pend = false;
     uint32_t mma_ph = 0;
@@ -584,13 +590,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int64_t j0 = kbeg + (int64_t)i * BK;
       const int nvalid = (int)min((int64_t)BK, kend - j0);
       bool okw = tc::mbar_wait(&S.bar_rk[b], (uint32_t)(i >> 1) & 1u, P.wait_debug);
-      if (!group_sync_and(BAR_K, 128, okw && !*(volatile int*)&S.abort)) {
+      if (!group_sync_and(BAR_K, KWN * 32, okw && !*(volatile int*)&S.abort)) {
         ok_wait = false;
         break;
       }
       waited = i + 1;
       // page-table entries of tile i + 2, read now for its fetch below
-      if (warp == KW0 + 3 && i + 2 < ntiles)
+      if (warp == VW0 - 1 && i + 2 < ntiles)
         kpref = kmode == KM_PAGED ? kbox_page(P, row0, j0 + 2 * BK, kend, kbox) : page_ahead(P, row0, j0 + 2 * BK, kend);
       EA_PTK(0)
       const uint8_t* rawb = rawk + b * RAWK_BUF + rbase;
@@ -600,7 +606,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t mx0 = 0, mx1 = 0, mk0 = NZ_NONE, mk1 = NZ_NONE;
       if (valid) {
 #pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
+        for (int cc = khf * (16 / KH); cc < (khf + 1) * (16 / KH); ++cc) {
           const uint4 a = *(const uint4*)KCHUNK(cc);
           const uint32_t m0 = a.x & 0x7FFF7FFFu, m1 = a.y & 0x7FFF7FFFu;
           const uint32_t m2 = a.z & 0x7FFF7FFFu, m3 = a.w & 0x7FFF7FFFu;
@@ -612,7 +618,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       uint32_t mx = __vmaxu2(mx0, mx1);
       mx = max(mx & 0xFFFFu, mx >> 16);
-      const int32_t mn = nz_key_min(__vmins2(mk0, mk1));
+      int32_t mn = nz_key_min(__vmins2(mk0, mk1));
+      if (KH == 2) {  // the other half of the key, from its other thread
+        S.kscan[khf][key][0] = mx;
+        S.kscan[khf][key][1] = (uint32_t)mn;
+        group_sync(BAR_K, KWN * 32);
+        mx = max(mx, S.kscan[khf ^ 1][key][0]);
+        mn = min(mn, (int32_t)S.kscan[khf ^ 1][key][1]);
+      }
       const int bad = mx >= 0x7F80u;
       const int lead = (mx == 0 || bad) ? INT32_MIN : lead_of_bits(mx);
       const int lsb = lead == INT32_MIN ? 0 : lead + 1 - P.W;
@@ -623,7 +636,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the score MMAs of tile i - 1 are done reading the K digits in tensor memory
       if (i > 0) {
         okw = tc::mbar_wait(&S.bar_smma, (uint32_t)(i - 1) & 1u, P.wait_debug);
-        if (!group_sync_and(BAR_K, 128, okw)) {
+        if (!group_sync_and(BAR_K, KWN * 32, okw)) {
           ok_wait = false;
           break;
         }
@@ -637,7 +650,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // 2^-100 (lsb < -126) takes the integer conversion.
       const bool norm = lead == INT32_MIN || lsb >= -126;
 #pragma unroll 1
-      for (int blk = 0; blk < 4; ++blk) {
+      for (int blk = khf * BLKS; blk < (khf + 1) * BLKS; ++blk) {
         uint32_t pl[NK][8];
 #pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) {
@@ -670,7 +683,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!fast && valid) {
         const uint32_t thr = (uint32_t)max(ebase, 0) << 7;
 #pragma unroll 1
-        for (int cc = 0; cc < 16; ++cc) {
+        for (int cc = khf * (16 / KH); cc < (khf + 1) * (16 / KH); ++cc) {
           const uint4 a = *(const uint4*)KCHUNK(cc);
           const uint32_t w[4] = {a.x, a.y, a.z, a.w};
           uint32_t bits = 0;
@@ -683,13 +696,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) S.klossy[b][key][q] = lmk[q];
-      S.klsb[b][key] = (int16_t)lsb;
-      S.kbad[b][key] = (uint8_t)(valid && bad);
+      for (int q = 0; q < 4; ++q)
+        if (q / (4 / KH) == khf) S.klossy[b][key][q] = lmk[q];
+      if (khf == 0) {
+        S.klsb[b][key] = (int16_t)lsb;
+        S.kbad[b][key] = (uint8_t)(valid && bad);
+      }
       // the key's fixed-point values where some query row is lossy (the consumers' error bound)
       for (int n = 0; n < nqlk; ++n) {
         int lost = 0, b2 = 0;
         const int ii = S.qlk[n];
+        if (ii / (D / KH) != khf) continue;
         const uint32_t kb = valid ? *(const uint16_t*)(KCHUNK(ii >> 3) + 2 * (ii & 7)) : 0u;
         S.kqv[b][key][n] = lead == INT32_MIN ? 0 : fixq(kb, lsb, lost, b2);
       }
@@ -697,23 +714,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::fence_before_sync();
       EA_PTK(2)
       // every K thread is done with the raw rows of tile i: fetch tile i + 2 into them
-      group_sync(BAR_K, 128);
+      group_sync(BAR_K, KWN * 32);
       if (i + 2 < ntiles) {
-        if (warp == KW0 + 3)
+        if (warp == VW0 - 1)
           fetch_k(P, &tmk, kmode, kbox, row0, kvbase, j0 + 2 * BK, (int)min((int64_t)BK, kend - j0 - 2 * BK),
                   rawk + b * RAWK_BUF, &S.bar_rk[b], kpref);
         issued = i + 3;
       }
       // the consumers are done with the score accumulators of tile i - 1
       okw = i > 0 ? tc::mbar_wait(&S.bar_p1, (uint32_t)(i - 1) & 1u, P.wait_debug) : true;
-      if (!group_sync_and(BAR_K, 128, okw)) {
+      if (!group_sync_and(BAR_K, KWN * 32, okw)) {
         ok_wait = false;
         break;
       }
       EA_PTK(3)
       // score MMAs of tile i: key digit plane t (A in TMEM) by lane 0 of K warp t; an issuing
       // thread waits while the tensor core takes its operands, so four issuers share that wait
-      if (lane == 0) {
+      if (lane == 0 && kw < NK) {
         const int t = kw;
         tc::fence_after_sync();
         constexpr uint32_t lbo_b = (NSQ / 8) * 128;
@@ -945,14 +962,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int b = i & 1;
       {
         const bool okw = tc::mbar_wait(&S.bar_smma, ph, P.wait_debug);  // the score MMAs of tile i
-        if (!group_sync_and(BAR_C, 256, okw && !*(volatile int*)&S.abort)) {
+        if (!group_sync_and(BAR_C, NC * 32, okw && !*(volatile int*)&S.abort)) {
           ok_wait = false;
           break;
         }
       }
       tc::fence_after_sync();
       EA_PT(0)
-      // ---------------- pass 1: certified logits (lane: key; rows h, h + NWGC, ..) ----------------
+      // ---------------- pass 1: certified logits (lane: key; rows h, h + NWG, ..) ----------------
       bool unc = false;
       {
         const int key = c;
@@ -962,7 +979,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int klsb = S.klsb[b][key];
         const int nqlk = S.nqlk;
 #pragma unroll 1
-        for (int g = h; g < nrows; g += NWGC) {
+        for (int g = h; g < nrows; g += NWG) {
           uint32_t dg[NK][4];
 #pragma unroll
           for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + COL_S + 32 * t + 4 * g, dg[t]);
@@ -1047,12 +1064,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       tc::fence_before_sync();
-      const bool any_unc = group_sync_or(BAR_C, 256, unc);
+      const bool any_unc = group_sync_or(BAR_C, NC * 32, unc);
       if (tid == 0) mbar_arrive(&S.bar_p1);  // the score accumulators and the raw K rows are free
       EA_PT(1)
       // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
       if (any_unc) {
-        for (int e0 = 0; e0 < nrows * BK; e0 += THREADS / 2) {
+        for (int e0 = 0; e0 < nrows * BK; e0 += NC * 32) {
           const int e = e0 + warp * 32 + lane;
           const uint32_t hit = __ballot_sync(0xffffffffu, e < nrows * BK && sT[e] == T_UNCERT);
           for (uint32_t m = hit; m; m &= m - 1) {
@@ -1073,10 +1090,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
-        group_sync(BAR_C, 256);
+        group_sync(BAR_C, NC * 32);
         // the tile bounds again, now over the exact logits too
 #pragma unroll 1
-        for (int g = h; g < nrows; g += NWGC) {
+        for (int g = h; g < nrows; g += NWG) {
           const uint32_t tb = sT[g * BK + c];
           const float tf = __uint_as_float(tb);
           int32_t rl = INT32_MIN, ll = INT32_MAX;
@@ -1091,12 +1108,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             S.rtlo[warp & 3][g] = ll;
           }
         }
-        group_sync(BAR_C, 256);
+        group_sync(BAR_C, NC * 32);
       }
       EA_PT(2)
       // ---------------- pass 2: weights, W digits ----------------
 #pragma unroll 1
-      for (int g = h; g < nrows; g += NWGC) {
+      for (int g = h; g < nrows; g += NWG) {
         const int key = c;
         const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
         const uint32_t tb = sT[g * BK + key];
@@ -1155,7 +1172,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc::fence_async_smem();
       bool okw = tc::mbar_wait(&S.bar_vready, ph, P.wait_debug);  // the producers' value digits of tile i
-      if (!group_sync_and(BAR_C, 256, okw)) {
+      if (!group_sync_and(BAR_C, NC * 32, okw)) {
         ok_wait = false;
         break;
       }
@@ -1185,7 +1202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint64_t ztile[RPT];
 #pragma unroll
       for (int ii = 0; ii < RPT; ++ii) {
-        const int g = h + NWGC * ii;
+        const int g = h + NWG * ii;
         sh_base[ii] = INT32_MIN;
         ztile[ii] = 0;
         if (g >= nrows) continue;
@@ -1255,7 +1272,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---------------- drain: N[g][c] += sum_k 2^(8k) G_k - 2^30 Z_tile, G_k = sum_{u + w = k} D_u[w] ----------------
 #pragma unroll
       for (int ii = 0; ii < RPT; ++ii) {
-        const int g = h + NWGC * ii;
+        const int g = h + NWG * ii;
         if (g >= nrows) break;  // uniform across the warp
         uint32_t d0[8], d1[8], d2[8], d3[8];
         tc::tmem_ld8(tlane + COL_O + 6 * g, d0);
@@ -1281,7 +1298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         N[ii] += shift_floor128(T, sh_base[ii]);
       }
       tc::fence_before_sync();
-      if (!group_sync_and(BAR_C, 256, ok_pv)) {
+      if (!group_sync_and(BAR_C, NC * 32, ok_pv)) {
         ok_wait = false;
         break;
       }
@@ -1301,10 +1318,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc::fence_before_sync();
   __syncthreads();  // every role is done: row status (also set by the producers) is final
   // ---------------- split partials of this CTA's rows (after every role is done) ----------------
-  if (warp < KW0) {
+  if (warp < NC) {
 #pragma unroll
     for (int ii = 0; ii < RPT; ++ii) {
-      const int g = h + NWGC * ii;
+      const int g = h + NWG * ii;
       if (g >= nrows) break;
       const int32_t row = S.rows[g];
       if (row < 0) continue;
@@ -1404,19 +1421,19 @@ static int k_fetch_mode(const Prob& P, CUtensorMap* tm, int* kbox) {
 // Grid (segments, splits); writes split partials (P.pR ..) for every listed row. max_rows: the
 // most rows any segment holds (1..8; 8 when unknown).
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st) {
+  // 8 consumer warps with 1, 2 or 4 row slots (segments of <= 2, 4, 8 rows)
+  auto k0 = tcd::tc_decode_kernel<1, 8>;
+  auto k1 = tcd::tc_decode_kernel<2, 8>;
+  auto k2 = tcd::tc_decode_kernel<4, 8>;
+  const int v = max_rows <= 2 ? 0 : max_rows <= 4 ? 1 : 2;
+  auto kern = v == 0 ? k0 : v == 1 ? k1 : k2;
   // the shared-memory opt-in is a property of the function on a device: set it once per device
   // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
   static bool attr_set[64][3] = {};
-  const int v = max_rows <= tcd::NWGC ? 0 : max_rows <= 2 * tcd::NWGC ? 1 : 2;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
-    cudaError_t e = v == 0 ? cudaFuncSetAttribute(tcd::tc_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)tcd::SMEM_BYTES)
-                    : v == 1 ? cudaFuncSetAttribute(tcd::tc_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                    (int)tcd::SMEM_BYTES)
-                             : cudaFuncSetAttribute(tcd::tc_decode_kernel<tcd::RPT_MAX>,
-                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
   }
@@ -1424,12 +1441,7 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
   int kbox = 0;
   const int kmode = k_fetch_mode(P, &tm, &kbox);
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
-  if (v == 0)
-    tcd::tc_decode_kernel<1><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
-  else if (v == 1)
-    tcd::tc_decode_kernel<2><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
-  else
-    tcd::tc_decode_kernel<tcd::RPT_MAX><<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
+  kern<<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
   return cudaGetLastError();
 }
 
