@@ -48,7 +48,10 @@ constexpr uint32_t TMEM_COLS = 512;
 
 // shared memory map (bytes)
 constexpr uint32_t Q_PLANE = BM * D;         // 16384
-constexpr uint32_t K_PLANE = BN * D;         // 8192
+// K planes: the 16-byte K chunks of the 64 keys 1040 bytes apart (LBO), not 1024, so the 8 chunks
+// of one key row that a quarter warp stores land in 8 different bank groups
+constexpr uint32_t KLBO = (BN / 8) * 128 + 16;  // 1040
+constexpr uint32_t K_PLANE = (D / 16) * KLBO;   // 8320
 constexpr uint32_t V_PLANE = DV * BN;        // 8192
 constexpr uint32_t W_PLANE = BM * BN;        // 8192
 constexpr uint32_t OFF_Q = 0;
@@ -101,6 +104,18 @@ static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 __device__ unsigned long long g_phase_cycles[16];
 #endif
 
+// byte offset of (key j, byte k) in a K digit plane (the K-major layout with the padded LBO)
+__device__ __forceinline__ uint32_t koff(uint32_t j, uint32_t k) {
+  return (k >> 4) * KLBO + (j >> 3) * 128u + (j & 7u) * 16u + (k & 15u);
+}
+// int32 fixed-point value of key j's element k from the K digit planes
+__device__ __forceinline__ int32_t read_fix_k(const uint8_t* sK, uint32_t j, uint32_t k) {
+  const uint32_t o = koff(j, k);
+  const uint32_t b0 = sK[o], b1 = sK[o + K_PLANE], b2 = sK[o + 2 * K_PLANE];
+  const int32_t b3 = (int8_t)sK[o + 3 * K_PLANE];
+  return (int32_t)(b0 | (b1 << 8) | (b2 << 16)) + (b3 << 24);
+}
+
 // Truncation bound of one windowed score, in units 2^(qlsb + klsb): for the lossy elements only,
 // |q k - Q K| <= |dq| |k| + |Q| |dk| with |dq|, |dk| < 1 unit and |k| < |K| + 1 unit when k is lossy.
 __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, const uint8_t* sK, int r, int kj) {
@@ -109,7 +124,7 @@ __device__ __noinline__ uint64_t score_err(const Small& S, const uint8_t* sQ, co
     const uint32_t ql = S.qlossy[r][w], kl = S.klossy[kj][w];
     for (uint32_t m = ql; m; m &= m - 1) {
       int i = 32 * w + __ffs(m) - 1;
-      int32_t kf = read_fix(sK, K_PLANE, kj, i, BN);
+      int32_t kf = read_fix_k(sK, kj, i);
       err += (uint64_t)(kf < 0 ? -kf : kf) + ((kl >> (i & 31)) & 1u);
     }
     for (uint32_t m = kl; m; m &= m - 1) {
@@ -138,7 +153,7 @@ __device__ __noinline__ double score_corr(const Small& S, const uint8_t* sQ, con
       const double q = (double)__uint_as_float((uint32_t)qrow[i] << 16);
       const double k = (double)__uint_as_float((uint32_t)krow[i] << 16);
       const double Qs = (double)read_fix(sQ, Q_PLANE, r, i, BM) * pq;
-      const double Ks = (double)read_fix(sK, K_PLANE, kj, i, BN) * pk;
+      const double Ks = (double)read_fix_k(sK, kj, i) * pk;
       const double t = __fma_rn(Qs, k - Ks, (q - Qs) * k);
       c += t;
       a += fabs(t);
@@ -164,7 +179,7 @@ __device__ __forceinline__ bool score_corr_cached(const Small& S, const uint8_t*
     double dk = 0.0;
     for (int f = 0; f < nk; ++f)
       if (S.kc_i[kj][f] == i) dk = (double)S.kc_d[kj][f];
-    const double k = (double)read_fix(sK, K_PLANE, kj, i, BN) * pk + dk;  // the element itself, exact
+    const double k = (double)read_fix_k(sK, kj, i) * pk + dk;  // the element itself, exact
     const double Qs = dk != 0.0 ? (double)read_fix(sQ, Q_PLANE, r, i, BM) * pq : 0.0;
     const double t = __fma_rn(Qs, dk, (double)S.qc_d[r][e] * k);
     c += t;
@@ -442,7 +457,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
       uint4 pl[NK];
       planes16<NK>(x, pl);
 #pragma unroll
-      for (int p = 0; p < NK; ++p) *(uint4*)(sK + p * K_PLANE + tc::kmajor_off(j, 16 * e8, BN)) = pl[p];
+      for (int p = 0; p < NK; ++p) *(uint4*)(sK + p * K_PLANE + koff(j, 16 * e8)) = pl[p];
       const uint32_t other = __shfl_xor_sync(0xffffffffu, lmask, 1);
       if ((e8 & 1) == 0) S.klossy[j][e8 >> 1] = lmask | (other << 16);
       if (e8 == 0) {
@@ -465,7 +480,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const int i = 32 * w + __ffs(m) - 1;
           if (n < LCAP) {
             const double k = (double)__uint_as_float((uint32_t)P.k[(base + j0 + jj) * D + i] << 16);
-            S.kc_d[jj][n] = (float)(k - (double)read_fix(sK, K_PLANE, jj, i, BN) * pk);  // exact
+            S.kc_d[jj][n] = (float)(k - (double)read_fix_k(sK, jj, i) * pk);  // exact
             S.kc_i[jj][n] = (uint8_t)i;
           }
           ++n;
@@ -487,7 +502,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const uint32_t idesc = tc::idesc_i8(128, BN, s == NQ - 1, t == NK - 1);
           for (int ks = 0; ks < D / 32; ++ks) {
             uint64_t ad = tc::smem_desc(aq + s * Q_PLANE + ks * 2 * (BM / 8) * 128, (BM / 8) * 128, 128);
-            uint64_t bd = tc::smem_desc(bk + t * K_PLANE + ks * 2 * (BN / 8) * 128, (BN / 8) * 128, 128);
+            uint64_t bd = tc::smem_desc(bk + t * K_PLANE + ks * 2 * KLBO, KLBO, 128);
             tc::mma_i8(tmem + BN * g, ad, bd, idesc, !first);
             first = false;
           }
@@ -602,7 +617,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             for (int u = 0; u < 4; ++u) {
               const int kj = 16 * u4 + 4 * c4 + u;
               const int klsb = (int32_t)(int16_t)(S.kmeta[kj] & 0xFFFFu);
-              const double t = dq * ((double)read_fix(sK, K_PLANE, kj, i, BN) * __hiloint2double((klsb + 1023) << 20, 0));
+              const double t = dq * ((double)read_fix_k(sK, kj, i) * __hiloint2double((klsb + 1023) << 20, 0));
               cr[u] += t;  // dq K 2^klsb: exact products (at most 8 x 27 bits), one rounding per sum
               ca[u] += fabs(t);
             }
@@ -1072,7 +1087,8 @@ cudaError_t launch_tc_prefill(const Prob& P, const int32_t* block_rows, int64_t 
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(tck::tc_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tck::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(tck::tc_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tck::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
