@@ -414,12 +414,16 @@ def run_config(R: Runner, name: str, args, headline: bool) -> dict:
     from exactattention_b200 import cuda, workloads
 
     world, rank = R.world, R.rank
-    kv_sharded = name == "c5" and (world > 1 or bool(args.kv_shard))
+    # c5 at N > 1: KV-range shards merged over NCCL. --kv-shard K/N on one GPU: only that key range
+    # of every segment, through the single-GPU launch (a smaller case of the same kernel, e.g. for a
+    # profile; no merge, no hash check)
+    kv_sharded = name == "c5" and world > 1
+    one_shard = name == "c5" and world == 1 and bool(args.kv_shard) and headline
     ks, kn = rank, world
-    if args.kv_shard and headline:
+    if one_shard:
         ks, kn = (int(x) for x in args.kv_shard.split("/"))
     if name == "c5":
-        case = workloads.device_case(name, R.dev, shard=ks, nshards=kn) if kv_sharded else \
+        case = workloads.device_case(name, R.dev, shard=ks, nshards=kn) if (kv_sharded or one_shard) else \
             workloads.device_case(name, R.dev)
         r0, r1 = 0, case["cfg"].rows
     else:
