@@ -422,6 +422,54 @@ def test_config_sha(ea, name, splits):
     assert st[5] == case["cfg"].pairs
 
 
+@pytest.mark.parametrize("seqs", [(0, 9)])
+def test_config4_tree_equals_sequential_decode(ea, seqs):
+    """Config 4 (speculative tree verification): every node row of the listed sequences, computed
+    as one tree launch (the 8192-key prefix on the tensor-core prefill kernel, the ancestor lists
+    on the CUDA cores, merged), has the bits of one-token decoding along its root-to-node path:
+    the tensor-core decode kernel over the prefix and the path's keys gathered into contiguous
+    rows (the reference checks the same identity on its CPU kernel, test_cpu_kernel.py:77-104)."""
+    import torch
+
+    from exactattention_b200 import cuda, workloads as w
+
+    case = w.device_case("c4")
+    cfg, kw = case["cfg"], case["kw"]
+    st = torch.zeros(12, dtype=torch.int64, device="cuda")
+    tree, flags = cuda.launch(case["q"], case["k"], case["v"], cfg.alpha, splits=3, stats=st, **kw)
+    torch.cuda.synchronize()
+    assert not flags.any().item()
+    assert int(st[7].item()) >= cfg.rows * cfg.prefix  # the prefixes ran on the tensor cores
+    P, Tq, T = cfg.prefix, cfg.q_tokens, cfg.kv_tokens
+    dev = case["k"].device
+    for b in seqs:
+        # gathered key rows: (kv head, node) -> prefix + the node's path, at slot (kvh * Tq + x) * (P + 8)
+        span = P + 8
+        idx, kl = [], []
+        for kvh in range(w.HKV):
+            base = (b * w.HKV + kvh) * T
+            for x in range(Tq):
+                path = np.array(cfg.ancestors(b, x), np.int64)
+                keys = np.concatenate([np.arange(P), P + path]) + base
+                idx.append(np.pad(keys, (0, span - len(keys)), constant_values=base))
+                kl.append(len(keys))
+        idx = torch.from_numpy(np.concatenate(idx)).to(dev)
+        Kg, Vg = case["k"].index_select(0, idx), case["v"].index_select(0, idx)
+        rows = np.arange(b * w.HQ * Tq, (b + 1) * w.HQ * Tq)  # canonical order (b, h, node)
+        h, x = (rows // Tq) % w.HQ, rows % Tq
+        slot = (h // w.GROUP) * Tq + x
+        base_g = (slot * span).astype(np.int64)
+        len_g = np.array(kl, np.int64)[slot]
+        q = case["q"][torch.from_numpy(rows).to(dev)]
+        seq, f2 = cuda.launch(q, Kg, Vg, cfg.alpha, kv_base=torch.from_numpy(base_g).to(dev),
+                              kv_len=torch.from_numpy(len_g).to(dev), max_row_keys=span,
+                              segments=torch.from_numpy(cuda.row_segments(base_g)).to(dev), segment_width=2,
+                              splits=4)
+        torch.cuda.synchronize()
+        assert not f2.any().item()
+        assert torch.equal(seq, tree[torch.from_numpy(rows).to(dev)]), f"sequence {b}"
+
+
 # ---------------------------------------------------------------------------
 # tensor-core (tcgen05) prefill kernel
 # ---------------------------------------------------------------------------
