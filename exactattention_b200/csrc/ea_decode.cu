@@ -1047,12 +1047,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
           sT[g * BK + key] = out;
-          // tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1)
+          // tile bound of the certified logits: w = RN24(2^t) <= 2^(floor(t) + 1) < 2^(ceil(t) + 1);
+          // a logit of magnitude 2^30 or more sends the row to the wide tier (whose exponents hold it)
           const float tf = __uint_as_float(out);
           int32_t rl = INT32_MIN, ll = INT32_MAX;
-          if (out != T_MASKED && out != T_UNCERT && fabsf(tf) < 1073741824.0f) {
-            rl = __float2int_ru(tf) + 1;
-            ll = __float2int_rd(tf);
+          if (out != T_MASKED && out != T_UNCERT) {
+            if (fabsf(tf) < 1073741824.0f) {
+              rl = __float2int_ru(tf) + 1;
+              ll = __float2int_rd(tf);
+            } else {
+              atomicMax(&S.rst[g], ST_TIER3);
+            }
           }
           rl = __reduce_max_sync(0xffffffffu, rl);
           ll = __reduce_min_sync(0xffffffffu, ll);
@@ -1097,9 +1102,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t tb = sT[g * BK + c];
           const float tf = __uint_as_float(tb);
           int32_t rl = INT32_MIN, ll = INT32_MAX;
-          if (tb != T_MASKED && fabsf(tf) < 1073741824.0f) {
-            rl = __float2int_ru(tf) + 1;
-            ll = __float2int_rd(tf);
+          if (tb != T_MASKED) {
+            if (fabsf(tf) < 1073741824.0f) {
+              rl = __float2int_ru(tf) + 1;
+              ll = __float2int_rd(tf);
+            } else {
+              atomicMax(&S.rst[g], ST_TIER3);  // |t| >= 2^30: the wide tier
+            }
           }
           rl = __reduce_max_sync(0xffffffffu, rl);
           ll = __reduce_min_sync(0xffffffffu, ll);

@@ -686,6 +686,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           if (fabsf(tf) < 1073741824.0f) {  // false for the NaN markers
             tmax = fmaxf(tmax, tf);
             tmin = fminf(tmin, tf);
+          } else if (outv[u] != T_MASKED && outv[u] != T_UNCERT) {
+            rstat = max(rstat, (int)ST_TIER3);  // |t| >= 2^30: the wide tier (whose exponents hold it)
           }
           any_unc |= outv[u] == T_UNCERT;
         }
@@ -728,10 +730,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
         float tmax = -INFINITY;
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
-          const float tf = __uint_as_float(sT[r * T_PITCH + 16 * u4 + u]);
+          const uint32_t tb = sT[r * T_PITCH + 16 * u4 + u];
+          const float tf = __uint_as_float(tb);
           if (fabsf(tf) < 1073741824.0f) {
             tmax = fmaxf(tmax, tf);
             tlo = fminf(tlo, tf);
+          } else if (tb != T_MASKED && tb != T_UNCERT) {
+            atomicMax(&S.rst[r], ST_TIER3);  // |t| >= 2^30: the wide tier
           }
         }
         S.rt[u4][r] = tmax == -INFINITY ? INT32_MIN : __float2int_ru(tmax) + 1;

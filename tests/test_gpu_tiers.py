@@ -203,3 +203,82 @@ def test_config_with_forced_rows_keeps_sha(ea, hooks, name, stride, tier):
     print(f"{name} forced tier {tier}: clean {clean_ms:.2f} ms, with {forced} forced rows {forced_ms:.2f} ms")
     if name == "c5":
         assert forced_ms < 2 * clean_ms, (clean_ms, forced_ms)
+
+
+def _row(qhead, kheads, vcol, d=128):
+    """One query row whose leading elements are `qhead` against keys whose leading elements are
+    kheads[j] (the rest zero) and values v_j[0] = vcol[j], as bf16 bits."""
+    import exactattention_b200 as ea
+
+    q = np.zeros((1, d), np.float32)
+    k = np.zeros((len(kheads), d), np.float32)
+    v = np.zeros((len(kheads), d), np.float32)
+    q[0, :len(qhead)] = qhead
+    for j, kh in enumerate(kheads):
+        k[j, :len(kh)] = kh
+    v[:, 0] = vcol
+    return ea.float_to_bf16_bits(q), ea.float_to_bf16_bits(k), ea.float_to_bf16_bits(v)
+
+
+@pytest.mark.parametrize("route", ["prefill", "decode", "forced"])
+def test_logits_between_2_30_and_2_62_are_exact(ea, hooks, route):
+    """Logits of 2^30 .. 2^62 (weight exponents past int32) send their row from the tensor-core
+    kernels to the wide tier, which keeps them exactly: equal to the exact oracle, whether the
+    prefill kernel (row blocks) or the decode kernel (a segment) ran tier 1, or the row was
+    forced past tiers 1 and 2. Near 2^31 an fp32 logit moves in steps of 256, so two keys tie at
+    the top and the third lies ~520 binades below (under the reference's 2^20 spread limit)."""
+    import torch
+
+    from exactattention_b200 import cuda
+    from oracle import exact
+
+    alpha = ea.default_alpha(128)
+    Q, K, V = _row([2.0 ** 17, 1.0], [[2.0 ** 17, 0.0], [2.0 ** 17, 0.0], [2.0 ** 17, -4096.0]], [1.0, 3.0, -2.0])
+    Q = np.repeat(Q, 2, axis=0)  # a GQA pair of identical rows
+    kb, kl = np.zeros(2, np.int64), np.full(2, 3, np.int64)
+    sched = dict(blocks=_t(cuda.row_blocks(kb, kl))) if route == "prefill" else \
+        dict(segments=_t(cuda.row_segments(kb)), segment_width=2)
+    if route == "forced":
+        hooks(1, 2, 0)
+    st = torch.zeros(12, dtype=torch.int64, device="cuda")
+    out, flags = cuda.launch(_t(Q), _t(K), _t(V), alpha, kv_base=_t(kb), kv_len=_t(kl), max_row_keys=3, stats=st,
+                             **sched)
+    torch.cuda.synchronize()
+    hooks(0, 0, 0)
+    assert not flags.any().item()
+    exp = exact.attention(Q, K, V, alpha)
+    assert exp[0, 0] == 0x4000  # 2.0: the mean of the two tied keys' values
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), exp)
+    if route != "forced":
+        assert int(st[7].item()) == 6  # the pairs ran on the tensor cores first
+
+
+def test_logits_from_2_62_are_a_domain_error_here(ea):
+    """A documented limit of this build: the wide tier keeps weight exponents in int64, so a row
+    whose logits reach 2^62 (|q . k| around 2^63, far outside bf16 model activations) is flagged
+    as a domain error, where the reference's unbounded Python integers still return its value
+    (here 2.0, the mean of the three values)."""
+    from oracle import exact
+
+    alpha = ea.default_alpha(128)
+    Q, K, V = _row([2.0 ** 40], [[2.0 ** 40]] * 3, [1.0, 2.0, 3.0])
+    assert exact.attention(Q, K, V, alpha)[0, 0] == 0x4000  # the reference's answer: 2.0
+    with pytest.raises(ea.ExactAttentionDomainError):
+        ea.attention(Q, K, V, alpha)
+
+
+def test_weights_spanning_1300_binades_through_the_wide_tier(ea, hooks):
+    """A row whose weights span ~1300 binades (beyond the wide tier's exact 1536-bit window, under
+    the reference's 2^20 spread limit), forced through tier 3: the counted truncation still
+    certifies it, equal to the exact oracle."""
+    from oracle import exact
+
+    alpha = ea.default_alpha(128)
+    # t = alpha s: 0, about -326, 0.13 and -1306 for s = 0, -2560, 1, -10240 (alpha = 0.1275):
+    # weights 1, 2^-326, 2^0.13, 2^-1306, with the values 1, 2^100, 0.5, 2^-20 the terms span
+    # ~1330 binades
+    Q, K, V = _row([1.0], [[0.0], [-2560.0], [1.0], [-10240.0]], [1.0, 2.0 ** 100, 0.5, 2.0 ** -20])
+    hooks(1, 2, 0)
+    out = ea.attention(Q, K, V, alpha)
+    hooks(0, 0, 0)
+    assert np.array_equal(out, exact.attention(Q, K, V, alpha))
