@@ -1,10 +1,10 @@
 """Writes the golden fixtures under tests/golden/ from the reference itself.
 
-Run where a checkout of the reference repository is available (its path in EA_REFERENCE_DIR,
-default ../../../reference relative to this file):
+Run where a checkout of the reference repository is available; its path must be given in
+EA_REFERENCE_DIR (there is no default):
 
-    python tests/golden/make_golden.py            # small fixtures (seconds)
-    python tests/golden/make_golden.py --configs  # + SHA-256 of the full synthetic configs (minutes)
+    EA_REFERENCE_DIR=<checkout> python tests/golden/make_golden.py            # small fixtures (seconds)
+    EA_REFERENCE_DIR=<checkout> python tests/golden/make_golden.py --configs  # + SHA-256 of the full synthetic configs (minutes)
 
 Outputs
   c1.npz              config 1 (README example): inputs and the reference's exact output
@@ -30,7 +30,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.abspath(os.path.join(HERE, "..", ".."))
-REF = os.environ.get("EA_REFERENCE_DIR", os.path.abspath(os.path.join(REPO, "..", "reference")))
+REF = os.environ.get("EA_REFERENCE_DIR", "")
+if not REF or not os.path.isdir(os.path.join(REF, "src", "exactattn")):
+    sys.exit("make_golden.py: set EA_REFERENCE_DIR to a checkout of the reference repository")
+REF = os.path.abspath(REF)
 sys.path.insert(0, os.path.join(REF, "src"))
 sys.path.insert(0, os.path.join(REF, "tests"))
 sys.path.insert(0, REPO)
