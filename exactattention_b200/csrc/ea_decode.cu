@@ -66,7 +66,7 @@ __device__ unsigned long long g_phase_cycles[16];
 #define EA_PT_DECL                    \
   unsigned long long* ea_pt_acc = S.pt_acc; \
   if (threadIdx.x < 16) ea_pt_acc[threadIdx.x] = 0;
-// K producers (thread 256) keep counters 8-11, V producers (thread 384) counters 12-15
+// K producers (thread 256) keep counters 8-11, V producers (their first thread) counters 12-15
 #define EA_PTK_INIT long long ptk_last = clock64();
 #define EA_PTK(i)                          \
   if (tid == 256) {                        \
@@ -76,7 +76,7 @@ __device__ unsigned long long g_phase_cycles[16];
   }
 #define EA_PTV_INIT long long ptv_last = clock64();
 #define EA_PTV(i)                           \
-  if (tid == 384) {                         \
+  if (tid == VW0 * 32) {                    \
     const long long pt_now = clock64();     \
     ea_pt_acc[12 + (i)] += pt_now - ptv_last; \
     ptv_last = pt_now;                      \
@@ -96,8 +96,13 @@ constexpr int BK = 128, D = 128, DV = 128, GD = 8;
 constexpr int NQ = 4, NK = 4, NW = 6, NV = 4;
 constexpr int FW = 48, FV = 30;  // V: 30-bit window, 4 digits (very few values fall below it)
 constexpr float V_MAGIC = 12582912.0f;  // 1.5 x 2^23: y + V_MAGIC has y + 2^22 in its low 23 bits
-constexpr int THREADS = 512;
-constexpr int VW0 = 12;  // first V producer warp; the consumers take warps 0 .. NC - 1, the K producers NC .. 11
+// warps: consumers 0 .. NC - 1, K producers NC .. NC + KW - 1, V producers the last four
+template <int NC, int KW>
+__host__ __device__ constexpr int threads_of() { return 32 * (NC + KW + 4); }
+// registers a thread of each role keeps with 8 K producer warps (640 threads, 96 registers a
+// thread at launch): the producer warpgroups give registers back to the consumers
+constexpr int REG_CONSUMER = 128, REG_PRODUCER = 72, REG_LAUNCH = 96;
+constexpr int REG_SPLIT = 256 * REG_CONSUMER + 384 * REG_PRODUCER;
 constexpr uint32_t VLCAP = 2;
 constexpr int NQL = 4;  // dimensions whose k values the K producers keep for the consumers' bound
 constexpr uint32_t VL_BOUNDED = 1u << 20;  // marks a channel without digits (all values bounded)
@@ -105,9 +110,13 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSQ = NQ * GD;  // score B rows: n = 4 g + s
 constexpr int NSW = NW * GD;  // P.V B rows: n = 6 g + w
 // TMEM columns: K digit planes (A of the scores; plane t at COL_K + 32 t, 4 bytes a column),
-// score accumulators (plane t at COL_S + 32 t + n), P.V accumulators (plane u at COL_O + 48 u + n)
+// score accumulators (plane t at COL_S + 32 t + n), P.V accumulators (plane u at COL_O + 48 u + n).
+// Segments of at most two rows (N = 8 score columns a plane) double-buffer the K digits and the
+// score accumulators instead: K buffer b at 128 b, scores of buffer b at 256 + 32 b + 8 t + n,
+// P.V accumulators at 320 + 48 u + n.
 constexpr uint32_t COL_K = 0, COL_S = 128, COL_O = 256;
-static_assert(COL_O + NV * NSW <= TMEM_COLS, "tensor memory budget");
+constexpr uint32_t DB_COL_S = 256, DB_COL_O = 320;
+static_assert(COL_O + NV * NSW <= TMEM_COLS && DB_COL_O + NV * NSW <= TMEM_COLS, "tensor memory budget");
 
 constexpr uint32_t RAWK_BUF = BK * D * 2;   // 32768: two swizzled halves of 128 x 128 bytes, or 128 dense rows
 constexpr uint32_t KHALF = BK * 128;         // 16384
@@ -137,6 +146,7 @@ struct Small {
   int16_t ve4[2][DV];  // per key half maxima of the current tile (INT16_MIN: none)
   uint64_t td[256];    // binary64 2^(j/256) of the fast weight path
   uint32_t kscan[2][BK][2];  // with two K threads a key: each half's largest magnitude and nonzero-minimum key
+  int64_t qsum[GD];    // per query row: the sum of its fixed-point elements (Toeplitz layout)
   int32_t qlk[NQL];    // the dimensions where some query row of the segment lost bits, ascending
   int32_t nqlk;        // their number, or -1 when there are more than NQL
   int32_t rows[GD];
@@ -150,7 +160,8 @@ struct Small {
   uint32_t zl[4][GD];
   // raw K / V tiles landed (per buffer); score MMAs done; pass 1 done; value digits and channel
   // data ready; P.V MMAs done
-  uint64_t bar_rk[2], bar_rv[2], bar_smma, bar_p1, bar_vready, bar_pv;
+  // (score MMAs / pass 1 by score buffer: one buffer, or two for double-buffered segments)
+  uint64_t bar_rk[2], bar_rv[2], bar_smma[2], bar_p1[2], bar_vready, bar_pv;
   int32_t abort;  // a bounded wait gave up in some role
   uint32_t tmem;
 #ifdef EA_PHASE_TIMERS
@@ -163,6 +174,36 @@ struct Small {
 
 constexpr uint32_t SMEM_BYTES = OFF_SMALL + sizeof(Small);
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+// The Toeplitz layout (segments of at most two rows, 8 K producer warps). Every element stays one
+// 32-bit word whose four bytes are its unsigned digits: a key element x (|x| < 2^27) as x + 2^27,
+// a value element x (|x| < 2^30) as x + 2^30. An MMA's K dimension runs over (element, byte): key
+// (or channel) r's A row holds its elements' words in tensor memory, one element a column. The B
+// tiles hold the other operand's digits shifted per output column: score column (g, k) holds, at
+// byte u of dimension i, query digit Q_(k-u)[g][i] (zero outside 0..3), so the accumulator of
+// column k is the digit group G_k = sum_(t + s = k) K_t . Q_s (k = 0..6) and no byte transposes
+// are needed on either side; the P.V tile likewise holds weight digit W_(k-u) at byte u of key j
+// (k = 0..8). The biases come out exactly: 2^27 times the row's query sum, 2^30 times the tile's
+// weight sum. B tiles use the 128-byte swizzle (conflict-free word stores).
+// Shared memory: raw K / V staging as above, score B tile (16 rows: n = 8 g + k), P.V B tile (32
+// rows: n = 16 g + k), logits, the rows' fixed-point query elements and the tile's weights.
+constexpr uint32_t T_QROWS = 16, T_WROWS = 32, T_KB = 512;  // B rows, K bytes of a B row
+constexpr uint32_t T_OFF_QT = OFF_RAWV + 2 * RAWV_BUF;
+constexpr uint32_t T_OFF_WT = T_OFF_QT + T_QROWS * T_KB;
+constexpr uint32_t T_OFF_T = T_OFF_WT + T_WROWS * T_KB;
+constexpr uint32_t T_OFF_QF = T_OFF_T + GD * BK * 4;
+constexpr uint32_t T_OFF_WV = T_OFF_QF + 2 * D * 4;
+constexpr uint32_t T_OFF_SMALL = T_OFF_WV + 2 * BK * 8;
+constexpr uint32_t T_SMEM_BYTES = T_OFF_SMALL + sizeof(Small);
+static_assert(T_SMEM_BYTES <= 227 * 1024 && T_OFF_QT % 1024 == 0 && T_OFF_WT % 1024 == 0, "Toeplitz layout");
+// Tensor memory (Toeplitz layout): K words at 0 (a dimension a column; one buffer); score
+// accumulators of buffer b at 128 + 64 b, four of them 16 columns apart (n = 8 g + k); the four
+// P.V accumulators at 256 + 32 a (n = 16 g + k); V words at 384 (a key a column, channel c in
+// lane c). Each MMA group (16 K steps of 8 elements x 4 bytes) is issued by four threads, four
+// consecutive K steps each into an accumulator of its own: a tcgen05.mma costs its issuing
+// thread tens of cycles, and separate issuers overlap.
+constexpr uint32_t T_COL_S = 128, T_COL_O = 256, T_COL_V = 384;
+constexpr uint32_t V_BIAS = 1u << 30;  // (the K bias is 2^W, W the launch's window bits)
 static_assert(OFF_V % 1024 == 0 && OFF_Q % 16 == 0 && OFF_W % 16 == 0 && OFF_RAWV % 1024 == 0, "operand alignment");
 // K fetch modes: 0 dense bulk copies of contiguous runs; 1 RANGE through the tensor map (one box
 // of 128 rows per half); 2 PAGED through the tensor map (boxes of `kbox` rows, a page or a
@@ -363,25 +404,48 @@ __device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2
 }
 
 // RPT: row slots per consumer thread (rows h, h + NWG, ..): segments of at most NWG RPT rows.
-// NC: consumer warps (8: two warpgroups, rows split between them; 4: one warpgroup with every row,
-// which leaves 8 K producer warps, two threads a key, for segments of at most 2 rows).
-template <int RPT, int NC>
-__global__ void __launch_bounds__(THREADS, 1)
+// NC: consumer warps (8: two warpgroups, rows split between them; 4: one warpgroup with every row).
+// KW: K producer warps (4: one thread a key; 8: two threads a key, each half the dimensions).
+// With 8 consumer and 8 K warps the block has 640 threads and rebalances registers per role
+// (setmaxnreg): the launch gives 96 a thread, the producers drop to REG_PRODUCER and the consumers
+// rise to REG_CONSUMER (256 x 128 + 384 x 72 = 60,416 <= 640 x 96 = 61,440).
+template <int RPT, int NC, int KW>
+__global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows, const __grid_constant__ CUtensorMap tmk, int kmode,
                      int kbox) {
+  constexpr int THREADS = threads_of<NC, KW>();
+  constexpr bool REBAL = THREADS > 512;  // per-role registers
+  static_assert(!REBAL || (NC == 8 && KW == 8 && REG_SPLIT <= THREADS * REG_LAUNCH), "register split");
   constexpr int NWG = NC / 4;          // consumer warpgroups
   constexpr int KW0 = NC;              // first K producer warp
-  constexpr int KWN = VW0 - NC;        // K producer warps: 4 or 8
+  constexpr int VW0 = NC + KW;         // first V producer warp
+  constexpr int KWN = KW;              // K producer warps: 4 or 8
   constexpr int KH = KWN / 4;          // K threads a key (each takes D / KH dimensions)
   constexpr int BLKS = 4 / KH;         // 32-dimension blocks a K thread slices
+  // One row slot (segments of <= 2 rows): the K digits and the score accumulators are double-
+  // buffered in tensor memory, so the K producers run up to two tiles ahead of the consumers'
+  // pass 1 instead of one. Tile i uses score buffer sbuf(i) and that buffer's barrier phase
+  // spar(i).
+  constexpr bool DB = RPT == 1;
+  // the 640-thread instantiation uses the Toeplitz layout (K and V words in tensor memory)
+  constexpr bool TOEP = REBAL;
+  static_assert(!TOEP || DB, "Toeplitz layout: segments of at most two rows");
+  constexpr uint32_t SPL = DB ? 8u : 32u;  // score accumulator columns a key digit plane
+  constexpr uint32_t COLO = TOEP ? T_COL_O : DB ? DB_COL_O : COL_O;
+  auto sbuf = [](int i) { return DB ? (i & 1) : 0; };
+  auto spar = [](int i) { return (uint32_t)(DB ? (i >> 1) & 1 : i & 1); };
+  auto col_k = [](int b) { return TOEP ? 0u : DB ? 128u * (uint32_t)b : COL_K; };
+  auto col_s = [](int b) { return TOEP ? T_COL_S + 64u * (uint32_t)b : DB ? DB_COL_S + 32u * (uint32_t)b : COL_S; };
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* rawk = smem + OFF_RAWK;
   uint8_t* rawv = smem + OFF_RAWV;
-  uint8_t* sV = smem + OFF_V;
-  uint8_t* sQ = smem + OFF_Q;
-  uint8_t* sW = smem + OFF_W;
-  uint32_t* sT = (uint32_t*)(smem + OFF_T);
-  Small& S = *(Small*)(smem + OFF_SMALL);
+  uint8_t* sV = smem + OFF_V;  // (not in the Toeplitz layout)
+  uint8_t* sQ = smem + (TOEP ? T_OFF_QT : OFF_Q);
+  uint8_t* sW = smem + (TOEP ? T_OFF_WT : OFF_W);
+  uint32_t* sT = (uint32_t*)(smem + (TOEP ? T_OFF_T : OFF_T));
+  int32_t* qfx = (int32_t*)(smem + T_OFF_QF);    // Toeplitz: the rows' fixed-point query elements
+  uint64_t* wval = (uint64_t*)(smem + T_OFF_WV);  // Toeplitz: the tile's weights W[g][key]
+  Small& S = *(Small*)(smem + (TOEP ? T_OFF_SMALL : OFF_SMALL));
   EA_PT_DECL
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -404,15 +468,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   for (int i = tid; i < DV; i += THREADS) S.ve[0][i] = S.ve[1][i] = INT32_MIN;
   for (int i = tid; i < GD * BK; i += THREADS) sT[i] = T_MASKED;
+  if (TOEP)  // both B tiles start zero (the unused digit positions and rows stay zero)
+    for (int i = tid; i < (int)((T_QROWS + T_WROWS) * T_KB / 16); i += THREADS) ((uint4*)sQ)[i] = make_uint4(0, 0, 0, 0);
   if (tid < 256) S.td[tid] = f64::g_exp2_d64[tid];
   if (tid == 0) {
     tc::mbar_init(&S.bar_rk[0], 1);
     tc::mbar_init(&S.bar_rk[1], 1);
     tc::mbar_init(&S.bar_rv[0], 1);
     tc::mbar_init(&S.bar_rv[1], 1);
-    tc::mbar_init(&S.bar_smma, NK);  // one commit per key digit's issuer
-    tc::mbar_init(&S.bar_pv, NV);    // one commit per value digit's issuer
-    tc::mbar_init(&S.bar_p1, 1);
+    // one commit per issuer (a key / value digit, or in the Toeplitz layout four K steps)
+    tc::mbar_init(&S.bar_smma[0], NK);
+    tc::mbar_init(&S.bar_smma[1], NK);
+    tc::mbar_init(&S.bar_pv, NV);
+    tc::mbar_init(&S.bar_p1[0], 1);
+    tc::mbar_init(&S.bar_p1[1], 1);
     tc::mbar_init(&S.bar_vready, 1);
     S.abort = 0;
   }
@@ -432,9 +501,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   const int nrows = S.nrows;
   if (nrows == 0) return;  // uniform: an all-padding segment
-  if (nrows > NWG * RPT) {
-    // more rows than this instantiation keeps sums for (a launch error): every row of the segment
-    // goes to the exact tier, and the run is flagged
+  if (nrows > NWG * RPT || (TOEP && (tc::smem_u32(smem) & 1023u))) {
+    // more rows than this instantiation keeps sums for, or swizzled tiles off their 1024-byte
+    // alignment (a launch error): every row of the segment goes to the exact tier, and the run
+    // is flagged
     for (int i = tid; i < nrows * (DV + 1); i += THREADS) {
       const int g = i / (DV + 1), ch = i % (DV + 1);
       const int32_t row = S.rows[g];
@@ -481,8 +551,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 
   // ---------------- query rows -> balanced digit planes (warp g: row g) ----------------
-  if (warp < GD) {
+  if (TOEP ? warp < 2 : warp < GD) {
     const int g = warp;
+    int64_t qs = 0;  // the row's fixed-point sum (Toeplitz)
     const int32_t row = S.rows[g];
     uint32_t bits[4];
     int lead = INT32_MIN, bad = 0;
@@ -505,14 +576,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) S.qlossy[g][m4] = lm;
       // balanced base-256 digits: x = sum_s d_s 256^s, d_s in [-128, 127] (|x| < 2^28)
       int32_t y = x;
+      uint32_t dq = 0;  // the four digits as bytes
 #pragma unroll
       for (int s = 0; s < NQ; ++s) {
         const int32_t dg = s == NQ - 1 ? y : (int32_t)(int8_t)(y & 0xFF);
-        sQ[tc::kmajor_off(4 * g + s, i, NSQ)] = (uint8_t)(int8_t)dg;
+        if (TOEP) dq |= (uint32_t)(uint8_t)(int8_t)dg << (8 * s);
+        else sQ[tc::kmajor_off(4 * g + s, i, NSQ)] = (uint8_t)(int8_t)dg;
         y = (y - dg) >> 8;
       }
+      if (TOEP) {
+        // score B row (g, k), bytes 4 i .. 4 i + 3: digits Q_k, Q_(k-1), Q_(k-2), Q_(k-3) (zero
+        // outside 0..3)
+        const uint32_t sel[7] = {0x4440u, 0x4401u, 0x4012u, 0x0123u, 0x1234u, 0x2344u, 0x3444u};
+#pragma unroll
+        for (int k = 0; k < 7; ++k)
+          *(uint32_t*)(sQ + tc::sw128_off(8 * g + k, 4 * i, T_QROWS)) = __byte_perm(dq, 0u, sel[k]);
+        qfx[g * D + i] = x;
+        qs += x;
+      }
+    }
+    if (TOEP) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
     }
     if (lane == 0) {
+      if (TOEP) S.qsum[g] = qs;
       S.qlsb[g] = lsb;
       if (bad && row >= 0) S.rst[g] = ST_DOMAIN;
     }
@@ -569,14 +657,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp >= KW0 && warp < VW0) {
     // ======================= K producers: one key per thread, digits into TMEM =======================
+    if (REBAL) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
     const int kw = warp - KW0;
     const int khf = kw >> 2;  // which D / KH dimensions of the key this thread takes
     const int key = 32 * (warp & 3) + lane;
     const int nqlk = max(S.nqlk, 0);
+    const uint32_t kbias = 1u << P.W;  // Toeplitz: key words x + 2^W (|x| < 2^W)
     const uint32_t tq = tmem + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's TMEM lane quadrant
     int waited = 0, issued = min(ntiles, 2);  // tiles [waited, issued) have fetches in flight
     bool mma_pend = false;
-    uint32_t mma_ph = 0;
+    int mma_last = 0;  // the last tile whose score MMAs this role issued
     // byte offset of 16-byte chunk c (dims 8c .. 8c + 7) of this thread's raw row: in the swizzled
     // halves (c / 8) * KHALF + 128 key + ((c % 8) ^ (key % 8)) 16, in dense rows 256 key + 16 c
     const bool swz = kmode != KM_DENSE;
@@ -633,14 +723,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool fast = lead == INT32_MIN || (lsb >= -126 && lsb <= 126 &&
                                               (mn == 32767 || nz_key_mag(mn) >= ((uint32_t)ebase << 7)));
       const float sc = scale_of(max(-126, min(126, lsb)));
-      // the score MMAs of tile i - 1 are done reading the K digits in tensor memory
-      if (i > 0) {
-        okw = tc::mbar_wait(&S.bar_smma, (uint32_t)(i - 1) & 1u, P.wait_debug);
+      // one K buffer: the score MMAs of tile i - 1 are done reading the K digits in tensor
+      // memory; two score buffers: the consumers' pass 1 of tile i - 2 is done (so are its score
+      // MMAs, and its score accumulators and key metadata slot are free)
+      if (i > 0 && (!DB || TOEP || i >= 2)) {
+        okw = true;
+        if (DB && i >= 2) okw = tc::mbar_wait(&S.bar_p1[b], spar(i - 2), P.wait_debug);
+        if (!DB || TOEP) okw = okw && tc::mbar_wait(&S.bar_smma[sbuf(i - 1)], spar(i - 1), P.wait_debug);
         if (!group_sync_and(BAR_K, KWN * 32, okw)) {
           ok_wait = false;
           break;
         }
-        mma_pend = false;
+        if (!DB) mma_pend = false;
       }
       tc::fence_after_sync();
       EA_PTK(1)
@@ -671,12 +765,20 @@ __global__ void __launch_bounds__(THREADS, 1)
               xs[e] = (uint32_t)fixq((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, lsb, lost, b2);
             }
           }
-          transpose4(xs[0], xs[1], xs[2], xs[3], pl[0][2 * g4], pl[1][2 * g4], pl[2][2 * g4], pl[3][2 * g4]);
-          transpose4(xs[4], xs[5], xs[6], xs[7], pl[0][2 * g4 + 1], pl[1][2 * g4 + 1], pl[2][2 * g4 + 1],
-                     pl[3][2 * g4 + 1]);
-        }
+          if (TOEP) {  // the words x + 2^W of dimensions 8 (4 blk + g4) .. + 7, one a column
 #pragma unroll
-        for (int t = 0; t < NK; ++t) tc::tmem_st8(tq + COL_K + 32 * t + 8 * blk, pl[t]);
+            for (int e = 0; e < 8; ++e) xs[e] += kbias;
+            tc::tmem_st8(tq + col_k(b) + 8 * (4 * blk + g4), xs);
+          } else {
+            transpose4(xs[0], xs[1], xs[2], xs[3], pl[0][2 * g4], pl[1][2 * g4], pl[2][2 * g4], pl[3][2 * g4]);
+            transpose4(xs[4], xs[5], xs[6], xs[7], pl[0][2 * g4 + 1], pl[1][2 * g4 + 1], pl[2][2 * g4 + 1],
+                       pl[3][2 * g4 + 1]);
+          }
+        }
+        if (!TOEP) {
+#pragma unroll
+          for (int t = 0; t < NK; ++t) tc::tmem_st8(tq + col_k(b) + 32 * t + 8 * blk, pl[t]);
+        }
       }
       // the elements that lost bits (exponent field below ebase), for the consumers' error bound
       uint32_t lmk[4] = {0u, 0u, 0u, 0u};
@@ -721,16 +823,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                   rawk + b * RAWK_BUF, &S.bar_rk[b], kpref);
         issued = i + 3;
       }
-      // the consumers are done with the score accumulators of tile i - 1
-      okw = i > 0 ? tc::mbar_wait(&S.bar_p1, (uint32_t)(i - 1) & 1u, P.wait_debug) : true;
-      if (!group_sync_and(BAR_K, KWN * 32, okw)) {
-        ok_wait = false;
-        break;
+      // one buffer: the consumers are done with the score accumulators of tile i - 1
+      if (!DB) {
+        okw = i > 0 ? tc::mbar_wait(&S.bar_p1[0], spar(i - 1), P.wait_debug) : true;
+        if (!group_sync_and(BAR_K, KWN * 32, okw)) {
+          ok_wait = false;
+          break;
+        }
       }
       EA_PTK(3)
-      // score MMAs of tile i: key digit plane t (A in TMEM) by lane 0 of K warp t; an issuing
-      // thread waits while the tensor core takes its operands, so four issuers share that wait
-      if (lane == 0 && kw < NK) {
+      if (TOEP) {
+        // score MMAs of tile i: lane 0 of K warp a issues K steps 4 a .. 4 a + 3 (dimensions
+        // 32 a .. 32 a + 31) into score accumulator a (N = 8 columns a row)
+        if (lane == 0 && kw < NK) {
+          tc::fence_after_sync();
+          const uint32_t idesc = tc::idesc_i8(128, 8 * nrows, false, true);
+          const uint32_t qa = tc::smem_u32(sQ);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int ks = 4 * kw + j;
+            tc::mma_i8_tmem_a(tmem + col_s(b) + 16 * kw, tmem + col_k(b) + 8 * ks,
+                              tc::smem_desc_sw128(qa + (ks >> 2) * (T_QROWS / 8) * 1024 + (ks & 3) * 32, 1024), idesc,
+                              j > 0);
+          }
+          tc::mma_commit(tc::smem_u32(&S.bar_smma[sbuf(i)]));
+        }
+      } else if (lane == 0 && kw < NK) {
+        // score MMAs of tile i: key digit plane t (A in TMEM) by lane 0 of K warp t; an issuing
+        // thread waits while the tensor core takes its operands, so four issuers share that wait
         const int t = kw;
         tc::fence_after_sync();
         constexpr uint32_t lbo_b = (NSQ / 8) * 128;
@@ -738,21 +858,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t idesc = tc::idesc_i8(128, nsq, t == NK - 1, true);
 #pragma unroll
         for (int ks = 0; ks < D / 32; ++ks)
-          tc::mma_i8_tmem_a(tmem + COL_S + 32 * t, tmem + COL_K + 32 * t + 8 * ks, bd0 + ((ks * 2 * lbo_b) >> 4),
-                            idesc, ks > 0);
-        tc::mma_commit(tc::smem_u32(&S.bar_smma));
+          tc::mma_i8_tmem_a(tmem + col_s(b) + SPL * t, tmem + col_k(b) + 32 * t + 8 * ks,
+                            bd0 + ((ks * 2 * lbo_b) >> 4), idesc, ks > 0);
+        tc::mma_commit(tc::smem_u32(&S.bar_smma[sbuf(i)]));
       }
       mma_pend = true;
-      mma_ph = (uint32_t)i & 1u;
+      mma_last = i;
     }
 #undef KCHUNK
     EA_PT_FLUSH_RANGE(256, 8, 12)
     if (!ok_wait) S.abort = 1;
     // what this role still has in flight gets a bounded wait before shared and tensor memory go
     for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rk[t & 1], (uint32_t)(t >> 1) & 1u, P.wait_debug);
-    if (mma_pend) tc::mbar_wait(&S.bar_smma, mma_ph, P.wait_debug);
-  } else if (warp >= VW0) {
+    // (each issuer's commit covers its earlier MMAs: the last tile's phase covers every tile)
+    if (mma_pend) tc::mbar_wait(&S.bar_smma[sbuf(mma_last)], spar(mma_last), P.wait_debug);
+  } else if (warp >= VW0 && warp < VW0 + 4) {
     // ======================= V producers: value digits into shared memory =======================
+    if (REBAL) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
     const int vt = tid - VW0 * 32;
     const int cp = vt & 63, kh = vt >> 6;  // channels 2 cp, 2 cp + 1; keys 64 kh .. 64 kh + 63
     // Slot s of this thread holds channel 2 cp + (s ^ swp): a quarter warp's digit stores then
@@ -828,9 +950,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         S.ve4[kh][2 * cp + h] = (int16_t)(m == 0 ? INT16_MIN : lead_of_bits(m) + 1);
       }
-      S.vl_n[par][vt] = 0;
       group_sync(BAR_V, 128);
       EA_PTV(1)
+      // the P.V MMAs of tile i - 1 are done reading the value digits; the consumers, who issued
+      // them after finishing tile i - 2, are also done with this parity's channel data
+      if (i > 0) {
+        okw = tc::mbar_wait(&S.bar_pv, (uint32_t)(i - 1) & 1u, P.wait_debug);
+        if (!group_sync_and(BAR_V, 128, okw)) {
+          ok_wait = false;
+          break;
+        }
+      }
+      EA_PTV(2)
       // running exponents of this thread's channels: the previous tiles' and this tile's
       int lsbh[2], keeph[2];
 #pragma unroll
@@ -844,64 +975,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // a channel whose maximum lies at the very bottom of the bf16 range keeps no digits
         keeph[h] = (ve == INT32_MIN || lsbh[h] >= -126) ? 1 : 0;
       }
-      // per slot: the channel, the byte permute that places its bf16 in the high half of a zero
-      // word (all zero without digits), and the scales of the two fused multiply-adds
-      int chs[2];
-      uint32_t sels[2];
-      float schi[2], sclo[2], clampv[2];
-#pragma unroll
-      for (int sl = 0; sl < 2; ++sl) {
-        const int h = sl ^ swp;
-        const int keep = h ? keeph[1] : keeph[0];
-        const int l = keep ? (h ? lsbh[1] : lsbh[0]) : 0;
-        chs[sl] = 2 * cp + h;
-        sels[sl] = keep ? (h ? 0x3244u : 0x1044u) : 0x4444u;
-        schi[sl] = scale_of(l + 8);       // 2^-(lsb + 8): the high part floor(x / 256)
-        sclo[sl] = scale_of(l);           // 2^-lsb
-        clampv[sl] = scale_of(-(l + 15));  // 2^(lsb + 15): above it x is a multiple of 256
-      }
-      // the P.V MMAs of tile i - 1 are done reading the value digit planes
-      if (i > 0) {
-        okw = tc::mbar_wait(&S.bar_pv, (uint32_t)(i - 1) & 1u, P.wait_debug);
-        if (!group_sync_and(BAR_V, 128, okw)) {
-          ok_wait = false;
-          break;
-        }
-      }
-      EA_PTV(2)
-      // Digits of x = floor(v 2^-lsb) (|x| < 2^30) = 256 h + l: fmaf_rz(v, 2^-(lsb + 8), 1.5 2^23) is
-      // 1.5 2^23 + h exactly (the product is exact, the sum positive, rounding toward zero is the
-      // floor), whose low three bytes are h + 2^22; the same on v clamped to +-2^(lsb + 15) with
-      // the scale 2^-lsb gives l = x mod 256 in the low byte (a value of magnitude 2^(lsb + 15) or
-      // more is a multiple of 2^(lsb + 8), so l = 0 for it and for the clamp bound alike). The
-      // digits are l and the three bytes of h + 2^22, i.e. of x + 2^30. Values of a channel
-      // without digits count as 0. Sixteen keys per step, both slots from the same words.
-#pragma unroll 1
-      for (int ck = 0; ck < 4; ++ck) {
-        uint32_t w[16];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) w[jj] = *(const uint32_t*)(vsrc + (16 * ck + jj) * (DV * 2));
-#pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          uint32_t pw[NV][4];
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t fh[4], fl[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float f = __uint_as_float(__byte_perm(w[4 * c4 + e], 0u, sels[sl]));
-              fh[e] = __float_as_uint(__fmaf_rz(f, schi[sl], V_MAGIC));
-              fl[e] = __float_as_uint(__fmaf_rz(fminf(fmaxf(f, -clampv[sl]), clampv[sl]), sclo[sl], V_MAGIC));
-            }
-            transpose3(fh[0], fh[1], fh[2], fh[3], pw[1][c4], pw[2][c4], pw[3][c4]);
-            pw[0][c4] = __byte_perm(__byte_perm(fl[0], fl[1], 0x0040), __byte_perm(fl[2], fl[3], 0x0040), 0x5410);
-          }
-#pragma unroll
-          for (int p = 0; p < NV; ++p)
-            *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(chs[sl], 64 * kh + 16 * ck, BK)) =
-                make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
-        }
-      }
+      S.vl_n[par][vt] = 0;
+      group_sync(BAR_V, 128);  // this parity's lists reset, S.ve[par] complete
       // Values below the V window (an exponent field under lsb + 134): each goes to its channel's
       // correction list with the exact part the floor dropped, or past the list's capacity to the
       // bound; in a channel without digits every nonzero value is bounded.
@@ -931,7 +1006,83 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!keep && any) atomicAdd(&S.vl_n[par][cc], VL_BOUNDED);  // the whole channel is bounded
         }
       }
-      tc::fence_async_smem();
+      if (TOEP) {
+        // Words x + 2^30 of x = floor(v 2^-lsb) (|x| < 2^30): the product rounded toward -inf is
+        // exact unless it is below 2^-126 in magnitude, where rounding down keeps the floor (0 or
+        // -1); the conversion rounds down. A channel without digits (scale 0) counts its values
+        // as 0, keys past the tile's end as 0. One channel a thread (its TMEM lane), 8 keys a store.
+        const int cv = 32 * (warp & 3) + lane;
+        const int vev = S.ve[par][cv];
+        const int lsbv = vev == INT32_MIN ? 0 : vev - FV;
+        const float scv = (vev == INT32_MIN || lsbv >= -126) ? scale_of(lsbv) : 0.0f;
+        const uint8_t* vcol = rawv + b * RAWV_BUF + 2 * cv;
+        const uint32_t tv = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + T_COL_V;
+        tc::fence_after_sync();  // after the P.V MMAs of tile i - 1 (the wait above)
+#pragma unroll 2
+        for (int j0 = 0; j0 < BK; j0 += 8) {
+          uint32_t wv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t bits = *(const uint16_t*)(vcol + (j0 + e) * (DV * 2));
+            const float y = __fmul_rd(__uint_as_float(bits << 16), scv);
+            wv[e] = j0 + e < nvalid ? (uint32_t)__float2int_rd(y) + V_BIAS : V_BIAS;
+          }
+          tc::tmem_st8(tv + j0, wv);
+        }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+      } else {
+        // per slot: the channel, the byte permute that places its bf16 in the high half of a zero
+        // word (all zero without digits), and the scales of the two fused multiply-adds
+        int chs[2];
+        uint32_t sels[2];
+        float schi[2], sclo[2], clampv[2];
+  #pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          const int h = sl ^ swp;
+          const int keep = h ? keeph[1] : keeph[0];
+          const int l = keep ? (h ? lsbh[1] : lsbh[0]) : 0;
+          chs[sl] = 2 * cp + h;
+          sels[sl] = keep ? (h ? 0x3244u : 0x1044u) : 0x4444u;
+          schi[sl] = scale_of(l + 8);       // 2^-(lsb + 8): the high part floor(x / 256)
+          sclo[sl] = scale_of(l);           // 2^-lsb
+          clampv[sl] = scale_of(-(l + 15));  // 2^(lsb + 15): above it x is a multiple of 256
+        }
+        // Digits of x = floor(v 2^-lsb) (|x| < 2^30) = 256 h + l: fmaf_rz(v, 2^-(lsb + 8), 1.5 2^23) is
+        // 1.5 2^23 + h exactly (the product is exact, the sum positive, rounding toward zero is the
+        // floor), whose low three bytes are h + 2^22; the same on v clamped to +-2^(lsb + 15) with
+        // the scale 2^-lsb gives l = x mod 256 in the low byte (a value of magnitude 2^(lsb + 15) or
+        // more is a multiple of 2^(lsb + 8), so l = 0 for it and for the clamp bound alike). The
+        // digits are l and the three bytes of h + 2^22, i.e. of x + 2^30. Values of a channel
+        // without digits count as 0. Sixteen keys per step, both slots from the same words.
+  #pragma unroll 1
+        for (int ck = 0; ck < 4; ++ck) {
+          uint32_t w[16];
+  #pragma unroll
+          for (int jj = 0; jj < 16; ++jj) w[jj] = *(const uint32_t*)(vsrc + (16 * ck + jj) * (DV * 2));
+  #pragma unroll
+          for (int sl = 0; sl < 2; ++sl) {
+            uint32_t pw[NV][4];
+  #pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              uint32_t fh[4], fl[4];
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float f = __uint_as_float(__byte_perm(w[4 * c4 + e], 0u, sels[sl]));
+                fh[e] = __float_as_uint(__fmaf_rz(f, schi[sl], V_MAGIC));
+                fl[e] = __float_as_uint(__fmaf_rz(fminf(fmaxf(f, -clampv[sl]), clampv[sl]), sclo[sl], V_MAGIC));
+              }
+              transpose3(fh[0], fh[1], fh[2], fh[3], pw[1][c4], pw[2][c4], pw[3][c4]);
+              pw[0][c4] = __byte_perm(__byte_perm(fl[0], fl[1], 0x0040), __byte_perm(fl[2], fl[3], 0x0040), 0x5410);
+            }
+  #pragma unroll
+            for (int p = 0; p < NV; ++p)
+              *(uint4*)(sV + p * V_PLANE + tc::kmajor_off(chs[sl], 64 * kh + 16 * ck, BK)) =
+                  make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
+          }
+        }
+        tc::fence_async_smem();
+      }
       group_sync(BAR_V, 128);
       EA_PTV(3)
       if (vt == 0) mbar_arrive(&S.bar_vready);  // value digits and channel data of tile i
@@ -945,11 +1096,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         issued = i + 3;
       }
     }
-    EA_PT_FLUSH_RANGE(384, 12, 16)
+    EA_PT_FLUSH_RANGE(VW0 * 32, 12, 16)
     if (!ok_wait) S.abort = 1;
     for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rv[t & 1], (uint32_t)(t >> 1) & 1u, P.wait_debug);
   } else {
     // ======================= consumer warpgroups: logits, weights, merges, drains =======================
+    if (REBAL) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_CONSUMER));
     const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     int par = 0;
     bool pv_pending = false;
@@ -961,7 +1113,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t ph = (uint32_t)i & 1u;
       const int b = i & 1;
       {
-        const bool okw = tc::mbar_wait(&S.bar_smma, ph, P.wait_debug);  // the score MMAs of tile i
+        const bool okw = tc::mbar_wait(&S.bar_smma[sbuf(i)], spar(i), P.wait_debug);  // the score MMAs of tile i
         if (!group_sync_and(BAR_C, NC * 32, okw && !*(volatile int*)&S.abort)) {
           ok_wait = false;
           break;
@@ -981,25 +1133,47 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int g = h; g < nrows; g += NWG) {
           uint32_t dg[NK][4];
+          uint32_t gt[8];  // Toeplitz: the digit groups G_0 .. G_6 of the biased key words
+          if (TOEP) {  // the four accumulators' digit groups, summed
+            uint32_t g1[8], g2[8], g3[8];
+            tc::tmem_ld8(tlane + col_s(b) + 8 * g, gt);
+            tc::tmem_ld8(tlane + col_s(b) + 16 + 8 * g, g1);
+            tc::tmem_ld8(tlane + col_s(b) + 32 + 8 * g, g2);
+            tc::tmem_ld8(tlane + col_s(b) + 48 + 8 * g, g3);
+            tc::tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + COL_S + 32 * t + 4 * g, dg[t]);
+            for (int k = 0; k < 7; ++k) gt[k] += g1[k] + g2[k] + g3[k];
+          } else {
+#pragma unroll
+            for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + col_s(b) + SPL * t + 4 * g, dg[t]);
+          }
           tc::tmem_wait_ld();
           uint32_t out = T_MASKED;
           if (key < nvalid && j0 + key < S.len[g] && S.rows[g] >= 0) {
             if (kbad) {
               atomicMax(&S.rst[g], ST_DOMAIN);
             } else {
-              // digit products (t, s) grouped by t + s: G_k = sum_{t + s = k} dg[t][s]
-              const int32_t G0 = (int32_t)dg[0][0];
-              const int32_t G1 = (int32_t)dg[0][1] + (int32_t)dg[1][0];
-              const int32_t G2 = (int32_t)dg[0][2] + (int32_t)dg[1][1] + (int32_t)dg[2][0];
-              const int32_t G3 = (int32_t)dg[0][3] + (int32_t)dg[1][2] + (int32_t)dg[2][1] + (int32_t)dg[3][0];
-              const int32_t G4 = (int32_t)dg[1][3] + (int32_t)dg[2][2] + (int32_t)dg[3][1];
-              const int32_t G5 = (int32_t)dg[2][3] + (int32_t)dg[3][2];
-              const int32_t G6 = (int32_t)dg[3][3];
-              const uint32_t lo4[4] = {(uint32_t)G0, (uint32_t)G1, (uint32_t)G2, (uint32_t)G3};
-              const uint32_t hi3[3] = {(uint32_t)G4, (uint32_t)G5, (uint32_t)G6};
-              const int64_t acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
+              int64_t acc;
+              if (TOEP) {
+                // sum_k G_k 2^(8k) = q . (k + 2^W) exactly; taken mod 2^64, after the bias
+                // 2^W q_sum is removed the result is q . k (|q . k| < 2^61)
+                uint64_t u = 0;
+#pragma unroll
+                for (int k = 0; k < 7; ++k) u += (uint64_t)(int64_t)(int32_t)gt[k] << (8 * k);
+                acc = (int64_t)(u - ((uint64_t)S.qsum[g] << P.W));
+              } else {
+                // digit products (t, s) grouped by t + s: G_k = sum_{t + s = k} dg[t][s]
+                const int32_t G0 = (int32_t)dg[0][0];
+                const int32_t G1 = (int32_t)dg[0][1] + (int32_t)dg[1][0];
+                const int32_t G2 = (int32_t)dg[0][2] + (int32_t)dg[1][1] + (int32_t)dg[2][0];
+                const int32_t G3 = (int32_t)dg[0][3] + (int32_t)dg[1][2] + (int32_t)dg[2][1] + (int32_t)dg[3][0];
+                const int32_t G4 = (int32_t)dg[1][3] + (int32_t)dg[2][2] + (int32_t)dg[3][1];
+                const int32_t G5 = (int32_t)dg[2][3] + (int32_t)dg[3][2];
+                const int32_t G6 = (int32_t)dg[3][3];
+                const uint32_t lo4[4] = {(uint32_t)G0, (uint32_t)G1, (uint32_t)G2, (uint32_t)G3};
+                const uint32_t hi3[3] = {(uint32_t)G4, (uint32_t)G5, (uint32_t)G6};
+                acc = recomb<4>(lo4) + (int64_t)((uint64_t)recomb<3>(hi3) << 32);
+              }
               const bool qlossy = (S.qlossy[g][0] | S.qlossy[g][1] | S.qlossy[g][2] | S.qlossy[g][3]) != 0;
               const int sexp = S.qlsb[g] + klsb;
               uint32_t fb;
@@ -1023,7 +1197,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                   const uint32_t kl = kl4[wd];
                   for (uint32_t m = kl; m; m &= m - 1) {
                     const int ii = 32 * wd + __ffs(m) - 1;
-                    const int32_t qf = q_fix(sQ, g, ii);
+                    const int32_t qf = TOEP ? qfx[g * D + ii] : q_fix(sQ, g, ii);
                     err += (uint64_t)(qf < 0 ? -qf : qf);
                   }
                 }
@@ -1039,7 +1213,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               } else {
                 Rnd t = rnd_zero();
                 const int ls = (qlossy || klossy) ? logit_bounded(acc, err, sexp, P.am, P.ae, t)
-                                                  : logit_exact64(acc, sexp, P.am, P.ae, t);
+                                                  : logit_exact_ool(acc, sexp, P.am, P.ae, t);
                 if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
                 else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
                 else atomicMax(&S.rst[g], ST_DOMAIN);
@@ -1070,7 +1244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc::fence_before_sync();
       const bool any_unc = group_sync_or(BAR_C, NC * 32, unc);
-      if (tid == 0) mbar_arrive(&S.bar_p1);  // the score accumulators and the raw K rows are free
+      if (tid == 0) mbar_arrive(&S.bar_p1[sbuf(i)]);  // the score accumulators and key metadata of tile i are free
       EA_PT(1)
       // ---------------- exact scores of the uncertified pairs, one warp per pair ----------------
       if (any_unc) {
@@ -1146,7 +1320,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const Rnd t = rnd_from_f32(tb);
             uint32_t Mi;
             int64_t Ei;
-            ws = weight_from_logit(t, g_ta64, g_tb64, Mi, Ei);
+            ws = weight_ool(t, Mi, Ei);
             if (ws == W_RISKY) {
               ++n_wide;
               ws = wide_weight(t, Mi, Ei);
@@ -1170,8 +1344,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+        if (TOEP) {
+          // P.V B row (g, k), bytes 4 key .. 4 key + 3: weight digits W_k, W_(k-1), W_(k-2),
+          // W_(k-3) (zero outside 0..5; W < 2^48)
+          const uint32_t wl = (uint32_t)W, wh = (uint32_t)(W >> 32);
+          const uint32_t sel[9] = {0x4440u, 0x4401u, 0x4012u, 0x0123u, 0x1234u, 0x2345u, 0x3456u, 0x4566u, 0x5666u};
 #pragma unroll
-        for (int wd = 0; wd < NW; ++wd) sW[tc::kmajor_off(6 * g + wd, key, NSW)] = (uint8_t)(W >> (8 * wd));
+          for (int k = 0; k < 9; ++k)
+            *(uint32_t*)(sW + tc::sw128_off(16 * g + k, 4 * key, T_WROWS)) =
+                k < 4 ? __byte_perm(wl, 0u, sel[k]) : __byte_perm(wl, wh, sel[k]);
+          wval[g * BK + key] = W;
+        } else {
+#pragma unroll
+          for (int wd = 0; wd < NW; ++wd) sW[tc::kmajor_off(6 * g + wd, key, NSW)] = (uint8_t)(W >> (8 * wd));
+        }
         const uint64_t zs = warp_sum_u64(W);
         const uint32_t zl = __reduce_add_sync(0xffffffffu, lw);
         if (lane == 0) {
@@ -1187,8 +1373,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       EA_PT(3)
       // ---------------- P.V MMAs: 4 value digits x (N: the rows' weight digits) ----------------
-      // value digit u to its own accumulator, issued by lane 0 of consumer warp u
-      if (lane == 0 && warp < NV) {
+      if (TOEP) {
+        // lane 0 of consumer warp a issues K steps 4 a .. 4 a + 3 (keys 32 a .. 32 a + 31; A: the
+        // V words in tensor memory) into P.V accumulator a (N = 16 columns a row)
+        if (lane == 0 && warp < NV) {
+          tc::fence_after_sync();
+          const uint32_t idesc = tc::idesc_i8(128, 16 * nrows, false, false);
+          const uint32_t wa = tc::smem_u32(sW);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int ks = 4 * warp + j;
+            tc::mma_i8_tmem_a(tmem + COLO + 32 * warp, tmem + T_COL_V + 8 * ks,
+                              tc::smem_desc_sw128(wa + (ks >> 2) * (T_WROWS / 8) * 1024 + (ks & 3) * 32, 1024), idesc,
+                              j > 0);
+          }
+          tc::mma_commit(tc::smem_u32(&S.bar_pv));
+        }
+      } else if (lane == 0 && warp < NV) {
+        // value digit u to its own accumulator, issued by lane 0 of consumer warp u
         const int u = warp;
         tc::fence_after_sync();
         constexpr uint32_t lbo_a = (DV / 8) * 128, lbo_b = (NSW / 8) * 128;
@@ -1197,7 +1399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t idesc = tc::idesc_i8(128, npv, false, false);
 #pragma unroll
         for (int ks = 0; ks < BK / 32; ++ks)
-          tc::mma_i8(tmem + COL_O + NSW * u, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
+          tc::mma_i8(tmem + COLO + NSW * u, ad0 + ((ks * 2 * lbo_a) >> 4), bd0 + ((ks * 2 * lbo_b) >> 4), idesc,
                      ks > 0);
         tc::mma_commit(tc::smem_u32(&S.bar_pv));
       }
@@ -1255,8 +1457,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t ck = S.vl_k[par][c][k];
             const int key = (int)(ck & 0xFFu);
             uint64_t W = 0;
+            if (TOEP) {
+              W = wval[g * BK + key];
+            } else {
 #pragma unroll
-            for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
+              for (int wd = 0; wd < NW; ++wd) W |= (uint64_t)sW[tc::kmajor_off(6 * g + wd, key, NSW)] << (8 * wd);
+            }
             corr += shift_floor128((i128)(int64_t)W * S.vl_dx[par][c][k], sb - 24);  // 0 <= W dx < 2^72
             cerr += (sb - 24 < 0) ? 1u : 0u;
             if ((ck >> 8) & 1u) cerr += scale_ceil128((u128)W + 1, sb - 24);
@@ -1284,22 +1490,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int g = h + NWG * ii;
         if (g >= nrows) break;  // uniform across the warp
         uint32_t d0[8], d1[8], d2[8], d3[8];
-        tc::tmem_ld8(tlane + COL_O + 6 * g, d0);
-        tc::tmem_ld8(tlane + COL_O + NSW + 6 * g, d1);
-        tc::tmem_ld8(tlane + COL_O + 2 * NSW + 6 * g, d2);
-        tc::tmem_ld8(tlane + COL_O + 3 * NSW + 6 * g, d3);
-        tc::tmem_wait_ld();
-        if (sh_base[ii] == INT32_MIN) continue;
-        // unsigned digits: 0 <= D_u[w] < 128 keys x 255 x 255 < 2^23, each group (<= 4 terms) < 2^25
-        const int64_t s0 = (int64_t)d0[0];
-        const int64_t s1 = (int64_t)d0[1] + d1[0];
-        const int64_t s2 = (int64_t)d0[2] + d1[1] + d2[0];
-        const int64_t s3 = (int64_t)d0[3] + d1[2] + d2[1] + d3[0];
-        const int64_t s4 = (int64_t)d0[4] + d1[3] + d2[2] + d3[1];
-        const int64_t s5 = (int64_t)d0[5] + d1[4] + d2[3] + d3[2];
-        const int64_t s6 = (int64_t)d1[5] + d2[4] + d3[3];
-        const int64_t s7 = (int64_t)d2[5] + d3[4];
-        const int64_t s8 = (int64_t)d3[5];
+        int64_t s0, s1, s2, s3, s4, s5, s6, s7, s8;
+        if (TOEP) {
+          // the digit groups G_0 .. G_8, summed over the four accumulators (each < 4 x 128 x 255
+          // x 255 < 2^26 in all)
+          s0 = s1 = s2 = s3 = s4 = s5 = s6 = s7 = s8 = 0;
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            tc::tmem_ld8(tlane + COLO + 32 * a + 16 * g, d0);
+            tc::tmem_ld8(tlane + COLO + 32 * a + 16 * g + 8, d1);
+            tc::tmem_wait_ld();
+            s0 += d0[0], s1 += d0[1], s2 += d0[2], s3 += d0[3], s4 += d0[4], s5 += d0[5], s6 += d0[6], s7 += d0[7];
+            s8 += d1[0];
+          }
+          if (sh_base[ii] == INT32_MIN) continue;
+        } else {
+          tc::tmem_ld8(tlane + COLO + 6 * g, d0);
+          tc::tmem_ld8(tlane + COLO + NSW + 6 * g, d1);
+          tc::tmem_ld8(tlane + COLO + 2 * NSW + 6 * g, d2);
+          tc::tmem_ld8(tlane + COLO + 3 * NSW + 6 * g, d3);
+          tc::tmem_wait_ld();
+          if (sh_base[ii] == INT32_MIN) continue;
+          // unsigned digits: 0 <= D_u[w] < 128 keys x 255 x 255 < 2^23, each group (<= 4 terms) < 2^25
+          s0 = (int64_t)d0[0];
+          s1 = (int64_t)d0[1] + d1[0];
+          s2 = (int64_t)d0[2] + d1[1] + d2[0];
+          s3 = (int64_t)d0[3] + d1[2] + d2[1] + d3[0];
+          s4 = (int64_t)d0[4] + d1[3] + d2[2] + d3[1];
+          s5 = (int64_t)d0[5] + d1[4] + d2[3] + d3[2];
+          s6 = (int64_t)d1[5] + d2[4] + d3[3];
+          s7 = (int64_t)d2[5] + d3[4];
+          s8 = (int64_t)d3[5];
+        }
         const int64_t lo = s0 + (s1 << 8) + (s2 << 16) + (s3 << 24);  // < 2^50
         const int64_t hi = s4 + (s5 << 8) + (s6 << 16) + (s7 << 24);
         // sum_keys W (x + 2^30) - 2^30 sum_keys W = sum_keys W x, exactly
@@ -1430,19 +1652,30 @@ static int k_fetch_mode(const Prob& P, CUtensorMap* tm, int* kbox) {
 // Grid (segments, splits); writes split partials (P.pR ..) for every listed row. max_rows: the
 // most rows any segment holds (1..8; 8 when unknown).
 cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nseg, int max_rows, cudaStream_t st) {
-  // 8 consumer warps with 1, 2 or 4 row slots (segments of <= 2, 4, 8 rows)
-  auto k0 = tcd::tc_decode_kernel<1, 8>;
-  auto k1 = tcd::tc_decode_kernel<2, 8>;
-  auto k2 = tcd::tc_decode_kernel<4, 8>;
-  const int v = max_rows <= 2 ? 0 : max_rows <= 4 ? 1 : 2;
-  auto kern = v == 0 ? k0 : v == 1 ? k1 : k2;
+  // 8 consumer warps with 1, 2 or 4 row slots (segments of <= 2, 4, 8 rows); segments of <= 2
+  // rows take 8 K producer warps (640 threads) when the build gives the block the registers its
+  // per-role split draws on
+  auto k0 = tcd::tc_decode_kernel<1, 8, 8>;
+  auto k0s = tcd::tc_decode_kernel<1, 8, 4>;
+  auto k1 = tcd::tc_decode_kernel<2, 8, 4>;
+  auto k2 = tcd::tc_decode_kernel<4, 8, 4>;
   // the shared-memory opt-in is a property of the function on a device: set it once per device
   // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
-  static bool attr_set[64][3] = {};
+  static bool attr_set[64][4] = {};
+  static int wide_ok = -1;  // k0's launch registers cover its split (checked once)
+  if (wide_ok < 0) {
+    cudaFuncAttributes fa;
+    wide_ok = cudaFuncGetAttributes(&fa, k0) == cudaSuccess && fa.maxThreadsPerBlock >= tcd::threads_of<8, 8>() &&
+              fa.numRegs * tcd::threads_of<8, 8>() >= tcd::REG_SPLIT;
+  }
+  const int v = max_rows <= 2 ? (wide_ok ? 0 : 3) : max_rows <= 4 ? 1 : 2;
+  auto kern = v == 0 ? k0 : v == 1 ? k1 : v == 2 ? k2 : k0s;
+  const int threads = v == 0 ? tcd::threads_of<8, 8>() : tcd::threads_of<8, 4>();
+  const int smem = v == 0 ? (int)tcd::T_SMEM_BYTES : (int)tcd::SMEM_BYTES;  // (the 640-thread kernel: Toeplitz layout)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcd::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
   }
@@ -1450,7 +1683,7 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
   int kbox = 0;
   const int kmode = k_fetch_mode(P, &tm, &kbox);
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
-  kern<<<grid, tcd::THREADS, tcd::SMEM_BYTES, st>>>(P, seg_rows, tm, kmode, kbox);
+  kern<<<grid, threads, smem, st>>>(P, seg_rows, tm, kmode, kbox);
   return cudaGetLastError();
 }
 

@@ -670,7 +670,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
             } else {
               Rnd t = rnd_zero();
               const int ls = (qlossy || klossy) ? logit_bounded(acc[u], err, sexp, P.am, P.ae, t)
-                                                : logit_exact64(acc[u], sexp, P.am, P.ae, t);
+                                                : logit_exact_ool(acc[u], sexp, P.am, P.ae, t);
               if (ls == LOGIT_OK) out = rnd_to_f32_bits(t);
               else if (ls == LOGIT_UNCERTIFIED) out = T_UNCERT;
               else rstat = ST_DOMAIN;
@@ -786,7 +786,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_prefill_kernel(Prob P, const in
           const Rnd t = rnd_from_f32(sT[r * T_PITCH + 16 * u4 + 4 * wd + u]);
           uint32_t M;
           int64_t E;
-          int ws = weight_from_logit(t, g_ta64, g_tb64, M, E);
+          int ws = weight_ool(t, M, E);
           if (ws == W_RISKY) {
             ++n_wide;
             ws = wide_weight(t, M, E);

@@ -183,6 +183,15 @@ static __device__ __noinline__ int logit_bounded(int64_t acc, uint64_t err, int 
   return logit_from_interval(acc, err, sexp, am, ae, t);
 }
 
+// The integer paths behind the binary64 fast paths, out of line: rarely taken, they would
+// otherwise sit between the hot instructions of the tile loops
+static __device__ __noinline__ int logit_exact_ool(int64_t acc, int sexp, int32_t am, int32_t ae, Rnd& t) {
+  return logit_exact64(acc, sexp, am, ae, t);
+}
+static __device__ __noinline__ int weight_ool(const Rnd& t, uint32_t& M, int64_t& E) {
+  return weight_from_logit(t, g_ta64, g_tb64, M, E);
+}
+
 static __device__ __noinline__ int wide_weight(const Rnd& t, uint32_t& M, int64_t& E) {
   return weight_from_logit_wide(t, g_ta128, g_tb128, M, E);
 }

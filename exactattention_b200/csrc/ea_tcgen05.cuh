@@ -30,6 +30,30 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;                // base offset 0, legacy LBO mode, layout type 0 (no swizzle)
 }
 
+// byte offset of (row n, byte k) in a K-major tile of `rows` rows (a multiple of 8) with the
+// 128-byte swizzle: 1024-byte atoms of 8 rows x 128 bytes, the atoms of one 128-byte K column
+// contiguous (8-row groups 1024 bytes apart), K columns (rows / 8) 1024 bytes apart, and 16-byte
+// chunk c of row n stored at chunk c ^ (n % 8) of its atom row. The tile starts on a 1024-byte
+// boundary.
+__host__ __device__ __forceinline__ uint32_t sw128_off(uint32_t n, uint32_t k, uint32_t rows) {
+  return ((k >> 7) * (rows >> 3) + (n >> 3)) * 1024u + (n & 7u) * 128u + ((((k >> 4) & 7u) ^ (n & 7u)) << 4) +
+         (k & 15u);
+}
+
+// shared-memory matrix descriptor of such a tile (version 1, layout SWIZZLE_128B): `saddr` the
+// start of the 32-byte K step inside its atom column (the hardware applies the swizzle to the
+// address bits), 8-row groups `sbo_bytes` apart; the leading-byte offset is unused by swizzled
+// K-major layouts
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // instruction descriptor of kind::i8 with s32 accumulation, both operands K-major
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, bool a_signed, bool b_signed) {
   return (2u << 4)                           // D format: s32
