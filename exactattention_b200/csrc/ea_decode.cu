@@ -347,6 +347,16 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
 }
 
+// N and its error bound in a unit 2^d times coarser (floor, ceil + 1), out of line: the row's
+// bound or the channel's exponent grows on few tiles
+struct NScaled {
+  i128 n;
+  u128 e;
+};
+static __device__ __noinline__ NScaled rescale_n_ool(i128 n, u128 e, int d) {
+  return NScaled{shift_floor128(n, -d), scale_ceil128(e, -d) + 1};
+}
+
 // The part of bf16 `bits` (value v) that FLOORING v 2^-lsb to an integer dropped, v 2^-lsb -
 // floor(v 2^-lsb) in [0, 1), in units 2^-24, itself floored (< 2^24); `lost2` when bits remain
 // below that unit.
@@ -377,6 +387,28 @@ __device__ __forceinline__ int32_t lost_part24(uint32_t bits, int lsb, int& lost
   const uint64_t rm = ((uint64_t)1 << r) - 1;
   lost2 = (low & rm) != 0;
   return (int32_t)((1u << 24) - (uint32_t)(((uint64_t)low + rm) >> r));
+}
+
+// Fixed point (fixq) of the four bf16 of words w0, w1 at lsb, out of line: only keys whose
+// largest element lies below 2^-100 take it, and inlined its 32 copies would crowd the K
+// producers' hot loop
+static __device__ __noinline__ uint4 fixq4_ool(uint32_t w0, uint32_t w1, int lsb) {
+  int lost = 0, b2 = 0;
+  uint4 r;
+  r.x = (uint32_t)fixq(w0 & 0xFFFFu, lsb, lost, b2);
+  r.y = (uint32_t)fixq(w0 >> 16, lsb, lost, b2);
+  r.z = (uint32_t)fixq(w1 & 0xFFFFu, lsb, lost, b2);
+  r.w = (uint32_t)fixq(w1 >> 16, lsb, lost, b2);
+  return r;
+}
+
+// logit_interval_f64 out of line (pairs with lossy elements only): bits 0-31 the logit, bit 32
+// `differ`, bit 33 `done`
+static __device__ __noinline__ uint64_t logit_interval_ool(int64_t acc, uint64_t err, int sexp, double am_d, int32_t ae) {
+  uint32_t fb = 0;
+  bool differ = false;
+  const bool done = f64::logit_interval_f64(acc, err, sexp, am_d, ae, fb, differ);
+  return (uint64_t)fb | ((uint64_t)differ << 32) | ((uint64_t)done << 33);
 }
 
 // q row g's fixed-point element i from its balanced digit planes in the score B tile
@@ -759,11 +791,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
               xs[2 * q + 1] = fixf_hi(w[q], sc);
             }
           } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              int lost = 0, b2 = 0;
-              xs[e] = (uint32_t)fixq((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu, lsb, lost, b2);
-            }
+            const uint4 lo = fixq4_ool(w[0], w[1], lsb), hi = fixq4_ool(w[2], w[3], lsb);
+            xs[0] = lo.x, xs[1] = lo.y, xs[2] = lo.z, xs[3] = lo.w;
+            xs[4] = hi.x, xs[5] = hi.y, xs[6] = hi.z, xs[7] = hi.w;
           }
           if (TOEP) {  // the words x + 2^W of dimensions 8 (4 blk + g4) .. + 7, one a column
 #pragma unroll
@@ -1201,7 +1231,10 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
                     err += (uint64_t)(qf < 0 ? -qf : qf);
                   }
                 }
-                done = f64::logit_interval_f64(acc, err, sexp, am_d, P.ae, fb, differ);
+                const uint64_t r = logit_interval_ool(acc, err, sexp, am_d, P.ae);
+                fb = (uint32_t)r;
+                differ = (r >> 32) & 1u;
+                done = (r >> 33) & 1u;
               } else {
                 done = f64::logit_f64(acc, sexp, am_d, P.ae, fb);
               }
@@ -1418,9 +1451,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         ztile[ii] = 0;
         if (g >= nrows) continue;
         if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
-          const int d = ve_now - vec;
-          N[ii] = shift_floor128(N[ii], -d);
-          Nerr[ii] = scale_ceil128(Nerr[ii], -d) + 1;
+          const NScaled r = rescale_n_ool(N[ii], Nerr[ii], ve_now - vec);
+          N[ii] = r.n;
+          Nerr[ii] = r.e;
         }
         const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
         if (Rt == INT32_MIN) continue;
@@ -1428,8 +1461,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         const int32_t Rn = R[ii] == R_EMPTY ? Rt : max(R[ii], Rt);
         if (R[ii] != R_EMPTY && Rn > R[ii]) {
           const int d = Rn - R[ii];
-          N[ii] = shift_floor128(N[ii], -d);
-          Nerr[ii] = scale_ceil128(Nerr[ii], -d) + 1;
+          const NScaled r = rescale_n_ool(N[ii], Nerr[ii], d);
+          N[ii] = r.n;
+          Nerr[ii] = r.e;
           int lost;
           Z[ii] = floor_shift(Z[ii], -d, lost);
           Zerr[ii] = scale_ceil(Zerr[ii], -d) + (uint64_t)lost;
@@ -1441,10 +1475,10 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         const int zsh = (Rt - FW) - (Rn - FZ);
         int lost = 0;
         Z[ii] += floor_shift((int64_t)zt, zsh, lost);
-        Zerr[ii] += scale_ceil(nlw, zsh) + (uint64_t)lost;
+        Zerr[ii] += (nlw ? scale_ceil(nlw, zsh) : 0) + (uint64_t)lost;
         const int sb = (Rt - FW - FV) - (Rn - FN);
         sh_base[ii] = sb;
-        Nerr[ii] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
+        if (nlw) Nerr[ii] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
         // values that lost bits in the V window: their lost parts times the weights, added exactly up
         // to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units
         // times one V unit per such value
