@@ -101,7 +101,7 @@ template <int NC, int KW>
 __host__ __device__ constexpr int threads_of() { return 32 * (NC + KW + 4); }
 // registers a thread of each role keeps with 8 K producer warps (640 threads, 96 registers a
 // thread at launch): the producer warpgroups give registers back to the consumers
-constexpr int REG_CONSUMER = 128, REG_PRODUCER = 72, REG_LAUNCH = 96;
+constexpr int REG_CONSUMER = 120, REG_PRODUCER = 80, REG_LAUNCH = 96;
 constexpr int REG_SPLIT = 256 * REG_CONSUMER + 384 * REG_PRODUCER;
 constexpr uint32_t VLCAP = 2;
 constexpr int NQL = 4;  // dimensions whose k values the K producers keep for the consumers' bound
@@ -161,7 +161,7 @@ struct Small {
   // raw K / V tiles landed (per buffer); score MMAs done; pass 1 done; value digits and channel
   // data ready; P.V MMAs done
   // (score MMAs / pass 1 by score buffer: one buffer, or two for double-buffered segments)
-  uint64_t bar_rk[2], bar_rv[2], bar_smma[2], bar_p1[2], bar_vready, bar_pv;
+  uint64_t bar_rk[2], bar_rv[3], bar_smma[2], bar_p1[2], bar_vready, bar_pv;
   int32_t abort;  // a bounded wait gave up in some role
   uint32_t tmem;
 #ifdef EA_PHASE_TIMERS
@@ -185,10 +185,11 @@ static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 // are needed on either side; the P.V tile likewise holds weight digit W_(k-u) at byte u of key j
 // (k = 0..8). The biases come out exactly: 2^27 times the row's query sum, 2^30 times the tile's
 // weight sum. B tiles use the 128-byte swizzle (conflict-free word stores).
-// Shared memory: raw K / V staging as above, score B tile (16 rows: n = 8 g + k), P.V B tile (32
+// Shared memory: raw K staging as above, raw V staging in three buffers (V tiles fetched three
+// ahead), score B tile (16 rows: n = 8 g + k), P.V B tile (32
 // rows: n = 16 g + k), logits, the rows' fixed-point query elements and the tile's weights.
 constexpr uint32_t T_QROWS = 16, T_WROWS = 32, T_KB = 512;  // B rows, K bytes of a B row
-constexpr uint32_t T_OFF_QT = OFF_RAWV + 2 * RAWV_BUF;
+constexpr uint32_t T_OFF_QT = OFF_RAWV + 3 * RAWV_BUF;
 constexpr uint32_t T_OFF_WT = T_OFF_QT + T_QROWS * T_KB;
 constexpr uint32_t T_OFF_T = T_OFF_WT + T_WROWS * T_KB;
 constexpr uint32_t T_OFF_QF = T_OFF_T + GD * BK * 4;
@@ -440,7 +441,7 @@ __device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2
 // KW: K producer warps (4: one thread a key; 8: two threads a key, each half the dimensions).
 // With 8 consumer and 8 K warps the block has 640 threads and rebalances registers per role
 // (setmaxnreg): the launch gives 96 a thread, the producers drop to REG_PRODUCER and the consumers
-// rise to REG_CONSUMER (256 x 128 + 384 x 72 = 60,416 <= 640 x 96 = 61,440).
+// rise to REG_CONSUMER (256 x 120 + 384 x 80 = 61,440 = 640 x 96).
 template <int RPT, int NC, int KW>
 __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows, const __grid_constant__ CUtensorMap tmk, int kmode,
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
   constexpr bool DB = RPT == 1;
   // the 640-thread instantiation uses the Toeplitz layout (K and V words in tensor memory)
   constexpr bool TOEP = REBAL;
+  constexpr int VST = TOEP ? 3 : 2;  // raw V staging buffers
   static_assert(!TOEP || DB, "Toeplitz layout: segments of at most two rows");
   constexpr uint32_t SPL = DB ? 8u : 32u;  // score accumulator columns a key digit plane
   constexpr uint32_t COLO = TOEP ? T_COL_O : DB ? DB_COL_O : COL_O;
@@ -508,6 +510,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     tc::mbar_init(&S.bar_rk[1], 1);
     tc::mbar_init(&S.bar_rv[0], 1);
     tc::mbar_init(&S.bar_rv[1], 1);
+    tc::mbar_init(&S.bar_rv[2], 1);
     // one commit per issuer (a key / value digit, or in the Toeplitz layout four K steps)
     tc::mbar_init(&S.bar_smma[0], NK);
     tc::mbar_init(&S.bar_smma[1], NK);
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
               &S.bar_rk[t], pref);
     }
   if (warp == VW0 + 3)
-    for (int t = 0; t < 2 && t < ntiles; ++t) {
+    for (int t = 0; t < VST && t < ntiles; ++t) {
       const int64_t j0 = kbeg + (int64_t)t * BK;
       fetch_rows(P, P.v, row0, kvbase, j0, (int)min((int64_t)BK, kend - j0), rawv + t * RAWV_BUF, &S.bar_rv[t]);
     }
@@ -912,14 +915,14 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     // of the 32-bit word of both channels by one byte permute (which also zeroes it for a channel
     // without digits).
     const int swp = (cp >> 2) & 1;
-    int waited = 0, issued = min(ntiles, 2);  // tiles [waited, issued) have fetches in flight
+    int waited = 0, issued = min(ntiles, VST);  // tiles [waited, issued) have fetches in flight
     EA_PTV_INIT
     for (int i = 0; i < ntiles; ++i) {
-      const int b = i & 1, par = b;
+      const int b = i % VST, par = i & 1;  // raw buffer; tile parity of the channel data
       const int64_t j0 = kbeg + (int64_t)i * BK;
       const int nvalid = (int)min((int64_t)BK, kend - j0);
-      const int64_t pref = warp == VW0 + 3 ? page_ahead(P, row0, j0 + 2 * BK, kend) : -1;
-      bool okw = tc::mbar_wait(&S.bar_rv[b], (uint32_t)(i >> 1) & 1u, P.wait_debug);
+      const int64_t pref = warp == VW0 + 3 ? page_ahead(P, row0, j0 + VST * BK, kend) : -1;
+      bool okw = tc::mbar_wait(&S.bar_rv[b], (uint32_t)(i / VST) & 1u, P.wait_debug);
       if (!group_sync_and(BAR_V, 128, okw && !*(volatile int*)&S.abort)) {
         ok_wait = false;
         break;
@@ -1116,19 +1119,19 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
       group_sync(BAR_V, 128);
       EA_PTV(3)
       if (vt == 0) mbar_arrive(&S.bar_vready);  // value digits and channel data of tile i
-      // the raw V rows of tile i are consumed: fetch tile i + 2 into them
-      if (i + 2 < ntiles) {
+      // the raw V rows of tile i are consumed: fetch tile i + VST into them
+      if (i + VST < ntiles) {
         if (warp == VW0 + 3) {
           tc::fence_async_smem();
-          fetch_rows(P, P.v, row0, kvbase, j0 + 2 * BK, (int)min((int64_t)BK, kend - j0 - 2 * BK), rawv + b * RAWV_BUF,
-                     &S.bar_rv[b], pref);
+          fetch_rows(P, P.v, row0, kvbase, j0 + VST * BK, (int)min((int64_t)BK, kend - j0 - VST * BK),
+                     rawv + b * RAWV_BUF, &S.bar_rv[b], pref);
         }
-        issued = i + 3;
+        issued = i + VST + 1;
       }
     }
     EA_PT_FLUSH_RANGE(VW0 * 32, 12, 16)
     if (!ok_wait) S.abort = 1;
-    for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rv[t & 1], (uint32_t)(t >> 1) & 1u, P.wait_debug);
+    for (int t = waited; t < issued; ++t) tc::mbar_wait(&S.bar_rv[t % VST], (uint32_t)(t / VST) & 1u, P.wait_debug);
   } else {
     // ======================= consumer warpgroups: logits, weights, merges, drains =======================
     if (REBAL) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_CONSUMER));
