@@ -49,7 +49,7 @@ BF16_EQUIV_FLOPS_PER_PAIR = 512  # 4 d
 KV_BYTES_PER_KEY = 512           # bf16 K and V rows of d = 128 for one kv head, read once
 HOT_KERNEL = {"c2": "tc_prefill_kernel", "c3": "tc_decode_kernel", "c4": "tc_prefill_kernel",
               "c5": "tc_decode_kernel"}
-DEFAULT_SPLITS = {"c2": 1, "c3": 6, "c4": 1, "c5": 32}
+DEFAULT_SPLITS = {"c2": 1, "c3": 8, "c4": 1, "c5": 32}
 # our kernel launches per step: tier 1, split combine / list kernel, and the fallback tiers'
 # fixed launches (they run on device-side counts, so they launch every step); KV-sharded c5: the
 # decode kernel, the split combine (export), the gathered merge, and the fixed-capacity wide tier
@@ -399,7 +399,7 @@ class Runner:
 def config_splits(name: str, case: dict, sms: int) -> int:
     """KV splits of a config's rank share: c4's prefix blocks (128 rows each) are too few to fill
     the GPU, so each takes enough KV splits for about 1.5 waves; the others use their measured
-    best (c2 1, c3 6, c5 32)."""
+    best (c2 1, c3 8, c5 32)."""
     if name == "c4":
         nb = int(case["kw"]["blocks"].shape[0])
         return max(1, -(-3 * sms // (2 * nb)))
