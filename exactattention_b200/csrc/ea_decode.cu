@@ -1043,7 +1043,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         // Words x + 2^30 of x = floor(v 2^-lsb) (|x| < 2^30): the product rounded toward -inf is
         // exact unless it is below 2^-126 in magnitude, where rounding down keeps the floor (0 or
         // -1); the conversion rounds down. A channel without digits (scale 0) counts its values
-        // as 0, keys past the tile's end as 0. One channel a thread (its TMEM lane), 8 keys a store.
+        // as 0. Keys past the tile's end keep whatever word their stale rows give: their weights
+        // are 0 (and the digit-group bounds hold for any bytes). One channel a thread (its TMEM
+        // lane), 8 keys a store.
         const int cv = 32 * (warp & 3) + lane;
         const int vev = S.ve[par][cv];
         const int lsbv = vev == INT32_MIN ? 0 : vev - FV;
@@ -1058,7 +1060,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
           for (int e = 0; e < 8; ++e) {
             const uint32_t bits = *(const uint16_t*)(vcol + (j0 + e) * (DV * 2));
             const float y = __fmul_rd(__uint_as_float(bits << 16), scv);
-            wv[e] = j0 + e < nvalid ? (uint32_t)__float2int_rd(y) + V_BIAS : V_BIAS;
+            wv[e] = (uint32_t)__float2int_rd(y) + V_BIAS;
           }
           tc::tmem_st8(tv + j0, wv);
         }
