@@ -194,7 +194,18 @@ constexpr uint32_t T_OFF_WT = T_OFF_QT + T_QROWS * T_KB;
 constexpr uint32_t T_OFF_T = T_OFF_WT + T_WROWS * T_KB;
 constexpr uint32_t T_OFF_QF = T_OFF_T + GD * BK * 4;
 constexpr uint32_t T_OFF_WV = T_OFF_QF + 2 * D * 4;
-constexpr uint32_t T_OFF_SMALL = T_OFF_WV + 2 * BK * 8;
+// Lost parts of window elements (Toeplitz layout), for the exact correction of lossy scores: per
+// tile parity, K thread half h and key, up to 2 elements (dimension, dk = k - K 2^klsb, exact in
+// fp32) and their count (more than 2: the list is incomplete); per query row and listed lossy
+// dimension n (S.qlk), dq = q - Q 2^qlsb (0 where the row lost nothing)
+struct KcArea {
+  float kcd[2][2][BK][2];
+  uint8_t kci[2][2][BK][2];
+  uint8_t kcn[2][2][BK];
+  float qdq[2][NQL];
+};
+constexpr uint32_t T_OFF_KC = T_OFF_WV + 2 * BK * 8;
+constexpr uint32_t T_OFF_SMALL = T_OFF_KC + (uint32_t)((sizeof(KcArea) + 15) / 16 * 16);
 constexpr uint32_t T_SMEM_BYTES = T_OFF_SMALL + sizeof(Small);
 static_assert(T_SMEM_BYTES <= 227 * 1024 && T_OFF_QT % 1024 == 0 && T_OFF_WT % 1024 == 0, "Toeplitz layout");
 // Tensor memory (Toeplitz layout): K words at 0 (a dimension a column; one buffer); score
@@ -410,6 +421,50 @@ static __device__ __noinline__ uint64_t logit_interval_ool(int64_t acc, uint64_t
   bool differ = false;
   const bool done = f64::logit_interval_f64(acc, err, sexp, am_d, ae, fb, differ);
   return (uint64_t)fb | ((uint64_t)differ << 32) | ((uint64_t)done << 33);
+}
+
+// The logit of a score whose windows lost bits, from the exact binary64 correction of its lossy
+// elements (Toeplitz layout; out of line, the pairs with lost bits only): with q = Q 2^qlsb + dq and
+// k = K 2^klsb + dk, q k - Q K 2^(qlsb + klsb) = Q 2^qlsb dk + dq k summed over the row's lossy
+// dimensions (k exact from K and dk) and the key's other lossy elements; one rounding per term
+// and per sum, |corr - c| <= (n + 2) 2^-53 sum |terms|. Bits 0-31 the logit, bit 32 set when it
+// is certified; 0 when a list is incomplete (the caller falls back on the truncation bound).
+static __device__ __noinline__ uint64_t lossy_corr_logit(const Small& S, const KcArea& KC, const int32_t* qfx_g, int g,
+                                                         int b, int key, bool klossy, int64_t acc, int qlsb, int klsb,
+                                                         double am_d, int32_t ae) {
+  const int nql = S.nqlk;
+  const int n0 = klossy ? KC.kcn[b][0][key] : 0, n1 = klossy ? KC.kcn[b][1][key] : 0;
+  if (nql < 0 || n0 > 2 || n1 > 2 || qlsb < -1000 || klsb < -1000 || qlsb > 1000 || klsb > 1000) return 0;
+  const double pq = __hiloint2double((qlsb + 1023) << 20, 0), pk = __hiloint2double((klsb + 1023) << 20, 0);
+  double c = 0.0, a = 0.0;
+  int cnt = 0;
+  for (int n = 0; n < nql; ++n) {  // the row's lossy dimensions
+    const int i = S.qlk[n];
+    if (!((S.qlossy[g][i >> 5] >> (i & 31)) & 1u)) continue;
+    double dk = 0.0;
+    for (int h = 0; h < 2; ++h)
+      for (int e = 0; e < (h ? n1 : n0); ++e)
+        if (KC.kci[b][h][key][e] == i) dk = (double)KC.kcd[b][h][key][e];
+    const double k = (double)S.kqv[b][key][n] * pk + dk;  // the element itself, exact
+    const double Qs = dk != 0.0 ? (double)qfx_g[i] * pq : 0.0;
+    const double t = __fma_rn(Qs, dk, (double)KC.qdq[g][n] * k);
+    c += t;
+    a += fabs(t);
+    ++cnt;
+  }
+  for (int h = 0; h < 2; ++h)  // the key's other lossy elements: Q 2^qlsb dk, exact
+    for (int e = 0; e < (h ? n1 : n0); ++e) {
+      const int i = KC.kci[b][h][key][e];
+      if ((S.qlossy[g][i >> 5] >> (i & 31)) & 1u) continue;
+      const double t = (double)qfx_g[i] * pq * (double)KC.kcd[b][h][key][e];
+      c += t;
+      a += fabs(t);
+      ++cnt;
+    }
+  const double err = (double)(cnt + 2) * 1.1102230246251565e-16 * a * 1.000001;
+  uint32_t fb = 0;
+  if (!f64::logit_f64_corr(acc, qlsb + klsb, c, err, am_d, ae, fb)) return 0;
+  return (uint64_t)fb | (1ull << 32);
 }
 
 // q row g's fixed-point element i from its balanced digit planes in the score B tile
@@ -652,6 +707,22 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
       }
     }
     S.nqlk = n <= NQL ? n : -1;
+    if (TOEP && n <= NQL) {  // the rows' lost parts at the listed dimensions (exact, as dk)
+      KcArea& KC = *(KcArea*)(smem + T_OFF_KC);
+      for (int g = 0; g < 2; ++g)
+        for (int m = 0; m < NQL; ++m) {
+          float dq = 0.0f;
+          if (g < nrows && m < n && S.rows[g] >= 0) {
+            const int i = S.qlk[m];
+            if ((S.qlossy[g][i >> 5] >> (i & 31)) & 1u) {
+              const uint32_t qb = P.q[(int64_t)S.rows[g] * D + i];
+              dq = (float)((double)__uint_as_float(qb << 16) -
+                           (double)qfx[g * D + i] * __hiloint2double((max(S.qlsb[g], -1022) + 1023) << 20, 0));
+            }
+          }
+          KC.qdq[g][m] = dq;
+        }
+    }
   }
   tc::fence_async_smem();
   tc::fence_before_sync();
@@ -817,6 +888,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
       uint32_t lmk[4] = {0u, 0u, 0u, 0u};
       if (!fast && valid) {
         const uint32_t thr = (uint32_t)max(ebase, 0) << 7;
+        int nkc = 0;  // Toeplitz: this half's lossy elements, the first two with their lost parts
 #pragma unroll 1
         for (int cc = khf * (16 / KH); cc < (khf + 1) * (16 / KH); ++cc) {
           const uint4 a = *(const uint4*)KCHUNK(cc);
@@ -828,7 +900,25 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
             bits |= (uint32_t)(mg != 0 && mg < thr) << e;
           }
           lmk[cc >> 2] |= bits << (8 * (cc & 3));
+          if (TOEP) {
+            KcArea& KC = *(KcArea*)(smem + T_OFF_KC);
+            for (uint32_t m = bits; m; m &= m - 1) {
+              const int e = __ffs(m) - 1;
+              if (nkc < 2) {
+                const uint32_t bb = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+                int lost = 0, b2 = 0;
+                const int32_t x = fixq(bb, lsb, lost, b2);
+                // k - K 2^lsb: the bits of k below the window, exact in binary64 and in fp32
+                const double dk = (double)__uint_as_float(bb << 16) -
+                                  (double)x * __hiloint2double((max(lsb, -1022) + 1023) << 20, 0);
+                KC.kci[b][khf][key][nkc] = (uint8_t)(8 * cc + e);
+                KC.kcd[b][khf][key][nkc] = (float)dk;
+              }
+              ++nkc;
+            }
+          }
         }
+        if (TOEP) ((KcArea*)(smem + T_OFF_KC))->kcn[b][khf][key] = (uint8_t)min(nkc, 255);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -1214,7 +1304,14 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
               uint32_t fb;
               bool done = false, differ = false;
               uint64_t err = 0;
-              if (qlossy || klossy) {
+              if (TOEP && (qlossy || klossy)) {  // first the exact correction of the lost parts
+                const uint64_t r = lossy_corr_logit(S, *(const KcArea*)(smem + T_OFF_KC), qfx + g * D, g, b, key, klossy,
+                                                    acc, S.qlsb[g], klsb, am_d, P.ae);
+                fb = (uint32_t)r;
+                done = (r >> 32) & 1u;
+              }
+              if (done) {
+              } else if (qlossy || klossy) {
                 // |q k - Q K| <= |dq| |k| + |Q| |dk| over the lossy elements (units 2^(qlsb + klsb));
                 // |k|'s fixed point as the K producers kept it (beyond their list: |K| < 2^W),
                 // |Q| from the query digits
