@@ -542,6 +542,130 @@ __global__ void __launch_bounds__(128) combine_kernel(Prob P) {
     finalize_row<CPL>(P, r, o.status, o.R, o.Z, o.Ze, o.NR, o.N, o.Ne, lane);
 }
 
+// The same split combine with a block of 128 threads per row (dv <= 128): warp 0 merges the row's
+// exponents, status and Z over the splits (lane-strided, then warp reductions: integer sums taken
+// modulo 2^64 are order-free, so the bits equal the sequential merge's), thread c merges channel c,
+// and the fits / certification votes cover the whole block. Rows with few splits' worth of work
+// each (a long decode row cut into 32 splits) no longer wait on one warp's serial loop over
+// splits x channels.
+__global__ void __launch_bounds__(128) combine_row_kernel(Prob P) {
+  __shared__ int32_t s_R, s_st;
+  __shared__ int64_t s_Z;
+  __shared__ uint64_t s_Ze;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t r = blockIdx.x;
+  const int S = P.splits, dv = P.dv;
+  const int64_t stride = P.rows;
+  if (tid < 32) {
+    int status = ST_OK;
+    int32_t R = R_EMPTY, Rmin = INT32_MAX;  // R_EMPTY is INT32_MIN: below every exponent
+    for (int s = lane; s < S; s += 32) {
+      const int64_t pi = r + (int64_t)s * stride;
+      status = max(status, P.pSt[pi]);
+      const int32_t x = P.pR[pi];
+      if (x != R_EMPTY) {
+        R = max(R, x);
+        Rmin = min(Rmin, x);
+      }
+    }
+    status = __reduce_max_sync(0xffffffffu, status);
+    R = __reduce_max_sync(0xffffffffu, R);
+    Rmin = __reduce_min_sync(0xffffffffu, Rmin);
+    if (status == ST_OK && R != R_EMPTY && (int64_t)R - Rmin > SPREAD_CHECK) status = ST_TIER3;
+    int64_t Z = 0;
+    uint64_t Ze = 0;
+    if (status == ST_OK && R != R_EMPTY) {
+      for (int s = lane; s < S; s += 32) {
+        const int64_t pi = r + (int64_t)s * stride;
+        if (P.pR[pi] == R_EMPTY) continue;
+        int64_t z = P.pZ[pi];
+        uint64_t ze = P.pZe[pi];
+        rescale(z, ze, R - P.pR[pi]);
+        Z += z;
+        Ze += ze;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        Z += __shfl_xor_sync(0xffffffffu, Z, o);
+        Ze += __shfl_xor_sync(0xffffffffu, Ze, o);
+      }
+    }
+    if (lane == 0) {
+      s_R = R;
+      s_st = status;
+      s_Z = Z;
+      s_Ze = Ze;
+    }
+  }
+  __syncthreads();
+  const int32_t R = s_R;
+  const int64_t Z = s_Z;
+  const uint64_t Ze = s_Ze;
+  int status = s_st;
+  bool ok = true;
+  if (status == ST_OK && R != R_EMPTY) ok = fits63(Z, Ze);
+  const int c = tid;
+  int32_t NR = R_EMPTY;
+  int64_t N = 0;
+  uint64_t Ne = 0;
+  if (c < dv && status == ST_OK) {
+    for (int s = 0; s < S; ++s) {
+      const int32_t x = P.pNR[(r + (int64_t)s * stride) * dv + c];
+      if (x != R_EMPTY) NR = max(NR, x);
+    }
+    if (NR != R_EMPTY) {
+      for (int s = 0; s < S; ++s) {
+        const int64_t pc = (r + (int64_t)s * stride) * dv + c;
+        const int32_t x = P.pNR[pc];
+        if (x == R_EMPTY) continue;
+        int64_t n = P.pN[pc];
+        uint64_t ne = P.pNe[pc];
+        rescale(n, ne, NR - x);
+        N += n;
+        Ne += ne;
+      }
+      ok &= fits63(N, Ne);
+    }
+  }
+  if (!__syncthreads_and(ok) && status == ST_OK) status = ST_TIER3;
+  if (P.export_partials) {
+    if (tid == 0) {
+      P.xR[r] = R;
+      P.xZ[r] = Z;
+      P.xZe[r] = Ze;
+      P.xSt[r] = status;
+    }
+    if (c < dv) {
+      P.xNR[r * dv + c] = NR;
+      P.xN[r * dv + c] = N;
+      P.xNe[r * dv + c] = Ne;
+    }
+    return;
+  }
+  if (status == ST_DOMAIN) {
+    if (c < dv) write_out(P, r, c, rnd_zero());
+    if (tid == 0) {
+      P.flags[r] = 2;
+      stat_add(P, STAT_DOMAIN_ROWS, 1);
+    }
+    return;
+  }
+  bool cert = status == ST_OK;
+  Rnd res = rnd_zero();
+  if (cert && c < dv && R != R_EMPTY && NR != R_EMPTY) {
+    const int p = P.fp32 ? FP32_P : BF16_P, qmin = P.fp32 ? FP32_QMIN : BF16_QMIN;
+    cert = certify_ratio(N, Ne, (int64_t)NR - P.FZ, Z, Ze, (int64_t)R - P.FZ, p, qmin, 127, res);
+  }
+  cert = __syncthreads_and(cert);
+  const bool forced = cert && forced_uncertified(P, r);
+  if (!cert || forced) {
+    if (tid == 0) leave_tier(P, r, forced);
+    return;
+  }
+  if (c < dv) write_out(P, r, c, res);
+  if (tid == 0) P.flags[r] = 0;
+}
+
 // ---------------------------------------------------------------------------
 // tier 2: the rows tier 1 left uncertified, int64 fixed point on the CUDA cores, each row's keys
 // cut into chunks over the whole GPU (the reference reruns its uncertified pairs with int64 P.V
@@ -1443,7 +1567,8 @@ cudaError_t launch_simt(const Prob& P, cudaStream_t st) {
 
 cudaError_t launch_combine(const Prob& P, cudaStream_t st) {
   const unsigned g = (unsigned)((P.rows + 3) / 4);
-  if (P.dv <= 32) combine_kernel<1><<<g, 128, 0, st>>>(P);
+  if (P.dv <= 128 && P.rows <= 0x7FFFFFFF) combine_row_kernel<<<(unsigned)P.rows, 128, 0, st>>>(P);
+  else if (P.dv <= 32) combine_kernel<1><<<g, 128, 0, st>>>(P);
   else if (P.dv <= 64) combine_kernel<2><<<g, 128, 0, st>>>(P);
   else if (P.dv <= 128) combine_kernel<4><<<g, 128, 0, st>>>(P);
   else combine_kernel<8><<<g, 128, 0, st>>>(P);
