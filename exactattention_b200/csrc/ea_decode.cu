@@ -750,6 +750,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
   i128 N[RPT];
   uint64_t Zerr[RPT];
   u128 Nerr[RPT];
+  // floors of the tiles' shifts into N not yet added to Nerr (folded in before any rescale and at
+  // the end, which gives Nerr's exact sequence of values where it is used)
+  uint32_t nfl[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     R[i] = R_EMPTY;
@@ -758,6 +761,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     N[i] = 0;
     Zerr[i] = 0;
     Nerr[i] = 0;
+    nfl[i] = 0;
   }
   int32_t vec = INT32_MIN;  // this channel's VE as last applied to N
 
@@ -1553,31 +1557,42 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         ztile[ii] = 0;
         if (g >= nrows) continue;
         if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
+          Nerr[ii] += nfl[ii];
+          nfl[ii] = 0;
           const NScaled r = rescale_n_ool(N[ii], Nerr[ii], ve_now - vec);
           N[ii] = r.n;
           Nerr[ii] = r.e;
         }
         const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
         if (Rt == INT32_MIN) continue;
-        Tlo[ii] = min(Tlo[ii], min(min(S.rtlo[0][g], S.rtlo[1][g]), min(S.rtlo[2][g], S.rtlo[3][g])));
+        // Z, its error and the lowest logit are the row's: the channel-0 thread keeps them (it
+        // writes them with the partials)
+        if (c == 0)
+          Tlo[ii] = min(Tlo[ii], min(min(S.rtlo[0][g], S.rtlo[1][g]), min(S.rtlo[2][g], S.rtlo[3][g])));
         const int32_t Rn = R[ii] == R_EMPTY ? Rt : max(R[ii], Rt);
         if (R[ii] != R_EMPTY && Rn > R[ii]) {
           const int d = Rn - R[ii];
+          Nerr[ii] += nfl[ii];
+          nfl[ii] = 0;
           const NScaled r = rescale_n_ool(N[ii], Nerr[ii], d);
           N[ii] = r.n;
           Nerr[ii] = r.e;
-          int lost;
-          Z[ii] = floor_shift(Z[ii], -d, lost);
-          Zerr[ii] = scale_ceil(Zerr[ii], -d) + (uint64_t)lost;
+          if (c == 0) {
+            int lost;
+            Z[ii] = floor_shift(Z[ii], -d, lost);
+            Zerr[ii] = scale_ceil(Zerr[ii], -d) + (uint64_t)lost;
+          }
         }
         R[ii] = Rn;
         const uint64_t zt = S.zs[0][g] + S.zs[1][g] + S.zs[2][g] + S.zs[3][g];
         ztile[ii] = zt;
         const uint64_t nlw = (uint64_t)S.zl[0][g] + S.zl[1][g] + S.zl[2][g] + S.zl[3][g];
-        const int zsh = (Rt - FW) - (Rn - FZ);
-        int lost = 0;
-        Z[ii] += floor_shift((int64_t)zt, zsh, lost);
-        Zerr[ii] += (nlw ? scale_ceil(nlw, zsh) : 0) + (uint64_t)lost;
+        if (c == 0) {
+          const int zsh = (Rt - FW) - (Rn - FZ);
+          int lost = 0;
+          Z[ii] += floor_shift((int64_t)zt, zsh, lost);
+          Zerr[ii] += (nlw ? scale_ceil(nlw, zsh) : 0) + (uint64_t)lost;
+        }
         const int sb = (Rt - FW - FV) - (Rn - FN);
         sh_base[ii] = sb;
         if (nlw) Nerr[ii] += scale_ceil128(nlw, sb + FV);  // truncated weights: < 1 W unit times |v| < 2^VE_c
@@ -1585,7 +1600,8 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         // to a floor (units 2^(sb - 24)); beyond the list's capacity, the bound of < W + 1 W units
         // times one V unit per such value
         const uint32_t nl = S.vl_n[par][c];
-        if (nl <= VLCAP) {
+        if (nl == 0) {
+        } else if (nl <= VLCAP) {
           i128 corr = 0;
           u128 cerr = 0;
 #pragma unroll 1
@@ -1611,7 +1627,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
           // bounded over every key of the tile: sum (W + 1) = Z_tile + 128
           Nerr[ii] += scale_ceil128((u128)zt + BK, sb + (nl >= VL_BOUNDED ? FV : 0));
         }
-        Nerr[ii] += (sb < 0);  // the floor of the tile's one shift into N
+        nfl[ii] += (sb < 0);  // the floor of the tile's one shift into N
       }
       vec = ve_now;
       EA_PT(4)
@@ -1712,6 +1728,7 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
       // one-sided [N, N + Nerr] in units 2^(NR - P.FZ) with |N| < 2^(P.FZ + klog - 2) < (this
       // split's keys) 2^P.FZ, the bound the exact merge of partials relies on: take the finest unit
       // 2^s (s >= 0) that keeps the interval ends below it, floor the low end, ceil the high end
+      Nerr[ii] += nfl[ii];
       const i128 lo = N[ii] - (i128)Nerr[ii], hi = N[ii] + (i128)Nerr[ii];
       const u128 mag = (u128)(lo < 0 ? -lo : lo) > (u128)(hi < 0 ? -hi : hi) ? (u128)(lo < 0 ? -lo : lo)
                                                                                 : (u128)(hi < 0 ? -hi : hi);
