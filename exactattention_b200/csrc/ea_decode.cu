@@ -359,16 +359,6 @@ __device__ __forceinline__ u128 scale_ceil128(u128 u, int s) {
   return (u >> r) + ((u & (((u128)1 << r) - 1)) != 0);
 }
 
-// N and its error bound in a unit 2^d times coarser (floor, ceil + 1), out of line: the row's
-// bound or the channel's exponent grows on few tiles
-struct NScaled {
-  i128 n;
-  u128 e;
-};
-static __device__ __noinline__ NScaled rescale_n_ool(i128 n, u128 e, int d) {
-  return NScaled{shift_floor128(n, -d), scale_ceil128(e, -d) + 1};
-}
-
 // The part of bf16 `bits` (value v) that FLOORING v 2^-lsb to an integer dropped, v 2^-lsb -
 // floor(v 2^-lsb) in [0, 1), in units 2^-24, itself floored (< 2^24); `lost2` when bits remain
 // below that unit.
@@ -1556,32 +1546,28 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         sh_base[ii] = INT32_MIN;
         ztile[ii] = 0;
         if (g >= nrows) continue;
-        if (ve_now != vec && vec != INT32_MIN) {  // VE_c grew: N in the coarser unit
-          Nerr[ii] += nfl[ii];
-          nfl[ii] = 0;
-          const NScaled r = rescale_n_ool(N[ii], Nerr[ii], ve_now - vec);
-          N[ii] = r.n;
-          Nerr[ii] = r.e;
-        }
+        // N in a coarser unit when VE_c grew (this channel) or the row's bound R grows: one floor
+        // shift by both (nested floors of divisions compose), its bound ceil-shifted plus one
+        int dn = (ve_now != vec && vec != INT32_MIN) ? ve_now - vec : 0;
         const int32_t Rt = max(max(S.rt[0][g], S.rt[1][g]), max(S.rt[2][g], S.rt[3][g]));
+        const int32_t Rn = Rt == INT32_MIN ? R[ii] : R[ii] == R_EMPTY ? Rt : max(R[ii], Rt);
+        const int dr = (R[ii] != R_EMPTY && Rn > R[ii]) ? Rn - R[ii] : 0;
+        dn += dr;
+        if (dn > 0) {
+          const u128 e = Nerr[ii] + nfl[ii];
+          nfl[ii] = 0;
+          N[ii] = dn >= 127 ? (N[ii] < 0 ? (i128)-1 : (i128)0) : (N[ii] >> dn);
+          Nerr[ii] = (dn >= 128 ? (u128)(e != 0) : (e >> dn) + ((e & ((((u128)1) << dn) - 1)) != 0)) + 1;
+        }
         if (Rt == INT32_MIN) continue;
         // Z, its error and the lowest logit are the row's: the channel-0 thread keeps them (it
         // writes them with the partials)
         if (c == 0)
           Tlo[ii] = min(Tlo[ii], min(min(S.rtlo[0][g], S.rtlo[1][g]), min(S.rtlo[2][g], S.rtlo[3][g])));
-        const int32_t Rn = R[ii] == R_EMPTY ? Rt : max(R[ii], Rt);
-        if (R[ii] != R_EMPTY && Rn > R[ii]) {
-          const int d = Rn - R[ii];
-          Nerr[ii] += nfl[ii];
-          nfl[ii] = 0;
-          const NScaled r = rescale_n_ool(N[ii], Nerr[ii], d);
-          N[ii] = r.n;
-          Nerr[ii] = r.e;
-          if (c == 0) {
-            int lost;
-            Z[ii] = floor_shift(Z[ii], -d, lost);
-            Zerr[ii] = scale_ceil(Zerr[ii], -d) + (uint64_t)lost;
-          }
+        if (dr > 0 && c == 0) {
+          int lost;
+          Z[ii] = floor_shift(Z[ii], -dr, lost);
+          Zerr[ii] = scale_ceil(Zerr[ii], -dr) + (uint64_t)lost;
         }
         R[ii] = Rn;
         const uint64_t zt = S.zs[0][g] + S.zs[1][g] + S.zs[2][g] + S.zs[3][g];
