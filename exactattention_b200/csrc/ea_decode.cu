@@ -1632,16 +1632,21 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         if (TOEP) {
           // the digit groups G_0 .. G_8, summed over the four accumulators (each < 4 x 128 x 255
           // x 255 < 2^26 in all)
-          s0 = s1 = s2 = s3 = s4 = s5 = s6 = s7 = s8 = 0;
+          // (32-bit sums; two accumulators a wait)
+          uint32_t u[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-          for (int a = 0; a < 4; ++a) {
+          for (int a = 0; a < 4; a += 2) {
             tc::tmem_ld8(tlane + COLO + 32 * a + 16 * g, d0);
-            tc::tmem_ld8(tlane + COLO + 32 * a + 16 * g + 8, d1);
+            tc::tmem_ld2(tlane + COLO + 32 * a + 16 * g + 8, d1);
+            tc::tmem_ld8(tlane + COLO + 32 * (a + 1) + 16 * g, d2);
+            tc::tmem_ld2(tlane + COLO + 32 * (a + 1) + 16 * g + 8, d3);
             tc::tmem_wait_ld();
-            s0 += d0[0], s1 += d0[1], s2 += d0[2], s3 += d0[3], s4 += d0[4], s5 += d0[5], s6 += d0[6], s7 += d0[7];
-            s8 += d1[0];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) u[k] += d0[k] + d2[k];
+            u[8] += d1[0] + d3[0];
           }
           if (sh_base[ii] == INT32_MIN) continue;
+          s0 = u[0], s1 = u[1], s2 = u[2], s3 = u[3], s4 = u[4], s5 = u[5], s6 = u[6], s7 = u[7], s8 = u[8];
         } else {
           tc::tmem_ld8(tlane + COLO + 6 * g, d0);
           tc::tmem_ld8(tlane + COLO + NSW + 6 * g, d1);
