@@ -465,12 +465,6 @@ __device__ __forceinline__ int32_t q_fix(const uint8_t* sQ, int g, int i) {
   return x;
 }
 
-__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t x) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-
 // bytes 0, 1, 2 of four words as three words (byte k of word j -> byte j of output k)
 __device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t& p0,
                                            uint32_t& p1, uint32_t& p2) {
@@ -1487,7 +1481,9 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
 #pragma unroll
           for (int wd = 0; wd < NW; ++wd) sW[tc::kmajor_off(6 * g + wd, key, NSW)] = (uint8_t)(W >> (8 * wd));
         }
-        const uint64_t zs = warp_sum_u64(W);
+        // the warp's weight sum from two 32-bit reductions of W's 24-bit halves (W < 2^48)
+        const uint64_t zs = (uint64_t)__reduce_add_sync(0xffffffffu, (uint32_t)W & 0xFFFFFFu) +
+                            ((uint64_t)__reduce_add_sync(0xffffffffu, (uint32_t)(W >> 24)) << 24);
         const uint32_t zl = __reduce_add_sync(0xffffffffu, lw);
         if (lane == 0) {
           S.zs[warp & 3][g] = zs;
