@@ -481,7 +481,9 @@ __device__ __forceinline__ void transpose3(uint32_t x0, uint32_t x1, uint32_t x2
 // With 8 consumer and 8 K warps the block has 640 threads and rebalances registers per role
 // (setmaxnreg): the launch gives 96 a thread, the producers drop to REG_PRODUCER and the consumers
 // rise to REG_CONSUMER (256 x 120 + 384 x 80 = 61,440 = 640 x 96).
-template <int RPT, int NC, int KW>
+// SCA (Toeplitz layout): score accumulators, one issuer each (16 / SCA K steps an issuer): fewer
+// accumulators mean fewer TMEM reads and adds for the consumers, more MMAs an issuing K producer.
+template <int RPT, int NC, int KW, int SCA = 4>
 __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     tc_decode_kernel(Prob P, const int32_t* __restrict__ seg_rows, const __grid_constant__ CUtensorMap tmk, int kmode,
                      int kbox) {
@@ -551,8 +553,8 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
     tc::mbar_init(&S.bar_rv[1], 1);
     tc::mbar_init(&S.bar_rv[2], 1);
     // one commit per issuer (a key / value digit, or in the Toeplitz layout four K steps)
-    tc::mbar_init(&S.bar_smma[0], NK);
-    tc::mbar_init(&S.bar_smma[1], NK);
+    tc::mbar_init(&S.bar_smma[0], TOEP ? SCA : NK);
+    tc::mbar_init(&S.bar_smma[1], TOEP ? SCA : NK);
     tc::mbar_init(&S.bar_pv, NV);
     tc::mbar_init(&S.bar_p1[0], 1);
     tc::mbar_init(&S.bar_p1[1], 1);
@@ -944,15 +946,15 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
       }
       EA_PTK(3)
       if (TOEP) {
-        // score MMAs of tile i: lane 0 of K warp a issues K steps 4 a .. 4 a + 3 (dimensions
-        // 32 a .. 32 a + 31) into score accumulator a (N = 8 columns a row)
-        if (lane == 0 && kw < NK) {
+        // score MMAs of tile i: lane 0 of K warp a < SCA issues K steps 16 a / SCA .. (dimensions
+        // 128 a / SCA ..) into score accumulator a (N = 8 columns a row)
+        if (lane == 0 && kw < SCA) {
           tc::fence_after_sync();
           const uint32_t idesc = tc::idesc_i8(128, 8 * nrows, false, true);
           const uint32_t qa = tc::smem_u32(sQ);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int ks = 4 * kw + j;
+          for (int j = 0; j < 16 / SCA; ++j) {
+            const int ks = (16 / SCA) * kw + j;
             tc::mma_i8_tmem_a(tmem + col_s(b) + 16 * kw, tmem + col_k(b) + 8 * ks,
                               tc::smem_desc_sw128(qa + (ks >> 2) * (T_QROWS / 8) * 1024 + (ks & 3) * 32, 1024), idesc,
                               j > 0);
@@ -1247,15 +1249,22 @@ __global__ void __launch_bounds__(threads_of<NC, KW>(), 1)
         for (int g = h; g < nrows; g += NWG) {
           uint32_t dg[NK][4];
           uint32_t gt[8];  // Toeplitz: the digit groups G_0 .. G_6 of the biased key words
-          if (TOEP) {  // the four accumulators' digit groups, summed
-            uint32_t g1[8], g2[8], g3[8];
+          if (TOEP) {  // the accumulators' digit groups, summed
+            uint32_t g1[8];
             tc::tmem_ld8(tlane + col_s(b) + 8 * g, gt);
             tc::tmem_ld8(tlane + col_s(b) + 16 + 8 * g, g1);
-            tc::tmem_ld8(tlane + col_s(b) + 32 + 8 * g, g2);
-            tc::tmem_ld8(tlane + col_s(b) + 48 + 8 * g, g3);
-            tc::tmem_wait_ld();
+            if (SCA == 4) {
+              uint32_t g2[8], g3[8];
+              tc::tmem_ld8(tlane + col_s(b) + 32 + 8 * g, g2);
+              tc::tmem_ld8(tlane + col_s(b) + 48 + 8 * g, g3);
+              tc::tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 7; ++k) gt[k] += g1[k] + g2[k] + g3[k];
+              for (int k = 0; k < 7; ++k) gt[k] += g1[k] + g2[k] + g3[k];
+            } else {
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 7; ++k) gt[k] += g1[k];
+            }
           } else {
 #pragma unroll
             for (int t = 0; t < NK; ++t) tc::tmem_ld4(tlane + col_s(b) + SPL * t + 4 * g, dg[t]);
@@ -1795,23 +1804,32 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
   // 8 consumer warps with 1, 2 or 4 row slots (segments of <= 2, 4, 8 rows); segments of <= 2
   // rows take 8 K producer warps (640 threads) when the build gives the block the registers its
   // per-role split draws on
+  // (RANGE tiles, whose K producers have slack, take two score accumulators; paged ones four:
+  // measured on configs 5 and 3)
   auto k0 = tcd::tc_decode_kernel<1, 8, 8>;
+  auto k0r = tcd::tc_decode_kernel<1, 8, 8, 2>;
   auto k0s = tcd::tc_decode_kernel<1, 8, 4>;
   auto k1 = tcd::tc_decode_kernel<2, 8, 4>;
   auto k2 = tcd::tc_decode_kernel<4, 8, 4>;
+  CUtensorMap tm;
+  int kbox = 0;
+  const int kmode = k_fetch_mode(P, &tm, &kbox);
   // the shared-memory opt-in is a property of the function on a device: set it once per device
   // (not per launch, so a launch inside a stream capture issues nothing but the kernel)
-  static bool attr_set[64][4] = {};
-  static int wide_ok = -1;  // k0's launch registers cover its split (checked once)
+  static bool attr_set[64][5] = {};
+  static int wide_ok = -1;  // the 640-thread kernels' launch registers cover their split (checked once)
   if (wide_ok < 0) {
-    cudaFuncAttributes fa;
-    wide_ok = cudaFuncGetAttributes(&fa, k0) == cudaSuccess && fa.maxThreadsPerBlock >= tcd::threads_of<8, 8>() &&
-              fa.numRegs * tcd::threads_of<8, 8>() >= tcd::REG_SPLIT;
+    cudaFuncAttributes fa, fr;
+    wide_ok = cudaFuncGetAttributes(&fa, k0) == cudaSuccess && cudaFuncGetAttributes(&fr, k0r) == cudaSuccess &&
+              fa.maxThreadsPerBlock >= tcd::threads_of<8, 8>() && fr.maxThreadsPerBlock >= tcd::threads_of<8, 8>() &&
+              fa.numRegs * tcd::threads_of<8, 8>() >= tcd::REG_SPLIT &&
+              fr.numRegs * tcd::threads_of<8, 8>() >= tcd::REG_SPLIT;
   }
-  const int v = max_rows <= 2 ? (wide_ok ? 0 : 3) : max_rows <= 4 ? 1 : 2;
-  auto kern = v == 0 ? k0 : v == 1 ? k1 : v == 2 ? k2 : k0s;
-  const int threads = v == 0 ? tcd::threads_of<8, 8>() : tcd::threads_of<8, 4>();
-  const int smem = v == 0 ? (int)tcd::T_SMEM_BYTES : (int)tcd::SMEM_BYTES;  // (the 640-thread kernel: Toeplitz layout)
+  const int v = max_rows <= 2 ? (wide_ok ? (kmode == tcd::KM_RANGE ? 4 : 0) : 3) : max_rows <= 4 ? 1 : 2;
+  auto kern = v == 0 ? k0 : v == 4 ? k0r : v == 1 ? k1 : v == 2 ? k2 : k0s;
+  const bool wide = v == 0 || v == 4;  // the 640-thread kernels: Toeplitz layout
+  const int threads = wide ? tcd::threads_of<8, 8>() : tcd::threads_of<8, 4>();
+  const int smem = wide ? (int)tcd::T_SMEM_BYTES : (int)tcd::SMEM_BYTES;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
@@ -1819,9 +1837,6 @@ cudaError_t launch_tc_decode(const Prob& P, const int32_t* seg_rows, int64_t nse
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
   }
-  CUtensorMap tm;
-  int kbox = 0;
-  const int kmode = k_fetch_mode(P, &tm, &kbox);
   dim3 grid((unsigned)nseg, (unsigned)P.splits);
   kern<<<grid, threads, smem, st>>>(P, seg_rows, tm, kmode, kbox);
   return cudaGetLastError();
