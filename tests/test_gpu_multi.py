@@ -5,7 +5,6 @@ the bits one single-GPU launch gives over all keys. Skipped when the box has one
 """
 
 import os
-import socket
 from datetime import timedelta
 
 import numpy as np
@@ -16,10 +15,9 @@ from gen import bf16
 pytestmark = pytest.mark.gpu
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _store(result_dir: str) -> str:
+    # a file rendezvous in the test's own directory: no TCP port to race other processes for
+    return "file://" + os.path.join(result_dir, "pg_store")
 
 
 def _case(d=128):
@@ -37,11 +35,11 @@ def _worker(rank, world, port, result_dir):
     import exactattention_b200 as ea
     from exactattention_b200 import dist as ea_dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
-                            device_id=dev)
+    dist.init_process_group("nccl", init_method=_store(result_dir), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
     try:
         Q, K, V, kl = _case()
         n = K.shape[0]
@@ -68,7 +66,7 @@ def test_nccl_kv_sharded_matches_single_gpu(world, tmp_path):
 
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, 0, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     Q, K, V, kl = _case()
     dev = torch.device("cuda", 0)
@@ -86,10 +84,11 @@ def _c5_worker(rank, world, port, result_dir):
 
     from exactattention_b200 import dist as ea_dist, workloads as w
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    dist.init_process_group("nccl", init_method=_store(result_dir), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=dev)
     try:
         case = w.device_case("c5", dev, shard=rank, nshards=world)
         kw = dict(case["kw"])
@@ -120,7 +119,7 @@ def test_nccl_c5_sharded_sha(tmp_path):
     gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "configs.json"))).get("c5")
     if gold is None:
         pytest.skip("no golden SHA for c5")
-    mp.start_processes(_c5_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_c5_worker, args=(world, 0, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
         for sync in (1, 0):
@@ -141,10 +140,11 @@ def _raw_comm_worker(rank, world, port, result_dir):
     import exactattention_b200 as ea
     from exactattention_b200 import cuda, dist as ea_dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    dist.init_process_group("nccl", init_method=_store(result_dir), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
     nccl = ctypes.CDLL("libnccl.so.2")
 
     class UniqueId(ctypes.Structure):
@@ -193,7 +193,7 @@ def test_merge_partials_nccl_raw_communicator(tmp_path):
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 GPUs")
-    mp.start_processes(_raw_comm_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_raw_comm_worker, args=(world, 0, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
         assert bool(np.load(tmp_path / f"raw_same_{r}.npy")[0]), r
